@@ -1,0 +1,466 @@
+// The fused 3x3 convolution on the tcgen05 tensor cores: an implicit GEMM
+// with no im2col buffer.
+//
+//   D[q][co] = sum over (chunk c, tap t, channel i) of X[q + off(t)][c*KC + i] * W[co][(c*9 + t)*KC + i]
+//   out[q][co] = ReLU(scale[co] * D[q][co] + shift[co] (+ skip[q][co]))
+//
+// q runs over frame rows (kernels.hpp), so a tap is a constant row offset
+// off(t) = dy*(n+1) + dx. One CTA owns a 128-row tile of q at a time
+// (persistent over tiles). For each 128-byte channel chunk, TMA stages ONE
+// "halo" tile of 128 + 2(n+2) rows; the nine taps are nine row-shifted
+// views of it, addressed by moving the start of the MMA's shared-memory
+// descriptor (the halo is read from L2 once per chunk, not nine times). The
+// weights of each (chunk, tap) arrive as an N x 128-byte TMA tile. Both use
+// the 128-byte swizzle. The accumulator lives in TMEM, double-buffered, so
+// the epilogue of one tile overlaps the MMAs of the next.
+//
+// Warp roles (192 threads): warp 0 issues TMA, warp 1 issues tcgen05.mma,
+// warps 2-5 run the epilogue (TMEM -> registers -> BN, skip, ReLU -> HBM).
+//
+// Replaces the reference's SIMT gemm_tiled<..., Op::Conv> and
+// launchConvBnRelu (src/cuda/kernels.cu:82-180, 215-224): same epilogue
+// arithmetic (scale*acc + shift rounded separately, + skip, x > 0 ? x : 0),
+// tensor-core accumulation instead of one fmaf chain per output.
+#include <algorithm>
+#include <atomic>
+#include <cstdio>
+
+#include "kernels.hpp"
+#include "sm100.cuh"
+
+namespace azb {
+
+namespace {
+
+template <int N, bool kBf16, bool kSplit>
+struct ConvCfg {
+    static constexpr int kEsz = kBf16 ? 2 : 4;
+    static constexpr int kKc = 128 / kEsz;          // channels per 128-byte chunk
+    static constexpr int kKstep = kBf16 ? 16 : 8;   // K of one MMA (32 bytes)
+    static constexpr int kSteps = kKc / kKstep;     // MMAs per chunk and tap
+    static constexpr int kOps = kSplit ? 2 : 1;     // operand planes per stage
+    static constexpr uint32_t kBBytes = uint32_t(N) * 128u;
+    static constexpr uint32_t kTmemCols = 2 * N <= 64 ? 64 : (2 * N <= 128 ? 128 : (2 * N <= 256 ? 256 : 512));
+    static constexpr uint32_t kIdesc = umma_idesc(N, kBf16);
+    static_assert(N % 32 == 0 && N >= 32 && N <= 256, "N is a multiple of 32 in [32, 256]");
+};
+
+constexpr int kThreads = 192;
+constexpr int kMaxStages = 8;
+
+// Shared memory: [halo buffers][weight buffers][barriers][tmem slot].
+struct Smem {
+    uint8_t* a;
+    uint8_t* b;
+    uint64_t *a_full, *a_empty, *b_full, *b_empty, *acc_full, *acc_empty, *done;
+    uint32_t* tmem_slot;
+};
+
+__device__ __forceinline__ Smem carve(uint8_t* raw, int sa, int sb, int ops, int a_bytes, uint32_t b_bytes) {
+    Smem s;
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+    s.a = base;
+    s.b = base + size_t(sa) * ops * a_bytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(s.b + size_t(sb) * ops * b_bytes);
+    s.a_full = bars;
+    s.a_empty = s.a_full + sa;
+    s.b_full = s.a_empty + sa;
+    s.b_empty = s.b_full + sb;
+    s.acc_full = s.b_empty + sb;
+    s.acc_empty = s.acc_full + 2;
+    s.done = s.acc_empty + 2;
+    s.tmem_slot = reinterpret_cast<uint32_t*>(s.done + 1);
+    return s;
+}
+
+__host__ __device__ constexpr size_t smem_total(int sa, int sb, int ops, int a_bytes, uint32_t b_bytes) {
+    return 1024 + size_t(sa) * ops * a_bytes + size_t(sb) * ops * b_bytes + (2 * sa + 2 * sb + 5) * 8 + 16;
+}
+
+template <int N, bool kBf16, bool kSplit>
+__global__ void __launch_bounds__(kThreads, 1)
+    conv3x3_tc(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAlo,
+               const __grid_constant__ CUtensorMap mW, const __grid_constant__ CUtensorMap mWlo, const ConvArgs p) {
+    using C = ConvCfg<N, kBf16, kSplit>;
+    extern __shared__ uint8_t smem_raw[];
+    const Smem sm = carve(smem_raw, p.sa, p.sb, C::kOps, p.a_bytes, C::kBBytes);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < p.sa; ++i) {
+            mbar_init(&sm.a_full[i], 1);
+            mbar_init(&sm.a_empty[i], 1);
+        }
+        for (int i = 0; i < p.sb; ++i) {
+            mbar_init(&sm.b_full[i], 1);
+            mbar_init(&sm.b_empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&sm.acc_full[i], 1);
+            mbar_init(&sm.acc_empty[i], 128);
+        }
+        mbar_init(sm.done, 1);
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_map(&mA);
+        tma_prefetch_map(&mW);
+        if (kSplit) {
+            tma_prefetch_map(&mAlo);
+            tma_prefetch_map(&mWlo);
+        }
+    }
+    if (warp == 1) tmem_alloc(sm.tmem_slot, C::kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *sm.tmem_slot;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------- producer
+        if (lane == 0) {
+            uint32_t ia = 0, ib = 0;
+            const uint32_t a_tx = uint32_t(p.halo_rows) * 128u * C::kOps;
+            const uint32_t b_tx = C::kBBytes * C::kOps;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < p.ntiles && ok; tile += gridDim.x) {
+                const int y0 = tile * 128 - (p.n + 2);
+                for (int c = 0; c < p.nchunks && ok; ++c) {
+                    const int sa = ia % p.sa;
+                    if (!(ok = mbar_wait(&sm.a_empty[sa], ((ia / p.sa) & 1) ^ 1, p.err, kErrWaitProducer))) break;
+                    mbar_arrive_expect_tx(&sm.a_full[sa], a_tx);
+                    uint8_t* abuf = sm.a + size_t(sa) * C::kOps * p.a_bytes;
+                    tma_load_2d(&mA, abuf, &sm.a_full[sa], c * C::kKc, y0);
+                    if (kSplit) tma_load_2d(&mAlo, abuf + p.a_bytes, &sm.a_full[sa], c * C::kKc, y0);
+                    ++ia;
+                    for (int t = 0; t < 9; ++t) {
+                        const int sb = ib % p.sb;
+                        if (!(ok = mbar_wait(&sm.b_empty[sb], ((ib / p.sb) & 1) ^ 1, p.err, kErrWaitProducer))) break;
+                        mbar_arrive_expect_tx(&sm.b_full[sb], b_tx);
+                        uint8_t* bbuf = sm.b + size_t(sb) * C::kOps * C::kBBytes;
+                        tma_load_2d(&mW, bbuf, &sm.b_full[sb], (c * 9 + t) * C::kKc, 0);
+                        if (kSplit) tma_load_2d(&mWlo, bbuf + C::kBBytes, &sm.b_full[sb], (c * 9 + t) * C::kKc, 0);
+                        ++ib;
+                    }
+                }
+            }
+            // Every copy this thread issued has landed before the CTA may exit:
+            // wait (bounded) for each stage's most recent load.
+            for (uint32_t s = 0; s < uint32_t(p.sa) && s < ia; ++s) {
+                const uint32_t uses = (ia - s + p.sa - 1) / p.sa;
+                mbar_wait(&sm.a_full[s], (uses - 1) & 1, p.err, kErrWaitDrain);
+            }
+            for (uint32_t s = 0; s < uint32_t(p.sb) && s < ib; ++s) {
+                const uint32_t uses = (ib - s + p.sb - 1) / p.sb;
+                mbar_wait(&sm.b_full[s], (uses - 1) & 1, p.err, kErrWaitDrain);
+            }
+        }
+    } else if (warp == 1) {
+        // --------------------------------------------------------- MMA issue
+        if (lane == 0) {
+            uint32_t ia = 0, ib = 0, j = 0;
+            bool ok = true;
+            const uint32_t a_base = smem_u32(sm.a), b_base = smem_u32(sm.b);
+            for (int tile = blockIdx.x; tile < p.ntiles && ok; tile += gridDim.x, ++j) {
+                const uint32_t acc = j & 1;
+                if (!(ok = mbar_wait(&sm.acc_empty[acc], ((j >> 1) & 1) ^ 1, p.err, kErrWaitMma))) break;
+                tc_fence_after();
+                const uint32_t d = tmem + acc * N;
+                for (int c = 0; c < p.nchunks && ok; ++c) {
+                    const int sa = ia % p.sa;
+                    if (!(ok = mbar_wait(&sm.a_full[sa], (ia / p.sa) & 1, p.err, kErrWaitMma))) break;
+                    const uint32_t abuf = a_base + uint32_t(sa) * C::kOps * p.a_bytes;
+                    for (int t = 0; t < 9; ++t) {
+                        const int sb = ib % p.sb;
+                        if (!(ok = mbar_wait(&sm.b_full[sb], (ib / p.sb) & 1, p.err, kErrWaitMma))) break;
+                        tc_fence_after();
+                        const uint32_t bbuf = b_base + uint32_t(sb) * C::kOps * C::kBBytes;
+                        const int dy = t / 3 - 1, dx = t % 3 - 1;
+                        const uint32_t row = uint32_t(p.n + 2 + dy * (p.n + 1) + dx);
+                        for (int k = 0; k < C::kSteps; ++k) {
+                            const uint32_t aoff = row * 128u + uint32_t(k) * 32u;
+                            const uint64_t ad = sw128_desc(abuf + aoff, p.base_offset_mode);
+                            const uint64_t bd = sw128_desc(bbuf + uint32_t(k) * 32u, p.base_offset_mode);
+                            const uint32_t accumulate = (c | t | k) != 0;
+                            umma<kBf16>(d, ad, bd, C::kIdesc, accumulate);
+                            if (kSplit) {
+                                const uint64_t bdl = sw128_desc(bbuf + C::kBBytes + uint32_t(k) * 32u, p.base_offset_mode);
+                                const uint64_t adl = sw128_desc(abuf + p.a_bytes + aoff, p.base_offset_mode);
+                                umma<kBf16>(d, ad, bdl, C::kIdesc, 1);
+                                umma<kBf16>(d, adl, bd, C::kIdesc, 1);
+                            }
+                        }
+                        umma_commit(&sm.b_empty[sb]);   // frees the weight buffer once read
+                        ++ib;
+                    }
+                    if (!ok) break;
+                    umma_commit(&sm.a_empty[sa]);       // frees the halo buffer
+                    ++ia;
+                }
+                if (!ok) break;
+                umma_commit(&sm.acc_full[acc]);         // the tile's accumulator is complete
+            }
+            // All MMAs issued by this thread are complete before teardown.
+            umma_commit(sm.done);
+            mbar_wait(sm.done, 0, p.err, kErrWaitDrain);
+        }
+    } else {
+        // ----------------------------------------------------------- epilogue
+        const int quarter = warp & 3;                 // TMEM lanes this warp may read
+        const int row_in_tile = quarter * 32 + lane;
+        const int n1 = p.n + 1;
+        uint32_t j = 0;
+        for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++j) {
+            const uint32_t acc = j & 1;
+            if (!mbar_wait(&sm.acc_full[acc], (j >> 1) & 1, p.err, kErrWaitEpilogue)) break;
+            tc_fence_after();
+            const int q = tile * 128 + row_in_tile;
+            bool valid = q < p.rows;
+            if (valid) {
+                const int r = q % p.S;
+                valid = r >= n1 && (r % n1) != p.n;
+            }
+            const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + acc * N;
+#pragma unroll 1
+            for (int c0 = 0; c0 < N; c0 += 32) {
+                uint32_t v[32];
+                tmem_ld32(taddr + c0, v);
+                tmem_wait_ld();
+                if (!valid) continue;
+                float y[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    y[i] = __fadd_rn(__fmul_rn(__ldg(p.scale + c0 + i), __uint_as_float(v[i])), __ldg(p.shift + c0 + i));
+                const size_t off = size_t(q) * p.ld + c0;
+                if constexpr (kBf16) {
+                    if (p.skip) {
+                        const uint4* sk = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.skip) + off);
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const uint4 w4 = sk[u];
+                            const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&w4);
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const float2 f = __bfloat1622float2(h2[e]);
+                                y[u * 8 + 2 * e] = __fadd_rn(y[u * 8 + 2 * e], f.x);
+                                y[u * 8 + 2 * e + 1] = __fadd_rn(y[u * 8 + 2 * e + 1], f.y);
+                            }
+                        }
+                    }
+                    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + off);
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        uint4 w4;
+                        __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&w4);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float a0 = y[u * 8 + 2 * e], a1 = y[u * 8 + 2 * e + 1];
+                            h2[e] = __floats2bfloat162_rn(a0 > 0.0f ? a0 : 0.0f, a1 > 0.0f ? a1 : 0.0f);
+                        }
+                        dst[u] = w4;
+                    }
+                } else {
+                    if (p.skip) {
+                        const float4* sk = reinterpret_cast<const float4*>(static_cast<const float*>(p.skip) + off);
+                        const float4* skl = kSplit ? reinterpret_cast<const float4*>(static_cast<const float*>(p.skip_lo) + off) : nullptr;
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) {
+                            float4 s4 = sk[u];
+                            if (kSplit) {
+                                const float4 l4 = skl[u];
+                                s4.x = __fadd_rn(s4.x, l4.x);
+                                s4.y = __fadd_rn(s4.y, l4.y);
+                                s4.z = __fadd_rn(s4.z, l4.z);
+                                s4.w = __fadd_rn(s4.w, l4.w);
+                            }
+                            y[4 * u] = __fadd_rn(y[4 * u], s4.x);
+                            y[4 * u + 1] = __fadd_rn(y[4 * u + 1], s4.y);
+                            y[4 * u + 2] = __fadd_rn(y[4 * u + 2], s4.z);
+                            y[4 * u + 3] = __fadd_rn(y[4 * u + 3], s4.w);
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) y[i] = y[i] > 0.0f ? y[i] : 0.0f;
+                    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + off);
+                    if constexpr (kSplit) {
+                        float4* dlo = reinterpret_cast<float4*>(static_cast<float*>(p.out_lo) + off);
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) {
+                            float4 h, l;
+                            h.x = to_tf32(y[4 * u]);     l.x = __fsub_rn(y[4 * u], h.x);
+                            h.y = to_tf32(y[4 * u + 1]); l.y = __fsub_rn(y[4 * u + 1], h.y);
+                            h.z = to_tf32(y[4 * u + 2]); l.z = __fsub_rn(y[4 * u + 2], h.z);
+                            h.w = to_tf32(y[4 * u + 3]); l.w = __fsub_rn(y[4 * u + 3], h.w);
+                            dst[u] = h;
+                            dlo[u] = l;
+                        }
+                    } else {
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) dst[u] = make_float4(y[4 * u], y[4 * u + 1], y[4 * u + 2], y[4 * u + 3]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&sm.acc_empty[acc]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, C::kTmemCols);
+    }
+}
+
+// ------------------------------------------------------------------- probe
+
+// One CTA, one thread issuing: stage a halo tile and k_chunks weight tiles
+// (weight chunk c at K offset c*9*KC, i.e. tap 0 of chunk c), run the MMAs
+// on the view starting at row `shift`, and write D raw (fp32 [128][N]).
+template <int N, bool kBf16>
+__global__ void __launch_bounds__(128, 1)
+    umma_probe(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mW, int halo_rows,
+               int a_bytes, int shift, int k_chunks, int base_offset_mode, float* out, int* err) {
+    using C = ConvCfg<N, kBf16, false>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* a = base;
+    uint8_t* b = base + a_bytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(b + C::kBBytes);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_barrier_init();
+    }
+    if (warp == 0) tmem_alloc(tslot, C::kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    if (threadIdx.x == 0) {
+        for (int c = 0; c < k_chunks; ++c) {
+            mbar_arrive_expect_tx(&bars[0], uint32_t(halo_rows) * 128u + C::kBBytes);
+            tma_load_2d(&mA, a, &bars[0], c * C::kKc, 0);
+            tma_load_2d(&mW, b, &bars[0], c * 9 * C::kKc, 0);
+            if (!mbar_wait(&bars[0], c & 1, err, kErrWaitMma)) break;
+            tc_fence_after();
+            for (int k = 0; k < C::kSteps; ++k) {
+                const uint64_t ad = sw128_desc(smem_u32(a) + uint32_t(shift) * 128u + k * 32u, base_offset_mode);
+                const uint64_t bd = sw128_desc(smem_u32(b) + k * 32u, base_offset_mode);
+                umma<kBf16>(tmem, ad, bd, C::kIdesc, (c | k) != 0);
+            }
+            umma_commit(&bars[1]);
+            if (!mbar_wait(&bars[1], c & 1, err, kErrWaitMma)) break;
+        }
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t taddr = tmem + (uint32_t(warp * 32) << 16);
+    for (int c0 = 0; c0 < N; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(taddr + c0, v);
+        tmem_wait_ld();
+        for (int i = 0; i < 32; ++i) out[size_t(warp * 32 + lane) * N + c0 + i] = __uint_as_float(v[i]);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, C::kTmemCols);
+    }
+}
+
+template <int N, bool kBf16, bool kSplit>
+cudaError_t launch_one(const ConvMaps& m, const ConvArgs& a, int sms, cudaStream_t s) {
+    using C = ConvCfg<N, kBf16, kSplit>;
+    const size_t smem = smem_total(a.sa, a.sb, C::kOps, a.a_bytes, C::kBBytes);
+    static std::atomic<size_t> configured{0};   // the largest size this instantiation was opened for
+    if (smem > configured.load()) {
+        const cudaError_t e = cudaFuncSetAttribute(conv3x3_tc<N, kBf16, kSplit>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return e;
+        configured = smem;
+    }
+    const int grid = std::max(1, std::min(a.ntiles, sms));
+    conv3x3_tc<N, kBf16, kSplit><<<grid, kThreads, smem, s>>>(m.a, m.a_lo, m.w, m.w_lo, a);
+    return cudaGetLastError();
+}
+
+template <bool kBf16, bool kSplit>
+cudaError_t dispatch_n(int n_out, const ConvMaps& m, const ConvArgs& a, int sms, cudaStream_t s) {
+    switch (n_out) {
+        case 32: return launch_one<32, kBf16, kSplit>(m, a, sms, s);
+        case 64: return launch_one<64, kBf16, kSplit>(m, a, sms, s);
+        case 128: return launch_one<128, kBf16, kSplit>(m, a, sms, s);
+        case 256: return launch_one<256, kBf16, kSplit>(m, a, sms, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+template <int N, bool kBf16>
+cudaError_t probe_one(const ConvMaps& m, int halo_rows, int shift, int k_chunks, int bom, float* out, int* err,
+                      cudaStream_t s) {
+    using C = ConvCfg<N, kBf16, false>;
+    const int a_bytes = (halo_rows * 128 + 1023) / 1024 * 1024;
+    const size_t smem = 1024 + size_t(a_bytes) + C::kBBytes + 64;
+    cudaError_t e = cudaFuncSetAttribute(umma_probe<N, kBf16>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    umma_probe<N, kBf16><<<1, 128, smem, s>>>(m.a, m.w, halo_rows, a_bytes, shift, k_chunks, bom, out, err);
+    return cudaGetLastError();
+}
+
+} // namespace
+
+size_t conv_smem_bytes(int n_out, int precision, int halo_rows, int* sa_out, int* sb_out) {
+    const int ops = precision == kTF32x3 ? 2 : 1;
+    const int a_bytes = (halo_rows * 128 + 1023) / 1024 * 1024;
+    const uint32_t b_bytes = uint32_t(n_out) * 128u;
+    constexpr size_t kMax = 227 * 1024;
+    int sa = 2, sb = 2;
+    for (int cand = kMaxStages; cand >= 2; --cand)
+        if (smem_total(2, cand, ops, a_bytes, b_bytes) <= kMax) {
+            sb = cand;
+            break;
+        }
+    // A third halo buffer only if it still leaves four weight buffers.
+    if (smem_total(3, std::max(sb - 1, 4), ops, a_bytes, b_bytes) <= kMax && sb >= 5) {
+        sa = 3;
+        while (sb > 2 && smem_total(sa, sb, ops, a_bytes, b_bytes) > kMax) --sb;
+    }
+    if (sa_out) *sa_out = sa;
+    if (sb_out) *sb_out = sb;
+    return smem_total(sa, sb, ops, a_bytes, b_bytes);
+}
+
+cudaError_t launch_conv(const ConvMaps& maps, const ConvArgs& a, int n_out, int precision, int sms, cudaStream_t s) {
+    if (a.ntiles <= 0) return cudaSuccess;
+    if (a.sa < 2 || a.sa > kMaxStages || a.sb < 2 || a.sb > kMaxStages) return cudaErrorInvalidValue;
+    switch (precision) {
+        case kTF32: return dispatch_n<false, false>(n_out, maps, a, sms, s);
+        case kTF32x3: return dispatch_n<false, true>(n_out, maps, a, sms, s);
+        case kBF16: return dispatch_n<true, false>(n_out, maps, a, sms, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_umma_probe(const ConvMaps& maps, int n_out, int precision, int halo_rows, int shift_rows,
+                              int k_chunks, int base_offset_mode, float* d_out, int* err, cudaStream_t s) {
+    const bool bf16 = precision == kBF16;
+    if (shift_rows < 0 || shift_rows + 128 > halo_rows) return cudaErrorInvalidValue;
+    switch (n_out) {
+        case 32: return bf16 ? probe_one<32, true>(maps, halo_rows, shift_rows, k_chunks, base_offset_mode, d_out, err, s)
+                             : probe_one<32, false>(maps, halo_rows, shift_rows, k_chunks, base_offset_mode, d_out, err, s);
+        case 64: return bf16 ? probe_one<64, true>(maps, halo_rows, shift_rows, k_chunks, base_offset_mode, d_out, err, s)
+                             : probe_one<64, false>(maps, halo_rows, shift_rows, k_chunks, base_offset_mode, d_out, err, s);
+        case 128: return bf16 ? probe_one<128, true>(maps, halo_rows, shift_rows, k_chunks, base_offset_mode, d_out, err, s)
+                              : probe_one<128, false>(maps, halo_rows, shift_rows, k_chunks, base_offset_mode, d_out, err, s);
+        case 256: return bf16 ? probe_one<256, true>(maps, halo_rows, shift_rows, k_chunks, base_offset_mode, d_out, err, s)
+                              : probe_one<256, false>(maps, halo_rows, shift_rows, k_chunks, base_offset_mode, d_out, err, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+} // namespace azb

@@ -1,0 +1,941 @@
+// The engine's host side (engine.hpp). Weights are reordered once per upload
+// into the layouts the kernels read; a pass is a fixed sequence of launches
+// on one stream: the stem, 2 x blocks fused tensor-core convolutions and the
+// fused heads.
+#include "engine.hpp"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <stdexcept>
+
+#include "../../include/azb200.h"
+
+#ifndef AZB_KERNEL_HASH
+#define AZB_KERNEL_HASH "00000000"
+#endif
+
+namespace azb {
+
+void check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) throw std::runtime_error(std::string("cuda: ") + what + ": " + cudaGetErrorString(e));
+}
+
+NetShape NetShape::from(const azb_net_desc& d) {
+    NetShape s{d.board, d.history, d.blocks, d.filters, d.value_hidden, d.ownership != 0};
+    if (s.board < 5 || s.board > 19) throw std::invalid_argument("azb: board size must be in 5..19");
+    if (s.history < 1 || s.blocks < 0 || s.value_hidden < 1) throw std::invalid_argument("azb: bad network shape");
+    if (s.filters < 8 || s.filters > 256 || s.filters % 8 != 0)
+        throw std::invalid_argument("azb: filters must be a multiple of 8 in [8, 256]");
+    return s;
+}
+
+const char* precision_name(int p) {
+    switch (p) {
+        case kTF32: return "tf32";
+        case kTF32x3: return "tf32x3";
+        case kBF16: return "bf16";
+        default: return "unknown";
+    }
+}
+
+// ------------------------------------------------------------------ layout
+
+namespace {
+
+size_t align64(size_t f) { return (f + 63) / 64 * 64; }
+
+void push(std::vector<LayoutEntry>& list, size_t& floats, const std::string& name, size_t size) {
+    list.push_back({name, size, floats});
+    floats = align64(floats + size);
+}
+
+} // namespace
+
+Layout Layout::of(const NetShape& s) {
+    Layout L;
+    const size_t F = size_t(s.filters), P = size_t(s.planes()), A = size_t(s.area()), V = size_t(s.value_hidden);
+    auto bn = [&](const std::string& pre, size_t c) {
+        push(L.params, L.param_floats, pre + ".gamma", c);
+        push(L.params, L.param_floats, pre + ".beta", c);
+    };
+    auto stats = [&](const std::string& pre, size_t c) {
+        push(L.buffers, L.buffer_floats, pre + ".runMean", c);
+        push(L.buffers, L.buffer_floats, pre + ".runVar", c);
+    };
+    push(L.params, L.param_floats, "stem.conv.w", F * P * 9);
+    bn("stem.bn", F);
+    for (int i = 0; i < s.blocks; ++i) {
+        const std::string pre = "block" + std::to_string(i);
+        push(L.params, L.param_floats, pre + ".conv1.w", F * F * 9);
+        bn(pre + ".bn1", F);
+        push(L.params, L.param_floats, pre + ".conv2.w", F * F * 9);
+        bn(pre + ".bn2", F);
+    }
+    push(L.params, L.param_floats, "policy.conv.w", 2 * F);
+    bn("policy.bn", 2);
+    push(L.params, L.param_floats, "policy.fc.w", (A + 1) * 2 * A);
+    push(L.params, L.param_floats, "policy.fc.b", A + 1);
+    push(L.params, L.param_floats, "value.conv.w", F);
+    bn("value.bn", 1);
+    push(L.params, L.param_floats, "value.fc1.w", V * A);
+    push(L.params, L.param_floats, "value.fc1.b", V);
+    push(L.params, L.param_floats, "value.fc2.w", V);
+    push(L.params, L.param_floats, "value.fc2.b", 1);
+    if (s.ownership) {
+        push(L.params, L.param_floats, "ownership.conv.w", F);
+        bn("ownership.bn", 1);
+    }
+    stats("stem.bn", F);
+    for (int i = 0; i < s.blocks; ++i) {
+        const std::string pre = "block" + std::to_string(i);
+        stats(pre + ".bn1", F);
+        stats(pre + ".bn2", F);
+    }
+    stats("policy.bn", 2);
+    stats("value.bn", 1);
+    if (s.ownership) stats("ownership.bn", 1);
+    return L;
+}
+
+const LayoutEntry& Layout::param(const std::string& name) const {
+    for (const LayoutEntry& e : params)
+        if (e.name == name) return e;
+    throw std::logic_error("azb: no parameter '" + name + "'");
+}
+
+const LayoutEntry& Layout::buffer(const std::string& name) const {
+    for (const LayoutEntry& e : buffers)
+        if (e.name == name) return e;
+    throw std::logic_error("azb: no buffer '" + name + "'");
+}
+
+// ------------------------------------------------------------------ device
+
+namespace {
+
+std::string version_text(int v) { return std::to_string(v / 1000) + "." + std::to_string((v % 1000) / 10); }
+
+void set_up(int device, DeviceInfo& d) {
+    int count = 0;
+    const cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("no CUDA device: ") + cudaGetErrorString(e));
+    if (count < 1) throw std::runtime_error("no CUDA device");
+    if (device < 0 || device >= count)
+        throw std::runtime_error("no CUDA device " + std::to_string(device) + " (" + std::to_string(count) + " present)");
+    check(cudaSetDevice(device), "cudaSetDevice");
+    cudaDeviceProp prop;
+    check(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+    d.name = prop.name;
+    d.architecture = 10 * prop.major + prop.minor;
+    d.sms = prop.multiProcessorCount;
+    d.total_memory = prop.totalGlobalMem;
+    const std::string sm = "sm_" + std::to_string(d.architecture);
+    // SASS for sm_100a only: another architecture finds no machine code.
+    cudaFuncAttributes attr;
+    if (fill_attributes(&attr) != cudaSuccess) {
+        cudaGetLastError();
+        throw std::runtime_error("no kernels for this GPU (" + sm + "; built for sm_100a)");
+    }
+    d.binary_version = attr.binaryVersion;
+    if (d.binary_version != d.architecture || d.architecture != 100)
+        throw std::runtime_error("kernels built for sm_" + std::to_string(d.binary_version) + "; this GPU is " + sm);
+    // A first kernel, through memory, a stream and back.
+    float* probe = nullptr;
+    check(cudaMalloc(&probe, 16 * sizeof(float)), "cudaMalloc");
+    cudaStream_t s;
+    check(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate");
+    float host[16] = {};
+    cudaError_t r = launch_fill(probe, 16, 1.5f, s);
+    if (r == cudaSuccess) r = cudaMemcpyAsync(host, probe, sizeof host, cudaMemcpyDeviceToHost, s);
+    if (r == cudaSuccess) r = cudaStreamSynchronize(s);
+    cudaStreamDestroy(s);
+    cudaFree(probe);
+    check(r, "first kernel");
+    for (float v : host)
+        if (v != 1.5f) throw std::runtime_error("the first kernel wrote wrong values");
+    int drv = 0, rt = 0;
+    check(cudaDriverGetVersion(&drv), "cudaDriverGetVersion");
+    check(cudaRuntimeGetVersion(&rt), "cudaRuntimeGetVersion");
+    d.description = d.name + " " + sm + ", driver API " + version_text(drv) + ", runtime " + version_text(rt) +
+                    ", kernels " + AZB_KERNEL_HASH;
+    d.usable = true;
+}
+
+} // namespace
+
+const DeviceInfo& device_info(int device) {
+    static std::mutex m;
+    static std::vector<std::unique_ptr<DeviceInfo>> infos(64);
+    if (device < 0 || device >= 64) {
+        static DeviceInfo bad;
+        bad.why = "device index out of range";
+        return bad;
+    }
+    std::lock_guard<std::mutex> lock(m);
+    auto& slot = infos[static_cast<size_t>(device)];
+    if (!slot) {
+        slot = std::make_unique<DeviceInfo>();
+        try {
+            set_up(device, *slot);
+        } catch (const std::exception& e) {
+            slot->usable = false;
+            slot->why = e.what();
+        }
+    }
+    return *slot;
+}
+
+const DeviceInfo& require_device(int device) {
+    const DeviceInfo& d = device_info(device);
+    if (!d.usable) throw std::runtime_error("cuda: " + d.why);
+    check(cudaSetDevice(device), "cudaSetDevice");
+    return d;
+}
+
+// ----------------------------------------------------------- tensor maps
+
+namespace {
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_tiled() {
+    static EncodeTiled fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<EncodeTiled>(p);
+    }();
+    if (!fn) throw std::runtime_error("cuda: cuTensorMapEncodeTiled is not available from the driver");
+    return fn;
+}
+
+// ---------------------------------------------------------- conversions
+
+uint32_t bits(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    return u;
+}
+
+float from_bits(uint32_t u) {
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+// Round to nearest, ties away from zero, keeping 10 mantissa bits (the
+// rounding of cvt.rna.tf32.f32); the low 13 bits of the result are zero.
+float tf32_rna(float x) {
+    const uint32_t u = bits(x);
+    if ((u & 0x7F800000u) == 0x7F800000u) return x;
+    return from_bits((u + 0x1000u) & 0xFFFFE000u);
+}
+
+// Round to nearest even bfloat16.
+uint16_t bf16_rne(float x) {
+    const uint32_t u = bits(x);
+    if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FC0;
+    return static_cast<uint16_t>((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
+
+// BatchNorm2d::forwardInfer's folding (src/layers.cpp:91-92), as bn_fold
+// computes it on the reference's GPU (src/cuda/kernels.cu:37-41): float,
+// each operation rounded on its own.
+void fold_bn(const float* gamma, const float* beta, const float* mean, const float* var, int C, float* scale,
+             float* shift) {
+    for (int c = 0; c < C; ++c) {
+        const float sd = std::sqrt(var[c] + 1e-5f);
+        scale[c] = gamma[c] / sd;
+        const float prod = scale[c] * mean[c];
+        shift[c] = beta[c] - prod;
+    }
+}
+
+int round_up(int x, int m) { return (x + m - 1) / m * m; }
+
+int n_out_for(int filters) { return filters <= 32 ? 32 : filters <= 64 ? 64 : filters <= 128 ? 128 : 256; }
+
+int cpad_for(int filters, int precision) {
+    return std::max(round_up(filters, chunk_channels(precision)), n_out_for(filters));
+}
+
+// Sub-allocation of one device arena, 256-byte aligned pieces.
+struct Carver {
+    size_t used = 0;
+    size_t take(size_t bytes) {
+        const size_t off = used;
+        used = (used + bytes + 255) / 256 * 256;
+        return off;
+    }
+};
+
+} // namespace
+
+// A row-major [rows][inner] tensor read in boxes of box_inner x box_rows
+// with the 128-byte swizzle; rows outside [0, rows) read as zero.
+CUtensorMap make_tensor_map(const void* base, int precision, uint64_t inner, uint64_t rows, uint32_t box_inner,
+                     uint32_t box_rows) {
+    CUtensorMap m;
+    const size_t esz = size_t(elem_bytes(precision));
+    const cuuint64_t dims[2] = {inner, rows};
+    const cuuint64_t strides[1] = {inner * esz};
+    const cuuint32_t box[2] = {box_inner, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode_tiled()(&m, precision == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                                      2, const_cast<void*>(base), dims, strides, box, estr,
+                                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuda: cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+    return m;
+}
+
+
+// ---------------------------------------------------------------- weights
+
+size_t Weights::bytes_for(const NetShape& s, int precision) {
+    const int F = s.filters, n_out = n_out_for(F), cpad = cpad_for(F, precision);
+    const size_t A = size_t(s.area()), V = size_t(s.value_hidden);
+    const size_t esz = size_t(elem_bytes(precision)), planes = precision == kTF32x3 ? 2 : 1;
+    Carver c;
+    c.take(size_t(F) * s.planes() * 9 * 4);
+    c.take(size_t(F) * 4);
+    c.take(size_t(F) * 4);
+    for (int i = 0; i < 2 * s.blocks; ++i) {
+        c.take(size_t(n_out) * 4);
+        c.take(size_t(n_out) * 4);
+        for (size_t p = 0; p < planes; ++p) c.take(size_t(n_out) * 9 * cpad * esz);
+    }
+    c.take(2 * size_t(F) * 4);
+    c.take(8);
+    c.take(8);
+    c.take((A + 1) * 2 * A * 4);
+    c.take((A + 1) * 4);
+    c.take(size_t(F) * 4);
+    c.take(4);
+    c.take(4);
+    c.take(V * A * 4);
+    c.take(V * 4);
+    c.take(V * 4);
+    c.take(4);
+    c.take(size_t(F) * 4);
+    c.take(4);
+    c.take(4);
+    return c.used;
+}
+
+Weights::Weights(const NetShape& s, int precision, int device, const float* params, size_t n_params,
+                 const float* buffers, size_t n_buffers)
+    : shape_(s), precision_(precision), device_(device) {
+    if (precision != kTF32 && precision != kTF32x3 && precision != kBF16)
+        throw std::invalid_argument("azb: unknown precision " + std::to_string(precision));
+    require_device(device);
+    const Layout L = Layout::of(s);
+    if (n_params != L.param_floats)
+        throw std::logic_error("azb: the parameter arena has " + std::to_string(n_params) + " floats, the layout " +
+                               std::to_string(L.param_floats));
+    if (n_buffers != L.buffer_floats)
+        throw std::logic_error("azb: the statistics arena has " + std::to_string(n_buffers) + " floats, the layout " +
+                               std::to_string(L.buffer_floats));
+    const int F = s.filters, P = s.planes(), A = s.area(), V = s.value_hidden;
+    n_out_ = n_out_for(F);
+    cpad_ = cpad_for(F, precision);
+    const int KC = chunk_channels(precision), nchunks = cpad_ / KC, Kp = 9 * cpad_;
+    const size_t esz = size_t(elem_bytes(precision));
+    const bool split = precision == kTF32x3;
+    auto P_ = [&](const std::string& n) { return params + L.param(n).offset; };
+    auto B_ = [&](const std::string& n) { return buffers + L.buffer(n).offset; };
+
+    std::vector<uint8_t> img(bytes_for(s, precision), 0);
+    Carver c;
+    auto put = [&](const void* src, size_t bytes) {
+        const size_t off = c.take(bytes);
+        std::memcpy(img.data() + off, src, bytes);
+        return off;
+    };
+    std::vector<size_t> offs;
+    // stem: the reference's [F][P*9] weights and its folded batch norm
+    std::vector<float> sc(size_t(std::max(F, n_out_)), 0.0f), sh(sc.size(), 0.0f);
+    const size_t o_stem_w = put(P_("stem.conv.w"), size_t(F) * P * 9 * 4);
+    fold_bn(P_("stem.bn.gamma"), P_("stem.bn.beta"), B_("stem.bn.runMean"), B_("stem.bn.runVar"), F, sc.data(), sh.data());
+    const size_t o_stem_sc = put(sc.data(), size_t(F) * 4), o_stem_sh = put(sh.data(), size_t(F) * 4);
+
+    struct ConvOffs {
+        size_t scale, shift, w, w_lo;
+    };
+    std::vector<ConvOffs> co(size_t(2 * s.blocks));
+    std::vector<uint8_t> wk(size_t(n_out_) * Kp * esz), wl(split ? size_t(n_out_) * Kp * 4 : 0);
+    for (int i = 0; i < 2 * s.blocks; ++i) {
+        const std::string pre = "block" + std::to_string(i / 2) + (i % 2 ? ".conv2" : ".conv1");
+        const std::string bn = "block" + std::to_string(i / 2) + (i % 2 ? ".bn2" : ".bn1");
+        std::fill(sc.begin(), sc.end(), 0.0f);
+        std::fill(sh.begin(), sh.end(), 0.0f);
+        fold_bn(P_(bn + ".gamma"), P_(bn + ".beta"), B_(bn + ".runMean"), B_(bn + ".runVar"), F, sc.data(), sh.data());
+        co[size_t(i)].scale = put(sc.data(), size_t(n_out_) * 4);
+        co[size_t(i)].shift = put(sh.data(), size_t(n_out_) * 4);
+        // Kernel order: K index (chunk*9 + tap)*KC + channel-in-chunk; the
+        // reference's is channel*9 + tap (src/layers.cpp:44-45).
+        const float* w = P_(pre + ".w");
+        std::fill(wk.begin(), wk.end(), 0);
+        std::fill(wl.begin(), wl.end(), 0);
+        for (int o = 0; o < F; ++o)
+            for (int ci = 0; ci < F; ++ci)
+                for (int t = 0; t < 9; ++t) {
+                    const float v = w[(size_t(o) * F + ci) * 9 + t];
+                    const size_t k = size_t(o) * Kp + size_t((ci / KC) * 9 + t) * KC + ci % KC;
+                    if (precision == kBF16) {
+                        const uint16_t h = bf16_rne(v);
+                        std::memcpy(wk.data() + k * 2, &h, 2);
+                    } else {
+                        const float hi = tf32_rna(v);
+                        std::memcpy(wk.data() + k * 4, &hi, 4);
+                        if (split) {
+                            const float lo = v - hi;
+                            std::memcpy(wl.data() + k * 4, &lo, 4);
+                        }
+                    }
+                }
+        (void)nchunks;
+        co[size_t(i)].w = put(wk.data(), wk.size());
+        co[size_t(i)].w_lo = split ? put(wl.data(), wl.size()) : 0;
+    }
+    // heads
+    std::vector<float> hsc(2), hsh(2);
+    const size_t o_pw = put(P_("policy.conv.w"), size_t(2) * F * 4);
+    fold_bn(P_("policy.bn.gamma"), P_("policy.bn.beta"), B_("policy.bn.runMean"), B_("policy.bn.runVar"), 2, hsc.data(), hsh.data());
+    const size_t o_psc = put(hsc.data(), 8), o_psh = put(hsh.data(), 8);
+    const size_t o_fcw = put(P_("policy.fc.w"), size_t(A + 1) * 2 * A * 4);
+    const size_t o_fcb = put(P_("policy.fc.b"), size_t(A + 1) * 4);
+    const size_t o_vw = put(P_("value.conv.w"), size_t(F) * 4);
+    fold_bn(P_("value.bn.gamma"), P_("value.bn.beta"), B_("value.bn.runMean"), B_("value.bn.runVar"), 1, hsc.data(), hsh.data());
+    const size_t o_vsc = put(hsc.data(), 4), o_vsh = put(hsh.data(), 4);
+    const size_t o_v1w = put(P_("value.fc1.w"), size_t(V) * A * 4);
+    const size_t o_v1b = put(P_("value.fc1.b"), size_t(V) * 4);
+    const size_t o_v2w = put(P_("value.fc2.w"), size_t(V) * 4);
+    const size_t o_v2b = put(P_("value.fc2.b"), 4);
+    size_t o_ow = 0, o_osc = 0, o_osh = 0;
+    if (s.ownership) {
+        o_ow = put(P_("ownership.conv.w"), size_t(F) * 4);
+        fold_bn(P_("ownership.bn.gamma"), P_("ownership.bn.beta"), B_("ownership.bn.runMean"), B_("ownership.bn.runVar"),
+                1, hsc.data(), hsh.data());
+        o_osc = put(hsc.data(), 4);
+        o_osh = put(hsh.data(), 4);
+    }
+    bytes_ = img.size();
+    check(cudaMalloc(&arena_, bytes_), "cudaMalloc weights");
+    const cudaError_t e = cudaMemcpy(arena_, img.data(), bytes_, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(arena_);
+        check(e, "upload weights");
+    }
+    auto at = [&](size_t off) { return reinterpret_cast<float*>(static_cast<uint8_t*>(arena_) + off); };
+    stem_w_ = at(o_stem_w);
+    stem_scale_ = at(o_stem_sc);
+    stem_shift_ = at(o_stem_sh);
+    convs_.resize(co.size());
+    for (size_t i = 0; i < co.size(); ++i) {
+        Conv& cv = convs_[i];
+        cv.scale = at(co[i].scale);
+        cv.shift = at(co[i].shift);
+        cv.w = at(co[i].w);
+        cv.map_w = make_tensor_map(cv.w, precision, uint64_t(Kp), uint64_t(n_out_), uint32_t(KC), uint32_t(n_out_));
+        if (split) {
+            cv.w_lo = at(co[i].w_lo);
+            cv.map_w_lo = make_tensor_map(cv.w_lo, precision, uint64_t(Kp), uint64_t(n_out_), uint32_t(KC), uint32_t(n_out_));
+        } else {
+            cv.map_w_lo = cv.map_w;
+        }
+    }
+    head_.ld = cpad_;
+    head_.n = s.board;
+    head_.S = (s.board + 1) * (s.board + 1);
+    head_.A = A;
+    head_.F = F;
+    head_.V = V;
+    head_.ownership = s.ownership;
+    head_.pol_w = at(o_pw);
+    head_.pol_scale = at(o_psc);
+    head_.pol_shift = at(o_psh);
+    head_.fc_w = at(o_fcw);
+    head_.fc_b = at(o_fcb);
+    head_.val_w = at(o_vw);
+    head_.val_scale = at(o_vsc);
+    head_.val_shift = at(o_vsh);
+    head_.v1_w = at(o_v1w);
+    head_.v1_b = at(o_v1b);
+    head_.v2_w = at(o_v2w);
+    head_.v2_b = at(o_v2b);
+    if (s.ownership) {
+        head_.own_w = at(o_ow);
+        head_.own_scale = at(o_osc);
+        head_.own_shift = at(o_osh);
+    }
+}
+
+Weights::~Weights() {
+    if (arena_) {
+        cudaSetDevice(device_);
+        cudaFree(arena_);
+    }
+}
+
+// -------------------------------------------------------------- workspace
+
+size_t Workspace::bytes_for(const NetShape& s, int precision, int max_batch) {
+    const Frame fr(s.board);
+    const size_t rows = size_t(max_batch) * fr.S;
+    const size_t cpad = size_t(cpad_for(s.filters, precision)), esz = size_t(elem_bytes(precision));
+    const size_t A = size_t(s.area()), L = size_t(s.actions()), B = size_t(max_batch);
+    Carver c;
+    c.take(B * s.planes() * A * 4);
+    for (int i = 0; i < 3; ++i) c.take(rows * cpad * esz);
+    if (precision == kTF32x3)
+        for (int i = 0; i < 3; ++i) c.take(rows * cpad * 4);
+    c.take(B * L * 4);
+    c.take(B * 4);
+    if (s.ownership) c.take(B * A * 4);
+    c.take(B * L * 4);
+    c.take(16);
+    return c.used;
+}
+
+Workspace::Workspace(const Weights& w, int max_batch) : max_batch_(max_batch) {
+    if (max_batch < 1) throw std::invalid_argument("azb: max_batch must be >= 1");
+    const NetShape& s = w.shape();
+    const int precision = w.precision();
+    const Frame fr(s.board);
+    const size_t rows = size_t(max_batch) * fr.S;
+    const size_t cpad = size_t(w.cpad()), esz = size_t(elem_bytes(precision));
+    const size_t A = size_t(s.area()), L = size_t(s.actions()), B = size_t(max_batch);
+    bytes_ = bytes_for(s, precision, max_batch);
+    check(cudaSetDevice(w.device()), "cudaSetDevice");
+    check(cudaMalloc(&arena_, bytes_), "cudaMalloc workspace");
+    // Zero once: the frames' padding rows are never written again.
+    const cudaError_t z = cudaMemset(arena_, 0, bytes_);
+    if (z != cudaSuccess) {
+        cudaFree(arena_);
+        check(z, "cudaMemset workspace");
+    }
+    Carver c;
+    auto at = [&](size_t off) { return static_cast<uint8_t*>(arena_) + off; };
+    stage = reinterpret_cast<float*>(at(c.take(B * s.planes() * A * 4)));
+    for (int i = 0; i < 3; ++i) trunk[i] = at(c.take(rows * cpad * esz));
+    if (precision == kTF32x3)
+        for (int i = 0; i < 3; ++i) trunk_lo[i] = at(c.take(rows * cpad * 4));
+    logits = reinterpret_cast<float*>(at(c.take(B * L * 4)));
+    values = reinterpret_cast<float*>(at(c.take(B * 4)));
+    if (s.ownership) ownership = reinterpret_cast<float*>(at(c.take(B * A * 4)));
+    probs = reinterpret_cast<float*>(at(c.take(B * L * 4)));
+    err = reinterpret_cast<int*>(at(c.take(16)));
+    const uint32_t KC = uint32_t(chunk_channels(precision));
+    for (int i = 0; i < 3; ++i) {
+        map[i] = make_tensor_map(trunk[i], precision, cpad, rows, KC, uint32_t(fr.halo));
+        map_lo[i] = precision == kTF32x3 ? make_tensor_map(trunk_lo[i], precision, cpad, rows, KC, uint32_t(fr.halo)) : map[i];
+    }
+}
+
+Workspace::~Workspace() {
+    if (arena_) cudaFree(arena_);
+}
+
+// ---------------------------------------------------------------- forward
+
+std::string kernel_error_text(int code) {
+    switch (code) {
+        case kErrWaitProducer: return "a tensor-core kernel's copy engine waited too long for a free stage";
+        case kErrWaitMma: return "a tensor-core kernel's MMA issue waited too long for its operands";
+        case kErrWaitEpilogue: return "a tensor-core kernel's epilogue waited too long for its accumulator";
+        case kErrWaitDrain: return "a tensor-core kernel timed out draining its copies";
+        case kErrProbeTimeout: return "bounded wait ran out";
+        default: return "kernel error " + std::to_string(code);
+    }
+}
+
+void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool probs, ConvTimer* timer) {
+    if (B < 1 || B > ws.max_batch()) throw std::invalid_argument("CudaNetwork: batch out of range");
+    const NetShape& sh = w.shape();
+    const int precision = w.precision();
+    const Frame fr(sh.board);
+    const DeviceInfo& dev = device_info(w.device());
+    check(cudaMemsetAsync(ws.err, 0, sizeof(int), s), "reset error word");
+
+    StemArgs st;
+    st.in = ws.stage;
+    st.B = B;
+    st.P = sh.planes();
+    st.n = sh.board;
+    st.S = fr.S;
+    st.F = sh.filters;
+    st.ld = w.cpad();
+    st.w = w.stem_w();
+    st.scale = w.stem_scale();
+    st.shift = w.stem_shift();
+    st.out = ws.trunk[0];
+    st.out_lo = ws.trunk_lo[0];
+    check(launch_stem(st, precision, s), "stem");
+
+    ConvArgs a{};
+    a.n = sh.board;
+    a.S = fr.S;
+    a.rows = B * fr.S;
+    a.ntiles = (a.rows + 127) / 128;
+    a.nchunks = w.cpad() / chunk_channels(precision);
+    a.ld = w.cpad();
+    a.halo_rows = fr.halo;
+    a.a_bytes = (fr.halo * 128 + 1023) / 1024 * 1024;
+    conv_smem_bytes(w.n_out(), precision, fr.halo, &a.sa, &a.sb);
+    a.base_offset_mode = 0;
+    a.err = ws.err;
+    int x = 0;
+    for (int i = 0; i < sh.blocks; ++i) {
+        const int mid = (x + 1) % 3, out = (x + 2) % 3;
+        for (int half = 0; half < 2; ++half) {
+            const Weights::Conv& cv = w.conv(2 * i + half);
+            const int in = half == 0 ? x : mid, dst = half == 0 ? mid : out;
+            ConvMaps m{ws.map[in], ws.map_lo[in], cv.map_w, cv.map_w_lo};
+            a.out = ws.trunk[dst];
+            a.out_lo = ws.trunk_lo[dst];
+            a.skip = half == 0 ? nullptr : ws.trunk[x];
+            a.skip_lo = half == 0 ? nullptr : ws.trunk_lo[x];
+            a.scale = cv.scale;
+            a.shift = cv.shift;
+            if (timer && timer->enabled) check(cudaEventRecord(timer->begin[size_t(2 * i + half)], s), "event");
+            check(launch_conv(m, a, w.n_out(), precision, dev.sms, s), "conv");
+            if (timer && timer->enabled) check(cudaEventRecord(timer->end[size_t(2 * i + half)], s), "event");
+        }
+        x = out;
+    }
+    HeadArgs h = w.head_args();
+    h.trunk = ws.trunk[x];
+    h.trunk_lo = ws.trunk_lo[x];
+    h.B = B;
+    h.logits = ws.logits;
+    h.values = ws.values;
+    h.ownership_out = ws.ownership;
+    h.probs = probs ? ws.probs : nullptr;
+    check(launch_heads(h, precision, s), "heads");
+}
+
+// -------------------------------------------------------------- inference
+
+Inference::Inference(const NetShape& s, const float* params, size_t n_params, const float* buffers, size_t n_buffers,
+                     int max_batch, int device, int precision)
+    : device_(device) {
+    require_device(device);
+    w_ = std::make_unique<Weights>(s, precision, device, params, n_params, buffers, n_buffers);
+    ws_ = std::make_unique<Workspace>(*w_, max_batch);
+    check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+    check(cudaHostAlloc(reinterpret_cast<void**>(&err_host_), sizeof(int), cudaHostAllocDefault), "cudaHostAlloc");
+    *err_host_ = 0;
+}
+
+Inference::~Inference() {
+    cudaSetDevice(device_);
+    if (stream_) {
+        cudaStreamSynchronize(stream_);
+        cudaStreamDestroy(stream_);
+    }
+    if (err_host_) cudaFreeHost(err_host_);
+    if (pin_in_) cudaFreeHost(pin_in_);
+    if (pin_out_) cudaFreeHost(pin_out_);
+    ws_.reset();
+    w_.reset();
+}
+
+void Inference::check_error_word() {
+    if (*err_host_ != 0) {
+        const int code = *err_host_;
+        *err_host_ = 0;
+        throw std::runtime_error("cuda: " + kernel_error_text(code));
+    }
+}
+
+void Inference::infer(const float* input, int B, float* logits, float* values, float* ownership, float* probs) {
+    const NetShape& s = w_->shape();
+    if (ownership && !s.ownership) throw std::invalid_argument("CudaInference: no ownership head");
+    if (B < 1 || B > ws_->max_batch()) throw std::invalid_argument("CudaInference: batch out of range");
+    check(cudaSetDevice(device_), "cudaSetDevice");
+    const size_t in = size_t(B) * s.planes() * s.area();
+    check(cudaMemcpyAsync(ws_->stage, input, in * 4, cudaMemcpyHostToDevice, stream_), "input");
+    encode_forward(*w_, *ws_, B, stream_, probs != nullptr);
+    check(cudaMemcpyAsync(logits, ws_->logits, size_t(B) * s.actions() * 4, cudaMemcpyDeviceToHost, stream_), "logits");
+    check(cudaMemcpyAsync(values, ws_->values, size_t(B) * 4, cudaMemcpyDeviceToHost, stream_), "values");
+    if (ownership)
+        check(cudaMemcpyAsync(ownership, ws_->ownership, size_t(B) * s.area() * 4, cudaMemcpyDeviceToHost, stream_),
+              "ownership");
+    if (probs)
+        check(cudaMemcpyAsync(probs, ws_->probs, size_t(B) * s.actions() * 4, cudaMemcpyDeviceToHost, stream_), "probs");
+    check(cudaMemcpyAsync(err_host_, ws_->err, sizeof(int), cudaMemcpyDeviceToHost, stream_), "error word");
+    check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+    check_error_word();
+}
+
+void Inference::stage(const float* input, int B) {
+    const NetShape& s = w_->shape();
+    if (B < 1 || B > ws_->max_batch()) throw std::invalid_argument("CudaInference: batch out of range");
+    check(cudaSetDevice(device_), "cudaSetDevice");
+    check(cudaMemcpyAsync(ws_->stage, input, size_t(B) * s.planes() * s.area() * 4, cudaMemcpyHostToDevice, stream_),
+          "input");
+    check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+}
+
+void Inference::enqueue(int B) {
+    check(cudaSetDevice(device_), "cudaSetDevice");
+    encode_forward(*w_, *ws_, B, stream_, true);
+}
+
+void Inference::sync() {
+    check(cudaSetDevice(device_), "cudaSetDevice");
+    check(cudaMemcpyAsync(err_host_, ws_->err, sizeof(int), cudaMemcpyDeviceToHost, stream_), "error word");
+    check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+    check_error_word();
+}
+
+void Inference::read(int B, float* logits, float* values, float* ownership, float* probs) {
+    const NetShape& s = w_->shape();
+    check(cudaSetDevice(device_), "cudaSetDevice");
+    if (logits) check(cudaMemcpyAsync(logits, ws_->logits, size_t(B) * s.actions() * 4, cudaMemcpyDeviceToHost, stream_), "logits");
+    if (values) check(cudaMemcpyAsync(values, ws_->values, size_t(B) * 4, cudaMemcpyDeviceToHost, stream_), "values");
+    if (ownership && s.ownership)
+        check(cudaMemcpyAsync(ownership, ws_->ownership, size_t(B) * s.area() * 4, cudaMemcpyDeviceToHost, stream_), "ownership");
+    if (probs) check(cudaMemcpyAsync(probs, ws_->probs, size_t(B) * s.actions() * 4, cudaMemcpyDeviceToHost, stream_), "probs");
+    sync();
+}
+
+void Inference::time(int B, int warmup, int steps, bool with_copies, double* ms, double* conv_ms) {
+    const NetShape& s = w_->shape();
+    if (B < 1 || B > ws_->max_batch()) throw std::invalid_argument("CudaInference: batch out of range");
+    check(cudaSetDevice(device_), "cudaSetDevice");
+    const size_t in_floats = size_t(B) * s.planes() * s.area();
+    const size_t out_floats = size_t(B) * s.actions();
+    if (with_copies && !pin_in_) {
+        check(cudaHostAlloc(reinterpret_cast<void**>(&pin_in_), size_t(ws_->max_batch()) * s.planes() * s.area() * 4,
+                            cudaHostAllocDefault), "cudaHostAlloc");
+        check(cudaHostAlloc(reinterpret_cast<void**>(&pin_out_), size_t(ws_->max_batch()) * (s.actions() + 1) * 4,
+                            cudaHostAllocDefault), "cudaHostAlloc");
+        check(cudaMemcpy(pin_in_, ws_->stage, in_floats * 4, cudaMemcpyDeviceToHost), "copy staged input");
+    }
+    auto pass = [&](ConvTimer* t) {
+        if (with_copies)
+            check(cudaMemcpyAsync(ws_->stage, pin_in_, in_floats * 4, cudaMemcpyHostToDevice, stream_), "input");
+        encode_forward(*w_, *ws_, B, stream_, false, t);
+        if (with_copies) {
+            check(cudaMemcpyAsync(pin_out_, ws_->logits, out_floats * 4, cudaMemcpyDeviceToHost, stream_), "logits");
+            check(cudaMemcpyAsync(pin_out_ + out_floats, ws_->values, size_t(B) * 4, cudaMemcpyDeviceToHost, stream_),
+                  "values");
+        }
+    };
+    for (int i = 0; i < warmup; ++i) pass(nullptr);
+    sync();
+    cudaEvent_t e0, e1;
+    check(cudaEventCreate(&e0), "cudaEventCreate");
+    check(cudaEventCreate(&e1), "cudaEventCreate");
+    check(cudaEventRecord(e0, stream_), "cudaEventRecord");
+    for (int i = 0; i < steps; ++i) pass(nullptr);
+    check(cudaEventRecord(e1, stream_), "cudaEventRecord");
+    check(cudaEventSynchronize(e1), "cudaEventSynchronize");
+    float total = 0.0f;
+    check(cudaEventElapsedTime(&total, e0, e1), "cudaEventElapsedTime");
+    *ms = total;
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    sync();
+    if (conv_ms) {
+        ConvTimer t;
+        t.enabled = true;
+        const size_t n = size_t(2 * s.blocks);
+        t.begin.resize(n);
+        t.end.resize(n);
+        for (size_t i = 0; i < n; ++i) {
+            check(cudaEventCreate(&t.begin[i]), "cudaEventCreate");
+            check(cudaEventCreate(&t.end[i]), "cudaEventCreate");
+        }
+        double sum = 0.0;
+        for (int k = 0; k < steps; ++k) {
+            pass(&t);
+            check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+            for (size_t i = 0; i < n; ++i) {
+                float d = 0.0f;
+                check(cudaEventElapsedTime(&d, t.begin[i], t.end[i]), "cudaEventElapsedTime");
+                sum += d;
+            }
+        }
+        for (size_t i = 0; i < n; ++i) {
+            cudaEventDestroy(t.begin[i]);
+            cudaEventDestroy(t.end[i]);
+        }
+        *conv_ms = sum;
+        sync();
+    }
+}
+
+// ------------------------------------------------------------------ hooks
+
+Hooks& hooks() {
+    static Hooks h;
+    return h;
+}
+
+// ------------------------------------------------------------------ runner
+
+namespace {
+
+// The completion thread's polling interval (src/cuda/cuda_runner.cu:47-48).
+constexpr int kPollFirstUs = 50, kPollLastUs = 200;
+constexpr size_t kMemoryMargin = size_t(512) << 20;
+
+cudaError_t wait_for(cudaEvent_t event) {
+    int sleep_us = kPollFirstUs;
+    for (;;) {
+        const cudaError_t e = cudaEventQuery(event);
+        if (e != cudaErrorNotReady) return e;
+        std::this_thread::sleep_for(std::chrono::microseconds(sleep_us));
+        sleep_us = std::min(kPollLastUs, 2 * sleep_us);
+    }
+}
+
+} // namespace
+
+Runner::Runner(const NetShape& s, const float* params, size_t n_params, const float* buffers, size_t n_buffers,
+               int max_batch, int slots, int device, int precision)
+    : shape_(s), device_(device), max_batch_(max_batch) {
+    if (max_batch < 1) throw std::invalid_argument("makeCudaRunner: maxBatch must be >= 1");
+    if (slots < 1 || slots > 2) throw std::invalid_argument("makeCudaRunner: slots must be in [1, 2]");
+    require_device(device);
+    check_fits(device, hub_bytes(s, precision, max_batch, slots), max_batch, 1);
+    w_ = std::make_unique<Weights>(s, precision, device, params, n_params, buffers, n_buffers);
+    for (int i = 0; i < slots; ++i) {
+        auto sl = std::make_unique<Slot>();
+        sl->ws = std::make_unique<Workspace>(*w_, max_batch);
+        check(cudaStreamCreateWithFlags(&sl->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+        check(cudaEventCreateWithFlags(&sl->event, cudaEventDisableTiming), "cudaEventCreate");
+        const size_t B = size_t(max_batch);
+        check(cudaHostAlloc(reinterpret_cast<void**>(&sl->in_host), B * s.planes() * s.area() * 4, cudaHostAllocDefault), "cudaHostAlloc");
+        check(cudaHostAlloc(reinterpret_cast<void**>(&sl->logits_host), B * s.actions() * 4, cudaHostAllocDefault), "cudaHostAlloc");
+        check(cudaHostAlloc(reinterpret_cast<void**>(&sl->values_host), B * 4, cudaHostAllocDefault), "cudaHostAlloc");
+        if (s.ownership)
+            check(cudaHostAlloc(reinterpret_cast<void**>(&sl->own_host), B * s.area() * 4, cudaHostAllocDefault), "cudaHostAlloc");
+        check(cudaHostAlloc(reinterpret_cast<void**>(&sl->err_host), sizeof(int), cudaHostAllocDefault), "cudaHostAlloc");
+        *sl->err_host = 0;
+        slots_.push_back(std::move(sl));
+    }
+    completion_ = std::thread([this] { completion_loop(); });
+}
+
+Runner::~Runner() {
+    {
+        std::lock_guard<std::mutex> lock(mutex_);
+        stop_ = true;
+    }
+    wake_.notify_all();
+    if (completion_.joinable()) completion_.join();   // after every pass in flight has been reported
+    cudaSetDevice(device_);
+    for (auto& sl : slots_) {
+        if (sl->stream) cudaStreamSynchronize(sl->stream);
+        if (sl->event) cudaEventDestroy(sl->event);
+        if (sl->stream) cudaStreamDestroy(sl->stream);
+        for (void* p : {static_cast<void*>(sl->in_host), static_cast<void*>(sl->logits_host),
+                        static_cast<void*>(sl->values_host), static_cast<void*>(sl->own_host),
+                        static_cast<void*>(sl->err_host)})
+            if (p) cudaFreeHost(p);
+        sl->ws.reset();
+    }
+}
+
+void Runner::begin(int slot, int B, Done done) {
+    std::string error;
+    if (slot < 0 || slot >= slots()) {
+        error = "runner: slot out of range";
+        slot = 0;
+    } else {
+        Slot& s = *slots_[size_t(slot)];
+        try {
+            check(cudaSetDevice(device_), "cudaSetDevice");
+            const size_t in = size_t(B) * shape_.planes() * shape_.area();
+            if (B >= 1 && B <= max_batch_)
+                check(cudaMemcpyAsync(s.ws->stage, s.in_host, in * 4, cudaMemcpyHostToDevice, s.stream), "input");
+            encode_forward(*w_, *s.ws, B, s.stream, false);
+            const int delay = hooks().copy_out_delay_us.load();
+            if (delay > 0) check(launch_spin(1000ull * unsigned(delay), s.stream), "spin");
+            check(cudaMemcpyAsync(s.logits_host, s.ws->logits, size_t(B) * shape_.actions() * 4, cudaMemcpyDeviceToHost,
+                                  s.stream), "logits");
+            check(cudaMemcpyAsync(s.values_host, s.ws->values, size_t(B) * 4, cudaMemcpyDeviceToHost, s.stream), "values");
+            if (shape_.ownership)
+                check(cudaMemcpyAsync(s.own_host, s.ws->ownership, size_t(B) * shape_.area() * 4, cudaMemcpyDeviceToHost,
+                                      s.stream), "ownership");
+            check(cudaMemcpyAsync(s.err_host, s.ws->err, sizeof(int), cudaMemcpyDeviceToHost, s.stream), "error word");
+            // Recorded after the copies: done means the outputs are on the host.
+            check(cudaEventRecord(s.event, s.stream), "cudaEventRecord");
+        } catch (const std::exception& e) {
+            error = e.what();
+            // The event may not cover this pass; make it complete trivially.
+            cudaGetLastError();
+            cudaEventRecord(s.event, s.stream);
+        }
+    }
+    {
+        std::lock_guard<std::mutex> lock(mutex_);
+        queue_.push_back(Pass{slot, std::move(done), std::move(error)});
+    }
+    wake_.notify_all();
+}
+
+void Runner::completion_loop() {
+    cudaSetDevice(device_);
+    for (;;) {
+        Pass pass;
+        {
+            std::unique_lock<std::mutex> lock(mutex_);
+            wake_.wait(lock, [&] { return stop_ || !queue_.empty(); });
+            if (queue_.empty()) return;   // stop_, and nothing in flight
+            pass = std::move(queue_.front());
+            queue_.pop_front();
+        }
+        std::string error = pass.error;
+        Slot& s = *slots_[size_t(pass.slot)];
+        const cudaError_t e = wait_for(s.event);
+        if (error.empty() && e != cudaSuccess) error = std::string("cuda: ") + cudaGetErrorString(e);
+        if (error.empty() && *s.err_host != 0) error = "cuda: " + kernel_error_text(*s.err_host);
+        *s.err_host = 0;
+        // Failure injection: after n passes, the next one fails (once).
+        int left = hooks().fail_countdown.load();
+        while (left > 0 && !hooks().fail_countdown.compare_exchange_weak(left, left - 1)) {
+        }
+        if (left == 1 && error.empty()) error = "cuda: injected failure (a test hook)";
+        ++hooks().passes_completed;
+        if (pass.done) pass.done(pass.slot, error);
+    }
+}
+
+// -------------------------------------------------------------- memory
+
+double hub_bytes(const NetShape& s, int precision, int max_batch, int slots) {
+    return double(slots) * double(Workspace::bytes_for(s, precision, max_batch)) +
+           double(Weights::bytes_for(s, precision));
+}
+
+void check_fits(int device, double need, int max_batch, int hubs) {
+    require_device(device);
+    double have;
+    const size_t limit = hooks().memory_limit.load();
+    if (limit > 0) {
+        have = double(limit);
+    } else {
+        size_t free_b = 0, total = 0;
+        check(cudaMemGetInfo(&free_b, &total), "cudaMemGetInfo");
+        have = free_b > kMemoryMargin ? double(free_b - kMemoryMargin) : 0.0;
+    }
+    if (need <= have) return;
+    throw std::runtime_error("cuda: inference needs " + std::to_string(static_cast<long long>(need / 1e6)) +
+                             " MB of GPU memory at inference_batch " + std::to_string(max_batch) +
+                             (hubs > 1 ? " (" + std::to_string(hubs) + " hubs)" : std::string()) + ", more than the " +
+                             std::to_string(static_cast<long long>(have / 1e6)) +
+                             " MB the GPU has free; lower inference_batch");
+}
+
+} // namespace azb

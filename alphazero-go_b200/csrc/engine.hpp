@@ -1,0 +1,231 @@
+// The engine's host side: device context, weights in kernel layout,
+// workspaces, the forward pass, the synchronous inference object and the
+// asynchronous batch runner. Plain C++17 over the CUDA runtime; the C ABI
+// (include/azb200.h) is a thin layer over these classes (capi.cu).
+#pragma once
+#include <atomic>
+#include <condition_variable>
+#include <cstddef>
+#include <cstdint>
+#include <deque>
+#include <functional>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "kernels.hpp"
+
+struct azb_net_desc;
+
+namespace azb {
+
+// Throws std::runtime_error("cuda: <what>: <error string>") unless cudaSuccess.
+void check(cudaError_t e, const char* what);
+
+// NetConfig with the engine's derived shapes.
+struct NetShape {
+    int board, history, blocks, filters, value_hidden, ownership;
+    int planes() const { return 2 * history + 2; }
+    int area() const { return board * board; }
+    int actions() const { return area() + 1; }
+    static NetShape from(const azb_net_desc& d);
+};
+
+// ParamLayout::of (include/azgo/param_layout.hpp:18-34; src/param_layout.cpp:18-29):
+// params() then buffers() order, each tensor at a 64-float offset.
+struct LayoutEntry {
+    std::string name;
+    size_t size, offset;
+};
+struct Layout {
+    std::vector<LayoutEntry> params, buffers;
+    size_t param_floats = 0, buffer_floats = 0;
+    static Layout of(const NetShape& s);
+    const LayoutEntry& param(const std::string& name) const;
+    const LayoutEntry& buffer(const std::string& name) const;
+};
+
+// Validates a device, checks the machine code matches it, runs a first kernel.
+struct DeviceInfo {
+    bool usable = false;
+    std::string why, name, description;   // description without the precision
+    int architecture = 0, binary_version = 0, sms = 0;
+    size_t total_memory = 0;
+};
+const DeviceInfo& device_info(int device);   // set up once per device (thread-safe)
+const DeviceInfo& require_device(int device);   // throws the reason when unusable
+
+const char* precision_name(int precision);
+
+// One network's weights on one device, in the kernels' layouts.
+class Weights {
+public:
+    Weights(const NetShape& s, int precision, int device, const float* params, size_t n_params, const float* buffers,
+            size_t n_buffers);
+    ~Weights();
+    Weights(const Weights&) = delete;
+    Weights& operator=(const Weights&) = delete;
+
+    struct Conv {
+        const float* scale = nullptr;   // [n_out] folded batch norm
+        const float* shift = nullptr;
+        const void* w = nullptr;        // [n_out][9*cpad] kernel layout (split: tf32 high part)
+        const void* w_lo = nullptr;     // split: low part
+        CUtensorMap map_w{}, map_w_lo{};
+    };
+    const NetShape& shape() const { return shape_; }
+    int precision() const { return precision_; }
+    int device() const { return device_; }
+    int cpad() const { return cpad_; }      // channels per stored pixel row
+    int n_out() const { return n_out_; }    // MMA N (filters rounded up)
+    size_t bytes() const { return bytes_; }
+    const float* stem_w() const { return stem_w_; }
+    const float* stem_scale() const { return stem_scale_; }
+    const float* stem_shift() const { return stem_shift_; }
+    const Conv& conv(int i) const { return convs_[static_cast<size_t>(i)]; }   // 2*block + (0|1)
+    HeadArgs head_args() const { return head_; }   // weights only
+
+    // Bytes of the device arena for these shapes (the memory checks).
+    static size_t bytes_for(const NetShape& s, int precision);
+
+private:
+    NetShape shape_;
+    int precision_, device_, cpad_, n_out_;
+    size_t bytes_ = 0;
+    void* arena_ = nullptr;
+    const float *stem_w_ = nullptr, *stem_scale_ = nullptr, *stem_shift_ = nullptr;
+    std::vector<Conv> convs_;
+    HeadArgs head_{};
+};
+
+// Activations and outputs for up to max_batch positions.
+class Workspace {
+public:
+    Workspace(const Weights& w, int max_batch);
+    ~Workspace();
+    Workspace(const Workspace&) = delete;
+    Workspace& operator=(const Workspace&) = delete;
+    int max_batch() const { return max_batch_; }
+    size_t bytes() const { return bytes_; }
+    static size_t bytes_for(const NetShape& s, int precision, int max_batch);
+
+    float* stage = nullptr;       // [max_batch][planes][area] fp32 input
+    void* trunk[3] = {};          // frame rows x cpad
+    void* trunk_lo[3] = {};       // split mode
+    float* logits = nullptr;      // [max_batch][actions]
+    float* values = nullptr;      // [max_batch]
+    float* ownership = nullptr;   // [max_batch][area] when the head exists
+    float* probs = nullptr;       // [max_batch][actions]
+    int* err = nullptr;           // kernel error word
+    CUtensorMap map[3]{}, map_lo[3]{};
+
+private:
+    int max_batch_;
+    size_t bytes_ = 0;
+    void* arena_ = nullptr;
+};
+
+// Per-conv-launch timing, for the roofline: events around each tower conv.
+struct ConvTimer {
+    std::vector<cudaEvent_t> begin, end;
+    bool enabled = false;
+};
+
+// Network::forward (src/network.cpp:228-309) on the GPU: stem, the tower's
+// fused convolutions, the fused heads; all on one stream.
+void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool probs, ConvTimer* timer = nullptr);
+
+// A row-major [rows][inner] tensor read by TMA in boxes of box_inner x
+// box_rows with the 128-byte swizzle; rows outside [0, rows) read as zero.
+CUtensorMap make_tensor_map(const void* base, int precision, uint64_t inner, uint64_t rows, uint32_t box_inner,
+                            uint32_t box_rows);
+
+// Turns a nonzero kernel error word into the message a pass reports.
+std::string kernel_error_text(int code);
+
+// CudaInference (include/azgo/cuda.hpp:72-84).
+class Inference {
+public:
+    Inference(const NetShape& s, const float* params, size_t n_params, const float* buffers, size_t n_buffers,
+              int max_batch, int device, int precision);
+    ~Inference();
+    void infer(const float* input, int B, float* logits, float* values, float* ownership, float* probs);
+    size_t bytes() const { return ws_->bytes(); }
+    void stage(const float* input, int B);
+    void enqueue(int B);
+    void sync();
+    void read(int B, float* logits, float* values, float* ownership, float* probs);
+    cudaStream_t stream() const { return stream_; }
+    // (total ms of K passes, summed conv-kernel ms)
+    void time(int B, int warmup, int steps, bool with_copies, double* ms, double* conv_ms);
+
+private:
+    void check_error_word();
+    int device_;
+    std::unique_ptr<Weights> w_;
+    std::unique_ptr<Workspace> ws_;
+    cudaStream_t stream_ = nullptr;
+    int* err_host_ = nullptr;    // pinned
+    float* pin_in_ = nullptr;    // pinned staging for the end-to-end timing
+    float* pin_out_ = nullptr;
+};
+
+// The BatchRunner (include/azgo/inference_hub.hpp:41-53; src/cuda/cuda_runner.cu:53-194).
+class Runner {
+public:
+    using Done = std::function<void(int slot, const std::string& error)>;
+    Runner(const NetShape& s, const float* params, size_t n_params, const float* buffers, size_t n_buffers,
+           int max_batch, int slots, int device, int precision);
+    ~Runner();
+    int slots() const { return static_cast<int>(slots_.size()); }
+    int max_batch() const { return max_batch_; }
+    float* input(int slot) { return slots_.at(static_cast<size_t>(slot))->in_host; }
+    const float* logits(int slot) const { return slots_.at(static_cast<size_t>(slot))->logits_host; }
+    const float* values(int slot) const { return slots_.at(static_cast<size_t>(slot))->values_host; }
+    const float* ownership(int slot) const { return slots_.at(static_cast<size_t>(slot))->own_host; }
+    void begin(int slot, int B, Done done);
+
+private:
+    struct Slot {
+        std::unique_ptr<Workspace> ws;
+        cudaStream_t stream = nullptr;
+        cudaEvent_t event = nullptr;
+        float *in_host = nullptr, *logits_host = nullptr, *values_host = nullptr, *own_host = nullptr;
+        int* err_host = nullptr;
+    };
+    struct Pass {
+        int slot;
+        Done done;
+        std::string error;
+    };
+    void completion_loop();
+    NetShape shape_;
+    int device_, max_batch_;
+    std::unique_ptr<Weights> w_;
+    std::vector<std::unique_ptr<Slot>> slots_;
+    std::mutex mutex_;
+    std::condition_variable wake_;
+    std::deque<Pass> queue_;
+    bool stop_ = false;
+    std::thread completion_;
+};
+
+// Memory checks (src/cuda/cuda_runner.cu:196-256).
+double hub_bytes(const NetShape& s, int precision, int max_batch, int slots);
+void check_fits(int device, double need, int max_batch, int hubs);
+
+// Test hooks (src/cuda/cuda_runner.cu:39-45, 258-267).
+struct Hooks {
+    std::atomic<uint64_t> chaos_seed{0};
+    std::atomic<int> fail_countdown{0};
+    std::atomic<size_t> memory_limit{0};
+    std::atomic<long long> passes_completed{0};
+    std::atomic<int> copy_out_delay_us{0};
+};
+Hooks& hooks();
+
+} // namespace azb

@@ -1,0 +1,126 @@
+// The engine's kernels as the host code launches them.
+//
+// Activation layout in HBM ("board frames"): NHWC rows of `ld` channels,
+// one row per pixel of a padded board. Board b occupies frame rows
+// [b*S, (b+1)*S) with S = (n+1)^2: frame row 0 is all padding, then n rows
+// of n+1 pixels whose last pixel is padding. Point (y, x) of board b is row
+//     q = b*S + (y+1)*(n+1) + x,
+// so the 3x3 neighbour (y+dy, x+dx) is row q + dy*(n+1) + dx for every point
+// of the board, and a neighbour off the board is always a padding row. The
+// padding rows are zeroed once when a buffer is allocated and no kernel ever
+// writes them, so a 3x3 convolution reads its 'same' padding as plain rows.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace azb {
+
+// Error codes a kernel leaves in its error word (0: none).
+enum KernelError : int {
+    kErrNone = 0,
+    kErrWaitProducer = 1,   // the TMA warp waited too long for a free stage
+    kErrWaitMma = 2,        // the MMA warp waited too long for data or a free accumulator
+    kErrWaitEpilogue = 3,   // the epilogue waited too long for an accumulator
+    kErrWaitDrain = 4,      // draining in-flight copies after an error timed out
+    kErrProbeTimeout = 5,   // the bounded-wait probe's wait ran out (expected by its test)
+};
+
+
+// The arithmetic a pass runs in (also the operand storage of the trunk).
+enum Precision : int {
+    kTF32 = 0,     // fp32 activations, tf32 tensor-core products, fp32 accumulate
+    kTF32x3 = 1,   // split tf32 (a_hi*b_hi + a_hi*b_lo + a_lo*b_hi): fp32-class accuracy
+    kBF16 = 2,     // bf16 activations and weights, fp32 accumulate
+};
+
+inline int elem_bytes(int precision) { return precision == kBF16 ? 2 : 4; }
+// Channels in one 128-byte K chunk of the implicit GEMM.
+inline int chunk_channels(int precision) { return 128 / elem_bytes(precision); }
+
+struct Frame {
+    int n;      // board size
+    int S;      // rows per board, (n+1)^2
+    int halo;   // rows a 128-row tile reads: 128 + 2(n+2)
+    explicit Frame(int board) : n(board), S((board + 1) * (board + 1)), halo(128 + 2 * (board + 2)) {}
+    size_t row(int b, int y, int x) const { return size_t(b) * S + size_t(y + 1) * (n + 1) + x; }
+};
+
+// One fused 3x3 convolution + folded batch norm (+ skip) + ReLU.
+struct ConvArgs {
+    int n, S;          // board, frame rows per board
+    int rows;          // B * S: frame rows of this pass
+    int ntiles;        // ceil(rows / 128)
+    int nchunks;       // input channels / chunk_channels
+    int ld;            // channels per stored pixel row (input, output and skip)
+    int halo_rows;     // 128 + 2(n+2)
+    int a_bytes;       // one halo buffer, rounded up to 1024
+    int sa, sb;        // pipeline depths: halo buffers, weight buffers
+    int base_offset_mode;   // shared-memory descriptor base offset form: 0 (the form the hardware reads)
+    void* out;         // [rows][ld] bf16 or f32 (split: the tf32 high part)
+    void* out_lo;      // split: f32 low part
+    const void* skip;  // null, or the residual input (same layout as out)
+    const void* skip_lo;
+    const float* scale;   // [N] folded batch norm (0 for padded channels)
+    const float* shift;   // [N]
+    int* err;          // kernel error word (KernelError)
+};
+
+struct ConvMaps {
+    CUtensorMap a, a_lo;   // input activations: box {chunk, halo_rows}
+    CUtensorMap w, w_lo;   // weights [N][9*Cin]: box {chunk, N}
+};
+
+// Shared memory a conv launch needs, and its pipeline depths.
+size_t conv_smem_bytes(int n_out, int precision, int halo_rows, int* sa, int* sb);
+
+// Enqueues the conv on `s`; grid = min(ntiles, sms).
+cudaError_t launch_conv(const ConvMaps& maps, const ConvArgs& a, int n_out, int precision, int sms, cudaStream_t s);
+
+// The stem: 3x3 conv from the [B][P][A] fp32 input straight to frame rows,
+// with its batch norm and ReLU (SIMT; the stem is < 0.2% of the FLOPs).
+struct StemArgs {
+    const float* in;    // [B][P][A]
+    int B, P, n, S, F, ld;
+    const float* w;     // [F][P*9], the reference's order
+    const float* scale; const float* shift;
+    void* out; void* out_lo;
+};
+cudaError_t launch_stem(const StemArgs& a, int precision, cudaStream_t s);
+
+// The fused heads: policy 1x1 conv + BN + ReLU + FC, value 1x1 conv + BN +
+// ReLU + FC + ReLU + FC + tanh, ownership 1x1 conv + BN + tanh, and the
+// softmax over the A+1 moves.
+struct HeadArgs {
+    const void* trunk; const void* trunk_lo;
+    int ld, n, S, A, F, V, B, ownership;
+    const float* pol_w;     // [2][F]
+    const float* pol_scale; const float* pol_shift;   // [2]
+    const float* fc_w; const float* fc_b;             // [A+1][2A], [A+1]
+    const float* val_w;     // [F]
+    const float* val_scale; const float* val_shift;   // [1]
+    const float* v1_w; const float* v1_b;             // [V][A], [V]
+    const float* v2_w; const float* v2_b;             // [V], [1]
+    const float* own_w; const float* own_scale; const float* own_shift;
+    float* logits;      // [B][A+1]
+    float* values;      // [B]
+    float* ownership_out;   // [B][A] or null
+    float* probs;       // [B][A+1] or null
+};
+cudaError_t launch_heads(const HeadArgs& a, int precision, cudaStream_t s);
+
+// Test hooks and context checks.
+cudaError_t launch_fill(float* data, size_t n, float value, cudaStream_t s);
+cudaError_t fill_attributes(cudaFuncAttributes* attr);
+cudaError_t launch_spin(unsigned long long ns, cudaStream_t s);
+// A kernel that waits on an mbarrier nothing arrives on, with a limit of
+// `limit_ns`; it leaves kErrProbeTimeout in *err and returns.
+cudaError_t launch_bounded_wait_probe(int* err, unsigned long long limit_ns, cudaStream_t s);
+
+// A single-CTA check of the tensor-core path: D[128][N] = A[s .. s+127][K] .
+// W[N][K]^T for a shifted view s of a staged halo tile (conv's tap views).
+cudaError_t launch_umma_probe(const ConvMaps& maps, int n_out, int precision, int halo_rows, int shift_rows,
+                              int k_chunks, int base_offset_mode, float* d_out, int* err, cudaStream_t s);
+
+} // namespace azb

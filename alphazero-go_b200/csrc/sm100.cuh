@@ -1,0 +1,199 @@
+// Blackwell (sm_100a) building blocks written as inline PTX: mbarriers with
+// bounded waits, TMA tile loads, and the tcgen05 tensor-core instructions
+// (TMEM allocation, MMA issue, commit, TMEM loads) with their shared-memory
+// and instruction descriptors.
+//
+// Every wait here is bounded by %globaltimer: a wait that runs past its
+// limit records an error code in a global word and returns false, so a
+// kernel that loses a barrier arrival ends with an error status instead of
+// hanging the GPU.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include "kernels.hpp"
+
+namespace azb {
+
+// How long one wait may block before the kernel gives up (nanoseconds).
+constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;   // 1 s
+
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_timer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ------------------------------------------------------------------ mbarrier
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// Makes barrier initialisation visible to the async proxy (TMA, tcgen05).
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Waits for the phase with the given parity to complete, for at most
+// kWaitLimitNs. On timeout records `code` in *err (first error wins) and
+// returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t start = global_timer();
+    for (;;) {
+        for (int i = 0; i < 32; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (global_timer() - start > kWaitLimitNs) {
+            atomicCAS(err, 0, code);
+            return false;
+        }
+    }
+}
+
+// --------------------------------------------------------------------- TMA
+
+__device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// A 2D tile of `map` at element coordinates (x, y) into shared memory at
+// `dst`, completing `bytes` of transaction on `bar`. x is a multiple of 16
+// bytes' worth of elements in every call of this engine (channel chunks of
+// 128 bytes). Rows outside the tensor (negative y included) read as zero.
+__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, void* dst, uint64_t* bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+// ------------------------------------------------------------------ tcgen05
+
+// Allocates `ncols` TMEM columns (a power of two >= 32) for this CTA and
+// writes the base address to shared memory at `dst`. Whole warp.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+// Whole warp.
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D (TMEM, fp32) (+)= A (smem, K-major) . B (smem, K-major)^T, one thread.
+// kind::f16 covers bf16 x bf16; kind::tf32 covers tf32 x tf32.
+template <bool kBf16>
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    if constexpr (kBf16) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+            ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+            ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+            : "memory");
+    }
+}
+
+// Arrives once on `bar` when every tcgen05.mma this thread issued so far has
+// completed (their shared-memory operands may then be overwritten).
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane (warp-collective:
+// lane i of the warp reads lane (taddr.lane + i)).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor for a K-major operand in the 128-byte
+// swizzle layout that TMA writes with CU_TENSOR_MAP_SWIZZLE_128B: rows of
+// 128 bytes, 8-row (1024-byte) swizzle atoms stacked along M/N (stride byte
+// offset 1024), leading byte offset unused (1). Bits 46-48 hold the fixed
+// value 0b001; bits 61-63 the swizzle mode (2 = 128-byte). The start address
+// may sit at ANY 128-byte row of a 1024-byte-aligned buffer with the matrix
+// base offset left at 0: the tensor core takes the swizzle phase from the
+// address bits themselves, exactly as TMA applied it (the single-CTA probe
+// checks every row shift against exact sums; setting the base offset to
+// (address >> 7) & 7 instead gives wrong products). The conv's nine taps are
+// such row-shifted views of one staged halo tile.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, int base_offset_mode = 0) {
+    uint64_t d = static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+    d |= 1ull << 16;                      // leading byte offset (unused for swizzled K-major)
+    d |= static_cast<uint64_t>(1024 >> 4) << 32;   // stride byte offset: one 8-row atom
+    d |= 1ull << 46;                      // fixed 0b001
+    if (base_offset_mode) d |= static_cast<uint64_t>((saddr >> 7) & 7u) << 49;
+    d |= 2ull << 61;                      // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor: fp32 accumulator, K-major A and B, M = 128.
+// a/b format 1 = bf16 (kind::f16), 2 = tf32 (kind::tf32).
+__host__ __device__ constexpr uint32_t umma_idesc(int n, bool bf16) {
+    return (1u << 4)                               // D format: f32
+           | ((bf16 ? 1u : 2u) << 7)               // A format
+           | ((bf16 ? 1u : 2u) << 10)              // B format
+           | (static_cast<uint32_t>(n >> 3) << 17) // N / 8
+           | (static_cast<uint32_t>(128 >> 4) << 24);   // M / 16
+}
+
+// Round-to-nearest (ties away) to tf32, as cvt.rna.tf32.f32 does; the low
+// 13 bits of the result are zero, so a tf32 MMA reads it exactly.
+__device__ __forceinline__ float to_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+} // namespace azb

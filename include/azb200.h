@@ -1,0 +1,171 @@
+/* azb200: a B200 (sm_100a) engine for the AlphaZero network evaluation of
+ * robominds/alphazero-go, behind a plain C ABI.
+ *
+ * The engine runs Network::infer's inference forward (residual tower +
+ * policy/value/ownership heads) on the GPU: tcgen05 tensor-core implicit-GEMM
+ * 3x3 convolutions with batch norm, skip and ReLU fused into the epilogue,
+ * and one fused head kernel. It is the drop-in for the reference's CUDA
+ * engine (include/azgo/cuda.hpp) and BatchRunner (include/azgo/inference_hub.hpp):
+ * the C++ adapter in alphazero-go_b200/host/azb_runner.hpp maps these calls
+ * onto those interfaces.
+ *
+ * Conventions: functions return 0 on success and a negative value on
+ * failure, with a message in err[0..err_cap) when err is not null. No C++
+ * exception crosses this boundary. Host arrays are plain float arrays in the
+ * reference's layouts: input [B][planes][area], logits [B][area+1], values
+ * [B], ownership [B][area]. Weights come as the two ParamLayout arenas
+ * (include/azgo/param_layout.hpp:18-34): params() then buffers(), each
+ * tensor at its 64-float offset.
+ */
+#ifndef AZB200_H
+#define AZB200_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* NetConfig (include/azgo/network.hpp:23-36). */
+typedef struct azb_net_desc {
+    int board;         /* 5..19 */
+    int history;       /* planes = 2*history + 2 */
+    int blocks;        /* residual blocks */
+    int filters;       /* a multiple of 8, at most 256 */
+    int value_hidden;
+    int ownership;     /* 0/1 */
+} azb_net_desc;
+
+/* The arithmetic of a pass. TF32: fp32 activations, tf32 tensor-core
+ * products, fp32 accumulation. TF32X3: the products split into tf32 high and
+ * low parts (three MMAs), fp32-class results. BF16: bf16 weights and
+ * activations, fp32 accumulation. */
+enum { AZB_TF32 = 0, AZB_TF32X3 = 1, AZB_BF16 = 2 };
+
+/* ---------------------------------------------------------------- layout */
+
+/* ParamLayout::of (include/azgo/param_layout.hpp:18-34, src/param_layout.cpp:18-29)
+ * for this shape: which = 0 params() order, 1 buffers() order. An adapter
+ * holding the reference Network checks its tensors against these names,
+ * sizes and offsets before upload, as CudaWeights::upload does
+ * (src/cuda/cuda_network.cu:24-41). */
+int azb_layout_count(const azb_net_desc* desc, int which);
+int azb_layout_entry(const azb_net_desc* desc, int which, int index, char* name, size_t name_cap, size_t* size,
+                     size_t* offset);
+size_t azb_layout_floats(const azb_net_desc* desc, int which);
+
+/* ---------------------------------------------------------------- device */
+
+/* cudaBuilt() (include/azgo/cuda.hpp:30): 1 in this library. */
+int azb_cuda_built(void);
+/* cudaAvailable(&why) (include/azgo/cuda.hpp:39): 1 when device `device` is a
+ * usable sm_100 GPU for this library's machine code; else 0 and the reason. */
+int azb_cuda_available(int device, char* why, size_t why_cap);
+/* cudaDescription() (include/azgo/cuda.hpp:49), with the precision added:
+ * "<GPU> sm_100, driver API x.y, runtime x.y, kernels <8 hex>, <precision>". */
+int azb_describe(int device, int precision, char* out, size_t cap);
+int azb_device_count(void);
+
+/* ------------------------------------------------------------ sync infer */
+
+typedef struct azb_infer azb_infer;
+
+/* CudaInference(net, maxBatch) (include/azgo/cuda.hpp:72-84): uploads the
+ * weights once (checked against the layout: an unknown, missing or
+ * mis-sized tensor is refused by name) and holds one workspace. */
+int azb_infer_create(const azb_net_desc* desc, const float* params, size_t n_params, const float* buffers,
+                     size_t n_buffers, int max_batch, int device, int precision, azb_infer** out, char* err,
+                     size_t err_cap);
+void azb_infer_destroy(azb_infer* h);
+/* CudaInference::infer: copy in, forward, copy out, wait. ownership may be
+ * null (needs the head otherwise); probs (softmax over area+1, may be null). */
+int azb_infer_run(azb_infer* h, const float* input, int B, float* logits, float* values, float* ownership,
+                  float* probs, char* err, size_t err_cap);
+/* CudaInference::bytes(): GPU memory of the activations. */
+size_t azb_infer_bytes(const azb_infer* h);
+
+/* Device-resident use, for timing the kernels alone: copy B positions into
+ * the workspace once, then enqueue forward passes on it (no host copies). */
+int azb_infer_stage(azb_infer* h, const float* input, int B, char* err, size_t err_cap);
+int azb_infer_enqueue(azb_infer* h, int B);
+/* Synchronizes and reports any error (CUDA or a kernel's error word). */
+int azb_infer_sync(azb_infer* h, char* err, size_t err_cap);
+/* The stream passes run on (a cudaStream_t), for events recorded on it. */
+void* azb_infer_stream(azb_infer* h);
+/* K passes of batch B after W warm-ups, timed with CUDA events on the
+ * engine's stream; *ms = total milliseconds of the K passes. with_copies:
+ * each pass also copies the input in from pinned host memory and the
+ * outputs back (the end-to-end path). The conv kernels' own time (the sum
+ * of their event-bracketed durations over the K passes) goes to *conv_ms
+ * when not null. */
+int azb_infer_time(azb_infer* h, int B, int warmup, int steps, int with_copies, double* ms, double* conv_ms,
+                   char* err, size_t err_cap);
+/* Read back the device outputs of the last enqueued pass. */
+int azb_infer_read(azb_infer* h, int B, float* logits, float* values, float* ownership, float* probs, char* err,
+                   size_t err_cap);
+
+/* --------------------------------------------------------------- runner */
+
+typedef struct azb_runner azb_runner;
+/* BatchRunner::begin's done(slot, error): error is "" on success. Called
+ * exactly once per begin, from the runner's completion thread. */
+typedef void (*azb_done_fn)(void* ctx, int slot, const char* error);
+
+/* makeCudaRunner(net, maxBatch, slots) (include/azgo/cuda.hpp:58,
+ * src/cuda/cuda_runner.cu:227-234): slots in [1, 2]; refuses with "cuda:
+ * inference needs N MB ...; lower inference_batch" before allocating when
+ * the slots would not fit the device's free memory. */
+int azb_runner_create(const azb_net_desc* desc, const float* params, size_t n_params, const float* buffers,
+                      size_t n_buffers, int max_batch, int slots, int device, int precision, azb_runner** out,
+                      char* err, size_t err_cap);
+/* Drains every pass in flight (each still gets its done call), then frees. */
+void azb_runner_destroy(azb_runner* r);
+int azb_runner_slots(const azb_runner* r);
+int azb_runner_max_batch(const azb_runner* r);
+/* BatchRunner::input(slot): pinned [max_batch][planes][area] staging. */
+float* azb_runner_input(azb_runner* r, int slot);
+/* BatchRunner::begin (include/azgo/inference_hub.hpp:41-53): enqueues copy
+ * in, forward, copy out and returns at once. A batch out of range or an
+ * enqueue error is reported through done (never by returning). */
+int azb_runner_begin(azb_runner* r, int slot, int B, azb_done_fn done, void* ctx);
+const float* azb_runner_logits(const azb_runner* r, int slot);
+const float* azb_runner_values(const azb_runner* r, int slot);
+const float* azb_runner_ownership(const azb_runner* r, int slot);
+
+/* ------------------------------------------------------- memory checks */
+
+/* CudaWorkspace::bytesFor (src/cuda/cuda_network.cu:199-201): device bytes
+ * of one slot's workspace at max_batch. */
+size_t azb_workspace_bytes(const azb_net_desc* desc, int max_batch, int precision);
+/* checkCudaInferenceMemory (include/azgo/cuda.hpp:63): 0 when `hubs` hubs of
+ * `slots_per_hub` slots at inference_batch fit on `device`, else -1 and the
+ * reference's message. */
+int azb_check_memory(const azb_net_desc* desc, int inference_batch, int hubs, int slots_per_hub, int device,
+                     int precision, char* err, size_t err_cap);
+
+/* ------------------------------------------------ test hooks (cuda_probe) */
+/* include/azgo/cuda.hpp:138-155 */
+void azb_probe_set_hub_chaos_seed(uint64_t seed);
+uint64_t azb_probe_hub_chaos_seed(void);
+void azb_probe_fail_passes_after(int n);
+void azb_probe_set_memory_limit(size_t bytes);
+long long azb_probe_passes_completed(void);
+void azb_probe_set_copy_out_delay(int microseconds);
+/* cuda_probe::binaryVersion / deviceArchitecture / fill (include/azgo/cuda.hpp:93-103). */
+int azb_probe_binary_version(int device);
+int azb_probe_device_architecture(int device);
+int azb_probe_fill(int device, float* data, size_t n, float value, size_t tail, char* err, size_t err_cap);
+/* A kernel that waits on a barrier nothing arrives on: returns the kernel's
+ * error word (5: its wait ran out after limit_ns) with the context intact. */
+int azb_probe_bounded_wait(int device, unsigned long long limit_ns, char* err, size_t err_cap);
+/* The tensor-core path alone on one CTA: D[128][n_out] = A[shift .. shift+127]
+ * . W^T over k_chunks 128-byte chunks, A [halo_rows][chunk*k_chunks] and W
+ * [n_out][9*chunk*k_chunks] given as host fp32 (converted per precision);
+ * D written to host fp32 [128][n_out]. */
+int azb_probe_umma(int device, int precision, int n_out, int halo_rows, int shift_rows, int k_chunks,
+                   int base_offset_mode, const float* a, const float* w, float* d, char* err, size_t err_cap);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

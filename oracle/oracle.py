@@ -1,0 +1,274 @@
+"""ctypes access to the CPU oracle (test infrastructure only).
+
+Two libraries, both built by oracle/Makefile:
+  * liboracle.so - the C restatement of the reference's CPU forward
+    (azoracle.c), plus its seeded network, batch-norm and input generators;
+  * _ref/libazref.so - the reference's own CPU network (robominds/alphazero-go
+    src/network.cpp, src/layers.cpp, src/backend*.cpp ...) compiled from its
+    sources, behind ref_shim.cpp's C ABI.
+Only tests/, the smoke check and bench.py's CPU-baseline / reference arm use
+this module. The GPU engine never imports it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libazref.so")
+
+
+@dataclass(frozen=True)
+class NetConfig:
+    """NetConfig (include/azgo/network.hpp:23-36)."""
+
+    board: int
+    history: int = 1
+    blocks: int = 1
+    filters: int = 32
+    value_hidden: int = 64
+    ownership: bool = False
+
+    @property
+    def planes(self) -> int:
+        return 2 * self.history + 2
+
+    @property
+    def area(self) -> int:
+        return self.board * self.board
+
+    @property
+    def actions(self) -> int:
+        return self.area + 1
+
+
+class _CCfg(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("board", "history", "blocks", "filters", "value_hidden", "ownership")]
+
+
+def _ccfg(cfg: NetConfig) -> _CCfg:
+    return _CCfg(cfg.board, cfg.history, cfg.blocks, cfg.filters, cfg.value_hidden, int(cfg.ownership))
+
+
+_F = C.POINTER(C.c_float)
+
+
+def _fp(a: np.ndarray | None):
+    if a is None:
+        return None
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_F)
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(ORACLE_SO):
+            raise RuntimeError(f"oracle not built: run `make -C {HERE} oracle`")
+        L = C.CDLL(ORACLE_SO)
+        P = C.POINTER(_CCfg)
+        L.az_layout_count.argtypes = [P, C.c_int]
+        L.az_layout_entry.argtypes = [P, C.c_int, C.c_int, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t),
+                                      C.POINTER(C.c_size_t), C.POINTER(C.c_int)]
+        L.az_layout_floats.argtypes = [P, C.c_int]
+        L.az_layout_floats.restype = C.c_size_t
+        L.az_network_init.argtypes = [P, C.c_uint64, _F, _F]
+        L.az_randomize.argtypes = [P, C.c_int, C.c_uint64, _F, _F]
+        L.az_inputs_positions.argtypes = [P, C.c_uint64, C.c_long, C.c_int, _F]
+        L.az_inputs_planes.argtypes = [C.c_uint64, C.c_size_t, _F]
+        for fn in (L.az_forward_f32, L.az_forward_f64):
+            fn.argtypes = [P, _F, _F, _F, C.c_int, _F, _F, _F, C.c_int]
+        L.az_derive_seed.argtypes = [C.c_uint64] * 4
+        L.az_derive_seed.restype = C.c_uint64
+        _lib = L
+    return _lib
+
+
+def layout(cfg: NetConfig, which: int):
+    """[(name, size, offset)] in params() (which=0) or buffers() (1) order."""
+    L = lib()
+    c = _ccfg(cfg)
+    out = []
+    name = C.create_string_buffer(64)
+    size, off, decay = C.c_size_t(), C.c_size_t(), C.c_int()
+    for i in range(L.az_layout_count(C.byref(c), which)):
+        L.az_layout_entry(C.byref(c), which, i, name, 64, C.byref(size), C.byref(off), C.byref(decay))
+        out.append((name.value.decode(), size.value, off.value))
+    return out
+
+
+def arena_floats(cfg: NetConfig):
+    c = _ccfg(cfg)
+    return lib().az_layout_floats(C.byref(c), 0), lib().az_layout_floats(C.byref(c), 1)
+
+
+KIND_BENCH, KIND_TEST = 0, 1
+
+
+def make_network(cfg: NetConfig, seed: int, kind: int | None = KIND_BENCH):
+    """Network(cfg, seed), then the batch-norm randomiser `kind` (None: none).
+    Returns the (params, buffers) arenas in ParamLayout order."""
+    np_, nb = arena_floats(cfg)
+    params = np.zeros(np_, np.float32)
+    buffers = np.zeros(nb, np.float32)
+    c = _ccfg(cfg)
+    lib().az_network_init(C.byref(c), seed, _fp(params), _fp(buffers))
+    if kind is not None:
+        lib().az_randomize(C.byref(c), kind, seed, _fp(params), _fp(buffers))
+    return params, buffers
+
+
+def positions(cfg: NetConfig, seed: int, B: int, first: int = 0) -> np.ndarray:
+    out = np.zeros((B, cfg.planes, cfg.area), np.float32)
+    c = _ccfg(cfg)
+    lib().az_inputs_positions(C.byref(c), seed, first, B, _fp(out))
+    return out
+
+
+def random_planes(cfg: NetConfig, seed: int, B: int) -> np.ndarray:
+    out = np.zeros((B, cfg.planes, cfg.area), np.float32)
+    lib().az_inputs_planes(seed, out.size, _fp(out))
+    return out
+
+
+def forward(cfg: NetConfig, params, buffers, x: np.ndarray, precision: str = "f32", threads: int = 1):
+    """(logits [B][A+1], values [B], ownership [B][A] or None)."""
+    x = np.ascontiguousarray(x, np.float32)
+    B = x.shape[0]
+    logits = np.zeros((B, cfg.actions), np.float32)
+    values = np.zeros(B, np.float32)
+    own = np.zeros((B, cfg.area), np.float32) if cfg.ownership else None
+    c = _ccfg(cfg)
+    fn = lib().az_forward_f32 if precision == "f32" else lib().az_forward_f64
+    fn(C.byref(c), _fp(params), _fp(buffers), _fp(x), B, _fp(logits), _fp(values), _fp(own), threads)
+    return logits, values, own
+
+
+# ------------------------------------------------------------ the reference
+
+
+_ref = None
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_SO)
+
+
+def ref() -> C.CDLL:
+    global _ref
+    if _ref is None:
+        if not ref_available():
+            raise RuntimeError("oracle/_ref/libazref.so not built (needs the reference tree)")
+        R = C.CDLL(REF_SO)
+        R.azref_net_create.argtypes = [C.c_int] * 6 + [C.c_uint64, C.c_int]
+        R.azref_net_create.restype = C.c_void_p
+        R.azref_net_destroy.argtypes = [C.c_void_p]
+        R.azref_floats.argtypes = [C.c_void_p, C.c_int]
+        R.azref_floats.restype = C.c_size_t
+        R.azref_layout_count.argtypes = [C.c_void_p, C.c_int]
+        R.azref_layout_entry.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_char_p, C.c_size_t,
+                                         C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]
+        R.azref_export.argtypes = [C.c_void_p, _F, _F]
+        R.azref_infer.argtypes = [C.c_void_p, C.c_char_p, _F, C.c_int, _F, _F, _F, C.c_char_p, C.c_size_t]
+        R.azref_inputs_positions.argtypes = [C.c_int, C.c_int, C.c_uint64, C.c_long, C.c_int, _F]
+        R.azref_inputs_planes.argtypes = [C.c_uint64, C.c_size_t, _F]
+        R.azref_bench_workers.argtypes = [C.c_void_p, C.c_char_p, C.c_int, C.c_int, _F, C.c_double,
+                                          C.c_longlong, C.POINTER(C.c_longlong), C.c_char_p, C.c_size_t]
+        R.azref_bench_workers.restype = C.c_double
+        R.azref_blas_description.restype = C.c_char_p
+        _ref = R
+    return _ref
+
+
+class RefNetwork:
+    """The reference's Network(cfg, seed) plus a randomiser, in its own code."""
+
+    def __init__(self, cfg: NetConfig, seed: int, kind: int | None = KIND_BENCH):
+        self.cfg = cfg
+        self.h = ref().azref_net_create(cfg.board, cfg.history, cfg.blocks, cfg.filters, cfg.value_hidden,
+                                        int(cfg.ownership), seed, -1 if kind is None else kind)
+        if not self.h:
+            raise RuntimeError("reference Network construction failed")
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            ref().azref_net_destroy(self.h)
+            self.h = None
+
+    def layout(self, which: int):
+        R = ref()
+        out = []
+        name = C.create_string_buffer(64)
+        size, off = C.c_size_t(), C.c_size_t()
+        for i in range(R.azref_layout_count(self.h, which)):
+            R.azref_layout_entry(self.h, which, i, name, 64, C.byref(size), C.byref(off))
+            out.append((name.value.decode(), size.value, off.value))
+        return out
+
+    def arenas(self):
+        R = ref()
+        params = np.zeros(R.azref_floats(self.h, 0), np.float32)
+        buffers = np.zeros(R.azref_floats(self.h, 1), np.float32)
+        R.azref_export(self.h, _fp(params), _fp(buffers))
+        return params, buffers
+
+    def infer(self, x: np.ndarray, backend: str = "naive"):
+        cfg = self.cfg
+        x = np.ascontiguousarray(x, np.float32)
+        B = x.shape[0]
+        logits = np.zeros((B, cfg.actions), np.float32)
+        values = np.zeros(B, np.float32)
+        own = np.zeros((B, cfg.area), np.float32) if cfg.ownership else None
+        err = C.create_string_buffer(256)
+        rc = ref().azref_infer(self.h, backend.encode(), _fp(x), B, _fp(logits), _fp(values), _fp(own), err, 256)
+        if rc != 0:
+            raise RuntimeError(err.value.decode())
+        return logits, values, own
+
+    def bench_workers(self, backend: str, workers: int, batch: int, x: np.ndarray, seconds: float = 0.0,
+                      max_calls: int = 0):
+        """(positions/s, positions) with `workers` threads of Network::infer at `batch`."""
+        x = np.ascontiguousarray(x, np.float32)
+        pos = C.c_longlong()
+        err = C.create_string_buffer(256)
+        rate = ref().azref_bench_workers(self.h, backend.encode(), workers, batch, _fp(x), seconds, max_calls,
+                                         C.byref(pos), err, 256)
+        if rate < 0:
+            raise RuntimeError(err.value.decode())
+        return rate, pos.value
+
+
+def ref_positions(cfg: NetConfig, seed: int, B: int, first: int = 0) -> np.ndarray:
+    out = np.zeros((B, cfg.planes, cfg.area), np.float32)
+    ref().azref_inputs_positions(cfg.board, cfg.history, seed, first, B, _fp(out))
+    return out
+
+
+def blas_description() -> str:
+    return ref().azref_blas_description().decode()
+
+
+# ------------------------------------------------------------------ metrics
+
+
+def max_err(x: np.ndarray, ref_: np.ndarray) -> float:
+    """maxErr = max|x - ref| / max|ref| (tests/test_cuda.cpp:150-171)."""
+    x = np.asarray(x, np.float64)
+    r = np.asarray(ref_, np.float64)
+    num = float(np.max(np.abs(x - r))) if x.size else 0.0
+    den = float(np.max(np.abs(r))) if r.size else 0.0
+    return num / den if den > 0 else num
+
+
+def softmax(logits: np.ndarray) -> np.ndarray:
+    z = np.asarray(logits, np.float64)
+    z = z - z.max(axis=-1, keepdims=True)
+    e = np.exp(z)
+    return e / e.sum(axis=-1, keepdims=True)
