@@ -114,6 +114,9 @@ def lib() -> C.CDLL:
             L.azb_probe_fill.argtypes = [C.c_int, _F, s, C.c_float, s] + err
             L.azb_probe_bounded_wait.argtypes = [C.c_int, C.c_ulonglong] + err
             L.azb_probe_umma.argtypes = [C.c_int] * 7 + [_F, _F, _F] + err
+            L.azb_synth_network.argtypes = [D, C.c_uint64, C.c_int, _F, _F]
+            L.azb_synth_positions.argtypes = [D, C.c_uint64, C.c_long, C.c_int, _F]
+            L.azb_device_pci_bus_id.argtypes = [C.c_int, C.c_char_p, s]
             _lib = L
     return _lib
 
@@ -165,6 +168,34 @@ def layout(desc: NetDesc, which: int):
     for i in range(L.azb_layout_count(C.byref(desc), which)):
         L.azb_layout_entry(C.byref(desc), which, i, name, 64, C.byref(size), C.byref(off))
         out.append((name.value.decode(), size.value, off.value))
+    return out
+
+
+def pci_bus_id(device: int = 0) -> str:
+    out = C.create_string_buffer(64)
+    return out.value.decode() if lib().azb_device_pci_bus_id(device, out, 64) == 0 else ""
+
+
+def arena_floats(desc: NetDesc) -> tuple[int, int]:
+    return lib().azb_layout_floats(C.byref(desc), 0), lib().azb_layout_floats(C.byref(desc), 1)
+
+
+def synth_network(desc: NetDesc, seed: int, kind: int = 0):
+    """Network(cfg, seed) plus a batch-norm randomiser (0 benchmark, 1 tests, -1 none):
+    the two ParamLayout arenas (params, buffers)."""
+    np_, nb = arena_floats(desc)
+    params = np.zeros(np_, np.float32)
+    buffers = np.zeros(nb, np.float32)
+    if lib().azb_synth_network(C.byref(desc), seed, kind, _fp(params), _fp(buffers)) != 0:
+        raise ValueError("azb_synth_network: bad network shape")
+    return params, buffers
+
+
+def synth_positions(desc: NetDesc, seed: int, B: int, first: int = 0) -> np.ndarray:
+    """B encoded positions [B][planes][area] (samples first .. first+B-1)."""
+    out = np.zeros((B, desc.planes, desc.area), np.float32)
+    if lib().azb_synth_positions(C.byref(desc), seed, first, B, _fp(out)) != 0:
+        raise ValueError("azb_synth_positions: bad network shape")
     return out
 
 

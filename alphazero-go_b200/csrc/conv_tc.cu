@@ -133,13 +133,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tma_load_2d(&mA, abuf, &sm.a_full[sa], c * C::kKc, y0);
                     if (kSplit) tma_load_2d(&mAlo, abuf + p.a_bytes, &sm.a_full[sa], c * C::kKc, y0);
                     ++ia;
-                    for (int t = 0; t < 9; ++t) {
+                    for (int t = 0; t < p.taps; ++t) {
                         const int sb = ib % p.sb;
                         if (!(ok = mbar_wait(&sm.b_empty[sb], ((ib / p.sb) & 1) ^ 1, p.err, kErrWaitProducer))) break;
                         mbar_arrive_expect_tx(&sm.b_full[sb], b_tx);
                         uint8_t* bbuf = sm.b + size_t(sb) * C::kOps * C::kBBytes;
-                        tma_load_2d(&mW, bbuf, &sm.b_full[sb], (c * 9 + t) * C::kKc, 0);
-                        if (kSplit) tma_load_2d(&mWlo, bbuf + C::kBBytes, &sm.b_full[sb], (c * 9 + t) * C::kKc, 0);
+                        tma_load_2d(&mW, bbuf, &sm.b_full[sb], (c * p.taps + t) * C::kKc, 0);
+                        if (kSplit) tma_load_2d(&mWlo, bbuf + C::kBBytes, &sm.b_full[sb], (c * p.taps + t) * C::kKc, 0);
                         ++ib;
                     }
                 }
@@ -170,12 +170,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int sa = ia % p.sa;
                     if (!(ok = mbar_wait(&sm.a_full[sa], (ia / p.sa) & 1, p.err, kErrWaitMma))) break;
                     const uint32_t abuf = a_base + uint32_t(sa) * C::kOps * p.a_bytes;
-                    for (int t = 0; t < 9; ++t) {
+                    for (int t = 0; t < p.taps; ++t) {
                         const int sb = ib % p.sb;
                         if (!(ok = mbar_wait(&sm.b_full[sb], (ib / p.sb) & 1, p.err, kErrWaitMma))) break;
                         tc_fence_after();
                         const uint32_t bbuf = b_base + uint32_t(sb) * C::kOps * C::kBBytes;
-                        const int dy = t / 3 - 1, dx = t % 3 - 1;
+                        const int tap = p.taps == 9 ? t : 4;   // one tap: the centre view, a plain GEMM
+                        const int dy = tap / 3 - 1, dx = tap % 3 - 1;
                         const uint32_t row = uint32_t(p.n + 2 + dy * (p.n + 1) + dx);
                         for (int k = 0; k < C::kSteps; ++k) {
                             const uint32_t aoff = row * 128u + uint32_t(k) * 32u;

@@ -298,18 +298,18 @@ CUtensorMap make_tensor_map(const void* base, int precision, uint64_t inner, uin
 
 // ---------------------------------------------------------------- weights
 
+int stem_k_for(const NetShape& s, int precision) { return round_up(9 * s.planes(), chunk_channels(precision)); }
+
 size_t Weights::bytes_for(const NetShape& s, int precision) {
-    const int F = s.filters, n_out = n_out_for(F), cpad = cpad_for(F, precision);
+    const int F = s.filters, n_out = n_out_for(F), cpad = cpad_for(F, precision), ks = stem_k_for(s, precision);
     const size_t A = size_t(s.area()), V = size_t(s.value_hidden);
     const size_t esz = size_t(elem_bytes(precision)), planes = precision == kTF32x3 ? 2 : 1;
     Carver c;
-    c.take(size_t(F) * s.planes() * 9 * 4);
-    c.take(size_t(F) * 4);
-    c.take(size_t(F) * 4);
-    for (int i = 0; i < 2 * s.blocks; ++i) {
+    for (int i = 0; i < 1 + 2 * s.blocks; ++i) {
         c.take(size_t(n_out) * 4);
         c.take(size_t(n_out) * 4);
-        for (size_t p = 0; p < planes; ++p) c.take(size_t(n_out) * 9 * cpad * esz);
+        const size_t k = i == 0 ? size_t(ks) : size_t(9) * cpad;
+        for (size_t p = 0; p < planes; ++p) c.take(size_t(n_out) * k * esz);
     }
     c.take(2 * size_t(F) * 4);
     c.take(8);
@@ -345,7 +345,8 @@ Weights::Weights(const NetShape& s, int precision, int device, const float* para
     const int F = s.filters, P = s.planes(), A = s.area(), V = s.value_hidden;
     n_out_ = n_out_for(F);
     cpad_ = cpad_for(F, precision);
-    const int KC = chunk_channels(precision), nchunks = cpad_ / KC, Kp = 9 * cpad_;
+    kstem_ = stem_k_for(s, precision);
+    const int KC = chunk_channels(precision), Kp = 9 * cpad_;
     const size_t esz = size_t(elem_bytes(precision));
     const bool split = precision == kTF32x3;
     auto P_ = [&](const std::string& n) { return params + L.param(n).offset; };
@@ -358,63 +359,71 @@ Weights::Weights(const NetShape& s, int precision, int device, const float* para
         std::memcpy(img.data() + off, src, bytes);
         return off;
     };
-    std::vector<size_t> offs;
-    // stem: the reference's [F][P*9] weights and its folded batch norm
-    std::vector<float> sc(size_t(std::max(F, n_out_)), 0.0f), sh(sc.size(), 0.0f);
-    const size_t o_stem_w = put(P_("stem.conv.w"), size_t(F) * P * 9 * 4);
-    fold_bn(P_("stem.bn.gamma"), P_("stem.bn.beta"), B_("stem.bn.runMean"), B_("stem.bn.runVar"), F, sc.data(), sh.data());
-    const size_t o_stem_sc = put(sc.data(), size_t(F) * 4), o_stem_sh = put(sh.data(), size_t(F) * 4);
-
     struct ConvOffs {
-        size_t scale, shift, w, w_lo;
+        size_t scale, shift, w, w_lo, k;
     };
-    std::vector<ConvOffs> co(size_t(2 * s.blocks));
-    std::vector<uint8_t> wk(size_t(n_out_) * Kp * esz), wl(split ? size_t(n_out_) * Kp * 4 : 0);
-    for (int i = 0; i < 2 * s.blocks; ++i) {
-        const std::string pre = "block" + std::to_string(i / 2) + (i % 2 ? ".conv2" : ".conv1");
-        const std::string bn = "block" + std::to_string(i / 2) + (i % 2 ? ".bn2" : ".bn1");
+    std::vector<ConvOffs> co(size_t(1 + 2 * s.blocks));
+    std::vector<float> sc(size_t(n_out_), 0.0f), sh(sc.size(), 0.0f);
+    // One conv in kernel layout: [n_out][k] elements, column col(o, ci, t)
+    // for the reference's w[o][ci*9 + t] (src/layers.cpp:44-45); folded BN
+    // scale/shift padded with zeros to n_out.
+    auto pack = [&](size_t i, const std::string& wname, const std::string& bn, int cin, size_t k, auto col) {
         std::fill(sc.begin(), sc.end(), 0.0f);
         std::fill(sh.begin(), sh.end(), 0.0f);
         fold_bn(P_(bn + ".gamma"), P_(bn + ".beta"), B_(bn + ".runMean"), B_(bn + ".runVar"), F, sc.data(), sh.data());
-        co[size_t(i)].scale = put(sc.data(), size_t(n_out_) * 4);
-        co[size_t(i)].shift = put(sh.data(), size_t(n_out_) * 4);
-        // Kernel order: K index (chunk*9 + tap)*KC + channel-in-chunk; the
-        // reference's is channel*9 + tap (src/layers.cpp:44-45).
-        const float* w = P_(pre + ".w");
-        std::fill(wk.begin(), wk.end(), 0);
-        std::fill(wl.begin(), wl.end(), 0);
+        co[i].scale = put(sc.data(), size_t(n_out_) * 4);
+        co[i].shift = put(sh.data(), size_t(n_out_) * 4);
+        co[i].k = k;
+        std::vector<uint8_t> wk(size_t(n_out_) * k * esz, 0), wl(split ? size_t(n_out_) * k * 4 : 0, 0);
+        const float* w = P_(wname);
         for (int o = 0; o < F; ++o)
-            for (int ci = 0; ci < F; ++ci)
+            for (int ci = 0; ci < cin; ++ci)
                 for (int t = 0; t < 9; ++t) {
-                    const float v = w[(size_t(o) * F + ci) * 9 + t];
-                    const size_t k = size_t(o) * Kp + size_t((ci / KC) * 9 + t) * KC + ci % KC;
+                    const float v = w[(size_t(o) * cin + ci) * 9 + t];
+                    const size_t at = size_t(o) * k + col(ci, t);
                     if (precision == kBF16) {
                         const uint16_t h = bf16_rne(v);
-                        std::memcpy(wk.data() + k * 2, &h, 2);
+                        std::memcpy(wk.data() + at * 2, &h, 2);
                     } else {
                         const float hi = tf32_rna(v);
-                        std::memcpy(wk.data() + k * 4, &hi, 4);
+                        std::memcpy(wk.data() + at * 4, &hi, 4);
                         if (split) {
                             const float lo = v - hi;
-                            std::memcpy(wl.data() + k * 4, &lo, 4);
+                            std::memcpy(wl.data() + at * 4, &lo, 4);
                         }
                     }
                 }
-        (void)nchunks;
-        co[size_t(i)].w = put(wk.data(), wk.size());
-        co[size_t(i)].w_lo = split ? put(wl.data(), wl.size()) : 0;
+        co[i].w = put(wk.data(), wk.size());
+        co[i].w_lo = split ? put(wl.data(), wl.size()) : 0;
+    };
+    // The stem as a one-tap GEMM over its packed operand: column t*P + p.
+    pack(0, "stem.conv.w", "stem.bn", P, size_t(kstem_), [&](int ci, int t) { return size_t(t) * P + ci; });
+    // The tower: K index (chunk*9 + tap)*KC + channel-in-chunk.
+    for (int i = 0; i < 2 * s.blocks; ++i) {
+        const std::string blk = "block" + std::to_string(i / 2);
+        pack(size_t(1 + i), blk + (i % 2 ? ".conv2.w" : ".conv1.w"), blk + (i % 2 ? ".bn2" : ".bn1"), F, size_t(Kp),
+             [&](int ci, int t) { return size_t((ci / KC) * 9 + t) * KC + ci % KC; });
     }
-    // heads
+    // heads: the FC weights input-major ([in][out]) so the head kernel's
+    // thread-per-output loops read them coalesced.
+    auto transpose = [](const float* w, int out, int in) {
+        std::vector<float> t(size_t(out) * in);
+        for (int o = 0; o < out; ++o)
+            for (int i = 0; i < in; ++i) t[size_t(i) * out + o] = w[size_t(o) * in + i];
+        return t;
+    };
     std::vector<float> hsc(2), hsh(2);
     const size_t o_pw = put(P_("policy.conv.w"), size_t(2) * F * 4);
     fold_bn(P_("policy.bn.gamma"), P_("policy.bn.beta"), B_("policy.bn.runMean"), B_("policy.bn.runVar"), 2, hsc.data(), hsh.data());
     const size_t o_psc = put(hsc.data(), 8), o_psh = put(hsh.data(), 8);
-    const size_t o_fcw = put(P_("policy.fc.w"), size_t(A + 1) * 2 * A * 4);
+    const std::vector<float> fct = transpose(P_("policy.fc.w"), A + 1, 2 * A);
+    const size_t o_fcw = put(fct.data(), fct.size() * 4);
     const size_t o_fcb = put(P_("policy.fc.b"), size_t(A + 1) * 4);
     const size_t o_vw = put(P_("value.conv.w"), size_t(F) * 4);
     fold_bn(P_("value.bn.gamma"), P_("value.bn.beta"), B_("value.bn.runMean"), B_("value.bn.runVar"), 1, hsc.data(), hsh.data());
     const size_t o_vsc = put(hsc.data(), 4), o_vsh = put(hsh.data(), 4);
-    const size_t o_v1w = put(P_("value.fc1.w"), size_t(V) * A * 4);
+    const std::vector<float> v1t = transpose(P_("value.fc1.w"), V, A);
+    const size_t o_v1w = put(v1t.data(), v1t.size() * 4);
     const size_t o_v1b = put(P_("value.fc1.b"), size_t(V) * 4);
     const size_t o_v2w = put(P_("value.fc2.w"), size_t(V) * 4);
     const size_t o_v2b = put(P_("value.fc2.b"), 4);
@@ -431,22 +440,21 @@ Weights::Weights(const NetShape& s, int precision, int device, const float* para
     const cudaError_t e = cudaMemcpy(arena_, img.data(), bytes_, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
         cudaFree(arena_);
+        arena_ = nullptr;
         check(e, "upload weights");
     }
     auto at = [&](size_t off) { return reinterpret_cast<float*>(static_cast<uint8_t*>(arena_) + off); };
-    stem_w_ = at(o_stem_w);
-    stem_scale_ = at(o_stem_sc);
-    stem_shift_ = at(o_stem_sh);
     convs_.resize(co.size());
     for (size_t i = 0; i < co.size(); ++i) {
         Conv& cv = convs_[i];
         cv.scale = at(co[i].scale);
         cv.shift = at(co[i].shift);
         cv.w = at(co[i].w);
-        cv.map_w = make_tensor_map(cv.w, precision, uint64_t(Kp), uint64_t(n_out_), uint32_t(KC), uint32_t(n_out_));
+        cv.map_w = make_tensor_map(cv.w, precision, uint64_t(co[i].k), uint64_t(n_out_), uint32_t(KC), uint32_t(n_out_));
         if (split) {
             cv.w_lo = at(co[i].w_lo);
-            cv.map_w_lo = make_tensor_map(cv.w_lo, precision, uint64_t(Kp), uint64_t(n_out_), uint32_t(KC), uint32_t(n_out_));
+            cv.map_w_lo = make_tensor_map(cv.w_lo, precision, uint64_t(co[i].k), uint64_t(n_out_), uint32_t(KC),
+                                          uint32_t(n_out_));
         } else {
             cv.map_w_lo = cv.map_w;
         }
@@ -461,12 +469,12 @@ Weights::Weights(const NetShape& s, int precision, int device, const float* para
     head_.pol_w = at(o_pw);
     head_.pol_scale = at(o_psc);
     head_.pol_shift = at(o_psh);
-    head_.fc_w = at(o_fcw);
+    head_.fc_wt = at(o_fcw);
     head_.fc_b = at(o_fcb);
     head_.val_w = at(o_vw);
     head_.val_scale = at(o_vsc);
     head_.val_shift = at(o_vsh);
-    head_.v1_w = at(o_v1w);
+    head_.v1_wt = at(o_v1w);
     head_.v1_b = at(o_v1b);
     head_.v2_w = at(o_v2w);
     head_.v2_b = at(o_v2b);
@@ -493,6 +501,9 @@ size_t Workspace::bytes_for(const NetShape& s, int precision, int max_batch) {
     const size_t A = size_t(s.area()), L = size_t(s.actions()), B = size_t(max_batch);
     Carver c;
     c.take(B * s.planes() * A * 4);
+    const size_t ks = size_t(stem_k_for(s, precision));
+    c.take(rows * ks * esz);
+    if (precision == kTF32x3) c.take(rows * ks * 4);
     for (int i = 0; i < 3; ++i) c.take(rows * cpad * esz);
     if (precision == kTF32x3)
         for (int i = 0; i < 3; ++i) c.take(rows * cpad * 4);
@@ -524,6 +535,9 @@ Workspace::Workspace(const Weights& w, int max_batch) : max_batch_(max_batch) {
     Carver c;
     auto at = [&](size_t off) { return static_cast<uint8_t*>(arena_) + off; };
     stage = reinterpret_cast<float*>(at(c.take(B * s.planes() * A * 4)));
+    const size_t ks = size_t(w.kstem());
+    stem_in = at(c.take(rows * ks * esz));
+    if (precision == kTF32x3) stem_in_lo = at(c.take(rows * ks * 4));
     for (int i = 0; i < 3; ++i) trunk[i] = at(c.take(rows * cpad * esz));
     if (precision == kTF32x3)
         for (int i = 0; i < 3; ++i) trunk_lo[i] = at(c.take(rows * cpad * 4));
@@ -533,6 +547,8 @@ Workspace::Workspace(const Weights& w, int max_batch) : max_batch_(max_batch) {
     probs = reinterpret_cast<float*>(at(c.take(B * L * 4)));
     err = reinterpret_cast<int*>(at(c.take(16)));
     const uint32_t KC = uint32_t(chunk_channels(precision));
+    map_stem = make_tensor_map(stem_in, precision, ks, rows, KC, uint32_t(fr.halo));
+    map_stem_lo = precision == kTF32x3 ? make_tensor_map(stem_in_lo, precision, ks, rows, KC, uint32_t(fr.halo)) : map_stem;
     for (int i = 0; i < 3; ++i) {
         map[i] = make_tensor_map(trunk[i], precision, cpad, rows, KC, uint32_t(fr.halo));
         map_lo[i] = precision == kTF32x3 ? make_tensor_map(trunk_lo[i], precision, cpad, rows, KC, uint32_t(fr.halo)) : map[i];
@@ -570,44 +586,48 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
     st.P = sh.planes();
     st.n = sh.board;
     st.S = fr.S;
-    st.F = sh.filters;
-    st.ld = w.cpad();
-    st.w = w.stem_w();
-    st.scale = w.stem_scale();
-    st.shift = w.stem_shift();
-    st.out = ws.trunk[0];
-    st.out_lo = ws.trunk_lo[0];
-    check(launch_stem(st, precision, s), "stem");
+    st.ld = w.kstem();
+    st.out = ws.stem_in;
+    st.out_lo = ws.stem_in_lo;
+    check(launch_stem_im2col(st, precision, s), "stem operand");
 
     ConvArgs a{};
     a.n = sh.board;
     a.S = fr.S;
     a.rows = B * fr.S;
     a.ntiles = (a.rows + 127) / 128;
-    a.nchunks = w.cpad() / chunk_channels(precision);
     a.ld = w.cpad();
     a.halo_rows = fr.halo;
     a.a_bytes = (fr.halo * 128 + 1023) / 1024 * 1024;
     conv_smem_bytes(w.n_out(), precision, fr.halo, &a.sa, &a.sb);
     a.base_offset_mode = 0;
     a.err = ws.err;
+    auto conv = [&](int index, const CUtensorMap& in, const CUtensorMap& in_lo, int dst, const void* skip,
+                    const void* skip_lo, int taps, int nchunks, int timer_slot) {
+        const Weights::Conv& cv = w.conv(index);
+        ConvMaps m{in, in_lo, cv.map_w, cv.map_w_lo};
+        a.taps = taps;
+        a.nchunks = nchunks;
+        a.out = ws.trunk[dst];
+        a.out_lo = ws.trunk_lo[dst];
+        a.skip = skip;
+        a.skip_lo = skip_lo;
+        a.scale = cv.scale;
+        a.shift = cv.shift;
+        if (timer && timer->enabled && timer_slot >= 0) check(cudaEventRecord(timer->begin[size_t(timer_slot)], s), "event");
+        check(launch_conv(m, a, w.n_out(), precision, dev.sms, s), "conv");
+        if (timer && timer->enabled && timer_slot >= 0) check(cudaEventRecord(timer->end[size_t(timer_slot)], s), "event");
+    };
+    // The stem: conv -> BN -> ReLU as one tap over the packed operand.
+    conv(0, ws.map_stem, ws.map_stem_lo, 0, nullptr, nullptr, 1, w.kstem() / chunk_channels(precision), -1);
+    // The tower: conv -> BN -> ReLU -> conv -> BN -> + skip -> ReLU per block,
+    // rotating through three frame buffers.
+    const int tower_chunks = w.cpad() / chunk_channels(precision);
     int x = 0;
     for (int i = 0; i < sh.blocks; ++i) {
         const int mid = (x + 1) % 3, out = (x + 2) % 3;
-        for (int half = 0; half < 2; ++half) {
-            const Weights::Conv& cv = w.conv(2 * i + half);
-            const int in = half == 0 ? x : mid, dst = half == 0 ? mid : out;
-            ConvMaps m{ws.map[in], ws.map_lo[in], cv.map_w, cv.map_w_lo};
-            a.out = ws.trunk[dst];
-            a.out_lo = ws.trunk_lo[dst];
-            a.skip = half == 0 ? nullptr : ws.trunk[x];
-            a.skip_lo = half == 0 ? nullptr : ws.trunk_lo[x];
-            a.scale = cv.scale;
-            a.shift = cv.shift;
-            if (timer && timer->enabled) check(cudaEventRecord(timer->begin[size_t(2 * i + half)], s), "event");
-            check(launch_conv(m, a, w.n_out(), precision, dev.sms, s), "conv");
-            if (timer && timer->enabled) check(cudaEventRecord(timer->end[size_t(2 * i + half)], s), "event");
-        }
+        conv(1 + 2 * i, ws.map[x], ws.map_lo[x], mid, nullptr, nullptr, 9, tower_chunks, 2 * i);
+        conv(2 + 2 * i, ws.map[mid], ws.map_lo[mid], out, ws.trunk[x], ws.trunk_lo[x], 9, tower_chunks, 2 * i + 1);
         x = out;
     }
     HeadArgs h = w.head_args();

@@ -83,10 +83,9 @@ public:
     int cpad() const { return cpad_; }      // channels per stored pixel row
     int n_out() const { return n_out_; }    // MMA N (filters rounded up)
     size_t bytes() const { return bytes_; }
-    const float* stem_w() const { return stem_w_; }
-    const float* stem_scale() const { return stem_scale_; }
-    const float* stem_shift() const { return stem_shift_; }
-    const Conv& conv(int i) const { return convs_[static_cast<size_t>(i)]; }   // 2*block + (0|1)
+    int kstem() const { return kstem_; }    // the stem operand's K: 9*planes rounded up to whole chunks
+    // 0: the stem (one-tap GEMM over the packed operand); 1 + 2*block + (0|1): the tower.
+    const Conv& conv(int i) const { return convs_[static_cast<size_t>(i)]; }
     HeadArgs head_args() const { return head_; }   // weights only
 
     // Bytes of the device arena for these shapes (the memory checks).
@@ -94,10 +93,9 @@ public:
 
 private:
     NetShape shape_;
-    int precision_, device_, cpad_, n_out_;
+    int precision_, device_, cpad_, n_out_, kstem_;
     size_t bytes_ = 0;
     void* arena_ = nullptr;
-    const float *stem_w_ = nullptr, *stem_scale_ = nullptr, *stem_shift_ = nullptr;
     std::vector<Conv> convs_;
     HeadArgs head_{};
 };
@@ -114,6 +112,8 @@ public:
     static size_t bytes_for(const NetShape& s, int precision, int max_batch);
 
     float* stage = nullptr;       // [max_batch][planes][area] fp32 input
+    void* stem_in = nullptr;      // frame rows x kstem: the stem's packed operand
+    void* stem_in_lo = nullptr;   // split mode
     void* trunk[3] = {};          // frame rows x cpad
     void* trunk_lo[3] = {};       // split mode
     float* logits = nullptr;      // [max_batch][actions]
@@ -122,6 +122,7 @@ public:
     float* probs = nullptr;       // [max_batch][actions]
     int* err = nullptr;           // kernel error word
     CUtensorMap map[3]{}, map_lo[3]{};
+    CUtensorMap map_stem{}, map_stem_lo{};
 
 private:
     int max_batch_;

@@ -53,6 +53,7 @@ struct ConvArgs {
     int rows;          // B * S: frame rows of this pass
     int ntiles;        // ceil(rows / 128)
     int nchunks;       // input channels / chunk_channels
+    int taps;          // 9: the 3x3 views of the halo; 1: the centre view only (a plain GEMM over K)
     int ld;            // channels per stored pixel row (input, output and skip)
     int halo_rows;     // 128 + 2(n+2)
     int a_bytes;       // one halo buffer, rounded up to 1024
@@ -78,16 +79,15 @@ size_t conv_smem_bytes(int n_out, int precision, int halo_rows, int* sa, int* sb
 // Enqueues the conv on `s`; grid = min(ntiles, sms).
 cudaError_t launch_conv(const ConvMaps& maps, const ConvArgs& a, int n_out, int precision, int sms, cudaStream_t s);
 
-// The stem: 3x3 conv from the [B][P][A] fp32 input straight to frame rows,
-// with its batch norm and ReLU (SIMT; the stem is < 0.2% of the FLOPs).
+// The stem's packed operand: the [B][P][A] fp32 input unfolded into frame
+// rows of K = 9*P values (column t*P + p), ld elements apart. The stem conv
+// itself then runs as a one-tap GEMM on the tensor-core kernel.
 struct StemArgs {
     const float* in;    // [B][P][A]
-    int B, P, n, S, F, ld;
-    const float* w;     // [F][P*9], the reference's order
-    const float* scale; const float* shift;
+    int B, P, n, S, ld;
     void* out; void* out_lo;
 };
-cudaError_t launch_stem(const StemArgs& a, int precision, cudaStream_t s);
+cudaError_t launch_stem_im2col(const StemArgs& a, int precision, cudaStream_t s);
 
 // The fused heads: policy 1x1 conv + BN + ReLU + FC, value 1x1 conv + BN +
 // ReLU + FC + ReLU + FC + tanh, ownership 1x1 conv + BN + tanh, and the
@@ -97,10 +97,10 @@ struct HeadArgs {
     int ld, n, S, A, F, V, B, ownership;
     const float* pol_w;     // [2][F]
     const float* pol_scale; const float* pol_shift;   // [2]
-    const float* fc_w; const float* fc_b;             // [A+1][2A], [A+1]
+    const float* fc_wt; const float* fc_b;            // input-major [2A][A+1], [A+1]
     const float* val_w;     // [F]
     const float* val_scale; const float* val_shift;   // [1]
-    const float* v1_w; const float* v1_b;             // [V][A], [V]
+    const float* v1_wt; const float* v1_b;            // input-major [A][V], [V]
     const float* v2_w; const float* v2_b;             // [V], [1]
     const float* own_w; const float* own_scale; const float* own_shift;
     float* logits;      // [B][A+1]

@@ -18,79 +18,44 @@ unsigned blocks_for(size_t count, int threads) {
 
 // ---------------------------------------------------------------- the stem
 
-// One thread: one pixel, 8 consecutive output channels. Threads of a warp
-// share the channel group (weight loads are warp-uniform) and walk
-// consecutive pixels of the same plane (input loads coalesce). The sum over
-// k = ci*9 + ky*3 + kx runs in the reference's order; in the tf32 modes each
-// product and sum is rounded on its own as the naive backend does
-// (src/backend.cpp:115-140), so the stem matches it bit for bit.
+// The stem's input as a packed GEMM operand: for every board point, the
+// 9*P values its 3x3 window reads (tap-major: column t*P + p, t = ky*3 + kx,
+// 0 off the board), in the point's frame row. The stem then runs on the
+// tensor cores as a one-tap GEMM with K = 9*P (rounded up to whole 128-byte
+// chunks), instead of a 3x3 convolution over P channels padded to a chunk.
+// Frame padding rows and the columns past 9*P are never written (zero since
+// the buffer was allocated).
 template <int kMode>
-__global__ void __launch_bounds__(256) stem_kernel(const StemArgs a) {
-    const int A = a.n * a.n;
-    const size_t pixels = size_t(a.B) * A;
-    const int groups = a.F / 8;
-    const size_t total = pixels * groups;
+__global__ void __launch_bounds__(256) stem_im2col_kernel(const StemArgs a) {
+    const int A = a.n * a.n, K = 9 * a.P;
+    const size_t total = size_t(a.B) * A * K;
     for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
-        const int g = static_cast<int>(i / pixels);
-        const size_t pix = i % pixels;
-        const int b = static_cast<int>(pix / A), p = static_cast<int>(pix % A);
-        const int y = p / a.n, x = p % a.n;
-        float acc[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
-        const float* in = a.in + size_t(b) * a.P * A;
-        const float* w = a.w + size_t(g) * 8 * a.P * 9;
-        for (int ci = 0; ci < a.P; ++ci) {
-            for (int t = 0; t < 9; ++t) {
-                const int sy = y + t / 3 - 1, sx = x + t % 3 - 1;
-                const float v = (sy < 0 || sy >= a.n || sx < 0 || sx >= a.n) ? 0.0f : __ldg(in + size_t(ci) * A + sy * a.n + sx);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float wv = __ldg(w + size_t(j) * a.P * 9 + ci * 9 + t);
-                    if (kMode == kBF16) acc[j] = fmaf(wv, v, acc[j]);
-                    else acc[j] = __fadd_rn(acc[j], __fmul_rn(wv, v));
-                }
-            }
-        }
-        const size_t row = size_t(b) * a.S + size_t(y + 1) * (a.n + 1) + x;
-        const int c0 = g * 8;
-        float o[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float yv = __fadd_rn(__fmul_rn(__ldg(a.scale + c0 + j), acc[j]), __ldg(a.shift + c0 + j));
-            o[j] = yv > 0.0f ? yv : 0.0f;
-        }
+        const size_t pix = i / K;
+        const int k = static_cast<int>(i % K);
+        const int b = static_cast<int>(pix / A), pt = static_cast<int>(pix % A);
+        const int t = k / a.P, pl = k % a.P;
+        const int y = pt / a.n + t / 3 - 1, x = pt % a.n + t % 3 - 1;
+        const float v = (y < 0 || y >= a.n || x < 0 || x >= a.n)
+                            ? 0.0f
+                            : __ldg(a.in + (size_t(b) * a.P + pl) * A + y * a.n + x);
+        const size_t row = size_t(b) * a.S + size_t(pt / a.n + 1) * (a.n + 1) + pt % a.n;
+        const size_t off = row * a.ld + k;
         if (kMode == kBF16) {
-            uint4 w4;
-            __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&w4);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) h2[e] = __floats2bfloat162_rn(o[2 * e], o[2 * e + 1]);
-            *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + row * a.ld + c0) = w4;
+            static_cast<__nv_bfloat16*>(a.out)[off] = __float2bfloat16_rn(v);
         } else if (kMode == kTF32x3) {
-            float4* hi = reinterpret_cast<float4*>(static_cast<float*>(a.out) + row * a.ld + c0);
-            float4* lo = reinterpret_cast<float4*>(static_cast<float*>(a.out_lo) + row * a.ld + c0);
-            float h[8], l[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                h[j] = to_tf32(o[j]);
-                l[j] = __fsub_rn(o[j], h[j]);
-            }
-            hi[0] = make_float4(h[0], h[1], h[2], h[3]);
-            hi[1] = make_float4(h[4], h[5], h[6], h[7]);
-            lo[0] = make_float4(l[0], l[1], l[2], l[3]);
-            lo[1] = make_float4(l[4], l[5], l[6], l[7]);
+            const float h = to_tf32(v);
+            static_cast<float*>(a.out)[off] = h;
+            static_cast<float*>(a.out_lo)[off] = __fsub_rn(v, h);
         } else {
-            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + row * a.ld + c0);
-            dst[0] = make_float4(o[0], o[1], o[2], o[3]);
-            dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+            static_cast<float*>(a.out)[off] = v;
         }
     }
 }
 
 // --------------------------------------------------------------- the heads
 
-constexpr int kHeadSamples = 4;    // samples per CTA: the FC weights are read once per group
-constexpr int kHeadThreads = 256;
+constexpr int kHeadSamples = 8;    // samples per CTA: each FC weight is read once per group
+constexpr int kHeadThreads = 512;
 constexpr int kHeadWarps = kHeadThreads / 32;
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -141,18 +106,33 @@ __device__ __forceinline__ float bn_relu(float z, float scale, float shift) {
     return y > 0.0f ? y : 0.0f;
 }
 
-// One CTA: kHeadSamples samples. Phase 1 reads each sample's trunk once
-// (a warp per pixel, 16-byte loads across the channels) and produces the
-// head convolutions' outputs after batch norm: the policy features in the
-// reference's flatten order c*A + p (src/network.cpp:278-285), the value
-// features, and the ownership map. Phase 2 runs the FC layers from shared
-// memory with each weight row read once per group (a warp per output row,
-// coalesced), then tanh for the value and the softmax over A+1 moves.
+size_t head_smem_bytes(int F, int A, int V) {
+    return (size_t(4) * F + size_t(kHeadSamples) * (2 * A + A + V + A + 1)) * sizeof(float);
+}
+
+// One CTA: kHeadSamples samples.
+//  1. Each thread takes whole board points: it reads the point's F trunk
+//     channels with 16-byte loads (independent, so many are in flight) and
+//     sums the policy, value and ownership 1x1 convolutions in channel
+//     order, then applies their batch norms: the policy features land in the
+//     reference's flatten order c*A + p (src/network.cpp:278-285).
+//  2. Each thread owns one FC output (a policy logit or a value hidden unit)
+//     for all the group's samples, summing over the inputs in order; the FC
+//     weights are stored input-major, so a warp's loads of one input's
+//     weights are one coalesced line.
+//  3. One warp per sample: the value FC2 and tanh, and the softmax over
+//     the A+1 logits.
+// Every output is one thread's fixed-order sum over its own sample's data:
+// the results do not depend on the batch or on where a sample sits in it.
 template <int kMode>
 __global__ void __launch_bounds__(kHeadThreads) heads_kernel(const HeadArgs a) {
     extern __shared__ float hs[];
-    const int A = a.A, V = a.V, L = A + 1;
-    float* pol = hs;                               // [G][2A]
+    const int A = a.A, V = a.V, L = A + 1, F = a.F;
+    float* wpol0 = hs;
+    float* wpol1 = wpol0 + F;
+    float* wval = wpol1 + F;
+    float* wown = wval + F;
+    float* pol = wown + F;                         // [G][2A]
     float* val = pol + kHeadSamples * 2 * A;       // [G][A]
     float* hid = val + kHeadSamples * A;           // [G][V]
     float* lg = hid + kHeadSamples * V;            // [G][A+1]
@@ -161,83 +141,73 @@ __global__ void __launch_bounds__(kHeadThreads) heads_kernel(const HeadArgs a) {
     const int G = min(kHeadSamples, a.B - b0);
     constexpr int W = TrunkVec<kMode>::kWidth;
 
+    for (int i = threadIdx.x; i < F; i += kHeadThreads) {
+        wpol0[i] = a.pol_w[i];
+        wpol1[i] = a.pol_w[F + i];
+        wval[i] = a.val_w[i];
+        wown[i] = a.ownership ? a.own_w[i] : 0.0f;
+    }
+    __syncthreads();
     const float ps0 = a.pol_scale[0], ps1 = a.pol_scale[1], ph0 = a.pol_shift[0], ph1 = a.pol_shift[1];
     const float vs = a.val_scale[0], vh = a.val_shift[0];
     const float os = a.ownership ? a.own_scale[0] : 0.0f, oh = a.ownership ? a.own_shift[0] : 0.0f;
 
-    for (int item = warp; item < G * A; item += kHeadWarps) {
+    for (int item = threadIdx.x; item < G * A; item += kHeadThreads) {
         const int g = item / A, p = item % A;
-        const int b = b0 + g;
-        const size_t row = size_t(b) * a.S + size_t(p / a.n + 1) * (a.n + 1) + p % a.n;
+        const size_t row = size_t(b0 + g) * a.S + size_t(p / a.n + 1) * (a.n + 1) + p % a.n;
         float z0 = 0.0f, z1 = 0.0f, zv = 0.0f, zo = 0.0f;
-        for (int c = lane * W; c < a.F; c += 32 * W) {
+#pragma unroll 4
+        for (int c = 0; c < F; c += W) {
             float f[W];
             TrunkVec<kMode>::load(a, row * a.ld + c, f);
 #pragma unroll
             for (int e = 0; e < W; ++e) {
-                z0 = fmaf(__ldg(a.pol_w + c + e), f[e], z0);
-                z1 = fmaf(__ldg(a.pol_w + a.F + c + e), f[e], z1);
-                zv = fmaf(__ldg(a.val_w + c + e), f[e], zv);
-                if (a.ownership) zo = fmaf(__ldg(a.own_w + c + e), f[e], zo);
+                z0 = fmaf(wpol0[c + e], f[e], z0);
+                z1 = fmaf(wpol1[c + e], f[e], z1);
+                zv = fmaf(wval[c + e], f[e], zv);
+                zo = fmaf(wown[c + e], f[e], zo);
             }
         }
-        z0 = warp_sum(z0);
-        z1 = warp_sum(z1);
-        zv = warp_sum(zv);
-        if (a.ownership) zo = warp_sum(zo);
-        if (lane == 0) {
-            pol[g * 2 * A + p] = bn_relu(z0, ps0, ph0);
-            pol[g * 2 * A + A + p] = bn_relu(z1, ps1, ph1);
-            val[g * A + p] = bn_relu(zv, vs, vh);
-            if (a.ownership && a.ownership_out)
-                a.ownership_out[size_t(b) * A + p] = tanhf(__fadd_rn(__fmul_rn(os, zo), oh));
+        pol[g * 2 * A + p] = bn_relu(z0, ps0, ph0);
+        pol[g * 2 * A + A + p] = bn_relu(z1, ps1, ph1);
+        val[g * A + p] = bn_relu(zv, vs, vh);
+        if (a.ownership && a.ownership_out)
+            a.ownership_out[size_t(b0 + g) * A + p] = tanhf(__fadd_rn(__fmul_rn(os, zo), oh));
+    }
+    __syncthreads();
+
+    for (int o = threadIdx.x; o < L + V; o += kHeadThreads) {
+        float acc[kHeadSamples];
+#pragma unroll
+        for (int g = 0; g < kHeadSamples; ++g) acc[g] = 0.0f;
+        const bool policy = o < L;
+        const int n_in = policy ? 2 * A : A, out = policy ? o : o - L, stride = policy ? L : V;
+        const float* wt = policy ? a.fc_wt : a.v1_wt;      // [n_in][stride]
+        const float* x = policy ? pol : val;
+        const int ld = policy ? 2 * A : A;
+#pragma unroll 4
+        for (int i = 0; i < n_in; ++i) {
+            const float wv = __ldg(wt + size_t(i) * stride + out);
+#pragma unroll
+            for (int g = 0; g < kHeadSamples; ++g) acc[g] = fmaf(wv, x[g * ld + i], acc[g]);
+        }
+        if (policy) {
+            const float bias = __ldg(a.fc_b + out);
+            for (int g = 0; g < G; ++g) {
+                const float l = __fadd_rn(acc[g], bias);
+                lg[g * L + out] = l;
+                a.logits[size_t(b0 + g) * L + out] = l;
+            }
+        } else {
+            const float bias = __ldg(a.v1_b + out);
+            for (int g = 0; g < G; ++g) {
+                const float h = __fadd_rn(acc[g], bias);
+                hid[g * V + out] = h > 0.0f ? h : 0.0f;
+            }
         }
     }
     __syncthreads();
 
-    // policy FC: logits[g][o] = sum_i pol[g][i] * fc_w[o][i] + fc_b[o]
-    for (int o = warp; o < L; o += kHeadWarps) {
-        float acc[kHeadSamples] = {0.0f, 0.0f, 0.0f, 0.0f};
-        const float* wr = a.fc_w + size_t(o) * 2 * A;
-        for (int i = lane; i < 2 * A; i += 32) {
-            const float wv = __ldg(wr + i);
-#pragma unroll
-            for (int g = 0; g < kHeadSamples; ++g)
-                if (g < G) acc[g] = fmaf(wv, pol[g * 2 * A + i], acc[g]);
-        }
-#pragma unroll
-        for (int g = 0; g < kHeadSamples; ++g) acc[g] = warp_sum(acc[g]);
-        if (lane == 0) {
-            const float bias = __ldg(a.fc_b + o);
-            for (int g = 0; g < G; ++g) {
-                const float l = __fadd_rn(acc[g], bias);
-                lg[g * L + o] = l;
-                a.logits[size_t(b0 + g) * L + o] = l;
-            }
-        }
-    }
-    // value FC1 + ReLU
-    for (int v = warp; v < V; v += kHeadWarps) {
-        float acc[kHeadSamples] = {0.0f, 0.0f, 0.0f, 0.0f};
-        const float* wr = a.v1_w + size_t(v) * A;
-        for (int i = lane; i < A; i += 32) {
-            const float wv = __ldg(wr + i);
-#pragma unroll
-            for (int g = 0; g < kHeadSamples; ++g)
-                if (g < G) acc[g] = fmaf(wv, val[g * A + i], acc[g]);
-        }
-#pragma unroll
-        for (int g = 0; g < kHeadSamples; ++g) acc[g] = warp_sum(acc[g]);
-        if (lane == 0) {
-            const float bias = __ldg(a.v1_b + v);
-            for (int g = 0; g < G; ++g) {
-                const float h = __fadd_rn(acc[g], bias);
-                hid[g * V + v] = h > 0.0f ? h : 0.0f;
-            }
-        }
-    }
-    __syncthreads();
-    // value FC2 + tanh, and the softmax over the A+1 logits: one warp per sample.
     for (int g = warp; g < G; g += kHeadWarps) {
         float acc = 0.0f;
         for (int i = lane; i < V; i += 32) acc = fmaf(__ldg(a.v2_w + i), hid[g * V + i], acc);
@@ -288,15 +258,14 @@ __global__ void bounded_wait_probe(int* err, unsigned long long limit_ns) {
 
 } // namespace
 
-cudaError_t launch_stem(const StemArgs& a, int precision, cudaStream_t s) {
-    if (a.F % 8 != 0) return cudaErrorInvalidValue;
-    const size_t total = size_t(a.B) * a.n * a.n * (a.F / 8);
+cudaError_t launch_stem_im2col(const StemArgs& a, int precision, cudaStream_t s) {
+    const size_t total = size_t(a.B) * a.n * a.n * 9 * a.P;
     if (total == 0) return cudaSuccess;
     const unsigned grid = blocks_for(total, 256);
     switch (precision) {
-        case kTF32: stem_kernel<kTF32><<<grid, 256, 0, s>>>(a); break;
-        case kTF32x3: stem_kernel<kTF32x3><<<grid, 256, 0, s>>>(a); break;
-        case kBF16: stem_kernel<kBF16><<<grid, 256, 0, s>>>(a); break;
+        case kTF32: stem_im2col_kernel<kTF32><<<grid, 256, 0, s>>>(a); break;
+        case kTF32x3: stem_im2col_kernel<kTF32x3><<<grid, 256, 0, s>>>(a); break;
+        case kBF16: stem_im2col_kernel<kBF16><<<grid, 256, 0, s>>>(a); break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
@@ -306,14 +275,25 @@ cudaError_t launch_heads(const HeadArgs& a, int precision, cudaStream_t s) {
     if (a.B <= 0) return cudaSuccess;
     const int W = precision == kBF16 ? 8 : 4;
     if (a.F % W != 0) return cudaErrorInvalidValue;
-    const size_t smem = size_t(kHeadSamples) * (2 * a.A + a.A + a.V + a.A + 1) * sizeof(float);
+    const size_t smem = head_smem_bytes(a.F, a.A, a.V);
     const unsigned grid = static_cast<unsigned>((a.B + kHeadSamples - 1) / kHeadSamples);
+    cudaError_t e = cudaSuccess;
     switch (precision) {
-        case kTF32: heads_kernel<kTF32><<<grid, kHeadThreads, smem, s>>>(a); break;
-        case kTF32x3: heads_kernel<kTF32x3><<<grid, kHeadThreads, smem, s>>>(a); break;
-        case kBF16: heads_kernel<kBF16><<<grid, kHeadThreads, smem, s>>>(a); break;
+        case kTF32:
+            e = cudaFuncSetAttribute(heads_kernel<kTF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+            if (e == cudaSuccess) heads_kernel<kTF32><<<grid, kHeadThreads, smem, s>>>(a);
+            break;
+        case kTF32x3:
+            e = cudaFuncSetAttribute(heads_kernel<kTF32x3>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+            if (e == cudaSuccess) heads_kernel<kTF32x3><<<grid, kHeadThreads, smem, s>>>(a);
+            break;
+        case kBF16:
+            e = cudaFuncSetAttribute(heads_kernel<kBF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+            if (e == cudaSuccess) heads_kernel<kBF16><<<grid, kHeadThreads, smem, s>>>(a);
+            break;
         default: return cudaErrorInvalidValue;
     }
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 

@@ -1,0 +1,411 @@
+#!/usr/bin/env python
+"""Benchmark: 19x19 network positions/sec on B200 (one process per GPU).
+
+Workload ("C4"): a 19x19 board, 20 residual blocks
+of 256 filters, value_hidden 256, one history position (4 planes), batch
+1024 per GPU, bf16 weights and activations with fp32 accumulation. Weights
+are the reference's seeded Network(cfg, 1) with the benchmark's batch-norm
+statistics; inputs are seeded synthetic positions (stones occupied with
+p = 0.4, colours 50/50). One "step" is one forward pass over the batch.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl engine|reference]
+
+For N > 1 the driver launches one rank per GPU through torch.distributed.run;
+each rank runs its own batch on its own replica of the weights (broadcast
+once from rank 0 over NCCL), with no per-step collective: `scaling` is weak.
+
+Printed (rank 0, one JSON line):
+  value      positions/s over all ranks, inputs resident in HBM, device time
+             (CUDA events on the engine's stream, max over ranks);
+  e2e        the same through the runner's C ABI (BatchRunner, 2 slots in
+             flight), pinned host input copied in and logits/values copied
+             out inside every pass;
+  roofline   the tower convolution kernel: algorithmic FLOPs per launch over
+             its average CUDA-event duration, against the measured bf16 peak;
+  cpu_baseline  the reference's own CPU engine (blas, one worker per core at
+             batch 8) on a bounded sample, rank 0 at N = 1 only.
+`--impl reference` times the reference's CPU implementation (oracle/_ref,
+OpenBLAS, all host cores) on the same config and metric instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "alphazero-go_b200"))
+
+METRIC = "19x19 net positions/sec"
+UNIT = "positions/s"
+BOARD, BLOCKS, FILTERS, VALUE_HIDDEN, HISTORY = 19, 20, 256, 256, 1
+BATCH = 1024
+SEED = 1
+WORKLOAD = "C4: 19x19 board, 20 residual blocks x 256 filters, value_hidden 256, 4 input planes, batch 1024 per GPU"
+
+
+def conv_flops_per_position() -> float:
+    """2 * F^2 * 9 * A per 3x3 tower convolution (one launch covers the batch)."""
+    return 2.0 * FILTERS * FILTERS * 9 * BOARD * BOARD
+
+
+def flops_per_position() -> float:
+    A, F, P, V = BOARD * BOARD, FILTERS, 2 * HISTORY + 2, VALUE_HIDDEN
+    return (2 * BLOCKS * conv_flops_per_position() + 2.0 * F * P * 9 * A
+            + 2.0 * 3 * F * A + 2.0 * 2 * A * (A + 1) + 2.0 * A * V + 2.0 * V)
+
+
+def measured_peaks() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+def profiled_traffic() -> float | None:
+    """DRAM bytes per conv launch from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "conv3x3_tc_bf16_c4.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+# --------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """nvidia-smi sampled every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, bus_ids: list[str]):
+        self.bus_ids = [b.lower() for b in bus_ids if b]
+        self.proc = None
+        self.out = None
+
+    def start(self):
+        try:
+            self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.out, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            self.proc.wait()
+        self.out.flush()
+        self.out.seek(0)
+        rows = [r.split(",") for r in self.out.read().splitlines() if r.strip()]
+        self.out.close()
+        os.unlink(self.out.name)
+        sm, mx, reasons = [], [], set()
+        for r in rows:
+            r = [c.strip() for c in r]
+            if len(r) < 10:
+                continue
+            bus = r[1].lower()
+            if self.bus_ids and not any(bus.endswith(b[-12:]) or b.endswith(bus[-12:]) for b in self.bus_ids):
+                continue
+            try:
+                sm.append(float(r[2]))
+                mx.append(float(r[3]))
+            except ValueError:
+                continue
+            for name, v in zip(self.REASONS, r[6:10]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------- distributed
+
+
+class Dist:
+    def __init__(self, gpus: int):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.torch = None
+        if self.world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+            self.torch = torch
+        if gpus != self.world and self.rank == 0:
+            print(f"bench: --gpus {gpus} but WORLD_SIZE {self.world}; using {self.world}", file=sys.stderr)
+
+    def barrier(self):
+        if self.torch:
+            self.torch.distributed.barrier()
+            self.torch.cuda.synchronize()
+
+    def max(self, v: float) -> float:
+        if not self.torch:
+            return v
+        t = self.torch.tensor([v], dtype=self.torch.float64, device="cuda")
+        self.torch.distributed.all_reduce(t, op=self.torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    def broadcast(self, arr):
+        """Rank 0's numpy array to every rank, over NCCL."""
+        if not self.torch:
+            return arr
+        import numpy as np
+
+        t = self.torch.from_numpy(arr).cuda()
+        self.torch.distributed.broadcast(t, src=0)
+        return t.cpu().numpy().astype(np.float32, copy=False)
+
+    def close(self):
+        if self.torch:
+            self.torch.distributed.barrier()
+            self.torch.distributed.destroy_process_group()
+
+
+# ----------------------------------------------------------- CPU arms
+
+
+def cpu_reference_sample(steps: int, warmup: int, per_step_calls: int = 1, seconds: float = 0.0):
+    """The reference's CPU engine (oracle/_ref, blas, single-threaded per
+    worker as src/backend_blas.cpp:56-70 requires) on every host core.
+    Returns (positions/s, workers, sample description)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    cfg = O.NetConfig(BOARD, HISTORY, BLOCKS, FILTERS, VALUE_HIDDEN, False)
+    net = O.RefNetwork(cfg, SEED, O.KIND_BENCH)
+    x = O.ref_positions(cfg, SEED, 8)
+    cores = len(os.sched_getaffinity(0))
+    try:
+        import psutil
+
+        avail = psutil.virtual_memory().available
+        workers = max(1, min(cores, int(avail * 0.6 // (400 << 20))))   # ~300 MB of reference Workspace each
+    except ImportError:
+        workers = cores
+    backend = "blas" if "OpenBLAS" in O.blas_description() else "naive"
+    for _ in range(warmup):
+        net.bench_workers(backend, workers, 8, x, max_calls=1)
+    if seconds > 0:
+        rate, pos = net.bench_workers(backend, workers, 8, x, seconds=seconds)
+        sample = f"{workers} workers x batch 8, {pos} positions in ~{seconds:.0f} s ({backend}: {O.blas_description()})"
+        return rate, workers, sample
+    total_pos, total_t = 0, 0.0
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        _, pos = net.bench_workers(backend, workers, 8, x, max_calls=per_step_calls)
+        total_t += time.perf_counter() - t0
+        total_pos += pos
+    sample = (f"{steps} steps x {workers} workers x {per_step_calls} call(s) of batch 8 = {total_pos} positions "
+              f"({backend}: {O.blas_description()})")
+    return total_pos / total_t, workers, sample
+
+
+def run_reference(args):
+    n_gpus = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    try:
+        rate, workers, sample = cpu_reference_sample(args.steps, args.warmup)
+    except Exception as e:   # the reference build is missing or failed
+        print(json.dumps({"impl": "reference", "unavailable": f"reference CPU engine failed: {e}"}))
+        return
+    line = {
+        "metric": METRIC, "value": rate, "unit": UNIT, "n_gpus": n_gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD.replace("batch 1024 per GPU", "batch 8 per CPU worker"),
+                   "parallelism": f"{workers} CPU workers", "backend": "reference CPU (oracle/_ref)"},
+        "impl": "reference",
+        "cpu_baseline": {"value": rate, "unit": UNIT, "cores": workers, "kind": "reference", "sample": sample},
+        "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+# -------------------------------------------------------------- engine
+
+
+def run_engine(args, d: Dist):
+    import numpy as np
+
+    import azb200 as E
+
+    dev = d.local if d.world > 1 else 0
+    ok, why = E.cuda_available(dev)
+    if not ok:
+        raise SystemExit(f"bench: no usable GPU {dev}: {why}")
+    desc = E.NetDesc(BOARD, HISTORY, BLOCKS, FILTERS, VALUE_HIDDEN, 0)
+    precision = E.BF16
+    if d.rank == 0:
+        params, buffers = E.synth_network(desc, SEED, 0)
+    else:
+        np_, nb = E.arena_floats(desc)
+        params, buffers = np.zeros(np_, np.float32), np.zeros(nb, np.float32)
+    params, buffers = d.broadcast(params), d.broadcast(buffers)
+    x = E.synth_positions(desc, SEED, BATCH, first=d.rank * BATCH)
+    net = E.CudaInference(desc, params, buffers, BATCH, dev, precision)
+    net.stage(x)
+
+    # --- device-resident throughput: W untimed, then exactly K timed passes
+    net.time(BATCH, 0, args.warmup)
+    sampler = ClockSampler([E.pci_bus_id(dev)] if d.world == 1 else []) if d.rank == 0 else None
+    d.barrier()
+    if sampler:
+        sampler.start()
+    ms, _ = net.time(BATCH, 0, args.steps)
+    d.barrier()
+    clocks = sampler.stop() if sampler else None
+    ms = d.max(ms)
+    value = d.world * BATCH * args.steps / (ms / 1e3)
+
+    # --- the conv kernel alone, per launch (CUDA events around each launch)
+    _, conv_ms = net.time(BATCH, 0, max(2, min(args.steps, 5)), conv=True)
+    conv_launches = 2 * BLOCKS * max(2, min(args.steps, 5))
+    conv_avg_ms = d.max(conv_ms / conv_launches)
+    conv_tflops = conv_flops_per_position() * BATCH / (conv_avg_ms * 1e-3) / 1e12
+    net.close()
+
+    if args.only_device:
+        if d.rank == 0:
+            print(json.dumps({"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": d.world,
+                              "ms_per_step": ms / args.steps, "conv_avg_ms": conv_avg_ms,
+                              "conv_tflops": conv_tflops, "note": "device-only run (profiling)"}))
+        d.close()
+        return
+
+    # --- end to end through the runner (the BatchRunner drop-in), 2 slots in flight
+    runner = E.make_cuda_runner(desc, params, buffers, BATCH, 2, dev, precision)
+    for s in range(2):
+        runner.input(s)[:] = x
+    done_q, lock = [], threading.Condition()
+
+    def done(slot, err):
+        with lock:
+            done_q.append((slot, err))
+            lock.notify()
+
+    def run_passes(n):
+        inflight = 0
+        started = 0
+        for s in range(min(2, n)):
+            runner.begin(s, BATCH, done)
+            inflight += 1
+            started += 1
+        errors = []
+        while inflight:
+            with lock:
+                while not done_q:
+                    lock.wait()
+                slot, err = done_q.pop(0)
+            inflight -= 1
+            if err:
+                errors.append(err)
+            if started < n and not errors:
+                runner.begin(slot, BATCH, done)
+                inflight += 1
+                started += 1
+        if errors:
+            raise RuntimeError(errors[0])
+
+    run_passes(args.warmup)
+    d.barrier()
+    t0 = time.perf_counter()
+    run_passes(args.steps)
+    e2e_s = time.perf_counter() - t0
+    d.barrier()
+    e2e_s = d.max(e2e_s)
+    runner.close()
+    e2e = d.world * BATCH * args.steps / e2e_s
+
+    # --- CPU baseline: the reference's CPU engine on this box's cores (rank 0, N = 1)
+    cpu = None
+    if d.world == 1 and not args.no_cpu_baseline:
+        try:
+            rate, workers, sample = cpu_reference_sample(0, 0, seconds=args.cpu_seconds)
+            cpu = {"value": rate, "unit": UNIT, "cores": workers, "kind": "reference", "sample": sample}
+        except Exception as e:
+            cpu = {"value": None, "unit": UNIT, "cores": 0, "kind": "reference", "sample": f"unavailable: {e}"}
+
+    if d.rank == 0:
+        peaks = measured_peaks()
+        peak = peaks.get("bf16_tflops_sustained")
+        peak_note = "measured sustained bf16 (MEASURED_PEAKS.json)"
+        if peak is None:
+            peak, peak_note = 1400.0, "fallback sustained bf16"
+        traffic = profiled_traffic()
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": d.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_batch": BATCH * d.world, "parallelism": f"replicas x{d.world}",
+                       "precision": "bf16 weights/activations, fp32 accumulate",
+                       "l2": "inputs larger than L2 (3 x 189 MB activation frames per GPU)",
+                       "flop_per_position": flops_per_position()},
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": BATCH * 4 * BOARD * BOARD * 4 * d.world,
+                    "d2h_bytes_per_step": (BATCH * (BOARD * BOARD + 1) * 4 + BATCH * 4 + 4) * d.world,
+                    "how": "BatchRunner C ABI, 2 slots in flight, host wall clock, max over ranks"},
+            "roofline": {"bound": "tensor", "achieved": conv_tflops, "peak": peak, "unit": "TFLOP/s",
+                         "frac": conv_tflops / peak, "traffic": traffic, "peak_source": peak_note,
+                         "kernel": "conv3x3_tc<256,bf16>", "flop_per_launch": conv_flops_per_position() * BATCH,
+                         "avg_launch_ms": conv_avg_ms},
+            "tensor_tflops_whole_pass": flops_per_position() * BATCH * d.world * args.steps / (ms / 1e3) / 1e12,
+            "gpu_launches": args.steps * (2 * BLOCKS + 2),
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line))
+    d.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("engine", "reference"), default="engine")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only-device", action="store_true", help="device-resident passes only (for profilers)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        # The reference arm is CPU-only: rank 0 runs it, the other ranks exit
+        # at once (no process group, so nobody waits on anybody).
+        if int(os.environ.get("RANK", "0")) == 0:
+            run_reference(args)
+        return
+    run_engine(args, Dist(args.gpus))
+
+
+if __name__ == "__main__":
+    main()

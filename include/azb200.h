@@ -65,6 +65,20 @@ int azb_cuda_available(int device, char* why, size_t why_cap);
  * "<GPU> sm_100, driver API x.y, runtime x.y, kernels <8 hex>, <precision>". */
 int azb_describe(int device, int precision, char* out, size_t cap);
 int azb_device_count(void);
+/* The device's PCI bus id ("0000:1b:00.0"), to match it with nvidia-smi. */
+int azb_device_pci_bus_id(int device, char* out, size_t cap);
+
+/* ---------------------------------------------------------- synthetic data */
+/* No reference counterpart as an API: these restate the reference's seeded
+ * construction so benchmarks can build the reference's own networks and
+ * inputs without it. azb_synth_network = Network(cfg, seed)
+ * (src/network.cpp:77-111) then a batch-norm randomiser (kind 0: gamma
+ * U(0.5,1.5), beta N(0,0.1), mean N(0,0.1), var U(0.5,1.5) from
+ * Rng(deriveSeed(seed,1)); kind 1: tests/test_cuda.cpp:188-204; kind -1:
+ * none). azb_synth_positions: sample first+b from Rng(deriveSeed(seed, 2,
+ * first+b)), encoded as encodePlanes (src/encode.cpp:14-43). */
+int azb_synth_network(const azb_net_desc* desc, uint64_t seed, int kind, float* params, float* buffers);
+int azb_synth_positions(const azb_net_desc* desc, uint64_t seed, long first, int B, float* out);
 
 /* ------------------------------------------------------------ sync infer */
 
