@@ -192,6 +192,18 @@ int azb_check_memory(const azb_net_desc* desc, int inference_batch, int hubs, in
     });
 }
 
+size_t azb_weights_bytes(const azb_net_desc* desc, int precision) {
+    try {
+        return Weights::bytes_for(NetShape::from(*desc), precision);
+    } catch (...) {
+        return 0;
+    }
+}
+
+int azb_check_bytes(int device, double bytes, int inference_batch, int hubs, char* err, size_t err_cap) {
+    return guarded(err, err_cap, "", [&] { check_fits(device, bytes, inference_batch, hubs); });
+}
+
 // ------------------------------------------------------------ test hooks
 
 void azb_probe_set_hub_chaos_seed(uint64_t seed) { hooks().chaos_seed = seed; }

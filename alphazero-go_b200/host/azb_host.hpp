@@ -1,0 +1,33 @@
+// The C++ side of the drop-in (azgo_cuda_bridge.cpp): what a reference
+// build needs beyond include/azgo/cuda.hpp to place this engine's runners on
+// chosen GPUs and in a chosen arithmetic.
+#pragma once
+#include <memory>
+#include <vector>
+
+#include "azb200.h"
+#include "azgo/inference_hub.hpp"
+#include "azgo/network.hpp"
+
+namespace azb_host {
+
+// Device and precision (AZB_TF32, AZB_TF32X3, AZB_BF16) for the runners and
+// CudaInference objects made from now on.
+void setDefaults(int device, int precision);
+int defaultDevice();
+int defaultPrecision();
+
+azb_net_desc describe(const azgo::NetConfig& c);
+
+// The network's two ParamLayout arenas, each tensor checked by name and size
+// against the engine's layout (refusing unknown, missing or mis-sized ones).
+struct Arenas {
+    std::vector<float> params, buffers;
+};
+Arenas arenas(const azgo::Network& net);
+
+// makeCudaRunner on a given device (one hub per GPU); precision < 0: the default.
+std::unique_ptr<azgo::BatchRunner> makeCudaRunnerOn(const azgo::Network& net, int maxBatch, int slots, int device,
+                                                    int precision = -1);
+
+} // namespace azb_host

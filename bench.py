@@ -146,10 +146,15 @@ class ClockSampler:
 
 
 class Dist:
-    def __init__(self, gpus: int):
+    """One rank per GPU: RANK / LOCAL_RANK / WORLD_SIZE from the launcher.
+    NCCL on the GPUs; gloo on the CPU (the multi-rank host tests)."""
+
+    def __init__(self, gpus: int, backend: str | None = None):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.backend = backend or os.environ.get("AZB_DIST_BACKEND", "nccl")
+        self.device = "cuda" if self.backend == "nccl" else "cpu"
         self.torch = None
         if self.world > 1:
             import datetime
@@ -157,9 +162,12 @@ class Dist:
             import torch
             import torch.distributed as dist
 
-            torch.cuda.set_device(self.local)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                    device_id=torch.device("cuda", self.local))
+            timeout = datetime.timedelta(seconds=120)
+            if self.device == "cuda":
+                torch.cuda.set_device(self.local)
+                dist.init_process_group("nccl", timeout=timeout, device_id=torch.device("cuda", self.local))
+            else:
+                dist.init_process_group(self.backend, timeout=timeout)
             self.torch = torch
         if gpus != self.world and self.rank == 0:
             print(f"bench: --gpus {gpus} but WORLD_SIZE {self.world}; using {self.world}", file=sys.stderr)
@@ -167,22 +175,23 @@ class Dist:
     def barrier(self):
         if self.torch:
             self.torch.distributed.barrier()
-            self.torch.cuda.synchronize()
+            if self.device == "cuda":
+                self.torch.cuda.synchronize()
 
     def max(self, v: float) -> float:
         if not self.torch:
             return v
-        t = self.torch.tensor([v], dtype=self.torch.float64, device="cuda")
+        t = self.torch.tensor([v], dtype=self.torch.float64, device=self.device)
         self.torch.distributed.all_reduce(t, op=self.torch.distributed.ReduceOp.MAX)
         return float(t.item())
 
     def broadcast(self, arr):
-        """Rank 0's numpy array to every rank, over NCCL."""
+        """Rank 0's numpy array to every rank (once, at start: the weight replicas)."""
         if not self.torch:
             return arr
         import numpy as np
 
-        t = self.torch.from_numpy(arr).cuda()
+        t = self.torch.from_numpy(np.ascontiguousarray(arr)).to(self.device)
         self.torch.distributed.broadcast(t, src=0)
         return t.cpu().numpy().astype(np.float32, copy=False)
 
@@ -190,6 +199,7 @@ class Dist:
         if self.torch:
             self.torch.distributed.barrier()
             self.torch.distributed.destroy_process_group()
+            self.torch = None
 
 
 # ----------------------------------------------------------- CPU arms

@@ -6,7 +6,7 @@
  * 3x3 convolutions with batch norm, skip and ReLU fused into the epilogue,
  * and one fused head kernel. It is the drop-in for the reference's CUDA
  * engine (include/azgo/cuda.hpp) and BatchRunner (include/azgo/inference_hub.hpp):
- * the C++ adapter in alphazero-go_b200/host/azb_runner.hpp maps these calls
+ * the C++ bridge alphazero-go_b200/host/azgo_cuda_bridge.cpp maps these calls
  * onto those interfaces.
  *
  * Conventions: functions return 0 on success and a negative value on
@@ -156,6 +156,13 @@ size_t azb_workspace_bytes(const azb_net_desc* desc, int max_batch, int precisio
  * reference's message. */
 int azb_check_memory(const azb_net_desc* desc, int inference_batch, int hubs, int slots_per_hub, int device,
                      int precision, char* err, size_t err_cap);
+
+/* The engine's weight bytes on a device, and the reference's one combined
+ * check (src/cuda/cuda_runner.cu:203-223): 0 when `bytes` fit in the
+ * device's free memory less a 512 MB margin (or the test hook's limit),
+ * else -1 and "cuda: inference needs N MB ...; lower inference_batch". */
+size_t azb_weights_bytes(const azb_net_desc* desc, int precision);
+int azb_check_bytes(int device, double bytes, int inference_batch, int hubs, char* err, size_t err_cap);
 
 /* ------------------------------------------------ test hooks (cuda_probe) */
 /* include/azgo/cuda.hpp:138-155 */

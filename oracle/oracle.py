@@ -183,6 +183,9 @@ def ref() -> C.CDLL:
                                           C.c_longlong, C.POINTER(C.c_longlong), C.c_char_p, C.c_size_t]
         R.azref_bench_workers.restype = C.c_double
         R.azref_blas_description.restype = C.c_char_p
+        R.azref_rng_sample.argtypes = [C.c_uint64, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double)]
+        R.azref_derive_seed.argtypes = [C.c_uint64] * 4
+        R.azref_derive_seed.restype = C.c_uint64
         _ref = R
     return _ref
 
@@ -249,6 +252,44 @@ def ref_positions(cfg: NetConfig, seed: int, B: int, first: int = 0) -> np.ndarr
     out = np.zeros((B, cfg.planes, cfg.area), np.float32)
     ref().azref_inputs_positions(cfg.board, cfg.history, seed, first, B, _fp(out))
     return out
+
+
+def ref_rng_sample(seed: int, what: int, count: int, n: int = 0) -> np.ndarray:
+    """The reference Rng's outputs: what 0 next() as (hi, lo) pairs, 1 uniform, 2 below(n), 3 normal."""
+    out = np.zeros(count * (2 if what == 0 else 1), np.float64)
+    ref().azref_rng_sample(seed, what, n, count, out.ctypes.data_as(C.POINTER(C.c_double)))
+    return out
+
+
+def rng_sample(seed: int, what: int, count: int, n: int = 0) -> np.ndarray:
+    """The oracle's restated generator, same encoding as ref_rng_sample."""
+    L = lib()
+    L.az_rng_seed.argtypes = [C.c_void_p, C.c_uint64]
+    L.az_rng_next.argtypes = [C.c_void_p]
+    L.az_rng_next.restype = C.c_uint64
+    L.az_rng_uniform.argtypes = [C.c_void_p]
+    L.az_rng_uniform.restype = C.c_double
+    L.az_rng_below.argtypes = [C.c_void_p, C.c_int]
+    L.az_rng_normal.argtypes = [C.c_void_p]
+    L.az_rng_normal.restype = C.c_double
+    state = (C.c_uint64 * 4)()
+    L.az_rng_seed(state, seed)
+    out = []
+    for _ in range(count):
+        if what == 0:
+            v = L.az_rng_next(state)
+            out += [float(v >> 32), float(v & 0xFFFFFFFF)]
+        elif what == 1:
+            out.append(L.az_rng_uniform(state))
+        elif what == 2:
+            out.append(float(L.az_rng_below(state, n)))
+        else:
+            out.append(L.az_rng_normal(state))
+    return np.array(out, np.float64)
+
+
+def derive_seed(a: int, b: int = 0, c: int = 0, d: int = 0) -> int:
+    return int(lib().az_derive_seed(a, b, c, d))
 
 
 def blas_description() -> str:

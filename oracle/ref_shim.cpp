@@ -221,6 +221,28 @@ double azref_bench_workers(azref_net* h, const char* backend, int workers, int b
     }
 }
 
+// Raw generator outputs (src/rng.cpp), for the oracle's known-answer pins:
+// what = 0 next() (as two 32-bit halves in doubles: hi, lo), 1 uniform(),
+// 2 below(n), 3 normal().
+void azref_rng_sample(uint64_t seed, int what, int n, int count, double* out) {
+    Rng rng(seed);
+    for (int i = 0; i < count; ++i) {
+        switch (what) {
+            case 0: {
+                const uint64_t v = rng.next();
+                out[2 * i] = static_cast<double>(v >> 32);
+                out[2 * i + 1] = static_cast<double>(v & 0xFFFFFFFFull);
+                break;
+            }
+            case 1: out[i] = rng.uniform(); break;
+            case 2: out[i] = rng.below(n); break;
+            default: out[i] = rng.normal(); break;
+        }
+    }
+}
+
+uint64_t azref_derive_seed(uint64_t a, uint64_t b, uint64_t c, uint64_t d) { return deriveSeed(a, b, c, d); }
+
 const char* azref_blas_description() {
     static std::string d = blasAvailable() ? blasDescription() : std::string("naive only (built without BLAS)");
     return d.c_str();
