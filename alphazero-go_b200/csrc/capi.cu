@@ -8,13 +8,10 @@
 #include <vector>
 
 #include "../../include/azb200.h"
+#include "capi_types.hpp"
 #include "engine.hpp"
 
 using namespace azb;
-
-struct azb_infer {
-    std::unique_ptr<Inference> impl;
-};
 
 struct azb_runner {
     std::unique_ptr<Runner> impl;

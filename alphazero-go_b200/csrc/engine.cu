@@ -555,6 +555,39 @@ Workspace::Workspace(const Weights& w, int max_batch) : max_batch_(max_batch) {
     }
 }
 
+Workspace::Workspace(const Weights& w, int max_batch, void* memory) : max_batch_(max_batch) {
+    if (max_batch < 1) throw std::invalid_argument("azb: max_batch must be >= 1");
+    const NetShape& s = w.shape();
+    const int precision = w.precision();
+    const Frame fr(s.board);
+    const size_t rows = size_t(max_batch) * fr.S;
+    const size_t cpad = size_t(w.cpad()), esz = size_t(elem_bytes(precision));
+    const size_t A = size_t(s.area()), L = size_t(s.actions()), B = size_t(max_batch);
+    bytes_ = bytes_for(s, precision, max_batch);
+    uint8_t* base = static_cast<uint8_t*>(memory);
+    Carver c;
+    auto at = [&](size_t off) { return base + off; };
+    stage = reinterpret_cast<float*>(at(c.take(B * s.planes() * A * 4)));
+    const size_t ks = size_t(w.kstem());
+    stem_in = at(c.take(rows * ks * esz));
+    if (precision == kTF32x3) stem_in_lo = at(c.take(rows * ks * 4));
+    for (int i = 0; i < 3; ++i) trunk[i] = at(c.take(rows * cpad * esz));
+    if (precision == kTF32x3)
+        for (int i = 0; i < 3; ++i) trunk_lo[i] = at(c.take(rows * cpad * 4));
+    logits = reinterpret_cast<float*>(at(c.take(B * L * 4)));
+    values = reinterpret_cast<float*>(at(c.take(B * 4)));
+    if (s.ownership) ownership = reinterpret_cast<float*>(at(c.take(B * A * 4)));
+    probs = reinterpret_cast<float*>(at(c.take(B * L * 4)));
+    err = reinterpret_cast<int*>(at(c.take(16)));
+    const uint32_t KC = uint32_t(chunk_channels(precision));
+    map_stem = make_tensor_map(stem_in, precision, ks, rows, KC, uint32_t(fr.halo));
+    map_stem_lo = precision == kTF32x3 ? make_tensor_map(stem_in_lo, precision, ks, rows, KC, uint32_t(fr.halo)) : map_stem;
+    for (int i = 0; i < 3; ++i) {
+        map[i] = make_tensor_map(trunk[i], precision, cpad, rows, KC, uint32_t(fr.halo));
+        map_lo[i] = precision == kTF32x3 ? make_tensor_map(trunk_lo[i], precision, cpad, rows, KC, uint32_t(fr.halo)) : map[i];
+    }
+}
+
 Workspace::~Workspace() {
     if (arena_) cudaFree(arena_);
 }

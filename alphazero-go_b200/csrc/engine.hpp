@@ -104,6 +104,11 @@ private:
 class Workspace {
 public:
     Workspace(const Weights& w, int max_batch);
+    // The same layout placed in caller-provided device memory of at least
+    // bytes_for(shape, precision, max_batch) bytes, 256-byte aligned: nothing
+    // is allocated, cleared or freed (the caller zeroes it first, since the
+    // frames' padding rows must read zero).
+    Workspace(const Weights& w, int max_batch, void* memory);
     ~Workspace();
     Workspace(const Workspace&) = delete;
     Workspace& operator=(const Workspace&) = delete;
@@ -161,6 +166,8 @@ public:
     void sync();
     void read(int B, float* logits, float* values, float* ownership, float* probs);
     cudaStream_t stream() const { return stream_; }
+    const Weights& weights() const { return *w_; }
+    int* error_host() const { return err_host_; }   // pinned, one int
     // (total ms of K passes, summed conv-kernel ms)
     void time(int B, int warmup, int steps, bool with_copies, double* ms, double* conv_ms);
 

@@ -98,6 +98,24 @@ int azb_infer_run(azb_infer* h, const float* input, int B, float* logits, float*
 /* CudaInference::bytes(): GPU memory of the activations. */
 size_t azb_infer_bytes(const azb_infer* h);
 
+/* azb_infer_run without allocating: no counterpart in the reference. For
+ * callers that may not allocate device memory when they evaluate -- work
+ * being captured into a CUDA graph (cudaMalloc is not allowed during a
+ * capture), hosts whose own pool allocator owns the GPU's memory or that run
+ * under a fixed budget, latency-critical paths where cudaMalloc may
+ * synchronise the device. The handle is created once at set-up (that
+ * allocates, and uploads the weights); this call then runs the same forward
+ * pass with all its scratch (input staging, stem operand, activation frames,
+ * outputs, error word) in a static 32 MiB device array that every GPU
+ * loading this library holds until exit: enough, e.g., for batch 32 of the
+ * 19x19 20x256 network in bf16. A batch whose scratch exceeds it is refused
+ * with an error naming the size. The first call on a device looks the
+ * array's address up (make it before any stream capture). Every call shares
+ * the array and clears the part it uses; calls that overlap on the GPU race
+ * on it and must be serialised by the caller. */
+int azb_infer_run_noalloc(azb_infer* h, const float* input, int B, float* logits, float* values, float* ownership,
+                          char* err, size_t err_cap);
+
 /* Device-resident use, for timing the kernels alone: copy B positions into
  * the workspace once, then enqueue forward passes on it (no host copies). */
 int azb_infer_stage(azb_infer* h, const float* input, int B, char* err, size_t err_cap);
