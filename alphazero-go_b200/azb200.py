@@ -109,6 +109,7 @@ def lib() -> C.CDLL:
             L.azb_probe_set_memory_limit.argtypes = [s]
             L.azb_probe_passes_completed.restype = C.c_longlong
             L.azb_probe_set_copy_out_delay.argtypes = [C.c_int]
+            L.azb_probe_set_conv_path.argtypes = [C.c_int]
             L.azb_probe_binary_version.argtypes = [C.c_int]
             L.azb_probe_device_architecture.argtypes = [C.c_int]
             L.azb_probe_fill.argtypes = [C.c_int, _F, s, C.c_float, s] + err
@@ -409,6 +410,11 @@ class cuda_probe:
     @staticmethod
     def set_copy_out_delay(us: int):
         lib().azb_probe_set_copy_out_delay(us)
+
+    @staticmethod
+    def set_conv_path(path: int):
+        """0 default (single CTA per tile), 1 single CTA, 2 CTA pairs (M = 256)."""
+        lib().azb_probe_set_conv_path(path)
 
     @staticmethod
     def binary_version(device: int = 0) -> int:

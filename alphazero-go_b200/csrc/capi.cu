@@ -209,6 +209,7 @@ void azb_probe_fail_passes_after(int n) { hooks().fail_countdown = n > 0 ? n + 1
 void azb_probe_set_memory_limit(size_t bytes) { hooks().memory_limit = bytes; }
 long long azb_probe_passes_completed(void) { return hooks().passes_completed.load(); }
 void azb_probe_set_copy_out_delay(int us) { hooks().copy_out_delay_us = us > 0 ? us : 0; }
+void azb_probe_set_conv_path(int path) { set_conv_path(path); }
 
 int azb_probe_binary_version(int device) { return device_info(device).binary_version; }
 int azb_probe_device_architecture(int device) { return device_info(device).architecture; }

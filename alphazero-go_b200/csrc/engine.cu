@@ -451,12 +451,17 @@ Weights::Weights(const NetShape& s, int precision, int device, const float* para
         cv.shift = at(co[i].shift);
         cv.w = at(co[i].w);
         cv.map_w = make_tensor_map(cv.w, precision, uint64_t(co[i].k), uint64_t(n_out_), uint32_t(KC), uint32_t(n_out_));
+        cv.map_w_pair = make_tensor_map(cv.w, precision, uint64_t(co[i].k), uint64_t(n_out_), uint32_t(KC),
+                                        uint32_t(n_out_ / 2));
         if (split) {
             cv.w_lo = at(co[i].w_lo);
             cv.map_w_lo = make_tensor_map(cv.w_lo, precision, uint64_t(co[i].k), uint64_t(n_out_), uint32_t(KC),
                                           uint32_t(n_out_));
+            cv.map_w_lo_pair = make_tensor_map(cv.w_lo, precision, uint64_t(co[i].k), uint64_t(n_out_), uint32_t(KC),
+                                               uint32_t(n_out_ / 2));
         } else {
             cv.map_w_lo = cv.map_w;
+            cv.map_w_lo_pair = cv.map_w_pair;
         }
     }
     head_.ld = cpad_;
@@ -632,13 +637,12 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
     a.ld = w.cpad();
     a.halo_rows = fr.halo;
     a.a_bytes = (fr.halo * 128 + 1023) / 1024 * 1024;
-    conv_smem_bytes(w.n_out(), precision, fr.halo, &a.sa, &a.sb);
     a.base_offset_mode = 0;
     a.err = ws.err;
     auto conv = [&](int index, const CUtensorMap& in, const CUtensorMap& in_lo, int dst, const void* skip,
                     const void* skip_lo, int taps, int nchunks, int timer_slot) {
         const Weights::Conv& cv = w.conv(index);
-        ConvMaps m{in, in_lo, cv.map_w, cv.map_w_lo};
+        ConvMaps m{in, in_lo, cv.map_w, cv.map_w_lo, cv.map_w_pair, cv.map_w_lo_pair};
         a.taps = taps;
         a.nchunks = nchunks;
         a.out = ws.trunk[dst];

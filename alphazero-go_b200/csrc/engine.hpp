@@ -76,6 +76,7 @@ public:
         const void* w = nullptr;        // [n_out][9*cpad] kernel layout (split: tf32 high part)
         const void* w_lo = nullptr;     // split: low part
         CUtensorMap map_w{}, map_w_lo{};
+        CUtensorMap map_w_pair{}, map_w_lo_pair{};   // boxes of n_out/2 rows, for the CTA-pair form
     };
     const NetShape& shape() const { return shape_; }
     int precision() const { return precision_; }

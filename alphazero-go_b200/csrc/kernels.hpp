@@ -69,15 +69,21 @@ struct ConvArgs {
 };
 
 struct ConvMaps {
-    CUtensorMap a, a_lo;   // input activations: box {chunk, halo_rows}
-    CUtensorMap w, w_lo;   // weights [N][9*Cin]: box {chunk, N}
+    CUtensorMap a, a_lo;             // input activations: box {chunk, halo_rows}
+    CUtensorMap w, w_lo;             // weights [N][9*Cin]: box {chunk, N}
+    CUtensorMap w_pair, w_lo_pair;   // the same weights in boxes of {chunk, N/2}: one half per CTA of a pair
 };
 
-// Shared memory a conv launch needs, and its pipeline depths.
-size_t conv_smem_bytes(int n_out, int precision, int halo_rows, int* sa, int* sb);
+// Shared memory a conv launch needs, and its pipeline depths (pair: the
+// CTA-pair form, which stages half of each weight tile per CTA).
+size_t conv_smem_bytes(int n_out, int precision, int halo_rows, int* sa, int* sb, bool pair = false);
 
-// Enqueues the conv on `s`; grid = min(ntiles, sms).
+// Enqueues the conv on `s`: the single-CTA form, or the CTA-pair form
+// (2-CTA clusters, M = 256 per MMA) when the test hook selects it; the
+// pipeline depths in `a` are chosen here.
 cudaError_t launch_conv(const ConvMaps& maps, const ConvArgs& a, int n_out, int precision, int sms, cudaStream_t s);
+// Test hook: 0 default (single CTA), 1 single CTA, 2 CTA pairs.
+void set_conv_path(int path);
 
 // The stem's packed operand: the [B][P][A] fp32 input unfolded into frame
 // rows of K = 9*P values (column t*P + p), ld elements apart. The stem conv

@@ -157,6 +157,116 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// ------------------------------------------------- CTA pairs (cta_group::2)
+//
+// The two CTAs of a 2-CTA cluster compute one M = 256 tile together: each
+// stages its own 128 rows of A and half of B; the pair's leader (rank 0)
+// issues the MMAs, which read both CTAs' shared memory and write both CTAs'
+// TMEM. Each helper below addresses one CTA's barrier or memory at a time.
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// All threads of both CTAs: everything before (barrier inits, remote
+// arrivals) is visible to everything after.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The shared::cluster address of this CTA's shared-memory location `saddr`
+// as seen in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t mapa(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+
+// Arrive on an mbarrier given by its shared::cluster address (possibly the
+// peer CTA's), releasing this thread's prior work at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// mbar_wait with cluster-scope acquire: for barriers the peer CTA arrives on.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err, int code) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t start = global_timer();
+    for (;;) {
+        for (int i = 0; i < 32; ++i)
+            if (mbar_try_wait_cluster(bar, parity)) return true;
+        if (global_timer() - start > kWaitLimitNs) {
+            atomicCAS(err, 0, code);
+            return false;
+        }
+    }
+}
+
+// A 2D TMA tile into THIS CTA's shared memory, its transaction bytes
+// completing on the pair leader's barrier (`leader_bar`: a shared::cluster
+// address in rank 0). The tile lands in this CTA only.
+__device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, void* dst, uint32_t leader_bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(leader_bar), "r"(x), "r"(y)
+        : "memory");
+}
+
+// TMEM for a CTA pair: the same columns in both CTAs. Issued by the same warp
+// of both CTAs.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D (both CTAs' TMEM) (+)= A (both CTAs' shared memory, M = 256) . B (both
+// halves)^T. Issued by one thread of the leader.
+template <bool kBf16>
+__device__ __forceinline__ void umma_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    if constexpr (kBf16) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+            ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+            ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+            : "memory");
+    }
+}
+
+// Arrives once on the mbarrier at shared::cluster address `bar` (this CTA's
+// or the peer's) when the pair MMAs issued so far by this thread complete.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
 // Shared-memory matrix descriptor for a K-major operand in the 128-byte
 // swizzle layout that TMA writes with CU_TENSOR_MAP_SWIZZLE_128B: rows of
 // 128 bytes, 8-row (1024-byte) swizzle atoms stacked along M/N (stride byte
@@ -178,14 +288,14 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, int base_offset_m
     return d;
 }
 
-// Instruction descriptor: fp32 accumulator, K-major A and B, M = 128.
-// a/b format 1 = bf16 (kind::f16), 2 = tf32 (kind::tf32).
-__host__ __device__ constexpr uint32_t umma_idesc(int n, bool bf16) {
+// Instruction descriptor: fp32 accumulator, K-major A and B, M = 128 (one
+// CTA) or 256 (a CTA pair). a/b format 1 = bf16 (kind::f16), 2 = tf32.
+__host__ __device__ constexpr uint32_t umma_idesc(int n, bool bf16, int m = 128) {
     return (1u << 4)                               // D format: f32
            | ((bf16 ? 1u : 2u) << 7)               // A format
            | ((bf16 ? 1u : 2u) << 10)              // B format
            | (static_cast<uint32_t>(n >> 3) << 17) // N / 8
-           | (static_cast<uint32_t>(128 >> 4) << 24);   // M / 16
+           | (static_cast<uint32_t>(m >> 4) << 24);     // M / 16
 }
 
 // Round-to-nearest (ties away) to tf32, as cvt.rna.tf32.f32 does; the low

@@ -190,6 +190,10 @@ void azb_probe_fail_passes_after(int n);
 void azb_probe_set_memory_limit(size_t bytes);
 long long azb_probe_passes_completed(void);
 void azb_probe_set_copy_out_delay(int microseconds);
+/* Which tensor-core conv form passes use: 0 the default (one CTA per
+ * 128-row tile), 1 the same, 2 CTA pairs (2-CTA clusters, M = 256 per MMA,
+ * tcgen05 cta_group::2). For tests and measurements comparing the forms. */
+void azb_probe_set_conv_path(int path);
 /* cuda_probe::binaryVersion / deviceArchitecture / fill (include/azgo/cuda.hpp:93-103). */
 int azb_probe_binary_version(int device);
 int azb_probe_device_architecture(int device);

@@ -22,6 +22,15 @@ pytestmark = pytest.mark.gpu
 SEED = 40
 
 
+@pytest.fixture(params=[1, 2], ids=["single_cta", "cta_pair"])
+def conv_path(request, engine):
+    """Both tensor-core conv forms: one CTA per 128-row tile (M = 128) and
+    2-CTA clusters (M = 256, tcgen05 cta_group::2)."""
+    engine.cuda_probe.set_conv_path(request.param)
+    yield request.param
+    engine.cuda_probe.set_conv_path(0)
+
+
 def cfg(O, board, blocks, filters, vh=64, history=1, own=False):
     return O.NetConfig(board, history, blocks, filters, vh, own)
 
@@ -33,7 +42,7 @@ def run_gpu(engine, desc_cfg, params, buffers, x, precision, max_batch=None):
 
 
 @pytest.mark.parametrize("shape", [(5, 1, 8), (9, 2, 16), (9, 6, 32), (9, 0, 16), (19, 2, 16), (5, 4, 32)])
-def test_tf32x3_matches_reference_forward(engine, oracle, shape):
+def test_tf32x3_matches_reference_forward(engine, oracle, conv_path, shape):
     O = oracle
     c = cfg(O, *shape)
     params, buffers = O.make_network(c, SEED, O.KIND_TEST)
@@ -47,7 +56,7 @@ def test_tf32x3_matches_reference_forward(engine, oracle, shape):
 
 
 @pytest.mark.parametrize("precision", ["tf32", "bf16"])
-def test_fast_modes_track_reference(engine, oracle, precision):
+def test_fast_modes_track_reference(engine, oracle, conv_path, precision):
     O = oracle
     c = cfg(O, 9, 2, 32)
     params, buffers = O.make_network(c, SEED, O.KIND_TEST)
@@ -59,7 +68,7 @@ def test_fast_modes_track_reference(engine, oracle, precision):
     assert np.max(np.abs(vg - vr)) <= 5e-2
 
 
-def test_ownership_head(engine, oracle):
+def test_ownership_head(engine, oracle, conv_path):
     O = oracle
     c = cfg(O, 9, 2, 16, own=True)
     params, buffers = O.make_network(c, SEED, O.KIND_TEST)
@@ -70,7 +79,7 @@ def test_ownership_head(engine, oracle):
     assert np.max(np.abs(og - orf)) <= 1e-4
 
 
-def test_history_planes(engine, oracle):
+def test_history_planes(engine, oracle, conv_path):
     """history 8 (18 planes), as the reference's own test networks use."""
     O = oracle
     c = cfg(O, 9, 2, 16, history=8)
@@ -82,7 +91,7 @@ def test_history_planes(engine, oracle):
 
 
 @pytest.mark.parametrize("precision", ["tf32x3", "bf16", "tf32"])
-def test_batch_independent(engine, oracle, precision):
+def test_batch_independent(engine, oracle, conv_path, precision):
     """tests/test_cuda.cpp:855-898: alone == in any batch, bitwise."""
     O = oracle
     c = cfg(O, 13, 2, 32, own=True)
@@ -109,7 +118,7 @@ def test_batch_independent(engine, oracle, precision):
                         assert np.array_equal(out[k][slot], alone[k][0]), (s, size, slot, k)
 
 
-def test_repeatable(engine, oracle):
+def test_repeatable(engine, oracle, conv_path):
     O = oracle
     c = cfg(O, 9, 2, 16, own=True)
     params, buffers = O.make_network(c, 604, O.KIND_TEST)
@@ -125,3 +134,23 @@ def test_repeatable(engine, oracle):
         second = other.infer(x)
     for a, b in zip(first, second):
         assert np.array_equal(a, b)
+
+
+def test_conv_forms_agree_bf16(engine, oracle):
+    """bf16: each output is a sum of exactly representable products, so the
+    two forms may differ only by accumulation order inside the tensor core;
+    they are compared here to within the bf16 gates and reported."""
+    O = oracle
+    c = cfg(O, 19, 3, 128, 64)
+    params, buffers = O.make_network(c, 7, O.KIND_BENCH)
+    x = O.positions(c, 7, 64)
+    outs = []
+    for path in (1, 2):
+        engine.cuda_probe.set_conv_path(path)
+        try:
+            outs.append(run_gpu(engine, c, params, buffers, x, engine.BF16))
+        finally:
+            engine.cuda_probe.set_conv_path(0)
+    (l1, v1, _), (l2, v2, _) = outs
+    assert np.max(np.abs(O.softmax(l1) - O.softmax(l2))) <= 2e-2
+    assert np.max(np.abs(v1 - v2)) <= 2e-2
