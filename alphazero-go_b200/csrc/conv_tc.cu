@@ -77,6 +77,29 @@ __host__ __device__ constexpr size_t smem_total(int sa, int sb, int ops, int a_b
     return 1024 + size_t(sa) * ops * a_bytes + size_t(sb) * ops * b_bytes + (2 * sa + 2 * sb + 5) * 8 + 16;
 }
 
+// A position in a ring of pipeline stages: the stage and the parity of
+// its current phase, advanced by a compare instead of a division.
+struct Ring {
+    uint32_t idx = 0, phase = 0;
+    __device__ __forceinline__ void next(uint32_t stages) {
+        if (++idx == stages) {
+            idx = 0;
+            phase ^= 1u;
+        }
+    }
+};
+
+// The nine tap views' start rows inside a halo tile, as descriptor
+// increments (16-byte units): halo row n+2 + dy(n+1) + dx is frame row
+// q0 + dy(n+1) + dx. A one-tap pass (the stem GEMM) uses the centre view.
+__device__ __forceinline__ void tap_offsets(const ConvArgs& p, uint32_t (&off)[9]) {
+#pragma unroll
+    for (int t = 0; t < 9; ++t) {
+        const int tap = p.taps == 9 ? t : 4;
+        off[t] = uint32_t(p.n + 2 + (tap / 3 - 1) * (p.n + 1) + (tap % 3 - 1)) * 8u;
+    }
+}
+
 // One epilogue thread's accumulator row (TMEM lane of its warp) for a tile:
 // ReLU(scale * acc + shift (+ skip)) with the reference's separate roundings
 // (src/cuda/kernels.cu:172-176), stored as bf16, fp32, or the tf32 high
@@ -207,87 +230,90 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         // ---------------------------------------------------------- producer
         if (lane == 0) {
-            uint32_t ia = 0, ib = 0;
+            Ring ra, rb;
+            uint32_t na = 0, nb = 0;   // loads issued, for the drain below
             const uint32_t a_tx = uint32_t(p.halo_rows) * 128u * C::kOps;
             const uint32_t b_tx = C::kBBytes * C::kOps;
+            const size_t a_stage = size_t(C::kOps) * p.a_bytes;
             bool ok = true;
             for (int tile = blockIdx.x; tile < p.ntiles && ok; tile += gridDim.x) {
                 const int y0 = tile * 128 - (p.n + 2);
                 for (int c = 0; c < p.nchunks && ok; ++c) {
-                    const int sa = ia % p.sa;
-                    if (!(ok = mbar_wait(&sm.a_empty[sa], ((ia / p.sa) & 1) ^ 1, p.err, kErrWaitProducer))) break;
-                    mbar_arrive_expect_tx(&sm.a_full[sa], a_tx);
-                    uint8_t* abuf = sm.a + size_t(sa) * C::kOps * p.a_bytes;
-                    tma_load_2d(&mA, abuf, &sm.a_full[sa], c * C::kKc, y0);
-                    if (kSplit) tma_load_2d(&mAlo, abuf + p.a_bytes, &sm.a_full[sa], c * C::kKc, y0);
-                    ++ia;
+                    if (!(ok = mbar_wait(&sm.a_empty[ra.idx], ra.phase ^ 1u, p.err, kErrWaitProducer))) break;
+                    mbar_arrive_expect_tx(&sm.a_full[ra.idx], a_tx);
+                    uint8_t* abuf = sm.a + ra.idx * a_stage;
+                    tma_load_2d(&mA, abuf, &sm.a_full[ra.idx], c * C::kKc, y0);
+                    if (kSplit) tma_load_2d(&mAlo, abuf + p.a_bytes, &sm.a_full[ra.idx], c * C::kKc, y0);
+                    ra.next(p.sa);
+                    ++na;
                     for (int t = 0; t < p.taps; ++t) {
-                        const int sb = ib % p.sb;
-                        if (!(ok = mbar_wait(&sm.b_empty[sb], ((ib / p.sb) & 1) ^ 1, p.err, kErrWaitProducer))) break;
-                        mbar_arrive_expect_tx(&sm.b_full[sb], b_tx);
-                        uint8_t* bbuf = sm.b + size_t(sb) * C::kOps * C::kBBytes;
-                        tma_load_2d(&mW, bbuf, &sm.b_full[sb], (c * p.taps + t) * C::kKc, 0);
-                        if (kSplit) tma_load_2d(&mWlo, bbuf + C::kBBytes, &sm.b_full[sb], (c * p.taps + t) * C::kKc, 0);
-                        ++ib;
+                        if (!(ok = mbar_wait(&sm.b_empty[rb.idx], rb.phase ^ 1u, p.err, kErrWaitProducer))) break;
+                        mbar_arrive_expect_tx(&sm.b_full[rb.idx], b_tx);
+                        uint8_t* bbuf = sm.b + rb.idx * (C::kOps * C::kBBytes);
+                        tma_load_2d(&mW, bbuf, &sm.b_full[rb.idx], (c * p.taps + t) * C::kKc, 0);
+                        if (kSplit) tma_load_2d(&mWlo, bbuf + C::kBBytes, &sm.b_full[rb.idx], (c * p.taps + t) * C::kKc, 0);
+                        rb.next(p.sb);
+                        ++nb;
                     }
                 }
             }
             // Every copy this thread issued has landed before the CTA may exit:
             // wait (bounded) for each stage's most recent load.
-            for (uint32_t s = 0; s < uint32_t(p.sa) && s < ia; ++s) {
-                const uint32_t uses = (ia - s + p.sa - 1) / p.sa;
+            for (uint32_t s = 0; s < uint32_t(p.sa) && s < na; ++s) {
+                const uint32_t uses = (na - s + p.sa - 1) / p.sa;
                 mbar_wait(&sm.a_full[s], (uses - 1) & 1, p.err, kErrWaitDrain);
             }
-            for (uint32_t s = 0; s < uint32_t(p.sb) && s < ib; ++s) {
-                const uint32_t uses = (ib - s + p.sb - 1) / p.sb;
+            for (uint32_t s = 0; s < uint32_t(p.sb) && s < nb; ++s) {
+                const uint32_t uses = (nb - s + p.sb - 1) / p.sb;
                 mbar_wait(&sm.b_full[s], (uses - 1) & 1, p.err, kErrWaitDrain);
             }
         }
     } else if (warp == 1) {
         // --------------------------------------------------------- MMA issue
+        // One thread issues every MMA, so whatever it computes between two
+        // MMAs delays the next: descriptors are built once and advanced by
+        // additions, the tap loop is unrolled (its nine row offsets live in
+        // registers) and rings advance without divisions.
         if (lane == 0) {
-            uint32_t ia = 0, ib = 0, j = 0;
+            Ring ra, rb;
+            uint32_t j = 0;
             bool ok = true;
-            const uint32_t a_base = smem_u32(sm.a), b_base = smem_u32(sm.b);
+            const uint64_t a_desc = sw128_desc(smem_u32(sm.a)), b_desc = sw128_desc(smem_u32(sm.b));
+            const uint32_t a_stage = (uint32_t(C::kOps) * uint32_t(p.a_bytes)) >> 4, a_lo = uint32_t(p.a_bytes) >> 4;
+            constexpr uint32_t b_stage = (C::kOps * C::kBBytes) >> 4, b_lo = C::kBBytes >> 4;
+            uint32_t toff[9];
+            tap_offsets(p, toff);
             for (int tile = blockIdx.x; tile < p.ntiles && ok; tile += gridDim.x, ++j) {
                 const uint32_t acc = j & 1;
                 if (!(ok = mbar_wait(&sm.acc_empty[acc], ((j >> 1) & 1) ^ 1, p.err, kErrWaitMma))) break;
                 tc_fence_after();
                 const uint32_t d = tmem + acc * N;
                 for (int c = 0; c < p.nchunks && ok; ++c) {
-                    const int sa = ia % p.sa;
-                    if (!(ok = mbar_wait(&sm.a_full[sa], (ia / p.sa) & 1, p.err, kErrWaitMma))) break;
-                    const uint32_t abuf = a_base + uint32_t(sa) * C::kOps * p.a_bytes;
-                    for (int t = 0; t < p.taps; ++t) {
-                        const int sb = ib % p.sb;
-                        if (!(ok = mbar_wait(&sm.b_full[sb], (ib / p.sb) & 1, p.err, kErrWaitMma))) break;
+                    if (!(ok = mbar_wait(&sm.a_full[ra.idx], ra.phase, p.err, kErrWaitMma))) break;
+                    const uint64_t ac = a_desc + ra.idx * a_stage;
+#pragma unroll
+                    for (int t = 0; t < 9; ++t) {
+                        if (t >= p.taps) break;
+                        if (!(ok = mbar_wait(&sm.b_full[rb.idx], rb.phase, p.err, kErrWaitMma))) break;
                         tc_fence_after();
-                        const uint32_t bbuf = b_base + uint32_t(sb) * C::kOps * C::kBBytes;
-                        const int tap = p.taps == 9 ? t : 4;   // one tap: the centre view, a plain GEMM
-                        const int dy = tap / 3 - 1, dx = tap % 3 - 1;
-                        const uint32_t row = uint32_t(p.n + 2 + dy * (p.n + 1) + dx);
+                        const uint64_t at = ac + toff[t], bt = b_desc + rb.idx * b_stage;
+#pragma unroll
                         for (int k = 0; k < C::kSteps; ++k) {
-                            const uint32_t aoff = row * 128u + uint32_t(k) * 32u;
-                            const uint64_t ad = sw128_desc(abuf + aoff, p.base_offset_mode);
-                            const uint64_t bd = sw128_desc(bbuf + uint32_t(k) * 32u, p.base_offset_mode);
-                            const uint32_t accumulate = (c | t | k) != 0;
-                            umma<kBf16>(d, ad, bd, C::kIdesc, accumulate);
+                            umma<kBf16>(d, at + 2 * k, bt + 2 * k, C::kIdesc, (c | t | k) != 0);
                             if (kSplit) {
-                                const uint64_t bdl = sw128_desc(bbuf + C::kBBytes + uint32_t(k) * 32u, p.base_offset_mode);
-                                const uint64_t adl = sw128_desc(abuf + p.a_bytes + aoff, p.base_offset_mode);
-                                umma<kBf16>(d, ad, bdl, C::kIdesc, 1);
-                                umma<kBf16>(d, adl, bd, C::kIdesc, 1);
+                                umma<kBf16>(d, at + 2 * k, bt + b_lo + 2 * k, C::kIdesc, 1);
+                                umma<kBf16>(d, at + a_lo + 2 * k, bt + 2 * k, C::kIdesc, 1);
                             }
                         }
-                        umma_commit(&sm.b_empty[sb]);   // frees the weight buffer once read
-                        ++ib;
+                        umma_commit(&sm.b_empty[rb.idx]);   // frees the weight buffer once read
+                        rb.next(p.sb);
                     }
                     if (!ok) break;
-                    umma_commit(&sm.a_empty[sa]);       // frees the halo buffer
-                    ++ia;
+                    umma_commit(&sm.a_empty[ra.idx]);       // frees the halo buffer
+                    ra.next(p.sa);
                 }
                 if (!ok) break;
-                umma_commit(&sm.acc_full[acc]);         // the tile's accumulator is complete
+                umma_commit(&sm.acc_full[acc]);             // the tile's accumulator is complete
             }
             // All MMAs issued by this thread are complete before teardown.
             umma_commit(sm.done);
@@ -394,93 +420,99 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         // ---------------------------------------------------------- producer
         if (lane == 0) {
-            uint32_t ia = 0, ib = 0;
+            Ring ra, rb;
+            uint32_t na = 0, nb = 0;
             const uint32_t a_tx = uint32_t(p.halo_rows) * 128u * C::kOps * 2u;   // both CTAs
             const uint32_t b_tx = kHalfB * C::kOps * 2u;
+            const size_t a_stage = size_t(C::kOps) * p.a_bytes;
+            // Both CTAs' copies complete on the leader's full barriers.
+            const uint32_t a_full0 = mapa(smem_u32(sm.a_full), 0), b_full0 = mapa(smem_u32(sm.b_full), 0);
             bool ok = true;
             for (int pr = pair0; pr < npairs && ok; pr += pair_step) {
                 const int tile = 2 * pr + int(rank);
                 const int y0 = tile * 128 - (p.n + 2);
                 for (int c = 0; c < p.nchunks && ok; ++c) {
-                    const int sa = ia % p.sa;
-                    if (!(ok = mbar_wait(&sm.a_empty[sa], ((ia / p.sa) & 1) ^ 1, p.err, kErrWaitProducer))) break;
-                    if (leader) mbar_arrive_expect_tx(&sm.a_full[sa], a_tx);
-                    const uint32_t full = mapa(smem_u32(&sm.a_full[sa]), 0);
-                    uint8_t* abuf = sm.a + size_t(sa) * C::kOps * p.a_bytes;
+                    if (!(ok = mbar_wait(&sm.a_empty[ra.idx], ra.phase ^ 1u, p.err, kErrWaitProducer))) break;
+                    if (leader) mbar_arrive_expect_tx(&sm.a_full[ra.idx], a_tx);
+                    const uint32_t full = a_full0 + ra.idx * 8u;
+                    uint8_t* abuf = sm.a + ra.idx * a_stage;
                     tma_load_2d_pair(&mA, abuf, full, c * C::kKc, y0);
                     if (kSplit) tma_load_2d_pair(&mAlo, abuf + p.a_bytes, full, c * C::kKc, y0);
-                    ++ia;
+                    ra.next(p.sa);
+                    ++na;
                     for (int t = 0; t < p.taps; ++t) {
-                        const int sb = ib % p.sb;
-                        if (!(ok = mbar_wait(&sm.b_empty[sb], ((ib / p.sb) & 1) ^ 1, p.err, kErrWaitProducer))) break;
-                        if (leader) mbar_arrive_expect_tx(&sm.b_full[sb], b_tx);
-                        const uint32_t bfull = mapa(smem_u32(&sm.b_full[sb]), 0);
-                        uint8_t* bbuf = sm.b + size_t(sb) * C::kOps * kHalfB;
+                        if (!(ok = mbar_wait(&sm.b_empty[rb.idx], rb.phase ^ 1u, p.err, kErrWaitProducer))) break;
+                        if (leader) mbar_arrive_expect_tx(&sm.b_full[rb.idx], b_tx);
+                        const uint32_t bfull = b_full0 + rb.idx * 8u;
+                        uint8_t* bbuf = sm.b + rb.idx * (C::kOps * kHalfB);
                         const int x = (c * p.taps + t) * C::kKc, y = int(rank) * (N / 2);
                         tma_load_2d_pair(&mW, bbuf, bfull, x, y);
                         if (kSplit) tma_load_2d_pair(&mWlo, bbuf + kHalfB, bfull, x, y);
-                        ++ib;
+                        rb.next(p.sb);
+                        ++nb;
                     }
                 }
             }
             // The leader's full barriers count both CTAs' copies: once each
             // stage's last phase completed, every copy of the pair has landed.
             if (leader) {
-                for (uint32_t s = 0; s < uint32_t(p.sa) && s < ia; ++s)
-                    mbar_wait(&sm.a_full[s], ((ia - s + p.sa - 1) / p.sa - 1) & 1, p.err, kErrWaitDrain);
-                for (uint32_t s = 0; s < uint32_t(p.sb) && s < ib; ++s)
-                    mbar_wait(&sm.b_full[s], ((ib - s + p.sb - 1) / p.sb - 1) & 1, p.err, kErrWaitDrain);
+                for (uint32_t s = 0; s < uint32_t(p.sa) && s < na; ++s)
+                    mbar_wait(&sm.a_full[s], ((na - s + p.sa - 1) / p.sa - 1) & 1, p.err, kErrWaitDrain);
+                for (uint32_t s = 0; s < uint32_t(p.sb) && s < nb; ++s)
+                    mbar_wait(&sm.b_full[s], ((nb - s + p.sb - 1) / p.sb - 1) & 1, p.err, kErrWaitDrain);
             }
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issue (leader)
+        // As in the single-CTA form: descriptors advanced by additions, the
+        // tap loop unrolled, and the barrier addresses of both CTAs (for the
+        // commits that release each CTA's buffers) computed once.
         if (leader && lane == 0) {
-            uint32_t ia = 0, ib = 0, j = 0;
+            Ring ra, rb;
+            uint32_t j = 0;
             bool ok = true;
-            const uint32_t a_base = smem_u32(sm.a), b_base = smem_u32(sm.b);
-            auto both = [&](uint64_t* bar) {   // commit to this CTA's barrier and to the peer's
-                const uint32_t own = smem_u32(bar);
-                umma_commit_pair(mapa(own, 0));
-                umma_commit_pair(mapa(own, 1));
-            };
+            const uint64_t a_desc = sw128_desc(smem_u32(sm.a)), b_desc = sw128_desc(smem_u32(sm.b));
+            const uint32_t a_stage = (uint32_t(C::kOps) * uint32_t(p.a_bytes)) >> 4, a_lo = uint32_t(p.a_bytes) >> 4;
+            constexpr uint32_t b_stage = (C::kOps * kHalfB) >> 4, b_lo = kHalfB >> 4;
+            uint32_t toff[9];
+            tap_offsets(p, toff);
+            const uint32_t a_empty0 = mapa(smem_u32(sm.a_empty), 0), a_empty1 = mapa(smem_u32(sm.a_empty), 1);
+            const uint32_t b_empty0 = mapa(smem_u32(sm.b_empty), 0), b_empty1 = mapa(smem_u32(sm.b_empty), 1);
+            const uint32_t acc_full0 = mapa(smem_u32(sm.acc_full), 0), acc_full1 = mapa(smem_u32(sm.acc_full), 1);
             for (int pr = pair0; pr < npairs && ok; pr += pair_step, ++j) {
                 const uint32_t acc = j & 1;
                 if (!(ok = mbar_wait_cluster(&sm.acc_empty[acc], ((j >> 1) & 1) ^ 1, p.err, kErrWaitMma))) break;
                 tc_fence_after();
                 const uint32_t d = tmem + acc * N;
                 for (int c = 0; c < p.nchunks && ok; ++c) {
-                    const int sa = ia % p.sa;
-                    if (!(ok = mbar_wait(&sm.a_full[sa], (ia / p.sa) & 1, p.err, kErrWaitMma))) break;
-                    const uint32_t abuf = a_base + uint32_t(sa) * C::kOps * p.a_bytes;
-                    for (int t = 0; t < p.taps; ++t) {
-                        const int sb = ib % p.sb;
-                        if (!(ok = mbar_wait(&sm.b_full[sb], (ib / p.sb) & 1, p.err, kErrWaitMma))) break;
+                    if (!(ok = mbar_wait(&sm.a_full[ra.idx], ra.phase, p.err, kErrWaitMma))) break;
+                    const uint64_t ac = a_desc + ra.idx * a_stage;
+#pragma unroll
+                    for (int t = 0; t < 9; ++t) {
+                        if (t >= p.taps) break;
+                        if (!(ok = mbar_wait(&sm.b_full[rb.idx], rb.phase, p.err, kErrWaitMma))) break;
                         tc_fence_after();
-                        const uint32_t bbuf = b_base + uint32_t(sb) * C::kOps * kHalfB;
-                        const int tap = p.taps == 9 ? t : 4;
-                        const int dy = tap / 3 - 1, dx = tap % 3 - 1;
-                        const uint32_t row = uint32_t(p.n + 2 + dy * (p.n + 1) + dx);
+                        const uint64_t at = ac + toff[t], bt = b_desc + rb.idx * b_stage;
+#pragma unroll
                         for (int k = 0; k < C::kSteps; ++k) {
-                            const uint32_t aoff = row * 128u + uint32_t(k) * 32u;
-                            const uint64_t ad = sw128_desc(abuf + aoff, p.base_offset_mode);
-                            const uint64_t bd = sw128_desc(bbuf + uint32_t(k) * 32u, p.base_offset_mode);
-                            umma_pair<kBf16>(d, ad, bd, kIdesc, (c | t | k) != 0);
+                            umma_pair<kBf16>(d, at + 2 * k, bt + 2 * k, kIdesc, (c | t | k) != 0);
                             if (kSplit) {
-                                const uint64_t bdl = sw128_desc(bbuf + kHalfB + uint32_t(k) * 32u, p.base_offset_mode);
-                                const uint64_t adl = sw128_desc(abuf + p.a_bytes + aoff, p.base_offset_mode);
-                                umma_pair<kBf16>(d, ad, bdl, kIdesc, 1);
-                                umma_pair<kBf16>(d, adl, bd, kIdesc, 1);
+                                umma_pair<kBf16>(d, at + 2 * k, bt + b_lo + 2 * k, kIdesc, 1);
+                                umma_pair<kBf16>(d, at + a_lo + 2 * k, bt + 2 * k, kIdesc, 1);
                             }
                         }
-                        both(&sm.b_empty[sb]);
-                        ++ib;
+                        umma_commit_pair(b_empty0 + rb.idx * 8u);   // each CTA's weight half is free
+                        umma_commit_pair(b_empty1 + rb.idx * 8u);
+                        rb.next(p.sb);
                     }
                     if (!ok) break;
-                    both(&sm.a_empty[sa]);
-                    ++ia;
+                    umma_commit_pair(a_empty0 + ra.idx * 8u);
+                    umma_commit_pair(a_empty1 + ra.idx * 8u);
+                    ra.next(p.sa);
                 }
                 if (!ok) break;
-                both(&sm.acc_full[acc]);
+                umma_commit_pair(acc_full0 + acc * 8u);
+                umma_commit_pair(acc_full1 + acc * 8u);
             }
             umma_commit_pair(mapa(smem_u32(sm.done), 0));
             mbar_wait(sm.done, 0, p.err, kErrWaitDrain);
@@ -490,7 +522,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int quarter = warp & 3;
         const int row_in_tile = quarter * 32 + lane;
         const int n1 = p.n + 1;
-        const uint32_t leader_empty[2] = {mapa(smem_u32(&sm.acc_empty[0]), 0), mapa(smem_u32(&sm.acc_empty[1]), 0)};
+        const uint32_t leader_empty0 = mapa(smem_u32(&sm.acc_empty[0]), 0), leader_empty1 = leader_empty0 + 8u;
         uint32_t j = 0;
         for (int pr = pair0; pr < npairs; pr += pair_step, ++j) {
             const uint32_t acc = j & 1;
@@ -506,7 +538,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             store_epilogue<N, kBf16, kSplit>(p, taddr, q, valid);
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(leader_empty[acc]);
+            if (lane == 0) mbar_arrive_cluster(acc ? leader_empty1 : leader_empty0);
         }
     }
 
@@ -579,7 +611,7 @@ __global__ void __launch_bounds__(128, 1)
     }
 }
 
-std::atomic<int> g_conv_path{0};   // 0: choose (single CTA), 1: single CTA, 2: CTA pairs
+std::atomic<int> g_conv_path{0};   // 0: by width, 1: single CTA, 2: CTA pairs
 
 template <int N, bool kBf16, bool kSplit>
 cudaError_t launch_one(const ConvMaps& m, ConvArgs a, bool pair, int sms, cudaStream_t s) {
@@ -660,19 +692,21 @@ size_t conv_smem_bytes(int n_out, int precision, int halo_rows, int* sa_out, int
 
 void set_conv_path(int path) { g_conv_path = path; }
 
-// The single-CTA form is the default: measured on B200 at C4 it runs 5-10%
-// faster than the pair form (the pair's per-SM MMA rate is no better once
-// both CTAs' copies must land before each MMA, and its epilogue releases
-// cross the cluster); the pair form stays available for comparison.
-bool conv_uses_pairs(int ntiles) {
+// Which form a layer runs: by default the CTA pair for 256 output
+// channels, where a weight tile is 32 KB per tap and halving it per SM
+// pays (C4 bf16 on B200: 1217 against 1148 TFLOP/s per conv), and the
+// single-CTA form for narrower layers, whose weight tiles are small and
+// whose passes have fewer tiles to pair (C3 tf32: 393 against 329).
+bool conv_uses_pairs(int ntiles, int n_out) {
     const int path = g_conv_path.load();
+    if (path == 1) return false;
     if (path == 2) return ntiles >= 1;
-    return false;
+    return n_out == 256 && ntiles >= 2;
 }
 
 cudaError_t launch_conv(const ConvMaps& maps, const ConvArgs& a, int n_out, int precision, int sms, cudaStream_t s) {
     if (a.ntiles <= 0) return cudaSuccess;
-    const bool pair = conv_uses_pairs(a.ntiles);
+    const bool pair = conv_uses_pairs(a.ntiles, n_out);
     switch (precision) {
         case kTF32: return dispatch_n<false, false>(n_out, maps, a, pair, sms, s);
         case kTF32x3: return dispatch_n<false, true>(n_out, maps, a, pair, sms, s);

@@ -637,7 +637,6 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
     a.ld = w.cpad();
     a.halo_rows = fr.halo;
     a.a_bytes = (fr.halo * 128 + 1023) / 1024 * 1024;
-    a.base_offset_mode = 0;
     a.err = ws.err;
     auto conv = [&](int index, const CUtensorMap& in, const CUtensorMap& in_lo, int dst, const void* skip,
                     const void* skip_lo, int taps, int nchunks, int timer_slot) {

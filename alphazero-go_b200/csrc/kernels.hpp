@@ -58,7 +58,6 @@ struct ConvArgs {
     int halo_rows;     // 128 + 2(n+2)
     int a_bytes;       // one halo buffer, rounded up to 1024
     int sa, sb;        // pipeline depths: halo buffers, weight buffers
-    int base_offset_mode;   // shared-memory descriptor base offset form: 0 (the form the hardware reads)
     void* out;         // [rows][ld] bf16 or f32 (split: the tf32 high part)
     void* out_lo;      // split: f32 low part
     const void* skip;  // null, or the residual input (same layout as out)
@@ -78,11 +77,11 @@ struct ConvMaps {
 // CTA-pair form, which stages half of each weight tile per CTA).
 size_t conv_smem_bytes(int n_out, int precision, int halo_rows, int* sa, int* sb, bool pair = false);
 
-// Enqueues the conv on `s`: the single-CTA form, or the CTA-pair form
-// (2-CTA clusters, M = 256 per MMA) when the test hook selects it; the
-// pipeline depths in `a` are chosen here.
+// Enqueues the conv on `s`: the CTA-pair form (2-CTA clusters, M = 256 per
+// MMA) for 256 output channels, else the single-CTA form, unless the test
+// hook selects one; the pipeline depths in `a` are chosen here.
 cudaError_t launch_conv(const ConvMaps& maps, const ConvArgs& a, int n_out, int precision, int sms, cudaStream_t s);
-// Test hook: 0 default (single CTA), 1 single CTA, 2 CTA pairs.
+// Test hook: 0 by width (pairs at 256 output channels), 1 single CTA, 2 CTA pairs.
 void set_conv_path(int path);
 
 // The stem's packed operand: the [B][P][A] fp32 input unfolded into frame

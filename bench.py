@@ -30,6 +30,7 @@ OpenBLAS, all host cores) on the same config and metric instead.
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -71,7 +72,7 @@ def measured_peaks() -> dict:
 
 def profiled_traffic() -> float | None:
     """DRAM bytes per conv launch from the committed ncu summary, if any."""
-    path = os.path.join(ROOT, "profiles", "conv3x3_tc_bf16_c4.md")
+    path = os.path.join(ROOT, "profiles", "conv3x3_tc_pair_bf16_c4.md")
     try:
         for line in open(path):
             if line.startswith("traffic_bytes_per_launch:"):
@@ -85,9 +86,11 @@ def profiled_traffic() -> float | None:
 
 
 class ClockSampler:
-    """nvidia-smi sampled every 200 ms while the timed region runs."""
+    """nvidia-smi sampled every 200 ms; started before the warm-up (the tool
+    takes a moment to begin), kept to the samples taken inside the timed
+    region [mark_start, mark_stop] (the nearest one if none falls inside)."""
 
-    FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
     REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
@@ -96,6 +99,7 @@ class ClockSampler:
         self.bus_ids = [b.lower() for b in bus_ids if b]
         self.proc = None
         self.out = None
+        self.t0 = self.t1 = None
 
     def start(self):
         try:
@@ -104,7 +108,17 @@ class ClockSampler:
                                           "-lms", "200"], stdout=self.out, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return self
+        deadline = time.time() + 5.0   # until the first sample is written
+        while time.time() < deadline and os.path.getsize(self.out.name) == 0:
+            time.sleep(0.05)
         return self
+
+    def mark_start(self):
+        self.t0 = datetime.datetime.now()
+
+    def mark_stop(self):
+        self.t1 = datetime.datetime.now()
 
     def stop(self) -> dict | None:
         if self.proc is None:
@@ -120,26 +134,35 @@ class ClockSampler:
         rows = [r.split(",") for r in self.out.read().splitlines() if r.strip()]
         self.out.close()
         os.unlink(self.out.name)
-        sm, mx, reasons = [], [], set()
+        samples = []
         for r in rows:
             r = [c.strip() for c in r]
-            if len(r) < 10:
+            if len(r) < 11:
                 continue
-            bus = r[1].lower()
+            bus = r[2].lower()
             if self.bus_ids and not any(bus.endswith(b[-12:]) or b.endswith(bus[-12:]) for b in self.bus_ids):
                 continue
             try:
-                sm.append(float(r[2]))
-                mx.append(float(r[3]))
+                when = datetime.datetime.strptime(r[0], "%Y/%m/%d %H:%M:%S.%f")
+                samples.append((when, float(r[3]), float(r[4]), r[7:11]))
             except ValueError:
                 continue
-            for name, v in zip(self.REASONS, r[6:10]):
+        if not samples:
+            return None
+        inside = samples
+        if self.t0 and self.t1:
+            slack = datetime.timedelta(seconds=0.1)
+            inside = [x for x in samples if self.t0 - slack <= x[0] <= self.t1 + slack]
+            if not inside:
+                mid = self.t0 + (self.t1 - self.t0) / 2
+                inside = [min(samples, key=lambda x: abs((x[0] - mid).total_seconds()))]
+        reasons = set()
+        for x in inside:
+            for name, v in zip(self.REASONS, x[3]):
                 if v.lower() == "active":
                     reasons.add(name)
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return {"sm_mhz": statistics.median(x[1] for x in inside), "sm_max_mhz": max(x[2] for x in inside),
+                "reasons": sorted(reasons), "samples": len(inside)}
 
 
 # ---------------------------------------------------------- distributed
@@ -286,13 +309,15 @@ def run_engine(args, d: Dist):
     net.stage(x)
 
     # --- device-resident throughput: W untimed, then exactly K timed passes
+    sampler = ClockSampler([E.pci_bus_id(dev)] if d.world == 1 else []).start() if d.rank == 0 else None
     net.time(BATCH, 0, args.warmup)
-    sampler = ClockSampler([E.pci_bus_id(dev)] if d.world == 1 else []) if d.rank == 0 else None
     d.barrier()
     if sampler:
-        sampler.start()
+        sampler.mark_start()
     ms, _ = net.time(BATCH, 0, args.steps)
     d.barrier()
+    if sampler:
+        sampler.mark_stop()
     clocks = sampler.stop() if sampler else None
     ms = d.max(ms)
     value = d.world * BATCH * args.steps / (ms / 1e3)
@@ -385,7 +410,7 @@ def run_engine(args, d: Dist):
                     "how": "BatchRunner C ABI, 2 slots in flight, host wall clock, max over ranks"},
             "roofline": {"bound": "tensor", "achieved": conv_tflops, "peak": peak, "unit": "TFLOP/s",
                          "frac": conv_tflops / peak, "traffic": traffic, "peak_source": peak_note,
-                         "kernel": "conv3x3_tc<256,bf16>", "flop_per_launch": conv_flops_per_position() * BATCH,
+                         "kernel": "conv3x3_tc_pair<256,bf16>", "flop_per_launch": conv_flops_per_position() * BATCH,
                          "avg_launch_ms": conv_avg_ms},
             "tensor_tflops_whole_pass": flops_per_position() * BATCH * d.world * args.steps / (ms / 1e3) / 1e12,
             "gpu_launches": args.steps * (2 * BLOCKS + 2),

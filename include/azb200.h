@@ -190,9 +190,10 @@ void azb_probe_fail_passes_after(int n);
 void azb_probe_set_memory_limit(size_t bytes);
 long long azb_probe_passes_completed(void);
 void azb_probe_set_copy_out_delay(int microseconds);
-/* Which tensor-core conv form passes use: 0 the default (one CTA per
- * 128-row tile), 1 the same, 2 CTA pairs (2-CTA clusters, M = 256 per MMA,
- * tcgen05 cta_group::2). For tests and measurements comparing the forms. */
+/* Which tensor-core conv form passes use: 0 the default (CTA pairs, i.e.
+ * 2-CTA clusters with M = 256 per MMA via tcgen05 cta_group::2, for layers
+ * of 256 output channels; one CTA per 128-row tile otherwise), 1 always one
+ * CTA per tile, 2 always CTA pairs. For tests and measurements. */
 void azb_probe_set_conv_path(int path);
 /* cuda_probe::binaryVersion / deviceArchitecture / fill (include/azgo/cuda.hpp:93-103). */
 int azb_probe_binary_version(int device);
