@@ -88,6 +88,7 @@ def lib() -> C.CDLL:
             L.azb_infer_stream.restype = C.c_void_p
             L.azb_infer_time.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double),
                                          C.POINTER(C.c_double)] + err
+            L.azb_infer_time_stages.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_double), C.c_char_p, C.c_size_t]
             L.azb_infer_read.argtypes = [C.c_void_p, C.c_int, _F, _F, _F, _F] + err
             L.azb_runner_create.argtypes = [D, _F, s, _F, s, C.c_int, C.c_int, C.c_int, C.c_int,
                                             C.POINTER(C.c_void_p)] + err
@@ -289,6 +290,16 @@ class CudaInference:
         if rc != 0:
             raise CudaError(e.value.decode())
         return ms.value, (cms.value if conv else None)
+
+    STAGES = ("stem_operand", "stem_gemm", "tower", "head_conv", "head_fc", "head_out")
+
+    def time_stages(self, B: int, steps: int) -> dict:
+        """Device ms per stage, summed over `steps` passes (events around every launch)."""
+        out = (C.c_double * len(self.STAGES))()
+        e = _err()
+        if lib().azb_infer_time_stages(self.h, B, steps, out, e, 1024) != 0:
+            raise CudaError(e.value.decode())
+        return dict(zip(self.STAGES, list(out)))
 
     def read(self, B: int):
         d = self.desc

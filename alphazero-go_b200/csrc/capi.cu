@@ -120,6 +120,14 @@ int azb_infer_time(azb_infer* h, int B, int warmup, int steps, int with_copies, 
                    [&] { h->impl->time(B, warmup, steps, with_copies != 0, ms, conv_ms); });
 }
 
+int azb_infer_time_stages(azb_infer* h, int B, int steps, double* stage_ms, char* err, size_t err_cap) {
+    return guarded(err, err_cap, "GPU inference failed: ", [&] {
+        if (!stage_ms) throw std::invalid_argument("azb_infer_time_stages: null stage_ms");
+        double ms = 0.0;
+        h->impl->time(B, 0, steps, false, &ms, nullptr, stage_ms);
+    });
+}
+
 int azb_infer_read(azb_infer* h, int B, float* logits, float* values, float* ownership, float* probs, char* err,
                    size_t err_cap) {
     return guarded(err, err_cap, "GPU inference failed: ",

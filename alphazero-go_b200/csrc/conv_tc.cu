@@ -42,6 +42,11 @@ struct ConvCfg {
     static constexpr uint32_t kBBytes = uint32_t(N) * 128u;
     static constexpr uint32_t kTmemCols = 2 * N <= 64 ? 64 : (2 * N <= 128 ? 128 : (2 * N <= 256 ? 256 : 512));
     static constexpr uint32_t kIdesc = umma_idesc(N, kBf16);
+    // bf16 stores its output (and reads its residual input) through shared
+    // memory with TMA: per epilogue warp two 2 KB output boxes and two 2 KB
+    // residual boxes ({32 channels, 32 rows}, 64-byte swizzle).
+    static constexpr bool kEpiTma = kBf16 && !kSplit;
+    static constexpr uint32_t kEpiBytes = kEpiTma ? 4u * 4u * 2048u : 0u;
     static_assert(N % 32 == 0 && N >= 32 && N <= 256, "N is a multiple of 32 in [32, 256]");
 };
 
@@ -52,16 +57,20 @@ constexpr int kMaxStages = 8;
 struct Smem {
     uint8_t* a;
     uint8_t* b;
+    uint8_t* epi;   // bf16 epilogue boxes (4 warps x 8 KB), or nothing
     uint64_t *a_full, *a_empty, *b_full, *b_empty, *acc_full, *acc_empty, *done;
+    uint64_t* skip_full;   // 4 warps x 2 residual boxes
     uint32_t* tmem_slot;
 };
 
-__device__ __forceinline__ Smem carve(uint8_t* raw, int sa, int sb, int ops, int a_bytes, uint32_t b_bytes) {
+__device__ __forceinline__ Smem carve(uint8_t* raw, int sa, int sb, int ops, int a_bytes, uint32_t b_bytes,
+                                      uint32_t epi_bytes) {
     Smem s;
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
     s.a = base;
     s.b = base + size_t(sa) * ops * a_bytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(s.b + size_t(sb) * ops * b_bytes);
+    s.epi = s.b + size_t(sb) * ops * b_bytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(s.epi + epi_bytes);
     s.a_full = bars;
     s.a_empty = s.a_full + sa;
     s.b_full = s.a_empty + sa;
@@ -69,25 +78,15 @@ __device__ __forceinline__ Smem carve(uint8_t* raw, int sa, int sb, int ops, int
     s.acc_full = s.b_empty + sb;
     s.acc_empty = s.acc_full + 2;
     s.done = s.acc_empty + 2;
-    s.tmem_slot = reinterpret_cast<uint32_t*>(s.done + 1);
+    s.skip_full = s.done + 1;
+    s.tmem_slot = reinterpret_cast<uint32_t*>(s.skip_full + 8);
     return s;
 }
 
-__host__ __device__ constexpr size_t smem_total(int sa, int sb, int ops, int a_bytes, uint32_t b_bytes) {
-    return 1024 + size_t(sa) * ops * a_bytes + size_t(sb) * ops * b_bytes + (2 * sa + 2 * sb + 5) * 8 + 16;
+__host__ __device__ constexpr size_t smem_total(int sa, int sb, int ops, int a_bytes, uint32_t b_bytes,
+                                                uint32_t epi_bytes) {
+    return 1024 + size_t(sa) * ops * a_bytes + size_t(sb) * ops * b_bytes + epi_bytes + (2 * sa + 2 * sb + 13) * 8 + 16;
 }
-
-// A position in a ring of pipeline stages: the stage and the parity of
-// its current phase, advanced by a compare instead of a division.
-struct Ring {
-    uint32_t idx = 0, phase = 0;
-    __device__ __forceinline__ void next(uint32_t stages) {
-        if (++idx == stages) {
-            idx = 0;
-            phase ^= 1u;
-        }
-    }
-};
 
 // The nine tap views' start rows inside a halo tile, as descriptor
 // increments (16-byte units): halo row n+2 + dy(n+1) + dx is frame row
@@ -188,13 +187,97 @@ __device__ __forceinline__ void store_epilogue(const ConvArgs& p, uint32_t taddr
     }
 }
 
+// One epilogue warp's share of a tile in bf16 (32 rows from row0, all N
+// channels), through shared memory: per 32-channel chunk the warp's lanes
+// (one row each) write ReLU(scale * acc + shift (+ skip)) as bf16 into a
+// 2 KB box, swizzled as TMA's 64-byte swizzle lays it out (16-byte piece u
+// of row r at piece u ^ ((r >> 1) & 3): conflict-free), and one lane stores
+// the box with TMA. Padding rows are stored as zeros (they must stay zero),
+// rows past the frame are clipped by TMA. The residual input arrives the
+// same way, one chunk ahead, in two 2 KB boxes. Same arithmetic as
+// store_epilogue.
+struct EpiWarp {
+    uint8_t* obuf;        // 2 output boxes
+    uint8_t* sbuf;        // 2 residual boxes
+    uint64_t* sbar;       // their 2 barriers
+    uint32_t sphase = 0;  // bit i: parity of sbar[i]'s next phase
+};
+
+template <int N>
+__device__ __forceinline__ void store_epilogue_tma(const ConvArgs& p, const CUtensorMap* omap, const CUtensorMap* smap,
+                                                   uint32_t taddr, int row0, bool valid, EpiWarp& ew, int lane) {
+    constexpr int kChunks = N / 32;
+    constexpr uint32_t kBox = 2048;
+    if (row0 >= p.rows) return;   // all 32 rows past the frame: nothing to store
+    const bool skip = p.skip != nullptr;
+    const uint32_t swz = uint32_t((lane >> 1) & 3);
+    if (skip && lane == 0) {
+        mbar_arrive_expect_tx(&ew.sbar[0], kBox);
+        tma_load_2d(smap, ew.sbuf, &ew.sbar[0], 0, row0);
+    }
+#pragma unroll 1
+    for (int c = 0; c < kChunks; ++c) {
+        const int cb = c & 1;
+        if (skip && c + 1 < kChunks && lane == 0) {   // the other box was last read in chunk c-1
+            mbar_arrive_expect_tx(&ew.sbar[cb ^ 1], kBox);
+            tma_load_2d(smap, ew.sbuf + (cb ^ 1) * kBox, &ew.sbar[cb ^ 1], (c + 1) * 32, row0);
+        }
+        uint32_t v[32];
+        tmem_ld32(taddr + uint32_t(c) * 32u, v);
+        tmem_wait_ld();
+        float y[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            y[i] = __fadd_rn(__fmul_rn(__ldg(p.scale + c * 32 + i), __uint_as_float(v[i])), __ldg(p.shift + c * 32 + i));
+        if (skip) {
+            mbar_wait(&ew.sbar[cb], (ew.sphase >> cb) & 1u, p.err, kErrWaitEpilogue);
+            ew.sphase ^= 1u << cb;
+            const uint8_t* row = ew.sbuf + cb * kBox + uint32_t(lane) * 64u;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint4 w4 = *reinterpret_cast<const uint4*>(row + ((uint32_t(u) ^ swz) << 4));
+                const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&w4);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = __bfloat1622float2(h2[e]);
+                    y[u * 8 + 2 * e] = __fadd_rn(y[u * 8 + 2 * e], f.x);
+                    y[u * 8 + 2 * e + 1] = __fadd_rn(y[u * 8 + 2 * e + 1], f.y);
+                }
+            }
+        }
+        uint4 out[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&out[u]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float a0 = y[u * 8 + 2 * e], a1 = y[u * 8 + 2 * e + 1];
+                h2[e] = valid ? __floats2bfloat162_rn(a0 > 0.0f ? a0 : 0.0f, a1 > 0.0f ? a1 : 0.0f)
+                              : __floats2bfloat162_rn(0.0f, 0.0f);
+            }
+        }
+        if (lane == 0) bulk_wait_read<1>();   // the store from this box two chunks ago has read it
+        __syncwarp();
+        uint8_t* orow = ew.obuf + cb * kBox + uint32_t(lane) * 64u;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) *reinterpret_cast<uint4*>(orow + ((uint32_t(u) ^ swz) << 4)) = out[u];
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            tma_store_2d(omap, ew.obuf + cb * kBox, c * 32, row0);
+            bulk_commit();
+        }
+    }
+}
+
 template <int N, bool kBf16, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
     conv3x3_tc(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAlo,
-               const __grid_constant__ CUtensorMap mW, const __grid_constant__ CUtensorMap mWlo, const ConvArgs p) {
+               const __grid_constant__ CUtensorMap mW, const __grid_constant__ CUtensorMap mWlo,
+               const __grid_constant__ CUtensorMap mOut, const __grid_constant__ CUtensorMap mSkip, const ConvArgs p) {
     using C = ConvCfg<N, kBf16, kSplit>;
     extern __shared__ uint8_t smem_raw[];
-    const Smem sm = carve(smem_raw, p.sa, p.sb, C::kOps, p.a_bytes, C::kBBytes);
+    const Smem sm = carve(smem_raw, p.sa, p.sb, C::kOps, p.a_bytes, C::kBBytes, C::kEpiBytes);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
@@ -211,11 +294,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&sm.acc_empty[i], 128);
         }
         mbar_init(sm.done, 1);
+        for (int i = 0; i < 8; ++i) mbar_init(&sm.skip_full[i], 1);
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
         tma_prefetch_map(&mA);
         tma_prefetch_map(&mW);
+        if (C::kEpiTma) {
+            tma_prefetch_map(&mOut);
+            tma_prefetch_map(&mSkip);
+        }
         if (kSplit) {
             tma_prefetch_map(&mAlo);
             tma_prefetch_map(&mWlo);
@@ -324,6 +412,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int quarter = warp & 3;                 // TMEM lanes this warp may read
         const int row_in_tile = quarter * 32 + lane;
         const int n1 = p.n + 1;
+        EpiWarp ew;
+        ew.obuf = sm.epi + quarter * 8192;
+        ew.sbuf = ew.obuf + 4096;
+        ew.sbar = sm.skip_full + 2 * quarter;
         uint32_t j = 0;
         for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++j) {
             const uint32_t acc = j & 1;
@@ -336,10 +428,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 valid = r >= n1 && (r % n1) != p.n;
             }
             const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + acc * N;
-            store_epilogue<N, kBf16, kSplit>(p, taddr, q, valid);
+            if constexpr (C::kEpiTma) store_epilogue_tma<N>(p, &mOut, &mSkip, taddr, tile * 128 + quarter * 32, valid, ew, lane);
+            else store_epilogue<N, kBf16, kSplit>(p, taddr, q, valid);
             tc_fence_before();
             mbar_arrive(&sm.acc_empty[acc]);
         }
+        if (C::kEpiTma && lane == 0) bulk_wait_all();   // every output box written before the CTA exits
     }
 
     tc_fence_before();
@@ -374,12 +468,13 @@ template <int N, bool kBf16, bool kSplit>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     conv3x3_tc_pair(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAlo,
                     const __grid_constant__ CUtensorMap mW, const __grid_constant__ CUtensorMap mWlo,
+                    const __grid_constant__ CUtensorMap mOut, const __grid_constant__ CUtensorMap mSkip,
                     const ConvArgs p) {
     using C = ConvCfg<N, kBf16, kSplit>;
     constexpr uint32_t kHalfB = uint32_t(N / 2) * 128u;     // this CTA's half of a weight tile
     constexpr uint32_t kIdesc = umma_idesc(N, kBf16, 256);
     extern __shared__ uint8_t smem_raw[];
-    const Smem sm = carve(smem_raw, p.sa, p.sb, C::kOps, p.a_bytes, kHalfB);
+    const Smem sm = carve(smem_raw, p.sa, p.sb, C::kOps, p.a_bytes, kHalfB, C::kEpiBytes);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_rank();
     const bool leader = rank == 0;
@@ -398,11 +493,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mbar_init(&sm.acc_empty[i], 8);   // 4 epilogue warps x 2 CTAs
         }
         mbar_init(sm.done, 1);
+        for (int i = 0; i < 8; ++i) mbar_init(&sm.skip_full[i], 1);
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
         tma_prefetch_map(&mA);
         tma_prefetch_map(&mW);
+        if (C::kEpiTma) {
+            tma_prefetch_map(&mOut);
+            tma_prefetch_map(&mSkip);
+        }
         if (kSplit) {
             tma_prefetch_map(&mAlo);
             tma_prefetch_map(&mWlo);
@@ -523,6 +623,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int row_in_tile = quarter * 32 + lane;
         const int n1 = p.n + 1;
         const uint32_t leader_empty0 = mapa(smem_u32(&sm.acc_empty[0]), 0), leader_empty1 = leader_empty0 + 8u;
+        EpiWarp ew;
+        ew.obuf = sm.epi + quarter * 8192;
+        ew.sbuf = ew.obuf + 4096;
+        ew.sbar = sm.skip_full + 2 * quarter;
         uint32_t j = 0;
         for (int pr = pair0; pr < npairs; pr += pair_step, ++j) {
             const uint32_t acc = j & 1;
@@ -535,11 +639,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 valid = r >= n1 && (r % n1) != p.n;
             }
             const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + acc * N;
-            store_epilogue<N, kBf16, kSplit>(p, taddr, q, valid);
+            if constexpr (C::kEpiTma)
+                store_epilogue_tma<N>(p, &mOut, &mSkip, taddr, (2 * pr + int(rank)) * 128 + quarter * 32, valid, ew, lane);
+            else
+                store_epilogue<N, kBf16, kSplit>(p, taddr, q, valid);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(acc ? leader_empty1 : leader_empty0);
         }
+        if (C::kEpiTma && lane == 0) bulk_wait_all();
     }
 
     tc_fence_before();
@@ -618,7 +726,7 @@ cudaError_t launch_one(const ConvMaps& m, ConvArgs a, bool pair, int sms, cudaSt
     using C = ConvCfg<N, kBf16, kSplit>;
     const uint32_t b_bytes = pair ? C::kBBytes / 2 : C::kBBytes;
     conv_smem_bytes(N, kBf16 ? kBF16 : (kSplit ? kTF32x3 : kTF32), a.halo_rows, &a.sa, &a.sb, pair);
-    const size_t smem = smem_total(a.sa, a.sb, C::kOps, a.a_bytes, b_bytes);
+    const size_t smem = smem_total(a.sa, a.sb, C::kOps, a.a_bytes, b_bytes, C::kEpiBytes);
     if (pair) {
         static std::atomic<size_t> configured{0};
         if (smem > configured.load()) {
@@ -629,7 +737,7 @@ cudaError_t launch_one(const ConvMaps& m, ConvArgs a, bool pair, int sms, cudaSt
         }
         const int pairs = (a.ntiles + 1) / 2;
         const int grid = 2 * std::max(1, std::min(pairs, sms / 2));
-        conv3x3_tc_pair<N, kBf16, kSplit><<<grid, kThreads, smem, s>>>(m.a, m.a_lo, m.w_pair, m.w_lo_pair, a);
+        conv3x3_tc_pair<N, kBf16, kSplit><<<grid, kThreads, smem, s>>>(m.a, m.a_lo, m.w_pair, m.w_lo_pair, m.out, m.skip, a);
     } else {
         static std::atomic<size_t> configured{0};   // the largest size this instantiation was opened for
         if (smem > configured.load()) {
@@ -639,7 +747,7 @@ cudaError_t launch_one(const ConvMaps& m, ConvArgs a, bool pair, int sms, cudaSt
             configured = smem;
         }
         const int grid = std::max(1, std::min(a.ntiles, sms));
-        conv3x3_tc<N, kBf16, kSplit><<<grid, kThreads, smem, s>>>(m.a, m.a_lo, m.w, m.w_lo, a);
+        conv3x3_tc<N, kBf16, kSplit><<<grid, kThreads, smem, s>>>(m.a, m.a_lo, m.w, m.w_lo, m.out, m.skip, a);
     }
     return cudaGetLastError();
 }
@@ -673,21 +781,22 @@ size_t conv_smem_bytes(int n_out, int precision, int halo_rows, int* sa_out, int
     const int ops = precision == kTF32x3 ? 2 : 1;
     const int a_bytes = (halo_rows * 128 + 1023) / 1024 * 1024;
     const uint32_t b_bytes = uint32_t(pair ? n_out / 2 : n_out) * 128u;
+    const uint32_t epi = precision == kBF16 ? 4u * 4u * 2048u : 0u;   // ConvCfg::kEpiBytes
     constexpr size_t kMax = 227 * 1024;
     int sa = 2, sb = 2;
     for (int cand = kMaxStages; cand >= 2; --cand)
-        if (smem_total(2, cand, ops, a_bytes, b_bytes) <= kMax) {
+        if (smem_total(2, cand, ops, a_bytes, b_bytes, epi) <= kMax) {
             sb = cand;
             break;
         }
     // A third halo buffer only if it still leaves four weight buffers.
-    if (smem_total(3, std::max(sb - 1, 4), ops, a_bytes, b_bytes) <= kMax && sb >= 5) {
+    if (smem_total(3, std::max(sb - 1, 4), ops, a_bytes, b_bytes, epi) <= kMax && sb >= 5) {
         sa = 3;
-        while (sb > 2 && smem_total(sa, sb, ops, a_bytes, b_bytes) > kMax) --sb;
+        while (sb > 2 && smem_total(sa, sb, ops, a_bytes, b_bytes, epi) > kMax) --sb;
     }
     if (sa_out) *sa_out = sa;
     if (sb_out) *sb_out = sb;
-    return smem_total(sa, sb, ops, a_bytes, b_bytes);
+    return smem_total(sa, sb, ops, a_bytes, b_bytes, epi);
 }
 
 void set_conv_path(int path) { g_conv_path = path; }

@@ -280,7 +280,7 @@ struct Carver {
 // A row-major [rows][inner] tensor read in boxes of box_inner x box_rows
 // with the 128-byte swizzle; rows outside [0, rows) read as zero.
 CUtensorMap make_tensor_map(const void* base, int precision, uint64_t inner, uint64_t rows, uint32_t box_inner,
-                     uint32_t box_rows) {
+                     uint32_t box_rows, int swizzle_bytes) {
     CUtensorMap m;
     const size_t esz = size_t(elem_bytes(precision));
     const cuuint64_t dims[2] = {inner, rows};
@@ -289,7 +289,8 @@ CUtensorMap make_tensor_map(const void* base, int precision, uint64_t inner, uin
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = encode_tiled()(&m, precision == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                                       2, const_cast<void*>(base), dims, strides, box, estr,
-                                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                      swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw std::runtime_error("cuda: cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
     return m;
@@ -314,12 +315,12 @@ size_t Weights::bytes_for(const NetShape& s, int precision) {
     c.take(2 * size_t(F) * 4);
     c.take(8);
     c.take(8);
-    c.take((A + 1) * 2 * A * 4);
+    c.take((A + 1) * ((2 * A + 3) / 4 * 4) * 4);   // policy FC rows padded to 4 inputs
     c.take((A + 1) * 4);
     c.take(size_t(F) * 4);
     c.take(4);
     c.take(4);
-    c.take(V * A * 4);
+    c.take(V * ((A + 3) / 4 * 4) * 4);             // value FC1 rows padded to 4 inputs
     c.take(V * 4);
     c.take(V * 4);
     c.take(4);
@@ -356,6 +357,7 @@ Weights::Weights(const NetShape& s, int precision, int device, const float* para
     Carver c;
     auto put = [&](const void* src, size_t bytes) {
         const size_t off = c.take(bytes);
+        if (off + bytes > img.size()) throw std::logic_error("azb: weight image layout out of step with bytes_for");
         std::memcpy(img.data() + off, src, bytes);
         return off;
     };
@@ -404,25 +406,27 @@ Weights::Weights(const NetShape& s, int precision, int device, const float* para
         pack(size_t(1 + i), blk + (i % 2 ? ".conv2.w" : ".conv1.w"), blk + (i % 2 ? ".bn2" : ".bn1"), F, size_t(Kp),
              [&](int ci, int t) { return size_t((ci / KC) * 9 + t) * KC + ci % KC; });
     }
-    // heads: the FC weights input-major ([in][out]) so the head kernel's
-    // thread-per-output loops read them coalesced.
-    auto transpose = [](const float* w, int out, int in) {
-        std::vector<float> t(size_t(out) * in);
+    // heads: the FC weights output-major as the reference stores them
+    // ([out][in]), each row padded with zeros to a multiple of 4 inputs so
+    // the FC kernel reads it in 16-byte pieces.
+    auto pad_rows = [](const float* w, int out, int in) {
+        const int in4 = (in + 3) / 4 * 4;
+        std::vector<float> t(size_t(out) * in4, 0.0f);
         for (int o = 0; o < out; ++o)
-            for (int i = 0; i < in; ++i) t[size_t(i) * out + o] = w[size_t(o) * in + i];
+            for (int i = 0; i < in; ++i) t[size_t(o) * in4 + i] = w[size_t(o) * in + i];
         return t;
     };
     std::vector<float> hsc(2), hsh(2);
     const size_t o_pw = put(P_("policy.conv.w"), size_t(2) * F * 4);
     fold_bn(P_("policy.bn.gamma"), P_("policy.bn.beta"), B_("policy.bn.runMean"), B_("policy.bn.runVar"), 2, hsc.data(), hsh.data());
     const size_t o_psc = put(hsc.data(), 8), o_psh = put(hsh.data(), 8);
-    const std::vector<float> fct = transpose(P_("policy.fc.w"), A + 1, 2 * A);
+    const std::vector<float> fct = pad_rows(P_("policy.fc.w"), A + 1, 2 * A);
     const size_t o_fcw = put(fct.data(), fct.size() * 4);
     const size_t o_fcb = put(P_("policy.fc.b"), size_t(A + 1) * 4);
     const size_t o_vw = put(P_("value.conv.w"), size_t(F) * 4);
     fold_bn(P_("value.bn.gamma"), P_("value.bn.beta"), B_("value.bn.runMean"), B_("value.bn.runVar"), 1, hsc.data(), hsh.data());
     const size_t o_vsc = put(hsc.data(), 4), o_vsh = put(hsh.data(), 4);
-    const std::vector<float> v1t = transpose(P_("value.fc1.w"), V, A);
+    const std::vector<float> v1t = pad_rows(P_("value.fc1.w"), V, A);
     const size_t o_v1w = put(v1t.data(), v1t.size() * 4);
     const size_t o_v1b = put(P_("value.fc1.b"), size_t(V) * 4);
     const size_t o_v2w = put(P_("value.fc2.w"), size_t(V) * 4);
@@ -474,12 +478,12 @@ Weights::Weights(const NetShape& s, int precision, int device, const float* para
     head_.pol_w = at(o_pw);
     head_.pol_scale = at(o_psc);
     head_.pol_shift = at(o_psh);
-    head_.fc_wt = at(o_fcw);
+    head_.fc_w = at(o_fcw);
     head_.fc_b = at(o_fcb);
     head_.val_w = at(o_vw);
     head_.val_scale = at(o_vsc);
     head_.val_shift = at(o_vsh);
-    head_.v1_wt = at(o_v1w);
+    head_.v1_w = at(o_v1w);
     head_.v1_b = at(o_v1b);
     head_.v2_w = at(o_v2w);
     head_.v2_b = at(o_v2b);
@@ -516,60 +520,20 @@ size_t Workspace::bytes_for(const NetShape& s, int precision, int max_batch) {
     c.take(B * 4);
     if (s.ownership) c.take(B * A * 4);
     c.take(B * L * 4);
+    c.take(B * 3 * A * 4);
+    c.take(B * size_t(s.value_hidden) * 4);
     c.take(16);
     return c.used;
 }
 
-Workspace::Workspace(const Weights& w, int max_batch) : max_batch_(max_batch) {
-    if (max_batch < 1) throw std::invalid_argument("azb: max_batch must be >= 1");
+// The same carving as bytes_for, from `base`.
+void Workspace::place(const Weights& w, uint8_t* base) {
     const NetShape& s = w.shape();
     const int precision = w.precision();
     const Frame fr(s.board);
-    const size_t rows = size_t(max_batch) * fr.S;
+    const size_t rows = size_t(max_batch_) * fr.S;
     const size_t cpad = size_t(w.cpad()), esz = size_t(elem_bytes(precision));
-    const size_t A = size_t(s.area()), L = size_t(s.actions()), B = size_t(max_batch);
-    bytes_ = bytes_for(s, precision, max_batch);
-    check(cudaSetDevice(w.device()), "cudaSetDevice");
-    check(cudaMalloc(&arena_, bytes_), "cudaMalloc workspace");
-    // Zero once: the frames' padding rows are never written again.
-    const cudaError_t z = cudaMemset(arena_, 0, bytes_);
-    if (z != cudaSuccess) {
-        cudaFree(arena_);
-        check(z, "cudaMemset workspace");
-    }
-    Carver c;
-    auto at = [&](size_t off) { return static_cast<uint8_t*>(arena_) + off; };
-    stage = reinterpret_cast<float*>(at(c.take(B * s.planes() * A * 4)));
-    const size_t ks = size_t(w.kstem());
-    stem_in = at(c.take(rows * ks * esz));
-    if (precision == kTF32x3) stem_in_lo = at(c.take(rows * ks * 4));
-    for (int i = 0; i < 3; ++i) trunk[i] = at(c.take(rows * cpad * esz));
-    if (precision == kTF32x3)
-        for (int i = 0; i < 3; ++i) trunk_lo[i] = at(c.take(rows * cpad * 4));
-    logits = reinterpret_cast<float*>(at(c.take(B * L * 4)));
-    values = reinterpret_cast<float*>(at(c.take(B * 4)));
-    if (s.ownership) ownership = reinterpret_cast<float*>(at(c.take(B * A * 4)));
-    probs = reinterpret_cast<float*>(at(c.take(B * L * 4)));
-    err = reinterpret_cast<int*>(at(c.take(16)));
-    const uint32_t KC = uint32_t(chunk_channels(precision));
-    map_stem = make_tensor_map(stem_in, precision, ks, rows, KC, uint32_t(fr.halo));
-    map_stem_lo = precision == kTF32x3 ? make_tensor_map(stem_in_lo, precision, ks, rows, KC, uint32_t(fr.halo)) : map_stem;
-    for (int i = 0; i < 3; ++i) {
-        map[i] = make_tensor_map(trunk[i], precision, cpad, rows, KC, uint32_t(fr.halo));
-        map_lo[i] = precision == kTF32x3 ? make_tensor_map(trunk_lo[i], precision, cpad, rows, KC, uint32_t(fr.halo)) : map[i];
-    }
-}
-
-Workspace::Workspace(const Weights& w, int max_batch, void* memory) : max_batch_(max_batch) {
-    if (max_batch < 1) throw std::invalid_argument("azb: max_batch must be >= 1");
-    const NetShape& s = w.shape();
-    const int precision = w.precision();
-    const Frame fr(s.board);
-    const size_t rows = size_t(max_batch) * fr.S;
-    const size_t cpad = size_t(w.cpad()), esz = size_t(elem_bytes(precision));
-    const size_t A = size_t(s.area()), L = size_t(s.actions()), B = size_t(max_batch);
-    bytes_ = bytes_for(s, precision, max_batch);
-    uint8_t* base = static_cast<uint8_t*>(memory);
+    const size_t A = size_t(s.area()), L = size_t(s.actions()), B = size_t(max_batch_);
     Carver c;
     auto at = [&](size_t off) { return base + off; };
     stage = reinterpret_cast<float*>(at(c.take(B * s.planes() * A * 4)));
@@ -583,6 +547,8 @@ Workspace::Workspace(const Weights& w, int max_batch, void* memory) : max_batch_
     values = reinterpret_cast<float*>(at(c.take(B * 4)));
     if (s.ownership) ownership = reinterpret_cast<float*>(at(c.take(B * A * 4)));
     probs = reinterpret_cast<float*>(at(c.take(B * L * 4)));
+    feat = reinterpret_cast<float*>(at(c.take(B * 3 * A * 4)));
+    hid = reinterpret_cast<float*>(at(c.take(B * size_t(s.value_hidden) * 4)));
     err = reinterpret_cast<int*>(at(c.take(16)));
     const uint32_t KC = uint32_t(chunk_channels(precision));
     map_stem = make_tensor_map(stem_in, precision, ks, rows, KC, uint32_t(fr.halo));
@@ -590,7 +556,29 @@ Workspace::Workspace(const Weights& w, int max_batch, void* memory) : max_batch_
     for (int i = 0; i < 3; ++i) {
         map[i] = make_tensor_map(trunk[i], precision, cpad, rows, KC, uint32_t(fr.halo));
         map_lo[i] = precision == kTF32x3 ? make_tensor_map(trunk_lo[i], precision, cpad, rows, KC, uint32_t(fr.halo)) : map[i];
+        // bf16 conv epilogue boxes: {32 channels, 32 rows}, 64-byte rows, 64-byte swizzle.
+        emap[i] = precision == kBF16 ? make_tensor_map(trunk[i], precision, cpad, rows, 32, 32, 64) : map[i];
     }
+}
+
+Workspace::Workspace(const Weights& w, int max_batch) : max_batch_(max_batch) {
+    if (max_batch < 1) throw std::invalid_argument("azb: max_batch must be >= 1");
+    bytes_ = bytes_for(w.shape(), w.precision(), max_batch);
+    check(cudaSetDevice(w.device()), "cudaSetDevice");
+    check(cudaMalloc(&arena_, bytes_), "cudaMalloc workspace");
+    // Zero once: the frames' padding rows are never written again.
+    const cudaError_t z = cudaMemset(arena_, 0, bytes_);
+    if (z != cudaSuccess) {
+        cudaFree(arena_);
+        check(z, "cudaMemset workspace");
+    }
+    place(w, static_cast<uint8_t*>(arena_));
+}
+
+Workspace::Workspace(const Weights& w, int max_batch, void* memory) : max_batch_(max_batch) {
+    if (max_batch < 1) throw std::invalid_argument("azb: max_batch must be >= 1");
+    bytes_ = bytes_for(w.shape(), w.precision(), max_batch);
+    place(w, static_cast<uint8_t*>(memory));
 }
 
 Workspace::~Workspace() {
@@ -606,17 +594,26 @@ std::string kernel_error_text(int code) {
         case kErrWaitEpilogue: return "a tensor-core kernel's epilogue waited too long for its accumulator";
         case kErrWaitDrain: return "a tensor-core kernel timed out draining its copies";
         case kErrProbeTimeout: return "bounded wait ran out";
+        case kErrWaitHeadLoad: return "the head kernel's copy thread waited too long for a free stage";
+        case kErrWaitHeadData: return "the head kernel waited too long for its trunk rows";
         default: return "kernel error " + std::to_string(code);
     }
 }
 
-void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool probs, ConvTimer* timer) {
+void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool probs, PassTimer* timer) {
     if (B < 1 || B > ws.max_batch()) throw std::invalid_argument("CudaNetwork: batch out of range");
     const NetShape& sh = w.shape();
     const int precision = w.precision();
     const Frame fr(sh.board);
     const DeviceInfo& dev = device_info(w.device());
     check(cudaMemsetAsync(ws.err, 0, sizeof(int), s), "reset error word");
+    const bool timed = timer && timer->enabled;
+    auto mark_begin = [&](int slot) {
+        if (timed) check(cudaEventRecord(timer->begin[size_t(slot)], s), "event");
+    };
+    auto mark_end = [&](int slot) {
+        if (timed) check(cudaEventRecord(timer->end[size_t(slot)], s), "event");
+    };
 
     StemArgs st;
     st.in = ws.stage;
@@ -627,7 +624,9 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
     st.ld = w.kstem();
     st.out = ws.stem_in;
     st.out_lo = ws.stem_in_lo;
-    check(launch_stem_im2col(st, precision, s), "stem operand");
+    mark_begin(kSlotStemPack);
+    check(launch_stem_pack(st, precision, s), "stem operand");
+    mark_end(kSlotStemPack);
 
     ConvArgs a{};
     a.n = sh.board;
@@ -638,32 +637,33 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
     a.halo_rows = fr.halo;
     a.a_bytes = (fr.halo * 128 + 1023) / 1024 * 1024;
     a.err = ws.err;
-    auto conv = [&](int index, const CUtensorMap& in, const CUtensorMap& in_lo, int dst, const void* skip,
-                    const void* skip_lo, int taps, int nchunks, int timer_slot) {
+    auto conv = [&](int index, const CUtensorMap& in, const CUtensorMap& in_lo, int dst, int skip, int taps,
+                    int nchunks, int timer_slot) {
         const Weights::Conv& cv = w.conv(index);
-        ConvMaps m{in, in_lo, cv.map_w, cv.map_w_lo, cv.map_w_pair, cv.map_w_lo_pair};
+        ConvMaps m{in, in_lo, cv.map_w, cv.map_w_lo, cv.map_w_pair, cv.map_w_lo_pair, ws.emap[dst],
+                   ws.emap[skip >= 0 ? skip : dst]};
         a.taps = taps;
         a.nchunks = nchunks;
         a.out = ws.trunk[dst];
         a.out_lo = ws.trunk_lo[dst];
-        a.skip = skip;
-        a.skip_lo = skip_lo;
+        a.skip = skip >= 0 ? ws.trunk[skip] : nullptr;
+        a.skip_lo = skip >= 0 ? ws.trunk_lo[skip] : nullptr;
         a.scale = cv.scale;
         a.shift = cv.shift;
-        if (timer && timer->enabled && timer_slot >= 0) check(cudaEventRecord(timer->begin[size_t(timer_slot)], s), "event");
+        mark_begin(timer_slot);
         check(launch_conv(m, a, w.n_out(), precision, dev.sms, s), "conv");
-        if (timer && timer->enabled && timer_slot >= 0) check(cudaEventRecord(timer->end[size_t(timer_slot)], s), "event");
+        mark_end(timer_slot);
     };
     // The stem: conv -> BN -> ReLU as one tap over the packed operand.
-    conv(0, ws.map_stem, ws.map_stem_lo, 0, nullptr, nullptr, 1, w.kstem() / chunk_channels(precision), -1);
+    conv(0, ws.map_stem, ws.map_stem_lo, 0, -1, 1, w.kstem() / chunk_channels(precision), kSlotStemGemm);
     // The tower: conv -> BN -> ReLU -> conv -> BN -> + skip -> ReLU per block,
     // rotating through three frame buffers.
     const int tower_chunks = w.cpad() / chunk_channels(precision);
     int x = 0;
     for (int i = 0; i < sh.blocks; ++i) {
         const int mid = (x + 1) % 3, out = (x + 2) % 3;
-        conv(1 + 2 * i, ws.map[x], ws.map_lo[x], mid, nullptr, nullptr, 9, tower_chunks, 2 * i);
-        conv(2 + 2 * i, ws.map[mid], ws.map_lo[mid], out, ws.trunk[x], ws.trunk_lo[x], 9, tower_chunks, 2 * i + 1);
+        conv(1 + 2 * i, ws.map[x], ws.map_lo[x], mid, -1, 9, tower_chunks, kSlotTower + 2 * i);
+        conv(2 + 2 * i, ws.map[mid], ws.map_lo[mid], out, x, 9, tower_chunks, kSlotTower + 2 * i + 1);
         x = out;
     }
     HeadArgs h = w.head_args();
@@ -674,7 +674,18 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
     h.values = ws.values;
     h.ownership_out = ws.ownership;
     h.probs = probs ? ws.probs : nullptr;
-    check(launch_heads(h, precision, s), "heads");
+    h.feat = ws.feat;
+    h.hid = ws.hid;
+    h.err = ws.err;
+    mark_begin(kSlotHeadConv);
+    check(launch_head_conv(h, precision, dev.sms, s), "head convolutions");
+    mark_end(kSlotHeadConv);
+    mark_begin(kSlotHeadFc);
+    check(launch_head_fc(h, s), "head FC");
+    mark_end(kSlotHeadFc);
+    mark_begin(kSlotHeadOut);
+    check(launch_head_out(h, s), "head outputs");
+    mark_end(kSlotHeadOut);
 }
 
 // -------------------------------------------------------------- inference
@@ -763,7 +774,7 @@ void Inference::read(int B, float* logits, float* values, float* ownership, floa
     sync();
 }
 
-void Inference::time(int B, int warmup, int steps, bool with_copies, double* ms, double* conv_ms) {
+void Inference::time(int B, int warmup, int steps, bool with_copies, double* ms, double* conv_ms, double* stage_ms) {
     const NetShape& s = w_->shape();
     if (B < 1 || B > ws_->max_batch()) throw std::invalid_argument("CudaInference: batch out of range");
     check(cudaSetDevice(device_), "cudaSetDevice");
@@ -776,7 +787,7 @@ void Inference::time(int B, int warmup, int steps, bool with_copies, double* ms,
                             cudaHostAllocDefault), "cudaHostAlloc");
         check(cudaMemcpy(pin_in_, ws_->stage, in_floats * 4, cudaMemcpyDeviceToHost), "copy staged input");
     }
-    auto pass = [&](ConvTimer* t) {
+    auto pass = [&](PassTimer* t) {
         if (with_copies)
             check(cudaMemcpyAsync(ws_->stage, pin_in_, in_floats * 4, cudaMemcpyHostToDevice, stream_), "input");
         encode_forward(*w_, *ws_, B, stream_, false, t);
@@ -801,31 +812,36 @@ void Inference::time(int B, int warmup, int steps, bool with_copies, double* ms,
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
     sync();
-    if (conv_ms) {
-        ConvTimer t;
+    if (conv_ms || stage_ms) {
+        PassTimer t;
         t.enabled = true;
-        const size_t n = size_t(2 * s.blocks);
+        const size_t n = size_t(kSlotTower + 2 * s.blocks);
         t.begin.resize(n);
         t.end.resize(n);
         for (size_t i = 0; i < n; ++i) {
             check(cudaEventCreate(&t.begin[i]), "cudaEventCreate");
             check(cudaEventCreate(&t.end[i]), "cudaEventCreate");
         }
-        double sum = 0.0;
+        double stages[kTimedStages] = {};
         for (int k = 0; k < steps; ++k) {
             pass(&t);
             check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
             for (size_t i = 0; i < n; ++i) {
                 float d = 0.0f;
                 check(cudaEventElapsedTime(&d, t.begin[i], t.end[i]), "cudaEventElapsedTime");
-                sum += d;
+                const int slot = int(i);
+                const int stage = slot == kSlotStemPack ? 0 : slot == kSlotStemGemm ? 1 : slot == kSlotHeadConv ? 3
+                                : slot == kSlotHeadFc ? 4 : slot == kSlotHeadOut ? 5 : 2;
+                stages[stage] += d;
             }
         }
         for (size_t i = 0; i < n; ++i) {
             cudaEventDestroy(t.begin[i]);
             cudaEventDestroy(t.end[i]);
         }
-        *conv_ms = sum;
+        if (conv_ms) *conv_ms = stages[2];
+        if (stage_ms)
+            for (int i = 0; i < kTimedStages; ++i) stage_ms[i] = stages[i];
         sync();
     }
 }

@@ -126,30 +126,40 @@ public:
     float* values = nullptr;      // [max_batch]
     float* ownership = nullptr;   // [max_batch][area] when the head exists
     float* probs = nullptr;       // [max_batch][actions]
+    float* feat = nullptr;        // [max_batch][3 * area]: the heads' 1x1 conv features
+    float* hid = nullptr;         // [max_batch][value_hidden]: value FC1 output
     int* err = nullptr;           // kernel error word
     CUtensorMap map[3]{}, map_lo[3]{};
+    CUtensorMap emap[3]{};        // bf16: the frames in the conv epilogue's {32, 32} boxes
     CUtensorMap map_stem{}, map_stem_lo{};
 
 private:
+    void place(const Weights& w, uint8_t* base);   // carves the buffers and builds the tensor maps
     int max_batch_;
     size_t bytes_ = 0;
     void* arena_ = nullptr;
 };
 
-// Per-conv-launch timing, for the roofline: events around each tower conv.
-struct ConvTimer {
+// Per-launch timing, for the rooflines: events around each launch of a
+// pass. Slots: the stem operand, the stem GEMM, the three head launches,
+// then the tower convs (kSlotTower + i for conv i of 2 x blocks).
+struct PassTimer {
     std::vector<cudaEvent_t> begin, end;
     bool enabled = false;
 };
+enum TimerSlot : int { kSlotStemPack = 0, kSlotStemGemm, kSlotHeadConv, kSlotHeadFc, kSlotHeadOut, kSlotTower };
+// Stage totals Inference::time reports: these six, in this order.
+constexpr int kTimedStages = 6;   // stem operand, stem GEMM, tower, head conv, head FC, head finish
 
 // Network::forward (src/network.cpp:228-309) on the GPU: stem, the tower's
 // fused convolutions, the fused heads; all on one stream.
-void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool probs, ConvTimer* timer = nullptr);
+void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool probs, PassTimer* timer = nullptr);
 
 // A row-major [rows][inner] tensor read by TMA in boxes of box_inner x
-// box_rows with the 128-byte swizzle; rows outside [0, rows) read as zero.
+// box_rows with the 128-byte (or 64-byte) swizzle; rows outside [0, rows)
+// read as zero and are not written.
 CUtensorMap make_tensor_map(const void* base, int precision, uint64_t inner, uint64_t rows, uint32_t box_inner,
-                            uint32_t box_rows);
+                            uint32_t box_rows, int swizzle_bytes = 128);
 
 // Turns a nonzero kernel error word into the message a pass reports.
 std::string kernel_error_text(int code);
@@ -170,7 +180,10 @@ public:
     const Weights& weights() const { return *w_; }
     int* error_host() const { return err_host_; }   // pinned, one int
     // (total ms of K passes, summed conv-kernel ms)
-    void time(int B, int warmup, int steps, bool with_copies, double* ms, double* conv_ms);
+    // `steps` passes after `warmup`: their total ms; with conv_ms or
+    // stage_ms, `steps` more passes with an event around every launch give
+    // the summed tower-conv ms and the kTimedStages stage totals.
+    void time(int B, int warmup, int steps, bool with_copies, double* ms, double* conv_ms, double* stage_ms = nullptr);
 
 private:
     void check_error_word();

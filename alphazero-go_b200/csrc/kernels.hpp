@@ -25,6 +25,8 @@ enum KernelError : int {
     kErrWaitEpilogue = 3,   // the epilogue waited too long for an accumulator
     kErrWaitDrain = 4,      // draining in-flight copies after an error timed out
     kErrProbeTimeout = 5,   // the bounded-wait probe's wait ran out (expected by its test)
+    kErrWaitHeadLoad = 6,   // the head kernel's copy thread waited too long for a free stage
+    kErrWaitHeadData = 7,   // the head kernel's readers waited too long for a board row
 };
 
 
@@ -71,6 +73,7 @@ struct ConvMaps {
     CUtensorMap a, a_lo;             // input activations: box {chunk, halo_rows}
     CUtensorMap w, w_lo;             // weights [N][9*Cin]: box {chunk, N}
     CUtensorMap w_pair, w_lo_pair;   // the same weights in boxes of {chunk, N/2}: one half per CTA of a pair
+    CUtensorMap out, skip;           // bf16: the output and residual frames in boxes of {32, 32}, 64-byte swizzle
 };
 
 // Shared memory a conv launch needs, and its pipeline depths (pair: the
@@ -92,28 +95,34 @@ struct StemArgs {
     int B, P, n, S, ld;
     void* out; void* out_lo;
 };
-cudaError_t launch_stem_im2col(const StemArgs& a, int precision, cudaStream_t s);
+cudaError_t launch_stem_pack(const StemArgs& a, int precision, cudaStream_t s);
 
-// The fused heads: policy 1x1 conv + BN + ReLU + FC, value 1x1 conv + BN +
-// ReLU + FC + ReLU + FC + tanh, ownership 1x1 conv + BN + tanh, and the
-// softmax over the A+1 moves.
+// The heads: policy 1x1 conv + BN + ReLU + FC, value 1x1 conv + BN + ReLU +
+// FC + ReLU + FC + tanh, ownership 1x1 conv + BN + tanh, and the softmax
+// over the A+1 moves, in three launches (trunk stream, FC tiles, per-board
+// finish) through the small feat/hid scratch buffers.
 struct HeadArgs {
     const void* trunk; const void* trunk_lo;
     int ld, n, S, A, F, V, B, ownership;
     const float* pol_w;     // [2][F]
     const float* pol_scale; const float* pol_shift;   // [2]
-    const float* fc_wt; const float* fc_b;            // input-major [2A][A+1], [A+1]
+    const float* fc_w; const float* fc_b;             // [A+1][2A rounded up to 4], [A+1]
     const float* val_w;     // [F]
     const float* val_scale; const float* val_shift;   // [1]
-    const float* v1_wt; const float* v1_b;            // input-major [A][V], [V]
+    const float* v1_w; const float* v1_b;             // [V][A rounded up to 4], [V]
     const float* v2_w; const float* v2_b;             // [V], [1]
     const float* own_w; const float* own_scale; const float* own_shift;
     float* logits;      // [B][A+1]
     float* values;      // [B]
     float* ownership_out;   // [B][A] or null
     float* probs;       // [B][A+1] or null
+    float* feat;        // scratch [B][3A]: policy features (c*A + p), then value features
+    float* hid;         // scratch [B][V]: value FC1 after ReLU
+    int* err;           // kernel error word (a bounded wait that ran out)
 };
-cudaError_t launch_heads(const HeadArgs& a, int precision, cudaStream_t s);
+cudaError_t launch_head_conv(const HeadArgs& a, int precision, int sms, cudaStream_t s);   // 1x1 convs -> feat
+cudaError_t launch_head_fc(const HeadArgs& a, cudaStream_t s);                            // feat -> logits, hid
+cudaError_t launch_head_out(const HeadArgs& a, cudaStream_t s);                           // hid -> value; softmax
 
 // Test hooks and context checks.
 cudaError_t launch_fill(float* data, size_t n, float value, cudaStream_t s);

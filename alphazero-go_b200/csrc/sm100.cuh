@@ -32,6 +32,19 @@ __device__ __forceinline__ uint64_t global_timer() {
 
 // ------------------------------------------------------------------ mbarrier
 
+// A position in a ring of pipeline stages: the stage and the parity of
+// its current phase, advanced by a compare instead of a division.
+struct Ring {
+    uint32_t idx = 0, phase = 0;
+    __device__ __forceinline__ void next(uint32_t stages) {
+        if (++idx == stages) {
+            idx = 0;
+            phase ^= 1u;
+        }
+    }
+};
+
+
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
@@ -94,6 +107,40 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, void* dst, u
         ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
         : "memory");
 }
+
+// `bytes` (a multiple of 16) from global memory at `src` into shared memory
+// at `dst` (both 16-byte aligned) as one bulk copy, completing on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// A 2D tile from shared memory at `src` to `map` at element coordinates
+// (x, y) >= 0, in this thread's current bulk group; rows or columns outside
+// the tensor are not written.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+
+// Closes this thread's current bulk group.
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Waits until at most kPending of this thread's bulk groups still read
+// shared memory (their sources may then be overwritten).
+template <int kPending>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kPending) : "memory");
+}
+
+// Waits until every bulk group of this thread has completed its writes.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Orders this thread's earlier shared-memory writes before later async-proxy
+// (TMA, tensor core) accesses of them.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // ------------------------------------------------------------------ tcgen05
 

@@ -1,6 +1,7 @@
 // The stem convolution, the fused heads, and the small kernels the runner's
 // checks and test hooks use.
 #include <algorithm>
+#include <atomic>
 
 #include "kernels.hpp"
 #include "sm100.cuh"
@@ -23,40 +24,75 @@ unsigned blocks_for(size_t count, int threads) {
 // 0 off the board), in the point's frame row. The stem then runs on the
 // tensor cores as a one-tap GEMM with K = 9*P (rounded up to whole 128-byte
 // chunks), instead of a 3x3 convolution over P channels padded to a chunk.
-// Frame padding rows and the columns past 9*P are never written (zero since
-// the buffer was allocated).
+// One CTA per board (grid-stride): the board's P planes are staged in shared
+// memory, then consecutive threads write consecutive 16-byte pieces of the
+// frame rows (whole rows, the zero columns past 9*P included), so the stores
+// are coalesced. Frame padding rows are never written (zero since the
+// buffer was allocated).
 template <int kMode>
-__global__ void __launch_bounds__(256) stem_im2col_kernel(const StemArgs a) {
-    const int A = a.n * a.n, K = 9 * a.P;
-    const size_t total = size_t(a.B) * A * K;
-    for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
-        const size_t pix = i / K;
-        const int k = static_cast<int>(i % K);
-        const int b = static_cast<int>(pix / A), pt = static_cast<int>(pix % A);
-        const int t = k / a.P, pl = k % a.P;
-        const int y = pt / a.n + t / 3 - 1, x = pt % a.n + t % 3 - 1;
-        const float v = (y < 0 || y >= a.n || x < 0 || x >= a.n)
-                            ? 0.0f
-                            : __ldg(a.in + (size_t(b) * a.P + pl) * A + y * a.n + x);
-        const size_t row = size_t(b) * a.S + size_t(pt / a.n + 1) * (a.n + 1) + pt % a.n;
-        const size_t off = row * a.ld + k;
-        if (kMode == kBF16) {
-            static_cast<__nv_bfloat16*>(a.out)[off] = __float2bfloat16_rn(v);
-        } else if (kMode == kTF32x3) {
-            const float h = to_tf32(v);
-            static_cast<float*>(a.out)[off] = h;
-            static_cast<float*>(a.out_lo)[off] = __fsub_rn(v, h);
-        } else {
-            static_cast<float*>(a.out)[off] = v;
+__global__ void __launch_bounds__(256) stem_pack_kernel(const StemArgs a) {
+    extern __shared__ float planes[];   // [P][A]
+    constexpr int W = kMode == kBF16 ? 8 : 4;   // values per 16-byte piece
+    const int A = a.n * a.n, K = 9 * a.P, pieces = a.ld / W;
+    for (int b = blockIdx.x; b < a.B; b += gridDim.x) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < a.P * A; i += blockDim.x) planes[i] = __ldg(a.in + size_t(b) * a.P * A + i);
+        __syncthreads();
+        for (int item = threadIdx.x; item < A * pieces; item += blockDim.x) {
+            const int pt = item / pieces, j = item % pieces;
+            const int py = pt / a.n, px = pt % a.n;
+            float v[W];
+#pragma unroll
+            for (int e = 0; e < W; ++e) {
+                const int k = j * W + e;
+                v[e] = 0.0f;
+                if (k < K) {
+                    const int t = k / a.P, pl = k % a.P;
+                    const int y = py + t / 3 - 1, x = px + t % 3 - 1;
+                    if (y >= 0 && y < a.n && x >= 0 && x < a.n) v[e] = planes[pl * A + y * a.n + x];
+                }
+            }
+            const size_t off = (size_t(b) * a.S + size_t(py + 1) * (a.n + 1) + px) * a.ld + size_t(j) * W;
+            if (kMode == kBF16) {
+                uint4 w4;
+                __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&w4);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) h2[e] = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+                *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + off) = w4;
+            } else if (kMode == kTF32x3) {
+                float4 h, l;
+                h.x = to_tf32(v[0]); l.x = __fsub_rn(v[0], h.x);
+                h.y = to_tf32(v[1]); l.y = __fsub_rn(v[1], h.y);
+                h.z = to_tf32(v[2]); l.z = __fsub_rn(v[2], h.z);
+                h.w = to_tf32(v[3]); l.w = __fsub_rn(v[3], h.w);
+                *reinterpret_cast<float4*>(static_cast<float*>(a.out) + off) = h;
+                *reinterpret_cast<float4*>(static_cast<float*>(a.out_lo) + off) = l;
+            } else {
+                *reinterpret_cast<float4*>(static_cast<float*>(a.out) + off) = make_float4(v[0], v[1], v[2], v[3]);
+            }
         }
     }
 }
 
 // --------------------------------------------------------------- the heads
+//
+// Three launches, each at its own roofline:
+//  1. head_conv_kernel streams the trunk once through shared memory
+//     (bulk copies; HBM-bound): the policy (2),
+//     value (1) and ownership (1) 1x1 convolutions of every board point,
+//     their batch norms and ReLU (ownership: tanh, straight to its output);
+//     features land in a small [B][3A] buffer, the policy part in the
+//     reference's flatten order c*A + p (src/network.cpp:278-285).
+//  2. head_fc_kernel: the policy FC (2A -> A+1, + bias) and value FC1
+//     (A -> V, + bias, ReLU) for tiles of 16 boards x 32 outputs, each FC
+//     weight read once per tile, the tile's inputs in shared memory.
+//  3. head_out_kernel: one warp per board, the value FC2 and tanh, and the
+//     softmax over the A+1 logits.
+// Every output is a fixed-order sum over its own board's data: the results
+// do not depend on the batch or on where a board sits in it.
 
-constexpr int kHeadSamples = 8;    // samples per CTA: each FC weight is read once per group
-constexpr int kHeadThreads = 512;
-constexpr int kHeadWarps = kHeadThreads / 32;
+constexpr int kHeadThreads = 256;
+constexpr int kFcBoards = 16;    // boards per FC tile: each weight is read once per 16 boards
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -70,14 +106,15 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
-// 8 (bf16) or 4 (fp32) channels of a trunk row as floats; split mode sums hi + lo.
+// One 16-byte piece of a trunk row (and, split mode, of its low plane) as
+// floats: 8 bf16 or 4 fp32 channels; split mode adds hi + lo (one rounding).
 template <int kMode>
-struct TrunkVec {
+struct TrunkPiece {
     static constexpr int kWidth = kMode == kBF16 ? 8 : 4;
-    __device__ static void load(const HeadArgs& a, size_t off, float* f) {
+    uint4 hi, lo;
+    __device__ __forceinline__ void values(float* f) const {
         if (kMode == kBF16) {
-            const uint4 w4 = __ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.trunk) + off));
-            const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&w4);
+            const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&hi);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const float2 t = __bfloat1622float2(h2[e]);
@@ -85,18 +122,10 @@ struct TrunkVec {
                 f[2 * e + 1] = t.y;
             }
         } else {
-            float4 v = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(a.trunk) + off));
-            if (kMode == kTF32x3) {
-                const float4 l = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(a.trunk_lo) + off));
-                v.x = __fadd_rn(v.x, l.x);
-                v.y = __fadd_rn(v.y, l.y);
-                v.z = __fadd_rn(v.z, l.z);
-                v.w = __fadd_rn(v.w, l.w);
-            }
-            f[0] = v.x;
-            f[1] = v.y;
-            f[2] = v.z;
-            f[3] = v.w;
+            const float* h = reinterpret_cast<const float*>(&hi);
+            const float* l = reinterpret_cast<const float*>(&lo);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) f[e] = kMode == kTF32x3 ? __fadd_rn(h[e], l[e]) : h[e];
         }
     }
 };
@@ -106,123 +135,283 @@ __device__ __forceinline__ float bn_relu(float z, float scale, float shift) {
     return y > 0.0f ? y : 0.0f;
 }
 
-size_t head_smem_bytes(int F, int A, int V) {
-    return (size_t(4) * F + size_t(kHeadSamples) * (2 * A + A + V + A + 1)) * sizeof(float);
+// The trunk streamed once through shared memory. A copy thread (warp 8)
+// stages `kbr` board rows at a time into a ring of `stages` buffers: the n
+// real points of a board row are n consecutive frame rows, one bulk copy
+// each, so padding rows are never read. 8 reader warps take the staged rows
+// four "slots" at a time: kLpr lanes share one row (kLpr x kNch 16-byte
+// pieces, lane l reading pieces l, l + kLpr, ...: consecutive lanes,
+// consecutive pieces), each lane summing its channels into 4 slots x 4
+// heads = 16 partial sums with the 1x1 weights of its channels held in
+// registers. A reduce-scatter over the kLpr lanes (at the step over lane
+// bit b a lane keeps the half of its sums that bit selects and adds its
+// partner's copy; once one sum is left, a butterfly) leaves each lane its
+// finished sums, which it applies the batch norm to and stores. Every sum is the same tree of
+// additions whatever its slot: outputs do not depend on the batch.
+// Persistent CTAs, one per SM; every wait is bounded.
+constexpr int kHcReaders = 8;
+constexpr int kHcThreads = 32 * (kHcReaders + 1);
+
+// v / n for v >= 0 and n <= 19: below 2^20 with a float reciprocal ((v +
+// 0.5)/n stays at least 0.5/n away from the integers, above the float
+// error there), else by integer division.
+__device__ __forceinline__ int div_small(int v, int n, float inv_n) {
+    return v < (1 << 20) ? int((float(v) + 0.5f) * inv_n) : v / n;
+}
+constexpr int kHcSlots = 4;
+
+template <int kMode, int kLpr, int kNch>
+__global__ void __launch_bounds__(kHcThreads, 1)
+    head_conv_kernel(const HeadArgs a, int stages, int kbr, uint32_t row_bytes) {
+    extern __shared__ uint8_t hc_raw[];
+    constexpr int W = TrunkPiece<kMode>::kWidth, kC = kNch * W;
+    constexpr int kGroups = 32 / kLpr;                  // rows a warp holds per slot
+    constexpr int kStepRows = kHcSlots * kGroups;       // rows per warp step
+    constexpr int kLog = kLpr == 32 ? 5 : kLpr == 16 ? 4 : 3;
+    constexpr int kScatter = kLog < 4 ? kLog : 4;       // steps that halve the 16 sums
+    constexpr int kBfly = kLog - kScatter;              // butterfly steps after them
+    constexpr int kOwn = (kHcSlots * 4) >> kScatter;    // finished sums per lane
+    constexpr uint32_t kPlanes = kMode == kTF32x3 ? 2u : 1u;
+    const int n = a.n, A = a.A, board_rows = a.B * n;
+    const int nblk = (board_rows + kbr - 1) / kbr;
+    const uint32_t br_bytes = uint32_t(n) * row_bytes;              // one board row, one plane
+    const uint32_t plane_bytes = uint32_t(kbr) * br_bytes;          // one stage, one plane
+    uint8_t* buf = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(hc_raw) + 127) & ~uintptr_t(127));
+    uint64_t* full = reinterpret_cast<uint64_t*>(buf + size_t(stages) * kPlanes * plane_bytes);
+    uint64_t* empty = full + stages;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < stages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kHcReaders);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (warp == kHcReaders) {
+        // ------------------------------------------------------- copy thread
+        if (lane == 0) {
+            Ring r;
+            uint32_t issued = 0;
+            const uint8_t* hi = static_cast<const uint8_t*>(a.trunk);
+            const uint8_t* lo = static_cast<const uint8_t*>(a.trunk_lo);
+            for (int blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+                if (!mbar_wait(&empty[r.idx], r.phase ^ 1u, a.err, kErrWaitHeadLoad)) break;
+                const int first = blk * kbr, cnt = min(kbr, board_rows - first);
+                mbar_arrive_expect_tx(&full[r.idx], kPlanes * uint32_t(cnt) * br_bytes);
+                uint8_t* dst = buf + size_t(r.idx) * kPlanes * plane_bytes;
+                for (int i = 0; i < cnt; ++i) {
+                    const int b = (first + i) / n, y = (first + i) % n;
+                    const size_t row0 = size_t(b) * a.S + size_t(y + 1) * (n + 1);
+                    bulk_load(dst + i * br_bytes, hi + row0 * row_bytes, br_bytes, &full[r.idx]);
+                    if (kMode == kTF32x3)
+                        bulk_load(dst + plane_bytes + i * br_bytes, lo + row0 * row_bytes, br_bytes, &full[r.idx]);
+                }
+                r.next(uint32_t(stages));
+                ++issued;
+            }
+            // Every copy has landed before the CTA may exit.
+            for (uint32_t st = 0; st < uint32_t(stages) && st < issued; ++st) {
+                const uint32_t uses = (issued - st + stages - 1) / stages;
+                mbar_wait(&full[st], (uses - 1) & 1, a.err, kErrWaitDrain);
+            }
+        }
+        return;
+    }
+
+    // ----------------------------------------------------------- readers
+    const int l = lane % kLpr, grp = lane / kLpr;
+    float w[4][kC];
+#pragma unroll
+    for (int j = 0; j < kNch; ++j)
+#pragma unroll
+        for (int e = 0; e < W; ++e) {
+            const int ch = (l + j * kLpr) * W + e, i = j * W + e;
+            const bool real = ch < a.F;
+            w[0][i] = real ? __ldg(a.pol_w + ch) : 0.0f;
+            w[1][i] = real ? __ldg(a.pol_w + a.F + ch) : 0.0f;
+            w[2][i] = real ? __ldg(a.val_w + ch) : 0.0f;
+            w[3][i] = real && a.ownership ? __ldg(a.own_w + ch) : 0.0f;
+        }
+    // The batch norm of the sums this lane finishes (head k % 4 of its sums
+    // k = (l >> kBfly) * kOwn + j), the same for every step.
+    float bn_scale[kOwn], bn_shift[kOwn];
+#pragma unroll
+    for (int j = 0; j < kOwn; ++j) {
+        const int h = (((l >> kBfly) * kOwn) + j) % 4;
+        bn_scale[j] = h == 0 ? __ldg(a.pol_scale) : h == 1 ? __ldg(a.pol_scale + 1) : h == 2 ? __ldg(a.val_scale)
+                                                                                   : (a.ownership ? __ldg(a.own_scale) : 0.0f);
+        bn_shift[j] = h == 0 ? __ldg(a.pol_shift) : h == 1 ? __ldg(a.pol_shift + 1) : h == 2 ? __ldg(a.val_shift)
+                                                                                   : (a.ownership ? __ldg(a.own_shift) : 0.0f);
+    }
+    const bool writer = (l & ((1 << kBfly) - 1)) == 0;
+    const float inv_n = 1.0f / float(n);
+    Ring r;
+    for (int blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+        if (!mbar_wait(&full[r.idx], r.phase, a.err, kErrWaitHeadData)) break;
+        const uint8_t* stage = buf + size_t(r.idx) * kPlanes * plane_bytes;
+        const int first = blk * kbr, rows = min(kbr, board_rows - first) * n;
+        for (int base = warp * kStepRows; base < rows; base += kHcReaders * kStepRows) {
+            float acc[kHcSlots * 4];
+#pragma unroll
+            for (int s = 0; s < kHcSlots; ++s) {
+                const int row = base + s * kGroups + grp;
+                float z[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                if (row < rows) {
+#pragma unroll
+                    for (int j = 0; j < kNch; ++j) {
+                        const uint32_t off = uint32_t(row) * row_bytes + uint32_t(l + j * kLpr) * 16u;
+                        TrunkPiece<kMode> piece;
+                        piece.hi = *reinterpret_cast<const uint4*>(stage + off);
+                        if (kMode == kTF32x3) piece.lo = *reinterpret_cast<const uint4*>(stage + plane_bytes + off);
+                        float f[W];
+                        piece.values(f);
+#pragma unroll
+                        for (int e = 0; e < W; ++e)
+#pragma unroll
+                            for (int h = 0; h < 4; ++h) z[h] = fmaf(w[h][j * W + e], f[e], z[h]);
+                    }
+                }
+#pragma unroll
+                for (int h = 0; h < 4; ++h) acc[s * 4 + h] = z[h];
+            }
+            // Reduce-scatter over the high lane bits of the group while there
+            // is more than one sum to split, then a butterfly over the rest.
+#pragma unroll
+            for (int t = 0; t < kLog; ++t) {
+                const int off = kLpr >> (t + 1);
+                if (t < kScatter) {
+                    const int half = (kHcSlots * 2) >> t;
+                    const bool upper = (lane & off) != 0;
+#pragma unroll
+                    for (int k = 0; k < half; ++k) {
+                        const float send = upper ? acc[k] : acc[k + half];
+                        const float keep = upper ? acc[k + half] : acc[k];
+                        acc[k] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+                    }
+                } else {
+                    acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], off);
+                }
+            }
+            if (writer) {
+#pragma unroll
+                for (int j = 0; j < kOwn; ++j) {
+                    const int k = (l >> kBfly) * kOwn + j, s = k / 4, h = k % 4;
+                    const int row = base + s * kGroups + grp;
+                    if (row >= rows) continue;
+                    const int rq = div_small(row, n, inv_n), br = first + rq, x = row - rq * n;
+                    const int b = div_small(br, n, inv_n), p = (br - b * n) * n + x;
+                    const float y = __fadd_rn(__fmul_rn(bn_scale[j], acc[j]), bn_shift[j]);
+                    if (h < 3) {
+                        a.feat[size_t(b) * 3 * A + size_t(h) * A + p] = y > 0.0f ? y : 0.0f;
+                    } else if (a.ownership && a.ownership_out) {
+                        a.ownership_out[size_t(b) * A + p] = tanhf(y);
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[r.idx]);
+        r.next(uint32_t(stages));
+    }
 }
 
-// One CTA: kHeadSamples samples.
-//  1. Each thread takes whole board points: it reads the point's F trunk
-//     channels with 16-byte loads (independent, so many are in flight) and
-//     sums the policy, value and ownership 1x1 convolutions in channel
-//     order, then applies their batch norms: the policy features land in the
-//     reference's flatten order c*A + p (src/network.cpp:278-285).
-//  2. Each thread owns one FC output (a policy logit or a value hidden unit)
-//     for all the group's samples, summing over the inputs in order; the FC
-//     weights are stored input-major, so a warp's loads of one input's
-//     weights are one coalesced line.
-//  3. One warp per sample: the value FC2 and tanh, and the softmax over
-//     the A+1 logits.
-// Every output is one thread's fixed-order sum over its own sample's data:
-// the results do not depend on the batch or on where a sample sits in it.
-template <int kMode>
-__global__ void __launch_bounds__(kHeadThreads) heads_kernel(const HeadArgs a) {
-    extern __shared__ float hs[];
-    const int A = a.A, V = a.V, L = A + 1, F = a.F;
-    float* wpol0 = hs;
-    float* wpol1 = wpol0 + F;
-    float* wval = wpol1 + F;
-    float* wown = wval + F;
-    float* pol = wown + F;                         // [G][2A]
-    float* val = pol + kHeadSamples * 2 * A;       // [G][A]
-    float* hid = val + kHeadSamples * A;           // [G][V]
-    float* lg = hid + kHeadSamples * V;            // [G][A+1]
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int b0 = blockIdx.x * kHeadSamples;
-    const int G = min(kHeadSamples, a.B - b0);
-    constexpr int W = TrunkVec<kMode>::kWidth;
-
-    for (int i = threadIdx.x; i < F; i += kHeadThreads) {
-        wpol0[i] = a.pol_w[i];
-        wpol1[i] = a.pol_w[F + i];
-        wval[i] = a.val_w[i];
-        wown[i] = a.ownership ? a.own_w[i] : 0.0f;
+// A tile of kFcBoards (16) boards x 32 outputs of the policy FC (tiles
+// 0 .. ceil((A+1)/32) - 1 of gridDim.y) or of the value FC1 (the rest); the
+// tile's inputs, [16][n rounded up to 4], sit in shared memory. Each warp
+// takes kFcOuts (4) outputs for the 16 boards: lane l sums inputs
+// 4l .. 4l+3, 4l+128 .. in order (16-byte loads of the padded weight rows
+// and of the inputs, the inputs reused across the 4 outputs in registers),
+// then a reduce-scatter over the lanes (62 shuffles for 64 sums) leaves lane
+// l the totals k = 2l, 2l+1 (k = output*16 + board). Every total is the same
+// tree of additions over the same lanes, whatever its k: a board's outputs
+// do not depend on its slot in the tile.
+constexpr int kFcOuts = 4;
+__global__ void __launch_bounds__(kHeadThreads) head_fc_kernel(const HeadArgs a) {
+    extern __shared__ float4 xs[];
+    const int A = a.A, L = A + 1, V = a.V;
+    const int outs_per_cta = (kHeadThreads / 32) * kFcOuts;
+    const int pol_tiles = (L + outs_per_cta - 1) / outs_per_cta;
+    const bool policy = int(blockIdx.y) < pol_tiles;
+    const int n_in = policy ? 2 * A : A, n4 = (n_in + 3) / 4, ncols = policy ? L : V;
+    const int foff = policy ? 0 : 2 * A;
+    const int b0 = blockIdx.x * kFcBoards, G = min(kFcBoards, a.B - b0);
+    float* xf = reinterpret_cast<float*>(xs);
+    for (int idx = threadIdx.x; idx < kFcBoards * n4 * 4; idx += kHeadThreads) {
+        const int g = idx / (n4 * 4), i = idx % (n4 * 4);
+        xf[idx] = g < G && i < n_in ? a.feat[size_t(b0 + g) * 3 * A + foff + i] : 0.0f;
     }
     __syncthreads();
-    const float ps0 = a.pol_scale[0], ps1 = a.pol_scale[1], ph0 = a.pol_shift[0], ph1 = a.pol_shift[1];
-    const float vs = a.val_scale[0], vh = a.val_shift[0];
-    const float os = a.ownership ? a.own_scale[0] : 0.0f, oh = a.ownership ? a.own_shift[0] : 0.0f;
-
-    for (int item = threadIdx.x; item < G * A; item += kHeadThreads) {
-        const int g = item / A, p = item % A;
-        const size_t row = size_t(b0 + g) * a.S + size_t(p / a.n + 1) * (a.n + 1) + p % a.n;
-        float z0 = 0.0f, z1 = 0.0f, zv = 0.0f, zo = 0.0f;
-#pragma unroll 4
-        for (int c = 0; c < F; c += W) {
-            float f[W];
-            TrunkVec<kMode>::load(a, row * a.ld + c, f);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int o0 = (policy ? int(blockIdx.y) : int(blockIdx.y) - pol_tiles) * outs_per_cta + warp * kFcOuts;
+    if (o0 >= ncols) return;
+    const float4* W = reinterpret_cast<const float4*>(policy ? a.fc_w : a.v1_w);
+    float acc[kFcOuts * kFcBoards];
 #pragma unroll
-            for (int e = 0; e < W; ++e) {
-                z0 = fmaf(wpol0[c + e], f[e], z0);
-                z1 = fmaf(wpol1[c + e], f[e], z1);
-                zv = fmaf(wval[c + e], f[e], zv);
-                zo = fmaf(wown[c + e], f[e], zo);
-            }
-        }
-        pol[g * 2 * A + p] = bn_relu(z0, ps0, ph0);
-        pol[g * 2 * A + A + p] = bn_relu(z1, ps1, ph1);
-        val[g * A + p] = bn_relu(zv, vs, vh);
-        if (a.ownership && a.ownership_out)
-            a.ownership_out[size_t(b0 + g) * A + p] = tanhf(__fadd_rn(__fmul_rn(os, zo), oh));
-    }
-    __syncthreads();
-
-    for (int o = threadIdx.x; o < L + V; o += kHeadThreads) {
-        float acc[kHeadSamples];
+    for (int k = 0; k < kFcOuts * kFcBoards; ++k) acc[k] = 0.0f;
+    for (int j = lane; j < n4; j += 32) {
+        float4 w[kFcOuts];
 #pragma unroll
-        for (int g = 0; g < kHeadSamples; ++g) acc[g] = 0.0f;
-        const bool policy = o < L;
-        const int n_in = policy ? 2 * A : A, out = policy ? o : o - L, stride = policy ? L : V;
-        const float* wt = policy ? a.fc_wt : a.v1_wt;      // [n_in][stride]
-        const float* x = policy ? pol : val;
-        const int ld = policy ? 2 * A : A;
-#pragma unroll 4
-        for (int i = 0; i < n_in; ++i) {
-            const float wv = __ldg(wt + size_t(i) * stride + out);
+        for (int o = 0; o < kFcOuts; ++o)
+            w[o] = o0 + o < ncols ? __ldg(W + size_t(o0 + o) * n4 + j) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
-            for (int g = 0; g < kHeadSamples; ++g) acc[g] = fmaf(wv, x[g * ld + i], acc[g]);
-        }
-        if (policy) {
-            const float bias = __ldg(a.fc_b + out);
-            for (int g = 0; g < G; ++g) {
-                const float l = __fadd_rn(acc[g], bias);
-                lg[g * L + out] = l;
-                a.logits[size_t(b0 + g) * L + out] = l;
-            }
-        } else {
-            const float bias = __ldg(a.v1_b + out);
-            for (int g = 0; g < G; ++g) {
-                const float h = __fadd_rn(acc[g], bias);
-                hid[g * V + out] = h > 0.0f ? h : 0.0f;
+        for (int g = 0; g < kFcBoards; ++g) {
+            const float4 x = xs[g * n4 + j];
+#pragma unroll
+            for (int o = 0; o < kFcOuts; ++o) {
+                float& c = acc[o * kFcBoards + g];
+                c = fmaf(w[o].x, x.x, c);
+                c = fmaf(w[o].y, x.y, c);
+                c = fmaf(w[o].z, x.z, c);
+                c = fmaf(w[o].w, x.w, c);
             }
         }
     }
-    __syncthreads();
-
-    for (int g = warp; g < G; g += kHeadWarps) {
-        float acc = 0.0f;
-        for (int i = lane; i < V; i += 32) acc = fmaf(__ldg(a.v2_w + i), hid[g * V + i], acc);
-        acc = warp_sum(acc);
-        if (lane == 0) a.values[b0 + g] = tanhf(__fadd_rn(acc, __ldg(a.v2_b)));
-        if (a.probs) {
-            float m = -INFINITY;
-            for (int o = lane; o < L; o += 32) m = fmaxf(m, lg[g * L + o]);
-            m = warp_max(m);
-            float s = 0.0f;
-            for (int o = lane; o < L; o += 32) s += expf(lg[g * L + o] - m);
-            s = warp_sum(s);
-            const float inv = 1.0f / s;
-            for (int o = lane; o < L; o += 32) a.probs[size_t(b0 + g) * L + o] = expf(lg[g * L + o] - m) * inv;
+    // Reduce-scatter: at the step over lane bit b (offset 2^b), a lane keeps
+    // the half of its sums that bit selects and adds its partner's copy.
+#pragma unroll
+    for (int half = kFcOuts * kFcBoards / 2, off = 16; off >= 1; half >>= 1, off >>= 1) {
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int k = 0; k < half; ++k) {
+            const float send = upper ? acc[k] : acc[k + half];
+            const float keep = upper ? acc[k + half] : acc[k];
+            acc[k] = keep + __shfl_xor_sync(0xffffffffu, send, off);
         }
+    }
+    const float* bias = policy ? a.fc_b : a.v1_b;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const int k = 2 * lane + j, o = o0 + k / kFcBoards, g = k % kFcBoards;
+        if (o >= ncols || g >= G) continue;
+        const float y = __fadd_rn(acc[j], __ldg(bias + o));
+        if (policy) a.logits[size_t(b0 + g) * L + o] = y;
+        else a.hid[size_t(b0 + g) * V + o] = y > 0.0f ? y : 0.0f;
+    }
+}
+
+// One warp per board: value = tanh(v2 . hid + b2), and the softmax over the
+// A+1 logits when asked for.
+__global__ void __launch_bounds__(kHeadThreads) head_out_kernel(const HeadArgs a) {
+    const int lane = threadIdx.x & 31, L = a.A + 1, V = a.V;
+    const int b = blockIdx.x * (kHeadThreads / 32) + (threadIdx.x >> 5);
+    if (b >= a.B) return;
+    const float* hid = a.hid + size_t(b) * V;
+    float acc = 0.0f;
+    for (int i = lane; i < V; i += 32) acc = fmaf(__ldg(a.v2_w + i), hid[i], acc);
+    acc = warp_sum(acc);
+    if (lane == 0) a.values[b] = tanhf(__fadd_rn(acc, __ldg(a.v2_b)));
+    if (a.probs) {
+        const float* lg = a.logits + size_t(b) * L;
+        float m = -INFINITY;
+        for (int o = lane; o < L; o += 32) m = fmaxf(m, lg[o]);
+        m = warp_max(m);
+        float s = 0.0f;
+        for (int o = lane; o < L; o += 32) s += expf(lg[o] - m);
+        s = warp_sum(s);
+        const float inv = 1.0f / s;
+        for (int o = lane; o < L; o += 32) a.probs[size_t(b) * L + o] = expf(lg[o] - m) * inv;
     }
 }
 
@@ -258,42 +447,92 @@ __global__ void bounded_wait_probe(int* err, unsigned long long limit_ns) {
 
 } // namespace
 
-cudaError_t launch_stem_im2col(const StemArgs& a, int precision, cudaStream_t s) {
-    const size_t total = size_t(a.B) * a.n * a.n * 9 * a.P;
-    if (total == 0) return cudaSuccess;
-    const unsigned grid = blocks_for(total, 256);
+cudaError_t launch_stem_pack(const StemArgs& a, int precision, cudaStream_t s) {
+    if (a.B <= 0) return cudaSuccess;
+    const int W = precision == kBF16 ? 8 : 4;
+    if (a.ld % W != 0) return cudaErrorInvalidValue;
+    const size_t smem = size_t(a.P) * a.n * a.n * sizeof(float);
+    const unsigned grid = static_cast<unsigned>(std::min(a.B, 148 * 8));
     switch (precision) {
-        case kTF32: stem_im2col_kernel<kTF32><<<grid, 256, 0, s>>>(a); break;
-        case kTF32x3: stem_im2col_kernel<kTF32x3><<<grid, 256, 0, s>>>(a); break;
-        case kBF16: stem_im2col_kernel<kBF16><<<grid, 256, 0, s>>>(a); break;
+        case kTF32: stem_pack_kernel<kTF32><<<grid, 256, smem, s>>>(a); break;
+        case kTF32x3: stem_pack_kernel<kTF32x3><<<grid, 256, smem, s>>>(a); break;
+        case kBF16: stem_pack_kernel<kBF16><<<grid, 256, smem, s>>>(a); break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
 }
 
-cudaError_t launch_heads(const HeadArgs& a, int precision, cudaStream_t s) {
-    if (a.B <= 0) return cudaSuccess;
-    const int W = precision == kBF16 ? 8 : 4;
-    if (a.F % W != 0) return cudaErrorInvalidValue;
-    const size_t smem = head_smem_bytes(a.F, a.A, a.V);
-    const unsigned grid = static_cast<unsigned>((a.B + kHeadSamples - 1) / kHeadSamples);
-    cudaError_t e = cudaSuccess;
-    switch (precision) {
-        case kTF32:
-            e = cudaFuncSetAttribute(heads_kernel<kTF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-            if (e == cudaSuccess) heads_kernel<kTF32><<<grid, kHeadThreads, smem, s>>>(a);
-            break;
-        case kTF32x3:
-            e = cudaFuncSetAttribute(heads_kernel<kTF32x3>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-            if (e == cudaSuccess) heads_kernel<kTF32x3><<<grid, kHeadThreads, smem, s>>>(a);
-            break;
-        case kBF16:
-            e = cudaFuncSetAttribute(heads_kernel<kBF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-            if (e == cudaSuccess) heads_kernel<kBF16><<<grid, kHeadThreads, smem, s>>>(a);
-            break;
+namespace {
+
+// One persistent CTA per SM (fewer for small batches). A stage holds as
+// many board rows as about three reader steps cover (8 warps x 4 slots x
+// rows per slot each), capped so that at least two stages fit in 200 KB;
+// as many stages as fit, at most 8 (C4 bf16: 4 stages of 5 board rows).
+template <int kMode, int kLpr, int kNch>
+cudaError_t launch_head_conv_as(const HeadArgs& a, int sms, cudaStream_t s) {
+    const uint32_t row_bytes = uint32_t(a.ld) * (kMode == kBF16 ? 2u : 4u);
+    const size_t planes = kMode == kTF32x3 ? 2 : 1, br_bytes = size_t(a.n) * row_bytes * planes;
+    constexpr size_t kBudget = 200u << 10;
+    const int step_rows = kHcReaders * kHcSlots * (32 / kLpr);
+    int kbr = std::max(1, (step_rows * 3) / a.n);   // about three reader steps per stage
+    kbr = int(std::max<size_t>(1, std::min<size_t>(size_t(kbr), kBudget / 2 / br_bytes)));
+    kbr = std::min(kbr, a.B * a.n);
+    const size_t stage = size_t(kbr) * br_bytes;
+    const int stages = int(std::max<size_t>(2, std::min<size_t>(8, kBudget / stage)));
+    const size_t smem = 128 + size_t(stages) * stage + size_t(stages) * 16;
+    static std::atomic<size_t> opened{0};
+    if (smem > opened.load()) {
+        const cudaError_t e = cudaFuncSetAttribute(head_conv_kernel<kMode, kLpr, kNch>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return e;
+        opened = smem;
+    }
+    const int nblk = (a.B * a.n + kbr - 1) / kbr;
+    const unsigned grid = static_cast<unsigned>(std::max(1, std::min(nblk, sms)));
+    head_conv_kernel<kMode, kLpr, kNch><<<grid, kHcThreads, smem, s>>>(a, stages, kbr, row_bytes);
+    return cudaGetLastError();
+}
+
+template <int kMode>
+cudaError_t launch_head_conv_mode(const HeadArgs& a, int sms, cudaStream_t s) {
+    switch (a.ld / TrunkPiece<kMode>::kWidth) {   // 16-byte pieces per trunk row
+        case 8: return launch_head_conv_as<kMode, 8, 1>(a, sms, s);
+        case 16: return launch_head_conv_as<kMode, 16, 1>(a, sms, s);
+        case 32: return launch_head_conv_as<kMode, 32, 1>(a, sms, s);
+        case 64: return launch_head_conv_as<kMode, 32, 2>(a, sms, s);
         default: return cudaErrorInvalidValue;
     }
-    if (e != cudaSuccess) return e;
+}
+
+} // namespace
+
+cudaError_t launch_head_conv(const HeadArgs& a, int precision, int sms, cudaStream_t s) {
+    if (a.B <= 0) return cudaSuccess;
+    if ((a.ld * (precision == kBF16 ? 2 : 4)) % 16 != 0) return cudaErrorInvalidValue;
+    switch (precision) {
+        case kTF32: return launch_head_conv_mode<kTF32>(a, sms, s);
+        case kTF32x3: return launch_head_conv_mode<kTF32x3>(a, sms, s);
+        case kBF16: return launch_head_conv_mode<kBF16>(a, sms, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_head_fc(const HeadArgs& a, cudaStream_t s) {
+    if (a.B <= 0) return cudaSuccess;
+    const int L = a.A + 1, outs = (kHeadThreads / 32) * kFcOuts;
+    const dim3 grid((a.B + kFcBoards - 1) / kFcBoards, (L + outs - 1) / outs + (a.V + outs - 1) / outs);
+    const size_t smem = size_t((2 * a.A + 3) / 4) * 4 * kFcBoards * sizeof(float);
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(head_fc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return e;
+    }
+    head_fc_kernel<<<grid, kHeadThreads, smem, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_head_out(const HeadArgs& a, cudaStream_t s) {
+    if (a.B <= 0) return cudaSuccess;
+    head_out_kernel<<<(a.B + kHeadThreads / 32 - 1) / (kHeadThreads / 32), kHeadThreads, 0, s>>>(a);
     return cudaGetLastError();
 }
 

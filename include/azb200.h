@@ -132,6 +132,11 @@ void* azb_infer_stream(azb_infer* h);
  * when not null. */
 int azb_infer_time(azb_infer* h, int B, int warmup, int steps, int with_copies, double* ms, double* conv_ms,
                    char* err, size_t err_cap);
+/* Per-stage device time of `steps` passes (CUDA events around every launch,
+ * summed over the passes): stage_ms[0..5] = stem operand, stem GEMM, tower
+ * convs, head 1x1 convs, head FCs, head finish (value tanh, softmax).
+ * Measurement only; no reference counterpart. */
+int azb_infer_time_stages(azb_infer* h, int B, int steps, double* stage_ms, char* err, size_t err_cap);
 /* Read back the device outputs of the last enqueued pass. */
 int azb_infer_read(azb_infer* h, int B, float* logits, float* values, float* ownership, float* probs, char* err,
                    size_t err_cap);
