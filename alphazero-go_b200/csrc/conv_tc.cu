@@ -52,12 +52,14 @@ struct ConvCfg {
 
 constexpr int kThreads = 192;
 constexpr int kMaxStages = 8;
+constexpr uint32_t kBnBytes = 2 * 256 * 4;   // scale and shift of up to 256 channels
 
 // Shared memory: [halo buffers][weight buffers][barriers][tmem slot].
 struct Smem {
     uint8_t* a;
     uint8_t* b;
     uint8_t* epi;   // bf16 epilogue boxes (4 warps x 8 KB), or nothing
+    float* bn;      // the folded batch norm: scale[0..N), shift[N..2N)
     uint64_t *a_full, *a_empty, *b_full, *b_empty, *acc_full, *acc_empty, *done;
     uint64_t* skip_full;   // 4 warps x 2 residual boxes
     uint32_t* tmem_slot;
@@ -70,7 +72,8 @@ __device__ __forceinline__ Smem carve(uint8_t* raw, int sa, int sb, int ops, int
     s.a = base;
     s.b = base + size_t(sa) * ops * a_bytes;
     s.epi = s.b + size_t(sb) * ops * b_bytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(s.epi + epi_bytes);
+    s.bn = reinterpret_cast<float*>(s.epi + epi_bytes);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(s.epi + epi_bytes + kBnBytes);
     s.a_full = bars;
     s.a_empty = s.a_full + sa;
     s.b_full = s.a_empty + sa;
@@ -85,7 +88,8 @@ __device__ __forceinline__ Smem carve(uint8_t* raw, int sa, int sb, int ops, int
 
 __host__ __device__ constexpr size_t smem_total(int sa, int sb, int ops, int a_bytes, uint32_t b_bytes,
                                                 uint32_t epi_bytes) {
-    return 1024 + size_t(sa) * ops * a_bytes + size_t(sb) * ops * b_bytes + epi_bytes + (2 * sa + 2 * sb + 13) * 8 + 16;
+    return 1024 + size_t(sa) * ops * a_bytes + size_t(sb) * ops * b_bytes + epi_bytes + kBnBytes +
+           (2 * sa + 2 * sb + 13) * 8 + 16;
 }
 
 // The nine tap views' start rows inside a halo tile, as descriptor
@@ -204,8 +208,9 @@ struct EpiWarp {
 };
 
 template <int N>
-__device__ __forceinline__ void store_epilogue_tma(const ConvArgs& p, const CUtensorMap* omap, const CUtensorMap* smap,
-                                                   uint32_t taddr, int row0, bool valid, EpiWarp& ew, int lane) {
+__device__ __forceinline__ void store_epilogue_tma(const ConvArgs& p, const float* bn, const CUtensorMap* omap,
+                                                   const CUtensorMap* smap, uint32_t taddr, int row0, bool valid,
+                                                   EpiWarp& ew, int lane) {
     constexpr int kChunks = N / 32;
     constexpr uint32_t kBox = 2048;
     if (row0 >= p.rows) return;   // all 32 rows past the frame: nothing to store
@@ -228,7 +233,7 @@ __device__ __forceinline__ void store_epilogue_tma(const ConvArgs& p, const CUte
         float y[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-            y[i] = __fadd_rn(__fmul_rn(__ldg(p.scale + c * 32 + i), __uint_as_float(v[i])), __ldg(p.shift + c * 32 + i));
+            y[i] = __fadd_rn(__fmul_rn(bn[c * 32 + i], __uint_as_float(v[i])), bn[N + c * 32 + i]);
         if (skip) {
             mbar_wait(&ew.sbar[cb], (ew.sphase >> cb) & 1u, p.err, kErrWaitEpilogue);
             ew.sphase ^= 1u << cb;
@@ -310,6 +315,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
     if (warp == 1) tmem_alloc(sm.tmem_slot, C::kTmemCols);
+    for (int i = threadIdx.x; i < N; i += kThreads) {
+        sm.bn[i] = p.scale[i];
+        sm.bn[N + i] = p.shift[i];
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -428,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 valid = r >= n1 && (r % n1) != p.n;
             }
             const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + acc * N;
-            if constexpr (C::kEpiTma) store_epilogue_tma<N>(p, &mOut, &mSkip, taddr, tile * 128 + quarter * 32, valid, ew, lane);
+            if constexpr (C::kEpiTma) store_epilogue_tma<N>(p, sm.bn, &mOut, &mSkip, taddr, tile * 128 + quarter * 32, valid, ew, lane);
             else store_epilogue<N, kBf16, kSplit>(p, taddr, q, valid);
             tc_fence_before();
             mbar_arrive(&sm.acc_empty[acc]);
@@ -509,6 +518,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
     }
     if (warp == 1) tmem_alloc_pair(sm.tmem_slot, C::kTmemCols);
+    for (int i = threadIdx.x; i < N; i += kThreads) {
+        sm.bn[i] = p.scale[i];
+        sm.bn[N + i] = p.shift[i];
+    }
     tc_fence_before();
     __syncthreads();
     cluster_sync();   // both CTAs' barriers exist before either addresses the other's
@@ -640,7 +653,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + acc * N;
             if constexpr (C::kEpiTma)
-                store_epilogue_tma<N>(p, &mOut, &mSkip, taddr, (2 * pr + int(rank)) * 128 + quarter * 32, valid, ew, lane);
+                store_epilogue_tma<N>(p, sm.bn, &mOut, &mSkip, taddr, (2 * pr + int(rank)) * 128 + quarter * 32, valid, ew, lane);
             else
                 store_epilogue<N, kBf16, kSplit>(p, taddr, q, valid);
             tc_fence_before();

@@ -130,11 +130,6 @@ struct TrunkPiece {
     }
 };
 
-__device__ __forceinline__ float bn_relu(float z, float scale, float shift) {
-    const float y = __fadd_rn(__fmul_rn(scale, z), shift);
-    return y > 0.0f ? y : 0.0f;
-}
-
 // The trunk streamed once through shared memory. A copy thread (warp 8)
 // stages `kbr` board rows at a time into a ring of `stages` buffers: the n
 // real points of a board row are n consecutive frame rows, one bulk copy
