@@ -1,0 +1,65 @@
+"""Self-play with the reference's own search on a chosen engine.
+
+ctypes over host/_ref/libazselfplay.so (host/Makefile): the reference's
+playSelfPlayGame (src/selfplay.cpp:50) and WorkerEvaluators/InferenceHub
+(src/inference_hub.cpp), compiled from its sources with this package's
+drop-in bridge as its "cuda" engine. A slice of games is played the way the
+reference's playSelfPlayQueue plays one (src/selfplay_slice.cpp:93-149); the
+statistics are SliceStats', and playouts/s = positions x simulations /
+seconds, as the reference reports it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "host", "_ref", "libazselfplay.so")
+
+_libs: dict[str, C.CDLL] = {}
+
+
+def _lib(path: str) -> C.CDLL:
+    if path not in _libs:
+        if not os.path.exists(path):
+            raise RuntimeError(f"{path} is not built: make -C {os.path.join(HERE, 'host')} (needs the reference tree)")
+        L = C.CDLL(path)
+        F = C.POINTER(C.c_float)
+        L.azsp_play.argtypes = ([C.c_int] * 5 + [F, C.c_size_t, F, C.c_size_t, C.c_char_p] + [C.c_int] * 6 +
+                                [C.c_float, C.c_int, C.c_float, C.c_int, C.c_uint64, C.c_int, C.c_int, C.c_int,
+                                 C.POINTER(C.c_double), C.POINTER(C.c_longlong), C.POINTER(C.c_longlong),
+                                 C.POINTER(C.c_uint64), C.c_char_p, C.c_size_t])
+        L.azsp_play.restype = C.c_int
+        _libs[path] = L
+    return _libs[path]
+
+
+def play(desc, params: np.ndarray, buffers: np.ndarray, *, backend: str = "cuda", workers: int = 512,
+         inference_batch: int = 256, device: int = 0, precision: int = 2, simulations: int = 200,
+         mcts_batch: int = 8, c_puct: float = 1.5, temperature_moves: int = 7, komi: float = 7.5,
+         max_moves: int = 0, seed: int = 1, generation: int = 0, first: int = 0, count: int = 512,
+         lib_path: str | None = None) -> dict:
+    """Plays games [first, first + count) and returns the slice's statistics.
+
+    desc: an object with board, history, blocks, filters, value_hidden (the
+    network's shape); params/buffers: its two ParamLayout arenas (float32).
+    """
+    L = _lib(lib_path or LIB_PATH)
+    p = np.ascontiguousarray(params, np.float32)
+    b = np.ascontiguousarray(buffers, np.float32)
+    F = C.POINTER(C.c_float)
+    secs, pos, evals, h = C.c_double(), C.c_longlong(), C.c_longlong(), C.c_uint64()
+    err = C.create_string_buffer(1024)
+    rc = L.azsp_play(desc.board, desc.history, desc.blocks, desc.filters, desc.value_hidden,
+                     p.ctypes.data_as(F), p.size, b.ctypes.data_as(F), b.size, backend.encode(), workers,
+                     inference_batch, device, precision, simulations, mcts_batch, c_puct, temperature_moves, komi,
+                     max_moves, seed, generation, first, count, C.byref(secs), C.byref(pos), C.byref(evals),
+                     C.byref(h), err, 1024)
+    if rc != 0:
+        raise RuntimeError(err.value.decode())
+    s = secs.value
+    return {"seconds": s, "positions": pos.value, "evaluations": evals.value, "record_hash": h.value,
+            "playouts_per_s": pos.value * simulations / s if s > 0 else 0.0,
+            "evaluations_per_s": evals.value / s if s > 0 else 0.0}

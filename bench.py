@@ -23,7 +23,11 @@ Printed (rank 0, one JSON line):
   roofline   the tower convolution kernel: algorithmic FLOPs per launch over
              its average CUDA-event duration, against the measured bf16 peak;
   cpu_baseline  the reference's own CPU engine (blas, one worker per core at
-             batch 8) on a bounded sample, rank 0 at N = 1 only.
+             batch 8) on a bounded sample, rank 0 at N = 1 only;
+  selfplay   C5: playouts/s and positions
+             evaluated/s of the reference's own self-play (MCTS, rules,
+             InferenceHub) on this engine, 512 games per GPU, with the
+             reference's CPU self-play (blas) beside it at N = 1.
 `--impl reference` times the reference's CPU implementation (oracle/_ref,
 OpenBLAS, all host cores) on the same config and metric instead.
 """
@@ -49,6 +53,17 @@ BOARD, BLOCKS, FILTERS, VALUE_HIDDEN, HISTORY = 19, 20, 256, 256, 1
 BATCH = 1024
 SEED = 1
 WORKLOAD = "C4: 19x19 board, 20 residual blocks x 256 filters, value_hidden 256, 4 input planes, batch 1024 per GPU"
+
+# Self-play ("C5"): the 9x9 6x64 network of C2
+# (history 1, value_hidden 128, seeded as the benchmark's), PUCT MCTS with
+# 200 playouts per move and c_puct 1.5, 512 concurrent games per GPU, leaves
+# batched by the reference's InferenceHub into passes of up to 256, mcts
+# batch 8, and the rest of configs/9x9.cfg (komi 7.5, 7 sampled opening
+# moves, move cap 2n^2) with resignation off.
+SP_BOARD, SP_BLOCKS, SP_FILTERS, SP_VH = 9, 6, 64, 128
+SP_GAMES, SP_SIMS, SP_MCTS_BATCH, SP_CPUCT, SP_BATCH, SP_TEMP, SP_KOMI = 512, 200, 8, 1.5, 256, 7, 7.5
+SP_WORKLOAD = ("C5: self-play 9x9, 6x64 network (C2), 200 playouts/move, c_puct 1.5, 512 games per GPU, "
+               "inference batch 256, mcts batch 8, komi 7.5, 7 opening moves sampled, resignation off")
 
 
 def conv_flops_per_position() -> float:
@@ -86,7 +101,7 @@ def profiled_traffic() -> float | None:
 
 
 class ClockSampler:
-    """nvidia-smi sampled every 200 ms; started before the warm-up (the tool
+    """nvidia-smi sampled every 50 ms; started before the warm-up (the tool
     takes a moment to begin), kept to the samples taken inside the timed
     region [mark_start, mark_stop] (the nearest one if none falls inside)."""
 
@@ -105,7 +120,7 @@ class ClockSampler:
         try:
             self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=self.out, stderr=subprocess.DEVNULL)
+                                          "-lms", "50"], stdout=self.out, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
             return self
@@ -208,6 +223,13 @@ class Dist:
         self.torch.distributed.all_reduce(t, op=self.torch.distributed.ReduceOp.MAX)
         return float(t.item())
 
+    def sum(self, v: float) -> float:
+        if not self.torch:
+            return v
+        t = self.torch.tensor([v], dtype=self.torch.float64, device=self.device)
+        self.torch.distributed.all_reduce(t, op=self.torch.distributed.ReduceOp.SUM)
+        return float(t.item())
+
     def broadcast(self, arr):
         """Rank 0's numpy array to every rank (once, at start: the weight replicas)."""
         if not self.torch:
@@ -264,6 +286,27 @@ def cpu_reference_sample(steps: int, warmup: int, per_step_calls: int = 1, secon
     return total_pos / total_t, workers, sample
 
 
+def selfplay_cpu_sample(plies: int = 6):
+    """The reference's self-play on its own CPU engine (blas, one worker per
+    core; oracle/_ref/libazselfplay_ref.so): one game per worker, each cut at
+    `plies` plies (move cap), so the sample ends in seconds."""
+    sys.path.insert(0, os.path.join(ROOT, "alphazero-go_b200"))
+    import azb200 as E
+    import selfplay as SP
+
+    sp_desc = E.NetDesc(SP_BOARD, 1, SP_BLOCKS, SP_FILTERS, SP_VH, 0)
+    p, b = E.synth_network(sp_desc, SEED, 0)
+    workers = len(os.sched_getaffinity(0))
+    lib = os.path.join(ROOT, "oracle", "_ref", "libazselfplay_ref.so")
+    r = SP.play(sp_desc, p, b, backend="blas", workers=workers, simulations=SP_SIMS, mcts_batch=SP_MCTS_BATCH,
+                c_puct=SP_CPUCT, temperature_moves=SP_TEMP, komi=SP_KOMI, max_moves=plies, seed=SEED, count=workers,
+                lib_path=lib)
+    return {"playouts_per_s": r["playouts_per_s"], "positions_evaluated_per_s": r["evaluations_per_s"],
+            "cores": workers, "kind": "reference",
+            "sample": f"{workers} games x {plies} plies on {workers} workers (blas), {r['positions']} positions in "
+                      f"{r['seconds']:.1f} s"}
+
+
 def run_reference(args):
     n_gpus = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     try:
@@ -281,10 +324,41 @@ def run_reference(args):
         "cpu_baseline": {"value": rate, "unit": UNIT, "cores": workers, "kind": "reference", "sample": sample},
         "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_selfplay:
+        try:
+            line["selfplay"] = {"workload": SP_WORKLOAD, **selfplay_cpu_sample()}
+        except Exception as e:
+            line["selfplay"] = {"workload": SP_WORKLOAD, "unavailable": f"reference self-play failed: {e}"}
     print(json.dumps(line))
 
 
 # -------------------------------------------------------------- engine
+
+
+def run_selfplay(d: "Dist", dev: int) -> dict | None:
+    import azb200 as E
+    import selfplay as SP
+
+    sp_desc = E.NetDesc(SP_BOARD, 1, SP_BLOCKS, SP_FILTERS, SP_VH, 0)
+    p, b = E.synth_network(sp_desc, SEED, 0)
+    try:
+        r = SP.play(sp_desc, p, b, backend="cuda", workers=SP_GAMES, inference_batch=SP_BATCH, device=dev,
+                    precision=E.TF32X3, simulations=SP_SIMS, mcts_batch=SP_MCTS_BATCH, c_puct=SP_CPUCT,
+                    temperature_moves=SP_TEMP, komi=SP_KOMI, max_moves=0, seed=SEED, generation=0,
+                    first=d.rank * SP_GAMES, count=SP_GAMES)
+        ok = 1.0
+    except Exception as e:   # not built here, or failed: every rank still takes the same collectives
+        r, ok = {"seconds": 0.0, "positions": 0, "evaluations": 0}, 0.0
+        err = str(e)
+    secs = d.max(r["seconds"])
+    pos, evals, oks = d.sum(float(r["positions"])), d.sum(float(r["evaluations"])), d.sum(ok)
+    if oks < d.world:
+        return {"workload": SP_WORKLOAD, "unavailable": err if ok == 0.0 else "self-play failed on another rank"}
+    return {"workload": SP_WORKLOAD, "playouts_per_s": pos * SP_SIMS / secs, "positions_evaluated_per_s": evals / secs,
+            "games": SP_GAMES * d.world, "positions": int(pos), "evaluations": int(evals), "seconds": secs,
+            "precision": "tf32x3 (the mode that meets the parity gate on this network)",
+            "how": "the reference's playSelfPlayGame and InferenceHub over this engine's bridge "
+                   "(alphazero-go_b200/host), one slice of 512 games per GPU, host wall clock, max over ranks"}
 
 
 def run_engine(args, d: Dist):
@@ -390,6 +464,18 @@ def run_engine(args, d: Dist):
         except Exception as e:
             cpu = {"value": None, "unit": UNIT, "cores": 0, "kind": "reference", "sample": f"unavailable: {e}"}
 
+    # --- self-play (C5): the reference's search and hub on this engine, one
+    # slice of 512 games per rank (games [rank*512, (rank+1)*512)), host
+    # wall clock of the slice; playouts/s = positions x 200 / seconds
+    selfplay = None
+    if not args.no_selfplay:
+        selfplay = run_selfplay(d, dev)
+        if selfplay and d.world == 1 and not args.no_cpu_baseline:
+            try:
+                selfplay["cpu_baseline"] = selfplay_cpu_sample()
+            except Exception as e:
+                selfplay["cpu_baseline"] = {"unavailable": f"reference self-play failed: {e}"}
+
     if d.rank == 0:
         peaks = measured_peaks()
         peak = peaks.get("bf16_tflops_sustained")
@@ -413,10 +499,12 @@ def run_engine(args, d: Dist):
                          "kernel": "conv3x3_tc_pair<256,bf16>", "flop_per_launch": conv_flops_per_position() * BATCH,
                          "avg_launch_ms": conv_avg_ms},
             "tensor_tflops_whole_pass": flops_per_position() * BATCH * d.world * args.steps / (ms / 1e3) / 1e12,
-            "gpu_launches": args.steps * (2 * BLOCKS + 2),
+            "gpu_launches": args.steps * (2 * BLOCKS + 5),   # stem operand + stem GEMM + tower + 3 head launches
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
+        if selfplay is not None:
+            line["selfplay"] = selfplay
         print(json.dumps(line))
     d.close()
 
@@ -424,11 +512,12 @@ def run_engine(args, d: Dist):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("engine", "reference"), default="engine")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-selfplay", action="store_true", help="skip the C5 self-play figures")
     ap.add_argument("--only-device", action="store_true", help="device-resident passes only (for profilers)")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -1,0 +1,47 @@
+"""Self-play on the engine through the reference's own search and hub.
+
+Mirrors the reference's tests/test_cuda.cpp:1270-1295 (the determinism
+contract of a cuda engine's slice): the same games, byte for byte, for 1, 3
+and 8 workers, batches capped at 8 or 256, and the hub's chaos mode on or
+off. Records are compared through the driver's FNV-1a hash of every game in
+index order.
+"""
+import os
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG_LIB = os.path.join(ROOT, "alphazero-go_b200", "host", "_ref", "libazselfplay.so")
+
+
+@pytest.fixture(scope="module")
+def sp(engine):
+    if not os.path.exists(PKG_LIB):
+        pytest.skip("alphazero-go_b200/host/_ref/libazselfplay.so is not built (needs the reference tree)")
+    import selfplay
+
+    return selfplay
+
+
+@pytest.mark.parametrize("shape", [(5, 1, 8, 16), (9, 2, 16, 32)])
+@pytest.mark.parametrize("precision", ["tf32x3", "bf16"])
+def test_slice_independent_of_workers_and_batching(engine, sp, shape, precision):
+    d = engine.NetDesc(shape[0], 1, shape[1], shape[2], shape[3], 0)
+    p, b = engine.synth_network(d, 801, 1)
+    reference = None
+    for workers in (1, 3, 8):
+        for batch in (8, 256):
+            for chaos in (0, 21):
+                engine.cuda_probe.set_hub_chaos_seed(chaos)
+                try:
+                    r = sp.play(d, p, b, backend="cuda", workers=workers, inference_batch=batch,
+                                precision=engine.PRECISIONS[precision], simulations=32, mcts_batch=8,
+                                temperature_moves=6, seed=802, generation=3, first=10, count=6)
+                finally:
+                    engine.cuda_probe.set_hub_chaos_seed(0)
+                assert r["evaluations"] > 0
+                if reference is None:
+                    reference = r["record_hash"]
+                assert r["record_hash"] == reference, (workers, batch, chaos)

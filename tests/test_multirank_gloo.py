@@ -1,7 +1,9 @@
 """The multi-GPU host logic on CPU ranks (gloo, world size 2): the weight
 replicas broadcast once from rank 0 arrive bit-identical, each rank's
 positions are its own slice of one seeded sequence (weak scaling by batch),
-and the timing reduction takes the maximum over ranks. The GPU path of the
+the timing reduction takes the maximum over ranks, and self-play split by
+game slice across ranks plays the same games as one process playing them
+all. The GPU path of the
 same code runs each rank on its own device over NCCL with no per-step
 collective."""
 import os
@@ -38,8 +40,31 @@ def _rank_main(rank, world, port, out_dir):
     x = E.synth_positions(desc, 11, 4, first=d.rank * 4)
     d.barrier()
     worst = d.max(float(rank + 1) * 1.5)
-    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), params=params, buffers=buffers, x=x, worst=worst)
+    total = d.sum(float(rank + 1))
+    # Self-play by game slice: rank r plays games [3r, 3r + 3) of one
+    # generation (the reference's naive engine here; the bench runs the
+    # engine's "cuda" backend the same way, one slice per GPU).
+    sp_positions = -1.0
+    lib = _selfplay_lib()
+    if lib:
+        import selfplay as SP
+
+        sd = E.NetDesc(5, 1, 1, 8, 16, 0)
+        sp_p, sp_b = E.synth_network(sd, 801, 1)
+        r = SP.play(sd, sp_p, sp_b, backend="naive", workers=2, simulations=16, temperature_moves=6, seed=802,
+                    generation=3, first=3 * rank, count=3, lib_path=lib)
+        sp_positions = d.sum(float(r["positions"]))
+    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), params=params, buffers=buffers, x=x, worst=worst,
+             total=total, sp_positions=sp_positions)
     d.close()
+
+
+def _selfplay_lib():
+    for p in (os.path.join(ROOT, "oracle", "_ref", "libazselfplay_ref.so"),
+              os.path.join(ROOT, "alphazero-go_b200", "host", "_ref", "libazselfplay.so")):
+        if os.path.exists(p):
+            return p
+    return None
 
 
 def test_two_ranks_gloo(tmp_path):
@@ -61,5 +86,16 @@ def test_two_ranks_gloo(tmp_path):
     for r in (r0, r1):
         assert np.array_equal(r["params"], p) and np.array_equal(r["buffers"], b)
         assert float(r["worst"]) == 3.0
+        assert float(r["total"]) == 3.0
+    lib = _selfplay_lib()
+    if lib:
+        sys.path.insert(0, os.path.join(ROOT, "alphazero-go_b200"))
+        import selfplay as SP
+
+        sd = E.NetDesc(5, 1, 1, 8, 16, 0)
+        sp_p, sp_b = E.synth_network(sd, 801, 1)
+        whole_sp = SP.play(sd, sp_p, sp_b, backend="naive", workers=2, simulations=16, temperature_moves=6,
+                           seed=802, generation=3, first=0, count=6, lib_path=lib)
+        assert float(r0["sp_positions"]) == float(whole_sp["positions"]) == float(r1["sp_positions"])
     whole = E.synth_positions(desc, 11, 8)
     assert np.array_equal(r0["x"], whole[:4]) and np.array_equal(r1["x"], whole[4:])
