@@ -29,7 +29,9 @@ Printed (rank 0, one JSON line):
              InferenceHub) on this engine, 512 games per GPU, with the
              reference's CPU self-play (blas) beside it at N = 1.
 `--impl reference` times the reference's CPU implementation (oracle/_ref,
-OpenBLAS, all host cores) on the same config and metric instead.
+OpenBLAS, all host cores) on the same config and metric instead, and adds
+`ref_cuda`: the reference's own CUDA engine rebuilt for sm_100 on the same
+workload, and the reference's CPU self-play.
 """
 from __future__ import annotations
 
@@ -307,6 +309,29 @@ def selfplay_cpu_sample(plies: int = 6):
                       f"{r['seconds']:.1f} s"}
 
 
+def refcuda_sample(steps: int = 2):
+    """The reference's own CUDA engine (src/cuda, compiled unmodified for
+    sm_100 by `make -C oracle refcuda`) on the same C4 workload: fp32, batch
+    1024, wall clock of synchronous CudaInference::infer calls (host copies
+    included, as that engine always does them), after one untimed call."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    if not O.refcuda_built():
+        return {"unavailable": "oracle/_ref/libazrefcuda.so is not built (needs the reference tree)"}
+    ok, why = O.refcuda_available()
+    if not ok:
+        return {"unavailable": why}
+    cfg = O.NetConfig(BOARD, HISTORY, BLOCKS, FILTERS, VALUE_HIDDEN, False)
+    p, b = O.make_network(cfg, SEED, O.KIND_BENCH)
+    x = O.positions(cfg, SEED, BATCH)
+    with O.RefCudaInference(cfg, p, b, BATCH) as net:
+        secs = net.time(x, 1, steps)
+    return {"value": BATCH * steps / secs, "unit": UNIT, "dtype": "f32", "batch": BATCH, "steps": steps,
+            "engine": O.refcuda_description(),
+            "how": "the reference's src/cuda engine (SIMT fp32) built for sm_100, CudaInference::infer, wall clock"}
+
+
 def run_reference(args):
     n_gpus = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     try:
@@ -324,6 +349,10 @@ def run_reference(args):
         "cpu_baseline": {"value": rate, "unit": UNIT, "cores": workers, "kind": "reference", "sample": sample},
         "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    try:
+        line["ref_cuda"] = refcuda_sample()
+    except Exception as e:
+        line["ref_cuda"] = {"unavailable": f"the reference's CUDA engine (oracle/_ref/libazrefcuda.so) failed: {e}"}
     if not args.no_selfplay:
         try:
             line["selfplay"] = {"workload": SP_WORKLOAD, **selfplay_cpu_sample()}

@@ -313,3 +313,87 @@ def softmax(logits: np.ndarray) -> np.ndarray:
     z = z - z.max(axis=-1, keepdims=True)
     e = np.exp(z)
     return e / e.sum(axis=-1, keepdims=True)
+
+
+# ------------------------------------------------ the reference's CUDA engine
+
+REFCUDA_PATH = os.path.join(HERE, "_ref", "libazrefcuda.so")
+_refcuda = None
+
+
+def refcuda_built() -> bool:
+    return os.path.exists(REFCUDA_PATH)
+
+
+def refcuda() -> C.CDLL:
+    """oracle/_ref/libazrefcuda.so: the reference's src/cuda engine built for sm_100 (`make -C oracle refcuda`)."""
+    global _refcuda
+    if _refcuda is None:
+        L = C.CDLL(REFCUDA_PATH)
+        F = C.POINTER(C.c_float)
+        L.azrefcuda_available.argtypes = [C.c_char_p, C.c_size_t]
+        L.azrefcuda_description.argtypes = [C.c_char_p, C.c_size_t]
+        L.azrefcuda_create.argtypes = [C.c_int] * 5 + [F, C.c_size_t, F, C.c_size_t, C.c_int, C.c_char_p, C.c_size_t]
+        L.azrefcuda_create.restype = C.c_void_p
+        L.azrefcuda_destroy.argtypes = [C.c_void_p]
+        L.azrefcuda_infer.argtypes = [C.c_void_p, F, C.c_int, F, F, C.c_char_p, C.c_size_t]
+        L.azrefcuda_time.argtypes = [C.c_void_p, F, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double), C.c_char_p,
+                                     C.c_size_t]
+        _refcuda = L
+    return _refcuda
+
+
+def refcuda_available() -> tuple[bool, str]:
+    why = C.create_string_buffer(512)
+    ok = refcuda().azrefcuda_available(why, 512) == 1
+    return ok, why.value.decode()
+
+
+def refcuda_description() -> str:
+    out = C.create_string_buffer(512)
+    refcuda().azrefcuda_description(out, 512)
+    return out.value.decode()
+
+
+class RefCudaInference:
+    """The reference's CudaInference (include/azgo/cuda.hpp:72-84) on the given arenas."""
+
+    def __init__(self, cfg: NetConfig, params: np.ndarray, buffers: np.ndarray, max_batch: int):
+        self.cfg = cfg
+        p = np.ascontiguousarray(params, np.float32)
+        b = np.ascontiguousarray(buffers, np.float32)
+        err = C.create_string_buffer(1024)
+        self.h = refcuda().azrefcuda_create(cfg.board, cfg.history, cfg.blocks, cfg.filters, cfg.value_hidden,
+                                            _fp(p), p.size, _fp(b), b.size, max_batch, err, 1024)
+        if not self.h:
+            raise RuntimeError(err.value.decode())
+
+    def infer(self, x: np.ndarray):
+        x = np.ascontiguousarray(x, np.float32)
+        B = x.shape[0]
+        logits = np.empty((B, self.cfg.area + 1), np.float32)
+        values = np.empty(B, np.float32)
+        err = C.create_string_buffer(1024)
+        if refcuda().azrefcuda_infer(self.h, _fp(x), B, _fp(logits), _fp(values), err, 1024) != 0:
+            raise RuntimeError(err.value.decode())
+        return logits, values
+
+    def time(self, x: np.ndarray, warmup: int, steps: int) -> float:
+        """Wall seconds of `steps` synchronous infer calls on x (copies included)."""
+        x = np.ascontiguousarray(x, np.float32)
+        secs = C.c_double()
+        err = C.create_string_buffer(1024)
+        if refcuda().azrefcuda_time(self.h, _fp(x), x.shape[0], warmup, steps, C.byref(secs), err, 1024) != 0:
+            raise RuntimeError(err.value.decode())
+        return secs.value
+
+    def close(self):
+        if self.h:
+            refcuda().azrefcuda_destroy(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
