@@ -42,11 +42,12 @@ struct ConvCfg {
     static constexpr uint32_t kBBytes = uint32_t(N) * 128u;
     static constexpr uint32_t kTmemCols = 2 * N <= 64 ? 64 : (2 * N <= 128 ? 128 : (2 * N <= 256 ? 256 : 512));
     static constexpr uint32_t kIdesc = umma_idesc(N, kBf16);
-    // bf16 stores its output (and reads its residual input) through shared
-    // memory with TMA: per epilogue warp two 2 KB output boxes and two 2 KB
-    // residual boxes ({32 channels, 32 rows}, 64-byte swizzle).
-    static constexpr bool kEpiTma = kBf16 && !kSplit;
-    static constexpr uint32_t kEpiBytes = kEpiTma ? 4u * 4u * 2048u : 0u;
+    // bf16 and plain tf32 store their output (and read their residual input)
+    // through shared memory with TMA: per epilogue warp two output boxes and
+    // two residual boxes of {32 channels, 32 rows} (2 KB bf16, 4 KB fp32);
+    // the split mode's two planes keep direct stores.
+    static constexpr bool kEpiTma = !kSplit;
+    static constexpr uint32_t kEpiBytes = kEpiTma ? 4u * 4u * (kBf16 ? 2048u : 4096u) : 0u;
     static_assert(N % 32 == 0 && N >= 32 && N <= 256, "N is a multiple of 32 in [32, 256]");
 };
 
@@ -191,14 +192,15 @@ __device__ __forceinline__ void store_epilogue(const ConvArgs& p, uint32_t taddr
     }
 }
 
-// One epilogue warp's share of a tile in bf16 (32 rows from row0, all N
-// channels), through shared memory: per 32-channel chunk the warp's lanes
-// (one row each) write ReLU(scale * acc + shift (+ skip)) as bf16 into a
-// 2 KB box, swizzled as TMA's 64-byte swizzle lays it out (16-byte piece u
-// of row r at piece u ^ ((r >> 1) & 3): conflict-free), and one lane stores
-// the box with TMA. Padding rows are stored as zeros (they must stay zero),
-// rows past the frame are clipped by TMA. The residual input arrives the
-// same way, one chunk ahead, in two 2 KB boxes. Same arithmetic as
+// One epilogue warp's share of a tile (32 rows from row0, all N channels),
+// through shared memory: per 32-channel chunk the warp's lanes (one row
+// each) write ReLU(scale * acc + shift (+ skip)) into a box of 32 rows x 32
+// channels (bf16: 64-byte rows, 2 KB; fp32: 128-byte rows, 4 KB), swizzled
+// as TMA's 64-byte / 128-byte swizzle lays it out (16-byte piece u of row r
+// at piece u ^ ((r >> 1) & 3), resp. u ^ (r & 7): conflict-free), and one
+// lane stores the box with TMA. Padding rows are stored as zeros (they must
+// stay zero), rows past the frame are clipped by TMA. The residual input
+// arrives the same way, one chunk ahead, in two boxes. Same arithmetic as
 // store_epilogue.
 struct EpiWarp {
     uint8_t* obuf;        // 2 output boxes
@@ -207,15 +209,26 @@ struct EpiWarp {
     uint32_t sphase = 0;  // bit i: parity of sbar[i]'s next phase
 };
 
-template <int N>
+template <bool kBf16>
+struct EpiBox {
+    static constexpr uint32_t kRowBytes = kBf16 ? 64u : 128u;
+    static constexpr uint32_t kBytes = 32u * kRowBytes;
+    static constexpr int kPieces = int(kRowBytes / 16);   // 16-byte pieces per row
+    __device__ static uint32_t piece(int row, int u) {     // byte offset of piece u of `row`
+        const uint32_t sw = kBf16 ? uint32_t((row >> 1) & 3) : uint32_t(row & 7);
+        return uint32_t(row) * kRowBytes + ((uint32_t(u) ^ sw) << 4);
+    }
+};
+
+template <int N, bool kBf16>
 __device__ __forceinline__ void store_epilogue_tma(const ConvArgs& p, const float* bn, const CUtensorMap* omap,
                                                    const CUtensorMap* smap, uint32_t taddr, int row0, bool valid,
                                                    EpiWarp& ew, int lane) {
+    using Box = EpiBox<kBf16>;
     constexpr int kChunks = N / 32;
-    constexpr uint32_t kBox = 2048;
+    constexpr uint32_t kBox = Box::kBytes;
     if (row0 >= p.rows) return;   // all 32 rows past the frame: nothing to store
     const bool skip = p.skip != nullptr;
-    const uint32_t swz = uint32_t((lane >> 1) & 3);
     if (skip && lane == 0) {
         mbar_arrive_expect_tx(&ew.sbar[0], kBox);
         tma_load_2d(smap, ew.sbuf, &ew.sbar[0], 0, row0);
@@ -237,39 +250,54 @@ __device__ __forceinline__ void store_epilogue_tma(const ConvArgs& p, const floa
         if (skip) {
             mbar_wait(&ew.sbar[cb], (ew.sphase >> cb) & 1u, p.err, kErrWaitEpilogue);
             ew.sphase ^= 1u << cb;
-            const uint8_t* row = ew.sbuf + cb * kBox + uint32_t(lane) * 64u;
+            const uint8_t* box = ew.sbuf + cb * kBox;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const uint4 w4 = *reinterpret_cast<const uint4*>(row + ((uint32_t(u) ^ swz) << 4));
-                const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&w4);
+            for (int u = 0; u < Box::kPieces; ++u) {
+                const uint4 w4 = *reinterpret_cast<const uint4*>(box + Box::piece(lane, u));
+                if constexpr (kBf16) {
+                    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&w4);
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 f = __bfloat1622float2(h2[e]);
-                    y[u * 8 + 2 * e] = __fadd_rn(y[u * 8 + 2 * e], f.x);
-                    y[u * 8 + 2 * e + 1] = __fadd_rn(y[u * 8 + 2 * e + 1], f.y);
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 f = __bfloat1622float2(h2[e]);
+                        y[u * 8 + 2 * e] = __fadd_rn(y[u * 8 + 2 * e], f.x);
+                        y[u * 8 + 2 * e + 1] = __fadd_rn(y[u * 8 + 2 * e + 1], f.y);
+                    }
+                } else {
+                    const float* f = reinterpret_cast<const float*>(&w4);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) y[u * 4 + e] = __fadd_rn(y[u * 4 + e], f[e]);
                 }
             }
         }
-        uint4 out[4];
+        uint4 out[Box::kPieces];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&out[u]);
+        for (int u = 0; u < Box::kPieces; ++u) {
+            if constexpr (kBf16) {
+                __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&out[u]);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float a0 = y[u * 8 + 2 * e], a1 = y[u * 8 + 2 * e + 1];
-                h2[e] = valid ? __floats2bfloat162_rn(a0 > 0.0f ? a0 : 0.0f, a1 > 0.0f ? a1 : 0.0f)
-                              : __floats2bfloat162_rn(0.0f, 0.0f);
+                for (int e = 0; e < 4; ++e) {
+                    const float a0 = y[u * 8 + 2 * e], a1 = y[u * 8 + 2 * e + 1];
+                    h2[e] = valid ? __floats2bfloat162_rn(a0 > 0.0f ? a0 : 0.0f, a1 > 0.0f ? a1 : 0.0f)
+                                  : __floats2bfloat162_rn(0.0f, 0.0f);
+                }
+            } else {
+                float* f = reinterpret_cast<float*>(&out[u]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float a = y[u * 4 + e];
+                    f[e] = valid && a > 0.0f ? a : 0.0f;
+                }
             }
         }
         if (lane == 0) bulk_wait_read<1>();   // the store from this box two chunks ago has read it
         __syncwarp();
-        uint8_t* orow = ew.obuf + cb * kBox + uint32_t(lane) * 64u;
+        uint8_t* obox = ew.obuf + cb * kBox;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) *reinterpret_cast<uint4*>(orow + ((uint32_t(u) ^ swz) << 4)) = out[u];
+        for (int u = 0; u < Box::kPieces; ++u) *reinterpret_cast<uint4*>(obox + Box::piece(lane, u)) = out[u];
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-            tma_store_2d(omap, ew.obuf + cb * kBox, c * 32, row0);
+            tma_store_2d(omap, obox, c * 32, row0);
             bulk_commit();
         }
     }
@@ -422,8 +450,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int row_in_tile = quarter * 32 + lane;
         const int n1 = p.n + 1;
         EpiWarp ew;
-        ew.obuf = sm.epi + quarter * 8192;
-        ew.sbuf = ew.obuf + 4096;
+        ew.obuf = sm.epi + quarter * (C::kEpiBytes / 4);
+        ew.sbuf = ew.obuf + C::kEpiBytes / 8;
         ew.sbar = sm.skip_full + 2 * quarter;
         uint32_t j = 0;
         for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++j) {
@@ -437,7 +465,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 valid = r >= n1 && (r % n1) != p.n;
             }
             const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + acc * N;
-            if constexpr (C::kEpiTma) store_epilogue_tma<N>(p, sm.bn, &mOut, &mSkip, taddr, tile * 128 + quarter * 32, valid, ew, lane);
+            if constexpr (C::kEpiTma) store_epilogue_tma<N, kBf16>(p, sm.bn, &mOut, &mSkip, taddr, tile * 128 + quarter * 32, valid, ew, lane);
             else store_epilogue<N, kBf16, kSplit>(p, taddr, q, valid);
             tc_fence_before();
             mbar_arrive(&sm.acc_empty[acc]);
@@ -637,8 +665,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int n1 = p.n + 1;
         const uint32_t leader_empty0 = mapa(smem_u32(&sm.acc_empty[0]), 0), leader_empty1 = leader_empty0 + 8u;
         EpiWarp ew;
-        ew.obuf = sm.epi + quarter * 8192;
-        ew.sbuf = ew.obuf + 4096;
+        ew.obuf = sm.epi + quarter * (C::kEpiBytes / 4);
+        ew.sbuf = ew.obuf + C::kEpiBytes / 8;
         ew.sbar = sm.skip_full + 2 * quarter;
         uint32_t j = 0;
         for (int pr = pair0; pr < npairs; pr += pair_step, ++j) {
@@ -653,7 +681,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + acc * N;
             if constexpr (C::kEpiTma)
-                store_epilogue_tma<N>(p, sm.bn, &mOut, &mSkip, taddr, (2 * pr + int(rank)) * 128 + quarter * 32, valid, ew, lane);
+                store_epilogue_tma<N, kBf16>(p, sm.bn, &mOut, &mSkip, taddr, (2 * pr + int(rank)) * 128 + quarter * 32, valid, ew, lane);
             else
                 store_epilogue<N, kBf16, kSplit>(p, taddr, q, valid);
             tc_fence_before();
@@ -794,7 +822,7 @@ size_t conv_smem_bytes(int n_out, int precision, int halo_rows, int* sa_out, int
     const int ops = precision == kTF32x3 ? 2 : 1;
     const int a_bytes = (halo_rows * 128 + 1023) / 1024 * 1024;
     const uint32_t b_bytes = uint32_t(pair ? n_out / 2 : n_out) * 128u;
-    const uint32_t epi = precision == kBF16 ? 4u * 4u * 2048u : 0u;   // ConvCfg::kEpiBytes
+    const uint32_t epi = precision == kBF16 ? 4u * 4u * 2048u : precision == kTF32 ? 4u * 4u * 4096u : 0u;   // kEpiBytes
     constexpr size_t kMax = 227 * 1024;
     int sa = 2, sb = 2;
     for (int cand = kMaxStages; cand >= 2; --cand)

@@ -556,8 +556,12 @@ void Workspace::place(const Weights& w, uint8_t* base) {
     for (int i = 0; i < 3; ++i) {
         map[i] = make_tensor_map(trunk[i], precision, cpad, rows, KC, uint32_t(fr.halo));
         map_lo[i] = precision == kTF32x3 ? make_tensor_map(trunk_lo[i], precision, cpad, rows, KC, uint32_t(fr.halo)) : map[i];
-        // bf16 conv epilogue boxes: {32 channels, 32 rows}, 64-byte rows, 64-byte swizzle.
-        emap[i] = precision == kBF16 ? make_tensor_map(trunk[i], precision, cpad, rows, 32, 32, 64) : map[i];
+        // The conv epilogue's boxes: {32 channels, 32 rows}; bf16 64-byte rows
+        // with the 64-byte swizzle, fp32 (plain tf32) 128-byte rows with the
+        // 128-byte swizzle. The split mode stores directly.
+        if (precision == kBF16) emap[i] = make_tensor_map(trunk[i], precision, cpad, rows, 32, 32, 64);
+        else if (precision == kTF32) emap[i] = make_tensor_map(trunk[i], precision, cpad, rows, 32, 32, 128);
+        else emap[i] = map[i];
     }
 }
 

@@ -130,7 +130,7 @@ public:
     float* hid = nullptr;         // [max_batch][value_hidden]: value FC1 output
     int* err = nullptr;           // kernel error word
     CUtensorMap map[3]{}, map_lo[3]{};
-    CUtensorMap emap[3]{};        // bf16: the frames in the conv epilogue's {32, 32} boxes
+    CUtensorMap emap[3]{};        // bf16, tf32: the frames in the conv epilogue's {32, 32} boxes
     CUtensorMap map_stem{}, map_stem_lo{};
 
 private:

@@ -73,7 +73,7 @@ struct ConvMaps {
     CUtensorMap a, a_lo;             // input activations: box {chunk, halo_rows}
     CUtensorMap w, w_lo;             // weights [N][9*Cin]: box {chunk, N}
     CUtensorMap w_pair, w_lo_pair;   // the same weights in boxes of {chunk, N/2}: one half per CTA of a pair
-    CUtensorMap out, skip;           // bf16: the output and residual frames in boxes of {32, 32}, 64-byte swizzle
+    CUtensorMap out, skip;           // bf16/tf32: the output and residual frames in boxes of {32, 32} (epilogue)
 };
 
 // Shared memory a conv launch needs, and its pipeline depths (pair: the

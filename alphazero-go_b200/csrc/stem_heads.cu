@@ -133,7 +133,7 @@ struct TrunkPiece {
 // The trunk streamed once through shared memory. A copy thread (warp 8)
 // stages `kbr` board rows at a time into a ring of `stages` buffers: the n
 // real points of a board row are n consecutive frame rows, one bulk copy
-// each, so padding rows are never read. 8 reader warps take the staged rows
+// each, so padding rows are never read. 16 reader warps take the staged rows
 // four "slots" at a time: kLpr lanes share one row (kLpr x kNch 16-byte
 // pieces, lane l reading pieces l, l + kLpr, ...: consecutive lanes,
 // consecutive pieces), each lane summing its channels into 4 slots x 4
@@ -144,7 +144,7 @@ struct TrunkPiece {
 // finished sums, which it applies the batch norm to and stores. Every sum is the same tree of
 // additions whatever its slot: outputs do not depend on the batch.
 // Persistent CTAs, one per SM; every wait is bounded.
-constexpr int kHcReaders = 8;
+constexpr int kHcReaders = 16;
 constexpr int kHcThreads = 32 * (kHcReaders + 1);
 
 // v / n for v >= 0 and n <= 19: below 2^20 with a float reciprocal ((v +
@@ -460,16 +460,16 @@ cudaError_t launch_stem_pack(const StemArgs& a, int precision, cudaStream_t s) {
 namespace {
 
 // One persistent CTA per SM (fewer for small batches). A stage holds as
-// many board rows as about three reader steps cover (8 warps x 4 slots x
+// many board rows as about three reader steps cover (16 warps x 4 slots x
 // rows per slot each), capped so that at least two stages fit in 200 KB;
-// as many stages as fit, at most 8 (C4 bf16: 4 stages of 5 board rows).
+// as many stages as fit, at most 8 (C4 bf16: 2 stages of 10 board rows).
 template <int kMode, int kLpr, int kNch>
 cudaError_t launch_head_conv_as(const HeadArgs& a, int sms, cudaStream_t s) {
     const uint32_t row_bytes = uint32_t(a.ld) * (kMode == kBF16 ? 2u : 4u);
     const size_t planes = kMode == kTF32x3 ? 2 : 1, br_bytes = size_t(a.n) * row_bytes * planes;
     constexpr size_t kBudget = 200u << 10;
     const int step_rows = kHcReaders * kHcSlots * (32 / kLpr);
-    int kbr = std::max(1, (step_rows * 3) / a.n);   // about three reader steps per stage
+    int kbr = std::max(1, (step_rows * 3) / a.n);   // about three reader steps per stage, if two stages fit
     kbr = int(std::max<size_t>(1, std::min<size_t>(size_t(kbr), kBudget / 2 / br_bytes)));
     kbr = std::min(kbr, a.B * a.n);
     const size_t stage = size_t(kbr) * br_bytes;
