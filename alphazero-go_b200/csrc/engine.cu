@@ -503,6 +503,14 @@ Weights::~Weights() {
 
 // -------------------------------------------------------------- workspace
 
+// Floats per board of the heads' feature buffer: the 2A policy features and
+// the A value features, each padded with zeros to a multiple of 4 (16-byte
+// rows for the FC kernel's loads).
+size_t feat_floats(const NetShape& s) {
+    const size_t A = size_t(s.area());
+    return (2 * A + 3) / 4 * 4 + (A + 3) / 4 * 4;
+}
+
 size_t Workspace::bytes_for(const NetShape& s, int precision, int max_batch) {
     const Frame fr(s.board);
     const size_t rows = size_t(max_batch) * fr.S;
@@ -520,7 +528,7 @@ size_t Workspace::bytes_for(const NetShape& s, int precision, int max_batch) {
     c.take(B * 4);
     if (s.ownership) c.take(B * A * 4);
     c.take(B * L * 4);
-    c.take(B * 3 * A * 4);
+    c.take(B * feat_floats(s) * 4);
     c.take(B * size_t(s.value_hidden) * 4);
     c.take(16);
     return c.used;
@@ -547,7 +555,7 @@ void Workspace::place(const Weights& w, uint8_t* base) {
     values = reinterpret_cast<float*>(at(c.take(B * 4)));
     if (s.ownership) ownership = reinterpret_cast<float*>(at(c.take(B * A * 4)));
     probs = reinterpret_cast<float*>(at(c.take(B * L * 4)));
-    feat = reinterpret_cast<float*>(at(c.take(B * 3 * A * 4)));
+    feat = reinterpret_cast<float*>(at(c.take(B * feat_floats(s) * 4)));
     hid = reinterpret_cast<float*>(at(c.take(B * size_t(s.value_hidden) * 4)));
     err = reinterpret_cast<int*>(at(c.take(16)));
     const uint32_t KC = uint32_t(chunk_channels(precision));
@@ -679,6 +687,8 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
     h.ownership_out = ws.ownership;
     h.probs = probs ? ws.probs : nullptr;
     h.feat = ws.feat;
+    h.feat_val = int((2 * size_t(sh.area()) + 3) / 4 * 4);
+    h.feat_ld = int(feat_floats(sh));
     h.hid = ws.hid;
     h.err = ws.err;
     mark_begin(kSlotHeadConv);

@@ -126,7 +126,7 @@ public:
     float* values = nullptr;      // [max_batch]
     float* ownership = nullptr;   // [max_batch][area] when the head exists
     float* probs = nullptr;       // [max_batch][actions]
-    float* feat = nullptr;        // [max_batch][3 * area]: the heads' 1x1 conv features
+    float* feat = nullptr;        // [max_batch][feat_floats]: the heads' 1x1 conv features
     float* hid = nullptr;         // [max_batch][value_hidden]: value FC1 output
     int* err = nullptr;           // kernel error word
     CUtensorMap map[3]{}, map_lo[3]{};
@@ -153,6 +153,7 @@ constexpr int kTimedStages = 6;   // stem operand, stem GEMM, tower, head conv, 
 
 // Network::forward (src/network.cpp:228-309) on the GPU: stem, the tower's
 // fused convolutions, the fused heads; all on one stream.
+size_t feat_floats(const NetShape& s);   // floats per board of the heads' feature buffer
 void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool probs, PassTimer* timer = nullptr);
 
 // A row-major [rows][inner] tensor read by TMA in boxes of box_inner x

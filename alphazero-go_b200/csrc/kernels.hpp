@@ -116,7 +116,9 @@ struct HeadArgs {
     float* values;      // [B]
     float* ownership_out;   // [B][A] or null
     float* probs;       // [B][A+1] or null
-    float* feat;        // scratch [B][3A]: policy features (c*A + p), then value features
+    float* feat;        // scratch [B][feat_ld]: policy features (c*A + p), zeros to a multiple of 4,
+                        // then value features from feat_val, zeros to a multiple of 4
+    int feat_ld, feat_val;
     float* hid;         // scratch [B][V]: value FC1 after ReLU
     int* err;           // kernel error word (a bounded wait that ran out)
 };

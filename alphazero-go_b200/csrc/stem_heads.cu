@@ -31,25 +31,38 @@ unsigned blocks_for(size_t count, int threads) {
 // buffer was allocated).
 template <int kMode>
 __global__ void __launch_bounds__(256) stem_pack_kernel(const StemArgs a) {
-    extern __shared__ float planes[];   // [P][A]
+    extern __shared__ float planes[];   // [P][A], then the column table
     constexpr int W = kMode == kBF16 ? 8 : 4;   // values per 16-byte piece
     const int A = a.n * a.n, K = 9 * a.P, pieces = a.ld / W;
+    // Column k of a row reads plane k % P at tap t = k / P: table[e][j] for
+    // k = j*W + e holds (plane * A) << 4 | (dy+1) << 2 | (dx+1), or -1 past
+    // K (laid out by e so that the lanes, consecutive j, read consecutive
+    // words).
+    int* table = reinterpret_cast<int*>(planes + size_t(a.P) * A);
+    for (int i = threadIdx.x; i < W * pieces; i += blockDim.x) {
+        const int e = i / pieces, j = i % pieces, k = j * W + e;
+        int code = -1;
+        if (k < K) {
+            const int t = k / a.P, pl = k % a.P;
+            code = ((pl * A) << 4) | ((t / 3) << 2) | (t % 3);
+        }
+        table[i] = code;
+    }
     for (int b = blockIdx.x; b < a.B; b += gridDim.x) {
         __syncthreads();
         for (int i = threadIdx.x; i < a.P * A; i += blockDim.x) planes[i] = __ldg(a.in + size_t(b) * a.P * A + i);
         __syncthreads();
         for (int item = threadIdx.x; item < A * pieces; item += blockDim.x) {
-            const int pt = item / pieces, j = item % pieces;
-            const int py = pt / a.n, px = pt % a.n;
+            const int pt = item / pieces, j = item - pt * pieces;
+            const int py = pt / a.n, px = pt - py * a.n;
             float v[W];
 #pragma unroll
             for (int e = 0; e < W; ++e) {
-                const int k = j * W + e;
+                const int code = table[e * pieces + j];
                 v[e] = 0.0f;
-                if (k < K) {
-                    const int t = k / a.P, pl = k % a.P;
-                    const int y = py + t / 3 - 1, x = px + t % 3 - 1;
-                    if (y >= 0 && y < a.n && x >= 0 && x < a.n) v[e] = planes[pl * A + y * a.n + x];
+                if (code >= 0) {
+                    const int y = py + ((code >> 2) & 3) - 1, x = px + (code & 3) - 1;
+                    if (y >= 0 && y < a.n && x >= 0 && x < a.n) v[e] = planes[(code >> 4) + y * a.n + x];
                 }
             }
             const size_t off = (size_t(b) * a.S + size_t(py + 1) * (a.n + 1) + px) * a.ld + size_t(j) * W;
@@ -299,7 +312,7 @@ __global__ void __launch_bounds__(kHcThreads, 1)
                     const int b = div_small(br, n, inv_n), p = (br - b * n) * n + x;
                     const float y = __fadd_rn(__fmul_rn(bn_scale[j], acc[j]), bn_shift[j]);
                     if (h < 3) {
-                        a.feat[size_t(b) * 3 * A + size_t(h) * A + p] = y > 0.0f ? y : 0.0f;
+                        a.feat[size_t(b) * a.feat_ld + (h == 2 ? a.feat_val : h * A) + p] = y > 0.0f ? y : 0.0f;
                     } else if (a.ownership && a.ownership_out) {
                         a.ownership_out[size_t(b) * A + p] = tanhf(y);
                     }
@@ -330,12 +343,12 @@ __global__ void __launch_bounds__(kHeadThreads) head_fc_kernel(const HeadArgs a)
     const int pol_tiles = (L + outs_per_cta - 1) / outs_per_cta;
     const bool policy = int(blockIdx.y) < pol_tiles;
     const int n_in = policy ? 2 * A : A, n4 = (n_in + 3) / 4, ncols = policy ? L : V;
-    const int foff = policy ? 0 : 2 * A;
+    const int foff = policy ? 0 : a.feat_val;   // multiples of 4 floats, as is feat_ld
     const int b0 = blockIdx.x * kFcBoards, G = min(kFcBoards, a.B - b0);
-    float* xf = reinterpret_cast<float*>(xs);
-    for (int idx = threadIdx.x; idx < kFcBoards * n4 * 4; idx += kHeadThreads) {
-        const int g = idx / (n4 * 4), i = idx % (n4 * 4);
-        xf[idx] = g < G && i < n_in ? a.feat[size_t(b0 + g) * 3 * A + foff + i] : 0.0f;
+    const float4* feat4 = reinterpret_cast<const float4*>(a.feat);
+    for (int idx = threadIdx.x; idx < kFcBoards * n4; idx += kHeadThreads) {
+        const int g = idx / n4, j = idx - g * n4;
+        xs[idx] = g < G ? feat4[(size_t(b0 + g) * a.feat_ld + foff) / 4 + j] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -446,7 +459,7 @@ cudaError_t launch_stem_pack(const StemArgs& a, int precision, cudaStream_t s) {
     if (a.B <= 0) return cudaSuccess;
     const int W = precision == kBF16 ? 8 : 4;
     if (a.ld % W != 0) return cudaErrorInvalidValue;
-    const size_t smem = size_t(a.P) * a.n * a.n * sizeof(float);
+    const size_t smem = size_t(a.P) * a.n * a.n * sizeof(float) + size_t(a.ld) * sizeof(int);
     const unsigned grid = static_cast<unsigned>(std::min(a.B, 148 * 8));
     switch (precision) {
         case kTF32: stem_pack_kernel<kTF32><<<grid, 256, smem, s>>>(a); break;
