@@ -20,6 +20,10 @@
 // in index order, so callers can check that the games do not depend on the
 // number of workers, the batch cap or the hub's chaos mode.
 //
+// azsp_arena plays an arena wave the same way: the reference's
+// playArenaGames (src/arena.cpp) on waveSlice(wave, first, count), with one
+// evaluator set (one hub, for cuda) per network, the games hashed in order.
+//
 // Built by alphazero-go_b200/host/Makefile from the reference's sources.
 #include <algorithm>
 #include <atomic>
@@ -27,12 +31,14 @@
 #include <cstdint>
 #include <cstring>
 #include <exception>
+#include <memory>
 #include <mutex>
 #include <stdexcept>
 #include <string>
 #include <thread>
 #include <vector>
 
+#include "azgo/arena.hpp"
 #include "azgo/evaluator.hpp"
 #include "azgo/inference_hub.hpp"
 #include "azgo/mcts.hpp"
@@ -122,7 +128,22 @@ void load_arenas(Network& net, const float* params, size_t n_params, const float
     for (size_t i = 0; i < bv.size(); ++i) std::memcpy(bv[i].value, buffers + L.buffers[i].offset, bv[i].size * 4);
 }
 
+NetConfig make_config(int board, int history, int blocks, int filters, int value_hidden) {
+    NetConfig cfg;
+    cfg.boardSize = board;
+    cfg.history = history;
+    cfg.blocks = blocks;
+    cfg.filters = filters;
+    cfg.valueHidden = value_hidden;
+    return cfg;
+}
+
 } // namespace
+
+// The reference's setThreadQos (src/selfplay_slice.cpp:34-40) asks macOS to
+// schedule a worker at a QoS class and does nothing elsewhere; arena.cpp
+// calls it, and selfplay_slice.cpp (which defines it) is not linked here.
+void azgo::setThreadQos(CpuQos) {}
 
 extern "C" {
 
@@ -141,13 +162,7 @@ int azsp_play(int board, int history, int blocks, int filters, int value_hidden,
         (void)device;
         (void)precision;
 #endif
-        NetConfig cfg;
-        cfg.boardSize = board;
-        cfg.history = history;
-        cfg.blocks = blocks;
-        cfg.filters = filters;
-        cfg.valueHidden = value_hidden;
-        Network net(cfg, 0);
+        Network net(make_config(board, history, blocks, filters, value_hidden), 0);
         load_arenas(net, params, n_params, buffers, n_buffers);
 
         SelfPlayConfig sp;
@@ -195,6 +210,80 @@ int azsp_play(int board, int history, int blocks, int filters, int value_hidden,
         if (evaluations) *evaluations = evaluators.evaluations();
         Fnv f;
         for (const GameRecord& g : records) hash_record(f, g);
+        if (record_hash) *record_hash = f.h;
+        return 0;
+    } catch (const std::exception& e) {
+        put(err, cap, e.what());
+        return -1;
+    }
+}
+
+// An arena wave: matches m = 0 .. n_matches-1 between network a_net[m] and
+// network b_net[m] (or, when b_net[m] < 0, a uniform bot searching
+// bot_sims[m] playouts), games[m] games seeded seeds[m]; games [first, first
+// + count) of the wave (numbered match-major) are played with
+// playArenaGames(waveSlice(wave, first, count), cfg, run) on the networks
+// loaded from their arenas. Reports A's total score, the evaluations, an
+// FNV-1a hash of every game's (score, moves) in order, and (game_hashes, when
+// not null: `count` entries) each game's own hash. 0, or -1 with err.
+int azsp_arena(int board, int history, int blocks, int filters, int value_hidden, int n_nets,
+               const float* const* params, const size_t* n_params, const float* const* buffers,
+               const size_t* n_buffers, int n_matches, const int* a_net, const int* b_net, const int* bot_sims,
+               const int* games, const uint64_t* seeds, int first, int count, int simulations, int mcts_batch,
+               int temperature_moves, const char* backend, int workers, int inference_batch, int device,
+               int precision, double* score_a, long long* evaluations, uint64_t* record_hash, uint64_t* game_hashes,
+               char* err, size_t cap) {
+    try {
+#ifdef AZSP_WITH_ENGINE
+        azb_host::setDefaults(device, precision);
+#else
+        (void)device;
+        (void)precision;
+#endif
+        const NetConfig cfg = make_config(board, history, blocks, filters, value_hidden);
+        std::vector<std::unique_ptr<Network>> nets;
+        for (int i = 0; i < n_nets; ++i) {
+            nets.push_back(std::make_unique<Network>(cfg, 0));
+            load_arenas(*nets.back(), params[i], n_params[i], buffers[i], n_buffers[i]);
+        }
+        auto net_at = [&](int i) -> const Network& {
+            if (i < 0 || i >= n_nets) throw std::invalid_argument("azsp_arena: no network " + std::to_string(i));
+            return *nets[static_cast<size_t>(i)];
+        };
+        std::vector<ArenaMatchSpec> wave;
+        for (int m = 0; m < n_matches; ++m) {
+            ArenaMatchSpec spec;
+            spec.a = ArenaPlayer::network(net_at(a_net[m]));
+            spec.b = b_net[m] >= 0 ? ArenaPlayer::network(net_at(b_net[m])) : ArenaPlayer::bot(bot_sims[m]);
+            spec.games = games[m];
+            spec.seed = seeds[m];
+            wave.push_back(spec);
+        }
+        ArenaConfig ac;
+        ac.simulations = simulations;
+        ac.mctsBatch = mcts_batch;
+        ac.temperatureMoves = temperature_moves;
+        EngineRun run;
+        run.backend = backend;
+        run.workers = workers;
+        run.inferenceBatch = inference_batch;
+        SliceStats stats;
+        const std::vector<ArenaGameResult> played = playArenaGames(waveSlice(wave, first, count), ac, run, &stats);
+        Fnv f;
+        double total = 0;
+        for (size_t i = 0; i < played.size(); ++i) {
+            const ArenaGameResult& g = played[i];
+            Fnv one;
+            for (Fnv* h : {&f, &one}) {
+                h->value(g.scoreA);
+                h->value(g.moves.size());
+                h->bytes(g.moves.data(), g.moves.size() * sizeof(int));
+            }
+            if (game_hashes && i < static_cast<size_t>(count)) game_hashes[i] = one.h;
+            total += g.scoreA;
+        }
+        if (score_a) *score_a = total;
+        if (evaluations) *evaluations = stats.evaluations;
         if (record_hash) *record_hash = f.h;
         return 0;
     } catch (const std::exception& e) {

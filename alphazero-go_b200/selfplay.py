@@ -6,7 +6,8 @@ playSelfPlayGame (src/selfplay.cpp:50) and WorkerEvaluators/InferenceHub
 drop-in bridge as its "cuda" engine. A slice of games is played the way the
 reference's playSelfPlayQueue plays one (src/selfplay_slice.cpp:93-149); the
 statistics are SliceStats', and playouts/s = positions x simulations /
-seconds, as the reference reports it.
+seconds, as the reference reports it. `arena` plays an arena wave (several
+matches, one hub per network) through the reference's playArenaGames.
 """
 from __future__ import annotations
 
@@ -32,6 +33,12 @@ def _lib(path: str) -> C.CDLL:
                                  C.POINTER(C.c_double), C.POINTER(C.c_longlong), C.POINTER(C.c_longlong),
                                  C.POINTER(C.c_uint64), C.c_char_p, C.c_size_t])
         L.azsp_play.restype = C.c_int
+        PF, PS = C.POINTER(F), C.POINTER(C.c_size_t)
+        PI, PU = C.POINTER(C.c_int), C.POINTER(C.c_uint64)
+        L.azsp_arena.argtypes = ([C.c_int] * 6 + [PF, PS, PF, PS, C.c_int, PI, PI, PI, PI, PU] + [C.c_int] * 5 +
+                                 [C.c_char_p] + [C.c_int] * 4 + [C.POINTER(C.c_double), C.POINTER(C.c_longlong),
+                                                                 PU, PU, C.c_char_p, C.c_size_t])
+        L.azsp_arena.restype = C.c_int
         _libs[path] = L
     return _libs[path]
 
@@ -63,3 +70,40 @@ def play(desc, params: np.ndarray, buffers: np.ndarray, *, backend: str = "cuda"
     return {"seconds": s, "positions": pos.value, "evaluations": evals.value, "record_hash": h.value,
             "playouts_per_s": pos.value * simulations / s if s > 0 else 0.0,
             "evaluations_per_s": evals.value / s if s > 0 else 0.0}
+
+
+def arena(desc, nets: list, matches: list, *, first: int = 0, count: int | None = None, simulations: int = 100,
+          mcts_batch: int = 8, temperature_moves: int = 4, backend: str = "cuda", workers: int = 0,
+          inference_batch: int = 256, device: int = 0, precision: int = 2, lib_path: str | None = None) -> dict:
+    """An arena wave through the reference's playArenaGames (src/arena.cpp).
+
+    nets: [(params, buffers), ...]; matches: [(a, b, games, seed), ...] with
+    a, b network indices, or b = ("bot", simulations) for a uniform bot.
+    Games [first, first + count) of the wave (match-major) are played."""
+    L = _lib(lib_path or LIB_PATH)
+    F = C.POINTER(C.c_float)
+    arrs = [(np.ascontiguousarray(p, np.float32), np.ascontiguousarray(b, np.float32)) for p, b in nets]
+    n = len(arrs)
+    P = (F * n)(*[a[0].ctypes.data_as(F) for a in arrs])
+    B = (F * n)(*[a[1].ctypes.data_as(F) for a in arrs])
+    NP = (C.c_size_t * n)(*[a[0].size for a in arrs])
+    NB = (C.c_size_t * n)(*[a[1].size for a in arrs])
+    m = len(matches)
+    a_net = (C.c_int * m)(*[x[0] for x in matches])
+    b_net = (C.c_int * m)(*[x[1] if isinstance(x[1], int) else -1 for x in matches])
+    bots = (C.c_int * m)(*[0 if isinstance(x[1], int) else x[1][1] for x in matches])
+    games = (C.c_int * m)(*[x[2] for x in matches])
+    seeds = (C.c_uint64 * m)(*[x[3] for x in matches])
+    if count is None:
+        count = sum(x[2] for x in matches) - first
+    score, evals, h = C.c_double(), C.c_longlong(), C.c_uint64()
+    per_game = (C.c_uint64 * max(1, count))()
+    err = C.create_string_buffer(1024)
+    rc = L.azsp_arena(desc.board, desc.history, desc.blocks, desc.filters, desc.value_hidden, n, P, NP, B, NB, m,
+                      a_net, b_net, bots, games, seeds, first, count, simulations, mcts_batch, temperature_moves,
+                      backend.encode(), workers, inference_batch, device, precision, C.byref(score), C.byref(evals),
+                      C.byref(h), per_game, err, 1024)
+    if rc != 0:
+        raise RuntimeError(err.value.decode())
+    return {"score_a": score.value, "evaluations": evals.value, "record_hash": h.value,
+            "games": list(per_game)[:count]}

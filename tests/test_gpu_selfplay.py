@@ -1,6 +1,6 @@
 """Self-play on the engine through the reference's own search and hub.
 
-Mirrors the reference's tests/test_cuda.cpp:1270-1295 (the determinism
+Mirrors the reference's tests/test_cuda.cpp:1270-1348 (the determinism
 contract of a cuda engine's slice): the same games, byte for byte, for 1, 3
 and 8 workers, batches capped at 8 or 256, and the hub's chaos mode on or
 off. Records are compared through the driver's FNV-1a hash of every game in
@@ -45,3 +45,31 @@ def test_slice_independent_of_workers_and_batching(engine, sp, shape, precision)
                 if reference is None:
                     reference = r["record_hash"]
                 assert r["record_hash"] == reference, (workers, batch, chaos)
+
+
+WAVE = [(0, 1, 6, 901), (0, ("bot", 8), 4, 902), (0, 2, 4, 903)]
+
+
+def test_arena_wave_independent_of_workers_and_batching(engine, sp):
+    """tests/test_cuda.cpp:1301-1348: an arena wave on the cuda engine (one hub per network, three
+    networks sharing the GPU) plays the same games for any workers, batch cap and chaos mode, and a
+    wave played in two slices plays what the whole wave plays."""
+    d = engine.NetDesc(5, 1, 1, 8, 16, 0)
+    nets = [engine.synth_network(d, s, 1) for s in (811, 812, 813)]
+    kw = dict(simulations=16, mcts_batch=4, temperature_moves=2, backend="cuda", precision=engine.TF32X3)
+    reference = None
+    for workers in (1, 3, 0):
+        for batch in (8, 256):
+            for chaos in (0, 23):
+                engine.cuda_probe.set_hub_chaos_seed(chaos)
+                try:
+                    r = sp.arena(d, nets, WAVE, first=0, count=14, workers=workers, inference_batch=batch, **kw)
+                finally:
+                    engine.cuda_probe.set_hub_chaos_seed(0)
+                assert r["evaluations"] > 0
+                if reference is None:
+                    reference = r["games"]
+                assert r["games"] == reference, (workers, batch, chaos)
+    a = sp.arena(d, nets, WAVE, first=0, count=5, **kw)
+    b = sp.arena(d, nets, WAVE, first=5, count=9, **kw)
+    assert a["games"] + b["games"] == reference

@@ -53,3 +53,30 @@ def test_bad_arenas_are_refused():
         SP.play(d, p[:-64], b, backend="naive", workers=1, simulations=8, count=1, lib_path=REF_LIB)
     with pytest.raises(RuntimeError):
         SP.play(d, p, b, backend="no-such-engine", workers=1, simulations=8, count=1, lib_path=REF_LIB)
+
+
+WAVE = [(0, 1, 6, 901), (0, ("bot", 8), 4, 902), (0, 2, 4, 903)]
+
+
+def _wave_nets(E):
+    d = E.NetDesc(5, 1, 1, 8, 16, 0)
+    return d, [E.synth_network(d, s, 1) for s in (811, 812, 813)]
+
+
+def test_arena_wave_independent_of_workers_and_slicing():
+    """The reference's arena-wave contract (tests/test_cuda.cpp:1301-1348) on its naive engine: the same
+    games for any number of workers, and a wave played in two slices equals the whole wave."""
+    _need(REF_LIB)
+    import azb200 as E
+    import selfplay as SP
+
+    d, nets = _wave_nets(E)
+    kw = dict(simulations=16, mcts_batch=4, temperature_moves=2, backend="naive", lib_path=REF_LIB)
+    whole = {SP.arena(d, nets, WAVE, first=0, count=14, workers=w, **kw)["record_hash"] for w in (1, 3, 0)}
+    assert len(whole) == 1
+    a = SP.arena(d, nets, WAVE, first=0, count=5, workers=2, **kw)
+    b = SP.arena(d, nets, WAVE, first=5, count=9, workers=2, **kw)
+    total = SP.arena(d, nets, WAVE, first=0, count=14, workers=2, **kw)
+    assert a["games"] + b["games"] == total["games"]
+    assert a["score_a"] + b["score_a"] == total["score_a"]
+    assert total["evaluations"] > 0
