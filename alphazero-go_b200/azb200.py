@@ -79,6 +79,9 @@ def lib() -> C.CDLL:
             L.azb_infer_create.argtypes = [D, _F, s, _F, s, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_void_p)] + err
             L.azb_infer_destroy.argtypes = [C.c_void_p]
             L.azb_infer_run.argtypes = [C.c_void_p, _F, C.c_int, _F, _F, _F, _F] + err
+            L.azb_stones_record_bytes.argtypes = [C.c_int, C.c_int]
+            L.azb_stones_record_bytes.restype = C.c_size_t
+            L.azb_infer_run_stones.argtypes = [C.c_void_p, C.c_void_p, C.c_int, _F, _F, _F] + err
             L.azb_infer_bytes.argtypes = [C.c_void_p]
             L.azb_infer_bytes.restype = s
             L.azb_infer_stage.argtypes = [C.c_void_p, _F, C.c_int] + err
@@ -259,6 +262,22 @@ class CudaInference:
             raise CudaError(e.value.decode())
         return (logits, values, own, pr) if probs else (logits, values, own)
 
+    def infer_stones(self, records: np.ndarray, ownership: bool = None):
+        """infer() from position records (stones_records): the planes are encoded on the device."""
+        records = np.ascontiguousarray(records, np.uint8)
+        B = records.shape[0]
+        d = self.desc
+        if records.shape[1] != stones_record_bytes(d.history, d.board):
+            raise ValueError("records: wrong record size")
+        logits = np.empty((B, d.actions), np.float32)
+        values = np.empty(B, np.float32)
+        own = np.empty((B, d.area), np.float32) if (d.ownership if ownership is None else ownership) else None
+        e = _err()
+        if lib().azb_infer_run_stones(self.h, records.ctypes.data, B, _fp(logits), _fp(values), _fp(own), e,
+                                      1024) != 0:
+            raise CudaError(e.value.decode())
+        return logits, values, own
+
     def bytes(self) -> int:
         return lib().azb_infer_bytes(self.h)
 
@@ -311,6 +330,30 @@ class CudaInference:
         if lib().azb_infer_read(self.h, B, _fp(logits), _fp(values), _fp(own), _fp(pr), e, 1024) != 0:
             raise CudaError(e.value.decode())
         return logits, values, own, pr
+
+
+# ----------------------------------------------------------- position records
+
+
+def stones_record_bytes(history: int, board: int) -> int:
+    """Bytes of one position record (include/azb200.h, azb_stones_record_bytes)."""
+    return int(lib().azb_stones_record_bytes(history, board))
+
+
+def stones_records(stones: np.ndarray, to_move: np.ndarray, available: np.ndarray | None = None,
+                   sym: np.ndarray | None = None) -> np.ndarray:
+    """Position records from stones [B][H][n*n] (0 empty, 1 Black, 2 White; row k = k plies ago),
+    to_move [B] (1 Black, 2 White), the history positions present [B] (default H) and the
+    symmetries [B] (default 0): [B][stones_record_bytes] uint8."""
+    stones = np.asarray(stones, np.uint8)
+    B, H, A = stones.shape
+    n = int(round(A ** 0.5))
+    rec = np.zeros((B, stones_record_bytes(H, n)), np.uint8)
+    rec[:, :H * A] = stones.reshape(B, H * A)
+    rec[:, H * A] = np.asarray(to_move, np.uint8)
+    rec[:, H * A + 1] = H if available is None else np.asarray(available, np.uint8)
+    rec[:, H * A + 2] = 0 if sym is None else np.asarray(sym, np.uint8)
+    return rec
 
 
 # ------------------------------------------------------------------ runner

@@ -120,6 +120,18 @@ int azb_infer_time(azb_infer* h, int B, int warmup, int steps, int with_copies, 
                    [&] { h->impl->time(B, warmup, steps, with_copies != 0, ms, conv_ms); });
 }
 
+size_t azb_stones_record_bytes(int history, int board) {
+    return history < 1 || board < 1 ? 0 : stones_record_bytes(history, board);
+}
+
+int azb_infer_run_stones(azb_infer* h, const uint8_t* records, int B, float* logits, float* values, float* ownership,
+                         char* err, size_t err_cap) {
+    return guarded(err, err_cap, "GPU inference failed: ", [&] {
+        if (!h || !records || !logits || !values) throw std::invalid_argument("azb_infer_run_stones: null argument");
+        h->impl->infer_stones(records, B, logits, values, ownership);
+    });
+}
+
 int azb_infer_time_stages(azb_infer* h, int B, int steps, double* stage_ms, char* err, size_t err_cap) {
     return guarded(err, err_cap, "GPU inference failed: ", [&] {
         if (!stage_ms) throw std::invalid_argument("azb_infer_time_stages: null stage_ms");

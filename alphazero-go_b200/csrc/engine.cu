@@ -530,6 +530,7 @@ size_t Workspace::bytes_for(const NetShape& s, int precision, int max_batch) {
     c.take(B * L * 4);
     c.take(B * feat_floats(s) * 4);
     c.take(B * size_t(s.value_hidden) * 4);
+    c.take(B * stones_record_bytes(s.history, s.board));
     c.take(16);
     return c.used;
 }
@@ -557,6 +558,7 @@ void Workspace::place(const Weights& w, uint8_t* base) {
     probs = reinterpret_cast<float*>(at(c.take(B * L * 4)));
     feat = reinterpret_cast<float*>(at(c.take(B * feat_floats(s) * 4)));
     hid = reinterpret_cast<float*>(at(c.take(B * size_t(s.value_hidden) * 4)));
+    records = at(c.take(B * stones_record_bytes(s.history, s.board)));
     err = reinterpret_cast<int*>(at(c.take(16)));
     const uint32_t KC = uint32_t(chunk_channels(precision));
     map_stem = make_tensor_map(stem_in, precision, ks, rows, KC, uint32_t(fr.halo));
@@ -751,6 +753,26 @@ void Inference::infer(const float* input, int B, float* logits, float* values, f
               "ownership");
     if (probs)
         check(cudaMemcpyAsync(probs, ws_->probs, size_t(B) * s.actions() * 4, cudaMemcpyDeviceToHost, stream_), "probs");
+    check(cudaMemcpyAsync(err_host_, ws_->err, sizeof(int), cudaMemcpyDeviceToHost, stream_), "error word");
+    check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+    check_error_word();
+}
+
+void Inference::infer_stones(const uint8_t* records, int B, float* logits, float* values, float* ownership) {
+    const NetShape& s = w_->shape();
+    if (ownership && !s.ownership) throw std::invalid_argument("CudaInference: no ownership head");
+    if (B < 1 || B > ws_->max_batch()) throw std::invalid_argument("CudaInference: batch out of range");
+    check(cudaSetDevice(device_), "cudaSetDevice");
+    check(cudaMemcpyAsync(ws_->records, records, size_t(B) * stones_record_bytes(s.history, s.board),
+                          cudaMemcpyHostToDevice, stream_), "records");
+    EncodeArgs e{ws_->records, B, s.history, s.board, ws_->stage};
+    check(launch_encode_planes(e, stream_), "encode");
+    encode_forward(*w_, *ws_, B, stream_, false);
+    check(cudaMemcpyAsync(logits, ws_->logits, size_t(B) * s.actions() * 4, cudaMemcpyDeviceToHost, stream_), "logits");
+    check(cudaMemcpyAsync(values, ws_->values, size_t(B) * 4, cudaMemcpyDeviceToHost, stream_), "values");
+    if (ownership)
+        check(cudaMemcpyAsync(ownership, ws_->ownership, size_t(B) * s.area() * 4, cudaMemcpyDeviceToHost, stream_),
+              "ownership");
     check(cudaMemcpyAsync(err_host_, ws_->err, sizeof(int), cudaMemcpyDeviceToHost, stream_), "error word");
     check(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
     check_error_word();

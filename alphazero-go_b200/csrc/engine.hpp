@@ -128,6 +128,7 @@ public:
     float* probs = nullptr;       // [max_batch][actions]
     float* feat = nullptr;        // [max_batch][feat_floats]: the heads' 1x1 conv features
     float* hid = nullptr;         // [max_batch][value_hidden]: value FC1 output
+    uint8_t* records = nullptr;   // [max_batch][stones_record_bytes]: encoder input (infer_stones)
     int* err = nullptr;           // kernel error word
     CUtensorMap map[3]{}, map_lo[3]{};
     CUtensorMap emap[3]{};        // bf16, tf32: the frames in the conv epilogue's {32, 32} boxes
@@ -172,6 +173,9 @@ public:
               int max_batch, int device, int precision);
     ~Inference();
     void infer(const float* input, int B, float* logits, float* values, float* ownership, float* probs);
+    // The same from position records (kernels.hpp's EncodeArgs): the planes
+    // are encoded on the device, so only the records cross to it.
+    void infer_stones(const uint8_t* records, int B, float* logits, float* values, float* ownership);
     size_t bytes() const { return ws_->bytes(); }
     void stage(const float* input, int B);
     void enqueue(int B);

@@ -97,6 +97,21 @@ struct StemArgs {
 };
 cudaError_t launch_stem_pack(const StemArgs& a, int precision, cudaStream_t s);
 
+// Positions as the reference's encoder takes them (src/encode.cpp:15-43), one
+// record of stones_record_bytes(H, n) bytes each: stones[H][n*n] Color bytes
+// (0 empty, 1 Black, 2 White; row k is the position k plies ago), then
+// toMove (1 Black, 2 White), the number of history positions present
+// (0..H), the symmetry (0..7, as transformPoint numbers them), and zero
+// padding to a multiple of 4 bytes. The kernel writes the [B][2H+2][n*n]
+// fp32 planes encodePlanes writes, into the stage buffer.
+__host__ __device__ inline size_t stones_record_bytes(int H, int n) { return (size_t(H) * n * n + 3 + 3) / 4 * 4; }
+struct EncodeArgs {
+    const uint8_t* records;
+    int B, H, n;
+    float* out;
+};
+cudaError_t launch_encode_planes(const EncodeArgs& a, cudaStream_t s);
+
 // The heads: policy 1x1 conv + BN + ReLU + FC, value 1x1 conv + BN + ReLU +
 // FC + ReLU + FC + tanh, ownership 1x1 conv + BN + tanh, and the softmax
 // over the A+1 moves, in three launches (trunk stream, FC tiles, per-board

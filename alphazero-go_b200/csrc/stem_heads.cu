@@ -87,6 +87,47 @@ __global__ void __launch_bounds__(256) stem_pack_kernel(const StemArgs a) {
     }
 }
 
+// ------------------------------------------------------------- the encoder
+
+// One thread per (position, point q): q's value in every plane. The
+// symmetry sends point p to transformPoint(sym, p), so q reads point
+// p = transformPoint(inverse(sym), q): mirror left-right (sym & 4) first,
+// then (sym & 3) clockwise quarter turns (src/symmetry.cpp:6-19); mirrored
+// symmetries are their own inverse, k turns are undone by 4 - k.
+__device__ __forceinline__ int transform_point(int sym, int point, int n) {
+    int row = point / n, col = point % n;
+    if (sym & 4) col = n - 1 - col;
+    for (int t = 0; t < (sym & 3); ++t) {
+        const int r = col, c = n - 1 - row;
+        row = r;
+        col = c;
+    }
+    return row * n + col;
+}
+
+__global__ void __launch_bounds__(256) encode_planes_kernel(const EncodeArgs a) {
+    const int A = a.n * a.n, P = 2 * a.H + 2;
+    const size_t rec = stones_record_bytes(a.H, a.n);
+    for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < size_t(a.B) * A;
+         i += size_t(gridDim.x) * blockDim.x) {
+        const int b = int(i / A), q = int(i % A);
+        const uint8_t* r = a.records + size_t(b) * rec;
+        const uint8_t* head = r + size_t(a.H) * A;
+        const int to_move = head[0], avail = min(int(head[1]), a.H), sym = head[2] & 7;
+        const int inv = (sym & 4) ? sym : (4 - sym) & 3;
+        const int p = transform_point(inv, q, a.n);
+        const int opp = to_move == 1 ? 2 : 1;
+        float* out = a.out + size_t(b) * P * A + q;
+        for (int k = 0; k < a.H; ++k) {
+            const int stone = k < avail ? r[size_t(k) * A + p] : 0;
+            out[size_t(2 * k) * A] = stone == to_move ? 1.0f : 0.0f;
+            out[size_t(2 * k + 1) * A] = stone == opp ? 1.0f : 0.0f;
+        }
+        out[size_t(2 * a.H) * A] = to_move == 1 ? 1.0f : 0.0f;
+        out[size_t(2 * a.H + 1) * A] = to_move == 1 ? 0.0f : 1.0f;
+    }
+}
+
 // --------------------------------------------------------------- the heads
 //
 // Three launches, each at its own roofline:
@@ -513,6 +554,12 @@ cudaError_t launch_head_conv_mode(const HeadArgs& a, int sms, cudaStream_t s) {
 }
 
 } // namespace
+
+cudaError_t launch_encode_planes(const EncodeArgs& a, cudaStream_t s) {
+    if (a.B <= 0) return cudaSuccess;
+    encode_planes_kernel<<<blocks_for(size_t(a.B) * a.n * a.n, 256), 256, 0, s>>>(a);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_head_conv(const HeadArgs& a, int precision, int sms, cudaStream_t s) {
     if (a.B <= 0) return cudaSuccess;

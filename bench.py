@@ -20,6 +20,8 @@ Printed (rank 0, one JSON line):
   e2e        the same through the runner's C ABI (BatchRunner, 2 slots in
              flight), pinned host input copied in and logits/values copied
              out inside every pass;
+  e2e_records  the same from position records (stone bytes; the planes are
+             encoded on the device), one synchronous call per pass;
   roofline   the tower convolution kernel: algorithmic FLOPs per launch over
              its average CUDA-event duration, against the measured bf16 peak;
   cpu_baseline  the reference's own CPU engine (blas, one worker per core at
@@ -430,9 +432,9 @@ def run_engine(args, d: Dist):
     conv_launches = 2 * BLOCKS * max(2, min(args.steps, 5))
     conv_avg_ms = d.max(conv_ms / conv_launches)
     conv_tflops = conv_flops_per_position() * BATCH / (conv_avg_ms * 1e-3) / 1e12
-    net.close()
 
     if args.only_device:
+        net.close()
         if d.rank == 0:
             print(json.dumps({"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": d.world,
                               "ms_per_step": ms / args.steps, "conv_avg_ms": conv_avg_ms,
@@ -484,6 +486,29 @@ def run_engine(args, d: Dist):
     runner.close()
     e2e = d.world * BATCH * args.steps / e2e_s
 
+    # --- end to end from position records (the device encoder): one synchronous
+    # CudaInference call per pass, records in and logits/values out every pass
+    stones = np.zeros((BATCH, 1, BOARD * BOARD), np.uint8)
+    to_move = np.where(x[:, 2, 0] == 1.0, 1, 2).astype(np.uint8)
+    for b in range(BATCH):
+        own, opp = (1, 2) if to_move[b] == 1 else (2, 1)
+        stones[b, 0][x[b, 0] == 1.0] = own
+        stones[b, 0][x[b, 1] == 1.0] = opp
+    records = E.stones_records(stones, to_move)
+    for _ in range(args.warmup):
+        net.infer_stones(records)
+    d.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        net.infer_stones(records)
+    rec_s = d.max(time.perf_counter() - t0)
+    e2e_records = {"value": d.world * BATCH * args.steps / rec_s, "unit": UNIT,
+                   "h2d_bytes_per_step": int(records.nbytes) * d.world,
+                   "d2h_bytes_per_step": (BATCH * (BOARD * BOARD + 1) * 4 + BATCH * 4 + 4) * d.world,
+                   "how": "CudaInference from position records (planes encoded on the device), one synchronous "
+                          "call per pass, host wall clock, max over ranks"}
+    net.close()
+
     # --- CPU baseline: the reference's CPU engine on this box's cores (rank 0, N = 1)
     cpu = None
     if d.world == 1 and not args.no_cpu_baseline:
@@ -531,6 +556,7 @@ def run_engine(args, d: Dist):
             "gpu_launches": args.steps * (2 * BLOCKS + 5),   # stem operand + stem GEMM + tower + 3 head launches
             "clocks": clocks,
             "cpu_baseline": cpu,
+            "e2e_records": e2e_records,
         }
         if selfplay is not None:
             line["selfplay"] = selfplay

@@ -132,6 +132,18 @@ void* azb_infer_stream(azb_infer* h);
  * when not null. */
 int azb_infer_time(azb_infer* h, int B, int warmup, int steps, int with_copies, double* ms, double* conv_ms,
                    char* err, size_t err_cap);
+/* Position records for azb_infer_run_stones: per position, stones[H][n*n]
+ * Color bytes (0 empty, 1 Black, 2 White; row k is the position k plies
+ * ago), then toMove (1 Black, 2 White), the number of history positions
+ * present (0..H), the symmetry (0..7, the reference's transformPoint
+ * numbering), and zero padding: azb_stones_record_bytes(H, n) bytes. */
+size_t azb_stones_record_bytes(int history, int board);
+/* CudaInference::infer from position records: the reference's encodePlanes
+ * (src/encode.cpp:15-43) runs on the device, so ~n*n*H bytes per position
+ * cross to it instead of (2H+2)*n*n floats. No reference counterpart (the
+ * reference encodes on the host: src/mcts.cpp:117-132). */
+int azb_infer_run_stones(azb_infer* h, const uint8_t* records, int B, float* logits, float* values, float* ownership,
+                         char* err, size_t err_cap);
 /* Per-stage device time of `steps` passes (CUDA events around every launch,
  * summed over the passes): stage_ms[0..5] = stem operand, stem GEMM, tower
  * convs, head 1x1 convs, head FCs, head finish (value tanh, softmax).

@@ -248,6 +248,17 @@ class RefNetwork:
         return rate, pos.value
 
 
+def ref_encode_records(cfg: NetConfig, records: np.ndarray) -> np.ndarray:
+    """The reference's encodePlanes on position records (see stones_records in the package)."""
+    records = np.ascontiguousarray(records, np.uint8)
+    B = records.shape[0]
+    out = np.zeros((B, cfg.planes, cfg.area), np.float32)
+    L = ref()
+    L.azref_encode_records.argtypes = [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_size_t, C.POINTER(C.c_float)]
+    L.azref_encode_records(cfg.board, cfg.history, B, records.ctypes.data, records.shape[1], _fp(out))
+    return out
+
+
 def ref_positions(cfg: NetConfig, seed: int, B: int, first: int = 0) -> np.ndarray:
     out = np.zeros((B, cfg.planes, cfg.area), np.float32)
     ref().azref_inputs_positions(cfg.board, cfg.history, seed, first, B, _fp(out))

@@ -164,6 +164,20 @@ void azref_inputs_positions(int board, int history, uint64_t seed, long first, i
     }
 }
 
+// The reference's encodePlanes (src/encode.cpp:15-43) on position records:
+// per position, stones[H][A] Color bytes (k plies ago), then toMove (1
+// Black, 2 White), the number of history positions present, the symmetry.
+void azref_encode_records(int board, int history, int B, const uint8_t* records, size_t record_bytes, float* out) {
+    const int A = board * board, P = numPlanes(history);
+    for (int b = 0; b < B; ++b) {
+        const uint8_t* r = records + static_cast<size_t>(b) * record_bytes;
+        const uint8_t* head = r + static_cast<size_t>(history) * A;
+        std::vector<const uint8_t*> stones;
+        for (int k = 0; k < head[1]; ++k) stones.push_back(r + static_cast<size_t>(k) * A);
+        encodePlanes(stones, board, static_cast<Color>(head[0]), history, head[2], out + static_cast<size_t>(b) * P * A);
+    }
+}
+
 void azref_inputs_planes(uint64_t seed, size_t count, float* out) {
     Rng rng(seed);
     for (size_t i = 0; i < count; ++i) out[i] = static_cast<float>(rng.below(2));
