@@ -351,6 +351,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *sm.tmem_slot;
+    // Set-up (barriers, TMEM, batch norm, descriptor prefetch) overlapped the
+    // previous kernel's tail; its activations are read only from here on.
+    grid_dependency_wait();
+    grid_launch_dependents();
 
     if (warp == 0) {
         // ---------------------------------------------------------- producer
@@ -555,6 +559,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     cluster_sync();   // both CTAs' barriers exist before either addresses the other's
     tc_fence_after();
     const uint32_t tmem = *sm.tmem_slot;
+    grid_dependency_wait();   // as in the single-CTA form
+    grid_launch_dependents();
     const int npairs = (p.ntiles + 1) / 2;
     const int pair0 = blockIdx.x >> 1, pair_step = gridDim.x >> 1;
 
@@ -778,7 +784,8 @@ cudaError_t launch_one(const ConvMaps& m, ConvArgs a, bool pair, int sms, cudaSt
         }
         const int pairs = (a.ntiles + 1) / 2;
         const int grid = 2 * std::max(1, std::min(pairs, sms / 2));
-        conv3x3_tc_pair<N, kBf16, kSplit><<<grid, kThreads, smem, s>>>(m.a, m.a_lo, m.w_pair, m.w_lo_pair, m.out, m.skip, a);
+        return launch_pdl(conv3x3_tc_pair<N, kBf16, kSplit>, dim3(grid), dim3(kThreads), smem, s, m.a, m.a_lo, m.w_pair,
+                          m.w_lo_pair, m.out, m.skip, a);
     } else {
         static std::atomic<size_t> configured{0};   // the largest size this instantiation was opened for
         if (smem > configured.load()) {
@@ -788,7 +795,8 @@ cudaError_t launch_one(const ConvMaps& m, ConvArgs a, bool pair, int sms, cudaSt
             configured = smem;
         }
         const int grid = std::max(1, std::min(a.ntiles, sms));
-        conv3x3_tc<N, kBf16, kSplit><<<grid, kThreads, smem, s>>>(m.a, m.a_lo, m.w, m.w_lo, m.out, m.skip, a);
+        return launch_pdl(conv3x3_tc<N, kBf16, kSplit>, dim3(grid), dim3(kThreads), smem, s, m.a, m.a_lo, m.w, m.w_lo,
+                          m.out, m.skip, a);
     }
     return cudaGetLastError();
 }

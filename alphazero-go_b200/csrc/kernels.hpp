@@ -17,6 +17,24 @@
 
 namespace azb {
 
+// Launches `kernel` on `s` with programmatic stream serialization: it may
+// begin while the previous kernel on the stream finishes, and waits for it
+// with grid_dependency_wait (sm100.cuh) before using that kernel's output.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Error codes a kernel leaves in its error word (0: none).
 enum KernelError : int {
     kErrNone = 0,

@@ -30,6 +30,18 @@ __device__ __forceinline__ uint64_t global_timer() {
     return t;
 }
 
+// ------------------------------------------ programmatic dependent launch
+
+// Waits until the kernels this one was launched after (with programmatic
+// stream serialization) have completed and their memory is visible; no-op
+// when there are none. Every kernel of a pass calls it before it touches an
+// activation another kernel wrote or reads.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Lets the next kernel of the stream start launching (its CTAs take SMs as
+// this kernel's free them and run up to their own grid_dependency_wait).
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------------------ mbarrier
 
 // A position in a ring of pipeline stages: the stage and the parity of

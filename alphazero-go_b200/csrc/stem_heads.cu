@@ -39,6 +39,8 @@ __global__ void __launch_bounds__(256) stem_pack_kernel(const StemArgs a) {
     // K (laid out by e so that the lanes, consecutive j, read consecutive
     // words).
     int* table = reinterpret_cast<int*>(planes + size_t(a.P) * A);
+    grid_dependency_wait();
+    grid_launch_dependents();
     for (int i = threadIdx.x; i < W * pieces; i += blockDim.x) {
         const int e = i / pieces, j = i % pieces, k = j * W + e;
         int code = -1;
@@ -106,6 +108,8 @@ __device__ __forceinline__ int transform_point(int sym, int point, int n) {
 }
 
 __global__ void __launch_bounds__(256) encode_planes_kernel(const EncodeArgs a) {
+    grid_dependency_wait();
+    grid_launch_dependents();
     const int A = a.n * a.n, P = 2 * a.H + 2;
     const size_t rec = stones_record_bytes(a.H, a.n);
     for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < size_t(a.B) * A;
@@ -237,6 +241,8 @@ __global__ void __launch_bounds__(kHcThreads, 1)
         fence_barrier_init();
     }
     __syncthreads();
+    grid_dependency_wait();
+    grid_launch_dependents();
 
     if (warp == kHcReaders) {
         // ------------------------------------------------------- copy thread
@@ -379,6 +385,8 @@ __global__ void __launch_bounds__(kHcThreads, 1)
 constexpr int kFcOuts = 4;
 __global__ void __launch_bounds__(kHeadThreads) head_fc_kernel(const HeadArgs a) {
     extern __shared__ float4 xs[];
+    grid_dependency_wait();
+    grid_launch_dependents();
     const int A = a.A, L = A + 1, V = a.V;
     const int outs_per_cta = (kHeadThreads / 32) * kFcOuts;
     const int pol_tiles = (L + outs_per_cta - 1) / outs_per_cta;
@@ -443,6 +451,8 @@ __global__ void __launch_bounds__(kHeadThreads) head_fc_kernel(const HeadArgs a)
 // One warp per board: value = tanh(v2 . hid + b2), and the softmax over the
 // A+1 logits when asked for.
 __global__ void __launch_bounds__(kHeadThreads) head_out_kernel(const HeadArgs a) {
+    grid_dependency_wait();
+    grid_launch_dependents();
     const int lane = threadIdx.x & 31, L = a.A + 1, V = a.V;
     const int b = blockIdx.x * (kHeadThreads / 32) + (threadIdx.x >> 5);
     if (b >= a.B) return;
@@ -503,12 +513,11 @@ cudaError_t launch_stem_pack(const StemArgs& a, int precision, cudaStream_t s) {
     const size_t smem = size_t(a.P) * a.n * a.n * sizeof(float) + size_t(a.ld) * sizeof(int);
     const unsigned grid = static_cast<unsigned>(std::min(a.B, 148 * 8));
     switch (precision) {
-        case kTF32: stem_pack_kernel<kTF32><<<grid, 256, smem, s>>>(a); break;
-        case kTF32x3: stem_pack_kernel<kTF32x3><<<grid, 256, smem, s>>>(a); break;
-        case kBF16: stem_pack_kernel<kBF16><<<grid, 256, smem, s>>>(a); break;
+        case kTF32: return launch_pdl(stem_pack_kernel<kTF32>, dim3(grid), dim3(256), smem, s, a);
+        case kTF32x3: return launch_pdl(stem_pack_kernel<kTF32x3>, dim3(grid), dim3(256), smem, s, a);
+        case kBF16: return launch_pdl(stem_pack_kernel<kBF16>, dim3(grid), dim3(256), smem, s, a);
         default: return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
 
 namespace {
@@ -538,8 +547,8 @@ cudaError_t launch_head_conv_as(const HeadArgs& a, int sms, cudaStream_t s) {
     }
     const int nblk = (a.B * a.n + kbr - 1) / kbr;
     const unsigned grid = static_cast<unsigned>(std::max(1, std::min(nblk, sms)));
-    head_conv_kernel<kMode, kLpr, kNch><<<grid, kHcThreads, smem, s>>>(a, stages, kbr, row_bytes);
-    return cudaGetLastError();
+    return launch_pdl(head_conv_kernel<kMode, kLpr, kNch>, dim3(grid), dim3(kHcThreads), smem, s, a, stages, kbr,
+                      row_bytes);
 }
 
 template <int kMode>
@@ -557,8 +566,7 @@ cudaError_t launch_head_conv_mode(const HeadArgs& a, int sms, cudaStream_t s) {
 
 cudaError_t launch_encode_planes(const EncodeArgs& a, cudaStream_t s) {
     if (a.B <= 0) return cudaSuccess;
-    encode_planes_kernel<<<blocks_for(size_t(a.B) * a.n * a.n, 256), 256, 0, s>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(encode_planes_kernel, dim3(blocks_for(size_t(a.B) * a.n * a.n, 256)), dim3(256), 0, s, a);
 }
 
 cudaError_t launch_head_conv(const HeadArgs& a, int precision, int sms, cudaStream_t s) {
@@ -581,14 +589,13 @@ cudaError_t launch_head_fc(const HeadArgs& a, cudaStream_t s) {
         const cudaError_t e = cudaFuncSetAttribute(head_fc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
         if (e != cudaSuccess) return e;
     }
-    head_fc_kernel<<<grid, kHeadThreads, smem, s>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(head_fc_kernel, grid, dim3(kHeadThreads), smem, s, a);
 }
 
 cudaError_t launch_head_out(const HeadArgs& a, cudaStream_t s) {
     if (a.B <= 0) return cudaSuccess;
-    head_out_kernel<<<(a.B + kHeadThreads / 32 - 1) / (kHeadThreads / 32), kHeadThreads, 0, s>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(head_out_kernel, dim3((a.B + kHeadThreads / 32 - 1) / (kHeadThreads / 32)), dim3(kHeadThreads), 0,
+                      s, a);
 }
 
 cudaError_t launch_fill(float* data, size_t n, float value, cudaStream_t s) {
