@@ -14,8 +14,9 @@
 // the 128-byte swizzle. The accumulator lives in TMEM, double-buffered, so
 // the epilogue of one tile overlaps the MMAs of the next.
 //
-// Warp roles (192 threads): warp 0 issues TMA, warp 1 issues tcgen05.mma,
-// warps 2-5 run the epilogue (TMEM -> registers -> BN, skip, ReLU -> HBM).
+// Warp roles (320 threads): warp 0 issues TMA, warp 1 issues tcgen05.mma,
+// warps 2-9 run the epilogue (TMEM -> registers -> BN, skip, ReLU -> HBM),
+// two warps per TMEM lane quarter, each on half of the columns.
 //
 // Replaces the reference's SIMT gemm_tiled<..., Op::Conv> and
 // launchConvBnRelu (src/cuda/kernels.cu:82-180, 215-224): same epilogue
@@ -32,6 +33,8 @@ namespace azb {
 
 namespace {
 
+constexpr int kEpiWarps = 8;   // epilogue warps per CTA
+
 template <int N, bool kBf16, bool kSplit>
 struct ConvCfg {
     static constexpr int kEsz = kBf16 ? 2 : 4;
@@ -43,15 +46,15 @@ struct ConvCfg {
     static constexpr uint32_t kTmemCols = 2 * N <= 64 ? 64 : (2 * N <= 128 ? 128 : (2 * N <= 256 ? 256 : 512));
     static constexpr uint32_t kIdesc = umma_idesc(N, kBf16);
     // bf16 and plain tf32 store their output (and read their residual input)
-    // through shared memory with TMA: per epilogue warp two output boxes and
-    // two residual boxes of {32 channels, 32 rows} (2 KB bf16, 4 KB fp32);
-    // the split mode's two planes keep direct stores.
+    // through shared memory with TMA, in boxes of {32 channels, 32 rows}: one
+    // output and one residual box per epilogue warp, 2 KB each (bf16) or 4 KB
+    // (fp32). The split mode's two planes keep direct stores.
     static constexpr bool kEpiTma = !kSplit;
-    static constexpr uint32_t kEpiBytes = kEpiTma ? 4u * 4u * (kBf16 ? 2048u : 4096u) : 0u;
+    static constexpr uint32_t kEpiBytes = kEpiTma ? uint32_t(kEpiWarps) * (kBf16 ? 4096u : 8192u) : 0u;
     static_assert(N % 32 == 0 && N >= 32 && N <= 256, "N is a multiple of 32 in [32, 256]");
 };
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 constexpr int kMaxStages = 8;
 constexpr uint32_t kBnBytes = 2 * 256 * 4;   // scale and shift of up to 256 channels
 
@@ -62,7 +65,7 @@ struct Smem {
     uint8_t* epi;   // bf16 epilogue boxes (4 warps x 8 KB), or nothing
     float* bn;      // the folded batch norm: scale[0..N), shift[N..2N)
     uint64_t *a_full, *a_empty, *b_full, *b_empty, *acc_full, *acc_empty, *done;
-    uint64_t* skip_full;   // 4 warps x 2 residual boxes
+    uint64_t* skip_full;   // 8 epilogue warps x 2 residual boxes
     uint32_t* tmem_slot;
 };
 
@@ -83,14 +86,14 @@ __device__ __forceinline__ Smem carve(uint8_t* raw, int sa, int sb, int ops, int
     s.acc_empty = s.acc_full + 2;
     s.done = s.acc_empty + 2;
     s.skip_full = s.done + 1;
-    s.tmem_slot = reinterpret_cast<uint32_t*>(s.skip_full + 8);
+    s.tmem_slot = reinterpret_cast<uint32_t*>(s.skip_full + 2 * kEpiWarps);
     return s;
 }
 
 __host__ __device__ constexpr size_t smem_total(int sa, int sb, int ops, int a_bytes, uint32_t b_bytes,
                                                 uint32_t epi_bytes) {
     return 1024 + size_t(sa) * ops * a_bytes + size_t(sb) * ops * b_bytes + epi_bytes + kBnBytes +
-           (2 * sa + 2 * sb + 13) * 8 + 16;
+           (2 * sa + 2 * sb + 5 + 2 * kEpiWarps) * 8 + 16;
 }
 
 // The nine tap views' start rows inside a halo tile, as descriptor
@@ -107,12 +110,14 @@ __device__ __forceinline__ void tap_offsets(const ConvArgs& p, uint32_t (&off)[9
 // One epilogue thread's accumulator row (TMEM lane of its warp) for a tile:
 // ReLU(scale * acc + shift (+ skip)) with the reference's separate roundings
 // (src/cuda/kernels.cu:172-176), stored as bf16, fp32, or the tf32 high
-// part and exact low remainder. Padding rows (valid false) read TMEM (the
-// load is warp-collective) and store nothing.
+// part and exact low remainder, for the 32-column chunks [c_begin, c_end).
+// Padding rows (valid false) read TMEM (the load is warp-collective) and
+// store nothing.
 template <int N, bool kBf16, bool kSplit>
-__device__ __forceinline__ void store_epilogue(const ConvArgs& p, uint32_t taddr, int q, bool valid) {
+__device__ __forceinline__ void store_epilogue(const ConvArgs& p, uint32_t taddr, int q, bool valid, int c_begin,
+                                               int c_end) {
 #pragma unroll 1
-    for (int c0 = 0; c0 < N; c0 += 32) {
+    for (int c0 = c_begin * 32; c0 < c_end * 32; c0 += 32) {
         uint32_t v[32];
         tmem_ld32(taddr + c0, v);
         tmem_wait_ld();
@@ -213,6 +218,7 @@ template <bool kBf16>
 struct EpiBox {
     static constexpr uint32_t kRowBytes = kBf16 ? 64u : 128u;
     static constexpr uint32_t kBytes = 32u * kRowBytes;
+    static constexpr int kBufs = 1;                        // output (and residual) boxes per warp
     static constexpr int kPieces = int(kRowBytes / 16);   // 16-byte pieces per row
     __device__ static uint32_t piece(int row, int u) {     // byte offset of piece u of `row`
         const uint32_t sw = kBf16 ? uint32_t((row >> 1) & 3) : uint32_t(row & 7);
@@ -220,23 +226,26 @@ struct EpiBox {
     }
 };
 
+// This warp's 32-column chunks [c_begin, c_end) of its 32 rows. With one
+// box per role (kBufs 1, as built) the next chunk's residual is requested as
+// soon as this chunk's has been read, and the output box is refilled once
+// the previous store has read it; with two, one chunk ahead and two behind.
 template <int N, bool kBf16>
 __device__ __forceinline__ void store_epilogue_tma(const ConvArgs& p, const float* bn, const CUtensorMap* omap,
                                                    const CUtensorMap* smap, uint32_t taddr, int row0, bool valid,
-                                                   EpiWarp& ew, int lane) {
+                                                   int c_begin, int c_end, EpiWarp& ew, int lane) {
     using Box = EpiBox<kBf16>;
-    constexpr int kChunks = N / 32;
     constexpr uint32_t kBox = Box::kBytes;
-    if (row0 >= p.rows) return;   // all 32 rows past the frame: nothing to store
+    if (row0 >= p.rows || c_begin >= c_end) return;   // nothing of this warp's to store
     const bool skip = p.skip != nullptr;
     if (skip && lane == 0) {
         mbar_arrive_expect_tx(&ew.sbar[0], kBox);
-        tma_load_2d(smap, ew.sbuf, &ew.sbar[0], 0, row0);
+        tma_load_2d(smap, ew.sbuf, &ew.sbar[0], c_begin * 32, row0);
     }
 #pragma unroll 1
-    for (int c = 0; c < kChunks; ++c) {
-        const int cb = c & 1;
-        if (skip && c + 1 < kChunks && lane == 0) {   // the other box was last read in chunk c-1
+    for (int c = c_begin; c < c_end; ++c) {
+        const int cb = Box::kBufs == 2 ? ((c - c_begin) & 1) : 0;
+        if (Box::kBufs == 2 && skip && c + 1 < c_end && lane == 0) {   // the other box was last read in chunk c-1
             mbar_arrive_expect_tx(&ew.sbar[cb ^ 1], kBox);
             tma_load_2d(smap, ew.sbuf + (cb ^ 1) * kBox, &ew.sbar[cb ^ 1], (c + 1) * 32, row0);
         }
@@ -268,6 +277,13 @@ __device__ __forceinline__ void store_epilogue_tma(const ConvArgs& p, const floa
                     for (int e = 0; e < 4; ++e) y[u * 4 + e] = __fadd_rn(y[u * 4 + e], f[e]);
                 }
             }
+            if (Box::kBufs == 1 && c + 1 < c_end) {   // the box is read: request the next chunk's residual
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&ew.sbar[0], kBox);
+                    tma_load_2d(smap, ew.sbuf, &ew.sbar[0], (c + 1) * 32, row0);
+                }
+            }
         }
         uint4 out[Box::kPieces];
 #pragma unroll
@@ -289,7 +305,11 @@ __device__ __forceinline__ void store_epilogue_tma(const ConvArgs& p, const floa
                 }
             }
         }
-        if (lane == 0) bulk_wait_read<1>();   // the store from this box two chunks ago has read it
+        // The store issued from this box kBufs chunks ago has read it.
+        if (lane == 0) {
+            if constexpr (Box::kBufs == 2) bulk_wait_read<1>();
+            else bulk_wait_read<0>();
+        }
         __syncwarp();
         uint8_t* obox = ew.obuf + cb * kBox;
 #pragma unroll
@@ -324,10 +344,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&sm.acc_full[i], 1);
-            mbar_init(&sm.acc_empty[i], 128);
+            mbar_init(&sm.acc_empty[i], 32 * kEpiWarps);
         }
         mbar_init(sm.done, 1);
-        for (int i = 0; i < 8; ++i) mbar_init(&sm.skip_full[i], 1);
+        for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&sm.skip_full[i], 1);
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
@@ -450,13 +470,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ----------------------------------------------------------- epilogue
-        const int quarter = warp & 3;                 // TMEM lanes this warp may read
+        // Eight warps: warp w reads TMEM lanes 32(w % 4) .. +31 (a warp may
+        // read only its own quarter) and, with the other warp on that
+        // quarter, splits the columns: warps 2-5 the first half, 6-9 the rest.
+        const int e = warp - 2, quarter = warp & 3;
+        constexpr int kChunks = N / 32;
+        const int c_begin = kChunks >= 2 ? (e >> 2) * (kChunks / 2) : (e >> 2) * kChunks;
+        const int c_end = kChunks >= 2 ? c_begin + kChunks / 2 : kChunks;
         const int row_in_tile = quarter * 32 + lane;
         const int n1 = p.n + 1;
         EpiWarp ew;
-        ew.obuf = sm.epi + quarter * (C::kEpiBytes / 4);
-        ew.sbuf = ew.obuf + C::kEpiBytes / 8;
-        ew.sbar = sm.skip_full + 2 * quarter;
+        ew.obuf = sm.epi + e * (C::kEpiBytes / kEpiWarps);
+        ew.sbuf = ew.obuf + C::kEpiBytes / kEpiWarps / 2;
+        ew.sbar = sm.skip_full + 2 * e;
         uint32_t j = 0;
         for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++j) {
             const uint32_t acc = j & 1;
@@ -469,8 +495,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 valid = r >= n1 && (r % n1) != p.n;
             }
             const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + acc * N;
-            if constexpr (C::kEpiTma) store_epilogue_tma<N, kBf16>(p, sm.bn, &mOut, &mSkip, taddr, tile * 128 + quarter * 32, valid, ew, lane);
-            else store_epilogue<N, kBf16, kSplit>(p, taddr, q, valid);
+            if constexpr (C::kEpiTma)
+                store_epilogue_tma<N, kBf16>(p, sm.bn, &mOut, &mSkip, taddr, tile * 128 + quarter * 32, valid, c_begin,
+                                             c_end, ew, lane);
+            else
+                store_epilogue<N, kBf16, kSplit>(p, taddr, q, valid, c_begin, c_end);
             tc_fence_before();
             mbar_arrive(&sm.acc_empty[acc]);
         }
@@ -531,10 +560,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&sm.acc_full[i], 1);
-            mbar_init(&sm.acc_empty[i], 8);   // 4 epilogue warps x 2 CTAs
+            mbar_init(&sm.acc_empty[i], 2 * kEpiWarps);   // every epilogue warp of both CTAs
         }
         mbar_init(sm.done, 1);
-        for (int i = 0; i < 8; ++i) mbar_init(&sm.skip_full[i], 1);
+        for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&sm.skip_full[i], 1);
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
@@ -666,14 +695,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
     } else {
         // ------------------------------------------- epilogue (both CTAs)
-        const int quarter = warp & 3;
+        // Eight warps per CTA, split as in the single-CTA form.
+        const int e = warp - 2, quarter = warp & 3;
+        constexpr int kChunks = N / 32;
+        const int c_begin = kChunks >= 2 ? (e >> 2) * (kChunks / 2) : (e >> 2) * kChunks;
+        const int c_end = kChunks >= 2 ? c_begin + kChunks / 2 : kChunks;
         const int row_in_tile = quarter * 32 + lane;
         const int n1 = p.n + 1;
         const uint32_t leader_empty0 = mapa(smem_u32(&sm.acc_empty[0]), 0), leader_empty1 = leader_empty0 + 8u;
         EpiWarp ew;
-        ew.obuf = sm.epi + quarter * (C::kEpiBytes / 4);
-        ew.sbuf = ew.obuf + C::kEpiBytes / 8;
-        ew.sbar = sm.skip_full + 2 * quarter;
+        ew.obuf = sm.epi + e * (C::kEpiBytes / kEpiWarps);
+        ew.sbuf = ew.obuf + C::kEpiBytes / kEpiWarps / 2;
+        ew.sbar = sm.skip_full + 2 * e;
         uint32_t j = 0;
         for (int pr = pair0; pr < npairs; pr += pair_step, ++j) {
             const uint32_t acc = j & 1;
@@ -687,9 +720,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + acc * N;
             if constexpr (C::kEpiTma)
-                store_epilogue_tma<N, kBf16>(p, sm.bn, &mOut, &mSkip, taddr, (2 * pr + int(rank)) * 128 + quarter * 32, valid, ew, lane);
+                store_epilogue_tma<N, kBf16>(p, sm.bn, &mOut, &mSkip, taddr, (2 * pr + int(rank)) * 128 + quarter * 32,
+                                             valid, c_begin, c_end, ew, lane);
             else
-                store_epilogue<N, kBf16, kSplit>(p, taddr, q, valid);
+                store_epilogue<N, kBf16, kSplit>(p, taddr, q, valid, c_begin, c_end);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(acc ? leader_empty1 : leader_empty0);
@@ -830,7 +864,7 @@ size_t conv_smem_bytes(int n_out, int precision, int halo_rows, int* sa_out, int
     const int ops = precision == kTF32x3 ? 2 : 1;
     const int a_bytes = (halo_rows * 128 + 1023) / 1024 * 1024;
     const uint32_t b_bytes = uint32_t(pair ? n_out / 2 : n_out) * 128u;
-    const uint32_t epi = precision == kBF16 ? 4u * 4u * 2048u : precision == kTF32 ? 4u * 4u * 4096u : 0u;   // kEpiBytes
+    const uint32_t epi = precision == kTF32x3 ? 0u : uint32_t(kEpiWarps) * (precision == kBF16 ? 4096u : 8192u);
     constexpr size_t kMax = 227 * 1024;
     int sa = 2, sb = 2;
     for (int cand = kMaxStages; cand >= 2; --cand)
