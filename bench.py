@@ -564,6 +564,119 @@ def run_engine(args, d: Dist):
     d.close()
 
 
+# ---------------------------------------------------------------- sweep
+
+SWEEP = {   # BASELINE.json configs[0..3]: (board, blocks, filters, value_hidden, batch)
+    "C1": (5, 4, 32, 64, 64), "C2": (9, 6, 64, 128, 256), "C3": (19, 10, 128, 256, 256), "C4": (19, 20, 256, 256, 1024),
+}
+
+
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_sweep(args):
+    """One JSON line per configuration C1..C4: this engine in each precision
+    (device-resident passes timed by CUDA events, and the runner's C ABI with
+    2 slots in flight, host wall clock), the reference's CPU engines (blas
+    and naive, one single-threaded worker per core at batch 8, bounded) and
+    the reference's own CUDA engine rebuilt for sm_100 at the config's batch."""
+    import numpy as np
+
+    import azb200 as E
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    ok, why = E.cuda_available(0)
+    if not ok:
+        raise SystemExit(f"bench: no usable GPU: {why}")
+    cores = len(os.sched_getaffinity(0))
+    for name, (n, blocks, filters, vh, B) in SWEEP.items():
+        desc = E.NetDesc(n, 1, blocks, filters, vh, 0)
+        cfg = O.NetConfig(n, 1, blocks, filters, vh, False)
+        params, buffers = E.synth_network(desc, SEED, 0)
+        x = E.synth_positions(desc, SEED, B)
+        conv_flop = 2.0 * filters * filters * 9 * n * n * B
+        line = {"config": name, "board": n, "blocks": blocks, "filters": filters, "value_hidden": vh, "batch": B,
+                "engine": {}, "host": {"cores": cores, "cpu": cpu_model()}}
+        for pname, prec in (("tf32x3", E.TF32X3), ("tf32", E.TF32), ("bf16", E.BF16)):
+            with E.CudaInference(desc, params, buffers, B, 0, prec) as net:
+                net.stage(x)
+                steps = 50 if B * n * n * filters < 1 << 26 else 10
+                ms, conv_ms = net.time(B, 5, steps, conv=True)
+            runner = E.make_cuda_runner(desc, params, buffers, B, 2, 0, prec)
+            for sl in range(2):
+                runner.input(sl)[:] = x
+            done_q, cv = [], threading.Condition()
+
+            def done(slot, err):
+                with cv:
+                    done_q.append((slot, err))
+                    cv.notify()
+
+            def passes(k):
+                inflight = started = 0
+                for sl in range(min(2, k)):
+                    runner.begin(sl, B, done)
+                    inflight += 1
+                    started += 1
+                while inflight:
+                    with cv:
+                        while not done_q:
+                            cv.wait()
+                        sl, err = done_q.pop(0)
+                    inflight -= 1
+                    if err:
+                        raise RuntimeError(err)
+                    if started < k:
+                        runner.begin(sl, B, done)
+                        inflight += 1
+                        started += 1
+
+            passes(3)
+            t0 = time.perf_counter()
+            passes(steps)
+            run_s = time.perf_counter() - t0
+            runner.close()
+            line["engine"][pname] = {"positions_per_s": B * steps / (ms / 1e3),
+                                     "runner_positions_per_s": B * steps / run_s,
+                                     "conv_tflops": conv_flop / (conv_ms / (steps * 2 * blocks) * 1e-3) / 1e12}
+        ref = {}
+        try:
+            net = O.RefNetwork(cfg, SEED, O.KIND_BENCH)
+            x8 = O.ref_positions(cfg, SEED, 8)
+            backends = ["blas"] if "OpenBLAS" in O.blas_description() else []
+            for be in backends + ["naive"]:
+                if be == "naive" and name == "C4":
+                    rate, pos = net.bench_workers(be, cores, 1, x8[:1], max_calls=1)   # ~10 s per call
+                    sample = f"{cores} workers x 1 call of batch 1"
+                else:
+                    rate, pos = net.bench_workers(be, cores, 8, x8, seconds=4.0)
+                    sample = f"{cores} workers x batch 8, ~4 s"
+                ref[be] = {"positions_per_s": rate, "sample": sample}
+        except Exception as e:
+            ref["error"] = str(e)
+        try:
+            if O.refcuda_built() and O.refcuda_available()[0]:
+                p, b = O.make_network(cfg, SEED, O.KIND_BENCH)
+                xs = O.positions(cfg, SEED, B)
+                with O.RefCudaInference(cfg, p, b, B) as rnet:
+                    steps = 10 if name != "C4" else 2
+                    secs = rnet.time(xs, 1, steps)
+                ref["cuda_sm100"] = {"positions_per_s": B * steps / secs, "dtype": "f32"}
+        except Exception as e:
+            ref["cuda_sm100_error"] = str(e)
+        line["reference"] = ref
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -574,9 +687,14 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-selfplay", action="store_true", help="skip the C5 self-play figures")
     ap.add_argument("--only-device", action="store_true", help="device-resident passes only (for profilers)")
+    ap.add_argument("--sweep", action="store_true",
+                    help="one JSON line per configuration C1..C4: every precision, runner, and the reference's engines")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.sweep:
+        run_sweep(args)
+        return
     if args.impl == "reference":
         # The reference arm is CPU-only: rank 0 runs it, the other ranks exit
         # at once (no process group, so nobody waits on anybody).
