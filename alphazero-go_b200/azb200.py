@@ -467,7 +467,7 @@ class cuda_probe:
 
     @staticmethod
     def set_conv_path(path: int):
-        """0 default (CTA pairs at 256 output channels), 1 single CTA, 2 CTA pairs (M = 256)."""
+        """0 default (by width), 1 one tile per CTA, 2 CTA pairs (M = 256), 3 two tiles per CTA (N <= 128)."""
         lib().azb_probe_set_conv_path(path)
 
     @staticmethod

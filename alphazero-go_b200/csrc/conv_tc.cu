@@ -35,7 +35,7 @@ namespace {
 
 constexpr int kEpiWarps = 8;   // epilogue warps per CTA
 
-template <int N, bool kBf16, bool kSplit>
+template <int N, bool kBf16, bool kSplit, int kTiles = 1>
 struct ConvCfg {
     static constexpr int kEsz = kBf16 ? 2 : 4;
     static constexpr int kKc = 128 / kEsz;          // channels per 128-byte chunk
@@ -43,7 +43,10 @@ struct ConvCfg {
     static constexpr int kSteps = kKc / kKstep;     // MMAs per chunk and tap
     static constexpr int kOps = kSplit ? 2 : 1;     // operand planes per stage
     static constexpr uint32_t kBBytes = uint32_t(N) * 128u;
-    static constexpr uint32_t kTmemCols = 2 * N <= 64 ? 64 : (2 * N <= 128 ? 128 : (2 * N <= 256 ? 256 : 512));
+    // Two accumulators (double buffering) of kTiles tiles x N columns each.
+    static constexpr int kAccCols = 2 * kTiles * N;
+    static constexpr uint32_t kTmemCols = kAccCols <= 64 ? 64 : (kAccCols <= 128 ? 128 : (kAccCols <= 256 ? 256 : 512));
+    static_assert(kAccCols <= 512, "the accumulators fit in TMEM's 512 columns");
     static constexpr uint32_t kIdesc = umma_idesc(N, kBf16);
     // bf16 and plain tf32 store their output (and read their residual input)
     // through shared memory with TMA, in boxes of {32 channels, 32 rows}: one
@@ -69,13 +72,15 @@ struct Smem {
     uint32_t* tmem_slot;
 };
 
-__device__ __forceinline__ Smem carve(uint8_t* raw, int sa, int sb, int ops, int a_bytes, uint32_t b_bytes,
-                                      uint32_t epi_bytes) {
+// a_ops halo buffers per A stage (operand planes x tiles), b_ops weight
+// buffers per B stage (operand planes).
+__device__ __forceinline__ Smem carve(uint8_t* raw, int sa, int sb, int a_ops, int b_ops, int a_bytes,
+                                      uint32_t b_bytes, uint32_t epi_bytes) {
     Smem s;
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
     s.a = base;
-    s.b = base + size_t(sa) * ops * a_bytes;
-    s.epi = s.b + size_t(sb) * ops * b_bytes;
+    s.b = base + size_t(sa) * a_ops * a_bytes;
+    s.epi = s.b + size_t(sb) * b_ops * b_bytes;
     s.bn = reinterpret_cast<float*>(s.epi + epi_bytes);
     uint64_t* bars = reinterpret_cast<uint64_t*>(s.epi + epi_bytes + kBnBytes);
     s.a_full = bars;
@@ -90,9 +95,9 @@ __device__ __forceinline__ Smem carve(uint8_t* raw, int sa, int sb, int ops, int
     return s;
 }
 
-__host__ __device__ constexpr size_t smem_total(int sa, int sb, int ops, int a_bytes, uint32_t b_bytes,
+__host__ __device__ constexpr size_t smem_total(int sa, int sb, int a_ops, int b_ops, int a_bytes, uint32_t b_bytes,
                                                 uint32_t epi_bytes) {
-    return 1024 + size_t(sa) * ops * a_bytes + size_t(sb) * ops * b_bytes + epi_bytes + kBnBytes +
+    return 1024 + size_t(sa) * a_ops * a_bytes + size_t(sb) * b_ops * b_bytes + epi_bytes + kBnBytes +
            (2 * sa + 2 * sb + 5 + 2 * kEpiWarps) * 8 + 16;
 }
 
@@ -323,14 +328,15 @@ __device__ __forceinline__ void store_epilogue_tma(const ConvArgs& p, const floa
     }
 }
 
-template <int N, bool kBf16, bool kSplit>
+template <int N, bool kBf16, bool kSplit, int kTiles>
 __global__ void __launch_bounds__(kThreads, 1)
     conv3x3_tc(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAlo,
                const __grid_constant__ CUtensorMap mW, const __grid_constant__ CUtensorMap mWlo,
                const __grid_constant__ CUtensorMap mOut, const __grid_constant__ CUtensorMap mSkip, const ConvArgs p) {
-    using C = ConvCfg<N, kBf16, kSplit>;
+    using C = ConvCfg<N, kBf16, kSplit, kTiles>;
     extern __shared__ uint8_t smem_raw[];
-    const Smem sm = carve(smem_raw, p.sa, p.sb, C::kOps, p.a_bytes, C::kBBytes, C::kEpiBytes);
+    const Smem sm = carve(smem_raw, p.sa, p.sb, C::kOps * kTiles, C::kOps, p.a_bytes, C::kBBytes, C::kEpiBytes);
+    const int ngroups = (p.ntiles + kTiles - 1) / kTiles;   // a CTA takes kTiles consecutive tiles at a time
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
@@ -381,18 +387,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             Ring ra, rb;
             uint32_t na = 0, nb = 0;   // loads issued, for the drain below
-            const uint32_t a_tx = uint32_t(p.halo_rows) * 128u * C::kOps;
+            const uint32_t a_tx = uint32_t(p.halo_rows) * 128u * C::kOps * kTiles;
             const uint32_t b_tx = C::kBBytes * C::kOps;
-            const size_t a_stage = size_t(C::kOps) * p.a_bytes;
+            const size_t a_stage = size_t(C::kOps) * kTiles * p.a_bytes;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < p.ntiles && ok; tile += gridDim.x) {
-                const int y0 = tile * 128 - (p.n + 2);
+            for (int g = blockIdx.x; g < ngroups && ok; g += gridDim.x) {
                 for (int c = 0; c < p.nchunks && ok; ++c) {
                     if (!(ok = mbar_wait(&sm.a_empty[ra.idx], ra.phase ^ 1u, p.err, kErrWaitProducer))) break;
                     mbar_arrive_expect_tx(&sm.a_full[ra.idx], a_tx);
-                    uint8_t* abuf = sm.a + ra.idx * a_stage;
-                    tma_load_2d(&mA, abuf, &sm.a_full[ra.idx], c * C::kKc, y0);
-                    if (kSplit) tma_load_2d(&mAlo, abuf + p.a_bytes, &sm.a_full[ra.idx], c * C::kKc, y0);
+#pragma unroll
+                    for (int u = 0; u < kTiles; ++u) {   // each tile's own halo (a tile past the frame reads zeros)
+                        const int y0 = (g * kTiles + u) * 128 - (p.n + 2);
+                        uint8_t* abuf = sm.a + ra.idx * a_stage + size_t(u) * C::kOps * p.a_bytes;
+                        tma_load_2d(&mA, abuf, &sm.a_full[ra.idx], c * C::kKc, y0);
+                        if (kSplit) tma_load_2d(&mAlo, abuf + p.a_bytes, &sm.a_full[ra.idx], c * C::kKc, y0);
+                    }
                     ra.next(p.sa);
                     ++na;
                     for (int t = 0; t < p.taps; ++t) {
@@ -428,15 +437,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t j = 0;
             bool ok = true;
             const uint64_t a_desc = sw128_desc(smem_u32(sm.a)), b_desc = sw128_desc(smem_u32(sm.b));
-            const uint32_t a_stage = (uint32_t(C::kOps) * uint32_t(p.a_bytes)) >> 4, a_lo = uint32_t(p.a_bytes) >> 4;
+            const uint32_t a_stage = (uint32_t(C::kOps * kTiles) * uint32_t(p.a_bytes)) >> 4,
+                           a_lo = uint32_t(p.a_bytes) >> 4, a_tile = (uint32_t(C::kOps) * uint32_t(p.a_bytes)) >> 4;
             constexpr uint32_t b_stage = (C::kOps * C::kBBytes) >> 4, b_lo = C::kBBytes >> 4;
             uint32_t toff[9];
             tap_offsets(p, toff);
-            for (int tile = blockIdx.x; tile < p.ntiles && ok; tile += gridDim.x, ++j) {
+            for (int g = blockIdx.x; g < ngroups && ok; g += gridDim.x, ++j) {
                 const uint32_t acc = j & 1;
                 if (!(ok = mbar_wait(&sm.acc_empty[acc], ((j >> 1) & 1) ^ 1, p.err, kErrWaitMma))) break;
                 tc_fence_after();
-                const uint32_t d = tmem + acc * N;
+                const uint32_t d = tmem + acc * (kTiles * N);   // tile u's accumulator at + u * N
                 for (int c = 0; c < p.nchunks && ok; ++c) {
                     if (!(ok = mbar_wait(&sm.a_full[ra.idx], ra.phase, p.err, kErrWaitMma))) break;
                     const uint64_t ac = a_desc + ra.idx * a_stage;
@@ -448,10 +458,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint64_t at = ac + toff[t], bt = b_desc + rb.idx * b_stage;
 #pragma unroll
                         for (int k = 0; k < C::kSteps; ++k) {
-                            umma<kBf16>(d, at + 2 * k, bt + 2 * k, C::kIdesc, (c | t | k) != 0);
-                            if (kSplit) {
-                                umma<kBf16>(d, at + 2 * k, bt + b_lo + 2 * k, C::kIdesc, 1);
-                                umma<kBf16>(d, at + a_lo + 2 * k, bt + 2 * k, C::kIdesc, 1);
+#pragma unroll
+                            for (int u = 0; u < kTiles; ++u) {   // every tile of the group reads this weight tile
+                                const uint32_t du = d + uint32_t(u) * N;
+                                const uint64_t au = at + u * a_tile;
+                                umma<kBf16>(du, au + 2 * k, bt + 2 * k, C::kIdesc, (c | t | k) != 0);
+                                if (kSplit) {
+                                    umma<kBf16>(du, au + 2 * k, bt + b_lo + 2 * k, C::kIdesc, 1);
+                                    umma<kBf16>(du, au + a_lo + 2 * k, bt + 2 * k, C::kIdesc, 1);
+                                }
                             }
                         }
                         umma_commit(&sm.b_empty[rb.idx]);   // frees the weight buffer once read
@@ -471,12 +486,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ----------------------------------------------------------- epilogue
         // Eight warps: warp w reads TMEM lanes 32(w % 4) .. +31 (a warp may
-        // read only its own quarter) and, with the other warp on that
-        // quarter, splits the columns: warps 2-5 the first half, 6-9 the rest.
+        // read only its own quarter). One tile per group: the two warps on a
+        // quarter split the columns (warps 2-5 the first half, 6-9 the
+        // rest). Two tiles: warps 2-5 finish tile 0 and warps 6-9 tile 1.
         const int e = warp - 2, quarter = warp & 3;
         constexpr int kChunks = N / 32;
-        const int c_begin = kChunks >= 2 ? (e >> 2) * (kChunks / 2) : (e >> 2) * kChunks;
-        const int c_end = kChunks >= 2 ? c_begin + kChunks / 2 : kChunks;
+        const int u = kTiles == 2 ? (e >> 2) : 0;
+        const int c_begin = kTiles == 2 ? 0 : (kChunks >= 2 ? (e >> 2) * (kChunks / 2) : (e >> 2) * kChunks);
+        const int c_end = kTiles == 2 ? kChunks : (kChunks >= 2 ? c_begin + kChunks / 2 : kChunks);
         const int row_in_tile = quarter * 32 + lane;
         const int n1 = p.n + 1;
         EpiWarp ew;
@@ -484,21 +501,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         ew.sbuf = ew.obuf + C::kEpiBytes / kEpiWarps / 2;
         ew.sbar = sm.skip_full + 2 * e;
         uint32_t j = 0;
-        for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++j) {
+        for (int g = blockIdx.x; g < ngroups; g += gridDim.x, ++j) {
             const uint32_t acc = j & 1;
             if (!mbar_wait(&sm.acc_full[acc], (j >> 1) & 1, p.err, kErrWaitEpilogue)) break;
             tc_fence_after();
+            const int tile = g * kTiles + u;
             const int q = tile * 128 + row_in_tile;
             bool valid = q < p.rows;
             if (valid) {
                 const int r = q % p.S;
                 valid = r >= n1 && (r % n1) != p.n;
             }
-            const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + acc * N;
+            const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + (acc * kTiles + u) * N;
             if constexpr (C::kEpiTma)
                 store_epilogue_tma<N, kBf16>(p, sm.bn, &mOut, &mSkip, taddr, tile * 128 + quarter * 32, valid, c_begin,
                                              c_end, ew, lane);
-            else
+            else if (tile < p.ntiles)
                 store_epilogue<N, kBf16, kSplit>(p, taddr, q, valid, c_begin, c_end);
             tc_fence_before();
             mbar_arrive(&sm.acc_empty[acc]);
@@ -544,7 +562,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     constexpr uint32_t kHalfB = uint32_t(N / 2) * 128u;     // this CTA's half of a weight tile
     constexpr uint32_t kIdesc = umma_idesc(N, kBf16, 256);
     extern __shared__ uint8_t smem_raw[];
-    const Smem sm = carve(smem_raw, p.sa, p.sb, C::kOps, p.a_bytes, kHalfB, C::kEpiBytes);
+    const Smem sm = carve(smem_raw, p.sa, p.sb, C::kOps, C::kOps, p.a_bytes, kHalfB, C::kEpiBytes);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_rank();
     const bool leader = rank == 0;
@@ -800,15 +818,36 @@ __global__ void __launch_bounds__(128, 1)
     }
 }
 
-std::atomic<int> g_conv_path{0};   // 0: by width, 1: single CTA, 2: CTA pairs
+std::atomic<int> g_conv_path{0};   // 0: by width, 1: one tile per CTA, 2: CTA pairs, 3: two tiles per CTA
+
+// The conv forms: one CTA per 128-row tile, one CTA per two tiles sharing
+// each weight tile (N <= 128: both accumulators fit in TMEM), or 2-CTA pairs.
+enum ConvForm : int { kFormSingle = 1, kFormPair = 2, kFormDual = 3 };
+
+template <int N, bool kBf16, bool kSplit, int kTiles>
+cudaError_t launch_single(const ConvMaps& m, ConvArgs a, int sms, cudaStream_t s) {
+    using C = ConvCfg<N, kBf16, kSplit, kTiles>;
+    conv_smem_bytes(N, kBf16 ? kBF16 : (kSplit ? kTF32x3 : kTF32), a.halo_rows, &a.sa, &a.sb, false, kTiles);
+    const size_t smem = smem_total(a.sa, a.sb, C::kOps * kTiles, C::kOps, a.a_bytes, C::kBBytes, C::kEpiBytes);
+    static std::atomic<size_t> configured{0};   // the largest size this instantiation was opened for
+    if (smem > configured.load()) {
+        const cudaError_t e = cudaFuncSetAttribute(conv3x3_tc<N, kBf16, kSplit, kTiles>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return e;
+        configured = smem;
+    }
+    const int groups = (a.ntiles + kTiles - 1) / kTiles;
+    const int grid = std::max(1, std::min(groups, sms));
+    return launch_pdl(conv3x3_tc<N, kBf16, kSplit, kTiles>, dim3(grid), dim3(kThreads), smem, s, m.a, m.a_lo, m.w,
+                      m.w_lo, m.out, m.skip, a);
+}
 
 template <int N, bool kBf16, bool kSplit>
-cudaError_t launch_one(const ConvMaps& m, ConvArgs a, bool pair, int sms, cudaStream_t s) {
+cudaError_t launch_one(const ConvMaps& m, ConvArgs a, int form, int sms, cudaStream_t s) {
     using C = ConvCfg<N, kBf16, kSplit>;
-    const uint32_t b_bytes = pair ? C::kBBytes / 2 : C::kBBytes;
-    conv_smem_bytes(N, kBf16 ? kBF16 : (kSplit ? kTF32x3 : kTF32), a.halo_rows, &a.sa, &a.sb, pair);
-    const size_t smem = smem_total(a.sa, a.sb, C::kOps, a.a_bytes, b_bytes, C::kEpiBytes);
-    if (pair) {
+    if (form == kFormPair) {
+        conv_smem_bytes(N, kBf16 ? kBF16 : (kSplit ? kTF32x3 : kTF32), a.halo_rows, &a.sa, &a.sb, true, 1);
+        const size_t smem = smem_total(a.sa, a.sb, C::kOps, C::kOps, a.a_bytes, C::kBBytes / 2, C::kEpiBytes);
         static std::atomic<size_t> configured{0};
         if (smem > configured.load()) {
             const cudaError_t e = cudaFuncSetAttribute(conv3x3_tc_pair<N, kBf16, kSplit>,
@@ -820,28 +859,20 @@ cudaError_t launch_one(const ConvMaps& m, ConvArgs a, bool pair, int sms, cudaSt
         const int grid = 2 * std::max(1, std::min(pairs, sms / 2));
         return launch_pdl(conv3x3_tc_pair<N, kBf16, kSplit>, dim3(grid), dim3(kThreads), smem, s, m.a, m.a_lo, m.w_pair,
                           m.w_lo_pair, m.out, m.skip, a);
-    } else {
-        static std::atomic<size_t> configured{0};   // the largest size this instantiation was opened for
-        if (smem > configured.load()) {
-            const cudaError_t e = cudaFuncSetAttribute(conv3x3_tc<N, kBf16, kSplit>,
-                                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-            if (e != cudaSuccess) return e;
-            configured = smem;
-        }
-        const int grid = std::max(1, std::min(a.ntiles, sms));
-        return launch_pdl(conv3x3_tc<N, kBf16, kSplit>, dim3(grid), dim3(kThreads), smem, s, m.a, m.a_lo, m.w, m.w_lo,
-                          m.out, m.skip, a);
     }
-    return cudaGetLastError();
+    if constexpr (N <= 128) {
+        if (form == kFormDual) return launch_single<N, kBf16, kSplit, 2>(m, a, sms, s);
+    }
+    return launch_single<N, kBf16, kSplit, 1>(m, a, sms, s);
 }
 
 template <bool kBf16, bool kSplit>
-cudaError_t dispatch_n(int n_out, const ConvMaps& m, const ConvArgs& a, bool pair, int sms, cudaStream_t s) {
+cudaError_t dispatch_n(int n_out, const ConvMaps& m, const ConvArgs& a, int form, int sms, cudaStream_t s) {
     switch (n_out) {
-        case 32: return launch_one<32, kBf16, kSplit>(m, a, pair, sms, s);
-        case 64: return launch_one<64, kBf16, kSplit>(m, a, pair, sms, s);
-        case 128: return launch_one<128, kBf16, kSplit>(m, a, pair, sms, s);
-        case 256: return launch_one<256, kBf16, kSplit>(m, a, pair, sms, s);
+        case 32: return launch_one<32, kBf16, kSplit>(m, a, form, sms, s);
+        case 64: return launch_one<64, kBf16, kSplit>(m, a, form, sms, s);
+        case 128: return launch_one<128, kBf16, kSplit>(m, a, form, sms, s);
+        case 256: return launch_one<256, kBf16, kSplit>(m, a, form, sms, s);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -860,49 +891,52 @@ cudaError_t probe_one(const ConvMaps& m, int halo_rows, int shift, int k_chunks,
 
 } // namespace
 
-size_t conv_smem_bytes(int n_out, int precision, int halo_rows, int* sa_out, int* sb_out, bool pair) {
-    const int ops = precision == kTF32x3 ? 2 : 1;
+size_t conv_smem_bytes(int n_out, int precision, int halo_rows, int* sa_out, int* sb_out, bool pair, int tiles) {
+    const int ops = precision == kTF32x3 ? 2 : 1, a_ops = ops * tiles;
     const int a_bytes = (halo_rows * 128 + 1023) / 1024 * 1024;
     const uint32_t b_bytes = uint32_t(pair ? n_out / 2 : n_out) * 128u;
     const uint32_t epi = precision == kTF32x3 ? 0u : uint32_t(kEpiWarps) * (precision == kBF16 ? 4096u : 8192u);
     constexpr size_t kMax = 227 * 1024;
     int sa = 2, sb = 2;
     for (int cand = kMaxStages; cand >= 2; --cand)
-        if (smem_total(2, cand, ops, a_bytes, b_bytes, epi) <= kMax) {
+        if (smem_total(2, cand, a_ops, ops, a_bytes, b_bytes, epi) <= kMax) {
             sb = cand;
             break;
         }
-    // A third halo buffer only if it still leaves four weight buffers.
-    if (smem_total(3, std::max(sb - 1, 4), ops, a_bytes, b_bytes, epi) <= kMax && sb >= 5) {
+    // A third halo stage only if it still leaves four weight buffers.
+    if (smem_total(3, std::max(sb - 1, 4), a_ops, ops, a_bytes, b_bytes, epi) <= kMax && sb >= 5) {
         sa = 3;
-        while (sb > 2 && smem_total(sa, sb, ops, a_bytes, b_bytes, epi) > kMax) --sb;
+        while (sb > 2 && smem_total(sa, sb, a_ops, ops, a_bytes, b_bytes, epi) > kMax) --sb;
     }
     if (sa_out) *sa_out = sa;
     if (sb_out) *sb_out = sb;
-    return smem_total(sa, sb, ops, a_bytes, b_bytes, epi);
+    return smem_total(sa, sb, a_ops, ops, a_bytes, b_bytes, epi);
 }
 
 void set_conv_path(int path) { g_conv_path = path; }
 
 // Which form a layer runs: by default the CTA pair for 256 output
 // channels, where a weight tile is 32 KB per tap and halving it per SM
-// pays (C4 bf16 on B200: 1217 against 1148 TFLOP/s per conv), and the
-// single-CTA form for narrower layers, whose weight tiles are small and
-// whose passes have fewer tiles to pair (C3 tf32: 393 against 329).
-bool conv_uses_pairs(int ntiles, int n_out) {
+// pays (C4 bf16 on B200: 1217 against 1148 TFLOP/s per conv), the two-tile
+// form for narrower layers with enough tiles to keep every SM busy (each
+// weight tile then feeds two accumulators), and one tile per CTA otherwise.
+int conv_form(int ntiles, int n_out, int sms) {
     const int path = g_conv_path.load();
-    if (path == 1) return false;
-    if (path == 2) return ntiles >= 1;
-    return n_out == 256 && ntiles >= 2;
+    if (path == kFormSingle) return kFormSingle;
+    if (path == kFormPair) return kFormPair;
+    if (path == kFormDual) return n_out <= 128 ? kFormDual : kFormSingle;
+    if (n_out == 256 && ntiles >= 2) return kFormPair;
+    if (n_out <= 128 && ntiles >= 2 * sms) return kFormDual;
+    return kFormSingle;
 }
 
 cudaError_t launch_conv(const ConvMaps& maps, const ConvArgs& a, int n_out, int precision, int sms, cudaStream_t s) {
     if (a.ntiles <= 0) return cudaSuccess;
-    const bool pair = conv_uses_pairs(a.ntiles, n_out);
+    const int form = conv_form(a.ntiles, n_out, sms);
     switch (precision) {
-        case kTF32: return dispatch_n<false, false>(n_out, maps, a, pair, sms, s);
-        case kTF32x3: return dispatch_n<false, true>(n_out, maps, a, pair, sms, s);
-        case kBF16: return dispatch_n<true, false>(n_out, maps, a, pair, sms, s);
+        case kTF32: return dispatch_n<false, false>(n_out, maps, a, form, sms, s);
+        case kTF32x3: return dispatch_n<false, true>(n_out, maps, a, form, sms, s);
+        case kBF16: return dispatch_n<true, false>(n_out, maps, a, form, sms, s);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -96,13 +96,15 @@ struct ConvMaps {
 
 // Shared memory a conv launch needs, and its pipeline depths (pair: the
 // CTA-pair form, which stages half of each weight tile per CTA).
-size_t conv_smem_bytes(int n_out, int precision, int halo_rows, int* sa, int* sb, bool pair = false);
+size_t conv_smem_bytes(int n_out, int precision, int halo_rows, int* sa, int* sb, bool pair = false, int tiles = 1);
 
-// Enqueues the conv on `s`: the CTA-pair form (2-CTA clusters, M = 256 per
-// MMA) for 256 output channels, else the single-CTA form, unless the test
-// hook selects one; the pipeline depths in `a` are chosen here.
+// Enqueues the conv on `s` in one of three forms: 2-CTA pairs (M = 256 per
+// MMA, tcgen05 cta_group::2) for 256 output channels; for 128 or fewer, two
+// tiles per CTA sharing each weight tile when there are at least two tiles
+// per SM, else one tile per CTA; unless the test hook selects a form. The
+// pipeline depths in `a` are chosen here.
 cudaError_t launch_conv(const ConvMaps& maps, const ConvArgs& a, int n_out, int precision, int sms, cudaStream_t s);
-// Test hook: 0 by width (pairs at 256 output channels), 1 single CTA, 2 CTA pairs.
+// Test hook: 0 by width, 1 one tile per CTA, 2 CTA pairs, 3 two tiles per CTA (N <= 128).
 void set_conv_path(int path);
 
 // The stem's packed operand: the [B][P][A] fp32 input unfolded into frame

@@ -209,8 +209,10 @@ long long azb_probe_passes_completed(void);
 void azb_probe_set_copy_out_delay(int microseconds);
 /* Which tensor-core conv form passes use: 0 the default (CTA pairs, i.e.
  * 2-CTA clusters with M = 256 per MMA via tcgen05 cta_group::2, for layers
- * of 256 output channels; one CTA per 128-row tile otherwise), 1 always one
- * CTA per tile, 2 always CTA pairs. For tests and measurements. */
+ * of 256 output channels; two 128-row tiles per CTA sharing each weight
+ * tile for layers of 128 or fewer with at least two tiles per SM; one tile
+ * per CTA otherwise), 1 always one tile per CTA, 2 always CTA pairs, 3 two
+ * tiles per CTA where N <= 128. For tests and measurements. */
 void azb_probe_set_conv_path(int path);
 /* cuda_probe::binaryVersion / deviceArchitecture / fill (include/azgo/cuda.hpp:93-103). */
 int azb_probe_binary_version(int device);

@@ -22,10 +22,11 @@ pytestmark = pytest.mark.gpu
 SEED = 40
 
 
-@pytest.fixture(params=[1, 2], ids=["single_cta", "cta_pair"])
+@pytest.fixture(params=[1, 2, 3], ids=["single_cta", "cta_pair", "two_tiles"])
 def conv_path(request, engine):
-    """Both tensor-core conv forms: one CTA per 128-row tile (M = 128) and
-    2-CTA clusters (M = 256, tcgen05 cta_group::2)."""
+    """Every tensor-core conv form: one CTA per 128-row tile (M = 128), 2-CTA
+    clusters (M = 256, tcgen05 cta_group::2), and two tiles per CTA sharing
+    each weight tile (N <= 128; wider layers fall back to one tile)."""
     engine.cuda_probe.set_conv_path(request.param)
     yield request.param
     engine.cuda_probe.set_conv_path(0)
@@ -145,12 +146,13 @@ def test_conv_forms_agree_bf16(engine, oracle):
     params, buffers = O.make_network(c, 7, O.KIND_BENCH)
     x = O.positions(c, 7, 64)
     outs = []
-    for path in (1, 2):
+    for path in (1, 2, 3):
         engine.cuda_probe.set_conv_path(path)
         try:
             outs.append(run_gpu(engine, c, params, buffers, x, engine.BF16))
         finally:
             engine.cuda_probe.set_conv_path(0)
-    (l1, v1, _), (l2, v2, _) = outs
-    assert np.max(np.abs(O.softmax(l1) - O.softmax(l2))) <= 2e-2
-    assert np.max(np.abs(v1 - v2)) <= 2e-2
+    (l1, v1, _) = outs[0]
+    for l2, v2, _ in outs[1:]:
+        assert np.max(np.abs(O.softmax(l1) - O.softmax(l2))) <= 2e-2
+        assert np.max(np.abs(v1 - v2)) <= 2e-2
