@@ -920,19 +920,23 @@ void set_conv_path(int path) { g_conv_path = path; }
 // pays (C4 bf16 on B200: 1217 against 1148 TFLOP/s per conv), the two-tile
 // form for narrower layers with enough tiles to keep every SM busy (each
 // weight tile then feeds two accumulators), and one tile per CTA otherwise.
-int conv_form(int ntiles, int n_out, int sms) {
+int conv_form(int ntiles, int n_out, int precision, int halo_rows, int sms) {
+    // The two-tile form stages two halos per stage; it must fit with at
+    // least two weight stages (the split mode at 128 channels does not).
+    const bool dual_fits = n_out <= 128 &&
+                           conv_smem_bytes(n_out, precision, halo_rows, nullptr, nullptr, false, 2) <= 227 * 1024;
     const int path = g_conv_path.load();
     if (path == kFormSingle) return kFormSingle;
     if (path == kFormPair) return kFormPair;
-    if (path == kFormDual) return n_out <= 128 ? kFormDual : kFormSingle;
+    if (path == kFormDual) return dual_fits ? kFormDual : kFormSingle;
     if (n_out == 256 && ntiles >= 2) return kFormPair;
-    if (n_out <= 128 && ntiles >= 2 * sms) return kFormDual;
+    if (dual_fits && ntiles >= 2 * sms) return kFormDual;
     return kFormSingle;
 }
 
 cudaError_t launch_conv(const ConvMaps& maps, const ConvArgs& a, int n_out, int precision, int sms, cudaStream_t s) {
     if (a.ntiles <= 0) return cudaSuccess;
-    const int form = conv_form(a.ntiles, n_out, sms);
+    const int form = conv_form(a.ntiles, n_out, precision, a.halo_rows, sms);
     switch (precision) {
         case kTF32: return dispatch_n<false, false>(n_out, maps, a, form, sms, s);
         case kTF32x3: return dispatch_n<false, true>(n_out, maps, a, form, sms, s);

@@ -156,3 +156,16 @@ def test_conv_forms_agree_bf16(engine, oracle):
     for l2, v2, _ in outs[1:]:
         assert np.max(np.abs(O.softmax(l1) - O.softmax(l2))) <= 2e-2
         assert np.max(np.abs(v1 - v2)) <= 2e-2
+
+
+def test_tf32x3_wide_layers_at_many_tiles(engine, oracle):
+    """128 channels in the split mode at more than two tiles per SM (the two-tile form's shared-memory
+    plan does not fit there, so the default must pick a form that does): parity as everywhere."""
+    O = oracle
+    c = cfg(O, 19, 1, 128, 64)
+    params, buffers = O.make_network(c, 48, O.KIND_TEST)
+    x = O.random_planes(c, 49, 160)   # 160 x 400 frame rows = 500 tiles
+    lr, vr, _ = O.forward(c, params, buffers, x, threads=8)
+    lg, vg, _ = run_gpu(engine, c, params, buffers, x, engine.TF32X3)
+    assert O.max_err(lg, lr) <= 1e-4
+    assert np.max(np.abs(vg - vr)) <= 1e-4
