@@ -112,92 +112,68 @@ __device__ __forceinline__ void tap_offsets(const ConvArgs& p, uint32_t (&off)[9
     }
 }
 
-// One epilogue thread's accumulator row (TMEM lane of its warp) for a tile:
-// ReLU(scale * acc + shift (+ skip)) with the reference's separate roundings
-// (src/cuda/kernels.cu:172-176), stored as bf16, fp32, or the tf32 high
-// part and exact low remainder, for the 32-column chunks [c_begin, c_end).
-// Padding rows (valid false) read TMEM (the load is warp-collective) and
-// store nothing.
-template <int N, bool kBf16, bool kSplit>
-__device__ __forceinline__ void store_epilogue(const ConvArgs& p, uint32_t taddr, int q, bool valid, int c_begin,
-                                               int c_end) {
+// One epilogue thread's accumulator row (TMEM lane of its warp) for a tile in
+// the split mode: ReLU(scale * acc + shift (+ skip)) with the reference's
+// separate roundings (src/cuda/kernels.cu:172-176), stored as the tf32 high
+// part and the exact low remainder, for the 32-column chunks [c_begin,
+// c_end). The row's residual (both planes) is requested before the TMEM load
+// so the two latencies overlap; the folded batch norm comes from shared
+// memory. Padding rows (valid false) read TMEM (the load is warp-collective)
+// and store nothing.
+template <int N>
+__device__ __forceinline__ void store_epilogue_split(const ConvArgs& p, const float* bn, uint32_t taddr, int q,
+                                                     bool valid, int c_begin, int c_end) {
 #pragma unroll 1
     for (int c0 = c_begin * 32; c0 < c_end * 32; c0 += 32) {
+        const size_t off = size_t(q) * p.ld + c0;
+        float4 sk[8];
+        const bool skip = valid && p.skip != nullptr;
+        if (skip) {
+            const float4* hi = reinterpret_cast<const float4*>(static_cast<const float*>(p.skip) + off);
+            const float4* lo = reinterpret_cast<const float4*>(static_cast<const float*>(p.skip_lo) + off);
+            float4 sl[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                sk[u] = hi[u];
+                sl[u] = lo[u];
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                sk[u].x = __fadd_rn(sk[u].x, sl[u].x);
+                sk[u].y = __fadd_rn(sk[u].y, sl[u].y);
+                sk[u].z = __fadd_rn(sk[u].z, sl[u].z);
+                sk[u].w = __fadd_rn(sk[u].w, sl[u].w);
+            }
+        }
         uint32_t v[32];
         tmem_ld32(taddr + c0, v);
         tmem_wait_ld();
         if (!valid) continue;
         float y[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-            y[i] = __fadd_rn(__fmul_rn(__ldg(p.scale + c0 + i), __uint_as_float(v[i])), __ldg(p.shift + c0 + i));
-        const size_t off = size_t(q) * p.ld + c0;
-        if constexpr (kBf16) {
-            if (p.skip) {
-                const uint4* sk = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.skip) + off);
+        for (int i = 0; i < 32; ++i) y[i] = __fadd_rn(__fmul_rn(bn[c0 + i], __uint_as_float(v[i])), bn[N + c0 + i]);
+        if (skip) {
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const uint4 w4 = sk[u];
-                    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&w4);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float2 f = __bfloat1622float2(h2[e]);
-                        y[u * 8 + 2 * e] = __fadd_rn(y[u * 8 + 2 * e], f.x);
-                        y[u * 8 + 2 * e + 1] = __fadd_rn(y[u * 8 + 2 * e + 1], f.y);
-                    }
-                }
+            for (int u = 0; u < 8; ++u) {
+                y[4 * u] = __fadd_rn(y[4 * u], sk[u].x);
+                y[4 * u + 1] = __fadd_rn(y[4 * u + 1], sk[u].y);
+                y[4 * u + 2] = __fadd_rn(y[4 * u + 2], sk[u].z);
+                y[4 * u + 3] = __fadd_rn(y[4 * u + 3], sk[u].w);
             }
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + off);
+        }
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                uint4 w4;
-                __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&w4);
+        for (int i = 0; i < 32; ++i) y[i] = y[i] > 0.0f ? y[i] : 0.0f;
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + off);
+        float4* dlo = reinterpret_cast<float4*>(static_cast<float*>(p.out_lo) + off);
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float a0 = y[u * 8 + 2 * e], a1 = y[u * 8 + 2 * e + 1];
-                    h2[e] = __floats2bfloat162_rn(a0 > 0.0f ? a0 : 0.0f, a1 > 0.0f ? a1 : 0.0f);
-                }
-                dst[u] = w4;
-            }
-        } else {
-            if (p.skip) {
-                const float4* sk = reinterpret_cast<const float4*>(static_cast<const float*>(p.skip) + off);
-                const float4* skl = kSplit ? reinterpret_cast<const float4*>(static_cast<const float*>(p.skip_lo) + off) : nullptr;
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    float4 s4 = sk[u];
-                    if (kSplit) {
-                        const float4 l4 = skl[u];
-                        s4.x = __fadd_rn(s4.x, l4.x);
-                        s4.y = __fadd_rn(s4.y, l4.y);
-                        s4.z = __fadd_rn(s4.z, l4.z);
-                        s4.w = __fadd_rn(s4.w, l4.w);
-                    }
-                    y[4 * u] = __fadd_rn(y[4 * u], s4.x);
-                    y[4 * u + 1] = __fadd_rn(y[4 * u + 1], s4.y);
-                    y[4 * u + 2] = __fadd_rn(y[4 * u + 2], s4.z);
-                    y[4 * u + 3] = __fadd_rn(y[4 * u + 3], s4.w);
-                }
-            }
-#pragma unroll
-            for (int i = 0; i < 32; ++i) y[i] = y[i] > 0.0f ? y[i] : 0.0f;
-            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + off);
-            if constexpr (kSplit) {
-                float4* dlo = reinterpret_cast<float4*>(static_cast<float*>(p.out_lo) + off);
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    float4 h, l;
-                    h.x = to_tf32(y[4 * u]);     l.x = __fsub_rn(y[4 * u], h.x);
-                    h.y = to_tf32(y[4 * u + 1]); l.y = __fsub_rn(y[4 * u + 1], h.y);
-                    h.z = to_tf32(y[4 * u + 2]); l.z = __fsub_rn(y[4 * u + 2], h.z);
-                    h.w = to_tf32(y[4 * u + 3]); l.w = __fsub_rn(y[4 * u + 3], h.w);
-                    dst[u] = h;
-                    dlo[u] = l;
-                }
-            } else {
-#pragma unroll
-                for (int u = 0; u < 8; ++u) dst[u] = make_float4(y[4 * u], y[4 * u + 1], y[4 * u + 2], y[4 * u + 3]);
-            }
+        for (int u = 0; u < 8; ++u) {
+            float4 h, l;
+            h.x = to_tf32(y[4 * u]);     l.x = __fsub_rn(y[4 * u], h.x);
+            h.y = to_tf32(y[4 * u + 1]); l.y = __fsub_rn(y[4 * u + 1], h.y);
+            h.z = to_tf32(y[4 * u + 2]); l.z = __fsub_rn(y[4 * u + 2], h.z);
+            h.w = to_tf32(y[4 * u + 3]); l.w = __fsub_rn(y[4 * u + 3], h.w);
+            dst[u] = h;
+            dlo[u] = l;
         }
     }
 }
@@ -517,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 store_epilogue_tma<N, kBf16>(p, sm.bn, &mOut, &mSkip, taddr, tile * 128 + quarter * 32, valid, c_begin,
                                              c_end, ew, lane);
             else if (tile < p.ntiles)
-                store_epilogue<N, kBf16, kSplit>(p, taddr, q, valid, c_begin, c_end);
+                store_epilogue_split<N>(p, sm.bn, taddr, q, valid, c_begin, c_end);
             tc_fence_before();
             mbar_arrive(&sm.acc_empty[acc]);
         }
@@ -741,7 +717,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 store_epilogue_tma<N, kBf16>(p, sm.bn, &mOut, &mSkip, taddr, (2 * pr + int(rank)) * 128 + quarter * 32,
                                              valid, c_begin, c_end, ew, lane);
             else
-                store_epilogue<N, kBf16, kSplit>(p, taddr, q, valid, c_begin, c_end);
+                store_epilogue_split<N>(p, sm.bn, taddr, q, valid, c_begin, c_end);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(acc ? leader_empty1 : leader_empty0);

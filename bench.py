@@ -581,6 +581,23 @@ def cpu_model() -> str:
     return "unknown"
 
 
+def run_profile_case(args):
+    """Device-resident passes of one configuration and precision, for ncu:
+    `--profile-case C2:tf32x3` runs W + K passes of C2 at its batch."""
+    import azb200 as E
+
+    name, _, pname = args.profile_case.partition(":")
+    n, blocks, filters, vh, B = SWEEP[name]
+    prec = {"tf32x3": E.TF32X3, "tf32": E.TF32, "bf16": E.BF16}[pname or "bf16"]
+    desc = E.NetDesc(n, 1, blocks, filters, vh, 0)
+    params, buffers = E.synth_network(desc, SEED, 0)
+    with E.CudaInference(desc, params, buffers, B, 0, prec) as net:
+        net.stage(E.synth_positions(desc, SEED, B))
+        ms, _ = net.time(B, args.warmup, args.steps)
+    print(json.dumps({"case": args.profile_case, "batch": B, "ms_per_pass": ms / args.steps,
+                      "positions_per_s": B * args.steps / (ms / 1e3)}))
+
+
 def run_sweep(args):
     """One JSON line per configuration C1..C4: this engine in each precision
     (device-resident passes timed by CUDA events, and the runner's C ABI with
@@ -687,6 +704,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-selfplay", action="store_true", help="skip the C5 self-play figures")
     ap.add_argument("--only-device", action="store_true", help="device-resident passes only (for profilers)")
+    ap.add_argument("--profile-case", default=None, help="CONFIG:PRECISION, e.g. C2:tf32x3: device passes only, for ncu")
     ap.add_argument("--sweep", action="store_true",
                     help="one JSON line per configuration C1..C4: every precision, runner, and the reference's engines")
     args = ap.parse_args()
@@ -694,6 +712,9 @@ def main():
         args.warmup = 3
     if args.sweep:
         run_sweep(args)
+        return
+    if args.profile_case:
+        run_profile_case(args)
         return
     if args.impl == "reference":
         # The reference arm is CPU-only: rank 0 runs it, the other ranks exit
