@@ -43,11 +43,20 @@ struct ConvCfg {
     static constexpr int kSteps = kKc / kKstep;     // MMAs per chunk and tap
     static constexpr int kOps = kSplit ? 2 : 1;     // operand planes per stage
     static constexpr uint32_t kBBytes = uint32_t(N) * 128u;
-    // Two accumulators (double buffering) of kTiles tiles x N columns each.
-    static constexpr int kAccCols = 2 * kTiles * N;
+    // The split mode at N <= 128 stacks the weight tile's two planes into one
+    // N' = 2N operand (they are adjacent in shared memory): one MMA computes
+    // a_hi.b_hi into columns [0, N) and a_hi.b_lo into [N, 2N), a second adds
+    // a_lo.b_hi into [0, N); the epilogue adds the halves. Two instructions
+    // per K step instead of three, for narrow layers whose MMAs are too
+    // short for one thread to issue three back to back.
+    static constexpr bool kStack = kSplit && N <= 128 && 2 * kTiles * 2 * N <= 512;
+    static constexpr int kTileCols = kStack ? 2 * N : N;   // TMEM columns of one tile's accumulator
+    // Two accumulators (double buffering) of kTiles tiles each.
+    static constexpr int kAccCols = 2 * kTiles * kTileCols;
     static constexpr uint32_t kTmemCols = kAccCols <= 64 ? 64 : (kAccCols <= 128 ? 128 : (kAccCols <= 256 ? 256 : 512));
     static_assert(kAccCols <= 512, "the accumulators fit in TMEM's 512 columns");
     static constexpr uint32_t kIdesc = umma_idesc(N, kBf16);
+    static constexpr uint32_t kIdescStack = umma_idesc(kStack ? 2 * N : N, kBf16);
     // bf16 and plain tf32 store their output (and read their residual input)
     // through shared memory with TMA, in boxes of {32 channels, 32 rows}: one
     // output and one residual box per epilogue warp, 2 KB each (bf16) or 4 KB
@@ -120,7 +129,7 @@ __device__ __forceinline__ void tap_offsets(const ConvArgs& p, uint32_t (&off)[9
 // so the two latencies overlap; the folded batch norm comes from shared
 // memory. Padding rows (valid false) read TMEM (the load is warp-collective)
 // and store nothing.
-template <int N>
+template <int N, bool kStack>
 __device__ __forceinline__ void store_epilogue_split(const ConvArgs& p, const float* bn, uint32_t taddr, int q,
                                                      bool valid, int c_begin, int c_end) {
 #pragma unroll 1
@@ -145,13 +154,17 @@ __device__ __forceinline__ void store_epilogue_split(const ConvArgs& p, const fl
                 sk[u].w = __fadd_rn(sk[u].w, sl[u].w);
             }
         }
-        uint32_t v[32];
+        uint32_t v[32], w[32];
         tmem_ld32(taddr + c0, v);
+        if (kStack) tmem_ld32(taddr + N + c0, w);   // the a_hi.b_lo half of a stacked accumulator
         tmem_wait_ld();
         if (!valid) continue;
         float y[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) y[i] = __fadd_rn(__fmul_rn(bn[c0 + i], __uint_as_float(v[i])), bn[N + c0 + i]);
+        for (int i = 0; i < 32; ++i) {
+            const float acc = kStack ? __fadd_rn(__uint_as_float(v[i]), __uint_as_float(w[i])) : __uint_as_float(v[i]);
+            y[i] = __fadd_rn(__fmul_rn(bn[c0 + i], acc), bn[N + c0 + i]);
+        }
         if (skip) {
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
@@ -422,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t acc = j & 1;
                 if (!(ok = mbar_wait(&sm.acc_empty[acc], ((j >> 1) & 1) ^ 1, p.err, kErrWaitMma))) break;
                 tc_fence_after();
-                const uint32_t d = tmem + acc * (kTiles * N);   // tile u's accumulator at + u * N
+                const uint32_t d = tmem + acc * (kTiles * C::kTileCols);   // tile u's at + u * kTileCols
                 for (int c = 0; c < p.nchunks && ok; ++c) {
                     if (!(ok = mbar_wait(&sm.a_full[ra.idx], ra.phase, p.err, kErrWaitMma))) break;
                     const uint64_t ac = a_desc + ra.idx * a_stage;
@@ -436,12 +449,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int k = 0; k < C::kSteps; ++k) {
 #pragma unroll
                             for (int u = 0; u < kTiles; ++u) {   // every tile of the group reads this weight tile
-                                const uint32_t du = d + uint32_t(u) * N;
+                                const uint32_t du = d + uint32_t(u) * C::kTileCols;
                                 const uint64_t au = at + u * a_tile;
-                                umma<kBf16>(du, au + 2 * k, bt + 2 * k, C::kIdesc, (c | t | k) != 0);
-                                if (kSplit) {
-                                    umma<kBf16>(du, au + 2 * k, bt + b_lo + 2 * k, C::kIdesc, 1);
+                                if constexpr (C::kStack) {   // [hi | lo] weight planes as one operand
+                                    umma<kBf16>(du, au + 2 * k, bt + 2 * k, C::kIdescStack, (c | t | k) != 0);
                                     umma<kBf16>(du, au + a_lo + 2 * k, bt + 2 * k, C::kIdesc, 1);
+                                } else {
+                                    umma<kBf16>(du, au + 2 * k, bt + 2 * k, C::kIdesc, (c | t | k) != 0);
+                                    if (kSplit) {
+                                        umma<kBf16>(du, au + 2 * k, bt + b_lo + 2 * k, C::kIdesc, 1);
+                                        umma<kBf16>(du, au + a_lo + 2 * k, bt + 2 * k, C::kIdesc, 1);
+                                    }
                                 }
                             }
                         }
@@ -488,12 +506,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int r = q % p.S;
                 valid = r >= n1 && (r % n1) != p.n;
             }
-            const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + (acc * kTiles + u) * N;
+            const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + (acc * kTiles + u) * C::kTileCols;
             if constexpr (C::kEpiTma)
                 store_epilogue_tma<N, kBf16>(p, sm.bn, &mOut, &mSkip, taddr, tile * 128 + quarter * 32, valid, c_begin,
                                              c_end, ew, lane);
             else if (tile < p.ntiles)
-                store_epilogue_split<N>(p, sm.bn, taddr, q, valid, c_begin, c_end);
+                store_epilogue_split<N, C::kStack>(p, sm.bn, taddr, q, valid, c_begin, c_end);
             tc_fence_before();
             mbar_arrive(&sm.acc_empty[acc]);
         }
@@ -717,7 +735,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 store_epilogue_tma<N, kBf16>(p, sm.bn, &mOut, &mSkip, taddr, (2 * pr + int(rank)) * 128 + quarter * 32,
                                              valid, c_begin, c_end, ew, lane);
             else
-                store_epilogue_split<N>(p, sm.bn, taddr, q, valid, c_begin, c_end);
+                store_epilogue_split<N, false>(p, sm.bn, taddr, q, valid, c_begin, c_end);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(acc ? leader_empty1 : leader_empty0);
