@@ -114,9 +114,11 @@ def lib() -> C.CDLL:
             L.azb_probe_passes_completed.restype = C.c_longlong
             L.azb_probe_set_copy_out_delay.argtypes = [C.c_int]
             L.azb_probe_set_conv_path.argtypes = [C.c_int]
+            L.azb_probe_set_conv_segment.argtypes = [C.c_int]
             L.azb_probe_binary_version.argtypes = [C.c_int]
             L.azb_probe_device_architecture.argtypes = [C.c_int]
             L.azb_probe_fill.argtypes = [C.c_int, _F, s, C.c_float, s] + err
+            L.azb_probe_tanh.argtypes = [C.c_int, _F, s] + err
             L.azb_probe_bounded_wait.argtypes = [C.c_int, C.c_ulonglong] + err
             L.azb_probe_umma.argtypes = [C.c_int] * 7 + [_F, _F, _F] + err
             L.azb_synth_network.argtypes = [D, C.c_uint64, C.c_int, _F, _F]
@@ -471,6 +473,11 @@ class cuda_probe:
         lib().azb_probe_set_conv_path(path)
 
     @staticmethod
+    def set_conv_segment(steps: int):
+        """tf32x3 (<= 128 channels): -1 default (accumulation segments of 3 taps, 9 at <= 64 channels), 0 one run per tile."""
+        lib().azb_probe_set_conv_segment(steps)
+
+    @staticmethod
     def binary_version(device: int = 0) -> int:
         return lib().azb_probe_binary_version(device)
 
@@ -483,6 +490,15 @@ class cuda_probe:
         e = _err()
         if lib().azb_probe_fill(device, _fp(data), n, value, tail, e, 1024) != 0:
             raise CudaError(e.value.decode())
+
+    @staticmethod
+    def tanh(x: np.ndarray, device: int = 0) -> np.ndarray:
+        """cuda_probe::tanhInPlace: tanhf on the device, as the heads compute the value and ownership."""
+        y = np.ascontiguousarray(x, np.float32).copy()
+        e = _err()
+        if lib().azb_probe_tanh(device, _fp(y), y.size, e, 1024) != 0:
+            raise CudaError(e.value.decode())
+        return y
 
     @staticmethod
     def bounded_wait(limit_ns: int, device: int = 0) -> int:

@@ -23,6 +23,7 @@ FLAGS = [
     "-O3", "-std=c++17", "-lineinfo", "-shared",
     "-Xcompiler", "-fPIC,-ffp-contract=off,-Wall",
     "--cudart", "static",
+    "-Xlinker", "-z,defs",   # an unresolved symbol fails the build, not the first load
     "-ccbin", "g++",
 ]
 

@@ -230,6 +230,7 @@ void azb_probe_set_memory_limit(size_t bytes) { hooks().memory_limit = bytes; }
 long long azb_probe_passes_completed(void) { return hooks().passes_completed.load(); }
 void azb_probe_set_copy_out_delay(int us) { hooks().copy_out_delay_us = us > 0 ? us : 0; }
 void azb_probe_set_conv_path(int path) { set_conv_path(path); }
+void azb_probe_set_conv_segment(int steps) { set_conv_segment(steps); }
 
 int azb_probe_binary_version(int device) { return device_info(device).binary_version; }
 int azb_probe_device_architecture(int device) { return device_info(device).architecture; }
@@ -244,6 +245,20 @@ int azb_probe_fill(int device, float* data, size_t n, float value, size_t tail, 
         if (e == cudaSuccess) e = cudaMemcpy(data, d, (n + tail) * sizeof(float), cudaMemcpyDeviceToHost);
         cudaFree(d);
         check(e, "fill");
+    });
+}
+
+int azb_probe_tanh(int device, float* data, size_t n, char* err, size_t err_cap) {
+    return guarded(err, err_cap, "", [&] {
+        require_device(device);
+        if (n == 0) return;
+        float* d = nullptr;
+        check(cudaMalloc(&d, n * sizeof(float)), "cudaMalloc");
+        cudaError_t e = cudaMemcpy(d, data, n * sizeof(float), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = launch_tanh(d, n, nullptr);
+        if (e == cudaSuccess) e = cudaMemcpy(data, d, n * sizeof(float), cudaMemcpyDeviceToHost);
+        cudaFree(d);
+        check(e, "tanh");
     });
 }
 

@@ -46,9 +46,10 @@ struct ConvCfg {
     // The split mode at N <= 128 stacks the weight tile's two planes into one
     // N' = 2N operand (they are adjacent in shared memory): one MMA computes
     // a_hi.b_hi into columns [0, N) and a_hi.b_lo into [N, 2N), a second adds
-    // a_lo.b_hi into [0, N); the epilogue adds the halves. Two instructions
+    // a_lo.b_hi into [N, 2N); the epilogue adds the halves. Two instructions
     // per K step instead of three, for narrow layers whose MMAs are too
-    // short for one thread to issue three back to back.
+    // short for one thread to issue three back to back; and the large
+    // products accumulate alone, in segments (kSeg).
     static constexpr bool kStack = kSplit && N <= 128 && 2 * kTiles * 2 * N <= 512;
     static constexpr int kTileCols = kStack ? 2 * N : N;   // TMEM columns of one tile's accumulator
     // Two accumulators (double buffering) of kTiles tiles each.
@@ -56,13 +57,15 @@ struct ConvCfg {
     static constexpr uint32_t kTmemCols = kAccCols <= 64 ? 64 : (kAccCols <= 128 ? 128 : (kAccCols <= 256 ? 256 : 512));
     static_assert(kAccCols <= 512, "the accumulators fit in TMEM's 512 columns");
     static constexpr uint32_t kIdesc = umma_idesc(N, kBf16);
-    static constexpr uint32_t kIdescStack = umma_idesc(kStack ? 2 * N : N, kBf16);
     // bf16 and plain tf32 store their output (and read their residual input)
     // through shared memory with TMA, in boxes of {32 channels, 32 rows}: one
     // output and one residual box per epilogue warp, 2 KB each (bf16) or 4 KB
-    // (fp32). The split mode's two planes keep direct stores.
+    // (fp32). The stacked split mode stores its two planes through one 4 KB
+    // box per warp (the residual read directly); the unstacked one stores
+    // directly.
     static constexpr bool kEpiTma = !kSplit;
-    static constexpr uint32_t kEpiBytes = kEpiTma ? uint32_t(kEpiWarps) * (kBf16 ? 4096u : 8192u) : 0u;
+    static constexpr uint32_t kEpiBytes =
+        kEpiTma ? uint32_t(kEpiWarps) * (kBf16 ? 4096u : 8192u) : (kStack ? uint32_t(kEpiWarps) * 4096u : 0u);
     static_assert(N % 32 == 0 && N >= 32 && N <= 256, "N is a multiple of 32 in [32, 256]");
 };
 
@@ -121,73 +124,97 @@ __device__ __forceinline__ void tap_offsets(const ConvArgs& p, uint32_t (&off)[9
     }
 }
 
+// One output element of the split mode from its accumulated sum:
+// ReLU(scale * acc + shift (+ skip)) with the reference's separate roundings
+// (src/cuda/kernels.cu:172-176), the skip given as its two planes.
+__device__ __forceinline__ float split_out(float acc, float scale, float shift, bool skip, float s_hi, float s_lo) {
+    float y = __fadd_rn(__fmul_rn(scale, acc), shift);
+    if (skip) y = __fadd_rn(y, __fadd_rn(s_hi, s_lo));
+    return y > 0.0f ? y : 0.0f;
+}
+
+// Stores 32 consecutive channels of one row as the tf32 high part (cvt.rna)
+// and the exact low remainder.
+__device__ __forceinline__ void store_split_planes(float* hi_dst, float* lo_dst, const float (&y)[32]) {
+    float4* dst = reinterpret_cast<float4*>(hi_dst);
+    float4* dlo = reinterpret_cast<float4*>(lo_dst);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+        float4 h, l;
+        h.x = to_tf32(y[4 * u]);     l.x = __fsub_rn(y[4 * u], h.x);
+        h.y = to_tf32(y[4 * u + 1]); l.y = __fsub_rn(y[4 * u + 1], h.y);
+        h.z = to_tf32(y[4 * u + 2]); l.z = __fsub_rn(y[4 * u + 2], h.z);
+        h.w = to_tf32(y[4 * u + 3]); l.w = __fsub_rn(y[4 * u + 3], h.w);
+        dst[u] = h;
+        dlo[u] = l;
+    }
+}
+
+// The stacked split mode accumulates a tile in segments (tcgen05's fp32
+// accumulation rounds toward zero at every MMA, so a long run on one
+// accumulator drifts toward zero; short runs summed in round-to-nearest
+// keep the sum within a few fp32 roundings). An epilogue thread adds one
+// segment's two halves ([0, N) the large products, [N, 2N) the small ones)
+// of its row's kMine 32-column chunks from c_begin into its running sums.
+template <int N, int kMine>
+__device__ __forceinline__ void add_segment(uint32_t taddr, int c_begin, float (&sum)[kMine * 32], bool first) {
+#pragma unroll
+    for (int cc = 0; cc < kMine; ++cc) {
+        uint32_t v[32], w[32];
+        tmem_ld32(taddr + uint32_t(c_begin + cc) * 32u, v);
+        tmem_ld32(taddr + uint32_t(N + (c_begin + cc) * 32), w);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {   // paired: half the instructions on this SM's issue slots
+            const float2 part = fadd2_rn(make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])),
+                                         make_float2(__uint_as_float(w[i]), __uint_as_float(w[i + 1])));
+            const float2 s2 = first ? part : fadd2_rn(make_float2(sum[cc * 32 + i], sum[cc * 32 + i + 1]), part);
+            sum[cc * 32 + i] = s2.x;
+            sum[cc * 32 + i + 1] = s2.y;
+        }
+    }
+}
+
 // One epilogue thread's accumulator row (TMEM lane of its warp) for a tile in
-// the split mode: ReLU(scale * acc + shift (+ skip)) with the reference's
-// separate roundings (src/cuda/kernels.cu:172-176), stored as the tf32 high
-// part and the exact low remainder, for the 32-column chunks [c_begin,
-// c_end). The row's residual (both planes) is requested before the TMEM load
-// so the two latencies overlap; the folded batch norm comes from shared
-// memory. Padding rows (valid false) read TMEM (the load is warp-collective)
-// and store nothing.
-template <int N, bool kStack>
+// the unstacked split mode (one accumulator run per tile), for the 32-column
+// chunks [c_begin, c_end). The row's residual (both planes) is requested
+// before the TMEM load so the two latencies overlap; the folded batch norm
+// comes from shared memory. Padding rows (valid false) read TMEM (the load is
+// warp-collective) and store nothing.
+template <int N>
 __device__ __forceinline__ void store_epilogue_split(const ConvArgs& p, const float* bn, uint32_t taddr, int q,
                                                      bool valid, int c_begin, int c_end) {
 #pragma unroll 1
     for (int c0 = c_begin * 32; c0 < c_end * 32; c0 += 32) {
         const size_t off = size_t(q) * p.ld + c0;
-        float4 sk[8];
+        float4 sk[8], sl[8];
         const bool skip = valid && p.skip != nullptr;
         if (skip) {
             const float4* hi = reinterpret_cast<const float4*>(static_cast<const float*>(p.skip) + off);
             const float4* lo = reinterpret_cast<const float4*>(static_cast<const float*>(p.skip_lo) + off);
-            float4 sl[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
                 sk[u] = hi[u];
                 sl[u] = lo[u];
             }
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                sk[u].x = __fadd_rn(sk[u].x, sl[u].x);
-                sk[u].y = __fadd_rn(sk[u].y, sl[u].y);
-                sk[u].z = __fadd_rn(sk[u].z, sl[u].z);
-                sk[u].w = __fadd_rn(sk[u].w, sl[u].w);
-            }
         }
-        uint32_t v[32], w[32];
+        uint32_t v[32];
         tmem_ld32(taddr + c0, v);
-        if (kStack) tmem_ld32(taddr + N + c0, w);   // the a_hi.b_lo half of a stacked accumulator
         tmem_wait_ld();
         if (!valid) continue;
         float y[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            const float acc = kStack ? __fadd_rn(__uint_as_float(v[i]), __uint_as_float(w[i])) : __uint_as_float(v[i]);
-            y[i] = __fadd_rn(__fmul_rn(bn[c0 + i], acc), bn[N + c0 + i]);
-        }
-        if (skip) {
+        for (int u = 0; u < 8; ++u) {
+            const float* h = &sk[u].x;
+            const float* l = &sl[u].x;
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                y[4 * u] = __fadd_rn(y[4 * u], sk[u].x);
-                y[4 * u + 1] = __fadd_rn(y[4 * u + 1], sk[u].y);
-                y[4 * u + 2] = __fadd_rn(y[4 * u + 2], sk[u].z);
-                y[4 * u + 3] = __fadd_rn(y[4 * u + 3], sk[u].w);
+            for (int e = 0; e < 4; ++e) {
+                const int i = 4 * u + e;
+                y[i] = split_out(__uint_as_float(v[i]), bn[c0 + i], bn[N + c0 + i], skip, skip ? h[e] : 0.0f,
+                                 skip ? l[e] : 0.0f);
             }
         }
-#pragma unroll
-        for (int i = 0; i < 32; ++i) y[i] = y[i] > 0.0f ? y[i] : 0.0f;
-        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + off);
-        float4* dlo = reinterpret_cast<float4*>(static_cast<float*>(p.out_lo) + off);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            float4 h, l;
-            h.x = to_tf32(y[4 * u]);     l.x = __fsub_rn(y[4 * u], h.x);
-            h.y = to_tf32(y[4 * u + 1]); l.y = __fsub_rn(y[4 * u + 1], h.y);
-            h.z = to_tf32(y[4 * u + 2]); l.z = __fsub_rn(y[4 * u + 2], h.z);
-            h.w = to_tf32(y[4 * u + 3]); l.w = __fsub_rn(y[4 * u + 3], h.w);
-            dst[u] = h;
-            dlo[u] = l;
-        }
+        store_split_planes(static_cast<float*>(p.out) + off, static_cast<float*>(p.out_lo) + off, y);
     }
 }
 
@@ -317,7 +344,78 @@ __device__ __forceinline__ void store_epilogue_tma(const ConvArgs& p, const floa
     }
 }
 
-template <int N, bool kBf16, bool kSplit, int kTiles>
+// The stacked split mode's store from the running sums (this thread's row
+// q, chunks [c_begin, c_begin + kMine)) through shared memory and TMA: per
+// 32-channel chunk the warp writes the high plane into its 4 KB box (32 rows
+// x 128 bytes, laid out as the 128-byte swizzle) and stores it with TMA,
+// then the low plane the same way once the box has been read. The residual
+// is read directly (it was prefetched into L2 at the tile's start). Padding
+// rows are stored as zeros (they must stay zero); rows past the frame are
+// clipped by TMA.
+template <int N, int kMine>
+__device__ __forceinline__ void store_split_sums(const ConvArgs& p, const float* bn, const float (&sum)[kMine * 32],
+                                                 const CUtensorMap* mhi, const CUtensorMap* mlo, uint8_t* box,
+                                                 int row0, int q, bool valid, int c_begin, int lane) {
+    using Box = EpiBox<false>;
+    if (row0 >= p.rows) return;   // the warp's rows are all past the frame
+    const bool skip = valid && p.skip != nullptr;
+#pragma unroll
+    for (int cc = 0; cc < kMine; ++cc) {
+        const int c0 = (c_begin + cc) * 32;
+        const size_t off = size_t(q) * p.ld + c0;
+        float4 sk[8], sl[8];
+        if (skip) {
+            const float4* hi = reinterpret_cast<const float4*>(static_cast<const float*>(p.skip) + off);
+            const float4* lo = reinterpret_cast<const float4*>(static_cast<const float*>(p.skip_lo) + off);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                sk[u] = hi[u];
+                sl[u] = lo[u];
+            }
+        }
+        float y[32];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const float* h = &sk[u].x;
+            const float* l = &sl[u].x;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int i = 4 * u + e;
+                y[i] = valid ? split_out(sum[cc * 32 + i], bn[c0 + i], bn[N + c0 + i], skip, skip ? h[e] : 0.0f,
+                                         skip ? l[e] : 0.0f)
+                             : 0.0f;
+            }
+        }
+#pragma unroll
+        for (int plane = 0; plane < 2; ++plane) {
+            float4 out[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                float* f = &out[u].x;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float v = y[4 * u + e], h = to_tf32(v);
+                    f[e] = plane == 0 ? h : __fsub_rn(v, h);
+                }
+            }
+            if (lane == 0) bulk_wait_read<0>();   // the box's previous store has read it
+            __syncwarp();
+#pragma unroll
+            for (int u = 0; u < 8; ++u) *reinterpret_cast<float4*>(box + Box::piece(lane, u)) = out[u];
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(plane == 0 ? mhi : mlo, box, c0, row0);
+                bulk_commit();
+            }
+        }
+    }
+}
+
+// kSeg: the stacked split mode's accumulation segment in taps (0: one run
+// per tile). mOut/mSkip: the epilogue's output and residual boxes; in the
+// stacked split mode the high and low output planes.
+template <int N, bool kBf16, bool kSplit, int kTiles, int kSeg>
 __global__ void __launch_bounds__(kThreads, 1)
     conv3x3_tc(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAlo,
                const __grid_constant__ CUtensorMap mW, const __grid_constant__ CUtensorMap mWlo,
@@ -339,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&sm.acc_full[i], 1);
-            mbar_init(&sm.acc_empty[i], 32 * kEpiWarps);
+            mbar_init(&sm.acc_empty[i], kEpiWarps);   // one arrival per epilogue warp
         }
         mbar_init(sm.done, 1);
         for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&sm.skip_full[i], 1);
@@ -348,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0 && lane == 0) {
         tma_prefetch_map(&mA);
         tma_prefetch_map(&mW);
-        if (C::kEpiTma) {
+        if (C::kEpiTma || C::kStack) {
             tma_prefetch_map(&mOut);
             tma_prefetch_map(&mSkip);
         }
@@ -431,47 +529,106 @@ __global__ void __launch_bounds__(kThreads, 1)
             constexpr uint32_t b_stage = (C::kOps * C::kBBytes) >> 4, b_lo = C::kBBytes >> 4;
             uint32_t toff[9];
             tap_offsets(p, toff);
-            for (int g = blockIdx.x; g < ngroups && ok; g += gridDim.x, ++j) {
-                const uint32_t acc = j & 1;
-                if (!(ok = mbar_wait(&sm.acc_empty[acc], ((j >> 1) & 1) ^ 1, p.err, kErrWaitMma))) break;
-                tc_fence_after();
-                const uint32_t d = tmem + acc * (kTiles * C::kTileCols);   // tile u's at + u * kTileCols
-                for (int c = 0; c < p.nchunks && ok; ++c) {
-                    if (!(ok = mbar_wait(&sm.a_full[ra.idx], ra.phase, p.err, kErrWaitMma))) break;
-                    const uint64_t ac = a_desc + ra.idx * a_stage;
+            if constexpr (kSeg == 0) {
+                // One accumulator run per tile.
+                for (int g = blockIdx.x; g < ngroups && ok; g += gridDim.x, ++j) {
+                    const uint32_t acc = j & 1;
+                    if (!(ok = mbar_wait(&sm.acc_empty[acc], ((j >> 1) & 1) ^ 1, p.err, kErrWaitMma))) break;
+                    tc_fence_after();
+                    const uint32_t d = tmem + acc * (kTiles * C::kTileCols);   // tile u's at + u * kTileCols
+                    for (int c = 0; c < p.nchunks && ok; ++c) {
+                        if (!(ok = mbar_wait(&sm.a_full[ra.idx], ra.phase, p.err, kErrWaitMma))) break;
+                        const uint64_t ac = a_desc + ra.idx * a_stage;
 #pragma unroll
-                    for (int t = 0; t < 9; ++t) {
-                        if (t >= p.taps) break;
-                        if (!(ok = mbar_wait(&sm.b_full[rb.idx], rb.phase, p.err, kErrWaitMma))) break;
-                        tc_fence_after();
-                        const uint64_t at = ac + toff[t], bt = b_desc + rb.idx * b_stage;
+                        for (int t = 0; t < 9; ++t) {
+                            if (t >= p.taps) break;
+                            if (!(ok = mbar_wait(&sm.b_full[rb.idx], rb.phase, p.err, kErrWaitMma))) break;
+                            tc_fence_after();
+                            const uint64_t at = ac + toff[t], bt = b_desc + rb.idx * b_stage;
 #pragma unroll
-                        for (int k = 0; k < C::kSteps; ++k) {
+                            for (int k = 0; k < C::kSteps; ++k) {
 #pragma unroll
-                            for (int u = 0; u < kTiles; ++u) {   // every tile of the group reads this weight tile
-                                const uint32_t du = d + uint32_t(u) * C::kTileCols;
-                                const uint64_t au = at + u * a_tile;
-                                if constexpr (C::kStack) {   // [hi | lo] weight planes as one operand
-                                    umma<kBf16>(du, au + 2 * k, bt + 2 * k, C::kIdescStack, (c | t | k) != 0);
-                                    umma<kBf16>(du, au + a_lo + 2 * k, bt + 2 * k, C::kIdesc, 1);
-                                } else {
-                                    umma<kBf16>(du, au + 2 * k, bt + 2 * k, C::kIdesc, (c | t | k) != 0);
-                                    if (kSplit) {
-                                        umma<kBf16>(du, au + 2 * k, bt + b_lo + 2 * k, C::kIdesc, 1);
-                                        umma<kBf16>(du, au + a_lo + 2 * k, bt + 2 * k, C::kIdesc, 1);
+                                for (int u = 0; u < kTiles; ++u) {   // every tile of the group reads this weight tile
+                                    const uint32_t du = d + uint32_t(u) * C::kTileCols;
+                                    const uint64_t au = at + u * a_tile;
+                                    if constexpr (C::kStack) {
+                                        // [hi | lo] weight planes as one operand: a_hi.b_hi
+                                        // into [0, N), a_hi.b_lo into [N, 2N); a_lo.b_hi into
+                                        // [N, 2N) too, so the large products alone
+                                        // accumulate in [0, N).
+                                        constexpr uint32_t kIdescStack = umma_idesc(2 * N, kBf16);
+                                        umma<kBf16>(du, au + 2 * k, bt + 2 * k, kIdescStack, (c | t | k) != 0);
+                                        umma<kBf16>(du + N, au + a_lo + 2 * k, bt + 2 * k, C::kIdesc, 1);
+                                    } else {
+                                        umma<kBf16>(du, au + 2 * k, bt + 2 * k, C::kIdesc, (c | t | k) != 0);
+                                        if (kSplit) {
+                                            umma<kBf16>(du, au + 2 * k, bt + b_lo + 2 * k, C::kIdesc, 1);
+                                            umma<kBf16>(du, au + a_lo + 2 * k, bt + 2 * k, C::kIdesc, 1);
+                                        }
                                     }
                                 }
                             }
+                            umma_commit(&sm.b_empty[rb.idx]);   // frees the weight buffer once read
+                            rb.next(p.sb);
                         }
-                        umma_commit(&sm.b_empty[rb.idx]);   // frees the weight buffer once read
-                        rb.next(p.sb);
+                        if (!ok) break;
+                        umma_commit(&sm.a_empty[ra.idx]);       // frees the halo buffer
+                        ra.next(p.sa);
                     }
                     if (!ok) break;
-                    umma_commit(&sm.a_empty[ra.idx]);       // frees the halo buffer
-                    ra.next(p.sa);
+                    umma_commit(&sm.acc_full[acc]);             // the tile's accumulator is complete
                 }
-                if (!ok) break;
-                umma_commit(&sm.acc_full[acc]);             // the tile's accumulator is complete
+            } else {
+                // The stacked split mode in segments of kSeg taps (a one-tap
+                // pass: of one chunk), each on the next accumulator; the
+                // epilogue sums them in fp32. Segment bounds fall on unrolled
+                // tap positions: a counter and branch per tap in this thread
+                // would slow every MMA after it.
+                static_assert(C::kStack && 9 % kSeg == 0, "segments: stacked split mode, kSeg divides 9");
+                const bool one_tap = p.taps == 1;
+                for (int g = blockIdx.x; g < ngroups && ok; g += gridDim.x) {
+                    uint32_t acc = 0, d = 0;
+                    for (int c = 0; c < p.nchunks && ok; ++c) {
+                        if (!(ok = mbar_wait(&sm.a_full[ra.idx], ra.phase, p.err, kErrWaitMma))) break;
+                        const uint64_t ac = a_desc + ra.idx * a_stage;
+#pragma unroll
+                        for (int t = 0; t < 9; ++t) {
+                            if (t >= p.taps) break;
+                            if (t % kSeg == 0) {   // open a segment on the next accumulator
+                                acc = j & 1;
+                                if (!(ok = mbar_wait(&sm.acc_empty[acc], ((j >> 1) & 1) ^ 1, p.err, kErrWaitMma))) break;
+                                d = tmem + acc * (kTiles * C::kTileCols);
+                            }
+                            if (!(ok = mbar_wait(&sm.b_full[rb.idx], rb.phase, p.err, kErrWaitMma))) break;
+                            tc_fence_after();
+                            const uint64_t at = ac + toff[t], bt = b_desc + rb.idx * b_stage;
+#pragma unroll
+                            for (int k = 0; k < C::kSteps; ++k) {
+#pragma unroll
+                                for (int u = 0; u < kTiles; ++u) {
+                                    const uint32_t du = d + uint32_t(u) * C::kTileCols;
+                                    const uint64_t au = at + u * a_tile;
+                                    constexpr uint32_t kIdescStack = umma_idesc(2 * N, kBf16);
+                                    umma<kBf16>(du, au + 2 * k, bt + 2 * k, kIdescStack, (t % kSeg) != 0 || k != 0);
+                                    umma<kBf16>(du + N, au + a_lo + 2 * k, bt + 2 * k, C::kIdesc, 1);
+                                }
+                            }
+                            umma_commit(&sm.b_empty[rb.idx]);
+                            rb.next(p.sb);
+                            if (t % kSeg == kSeg - 1) {   // the segment is complete
+                                umma_commit(&sm.acc_full[acc]);
+                                ++j;
+                            }
+                        }
+                        if (!ok) break;
+                        if (one_tap) {   // a one-tap pass closes its segment per chunk
+                            umma_commit(&sm.acc_full[acc]);
+                            ++j;
+                        }
+                        umma_commit(&sm.a_empty[ra.idx]);
+                        ra.next(p.sa);
+                    }
+                }
             }
             // All MMAs issued by this thread are complete before teardown.
             umma_commit(sm.done);
@@ -494,11 +651,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         ew.obuf = sm.epi + e * (C::kEpiBytes / kEpiWarps);
         ew.sbuf = ew.obuf + C::kEpiBytes / kEpiWarps / 2;
         ew.sbar = sm.skip_full + 2 * e;
-        uint32_t j = 0;
-        for (int g = blockIdx.x; g < ngroups; g += gridDim.x, ++j) {
-            const uint32_t acc = j & 1;
-            if (!mbar_wait(&sm.acc_full[acc], (j >> 1) & 1, p.err, kErrWaitEpilogue)) break;
-            tc_fence_after();
+        uint32_t j = 0;   // accumulator runs consumed (one per tile, or one per segment)
+        const int segs = kSeg == 0 ? 1 : (p.taps == 1 ? p.nchunks : p.nchunks * (9 / (kSeg > 0 ? kSeg : 1)));
+        for (int g = blockIdx.x; g < ngroups; g += gridDim.x) {
             const int tile = g * kTiles + u;
             const int q = tile * 128 + row_in_tile;
             bool valid = q < p.rows;
@@ -506,16 +661,52 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int r = q % p.S;
                 valid = r >= n1 && (r % n1) != p.n;
             }
-            const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + (acc * kTiles + u) * C::kTileCols;
-            if constexpr (C::kEpiTma)
-                store_epilogue_tma<N, kBf16>(p, sm.bn, &mOut, &mSkip, taddr, tile * 128 + quarter * 32, valid, c_begin,
-                                             c_end, ew, lane);
-            else if (tile < p.ntiles)
-                store_epilogue_split<N, C::kStack>(p, sm.bn, taddr, q, valid, c_begin, c_end);
-            tc_fence_before();
-            mbar_arrive(&sm.acc_empty[acc]);
+            const uint32_t lanes = tmem + (uint32_t(quarter * 32) << 16) + uint32_t(u) * C::kTileCols;
+            if constexpr (C::kStack) {
+                // The tile's segments, summed in registers; each accumulator
+                // is released as soon as it has been read.
+                constexpr int kMine = kTiles == 2 ? kChunks : (kChunks >= 2 ? kChunks / 2 : 1);
+                const bool mine = c_begin < c_end && tile < p.ntiles;
+                if (mine && valid && p.skip != nullptr) {   // the residual reaches L2 while the tile accumulates
+                    const size_t off = size_t(q) * p.ld + size_t(c_begin) * 32;
+#pragma unroll
+                    for (int cc = 0; cc < kMine; ++cc) {
+                        prefetch_l2(static_cast<const float*>(p.skip) + off + cc * 32);
+                        prefetch_l2(static_cast<const float*>(p.skip_lo) + off + cc * 32);
+                    }
+                }
+                float sum[kMine * 32];
+                bool ok = true;
+                for (int sg = 0; sg < segs; ++sg, ++j) {
+                    const uint32_t acc = j & 1;
+                    if (!(ok = mbar_wait(&sm.acc_full[acc], (j >> 1) & 1, p.err, kErrWaitEpilogue))) break;
+                    tc_fence_after();
+                    if (mine) add_segment<N, kMine>(lanes + acc * (kTiles * C::kTileCols), c_begin, sum, sg == 0);
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
+                }
+                if (!ok) break;
+                if (mine)
+                    store_split_sums<N, kMine>(p, sm.bn, sum, &mOut, &mSkip, ew.obuf, tile * 128 + quarter * 32, q, valid,
+                                               c_begin, lane);
+            } else {
+                const uint32_t acc = j & 1;
+                if (!mbar_wait(&sm.acc_full[acc], (j >> 1) & 1, p.err, kErrWaitEpilogue)) break;
+                tc_fence_after();
+                const uint32_t taddr = lanes + acc * (kTiles * C::kTileCols);
+                if constexpr (C::kEpiTma)
+                    store_epilogue_tma<N, kBf16>(p, sm.bn, &mOut, &mSkip, taddr, tile * 128 + quarter * 32, valid,
+                                                 c_begin, c_end, ew, lane);
+                else if (tile < p.ntiles)
+                    store_epilogue_split<N>(p, sm.bn, taddr, q, valid, c_begin, c_end);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
+                ++j;
+            }
         }
-        if (C::kEpiTma && lane == 0) bulk_wait_all();   // every output box written before the CTA exits
+        if ((C::kEpiTma || C::kStack) && lane == 0) bulk_wait_all();   // every output box written before the CTA exits
     }
 
     tc_fence_before();
@@ -735,7 +926,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 store_epilogue_tma<N, kBf16>(p, sm.bn, &mOut, &mSkip, taddr, (2 * pr + int(rank)) * 128 + quarter * 32,
                                              valid, c_begin, c_end, ew, lane);
             else
-                store_epilogue_split<N, false>(p, sm.bn, taddr, q, valid, c_begin, c_end);
+                store_epilogue_split<N>(p, sm.bn, taddr, q, valid, c_begin, c_end);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(acc ? leader_empty1 : leader_empty0);
@@ -814,26 +1005,45 @@ __global__ void __launch_bounds__(128, 1)
 
 std::atomic<int> g_conv_path{0};   // 0: by width, 1: one tile per CTA, 2: CTA pairs, 3: two tiles per CTA
 
+// Taps per accumulation segment: at 128 channels three (12 MMA K steps of 8
+// on the large products' accumulator before the epilogue takes the partial
+// sum), at 64 or fewer nine (one chunk): there the epilogue's extra work
+// per segment costs as much as the narrow layers' MMAs take, and a chunk's
+// 36 K steps already keep the sums within the reference's tolerance against
+// double precision.
+template <int N>
+constexpr int kDefaultSegment = N <= 64 ? 9 : 3;
+
 // The conv forms: one CTA per 128-row tile, one CTA per two tiles sharing
 // each weight tile (N <= 128: both accumulators fit in TMEM), or 2-CTA pairs.
 enum ConvForm : int { kFormSingle = 1, kFormPair = 2, kFormDual = 3 };
 
-template <int N, bool kBf16, bool kSplit, int kTiles>
-cudaError_t launch_single(const ConvMaps& m, ConvArgs a, int sms, cudaStream_t s) {
+template <int N, bool kBf16, bool kSplit, int kTiles, int kSeg>
+cudaError_t launch_single_seg(const ConvMaps& m, ConvArgs a, int sms, cudaStream_t s) {
     using C = ConvCfg<N, kBf16, kSplit, kTiles>;
     conv_smem_bytes(N, kBf16 ? kBF16 : (kSplit ? kTF32x3 : kTF32), a.halo_rows, &a.sa, &a.sb, false, kTiles);
     const size_t smem = smem_total(a.sa, a.sb, C::kOps * kTiles, C::kOps, a.a_bytes, C::kBBytes, C::kEpiBytes);
     static std::atomic<size_t> configured{0};   // the largest size this instantiation was opened for
     if (smem > configured.load()) {
-        const cudaError_t e = cudaFuncSetAttribute(conv3x3_tc<N, kBf16, kSplit, kTiles>,
+        const cudaError_t e = cudaFuncSetAttribute(conv3x3_tc<N, kBf16, kSplit, kTiles, kSeg>,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
         if (e != cudaSuccess) return e;
         configured = smem;
     }
     const int groups = (a.ntiles + kTiles - 1) / kTiles;
     const int grid = std::max(1, std::min(groups, sms));
-    return launch_pdl(conv3x3_tc<N, kBf16, kSplit, kTiles>, dim3(grid), dim3(kThreads), smem, s, m.a, m.a_lo, m.w,
-                      m.w_lo, m.out, m.skip, a);
+    return launch_pdl(conv3x3_tc<N, kBf16, kSplit, kTiles, kSeg>, dim3(grid), dim3(kThreads), smem, s, m.a, m.a_lo,
+                      m.w, m.w_lo, m.out, C::kStack ? m.out_lo : m.skip, a);
+}
+
+// The stacked split mode runs in segments of kDefaultSegment<N> taps unless
+// the test hook asks for one run per tile (a.seg == 0).
+template <int N, bool kBf16, bool kSplit, int kTiles>
+cudaError_t launch_single(const ConvMaps& m, ConvArgs a, int sms, cudaStream_t s) {
+    if constexpr (ConvCfg<N, kBf16, kSplit, kTiles>::kStack) {
+        if (a.seg != 0) return launch_single_seg<N, kBf16, kSplit, kTiles, kDefaultSegment<N>>(m, a, sms, s);
+    }
+    return launch_single_seg<N, kBf16, kSplit, kTiles, 0>(m, a, sms, s);
 }
 
 template <int N, bool kBf16, bool kSplit>
@@ -889,7 +1099,11 @@ size_t conv_smem_bytes(int n_out, int precision, int halo_rows, int* sa_out, int
     const int ops = precision == kTF32x3 ? 2 : 1, a_ops = ops * tiles;
     const int a_bytes = (halo_rows * 128 + 1023) / 1024 * 1024;
     const uint32_t b_bytes = uint32_t(pair ? n_out / 2 : n_out) * 128u;
-    const uint32_t epi = precision == kTF32x3 ? 0u : uint32_t(kEpiWarps) * (precision == kBF16 ? 4096u : 8192u);
+    // As ConvCfg::kEpiBytes: the stacked split mode (128 channels or fewer,
+    // both accumulators of every tile in TMEM) has one 4 KB box per warp.
+    const bool stacked = n_out <= 128 && 2 * tiles * 2 * n_out <= 512;
+    const uint32_t epi = precision == kTF32x3 ? (stacked ? uint32_t(kEpiWarps) * 4096u : 0u)
+                                              : uint32_t(kEpiWarps) * (precision == kBF16 ? 4096u : 8192u);
     constexpr size_t kMax = 227 * 1024;
     int sa = 2, sb = 2;
     for (int cand = kMaxStages; cand >= 2; --cand)
@@ -909,6 +1123,9 @@ size_t conv_smem_bytes(int n_out, int precision, int halo_rows, int* sa_out, int
 
 void set_conv_path(int path) { g_conv_path = path; }
 
+std::atomic<int> g_conv_segment{-1};
+void set_conv_segment(int steps) { g_conv_segment = steps; }
+
 // Which form a layer runs: by default the CTA pair for 256 output
 // channels, where a weight tile is 32 KB per tap and halving it per SM
 // pays (C4 bf16 on B200: 1217 against 1148 TFLOP/s per conv), the two-tile
@@ -917,7 +1134,9 @@ void set_conv_path(int path) { g_conv_path = path; }
 int conv_form(int ntiles, int n_out, int precision, int halo_rows, int sms) {
     // The two-tile form stages two halos per stage; it must fit with at
     // least two weight stages (the split mode at 128 channels does not).
-    const bool dual_fits = n_out <= 128 &&
+    // The split mode takes it only where both tiles' stacked accumulators
+    // fit in TMEM (64 channels or fewer), so its sums stay segmented.
+    const bool dual_fits = n_out <= (precision == kTF32x3 ? 64 : 128) &&
                            conv_smem_bytes(n_out, precision, halo_rows, nullptr, nullptr, false, 2) <= 227 * 1024;
     const int path = g_conv_path.load();
     if (path == kFormSingle) return kFormSingle;
@@ -928,9 +1147,12 @@ int conv_form(int ntiles, int n_out, int precision, int halo_rows, int sms) {
     return kFormSingle;
 }
 
-cudaError_t launch_conv(const ConvMaps& maps, const ConvArgs& a, int n_out, int precision, int sms, cudaStream_t s) {
-    if (a.ntiles <= 0) return cudaSuccess;
-    const int form = conv_form(a.ntiles, n_out, precision, a.halo_rows, sms);
+cudaError_t launch_conv(const ConvMaps& maps, const ConvArgs& args, int n_out, int precision, int sms, cudaStream_t s) {
+    if (args.ntiles <= 0) return cudaSuccess;
+    const int form = conv_form(args.ntiles, n_out, precision, args.halo_rows, sms);
+    ConvArgs a = args;
+    const int segment = g_conv_segment.load();
+    a.seg = segment < 0 ? 1 : segment;   // 0: one run per tile; otherwise segments of kDefaultSegment<N> taps
     switch (precision) {
         case kTF32: return dispatch_n<false, false>(n_out, maps, a, form, sms, s);
         case kTF32x3: return dispatch_n<false, true>(n_out, maps, a, form, sms, s);

@@ -567,11 +567,11 @@ void Workspace::place(const Weights& w, uint8_t* base) {
         map[i] = make_tensor_map(trunk[i], precision, cpad, rows, KC, uint32_t(fr.halo));
         map_lo[i] = precision == kTF32x3 ? make_tensor_map(trunk_lo[i], precision, cpad, rows, KC, uint32_t(fr.halo)) : map[i];
         // The conv epilogue's boxes: {32 channels, 32 rows}; bf16 64-byte rows
-        // with the 64-byte swizzle, fp32 (plain tf32) 128-byte rows with the
-        // 128-byte swizzle. The split mode stores directly.
+        // with the 64-byte swizzle, fp32 (tf32, and both planes of the split
+        // mode) 128-byte rows with the 128-byte swizzle.
         if (precision == kBF16) emap[i] = make_tensor_map(trunk[i], precision, cpad, rows, 32, 32, 64);
-        else if (precision == kTF32) emap[i] = make_tensor_map(trunk[i], precision, cpad, rows, 32, 32, 128);
-        else emap[i] = map[i];
+        else emap[i] = make_tensor_map(trunk[i], precision, cpad, rows, 32, 32, 128);
+        emap_lo[i] = precision == kTF32x3 ? make_tensor_map(trunk_lo[i], precision, cpad, rows, 32, 32, 128) : emap[i];
     }
 }
 
@@ -655,7 +655,7 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
                     int nchunks, int timer_slot) {
         const Weights::Conv& cv = w.conv(index);
         ConvMaps m{in, in_lo, cv.map_w, cv.map_w_lo, cv.map_w_pair, cv.map_w_lo_pair, ws.emap[dst],
-                   ws.emap[skip >= 0 ? skip : dst]};
+                   ws.emap[skip >= 0 ? skip : dst], ws.emap_lo[dst]};
         a.taps = taps;
         a.nchunks = nchunks;
         a.out = ws.trunk[dst];

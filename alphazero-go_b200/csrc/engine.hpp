@@ -131,7 +131,8 @@ public:
     uint8_t* records = nullptr;   // [max_batch][stones_record_bytes]: encoder input (infer_stones)
     int* err = nullptr;           // kernel error word
     CUtensorMap map[3]{}, map_lo[3]{};
-    CUtensorMap emap[3]{};        // bf16, tf32: the frames in the conv epilogue's {32, 32} boxes
+    CUtensorMap emap[3]{};        // the frames in the conv epilogue's {32, 32} boxes (split mode: high planes)
+    CUtensorMap emap_lo[3]{};     // split mode: the low planes in the same boxes
     CUtensorMap map_stem{}, map_stem_lo{};
 
 private:

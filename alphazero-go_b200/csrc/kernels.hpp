@@ -78,6 +78,7 @@ struct ConvArgs {
     int halo_rows;     // 128 + 2(n+2)
     int a_bytes;       // one halo buffer, rounded up to 1024
     int sa, sb;        // pipeline depths: halo buffers, weight buffers
+    int seg;           // stacked split mode: 0 one accumulator run per tile, else segments (3 or 9 taps by width)
     void* out;         // [rows][ld] bf16 or f32 (split: the tf32 high part)
     void* out_lo;      // split: f32 low part
     const void* skip;  // null, or the residual input (same layout as out)
@@ -92,6 +93,7 @@ struct ConvMaps {
     CUtensorMap w, w_lo;             // weights [N][9*Cin]: box {chunk, N}
     CUtensorMap w_pair, w_lo_pair;   // the same weights in boxes of {chunk, N/2}: one half per CTA of a pair
     CUtensorMap out, skip;           // bf16/tf32: the output and residual frames in boxes of {32, 32} (epilogue)
+    CUtensorMap out_lo;              // split mode: the output's low plane in boxes of {32, 32} (out: the high plane)
 };
 
 // Shared memory a conv launch needs, and its pipeline depths (pair: the
@@ -106,6 +108,10 @@ size_t conv_smem_bytes(int n_out, int precision, int halo_rows, int* sa, int* sb
 cudaError_t launch_conv(const ConvMaps& maps, const ConvArgs& a, int n_out, int precision, int sms, cudaStream_t s);
 // Test hook: 0 by width, 1 one tile per CTA, 2 CTA pairs, 3 two tiles per CTA (N <= 128).
 void set_conv_path(int path);
+// Test hook for the stacked split mode's accumulation: -1 the default
+// (segments of three taps at 128 channels, nine at 64 or fewer), 0 one
+// accumulator run per tile.
+void set_conv_segment(int steps);
 
 // The stem's packed operand: the [B][P][A] fp32 input unfolded into frame
 // rows of K = 9*P values (column t*P + p), ld elements apart. The stem conv
@@ -163,6 +169,7 @@ cudaError_t launch_head_out(const HeadArgs& a, cudaStream_t s);                 
 
 // Test hooks and context checks.
 cudaError_t launch_fill(float* data, size_t n, float value, cudaStream_t s);
+cudaError_t launch_tanh(float* data, size_t n, cudaStream_t s);   // data = tanhf(data), as the heads compute it
 cudaError_t fill_attributes(cudaFuncAttributes* attr);
 cudaError_t launch_spin(unsigned long long ns, cudaStream_t s);
 // A kernel that waits on an mbarrier nothing arrives on, with a limit of

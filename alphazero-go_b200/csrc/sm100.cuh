@@ -105,6 +105,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 
 // --------------------------------------------------------------------- TMA
 
+// Brings the 128-byte line holding `p` into L2.
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
+}
+
 __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -355,6 +360,20 @@ __host__ __device__ constexpr uint32_t umma_idesc(int n, bool bf16, int m = 128)
            | ((bf16 ? 1u : 2u) << 10)              // B format
            | (static_cast<uint32_t>(n >> 3) << 17) // N / 8
            | (static_cast<uint32_t>(m >> 4) << 24);     // M / 16
+}
+
+// Two IEEE round-to-nearest additions in one instruction (add.rn.f32x2,
+// sm_100): element-wise the same results as two __fadd_rn.
+__device__ __forceinline__ float2 fadd2_rn(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
 }
 
 // Round-to-nearest (ties away) to tf32, as cvt.rna.tf32.f32 does; the low

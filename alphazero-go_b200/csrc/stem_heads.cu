@@ -481,6 +481,11 @@ __global__ void fill_kernel(float* data, size_t n, float value) {
         data[i] = value;
 }
 
+__global__ void tanh_kernel(float* data, size_t n) {
+    for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
+        data[i] = tanhf(data[i]);
+}
+
 // Holds the GPU for `ns` nanoseconds of %globaltimer (a test hook; bounded).
 __global__ void spin_kernel(unsigned long long ns) {
     const uint64_t start = global_timer();
@@ -601,6 +606,12 @@ cudaError_t launch_head_out(const HeadArgs& a, cudaStream_t s) {
 cudaError_t launch_fill(float* data, size_t n, float value, cudaStream_t s) {
     if (n == 0) return cudaSuccess;
     fill_kernel<<<blocks_for(n, 256), 256, 0, s>>>(data, n, value);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_tanh(float* data, size_t n, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    tanh_kernel<<<blocks_for(n, 256), 256, 0, s>>>(data, n);
     return cudaGetLastError();
 }
 

@@ -25,6 +25,10 @@ struct Arenas {
     std::vector<float> params, buffers;
 };
 Arenas arenas(const azgo::Network& net);
+// The same against the layout of another shape (cuda_probe::checkUpload):
+// refuses, by name, the first tensor of net that layout does not have.
+Arenas arenas(const azgo::Network& net, const azgo::NetConfig& layout);
+azb_net_desc describe(const azgo::NetConfig& c);
 
 // makeCudaRunner on a given device (one hub per GPU); precision < 0: the default.
 std::unique_ptr<azgo::BatchRunner> makeCudaRunnerOn(const azgo::Network& net, int maxBatch, int slots, int device,

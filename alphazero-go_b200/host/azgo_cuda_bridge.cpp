@@ -14,9 +14,10 @@
 //   azb_host::makeCudaRunnerOn(net, maxBatch, slots, device) for one hub per
 //   GPU in a multi-GPU process.
 // The reference's kernel-level probes of its SIMT design (cuda_probe::gemm,
-// im2col3, bnInfer, relu, addInto, policyFlatten, biasAddRows, tanhInPlace,
-// convBnRelu, transposeInput) have no counterpart here: this engine has no
-// such kernels; its own kernel checks are the azb_probe_* entry points.
+// im2col3, bnInfer, relu, addInto, policyFlatten, biasAddRows, convBnRelu,
+// transposeInput) have no counterpart here: this engine has no such kernels;
+// its own kernel checks are the azb_probe_* entry points. tanhInPlace runs
+// the tanhf the head kernels use.
 #include <algorithm>
 #include <atomic>
 #include <cstdlib>
@@ -66,9 +67,11 @@ azb_net_desc describe(const azgo::NetConfig& c) {
     return azb_net_desc{c.boardSize, c.history, c.blocks, c.filters, c.valueHidden, c.ownership ? 1 : 0};
 }
 
-Arenas arenas(const azgo::Network& network) {
+Arenas arenas(const azgo::Network& network) { return arenas(network, network.config()); }
+
+Arenas arenas(const azgo::Network& network, const azgo::NetConfig& layout) {
     azgo::Network& net = const_cast<azgo::Network&>(network);   // params() hands out views; nothing is written
-    const azb_net_desc d = describe(net.config());
+    const azb_net_desc d = describe(layout);
     Arenas a;
     a.params.assign(azb_layout_floats(&d, 0), 0.0f);
     a.buffers.assign(azb_layout_floats(&d, 1), 0.0f);
@@ -241,9 +244,30 @@ void failPassesAfter(int n) { azb_probe_fail_passes_after(n); }
 void setMemoryLimit(size_t bytes) { azb_probe_set_memory_limit(bytes); }
 long long passesCompleted() { return azb_probe_passes_completed(); }
 void setCopyOutDelay(int microseconds) { azb_probe_set_copy_out_delay(microseconds); }
-void checkUpload(const Network& layoutNet, const Network& net) {
-    if (layoutNet.config() != net.config()) azb_host::arenas(net);   // the layout is the shape's: refuses by name
-    azb_host::arenas(net);
+void checkUpload(const Network& layoutNet, const Network& net) { azb_host::arenas(net, layoutNet.config()); }
+// The engine's pass for a shape reads exactly that shape's layout: every
+// tensor of net the encodeAs layout lacks is one such a pass never reads.
+void checkForwardReadsEveryTensor(const Network& network, const NetConfig& encodeAs) {
+    Network& net = const_cast<Network&>(network);
+    const azb_net_desc d = azb_host::describe(encodeAs);
+    std::vector<std::string> known;
+    char name[128];
+    size_t size = 0, offset = 0;
+    for (int which = 0; which < 2; ++which)
+        for (int i = 0, n = azb_layout_count(&d, which); i < n; ++i)
+            if (azb_layout_entry(&d, which, i, name, sizeof name, &size, &offset) == 0) known.emplace_back(name);
+    std::string unread;
+    auto scan = [&](const auto& views) {
+        for (const auto& v : views)
+            if (std::find(known.begin(), known.end(), v.name) == known.end()) unread += (unread.empty() ? "" : ", ") + v.name;
+    };
+    scan(net.params());
+    scan(net.buffers());
+    if (!unread.empty()) throw std::logic_error("GPU network: the pass never reads " + unread);
+}
+void tanhInPlace(float* x, size_t count) {
+    char err[512] = {};
+    if (azb_probe_tanh(azb_host::defaultDevice(), x, count, err, sizeof err) != 0) throw std::runtime_error(err);
 }
 
 } // namespace cuda_probe

@@ -214,10 +214,19 @@ void azb_probe_set_copy_out_delay(int microseconds);
  * per CTA otherwise), 1 always one tile per CTA, 2 always CTA pairs, 3 two
  * tiles per CTA where N <= 128. For tests and measurements. */
 void azb_probe_set_conv_path(int path);
+/* tf32x3 at 128 output channels or fewer accumulates each tile in segments
+ * (three taps at 128 channels, nine at 64 or fewer; a one-tap pass: one
+ * chunk), summed in fp32 round-to-nearest by the epilogue (tcgen05's fp32
+ * accumulation rounds toward zero at every MMA). -1 the default, 0 one
+ * accumulator run per tile (for measurements). */
+void azb_probe_set_conv_segment(int steps);
 /* cuda_probe::binaryVersion / deviceArchitecture / fill (include/azgo/cuda.hpp:93-103). */
 int azb_probe_binary_version(int device);
 int azb_probe_device_architecture(int device);
 int azb_probe_fill(int device, float* data, size_t n, float value, size_t tail, char* err, size_t err_cap);
+/* cuda_probe::tanhInPlace (include/azgo/cuda.hpp:112): data[0..n) = tanh(data) on the device, with the
+ * tanhf the head kernels use for the value and ownership outputs. */
+int azb_probe_tanh(int device, float* data, size_t n, char* err, size_t err_cap);
 /* A kernel that waits on a barrier nothing arrives on: returns the kernel's
  * error word (5: its wait ran out after limit_ns) with the context intact. */
 int azb_probe_bounded_wait(int device, unsigned long long limit_ns, char* err, size_t err_cap);

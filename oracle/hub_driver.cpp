@@ -6,8 +6,11 @@
 // TEST INFRASTRUCTURE ONLY: built by `make -C oracle hub` from the
 // reference's sources (the hub, evaluators, network) plus the bridge into
 // oracle/_ref/libazhub.so, loaded by tests/test_gpu_dropin.py.
+#include <dirent.h>
+
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <cstdint>
 #include <cstring>
 #include <memory>
@@ -185,6 +188,97 @@ int azhub_memory_refusal(size_t limit, int device, char* msg, size_t cap) {
     }
     cuda_probe::setMemoryLimit(0);
     return refused;
+}
+
+// cuda_probe::checkUpload(layout, net) (tests/test_cuda.cpp:920-930): net of
+// shape (board, history, blocks, filters, vh, own_net) uploaded against the
+// layout of the same shape with ownership own_layout. 0 accepted, 1 refused
+// with a logic_error (its message in msg), -1 any other error.
+int azhub_check_upload(int board, int history, int blocks, int filters, int vh, int own_layout, int own_net, char* msg,
+                       size_t cap) {
+    try {
+        const Network layout(config(board, history, blocks, filters, vh, own_layout), 1);
+        const Network net(config(board, history, blocks, filters, vh, own_net), 1);
+        cuda_probe::checkUpload(layout, net);
+        return 0;
+    } catch (const std::logic_error& e) {
+        put(msg, cap, e.what());
+        return 1;
+    } catch (const std::exception& e) {
+        put(msg, cap, e.what());
+        return -1;
+    }
+}
+
+// cuda_probe::checkForwardReadsEveryTensor(net, encodeAs)
+// (tests/test_cuda.cpp:932-949). Same codes as azhub_check_upload.
+int azhub_check_reads(int board, int history, int blocks, int filters, int vh, int own_net, int own_encode, char* msg,
+                      size_t cap) {
+    try {
+        const Network net(config(board, history, blocks, filters, vh, own_net), 1);
+        cuda_probe::checkForwardReadsEveryTensor(net, config(board, history, blocks, filters, vh, own_encode));
+        return 0;
+    } catch (const std::logic_error& e) {
+        put(msg, cap, e.what());
+        return 1;
+    } catch (const std::exception& e) {
+        put(msg, cap, e.what());
+        return -1;
+    }
+}
+
+// cuda_probe::tanhInPlace over x[0..n) on `device` (tests/test_cuda.cpp:492-512).
+int azhub_tanh(float* x, size_t n, int device, char* msg, size_t cap) {
+    try {
+        azb_host::setDefaults(device, AZB_TF32X3);
+        cuda_probe::tanhInPlace(x, n);
+        return 0;
+    } catch (const std::exception& e) {
+        put(msg, cap, e.what());
+        return -1;
+    }
+}
+
+namespace {
+int threadCount() {
+    int count = 0;
+    if (DIR* d = opendir("/proc/self/task")) {
+        while (const dirent* e = readdir(d))
+            if (e->d_name[0] != '.') ++count;
+        closedir(d);
+    }
+    return count;
+}
+} // namespace
+
+// makeCudaRunner created and destroyed `cycles` times, every other one with
+// a pass in flight, leaves no thread behind (tests/test_cuda.cpp:1220-1238).
+// Reports the process's thread count before and after (waiting up to 2 s for
+// exiting threads). 0, or -1 with msg.
+int azhub_runner_cycles(int cycles, int device, int* before, int* after, char* msg, size_t cap) {
+    try {
+        azb_host::setDefaults(device, AZB_BF16);
+        Network net(config(9, 1, 1, 8, 16, 0), 707);
+        randomize(net, 707);
+        const NetConfig& cfg = net.config();
+        { auto warm = makeCudaRunner(net, 8); }
+        *before = threadCount();
+        for (int i = 0; i < cycles; ++i) {
+            auto runner = makeCudaRunner(net, 8);
+            std::fill_n(runner->input(0), static_cast<size_t>(8) * cfg.planes() * cfg.area(), 0.5f);
+            if (i % 2) runner->begin(0, 8, [](int, std::string) {});
+        }
+        int now = threadCount();
+        for (int tries = 0; now > *before && tries < 100; ++tries) {
+            std::this_thread::sleep_for(std::chrono::milliseconds(20));
+            now = threadCount();
+        }
+        *after = now;
+        return 0;
+    } catch (const std::exception& e) {
+        put(msg, cap, e.what());
+        return -1;
+    }
 }
 
 } // extern "C"
