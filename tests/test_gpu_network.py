@@ -43,7 +43,7 @@ def run_gpu(engine, desc_cfg, params, buffers, x, precision, max_batch=None):
 
 
 @pytest.mark.parametrize("shape", [(5, 1, 8), (9, 2, 16), (9, 6, 32), (9, 0, 16), (19, 2, 16), (5, 4, 32), (9, 2, 64),
-                                   (13, 1, 128)])
+                                   (13, 1, 128), (9, 1, 256)])
 def test_tf32x3_matches_reference_forward(engine, oracle, conv_path, shape):
     O = oracle
     c = cfg(O, *shape)
