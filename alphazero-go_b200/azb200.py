@@ -76,6 +76,8 @@ def lib() -> C.CDLL:
             L.azb_layout_entry.argtypes = [D, C.c_int, C.c_int, C.c_char_p, s, C.POINTER(s), C.POINTER(s)]
             L.azb_layout_floats.argtypes = [D, C.c_int]
             L.azb_layout_floats.restype = s
+            L.azb_checkpoint_config.argtypes = [C.c_char_p, D, C.POINTER(s), C.POINTER(s), C.c_char_p, s]
+            L.azb_checkpoint_read.argtypes = [C.c_char_p, D, _F, s, _F, s, C.c_char_p, s]
             L.azb_infer_create.argtypes = [D, _F, s, _F, s, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_void_p)] + err
             L.azb_infer_destroy.argtypes = [C.c_void_p]
             L.azb_infer_run.argtypes = [C.c_void_p, _F, C.c_int, _F, _F, _F, _F] + err
@@ -185,6 +187,33 @@ def pci_bus_id(device: int = 0) -> str:
 
 def arena_floats(desc: NetDesc) -> tuple[int, int]:
     return lib().azb_layout_floats(C.byref(desc), 0), lib().azb_layout_floats(C.byref(desc), 1)
+
+
+def checkpoint_config(path: str) -> NetDesc:
+    """readCheckpointConfig (include/azgo/checkpoint.hpp:25): the header's shape.
+    Raises RuntimeError with the reference loader's message."""
+    return _checkpoint_header(path)[0]
+
+
+def _checkpoint_header(path: str):
+    d, e = NetDesc(), _err()
+    np_, nb = C.c_size_t(), C.c_size_t()
+    if lib().azb_checkpoint_config(os.fsencode(path), C.byref(d), C.byref(np_), C.byref(nb), e, 1024) != 0:
+        raise RuntimeError(e.value.decode())
+    return d, np_.value, nb.value
+
+
+def load_checkpoint(path: str):
+    """loadNetwork (include/azgo/checkpoint.hpp:24) into the engine's arenas:
+    (NetDesc, params, buffers), ready for CudaInference / make_cuda_runner.
+    Raises RuntimeError with the reference loader's message."""
+    d, np_, nb = _checkpoint_header(path)
+    params = np.zeros(np_, np.float32)
+    buffers = np.zeros(nb, np.float32)
+    e = _err()
+    if lib().azb_checkpoint_read(os.fsencode(path), C.byref(d), _fp(params), np_, _fp(buffers), nb, e, 1024) != 0:
+        raise RuntimeError(e.value.decode())
+    return d, params, buffers
 
 
 def synth_network(desc: NetDesc, seed: int, kind: int = 0):

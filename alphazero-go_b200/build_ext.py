@@ -29,7 +29,7 @@ FLAGS = [
 
 
 def sources():
-    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".cuh", ".hpp")))
+    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".cpp", ".cuh", ".hpp")))
 
 
 def kernel_hash() -> str:
@@ -59,7 +59,7 @@ def up_to_date() -> bool:
 def build(force: bool = False, verbose: bool = False) -> str:
     if not force and up_to_date():
         return OUT
-    cu = [p for p in sources() if p.endswith(".cu")]
+    cu = [p for p in sources() if p.endswith((".cu", ".cpp"))]
     cmd = [NVCC, *FLAGS, f"-DAZB_KERNEL_HASH=\"{kernel_hash()}\"", "-I", CSRC, "-I", INCLUDE, "-o", OUT + ".tmp", *cu]
     if verbose:
         print(" ".join(cmd))

@@ -54,6 +54,25 @@ int azb_layout_entry(const azb_net_desc* desc, int which, int index, char* name,
                      size_t* offset);
 size_t azb_layout_floats(const azb_net_desc* desc, int which);
 
+/* ------------------------------------------------------------ checkpoint */
+
+/* The reference's network checkpoint (.azn: saveNetwork / loadNetwork /
+ * readCheckpointConfig, include/azgo/checkpoint.hpp:12-23, src/checkpoint.cpp)
+ * for hosts without the reference's Network. azb_checkpoint_config reads the
+ * header's NetConfig (readCheckpointConfig) and the two arenas' sizes in
+ * floats (either pointer may be null); azb_checkpoint_read reads every
+ * tensor into arenas of those sizes at their layout offsets (zero between
+ * tensors), checking each
+ * tensor's name and size against the layout in params() then buffers()
+ * order, as loadNetwork does, and sets *desc. Both return 0, or -1 with the
+ * reference loader's message in err ("cannot open checkpoint <path>",
+ * "<path>: truncated", "<path>: unsupported version 7", ...). Any shape the
+ * reference accepts loads; the engine's own limits apply at creation. */
+int azb_checkpoint_config(const char* path, azb_net_desc* desc, size_t* n_params, size_t* n_buffers, char* err,
+                          size_t err_cap);
+int azb_checkpoint_read(const char* path, azb_net_desc* desc, float* params, size_t n_params, float* buffers,
+                        size_t n_buffers, char* err, size_t err_cap);
+
 /* ---------------------------------------------------------------- device */
 
 /* cudaBuilt() (include/azgo/cuda.hpp:30): 1 in this library. */

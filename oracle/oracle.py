@@ -186,6 +186,9 @@ def ref() -> C.CDLL:
         R.azref_rng_sample.argtypes = [C.c_uint64, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double)]
         R.azref_derive_seed.argtypes = [C.c_uint64] * 4
         R.azref_derive_seed.restype = C.c_uint64
+        R.azref_save_checkpoint.argtypes = [C.c_void_p, C.c_char_p, C.c_char_p, C.c_size_t]
+        R.azref_load_checkpoint.argtypes = [C.c_char_p, C.POINTER(C.c_int), _F, C.c_size_t, _F, C.c_size_t,
+                                            C.c_char_p, C.c_size_t]
         _ref = R
     return _ref
 
@@ -235,6 +238,12 @@ class RefNetwork:
             raise RuntimeError(err.value.decode())
         return logits, values, own
 
+    def save_checkpoint(self, path: str):
+        """The reference's saveNetwork (src/checkpoint.cpp:80-100) of this network."""
+        err = C.create_string_buffer(512)
+        if ref().azref_save_checkpoint(self.h, os.fsencode(path), err, 512) != 0:
+            raise RuntimeError(err.value.decode())
+
     def bench_workers(self, backend: str, workers: int, batch: int, x: np.ndarray, seconds: float = 0.0,
                       max_calls: int = 0):
         """(positions/s, positions) with `workers` threads of Network::infer at `batch`."""
@@ -246,6 +255,24 @@ class RefNetwork:
         if rate < 0:
             raise RuntimeError(err.value.decode())
         return rate, pos.value
+
+
+def ref_load_checkpoint(path: str):
+    """The reference's loadNetwork (src/checkpoint.cpp:102-133): (shape tuple
+    (board, history, blocks, filters, value_hidden, ownership), params,
+    buffers) when it loads, else the RuntimeError message it threw (a str)."""
+    R = ref()
+    shape = (C.c_int * 6)()
+    err = C.create_string_buffer(1024)
+    if R.azref_load_checkpoint(os.fsencode(path), shape, None, 0, None, 0, err, 1024) != 0:
+        return err.value.decode()
+    cfg = NetConfig(shape[0], shape[1], shape[2], shape[3], shape[4], bool(shape[5]))
+    np_, nb = arena_floats(cfg)
+    params = np.zeros(np_, np.float32)
+    buffers = np.zeros(nb, np.float32)
+    if R.azref_load_checkpoint(os.fsencode(path), shape, _fp(params), np_, _fp(buffers), nb, err, 1024) != 0:
+        return err.value.decode()
+    return tuple(shape), params, buffers
 
 
 def ref_encode_records(cfg: NetConfig, records: np.ndarray) -> np.ndarray:

@@ -22,6 +22,7 @@
 #include "azgo/backend.hpp"
 #include "azgo/board.hpp"
 #include "azgo/encode.hpp"
+#include "azgo/checkpoint.hpp"
 #include "azgo/network.hpp"
 #include "azgo/param_layout.hpp"
 #include "azgo/rng.hpp"
@@ -102,6 +103,46 @@ azref_net* azref_net_create(int board, int history, int blocks, int filters, int
 }
 
 void azref_net_destroy(azref_net* h) { delete h; }
+
+// saveNetwork (src/checkpoint.cpp:80-100) of the shim's network. 0, or -1 with err.
+int azref_save_checkpoint(azref_net* h, const char* path, char* err, size_t cap) {
+    try {
+        saveNetwork(h->net, path);
+        return 0;
+    } catch (const std::exception& e) {
+        fail(err, cap, e.what());
+        return -1;
+    }
+}
+
+// loadNetwork (src/checkpoint.cpp:102-133) of `path`: 0 when it loads (its
+// two arenas written when params/buffers are non-null and of the right
+// sizes, *shape = board, history, blocks, filters, value_hidden, ownership),
+// 1 with the loader's message when it throws.
+int azref_load_checkpoint(const char* path, int* shape, float* params, size_t n_params, float* buffers,
+                          size_t n_buffers, char* err, size_t cap) {
+    try {
+        Network net = loadNetwork(path);
+        const NetConfig& c = net.config();
+        const int v[6] = {c.boardSize, c.history, c.blocks, c.filters, c.valueHidden, c.ownership ? 1 : 0};
+        if (shape) std::memcpy(shape, v, sizeof v);
+        const ParamLayout L = ParamLayout::of(net);
+        if (params && buffers && n_params == L.paramFloats && n_buffers == L.bufferFloats) {
+            std::fill(params, params + n_params, 0.0f);
+            std::fill(buffers, buffers + n_buffers, 0.0f);
+            const auto views = net.params();
+            for (size_t i = 0; i < views.size(); ++i)
+                std::memcpy(params + L.params[i].offset, views[i].value, views[i].size * sizeof(float));
+            const auto bufs = net.buffers();
+            for (size_t i = 0; i < bufs.size(); ++i)
+                std::memcpy(buffers + L.buffers[i].offset, bufs[i].value, bufs[i].size * sizeof(float));
+        }
+        return 0;
+    } catch (const std::exception& e) {
+        fail(err, cap, e.what());
+        return 1;
+    }
+}
 
 size_t azref_floats(azref_net* h, int which) { return which == 0 ? h->layout.paramFloats : h->layout.bufferFloats; }
 
