@@ -117,6 +117,7 @@ def lib() -> C.CDLL:
             L.azb_probe_set_copy_out_delay.argtypes = [C.c_int]
             L.azb_probe_set_conv_path.argtypes = [C.c_int]
             L.azb_probe_set_conv_segment.argtypes = [C.c_int]
+            L.azb_probe_set_tower_fused.argtypes = [C.c_int]
             L.azb_probe_binary_version.argtypes = [C.c_int]
             L.azb_probe_device_architecture.argtypes = [C.c_int]
             L.azb_probe_fill.argtypes = [C.c_int, _F, s, C.c_float, s] + err
@@ -500,6 +501,11 @@ class cuda_probe:
     def set_conv_path(path: int):
         """0 default (by width), 1 one tile per CTA, 2 CTA pairs (M = 256), 3 two tiles per CTA (N <= 128)."""
         lib().azb_probe_set_conv_path(path)
+
+    @staticmethod
+    def set_tower_fused(mode: int):
+        """-1 default (one launch for the tower of boards up to 10x10 with <= 64 channels), 0 per-layer kernels."""
+        lib().azb_probe_set_tower_fused(mode)
 
     @staticmethod
     def set_conv_segment(steps: int):

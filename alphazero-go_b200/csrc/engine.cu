@@ -5,6 +5,7 @@
 #include "engine.hpp"
 
 #include <algorithm>
+#include <atomic>
 #include <chrono>
 #include <cmath>
 #include <cstring>
@@ -327,6 +328,7 @@ size_t Weights::bytes_for(const NetShape& s, int precision) {
     c.take(size_t(F) * 4);
     c.take(4);
     c.take(4);
+    c.take(size_t(2 * s.blocks) * sizeof(FusedLayer));   // the fused tower's layer table
     return c.used;
 }
 
@@ -439,6 +441,10 @@ Weights::Weights(const NetShape& s, int precision, int device, const float* para
         o_osc = put(hsc.data(), 4);
         o_osh = put(hsh.data(), 4);
     }
+    // The fused tower's layer table (tensor maps and batch-norm pointers of
+    // the tower convs), filled once the arena's addresses are known.
+    const size_t o_fused = c.take(size_t(2 * s.blocks) * sizeof(FusedLayer));
+    if (c.used > img.size()) throw std::logic_error("azb: weight image layout out of step with bytes_for");
     bytes_ = img.size();
     check(cudaMalloc(&arena_, bytes_), "cudaMalloc weights");
     const cudaError_t e = cudaMemcpy(arena_, img.data(), bytes_, cudaMemcpyHostToDevice);
@@ -466,6 +472,24 @@ Weights::Weights(const NetShape& s, int precision, int device, const float* para
         } else {
             cv.map_w_lo = cv.map_w;
             cv.map_w_lo_pair = cv.map_w_pair;
+        }
+    }
+    if (s.blocks > 0) {
+        std::vector<FusedLayer> table(size_t(2 * s.blocks));
+        for (size_t i = 0; i < table.size(); ++i) {
+            const Conv& cv = convs_[1 + i];
+            table[i].w = cv.map_w;
+            table[i].w_lo = cv.map_w_lo;
+            table[i].scale = cv.scale;
+            table[i].shift = cv.shift;
+        }
+        fused_ = reinterpret_cast<const FusedLayer*>(static_cast<uint8_t*>(arena_) + o_fused);
+        const cudaError_t te = cudaMemcpy(const_cast<FusedLayer*>(fused_), table.data(),
+                                          table.size() * sizeof(FusedLayer), cudaMemcpyHostToDevice);
+        if (te != cudaSuccess) {
+            cudaFree(arena_);
+            arena_ = nullptr;
+            check(te, "upload the fused tower's layer table");
         }
     }
     head_.ld = cpad_;
@@ -502,6 +526,29 @@ Weights::~Weights() {
 }
 
 // -------------------------------------------------------------- workspace
+
+namespace {
+std::atomic<int> g_tower_fused{-1};   // -1 default (on where it applies), 0 off
+}
+
+void set_tower_fused(int mode) { g_tower_fused = mode; }
+
+bool fused_tower_plan(const NetShape& s, int precision, FusedArgs* plan) {
+    const Frame fr(s.board);
+    const int n_out = n_out_for(s.filters);
+    if (s.blocks < 1 || fr.S > 128 || (n_out != 32 && n_out != 64)) return false;
+    FusedArgs a{};
+    a.n = s.board;
+    a.S = fr.S;
+    a.group = 128 / fr.S;
+    a.layers = 2 * s.blocks;
+    a.nch = cpad_for(s.filters, precision) / chunk_channels(precision);
+    a.top = round_up(s.board + 2, 8);
+    a.act_bytes = round_up((a.top + 128 + s.board + 2) * 128, 1024);
+    if (fused_tower_smem(n_out, precision, a.nch, a.act_bytes, a.layers, &a.stages) == 0) return false;
+    *plan = a;
+    return true;
+}
 
 // Floats per board of the heads' feature buffer: the 2A policy features and
 // the A value features, each padded with zeros to a multiple of 4 (16-byte
@@ -572,6 +619,12 @@ void Workspace::place(const Weights& w, uint8_t* base) {
         if (precision == kBF16) emap[i] = make_tensor_map(trunk[i], precision, cpad, rows, 32, 32, 64);
         else emap[i] = make_tensor_map(trunk[i], precision, cpad, rows, 32, 32, 128);
         emap_lo[i] = precision == kTF32x3 ? make_tensor_map(trunk_lo[i], precision, cpad, rows, 32, 32, 128) : emap[i];
+    }
+    fused = fused_tower_plan(s, precision, &fused_plan);
+    if (fused) {
+        const uint32_t box_rows = uint32_t(fused_plan.group * fr.S);
+        fmap = make_tensor_map(trunk[0], precision, cpad, rows, KC, box_rows, 128);
+        fmap_lo = precision == kTF32x3 ? make_tensor_map(trunk_lo[0], precision, cpad, rows, KC, box_rows, 128) : fmap;
     }
 }
 
@@ -674,11 +727,27 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
     // rotating through three frame buffers.
     const int tower_chunks = w.cpad() / chunk_channels(precision);
     int x = 0;
-    for (int i = 0; i < sh.blocks; ++i) {
-        const int mid = (x + 1) % 3, out = (x + 2) % 3;
-        conv(1 + 2 * i, ws.map[x], ws.map_lo[x], mid, -1, 9, tower_chunks, kSlotTower + 2 * i);
-        conv(2 + 2 * i, ws.map[mid], ws.map_lo[mid], out, x, 9, tower_chunks, kSlotTower + 2 * i + 1);
-        x = out;
+    if (ws.fused && g_tower_fused.load() != 0) {
+        // Small boards: the whole tower in one launch, in place on trunk[0].
+        FusedArgs fa = ws.fused_plan;
+        fa.boards = B;
+        fa.layer = w.fused_layers();
+        fa.err = ws.err;
+        const FusedMaps fm{ws.fmap, ws.fmap_lo, ws.fmap, ws.fmap_lo};
+        mark_begin(kSlotTower);
+        check(launch_fused_tower(fm, fa, w.n_out(), precision, dev.sms, s), "fused tower");
+        mark_end(kSlotTower);
+        for (int i = 1; i < 2 * sh.blocks; ++i) {   // the per-conv slots, empty
+            mark_begin(kSlotTower + i);
+            mark_end(kSlotTower + i);
+        }
+    } else {
+        for (int i = 0; i < sh.blocks; ++i) {
+            const int mid = (x + 1) % 3, out = (x + 2) % 3;
+            conv(1 + 2 * i, ws.map[x], ws.map_lo[x], mid, -1, 9, tower_chunks, kSlotTower + 2 * i);
+            conv(2 + 2 * i, ws.map[mid], ws.map_lo[mid], out, x, 9, tower_chunks, kSlotTower + 2 * i + 1);
+            x = out;
+        }
     }
     HeadArgs h = w.head_args();
     h.trunk = ws.trunk[x];

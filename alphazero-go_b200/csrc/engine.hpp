@@ -61,6 +61,13 @@ const DeviceInfo& require_device(int device);   // throws the reason when unusab
 
 const char* precision_name(int precision);
 
+// The fused tower's plan for a shape (boards whose frame rows fit one
+// 128-row tile, 32 or 64 output channels, at least one block; its shared
+// memory fits): false when the per-layer kernels run the tower.
+bool fused_tower_plan(const NetShape& s, int precision, FusedArgs* plan);
+// Test hook: -1 the default (fused where it applies), 0 per-layer kernels always.
+void set_tower_fused(int mode);
+
 // One network's weights on one device, in the kernels' layouts.
 class Weights {
 public:
@@ -88,6 +95,8 @@ public:
     // 0: the stem (one-tap GEMM over the packed operand); 1 + 2*block + (0|1): the tower.
     const Conv& conv(int i) const { return convs_[static_cast<size_t>(i)]; }
     HeadArgs head_args() const { return head_; }   // weights only
+    // The tower convs' table for the fused tower (device memory; null without blocks).
+    const FusedLayer* fused_layers() const { return fused_; }
 
     // Bytes of the device arena for these shapes (the memory checks).
     static size_t bytes_for(const NetShape& s, int precision);
@@ -99,6 +108,7 @@ private:
     void* arena_ = nullptr;
     std::vector<Conv> convs_;
     HeadArgs head_{};
+    const FusedLayer* fused_ = nullptr;
 };
 
 // Activations and outputs for up to max_batch positions.
@@ -133,6 +143,11 @@ public:
     CUtensorMap map[3]{}, map_lo[3]{};
     CUtensorMap emap[3]{};        // the frames in the conv epilogue's {32, 32} boxes (split mode: high planes)
     CUtensorMap emap_lo[3]{};     // split mode: the low planes in the same boxes
+    // The fused tower (small boards): its plan and trunk[0] (its input and
+    // output, in place) in boxes of {chunk, group * S} rows.
+    bool fused = false;
+    FusedArgs fused_plan{};
+    CUtensorMap fmap{}, fmap_lo{};
     CUtensorMap map_stem{}, map_stem_lo{};
 
 private:

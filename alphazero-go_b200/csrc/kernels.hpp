@@ -113,6 +113,43 @@ void set_conv_path(int path);
 // accumulator run per tile.
 void set_conv_segment(int steps);
 
+// The residual tower of a small board in one launch (tower_fused.cu): each
+// CTA keeps a group of whole boards' activations in shared memory through
+// every block. One conv's weights and folded batch norm, in device memory
+// (the kernel reads the tensor maps from there).
+struct FusedLayer {
+    CUtensorMap w, w_lo;   // weight tiles, box {chunk, n_out} (w_lo: the split mode's low plane)
+    const float* scale;    // [n_out]
+    const float* shift;
+    uint8_t pad[48];
+};
+static_assert(sizeof(FusedLayer) % 64 == 0, "tensor maps in device memory are 64-byte aligned");
+
+struct FusedArgs {
+    int n, S;            // board, frame rows per board
+    int boards;          // B
+    int group;           // boards per CTA group: group * S <= 128
+    int layers;          // 2 * blocks
+    int nch;             // 128-byte channel chunks per stored row (cpad / chunk)
+    int top;             // the group's first row in an activation buffer: >= n + 2, a multiple of 8
+    int act_bytes;       // one (plane, chunk) buffer: 1024-aligned, top + 128 + n + 2 rows of 128 bytes
+    int stages;          // weight ring depth (set by the launcher)
+    const FusedLayer* layer;   // [layers]
+    int* err;
+};
+
+// The tower's input (the stem's output) and output frames, boxes of
+// {chunk, group * S} rows, 128-byte swizzle (lo: the split mode's low planes).
+struct FusedMaps {
+    CUtensorMap in, in_lo, out, out_lo;
+};
+
+// Shared memory of a fused launch (0 when it does not fit), and its weight
+// ring depth.
+size_t fused_tower_smem(int n_out, int precision, int nch, int act_bytes, int layers, int* stages, int ctas = 1);
+cudaError_t launch_fused_tower(const FusedMaps& maps, const FusedArgs& a, int n_out, int precision, int sms,
+                               cudaStream_t s);
+
 // The stem's packed operand: the [B][P][A] fp32 input unfolded into frame
 // rows of K = 9*P values (column t*P + p), ld elements apart. The stem conv
 // itself then runs as a one-tap GEMM on the tensor-core kernel.

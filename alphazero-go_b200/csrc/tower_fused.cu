@@ -1,0 +1,472 @@
+// The residual tower of a small board (n <= 10, a board's frame rows fit one
+// 128-row tile) in one launch: each CTA takes a group of whole boards, loads
+// their stem output into shared memory once, runs every conv of every
+// residual block on the resident activations (tcgen05, operands straight
+// from shared memory, accumulators in TMEM), and stores the tower's output
+// once. A 3x3 conv of a board reads only that board's rows and zero padding,
+// so no CTA waits for another, and nothing goes back to HBM between layers:
+// at these sizes the per-layer launch and round trip, not the MMAs, are
+// what a pass costs.
+//
+// The arithmetic is the per-layer kernel's (conv_tc.cu) in the same order:
+// the same K order per MMA accumulator, the split mode's stacked
+// [a_hi.b_hi | a_hi.b_lo + a_lo.b_hi] accumulator per input chunk (its
+// segments), the same epilogue roundings; the outputs are the same bits.
+//
+// Shared memory: two activation buffers (x: a block's input and output, the
+// output written in place over the residual it reads; mid: the block's
+// middle activation), each [plane][chunk] sub-buffers of frame rows x 128
+// bytes in the 128-byte swizzle, the group's rows from row `top` (a multiple
+// of 8, at least n + 2: the zero halo above), zero elsewhere; a
+// ring of weight tiles (one (chunk, tap) tile per stage, both planes).
+//
+// Warps: 0 loads (the group's input, then every layer's weight tiles), 1
+// issues the MMAs and owns TMEM, 2-9 the epilogue (warp w reads TMEM lanes
+// 32(w % 4)...; the two warps of a lane quarter split the output columns).
+#include <algorithm>
+#include <atomic>
+
+#include "kernels.hpp"
+#include "sm100.cuh"
+
+namespace azb {
+
+namespace {
+
+constexpr int kFusedThreads = 320;
+constexpr int kFusedEpiWarps = 8;
+
+template <int N, bool kBf16, bool kSplit>
+struct FusedCfg {
+    static constexpr int kEsz = kBf16 ? 2 : 4;
+    static constexpr int kKc = 128 / kEsz;        // channels per 128-byte chunk
+    static constexpr int kSteps = 4;              // MMAs per chunk and tap (32 bytes of K each)
+    static constexpr int kOps = kSplit ? 2 : 1;   // operand planes
+    static constexpr uint32_t kWTile = uint32_t(N) * 128u;   // one plane of a weight tile
+    static constexpr uint32_t kStage = kOps * kWTile;
+    // Output columns per epilogue warp: halves of N (N = 32: one warp per
+    // lane quarter, the other idle).
+    static constexpr int kWarpCols = N >= 64 ? N / 2 : N;
+    static_assert(N == 32 || N == 64, "the fused tower runs 32 or 64 output channels");
+};
+
+// The TMEM columns a configuration needs: the split mode one stacked
+// accumulator (2N columns) per input chunk, else one of N.
+__host__ __device__ constexpr uint32_t fused_tmem_cols(int n_out, bool split, int nch) {
+    const int cols = split ? 2 * n_out * nch : n_out;
+    return cols <= 32 ? 32u : cols <= 64 ? 64u : cols <= 128 ? 128u : cols <= 256 ? 256u : 512u;
+}
+
+struct FusedSmem {
+    uint8_t* act[2];   // x, mid
+    uint8_t* ring;
+    float* bn;         // every layer's folded batch norm: layer l's scale at l * 2N, shift at l * 2N + N
+    uint64_t *wfull, *wempty, *in_full, *acc_full, *act_ready, *out_done, *done;
+    uint32_t* tmem_slot;
+};
+
+__device__ __forceinline__ FusedSmem fused_carve(uint8_t* raw, const FusedArgs& p, int ops, uint32_t stage_bytes,
+                                             int n_out) {
+    FusedSmem s;
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+    const size_t buf = size_t(ops) * p.nch * p.act_bytes;
+    s.act[0] = base;
+    s.act[1] = base + buf;
+    s.ring = base + 2 * buf;
+    s.bn = reinterpret_cast<float*>(s.ring + size_t(p.stages) * stage_bytes);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(s.bn + size_t(p.layers) * 2 * n_out);
+    s.wfull = bars;
+    s.wempty = bars + p.stages;
+    s.in_full = s.wempty + p.stages;
+    s.acc_full = s.in_full + 1;
+    s.act_ready = s.acc_full + 1;
+    s.out_done = s.act_ready + 1;
+    s.done = s.out_done + 1;
+    s.tmem_slot = reinterpret_cast<uint32_t*>(s.done + 1);
+    return s;
+}
+
+// Byte offset of 16-byte piece u of `row` in a 128-byte-swizzled sub-buffer
+// (as TMA's 128-byte swizzle and the MMA descriptors lay it out; the
+// sub-buffers are 1024-byte aligned).
+__device__ __forceinline__ uint32_t swz(int row, int u) {
+    return uint32_t(row) * 128u + ((uint32_t(u) ^ uint32_t(row & 7)) << 4);
+}
+
+// CTAs per SM: two where the configuration's registers and shared memory
+// allow (one CTA's epilogue then overlaps the other's MMAs), else one.
+template <bool kSplit>
+constexpr int kFusedCtas = kSplit ? 1 : 2;
+
+template <int N, bool kBf16, bool kSplit>
+__global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
+    tower_fused(const __grid_constant__ CUtensorMap mIn, const __grid_constant__ CUtensorMap mInLo,
+                const __grid_constant__ CUtensorMap mOut, const __grid_constant__ CUtensorMap mOutLo,
+                const FusedArgs p) {
+    using C = FusedCfg<N, kBf16, kSplit>;
+    extern __shared__ uint8_t smem_raw[];
+    const FusedSmem sm = fused_carve(smem_raw, p, C::kOps, C::kStage, N);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ngroups = (p.boards + p.group - 1) / p.group;
+    const int group_rows = p.group * p.S;
+    const uint32_t tmem_cols = fused_tmem_cols(N, kSplit, p.nch);
+
+    // Zero both activation buffers: the halos and the rows past the group
+    // stay zero for the whole launch.
+    {
+        const size_t words = 2 * size_t(C::kOps) * p.nch * p.act_bytes / 16;
+        uint4* w = reinterpret_cast<uint4*>(sm.act[0]);
+        for (size_t i = threadIdx.x; i < words; i += blockDim.x) w[i] = make_uint4(0, 0, 0, 0);
+        fence_proxy_async_smem();
+        // Every layer's batch norm into shared memory: the epilogue reads it
+        // on each layer's critical path. (Weights, not activations: no wait
+        // for the previous kernel is needed.)
+        for (int i = threadIdx.x; i < p.layers * 2 * N; i += blockDim.x) {
+            const int l = i / (2 * N), j = i % (2 * N);
+            sm.bn[i] = j < N ? p.layer[l].scale[j] : p.layer[l].shift[j - N];
+        }
+    }
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < p.stages; ++i) {
+            mbar_init(&sm.wfull[i], 1);
+            mbar_init(&sm.wempty[i], 1);
+        }
+        mbar_init(sm.in_full, 1);
+        mbar_init(sm.acc_full, 1);
+        mbar_init(sm.act_ready, kFusedEpiWarps);
+        mbar_init(sm.out_done, 1);
+        mbar_init(sm.done, 1);
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_map(&mIn);
+        tma_prefetch_map(&mOut);
+        if (kSplit) {
+            tma_prefetch_map(&mInLo);
+            tma_prefetch_map(&mOutLo);
+        }
+    }
+    if (warp == 1) tmem_alloc(sm.tmem_slot, tmem_cols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *sm.tmem_slot;
+    grid_dependency_wait();   // the stem's output is read from here on
+    grid_launch_dependents();
+
+    const uint32_t in_tx = uint32_t(group_rows) * 128u * C::kOps * p.nch;
+    if (warp == 0) {
+        // ---------------------------------------------------------- producer
+        if (lane == 0) {
+            Ring rw;
+            uint32_t nw = 0;
+            bool ok = true;
+            uint32_t k = 0;   // groups of this CTA so far
+            for (int g = blockIdx.x; g < ngroups && ok; g += gridDim.x, ++k) {
+                // The previous group's output has been stored (read out of x).
+                if (k > 0 && !(ok = mbar_wait(sm.out_done, (k - 1) & 1, p.err, kErrWaitProducer))) break;
+                mbar_arrive_expect_tx(sm.in_full, in_tx);
+                for (int pl = 0; pl < C::kOps; ++pl)
+                    for (int c = 0; c < p.nch; ++c)
+                        tma_load_2d(pl ? &mInLo : &mIn,
+                                    sm.act[0] + (size_t(pl) * p.nch + c) * p.act_bytes + size_t(p.top) * 128,
+                                    sm.in_full, c * C::kKc, g * group_rows);
+                for (int l = 0; l < p.layers && ok; ++l) {
+                    const FusedLayer& L = p.layer[l];
+                    for (int c = 0; c < p.nch && ok; ++c)
+                        for (int t = 0; t < 9; ++t) {
+                            if (!(ok = mbar_wait(&sm.wempty[rw.idx], rw.phase ^ 1u, p.err, kErrWaitProducer))) break;
+                            mbar_arrive_expect_tx(&sm.wfull[rw.idx], C::kStage);
+                            uint8_t* st = sm.ring + size_t(rw.idx) * C::kStage;
+                            tma_load_2d(&L.w, st, &sm.wfull[rw.idx], (c * 9 + t) * C::kKc, 0);
+                            if (kSplit) tma_load_2d(&L.w_lo, st + C::kWTile, &sm.wfull[rw.idx], (c * 9 + t) * C::kKc, 0);
+                            rw.next(p.stages);
+                            ++nw;
+                        }
+                }
+            }
+            // Every copy issued has landed before the CTA may exit.
+            for (uint32_t s = 0; s < uint32_t(p.stages) && s < nw; ++s) {
+                const uint32_t uses = (nw - s + p.stages - 1) / p.stages;
+                mbar_wait(&sm.wfull[s], (uses - 1) & 1, p.err, kErrWaitDrain);
+            }
+            if (k > 0) mbar_wait(sm.in_full, (k - 1) & 1, p.err, kErrWaitDrain);
+        }
+    } else if (warp == 1) {
+        // --------------------------------------------------------- MMA issue
+        if (lane == 0) {
+            Ring rw;
+            bool ok = true;
+            uint32_t k = 0, layers_done = 0;
+            const uint32_t a0 = smem_u32(sm.act[0]), a1 = smem_u32(sm.act[1]);
+            const uint64_t ring_desc = sw128_desc(smem_u32(sm.ring));
+            constexpr uint32_t kStage16 = C::kStage >> 4, kLo16 = C::kWTile >> 4;
+            const uint32_t plane16 = (uint32_t(p.nch) * uint32_t(p.act_bytes)) >> 4, chunk16 = uint32_t(p.act_bytes) >> 4;
+            // Tap t's view starts (top + dy(n+1) + dx) rows into the buffer
+            // (descriptor units of 16 bytes: 8 per row).
+            const uint32_t centre16 = uint32_t(p.top) * 8u, row16 = uint32_t(p.n + 1) * 8u;
+            for (int g = blockIdx.x; g < ngroups && ok; g += gridDim.x, ++k) {
+                for (int l = 0; l < p.layers && ok; ++l) {
+                    // The previous layer's epilogue has read TMEM and written
+                    // this layer's input; the first layer's input is loaded.
+                    if (layers_done > 0 &&
+                        !(ok = mbar_wait(sm.act_ready, (layers_done - 1) & 1, p.err, kErrWaitMma)))
+                        break;
+                    if (l == 0 && !(ok = mbar_wait(sm.in_full, k & 1, p.err, kErrWaitMma))) break;
+                    tc_fence_after();
+                    const uint64_t a_desc = sw128_desc((l & 1) ? a1 : a0);
+                    for (int c = 0; c < p.nch && ok; ++c) {
+                        const uint64_t ac = a_desc + c * chunk16;
+#pragma unroll
+                        for (int t = 0; t < 9; ++t) {
+                            if (!(ok = mbar_wait(&sm.wfull[rw.idx], rw.phase, p.err, kErrWaitMma))) break;
+                            tc_fence_after();
+                            const uint64_t at = ac + centre16 + (t / 3 - 1) * int(row16) + (t % 3 - 1) * 8,
+                                           bt = ring_desc + rw.idx * kStage16;
+#pragma unroll
+                            for (int kk = 0; kk < C::kSteps; ++kk) {
+                                if constexpr (kSplit) {
+                                    // Per input chunk its own stacked accumulator:
+                                    // [0, N) a_hi.b_hi, [N, 2N) a_hi.b_lo + a_lo.b_hi.
+                                    const uint32_t d = tmem + uint32_t(c) * 2u * N;
+                                    constexpr uint32_t kIdescStack = umma_idesc(2 * N, kBf16);
+                                    umma<kBf16>(d, at + 2 * kk, bt + 2 * kk, kIdescStack, (t | kk) != 0);
+                                    umma<kBf16>(d + N, at + plane16 + 2 * kk, bt + 2 * kk, umma_idesc(N, kBf16), 1);
+                                } else {
+                                    umma<kBf16>(tmem, at + 2 * kk, bt + 2 * kk, umma_idesc(N, kBf16), (c | t | kk) != 0);
+                                }
+                            }
+                            umma_commit(&sm.wempty[rw.idx]);
+                            rw.next(p.stages);
+                        }
+                    }
+                    if (!ok) break;
+                    umma_commit(sm.acc_full);
+                    ++layers_done;
+                }
+            }
+            (void)kLo16;
+            // Every MMA issued is complete before TMEM is freed (also after an error).
+            umma_commit(sm.done);
+            mbar_wait(sm.done, 0, p.err, kErrWaitDrain);
+        }
+    } else {
+        // ---------------------------------------------------------- epilogue
+        const int e = warp - 2, quarter = warp & 3, half = e >> 2;
+        const bool active = N >= 64 || half == 0;
+        const int col0 = half * C::kWarpCols;   // this warp's first output column
+        const int row = quarter * 32 + lane;    // row of the tile (and TMEM lane)
+        const int brow = p.top + row;           // its row in the activation buffers
+        const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16);
+        uint32_t k = 0, layers_done = 0;
+        bool ok = true;
+        for (int g = blockIdx.x; g < ngroups && ok; g += gridDim.x, ++k) {
+            const int boards = min(p.group, p.boards - g * p.group);
+            bool valid = row < boards * p.S;
+            if (valid) {
+                const int r = row % p.S;
+                valid = r >= p.n + 1 && (r % (p.n + 1)) != p.n;
+            }
+            for (int l = 0; l < p.layers && ok; ++l) {
+                if (!(ok = mbar_wait(sm.acc_full, layers_done & 1, p.err, kErrWaitEpilogue))) break;
+                tc_fence_after();
+                uint8_t* out = (l & 1) ? sm.act[0] : sm.act[1];
+                const bool skip = (l & 1) != 0;   // the block's second conv adds its input (x, written in place)
+                if (active) {
+#pragma unroll
+                    for (int cb = 0; cb < C::kWarpCols / 32; ++cb) {
+                        const int c0 = col0 + cb * 32;   // 32 output channels
+                        float acc[32];
+                        if constexpr (kSplit) {
+#pragma unroll 1
+                            for (int c = 0; c < p.nch; ++c) {
+                                uint32_t v[32], w[32];
+                                tmem_ld32(taddr + uint32_t(c) * 2u * N + uint32_t(c0), v);
+                                tmem_ld32(taddr + uint32_t(c) * 2u * N + uint32_t(N + c0), w);
+                                tmem_wait_ld();
+#pragma unroll
+                                for (int i = 0; i < 32; i += 2) {
+                                    const float2 part = fadd2_rn(make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])),
+                                                                 make_float2(__uint_as_float(w[i]), __uint_as_float(w[i + 1])));
+                                    const float2 s2 = c == 0 ? part : fadd2_rn(make_float2(acc[i], acc[i + 1]), part);
+                                    acc[i] = s2.x;
+                                    acc[i + 1] = s2.y;
+                                }
+                            }
+                        } else {
+                            uint32_t v[32];
+                            tmem_ld32(taddr + uint32_t(c0), v);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) acc[i] = __uint_as_float(v[i]);
+                        }
+                        if (valid) {
+                            // Per 16-byte piece: the batch norm, the residual, ReLU, the store
+                            // (the reference's separate roundings, src/cuda/kernels.cu:172-176).
+                            const float4* sc4 = reinterpret_cast<const float4*>(sm.bn + size_t(l) * 2 * N + c0);
+                            const float4* sh4 = reinterpret_cast<const float4*>(sm.bn + size_t(l) * 2 * N + N + c0);
+                            if constexpr (kBf16) {
+                                const int u0 = c0 / 8;   // one 128-byte chunk of 64 channels, 8 per piece
+#pragma unroll
+                                for (int u = 0; u < 4; ++u) {
+                                    float y[8];
+#pragma unroll
+                                    for (int h = 0; h < 2; ++h) {
+                                        const float4 a = sc4[2 * u + h], b = sh4[2 * u + h];
+                                        y[4 * h] = __fadd_rn(__fmul_rn(a.x, acc[8 * u + 4 * h]), b.x);
+                                        y[4 * h + 1] = __fadd_rn(__fmul_rn(a.y, acc[8 * u + 4 * h + 1]), b.y);
+                                        y[4 * h + 2] = __fadd_rn(__fmul_rn(a.z, acc[8 * u + 4 * h + 2]), b.z);
+                                        y[4 * h + 3] = __fadd_rn(__fmul_rn(a.w, acc[8 * u + 4 * h + 3]), b.w);
+                                    }
+                                    uint8_t* at = out + swz(brow, u0 + u);
+                                    if (skip) {
+                                        const uint4 w4 = *reinterpret_cast<const uint4*>(at);
+                                        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&w4);
+#pragma unroll
+                                        for (int q = 0; q < 4; ++q) {
+                                            const float2 f = __bfloat1622float2(h2[q]);
+                                            y[2 * q] = __fadd_rn(y[2 * q], f.x);
+                                            y[2 * q + 1] = __fadd_rn(y[2 * q + 1], f.y);
+                                        }
+                                    }
+                                    uint4 o;
+                                    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+                                    for (int q = 0; q < 4; ++q)
+                                        o2[q] = __floats2bfloat162_rn(y[2 * q] > 0.0f ? y[2 * q] : 0.0f,
+                                                                      y[2 * q + 1] > 0.0f ? y[2 * q + 1] : 0.0f);
+                                    *reinterpret_cast<uint4*>(at) = o;
+                                }
+                            } else {
+                                // fp32: channel block c0 is chunk c0 / 32 (split: both planes).
+                                uint8_t* hi = out + size_t(c0 / 32) * p.act_bytes;
+                                uint8_t* lo = out + (size_t(p.nch) + c0 / 32) * p.act_bytes;
+#pragma unroll
+                                for (int u = 0; u < 8; ++u) {
+                                    const float4 a = sc4[u], b = sh4[u];
+                                    float y[4] = {__fadd_rn(__fmul_rn(a.x, acc[4 * u]), b.x),
+                                                  __fadd_rn(__fmul_rn(a.y, acc[4 * u + 1]), b.y),
+                                                  __fadd_rn(__fmul_rn(a.z, acc[4 * u + 2]), b.z),
+                                                  __fadd_rn(__fmul_rn(a.w, acc[4 * u + 3]), b.w)};
+                                    if (skip) {
+                                        const float4 h = *reinterpret_cast<const float4*>(hi + swz(brow, u));
+                                        float4 r = h;
+                                        if constexpr (kSplit) {
+                                            const float4 l4 = *reinterpret_cast<const float4*>(lo + swz(brow, u));
+                                            r = make_float4(__fadd_rn(h.x, l4.x), __fadd_rn(h.y, l4.y), __fadd_rn(h.z, l4.z),
+                                                            __fadd_rn(h.w, l4.w));
+                                        }
+                                        y[0] = __fadd_rn(y[0], r.x);
+                                        y[1] = __fadd_rn(y[1], r.y);
+                                        y[2] = __fadd_rn(y[2], r.z);
+                                        y[3] = __fadd_rn(y[3], r.w);
+                                    }
+#pragma unroll
+                                    for (int q = 0; q < 4; ++q) y[q] = y[q] > 0.0f ? y[q] : 0.0f;
+                                    if constexpr (kSplit) {
+                                        float4 h, l4;
+                                        h.x = to_tf32(y[0]); l4.x = __fsub_rn(y[0], h.x);
+                                        h.y = to_tf32(y[1]); l4.y = __fsub_rn(y[1], h.y);
+                                        h.z = to_tf32(y[2]); l4.z = __fsub_rn(y[2], h.z);
+                                        h.w = to_tf32(y[3]); l4.w = __fsub_rn(y[3], h.w);
+                                        *reinterpret_cast<float4*>(hi + swz(brow, u)) = h;
+                                        *reinterpret_cast<float4*>(lo + swz(brow, u)) = l4;
+                                    } else {
+                                        *reinterpret_cast<float4*>(hi + swz(brow, u)) = make_float4(y[0], y[1], y[2], y[3]);
+                                    }
+                                }
+                            }
+                        }
+                    }
+                }
+                fence_proxy_async_smem();   // the writes, visible to the next layer's MMAs and the store
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(sm.act_ready);
+                ++layers_done;
+            }
+            if (!ok) break;
+            // The tower's output (x) leaves once every epilogue warp has
+            // written the last layer.
+            if (e == 0 && lane == 0) {
+                if (!(ok = mbar_wait(sm.act_ready, (layers_done - 1) & 1, p.err, kErrWaitEpilogue))) break;
+                for (int pl = 0; pl < C::kOps; ++pl)
+                    for (int c = 0; c < p.nch; ++c)
+                        tma_store_2d(pl ? &mOutLo : &mOut,
+                                     sm.act[0] + (size_t(pl) * p.nch + c) * p.act_bytes + size_t(p.top) * 128,
+                                     c * C::kKc, g * group_rows);
+                bulk_commit();
+                bulk_wait_read<0>();   // x may be overwritten by the next group's input
+                mbar_arrive(sm.out_done);
+            }
+        }
+        if (e == 0 && lane == 0) bulk_wait_all();   // every store complete before the CTA exits
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, tmem_cols);
+    }
+}
+
+template <int N, bool kBf16, bool kSplit>
+cudaError_t launch_fused_one(const FusedMaps& m, FusedArgs a, int sms, cudaStream_t s) {
+    using C = FusedCfg<N, kBf16, kSplit>;
+    const int precision = kBf16 ? kBF16 : (kSplit ? kTF32x3 : kTF32);
+    int ctas = kFusedCtas<kSplit>;
+    size_t smem = fused_tower_smem(N, precision, a.nch, a.act_bytes, a.layers, &a.stages, ctas);
+    if (smem == 0 && ctas > 1) smem = fused_tower_smem(N, precision, a.nch, a.act_bytes, a.layers, &a.stages, ctas = 1);
+    if (smem == 0) return cudaErrorInvalidValue;
+    static std::atomic<size_t> configured{0};
+    if (smem > configured.load()) {
+        const cudaError_t e = cudaFuncSetAttribute(tower_fused<N, kBf16, kSplit>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return e;
+        configured = smem;
+    }
+    const int groups = (a.boards + a.group - 1) / a.group;
+    const int grid = std::max(1, std::min(groups, sms * ctas));
+    (void)sizeof(C);
+    return launch_pdl(tower_fused<N, kBf16, kSplit>, dim3(grid), dim3(kFusedThreads), smem, s, m.in, m.in_lo, m.out,
+                      m.out_lo, a);
+}
+
+} // namespace
+
+size_t fused_tower_smem(int n_out, int precision, int nch, int act_bytes, int layers, int* stages, int ctas) {
+    const int ops = precision == kTF32x3 ? 2 : 1;
+    const size_t acts = 2 * size_t(ops) * nch * act_bytes;
+    const size_t stage = size_t(ops) * n_out * 128;
+    const size_t bn = size_t(layers) * 2 * n_out * 4;
+    // An SM's 228 KB, less 1 KB reserved per CTA, shared by `ctas` CTAs.
+    const size_t kMax = ctas > 1 ? (228 * 1024) / size_t(ctas) - 1024 : 227 * 1024;
+    for (int st = 8; st >= 2; --st) {
+        const size_t total = 1024 + acts + st * stage + bn + (2 * st + 5) * 8 + 16;
+        if (total <= kMax) {
+            if (stages) *stages = st;
+            return total;
+        }
+    }
+    return 0;
+}
+
+cudaError_t launch_fused_tower(const FusedMaps& m, const FusedArgs& a, int n_out, int precision, int sms,
+                               cudaStream_t s) {
+    if (a.boards <= 0 || a.layers <= 0) return cudaSuccess;
+    switch (precision) {
+        case kBF16:
+            return n_out == 32 ? launch_fused_one<32, true, false>(m, a, sms, s)
+                               : n_out == 64 ? launch_fused_one<64, true, false>(m, a, sms, s) : cudaErrorInvalidValue;
+        case kTF32:
+            return n_out == 32 ? launch_fused_one<32, false, false>(m, a, sms, s)
+                               : n_out == 64 ? launch_fused_one<64, false, false>(m, a, sms, s) : cudaErrorInvalidValue;
+        case kTF32x3:
+            return n_out == 32 ? launch_fused_one<32, false, true>(m, a, sms, s)
+                               : n_out == 64 ? launch_fused_one<64, false, true>(m, a, sms, s) : cudaErrorInvalidValue;
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+} // namespace azb

@@ -239,6 +239,12 @@ void azb_probe_set_conv_path(int path);
  * accumulation rounds toward zero at every MMA). -1 the default, 0 one
  * accumulator run per tile (for measurements). */
 void azb_probe_set_conv_segment(int steps);
+/* Boards whose frame rows fit one 128-row tile (n <= 10) with 32 or 64
+ * output channels run the residual tower as one launch, each CTA keeping a
+ * group of boards' activations in shared memory through every block (the
+ * same arithmetic as the per-layer kernels, bit for bit). -1 the default,
+ * 0 the per-layer kernels always. For tests and measurements. */
+void azb_probe_set_tower_fused(int mode);
 /* cuda_probe::binaryVersion / deviceArchitecture / fill (include/azgo/cuda.hpp:93-103). */
 int azb_probe_binary_version(int device);
 int azb_probe_device_architecture(int device);

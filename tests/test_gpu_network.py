@@ -28,7 +28,9 @@ def conv_path(request, engine):
     clusters (M = 256, tcgen05 cta_group::2), and two tiles per CTA sharing
     each weight tile (N <= 128; wider layers fall back to one tile)."""
     engine.cuda_probe.set_conv_path(request.param)
+    engine.cuda_probe.set_tower_fused(0)   # the per-layer kernels, also for small boards
     yield request.param
+    engine.cuda_probe.set_tower_fused(-1)
     engine.cuda_probe.set_conv_path(0)
 
 
