@@ -146,7 +146,8 @@ struct FusedMaps {
 
 // Shared memory of a fused launch (0 when it does not fit), and its weight
 // ring depth.
-size_t fused_tower_smem(int n_out, int precision, int nch, int act_bytes, int layers, int* stages, int ctas = 1);
+size_t fused_tower_smem(int n_out, int precision, int nch, int act_bytes, int layers, int* stages, int ctas = 1,
+                        int taps_per_stage = 1);
 cudaError_t launch_fused_tower(const FusedMaps& maps, const FusedArgs& a, int n_out, int precision, int sms,
                                cudaStream_t s);
 

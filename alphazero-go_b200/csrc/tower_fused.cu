@@ -36,14 +36,19 @@ namespace {
 constexpr int kFusedThreads = 320;
 constexpr int kFusedEpiWarps = 8;
 
-template <int N, bool kBf16, bool kSplit>
+template <int N, bool kBf16, bool kSplit, int kTps = 1>
 struct FusedCfg {
     static constexpr int kEsz = kBf16 ? 2 : 4;
     static constexpr int kKc = 128 / kEsz;        // channels per 128-byte chunk
     static constexpr int kSteps = 4;              // MMAs per chunk and tap (32 bytes of K each)
     static constexpr int kOps = kSplit ? 2 : 1;   // operand planes
     static constexpr uint32_t kWTile = uint32_t(N) * 128u;   // one plane of a weight tile
-    static constexpr uint32_t kStage = kOps * kWTile;
+    static constexpr uint32_t kTap = kOps * kWTile;     // one tap's weight tile, both planes
+    // A ring stage holds kTps consecutive taps' tiles: one wait and one
+    // commit of the MMA thread per kTps taps (each costs the issue loop
+    // about as much as an MMA).
+    static constexpr uint32_t kStage = uint32_t(kTps) * kTap;
+    static_assert(9 % kTps == 0, "taps per stage divide 9");
     // Output columns per epilogue warp: halves of N (N = 32: one warp per
     // lane quarter, the other idle).
     static constexpr int kWarpCols = N >= 64 ? N / 2 : N;
@@ -98,12 +103,12 @@ __device__ __forceinline__ uint32_t swz(int row, int u) {
 template <bool kSplit>
 constexpr int kFusedCtas = kSplit ? 1 : 2;
 
-template <int N, bool kBf16, bool kSplit>
+template <int N, bool kBf16, bool kSplit, int kTps>
 __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
     tower_fused(const __grid_constant__ CUtensorMap mIn, const __grid_constant__ CUtensorMap mInLo,
                 const __grid_constant__ CUtensorMap mOut, const __grid_constant__ CUtensorMap mOutLo,
                 const FusedArgs p) {
-    using C = FusedCfg<N, kBf16, kSplit>;
+    using C = FusedCfg<N, kBf16, kSplit, kTps>;
     extern __shared__ uint8_t smem_raw[];
     const FusedSmem sm = fused_carve(smem_raw, p, C::kOps, C::kStage, N);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -174,12 +179,15 @@ __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
                 for (int l = 0; l < p.layers && ok; ++l) {
                     const FusedLayer& L = p.layer[l];
                     for (int c = 0; c < p.nch && ok; ++c)
-                        for (int t = 0; t < 9; ++t) {
+                        for (int t0 = 0; t0 < 9; t0 += kTps) {
                             if (!(ok = mbar_wait(&sm.wempty[rw.idx], rw.phase ^ 1u, p.err, kErrWaitProducer))) break;
                             mbar_arrive_expect_tx(&sm.wfull[rw.idx], C::kStage);
-                            uint8_t* st = sm.ring + size_t(rw.idx) * C::kStage;
-                            tma_load_2d(&L.w, st, &sm.wfull[rw.idx], (c * 9 + t) * C::kKc, 0);
-                            if (kSplit) tma_load_2d(&L.w_lo, st + C::kWTile, &sm.wfull[rw.idx], (c * 9 + t) * C::kKc, 0);
+                            for (int j = 0; j < kTps; ++j) {
+                                uint8_t* st = sm.ring + size_t(rw.idx) * C::kStage + size_t(j) * C::kTap;
+                                const int x = (c * 9 + t0 + j) * C::kKc;
+                                tma_load_2d(&L.w, st, &sm.wfull[rw.idx], x, 0);
+                                if (kSplit) tma_load_2d(&L.w_lo, st + C::kWTile, &sm.wfull[rw.idx], x, 0);
+                            }
                             rw.next(p.stages);
                             ++nw;
                         }
@@ -200,7 +208,7 @@ __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
             uint32_t k = 0, layers_done = 0;
             const uint32_t a0 = smem_u32(sm.act[0]), a1 = smem_u32(sm.act[1]);
             const uint64_t ring_desc = sw128_desc(smem_u32(sm.ring));
-            constexpr uint32_t kStage16 = C::kStage >> 4, kLo16 = C::kWTile >> 4;
+            constexpr uint32_t kStage16 = C::kStage >> 4, kTap16 = C::kTap >> 4;
             const uint32_t plane16 = (uint32_t(p.nch) * uint32_t(p.act_bytes)) >> 4, chunk16 = uint32_t(p.act_bytes) >> 4;
             // Tap t's view starts (top + dy(n+1) + dx) rows into the buffer
             // (descriptor units of 16 bytes: 8 per row).
@@ -217,12 +225,16 @@ __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
                     const uint64_t a_desc = sw128_desc((l & 1) ? a1 : a0);
                     for (int c = 0; c < p.nch && ok; ++c) {
                         const uint64_t ac = a_desc + c * chunk16;
+                        uint64_t bs = 0;   // the current stage's descriptor
 #pragma unroll
                         for (int t = 0; t < 9; ++t) {
-                            if (!(ok = mbar_wait(&sm.wfull[rw.idx], rw.phase, p.err, kErrWaitMma))) break;
-                            tc_fence_after();
+                            if (t % kTps == 0) {
+                                if (!(ok = mbar_wait(&sm.wfull[rw.idx], rw.phase, p.err, kErrWaitMma))) break;
+                                tc_fence_after();
+                                bs = ring_desc + rw.idx * kStage16;
+                            }
                             const uint64_t at = ac + centre16 + (t / 3 - 1) * int(row16) + (t % 3 - 1) * 8,
-                                           bt = ring_desc + rw.idx * kStage16;
+                                           bt = bs + (t % kTps) * kTap16;
 #pragma unroll
                             for (int kk = 0; kk < C::kSteps; ++kk) {
                                 if constexpr (kSplit) {
@@ -236,8 +248,10 @@ __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
                                     umma<kBf16>(tmem, at + 2 * kk, bt + 2 * kk, umma_idesc(N, kBf16), (c | t | kk) != 0);
                                 }
                             }
-                            umma_commit(&sm.wempty[rw.idx]);
-                            rw.next(p.stages);
+                            if (t % kTps == kTps - 1) {
+                                umma_commit(&sm.wempty[rw.idx]);
+                                rw.next(p.stages);
+                            }
                         }
                     }
                     if (!ok) break;
@@ -245,7 +259,6 @@ __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
                     ++layers_done;
                 }
             }
-            (void)kLo16;
             // Every MMA issued is complete before TMEM is freed (also after an error).
             umma_commit(sm.done);
             mbar_wait(sm.done, 0, p.err, kErrWaitDrain);
@@ -411,34 +424,43 @@ __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
     }
 }
 
-template <int N, bool kBf16, bool kSplit>
-cudaError_t launch_fused_one(const FusedMaps& m, FusedArgs a, int sms, cudaStream_t s) {
-    using C = FusedCfg<N, kBf16, kSplit>;
-    const int precision = kBf16 ? kBF16 : (kSplit ? kTF32x3 : kTF32);
-    int ctas = kFusedCtas<kSplit>;
-    size_t smem = fused_tower_smem(N, precision, a.nch, a.act_bytes, a.layers, &a.stages, ctas);
-    if (smem == 0 && ctas > 1) smem = fused_tower_smem(N, precision, a.nch, a.act_bytes, a.layers, &a.stages, ctas = 1);
-    if (smem == 0) return cudaErrorInvalidValue;
+template <int N, bool kBf16, bool kSplit, int kTps>
+cudaError_t launch_fused_tps(const FusedMaps& m, const FusedArgs& a, size_t smem, int ctas, int sms, cudaStream_t s) {
     static std::atomic<size_t> configured{0};
     if (smem > configured.load()) {
-        const cudaError_t e = cudaFuncSetAttribute(tower_fused<N, kBf16, kSplit>,
+        const cudaError_t e = cudaFuncSetAttribute(tower_fused<N, kBf16, kSplit, kTps>,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
         if (e != cudaSuccess) return e;
         configured = smem;
     }
     const int groups = (a.boards + a.group - 1) / a.group;
     const int grid = std::max(1, std::min(groups, sms * ctas));
-    (void)sizeof(C);
-    return launch_pdl(tower_fused<N, kBf16, kSplit>, dim3(grid), dim3(kFusedThreads), smem, s, m.in, m.in_lo, m.out,
-                      m.out_lo, a);
+    return launch_pdl(tower_fused<N, kBf16, kSplit, kTps>, dim3(grid), dim3(kFusedThreads), smem, s, m.in, m.in_lo,
+                      m.out, m.out_lo, a);
+}
+
+// The shared-memory plan: two CTAs per SM where the configuration allows
+// it, then three taps per ring stage, each with at least two stages.
+template <int N, bool kBf16, bool kSplit>
+cudaError_t launch_fused_one(const FusedMaps& m, FusedArgs a, int sms, cudaStream_t s) {
+    const int precision = kBf16 ? kBF16 : (kSplit ? kTF32x3 : kTF32);
+    for (int ctas = kFusedCtas<kSplit>; ctas >= 1; --ctas)
+        for (int tps : {3, 1}) {
+            const size_t smem = fused_tower_smem(N, precision, a.nch, a.act_bytes, a.layers, &a.stages, ctas, tps);
+            if (smem == 0) continue;
+            return tps == 3 ? launch_fused_tps<N, kBf16, kSplit, 3>(m, a, smem, ctas, sms, s)
+                            : launch_fused_tps<N, kBf16, kSplit, 1>(m, a, smem, ctas, sms, s);
+        }
+    return cudaErrorInvalidValue;
 }
 
 } // namespace
 
-size_t fused_tower_smem(int n_out, int precision, int nch, int act_bytes, int layers, int* stages, int ctas) {
+size_t fused_tower_smem(int n_out, int precision, int nch, int act_bytes, int layers, int* stages, int ctas,
+                        int taps_per_stage) {
     const int ops = precision == kTF32x3 ? 2 : 1;
     const size_t acts = 2 * size_t(ops) * nch * act_bytes;
-    const size_t stage = size_t(ops) * n_out * 128;
+    const size_t stage = size_t(taps_per_stage) * ops * n_out * 128;
     const size_t bn = size_t(layers) * 2 * n_out * 4;
     // An SM's 228 KB, less 1 KB reserved per CTA, shared by `ctas` CTAs.
     const size_t kMax = ctas > 1 ? (228 * 1024) / size_t(ctas) - 1024 : 227 * 1024;
