@@ -962,15 +962,25 @@ Hooks& hooks() {
 
 namespace {
 
-// The completion thread's polling interval (src/cuda/cuda_runner.cu:47-48).
-constexpr int kPollFirstUs = 50, kPollLastUs = 200;
 constexpr size_t kMemoryMargin = size_t(512) << 20;
 
+// The completion thread polls a pass's event as the reference does (every
+// 50 to 200 us, src/cuda/cuda_runner.cu:47-48), but first yields for up to
+// kSpinUs: a small board's pass takes well under 100 us, and a sleep of
+// 50 us (more with the kernel's timer slack) would report it late and leave
+// the GPU idle. (A blocking-sync event woke the thread later still.)
+constexpr int kPollFirstUs = 50, kPollLastUs = 200, kSpinUs = 100;
+
 cudaError_t wait_for(cudaEvent_t event) {
+    const auto start = std::chrono::steady_clock::now();
     int sleep_us = kPollFirstUs;
     for (;;) {
         const cudaError_t e = cudaEventQuery(event);
         if (e != cudaErrorNotReady) return e;
+        if (std::chrono::steady_clock::now() - start < std::chrono::microseconds(kSpinUs)) {
+            std::this_thread::yield();
+            continue;
+        }
         std::this_thread::sleep_for(std::chrono::microseconds(sleep_us));
         sleep_us = std::min(kPollLastUs, 2 * sleep_us);
     }
