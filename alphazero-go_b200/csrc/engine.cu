@@ -328,7 +328,7 @@ size_t Weights::bytes_for(const NetShape& s, int precision) {
     c.take(size_t(F) * 4);
     c.take(4);
     c.take(4);
-    c.take(size_t(2 * s.blocks) * sizeof(FusedLayer));   // the fused tower's layer table
+    c.take(size_t(2 * s.blocks + 1) * sizeof(FusedLayer));   // the fused tower's layer table (+ the stem)
     return c.used;
 }
 
@@ -443,7 +443,7 @@ Weights::Weights(const NetShape& s, int precision, int device, const float* para
     }
     // The fused tower's layer table (tensor maps and batch-norm pointers of
     // the tower convs), filled once the arena's addresses are known.
-    const size_t o_fused = c.take(size_t(2 * s.blocks) * sizeof(FusedLayer));
+    const size_t o_fused = c.take(size_t(2 * s.blocks + 1) * sizeof(FusedLayer));
     if (c.used > img.size()) throw std::logic_error("azb: weight image layout out of step with bytes_for");
     bytes_ = img.size();
     check(cudaMalloc(&arena_, bytes_), "cudaMalloc weights");
@@ -475,9 +475,9 @@ Weights::Weights(const NetShape& s, int precision, int device, const float* para
         }
     }
     if (s.blocks > 0) {
-        std::vector<FusedLayer> table(size_t(2 * s.blocks));
+        std::vector<FusedLayer> table(size_t(2 * s.blocks + 1));   // the tower's convs, then the stem
         for (size_t i = 0; i < table.size(); ++i) {
-            const Conv& cv = convs_[1 + i];
+            const Conv& cv = convs_[i + 1 < table.size() ? 1 + i : 0];
             table[i].w = cv.map_w;
             table[i].w_lo = cv.map_w_lo;
             table[i].scale = cv.scale;
@@ -545,6 +545,10 @@ bool fused_tower_plan(const NetShape& s, int precision, FusedArgs* plan) {
     a.nch = cpad_for(s.filters, precision) / chunk_channels(precision);
     a.top = round_up(s.board + 2, 8);
     a.act_bytes = round_up((a.top + 128 + s.board + 2) * 128, 1024);
+    // The stem joins the launch when its packed operand has as many chunks
+    // as a stored row (it is staged in the mid buffer).
+    const int stem_nch = stem_k_for(s, precision) / chunk_channels(precision);
+    a.stem_nch = stem_nch == a.nch ? stem_nch : 0;
     if (fused_tower_smem(n_out, precision, a.nch, a.act_bytes, a.layers, &a.stages) == 0) return false;
     *plan = a;
     return true;
@@ -625,6 +629,12 @@ void Workspace::place(const Weights& w, uint8_t* base) {
         const uint32_t box_rows = uint32_t(fused_plan.group * fr.S);
         fmap = make_tensor_map(trunk[0], precision, cpad, rows, KC, box_rows, 128);
         fmap_lo = precision == kTF32x3 ? make_tensor_map(trunk_lo[0], precision, cpad, rows, KC, box_rows, 128) : fmap;
+        smap = fmap;
+        smap_lo = fmap_lo;
+        if (fused_plan.stem_nch > 0) {
+            smap = make_tensor_map(stem_in, precision, ks, rows, KC, box_rows, 128);
+            smap_lo = precision == kTF32x3 ? make_tensor_map(stem_in_lo, precision, ks, rows, KC, box_rows, 128) : smap;
+        }
     }
 }
 
@@ -721,19 +731,28 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
         check(launch_conv(m, a, w.n_out(), precision, dev.sms, s), "conv");
         mark_end(timer_slot);
     };
-    // The stem: conv -> BN -> ReLU as one tap over the packed operand.
-    conv(0, ws.map_stem, ws.map_stem_lo, 0, -1, 1, w.kstem() / chunk_channels(precision), kSlotStemGemm);
+    // The stem: conv -> BN -> ReLU as one tap over the packed operand (in
+    // the fused tower's launch when that runs it).
+    const bool fused = ws.fused && g_tower_fused.load() != 0;
+    if (fused && ws.fused_plan.stem_nch > 0) {
+        mark_begin(kSlotStemGemm);
+        mark_end(kSlotStemGemm);
+    } else {
+        conv(0, ws.map_stem, ws.map_stem_lo, 0, -1, 1, w.kstem() / chunk_channels(precision), kSlotStemGemm);
+    }
     // The tower: conv -> BN -> ReLU -> conv -> BN -> + skip -> ReLU per block,
     // rotating through three frame buffers.
     const int tower_chunks = w.cpad() / chunk_channels(precision);
     int x = 0;
-    if (ws.fused && g_tower_fused.load() != 0) {
-        // Small boards: the whole tower in one launch, in place on trunk[0].
+    if (fused) {
+        // Small boards: the whole tower (and the stem, where it fits) in one
+        // launch, in place on trunk[0].
         FusedArgs fa = ws.fused_plan;
         fa.boards = B;
         fa.layer = w.fused_layers();
+        fa.stem = w.fused_layers() + 2 * sh.blocks;
         fa.err = ws.err;
-        const FusedMaps fm{ws.fmap, ws.fmap_lo, ws.fmap, ws.fmap_lo};
+        const FusedMaps fm{ws.fmap, ws.fmap_lo, ws.fmap, ws.fmap_lo, ws.smap, ws.smap_lo};
         mark_begin(kSlotTower);
         check(launch_fused_tower(fm, fa, w.n_out(), precision, dev.sms, s), "fused tower");
         mark_end(kSlotTower);

@@ -148,6 +148,7 @@ public:
     bool fused = false;
     FusedArgs fused_plan{};
     CUtensorMap fmap{}, fmap_lo{};
+    CUtensorMap smap{}, smap_lo{};   // the stem's packed operand in the same boxes (when the stem runs there)
     CUtensorMap map_stem{}, map_stem_lo{};
 
 private:

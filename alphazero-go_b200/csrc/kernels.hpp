@@ -134,14 +134,18 @@ struct FusedArgs {
     int top;             // the group's first row in an activation buffer: >= n + 2, a multiple of 8
     int act_bytes;       // one (plane, chunk) buffer: 1024-aligned, top + 128 + n + 2 rows of 128 bytes
     int stages;          // weight ring depth (set by the launcher)
+    int stem_nch;        // > 0: the stem runs here too, over its packed operand of stem_nch (== nch) chunks
     const FusedLayer* layer;   // [layers]
+    const FusedLayer* stem;    // the stem conv (one tap), when stem_nch > 0
     int* err;
 };
 
 // The tower's input (the stem's output) and output frames, boxes of
-// {chunk, group * S} rows, 128-byte swizzle (lo: the split mode's low planes).
+// {chunk, group * S} rows, 128-byte swizzle (lo: the split mode's low planes);
+// with the stem in the kernel, its packed operand instead of the input.
 struct FusedMaps {
     CUtensorMap in, in_lo, out, out_lo;
+    CUtensorMap stem, stem_lo;   // the stem's packed operand in the same boxes (stem_nch > 0)
 };
 
 // Shared memory of a fused launch (0 when it does not fit), and its weight

@@ -79,7 +79,7 @@ __device__ __forceinline__ FusedSmem fused_carve(uint8_t* raw, const FusedArgs& 
     s.act[1] = base + buf;
     s.ring = base + 2 * buf;
     s.bn = reinterpret_cast<float*>(s.ring + size_t(p.stages) * stage_bytes);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(s.bn + size_t(p.layers) * 2 * n_out);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(s.bn + size_t(p.layers + 1) * 2 * n_out);
     s.wfull = bars;
     s.wempty = bars + p.stages;
     s.in_full = s.wempty + p.stages;
@@ -107,6 +107,7 @@ template <int N, bool kBf16, bool kSplit, int kTps>
 __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
     tower_fused(const __grid_constant__ CUtensorMap mIn, const __grid_constant__ CUtensorMap mInLo,
                 const __grid_constant__ CUtensorMap mOut, const __grid_constant__ CUtensorMap mOutLo,
+                const __grid_constant__ CUtensorMap mStem, const __grid_constant__ CUtensorMap mStemLo,
                 const FusedArgs p) {
     using C = FusedCfg<N, kBf16, kSplit, kTps>;
     extern __shared__ uint8_t smem_raw[];
@@ -126,9 +127,12 @@ __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
         // Every layer's batch norm into shared memory: the epilogue reads it
         // on each layer's critical path. (Weights, not activations: no wait
         // for the previous kernel is needed.)
-        for (int i = threadIdx.x; i < p.layers * 2 * N; i += blockDim.x) {
+        // (the stem's, when it runs here, after the tower's: entry `layers`)
+        const int nbn = (p.layers + (p.stem_nch > 0 ? 1 : 0)) * 2 * N;
+        for (int i = threadIdx.x; i < nbn; i += blockDim.x) {
             const int l = i / (2 * N), j = i % (2 * N);
-            sm.bn[i] = j < N ? p.layer[l].scale[j] : p.layer[l].shift[j - N];
+            const FusedLayer& L = l < p.layers ? p.layer[l] : *p.stem;
+            sm.bn[i] = j < N ? L.scale[j] : L.shift[j - N];
         }
     }
     if (threadIdx.x == 0) {
@@ -159,7 +163,11 @@ __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
     grid_dependency_wait();   // the stem's output is read from here on
     grid_launch_dependents();
 
-    const uint32_t in_tx = uint32_t(group_rows) * 128u * C::kOps * p.nch;
+    // With the stem here, the input is the stem's packed operand (stem_nch
+    // chunks, into mid) and step 0 is the stem (one tap); else the stem's
+    // output (into x). Steps 1.. (or 0..) are the tower's convs.
+    const int first = p.stem_nch > 0 ? 1 : 0, steps = p.layers + first;
+    const uint32_t in_tx = uint32_t(group_rows) * 128u * C::kOps * (first ? p.stem_nch : p.nch);
     if (warp == 0) {
         // ---------------------------------------------------------- producer
         if (lane == 0) {
@@ -172,19 +180,22 @@ __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
                 if (k > 0 && !(ok = mbar_wait(sm.out_done, (k - 1) & 1, p.err, kErrWaitProducer))) break;
                 mbar_arrive_expect_tx(sm.in_full, in_tx);
                 for (int pl = 0; pl < C::kOps; ++pl)
-                    for (int c = 0; c < p.nch; ++c)
-                        tma_load_2d(pl ? &mInLo : &mIn,
-                                    sm.act[0] + (size_t(pl) * p.nch + c) * p.act_bytes + size_t(p.top) * 128,
+                    for (int c = 0; c < (first ? p.stem_nch : p.nch); ++c)
+                        tma_load_2d(first ? (pl ? &mStemLo : &mStem) : (pl ? &mInLo : &mIn),
+                                    sm.act[first] + (size_t(pl) * p.nch + c) * p.act_bytes + size_t(p.top) * 128,
                                     sm.in_full, c * C::kKc, g * group_rows);
-                for (int l = 0; l < p.layers && ok; ++l) {
-                    const FusedLayer& L = p.layer[l];
-                    for (int c = 0; c < p.nch && ok; ++c)
-                        for (int t0 = 0; t0 < 9; t0 += kTps) {
+                for (int st_ = 0; st_ < steps && ok; ++st_) {
+                    const bool stem = st_ < first;
+                    const FusedLayer& L = stem ? *p.stem : p.layer[st_ - first];
+                    // The stem: one tile per chunk (its stage otherwise empty).
+                    const int taps = stem ? 1 : 9, per_stage = stem ? 1 : kTps;
+                    for (int c = 0; c < (stem ? p.stem_nch : p.nch) && ok; ++c)
+                        for (int t0 = 0; t0 < taps; t0 += per_stage) {
                             if (!(ok = mbar_wait(&sm.wempty[rw.idx], rw.phase ^ 1u, p.err, kErrWaitProducer))) break;
-                            mbar_arrive_expect_tx(&sm.wfull[rw.idx], C::kStage);
-                            for (int j = 0; j < kTps; ++j) {
+                            mbar_arrive_expect_tx(&sm.wfull[rw.idx], uint32_t(per_stage) * C::kTap);
+                            for (int j = 0; j < per_stage; ++j) {
                                 uint8_t* st = sm.ring + size_t(rw.idx) * C::kStage + size_t(j) * C::kTap;
-                                const int x = (c * 9 + t0 + j) * C::kKc;
+                                const int x = (c * taps + t0 + j) * C::kKc;
                                 tma_load_2d(&L.w, st, &sm.wfull[rw.idx], x, 0);
                                 if (kSplit) tma_load_2d(&L.w_lo, st + C::kWTile, &sm.wfull[rw.idx], x, 0);
                             }
@@ -214,14 +225,40 @@ __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
             // (descriptor units of 16 bytes: 8 per row).
             const uint32_t centre16 = uint32_t(p.top) * 8u, row16 = uint32_t(p.n + 1) * 8u;
             for (int g = blockIdx.x; g < ngroups && ok; g += gridDim.x, ++k) {
-                for (int l = 0; l < p.layers && ok; ++l) {
+                for (int st_ = 0; st_ < steps && ok; ++st_) {
                     // The previous layer's epilogue has read TMEM and written
                     // this layer's input; the first layer's input is loaded.
                     if (layers_done > 0 &&
                         !(ok = mbar_wait(sm.act_ready, (layers_done - 1) & 1, p.err, kErrWaitMma)))
                         break;
-                    if (l == 0 && !(ok = mbar_wait(sm.in_full, k & 1, p.err, kErrWaitMma))) break;
+                    if (st_ == 0 && !(ok = mbar_wait(sm.in_full, k & 1, p.err, kErrWaitMma))) break;
                     tc_fence_after();
+                    if (st_ < first) {
+                        // The stem: a one-tap GEMM over the packed operand in mid.
+                        for (int c = 0; c < p.stem_nch && ok; ++c) {
+                            if (!(ok = mbar_wait(&sm.wfull[rw.idx], rw.phase, p.err, kErrWaitMma))) break;
+                            tc_fence_after();
+                            const uint64_t at = sw128_desc(a1) + c * chunk16 + centre16, bt = ring_desc + rw.idx * kStage16;
+#pragma unroll
+                            for (int kk = 0; kk < C::kSteps; ++kk) {
+                                if constexpr (kSplit) {
+                                    const uint32_t d = tmem + uint32_t(c) * 2u * N;
+                                    constexpr uint32_t kIdescStack = umma_idesc(2 * N, kBf16);
+                                    umma<kBf16>(d, at + 2 * kk, bt + 2 * kk, kIdescStack, kk != 0);
+                                    umma<kBf16>(d + N, at + plane16 + 2 * kk, bt + 2 * kk, umma_idesc(N, kBf16), 1);
+                                } else {
+                                    umma<kBf16>(tmem, at + 2 * kk, bt + 2 * kk, umma_idesc(N, kBf16), (c | kk) != 0);
+                                }
+                            }
+                            umma_commit(&sm.wempty[rw.idx]);
+                            rw.next(p.stages);
+                        }
+                        if (!ok) break;
+                        umma_commit(sm.acc_full);
+                        ++layers_done;
+                        continue;
+                    }
+                    const int l = st_ - first;
                     const uint64_t a_desc = sw128_desc((l & 1) ? a1 : a0);
                     for (int c = 0; c < p.nch && ok; ++c) {
                         const uint64_t ac = a_desc + c * chunk16;
@@ -280,11 +317,13 @@ __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
                 const int r = row % p.S;
                 valid = r >= p.n + 1 && (r % (p.n + 1)) != p.n;
             }
-            for (int l = 0; l < p.layers && ok; ++l) {
+            for (int st_ = 0; st_ < steps && ok; ++st_) {
                 if (!(ok = mbar_wait(sm.acc_full, layers_done & 1, p.err, kErrWaitEpilogue))) break;
                 tc_fence_after();
-                uint8_t* out = (l & 1) ? sm.act[0] : sm.act[1];
-                const bool skip = (l & 1) != 0;   // the block's second conv adds its input (x, written in place)
+                const bool stem = st_ < first;
+                const int l = stem ? p.layers : st_ - first;   // the batch norm's entry
+                uint8_t* out = stem || (l & 1) ? sm.act[0] : sm.act[1];
+                const bool skip = !stem && (l & 1) != 0;   // the block's second conv adds its input (x, written in place)
                 if (active) {
 #pragma unroll
                     for (int cb = 0; cb < C::kWarpCols / 32; ++cb) {
@@ -436,7 +475,7 @@ cudaError_t launch_fused_tps(const FusedMaps& m, const FusedArgs& a, size_t smem
     const int groups = (a.boards + a.group - 1) / a.group;
     const int grid = std::max(1, std::min(groups, sms * ctas));
     return launch_pdl(tower_fused<N, kBf16, kSplit, kTps>, dim3(grid), dim3(kFusedThreads), smem, s, m.in, m.in_lo,
-                      m.out, m.out_lo, a);
+                      m.out, m.out_lo, m.stem, m.stem_lo, a);
 }
 
 // The shared-memory plan: two CTAs per SM where the configuration allows
@@ -461,7 +500,7 @@ size_t fused_tower_smem(int n_out, int precision, int nch, int act_bytes, int la
     const int ops = precision == kTF32x3 ? 2 : 1;
     const size_t acts = 2 * size_t(ops) * nch * act_bytes;
     const size_t stage = size_t(taps_per_stage) * ops * n_out * 128;
-    const size_t bn = size_t(layers) * 2 * n_out * 4;
+    const size_t bn = size_t(layers + 1) * 2 * n_out * 4;   // the tower's convs and the stem
     // An SM's 228 KB, less 1 KB reserved per CTA, shared by `ctas` CTAs.
     const size_t kMax = ctas > 1 ? (228 * 1024) / size_t(ctas) - 1024 : 227 * 1024;
     for (int st = 8; st >= 2; --st) {
