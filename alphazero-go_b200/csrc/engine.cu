@@ -742,6 +742,17 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
     }
     // The tower: conv -> BN -> ReLU -> conv -> BN -> + skip -> ReLU per block,
     // rotating through three frame buffers.
+    HeadArgs h = w.head_args();
+    h.B = B;
+    h.logits = ws.logits;
+    h.values = ws.values;
+    h.ownership_out = ws.ownership;
+    h.probs = probs ? ws.probs : nullptr;
+    h.feat = ws.feat;
+    h.feat_val = int((2 * size_t(sh.area()) + 3) / 4 * 4);
+    h.feat_ld = int(feat_floats(sh));
+    h.hid = ws.hid;
+    h.err = ws.err;
     const int tower_chunks = w.cpad() / chunk_channels(precision);
     int x = 0;
     if (fused) {
@@ -751,6 +762,8 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
         fa.boards = B;
         fa.layer = w.fused_layers();
         fa.stem = w.fused_layers() + 2 * sh.blocks;
+        fa.heads = 1;   // the heads' 1x1 convolutions from the resident trunk; no trunk is stored
+        fa.head = h;
         fa.err = ws.err;
         const FusedMaps fm{ws.fmap, ws.fmap_lo, ws.fmap, ws.fmap_lo, ws.smap, ws.smap_lo};
         mark_begin(kSlotTower);
@@ -768,21 +781,10 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
             x = out;
         }
     }
-    HeadArgs h = w.head_args();
     h.trunk = ws.trunk[x];
     h.trunk_lo = ws.trunk_lo[x];
-    h.B = B;
-    h.logits = ws.logits;
-    h.values = ws.values;
-    h.ownership_out = ws.ownership;
-    h.probs = probs ? ws.probs : nullptr;
-    h.feat = ws.feat;
-    h.feat_val = int((2 * size_t(sh.area()) + 3) / 4 * 4);
-    h.feat_ld = int(feat_floats(sh));
-    h.hid = ws.hid;
-    h.err = ws.err;
     mark_begin(kSlotHeadConv);
-    check(launch_head_conv(h, precision, dev.sms, s), "head convolutions");
+    if (!fused) check(launch_head_conv(h, precision, dev.sms, s), "head convolutions");   // fused: done in the tower
     mark_end(kSlotHeadConv);
     mark_begin(kSlotHeadFc);
     check(launch_head_fc(h, s), "head FC");

@@ -113,48 +113,6 @@ void set_conv_path(int path);
 // accumulator run per tile.
 void set_conv_segment(int steps);
 
-// The residual tower of a small board in one launch (tower_fused.cu): each
-// CTA keeps a group of whole boards' activations in shared memory through
-// every block. One conv's weights and folded batch norm, in device memory
-// (the kernel reads the tensor maps from there).
-struct FusedLayer {
-    CUtensorMap w, w_lo;   // weight tiles, box {chunk, n_out} (w_lo: the split mode's low plane)
-    const float* scale;    // [n_out]
-    const float* shift;
-    uint8_t pad[48];
-};
-static_assert(sizeof(FusedLayer) % 64 == 0, "tensor maps in device memory are 64-byte aligned");
-
-struct FusedArgs {
-    int n, S;            // board, frame rows per board
-    int boards;          // B
-    int group;           // boards per CTA group: group * S <= 128
-    int layers;          // 2 * blocks
-    int nch;             // 128-byte channel chunks per stored row (cpad / chunk)
-    int top;             // the group's first row in an activation buffer: >= n + 2, a multiple of 8
-    int act_bytes;       // one (plane, chunk) buffer: 1024-aligned, top + 128 + n + 2 rows of 128 bytes
-    int stages;          // weight ring depth (set by the launcher)
-    int stem_nch;        // > 0: the stem runs here too, over its packed operand of stem_nch (== nch) chunks
-    const FusedLayer* layer;   // [layers]
-    const FusedLayer* stem;    // the stem conv (one tap), when stem_nch > 0
-    int* err;
-};
-
-// The tower's input (the stem's output) and output frames, boxes of
-// {chunk, group * S} rows, 128-byte swizzle (lo: the split mode's low planes);
-// with the stem in the kernel, its packed operand instead of the input.
-struct FusedMaps {
-    CUtensorMap in, in_lo, out, out_lo;
-    CUtensorMap stem, stem_lo;   // the stem's packed operand in the same boxes (stem_nch > 0)
-};
-
-// Shared memory of a fused launch (0 when it does not fit), and its weight
-// ring depth.
-size_t fused_tower_smem(int n_out, int precision, int nch, int act_bytes, int layers, int* stages, int ctas = 1,
-                        int taps_per_stage = 1);
-cudaError_t launch_fused_tower(const FusedMaps& maps, const FusedArgs& a, int n_out, int precision, int sms,
-                               cudaStream_t s);
-
 // The stem's packed operand: the [B][P][A] fp32 input unfolded into frame
 // rows of K = 9*P values (column t*P + p), ld elements apart. The stem conv
 // itself then runs as a one-tap GEMM on the tensor-core kernel.
@@ -206,6 +164,51 @@ struct HeadArgs {
     int* err;           // kernel error word (a bounded wait that ran out)
 };
 cudaError_t launch_head_conv(const HeadArgs& a, int precision, int sms, cudaStream_t s);   // 1x1 convs -> feat
+
+// The residual tower of a small board in one launch (tower_fused.cu): each
+// CTA keeps a group of whole boards' activations in shared memory through
+// every block. One conv's weights and folded batch norm, in device memory
+// (the kernel reads the tensor maps from there).
+struct FusedLayer {
+    CUtensorMap w, w_lo;   // weight tiles, box {chunk, n_out} (w_lo: the split mode's low plane)
+    const float* scale;    // [n_out]
+    const float* shift;
+    uint8_t pad[48];
+};
+static_assert(sizeof(FusedLayer) % 64 == 0, "tensor maps in device memory are 64-byte aligned");
+
+struct FusedArgs {
+    int n, S;            // board, frame rows per board
+    int boards;          // B
+    int group;           // boards per CTA group: group * S <= 128
+    int layers;          // 2 * blocks
+    int nch;             // 128-byte channel chunks per stored row (cpad / chunk)
+    int top;             // the group's first row in an activation buffer: >= n + 2, a multiple of 8
+    int act_bytes;       // one (plane, chunk) buffer: 1024-aligned, top + 128 + n + 2 rows of 128 bytes
+    int stages;          // weight ring depth (set by the launcher)
+    int stem_nch;        // > 0: the stem runs here too, over its packed operand of stem_nch (== nch) chunks
+    const FusedLayer* layer;   // [layers]
+    const FusedLayer* stem;    // the stem conv (one tap), when stem_nch > 0
+    int heads;           // 1: the heads' 1x1 convolutions run here too (into head.feat), and no trunk is stored
+    HeadArgs head;
+    int* err;
+};
+
+// The tower's input (the stem's output) and output frames, boxes of
+// {chunk, group * S} rows, 128-byte swizzle (lo: the split mode's low planes);
+// with the stem in the kernel, its packed operand instead of the input.
+struct FusedMaps {
+    CUtensorMap in, in_lo, out, out_lo;
+    CUtensorMap stem, stem_lo;   // the stem's packed operand in the same boxes (stem_nch > 0)
+};
+
+// Shared memory of a fused launch (0 when it does not fit), and its weight
+// ring depth.
+size_t fused_tower_smem(int n_out, int precision, int nch, int act_bytes, int layers, int* stages, int ctas = 1,
+                        int taps_per_stage = 1);
+cudaError_t launch_fused_tower(const FusedMaps& maps, const FusedArgs& a, int n_out, int precision, int sms,
+                               cudaStream_t s);
+
 cudaError_t launch_head_fc(const HeadArgs& a, cudaStream_t s);                            // feat -> logits, hid
 cudaError_t launch_head_out(const HeadArgs& a, cudaStream_t s);                           // hid -> value; softmax
 

@@ -3,6 +3,7 @@
 #include <algorithm>
 #include <atomic>
 
+#include "head_rows.cuh"
 #include "kernels.hpp"
 #include "sm100.cuh"
 
@@ -164,30 +165,6 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
-// One 16-byte piece of a trunk row (and, split mode, of its low plane) as
-// floats: 8 bf16 or 4 fp32 channels; split mode adds hi + lo (one rounding).
-template <int kMode>
-struct TrunkPiece {
-    static constexpr int kWidth = kMode == kBF16 ? 8 : 4;
-    uint4 hi, lo;
-    __device__ __forceinline__ void values(float* f) const {
-        if (kMode == kBF16) {
-            const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&hi);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float2 t = __bfloat1622float2(h2[e]);
-                f[2 * e] = t.x;
-                f[2 * e + 1] = t.y;
-            }
-        } else {
-            const float* h = reinterpret_cast<const float*>(&hi);
-            const float* l = reinterpret_cast<const float*>(&lo);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) f[e] = kMode == kTF32x3 ? __fadd_rn(h[e], l[e]) : h[e];
-        }
-    }
-};
-
 // The trunk streamed once through shared memory. A copy thread (warp 8)
 // stages `kbr` board rows at a time into a ring of `stages` buffers: the n
 // real points of a board row are n consecutive frame rows, one bulk copy
@@ -205,27 +182,13 @@ struct TrunkPiece {
 constexpr int kHcReaders = 16;
 constexpr int kHcThreads = 32 * (kHcReaders + 1);
 
-// v / n for v >= 0 and n <= 19: below 2^20 with a float reciprocal ((v +
-// 0.5)/n stays at least 0.5/n away from the integers, above the float
-// error there), else by integer division.
-__device__ __forceinline__ int div_small(int v, int n, float inv_n) {
-    return v < (1 << 20) ? int((float(v) + 0.5f) * inv_n) : v / n;
-}
-constexpr int kHcSlots = 4;
 
 template <int kMode, int kLpr, int kNch>
 __global__ void __launch_bounds__(kHcThreads, 1)
     head_conv_kernel(const HeadArgs a, int stages, int kbr, uint32_t row_bytes) {
     extern __shared__ uint8_t hc_raw[];
-    constexpr int W = TrunkPiece<kMode>::kWidth, kC = kNch * W;
-    constexpr int kGroups = 32 / kLpr;                  // rows a warp holds per slot
-    constexpr int kStepRows = kHcSlots * kGroups;       // rows per warp step
-    constexpr int kLog = kLpr == 32 ? 5 : kLpr == 16 ? 4 : 3;
-    constexpr int kScatter = kLog < 4 ? kLog : 4;       // steps that halve the 16 sums
-    constexpr int kBfly = kLog - kScatter;              // butterfly steps after them
-    constexpr int kOwn = (kHcSlots * 4) >> kScatter;    // finished sums per lane
     constexpr uint32_t kPlanes = kMode == kTF32x3 ? 2u : 1u;
-    const int n = a.n, A = a.A, board_rows = a.B * n;
+    const int n = a.n, board_rows = a.B * n;
     const int nblk = (board_rows + kbr - 1) / kbr;
     const uint32_t br_bytes = uint32_t(n) * row_bytes;              // one board row, one plane
     const uint32_t plane_bytes = uint32_t(kbr) * br_bytes;          // one stage, one plane
@@ -276,96 +239,30 @@ __global__ void __launch_bounds__(kHcThreads, 1)
     }
 
     // ----------------------------------------------------------- readers
-    const int l = lane % kLpr, grp = lane / kLpr;
-    float w[4][kC];
-#pragma unroll
-    for (int j = 0; j < kNch; ++j)
-#pragma unroll
-        for (int e = 0; e < W; ++e) {
-            const int ch = (l + j * kLpr) * W + e, i = j * W + e;
-            const bool real = ch < a.F;
-            w[0][i] = real ? __ldg(a.pol_w + ch) : 0.0f;
-            w[1][i] = real ? __ldg(a.pol_w + a.F + ch) : 0.0f;
-            w[2][i] = real ? __ldg(a.val_w + ch) : 0.0f;
-            w[3][i] = real && a.ownership ? __ldg(a.own_w + ch) : 0.0f;
-        }
-    // The batch norm of the sums this lane finishes (head k % 4 of its sums
-    // k = (l >> kBfly) * kOwn + j), the same for every step.
-    float bn_scale[kOwn], bn_shift[kOwn];
-#pragma unroll
-    for (int j = 0; j < kOwn; ++j) {
-        const int h = (((l >> kBfly) * kOwn) + j) % 4;
-        bn_scale[j] = h == 0 ? __ldg(a.pol_scale) : h == 1 ? __ldg(a.pol_scale + 1) : h == 2 ? __ldg(a.val_scale)
-                                                                                   : (a.ownership ? __ldg(a.own_scale) : 0.0f);
-        bn_shift[j] = h == 0 ? __ldg(a.pol_shift) : h == 1 ? __ldg(a.pol_shift + 1) : h == 2 ? __ldg(a.val_shift)
-                                                                                   : (a.ownership ? __ldg(a.own_shift) : 0.0f);
-    }
-    const bool writer = (l & ((1 << kBfly) - 1)) == 0;
+    HeadLane<kMode, kLpr, kNch> hl;
+    hl.load(a, lane);
     const float inv_n = 1.0f / float(n);
     Ring r;
     for (int blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
         if (!mbar_wait(&full[r.idx], r.phase, a.err, kErrWaitHeadData)) break;
         const uint8_t* stage = buf + size_t(r.idx) * kPlanes * plane_bytes;
         const int first = blk * kbr, rows = min(kbr, board_rows - first) * n;
-        for (int base = warp * kStepRows; base < rows; base += kHcReaders * kStepRows) {
-            float acc[kHcSlots * 4];
-#pragma unroll
-            for (int s = 0; s < kHcSlots; ++s) {
-                const int row = base + s * kGroups + grp;
-                float z[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                if (row < rows) {
-#pragma unroll
-                    for (int j = 0; j < kNch; ++j) {
-                        const uint32_t off = uint32_t(row) * row_bytes + uint32_t(l + j * kLpr) * 16u;
-                        TrunkPiece<kMode> piece;
-                        piece.hi = *reinterpret_cast<const uint4*>(stage + off);
-                        if (kMode == kTF32x3) piece.lo = *reinterpret_cast<const uint4*>(stage + plane_bytes + off);
-                        float f[W];
-                        piece.values(f);
-#pragma unroll
-                        for (int e = 0; e < W; ++e)
-#pragma unroll
-                            for (int h = 0; h < 4; ++h) z[h] = fmaf(w[h][j * W + e], f[e], z[h]);
-                    }
-                }
-#pragma unroll
-                for (int h = 0; h < 4; ++h) acc[s * 4 + h] = z[h];
-            }
-            // Reduce-scatter over the high lane bits of the group while there
-            // is more than one sum to split, then a butterfly over the rest.
-#pragma unroll
-            for (int t = 0; t < kLog; ++t) {
-                const int off = kLpr >> (t + 1);
-                if (t < kScatter) {
-                    const int half = (kHcSlots * 2) >> t;
-                    const bool upper = (lane & off) != 0;
-#pragma unroll
-                    for (int k = 0; k < half; ++k) {
-                        const float send = upper ? acc[k] : acc[k + half];
-                        const float keep = upper ? acc[k + half] : acc[k];
-                        acc[k] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-                    }
-                } else {
-                    acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], off);
-                }
-            }
-            if (writer) {
-#pragma unroll
-                for (int j = 0; j < kOwn; ++j) {
-                    const int k = (l >> kBfly) * kOwn + j, s = k / 4, h = k % 4;
-                    const int row = base + s * kGroups + grp;
-                    if (row >= rows) continue;
-                    const int rq = div_small(row, n, inv_n), br = first + rq, x = row - rq * n;
-                    const int b = div_small(br, n, inv_n), p = (br - b * n) * n + x;
-                    const float y = __fadd_rn(__fmul_rn(bn_scale[j], acc[j]), bn_shift[j]);
-                    if (h < 3) {
-                        a.feat[size_t(b) * a.feat_ld + (h == 2 ? a.feat_val : h * A) + p] = y > 0.0f ? y : 0.0f;
-                    } else if (a.ownership && a.ownership_out) {
-                        a.ownership_out[size_t(b) * A + p] = tanhf(y);
-                    }
-                }
-            }
-        }
+        // Staged row `row` (the points of board rows first.., n per board row).
+        auto piece = [&](int row, int j) {
+            TrunkPiece<kMode> pc;
+            const uint32_t off = uint32_t(row) * row_bytes + uint32_t(j) * 16u;
+            pc.hi = *reinterpret_cast<const uint4*>(stage + off);
+            if (kMode == kTF32x3) pc.lo = *reinterpret_cast<const uint4*>(stage + plane_bytes + off);
+            return pc;
+        };
+        auto where = [&](int row, int* b, int* p) {
+            const int rq = div_small(row, n, inv_n), br = first + rq, x = row - rq * n;
+            *b = div_small(br, n, inv_n);
+            *p = (br - *b * n) * n + x;
+        };
+        for (int base = warp * HeadLane<kMode, kLpr, kNch>::kStepRows; base < rows;
+             base += kHcReaders * HeadLane<kMode, kLpr, kNch>::kStepRows)
+            hl.step(a, base, rows, piece, where, lane);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[r.idx]);
         r.next(uint32_t(stages));

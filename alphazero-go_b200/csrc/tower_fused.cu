@@ -26,6 +26,7 @@
 #include <algorithm>
 #include <atomic>
 
+#include "head_rows.cuh"
 #include "kernels.hpp"
 #include "sm100.cuh"
 
@@ -108,7 +109,7 @@ __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
     tower_fused(const __grid_constant__ CUtensorMap mIn, const __grid_constant__ CUtensorMap mInLo,
                 const __grid_constant__ CUtensorMap mOut, const __grid_constant__ CUtensorMap mOutLo,
                 const __grid_constant__ CUtensorMap mStem, const __grid_constant__ CUtensorMap mStemLo,
-                const FusedArgs p) {
+                const __grid_constant__ FusedArgs p) {
     using C = FusedCfg<N, kBf16, kSplit, kTps>;
     extern __shared__ uint8_t smem_raw[];
     const FusedSmem sm = fused_carve(smem_raw, p, C::kOps, C::kStage, N);
@@ -143,7 +144,7 @@ __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
         mbar_init(sm.in_full, 1);
         mbar_init(sm.acc_full, 1);
         mbar_init(sm.act_ready, kFusedEpiWarps);
-        mbar_init(sm.out_done, 1);
+        mbar_init(sm.out_done, p.heads ? kFusedEpiWarps : 1);   // heads: every epilogue warp reads x
         mbar_init(sm.done, 1);
         fence_barrier_init();
     }
@@ -438,9 +439,39 @@ __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
                 ++layers_done;
             }
             if (!ok) break;
-            // The tower's output (x) leaves once every epilogue warp has
-            // written the last layer.
-            if (e == 0 && lane == 0) {
+            if (p.heads) {
+                // The heads' 1x1 convolutions straight from x, with the head
+                // kernel's lane split and reduction tree (the same bits),
+                // once every epilogue warp has written the last layer.
+                if (!(ok = mbar_wait(sm.act_ready, (layers_done - 1) & 1, p.err, kErrWaitEpilogue))) break;
+                constexpr int kMode = kBf16 ? kBF16 : (kSplit ? kTF32x3 : kTF32);
+                constexpr int kLpr = kBf16 || N == 32 ? 8 : 16;   // 16-byte pieces per stored row
+                using H = HeadLane<kMode, kLpr, 1>;
+                H hl;
+                hl.load(p.head, lane);
+                const int A = p.n * p.n, pts = boards * A, n = p.n, S = p.S, top = p.top;
+                const int first_board = g * p.group;
+                const size_t act_bytes = size_t(p.act_bytes), lo_off = size_t(p.nch) * act_bytes;
+                const uint8_t* xbuf = sm.act[0];
+                auto piece = [=](int pt, int j) {   // point pt of the group: its row in x
+                    const int b = pt / A, q = pt - b * A, y = q / n, xx = q - y * n;
+                    const int brow = top + b * S + (y + 1) * (n + 1) + xx, c = j >> 3, u = j & 7;
+                    TrunkPiece<kMode> pc;
+                    pc.hi = *reinterpret_cast<const uint4*>(xbuf + size_t(c) * act_bytes + swz(brow, u));
+                    if (kSplit) pc.lo = *reinterpret_cast<const uint4*>(xbuf + lo_off + size_t(c) * act_bytes + swz(brow, u));
+                    return pc;
+                };
+                auto where = [=](int pt, int* b, int* q) {
+                    *b = first_board + pt / A;
+                    *q = pt % A;
+                };
+                for (int base = e * H::kStepRows; base < pts; base += kFusedEpiWarps * H::kStepRows)
+                    hl.step(p.head, base, pts, piece, where, lane);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(sm.out_done);   // x may be overwritten by the next group's input
+            } else if (e == 0 && lane == 0) {
+                // The tower's output (x) leaves once every epilogue warp has
+                // written the last layer.
                 if (!(ok = mbar_wait(sm.act_ready, (layers_done - 1) & 1, p.err, kErrWaitEpilogue))) break;
                 for (int pl = 0; pl < C::kOps; ++pl)
                     for (int c = 0; c < p.nch; ++c)

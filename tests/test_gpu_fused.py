@@ -26,7 +26,8 @@ def _run(engine, c, params, buffers, x, precision, fused):
 
 @pytest.mark.parametrize("precision", ["bf16", "tf32x3", "tf32"])
 @pytest.mark.parametrize("shape,B", [((5, 4, 32, 1, False), 7), ((9, 6, 64, 1, False), 64), ((9, 2, 16, 8, True), 5),
-                                     ((7, 3, 64, 2, True), 33), ((9, 1, 64, 1, False), 400), ((5, 2, 48, 1, False), 1)])
+                                     ((7, 3, 64, 2, True), 33), ((9, 1, 64, 1, False), 400), ((5, 2, 48, 1, False), 1),
+                                     ((10, 2, 64, 1, True), 13)])
 def test_fused_tower_equals_per_layer(engine, oracle, precision, shape, B):
     O = oracle
     n, blocks, filters, history, own = shape
