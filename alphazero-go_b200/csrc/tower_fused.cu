@@ -1,12 +1,13 @@
 // The residual tower of a small board (n <= 10, a board's frame rows fit one
 // 128-row tile) in one launch: each CTA takes a group of whole boards, loads
-// their stem output into shared memory once, runs every conv of every
-// residual block on the resident activations (tcgen05, operands straight
-// from shared memory, accumulators in TMEM), and stores the tower's output
-// once. A 3x3 conv of a board reads only that board's rows and zero padding,
-// so no CTA waits for another, and nothing goes back to HBM between layers:
-// at these sizes the per-layer launch and round trip, not the MMAs, are
-// what a pass costs.
+// their stem operand (or, where it does not fit, the stem's output) into
+// shared memory once, runs the stem and every conv of every residual block
+// on the resident activations (tcgen05, operands straight from shared
+// memory, accumulators in TMEM), then the heads' 1x1 convolutions on the
+// resident trunk (or stores the trunk, for the head kernel). A 3x3 conv of a
+// board reads only that board's rows and zero padding, so no CTA waits for
+// another, and nothing goes back to HBM between layers: at these sizes the
+// per-layer launch and round trip, not the MMAs, are what a pass costs.
 //
 // The arithmetic is the per-layer kernel's (conv_tc.cu) in the same order:
 // the same K order per MMA accumulator, the split mode's stacked
