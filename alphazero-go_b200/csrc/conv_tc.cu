@@ -353,7 +353,7 @@ __device__ __forceinline__ void store_epilogue_tma(const ConvArgs& p, const floa
 // rows are stored as zeros (they must stay zero); rows past the frame are
 // clipped by TMA.
 template <int N, int kMine>
-__device__ __forceinline__ void store_split_sums(const ConvArgs& p, const float* bn, const float (&sum)[kMine * 32],
+__device__ __forceinline__ void store_split_sums(const ConvArgs& p, const float* bn, float (&sum)[kMine * 32],
                                                  const CUtensorMap* mhi, const CUtensorMap* mlo, uint8_t* box,
                                                  int row0, int q, bool valid, int c_begin, int lane) {
     using Box = EpiBox<false>;
@@ -363,27 +363,24 @@ __device__ __forceinline__ void store_split_sums(const ConvArgs& p, const float*
     for (int cc = 0; cc < kMine; ++cc) {
         const int c0 = (c_begin + cc) * 32;
         const size_t off = size_t(q) * p.ld + c0;
-        float4 sk[8], sl[8];
-        if (skip) {
-            const float4* hi = reinterpret_cast<const float4*>(static_cast<const float*>(p.skip) + off);
-            const float4* lo = reinterpret_cast<const float4*>(static_cast<const float*>(p.skip_lo) + off);
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                sk[u] = hi[u];
-                sl[u] = lo[u];
-            }
-        }
-        float y[32];
+        const float4* hi = reinterpret_cast<const float4*>(static_cast<const float*>(p.skip) + off);
+        const float4* lo = reinterpret_cast<const float4*>(static_cast<const float*>(p.skip_lo) + off);
+        // The chunk's outputs replace its sums (no second 32-float array live
+        // beside the sums and the residual).
+        float* y = &sum[cc * 32];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-            const float* h = &sk[u].x;
-            const float* l = &sl[u].x;
+            float4 h4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), l4 = h4;
+            if (skip) {
+                h4 = hi[u];
+                l4 = lo[u];
+            }
+            const float* h = &h4.x;
+            const float* l = &l4.x;
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const int i = 4 * u + e;
-                y[i] = valid ? split_out(sum[cc * 32 + i], bn[c0 + i], bn[N + c0 + i], skip, skip ? h[e] : 0.0f,
-                                         skip ? l[e] : 0.0f)
-                             : 0.0f;
+                y[i] = valid ? split_out(y[i], bn[c0 + i], bn[N + c0 + i], skip, h[e], l[e]) : 0.0f;
             }
         }
 #pragma unroll
