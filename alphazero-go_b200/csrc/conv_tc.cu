@@ -70,6 +70,16 @@ struct ConvCfg {
 };
 
 constexpr int kThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+// The two-tile form adds warp 10, which issues the second tile's MMAs: one
+// thread issues an MMA about every 61 cycles, no faster than the tensor core
+// finishes an M = 128, N = 128 bf16 one (64 cycles), so with one issuing
+// thread narrow layers wait on the issue. The two tiles' accumulators are
+// disjoint TMEM columns; each thread commits its own MMAs, so the barriers
+// they commit to take one arrival per issuing thread.
+template <int kTiles>
+constexpr int kIssuersOf = kTiles == 2 ? 2 : 1;
+template <int kTiles>
+constexpr int kThreadsOf = kThreads + 32 * (kIssuersOf<kTiles> - 1);
 constexpr int kMaxStages = 8;
 constexpr uint32_t kBnBytes = 2 * 256 * 4;   // scale and shift of up to 256 channels
 
@@ -413,7 +423,7 @@ __device__ __forceinline__ void store_split_sums(const ConvArgs& p, const float*
 // per tile). mOut/mSkip: the epilogue's output and residual boxes; in the
 // stacked split mode the high and low output planes.
 template <int N, bool kBf16, bool kSplit, int kTiles, int kSeg>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
     conv3x3_tc(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAlo,
                const __grid_constant__ CUtensorMap mW, const __grid_constant__ CUtensorMap mWlo,
                const __grid_constant__ CUtensorMap mOut, const __grid_constant__ CUtensorMap mSkip, const ConvArgs p) {
@@ -422,21 +432,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     const Smem sm = carve(smem_raw, p.sa, p.sb, C::kOps * kTiles, C::kOps, p.a_bytes, C::kBBytes, C::kEpiBytes);
     const int ngroups = (p.ntiles + kTiles - 1) / kTiles;   // a CTA takes kTiles consecutive tiles at a time
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int kIssuers = kIssuersOf<kTiles>;   // MMA-issuing threads: warp 1 (and warp 10)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < p.sa; ++i) {
             mbar_init(&sm.a_full[i], 1);
-            mbar_init(&sm.a_empty[i], 1);
+            mbar_init(&sm.a_empty[i], kIssuers);
         }
         for (int i = 0; i < p.sb; ++i) {
             mbar_init(&sm.b_full[i], 1);
-            mbar_init(&sm.b_empty[i], 1);
+            mbar_init(&sm.b_empty[i], kIssuers);
         }
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&sm.acc_full[i], 1);
+            mbar_init(&sm.acc_full[i], kIssuers);
             mbar_init(&sm.acc_empty[i], kEpiWarps);   // one arrival per epilogue warp
         }
-        mbar_init(sm.done, 1);
+        mbar_init(sm.done, kIssuers);
         for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&sm.skip_full[i], 1);
         fence_barrier_init();
     }
@@ -453,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
     if (warp == 1) tmem_alloc(sm.tmem_slot, C::kTmemCols);
-    for (int i = threadIdx.x; i < N; i += kThreads) {
+    for (int i = threadIdx.x; i < N; i += kThreadsOf<kTiles>) {
         sm.bn[i] = p.scale[i];
         sm.bn[N + i] = p.shift[i];
     }
@@ -510,19 +521,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_wait(&sm.b_full[s], (uses - 1) & 1, p.err, kErrWaitDrain);
             }
         }
-    } else if (warp == 1) {
+    } else if (warp == 1 || warp == kEpiWarps + 2) {
         // --------------------------------------------------------- MMA issue
-        // One thread issues every MMA, so whatever it computes between two
-        // MMAs delays the next: descriptors are built once and advanced by
-        // additions, the tap loop is unrolled (its nine row offsets live in
-        // registers) and rings advance without divisions.
+        // One thread issues every MMA of its tiles, so whatever it computes
+        // between two MMAs delays the next: descriptors are built once and
+        // advanced by additions, the tap loop is unrolled (its nine row
+        // offsets live in registers) and rings advance without divisions.
+        // With two issuing threads each walks the same rings and waits,
+        // and issues and commits only its own tile's MMAs.
+        constexpr int kPer = kTiles / kIssuers;   // tiles this thread issues
+        const int first = warp == 1 ? 0 : kPer;   // its first tile in the group
         if (lane == 0) {
             Ring ra, rb;
             uint32_t j = 0;
             bool ok = true;
-            const uint64_t a_desc = sw128_desc(smem_u32(sm.a)), b_desc = sw128_desc(smem_u32(sm.b));
             const uint32_t a_stage = (uint32_t(C::kOps * kTiles) * uint32_t(p.a_bytes)) >> 4,
                            a_lo = uint32_t(p.a_bytes) >> 4, a_tile = (uint32_t(C::kOps) * uint32_t(p.a_bytes)) >> 4;
+            const uint64_t a_desc = sw128_desc(smem_u32(sm.a)) + uint64_t(first) * a_tile,
+                           b_desc = sw128_desc(smem_u32(sm.b));
+            const uint32_t tmem_mine = tmem + uint32_t(first) * C::kTileCols;
             constexpr uint32_t b_stage = (C::kOps * C::kBBytes) >> 4, b_lo = C::kBBytes >> 4;
             uint32_t toff[9];
             tap_offsets(p, toff);
@@ -532,7 +549,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t acc = j & 1;
                     if (!(ok = mbar_wait(&sm.acc_empty[acc], ((j >> 1) & 1) ^ 1, p.err, kErrWaitMma))) break;
                     tc_fence_after();
-                    const uint32_t d = tmem + acc * (kTiles * C::kTileCols);   // tile u's at + u * kTileCols
+                    const uint32_t d = tmem_mine + acc * (kTiles * C::kTileCols);   // tile u's at + u * kTileCols
                     for (int c = 0; c < p.nchunks && ok; ++c) {
                         if (!(ok = mbar_wait(&sm.a_full[ra.idx], ra.phase, p.err, kErrWaitMma))) break;
                         const uint64_t ac = a_desc + ra.idx * a_stage;
@@ -545,7 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                             for (int k = 0; k < C::kSteps; ++k) {
 #pragma unroll
-                                for (int u = 0; u < kTiles; ++u) {   // every tile of the group reads this weight tile
+                                for (int u = 0; u < kPer; ++u) {   // every tile of the group reads this weight tile
                                     const uint32_t du = d + uint32_t(u) * C::kTileCols;
                                     const uint64_t au = at + u * a_tile;
                                     if constexpr (C::kStack) {
@@ -594,7 +611,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             if (t % kSeg == 0) {   // open a segment on the next accumulator
                                 acc = j & 1;
                                 if (!(ok = mbar_wait(&sm.acc_empty[acc], ((j >> 1) & 1) ^ 1, p.err, kErrWaitMma))) break;
-                                d = tmem + acc * (kTiles * C::kTileCols);
+                                d = tmem_mine + acc * (kTiles * C::kTileCols);
                             }
                             if (!(ok = mbar_wait(&sm.b_full[rb.idx], rb.phase, p.err, kErrWaitMma))) break;
                             tc_fence_after();
@@ -602,7 +619,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                             for (int k = 0; k < C::kSteps; ++k) {
 #pragma unroll
-                                for (int u = 0; u < kTiles; ++u) {
+                                for (int u = 0; u < kPer; ++u) {
                                     const uint32_t du = d + uint32_t(u) * C::kTileCols;
                                     const uint64_t au = at + u * a_tile;
                                     constexpr uint32_t kIdescStack = umma_idesc(2 * N, kBf16);
@@ -1029,7 +1046,8 @@ cudaError_t launch_single_seg(const ConvMaps& m, ConvArgs a, int sms, cudaStream
     }
     const int groups = (a.ntiles + kTiles - 1) / kTiles;
     const int grid = std::max(1, std::min(groups, sms));
-    return launch_pdl(conv3x3_tc<N, kBf16, kSplit, kTiles, kSeg>, dim3(grid), dim3(kThreads), smem, s, m.a, m.a_lo,
+    return launch_pdl(conv3x3_tc<N, kBf16, kSplit, kTiles, kSeg>, dim3(grid), dim3(kThreadsOf<kTiles>), smem, s, m.a,
+                      m.a_lo,
                       m.w, m.w_lo, m.out, C::kStack ? m.out_lo : m.skip, a);
 }
 
