@@ -118,6 +118,7 @@ def lib() -> C.CDLL:
             L.azb_probe_set_conv_path.argtypes = [C.c_int]
             L.azb_probe_set_conv_segment.argtypes = [C.c_int]
             L.azb_probe_set_tower_fused.argtypes = [C.c_int]
+            L.azb_probe_set_tower_persistent.argtypes = [C.c_int]
             L.azb_probe_binary_version.argtypes = [C.c_int]
             L.azb_probe_device_architecture.argtypes = [C.c_int]
             L.azb_probe_fill.argtypes = [C.c_int, _F, s, C.c_float, s] + err
@@ -506,6 +507,11 @@ class cuda_probe:
     def set_tower_fused(mode: int):
         """-1 default (one launch for the tower of boards up to 10x10 with <= 64 channels), 0 per-layer kernels."""
         lib().azb_probe_set_tower_fused(mode)
+
+    @staticmethod
+    def set_tower_persistent(mode: int):
+        """bf16/tf32 towers too large to fuse: -1 default (one persistent launch at <= 128 channels), 0 per layer, 1 always."""
+        lib().azb_probe_set_tower_persistent(mode)
 
     @staticmethod
     def set_conv_segment(steps: int):

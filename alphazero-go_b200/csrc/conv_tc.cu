@@ -262,13 +262,13 @@ struct EpiBox {
 // soon as this chunk's has been read, and the output box is refilled once
 // the previous store has read it; with two, one chunk ahead and two behind.
 template <int N, bool kBf16>
-__device__ __forceinline__ void store_epilogue_tma(const ConvArgs& p, const float* bn, const CUtensorMap* omap,
-                                                   const CUtensorMap* smap, uint32_t taddr, int row0, bool valid,
-                                                   int c_begin, int c_end, EpiWarp& ew, int lane) {
+__device__ __forceinline__ void store_epilogue_tma(const ConvArgs& p, const float* scale, const float* shift,
+                                                   bool skip, const CUtensorMap* omap, const CUtensorMap* smap,
+                                                   uint32_t taddr, int row0, bool valid, int c_begin, int c_end,
+                                                   EpiWarp& ew, int lane) {
     using Box = EpiBox<kBf16>;
     constexpr uint32_t kBox = Box::kBytes;
     if (row0 >= p.rows || c_begin >= c_end) return;   // nothing of this warp's to store
-    const bool skip = p.skip != nullptr;
     if (skip && lane == 0) {
         mbar_arrive_expect_tx(&ew.sbar[0], kBox);
         tma_load_2d(smap, ew.sbuf, &ew.sbar[0], c_begin * 32, row0);
@@ -286,7 +286,7 @@ __device__ __forceinline__ void store_epilogue_tma(const ConvArgs& p, const floa
         float y[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-            y[i] = __fadd_rn(__fmul_rn(bn[c * 32 + i], __uint_as_float(v[i])), bn[N + c * 32 + i]);
+            y[i] = __fadd_rn(__fmul_rn(scale[c * 32 + i], __uint_as_float(v[i])), shift[c * 32 + i]);
         if (skip) {
             mbar_wait(&ew.sbar[cb], (ew.sphase >> cb) & 1u, p.err, kErrWaitEpilogue);
             ew.sphase ^= 1u << cb;
@@ -422,16 +422,40 @@ __device__ __forceinline__ void store_split_sums(const ConvArgs& p, const float*
 // kSeg: the stacked split mode's accumulation segment in taps (0: one run
 // per tile). mOut/mSkip: the epilogue's output and residual boxes; in the
 // stacked split mode the high and low output planes.
-template <int N, bool kBf16, bool kSplit, int kTiles, int kSeg>
+//
+// kPersist: the persistent tower (bf16 and tf32). Items are (layer, tile
+// group) = (it / ngroups, it % ngroups); the producer takes the pass's next
+// item from a global counter and hands its index to the MMA and epilogue
+// warps through a shared-memory ring. Every item's dependencies have lower
+// indices and were therefore taken by CTAs already running, so the tower
+// progresses however many of its CTAs are resident (another stream's
+// kernels may hold SMs, a second tower among them). The six maps are then the
+// three frames in halo boxes (mA, mAlo, mW) and in the epilogue's boxes
+// (mWlo, mOut, mSkip); the weights and batch norms come from p.tower. Each
+// epilogue warp adds 1 to its item's counter once its stores have landed;
+// an item's halo loads wait until the counters of the previous layer's
+// groups g-1, g, g+1 (the rows its halo reads) have reached kEpiWarps.
+// Writes need no wait of their own: the buffer an item overwrites was last
+// read by items that those same dependencies already include.
+template <int N, bool kBf16, bool kSplit, int kTiles, int kSeg, bool kPersist = false>
 __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
     conv3x3_tc(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAlo,
                const __grid_constant__ CUtensorMap mW, const __grid_constant__ CUtensorMap mWlo,
                const __grid_constant__ CUtensorMap mOut, const __grid_constant__ CUtensorMap mSkip, const ConvArgs p) {
     using C = ConvCfg<N, kBf16, kSplit, kTiles>;
+    static_assert(!kPersist || (!kSplit && kSeg == 0), "the persistent tower: bf16 and tf32");
     extern __shared__ uint8_t smem_raw[];
     const Smem sm = carve(smem_raw, p.sa, p.sb, C::kOps * kTiles, C::kOps, p.a_bytes, C::kBBytes, C::kEpiBytes);
     const int ngroups = (p.ntiles + kTiles - 1) / kTiles;   // a CTA takes kTiles consecutive tiles at a time
+    const int nitems = kPersist ? p.layers * ngroups : ngroups;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // The persistent tower's item ring lives where the batch norm would (its
+    // batch norms are read from p.tower): kItemSlots full and empty barriers,
+    // then the slots' item indices (-1: no more items).
+    constexpr int kItemSlots = 4;
+    uint64_t* item_full = reinterpret_cast<uint64_t*>(sm.bn);
+    uint64_t* item_empty = item_full + kItemSlots;
+    volatile int* item_slot = reinterpret_cast<volatile int*>(item_empty + kItemSlots);
     constexpr int kIssuers = kIssuersOf<kTiles>;   // MMA-issuing threads: warp 1 (and warp 10)
 
     if (threadIdx.x == 0) {
@@ -449,6 +473,11 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
         }
         mbar_init(sm.done, kIssuers);
         for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&sm.skip_full[i], 1);
+        if (kPersist)
+            for (int i = 0; i < kItemSlots; ++i) {
+                mbar_init(&item_full[i], 1);
+                mbar_init(&item_empty[i], kIssuers + kEpiWarps);   // every MMA issuer and epilogue warp reads it
+            }
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
@@ -464,10 +493,11 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
         }
     }
     if (warp == 1) tmem_alloc(sm.tmem_slot, C::kTmemCols);
-    for (int i = threadIdx.x; i < N; i += kThreadsOf<kTiles>) {
-        sm.bn[i] = p.scale[i];
-        sm.bn[N + i] = p.shift[i];
-    }
+    if (!kPersist)
+        for (int i = threadIdx.x; i < N; i += kThreadsOf<kTiles>) {
+            sm.bn[i] = p.scale[i];
+            sm.bn[N + i] = p.shift[i];
+        }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -486,7 +516,34 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
             const uint32_t b_tx = C::kBBytes * C::kOps;
             const size_t a_stage = size_t(C::kOps) * kTiles * p.a_bytes;
             bool ok = true;
-            for (int g = blockIdx.x; g < ngroups && ok; g += gridDim.x) {
+            Ring ri;
+            for (int k = 0; ok; ++k) {
+                int it = blockIdx.x + k * int(gridDim.x);
+                if constexpr (kPersist) {   // take the pass's next item and hand it on
+                    it = int(atomicAdd(p.flags + size_t(p.layers) * ngroups, 1u));
+                    if (!(ok = mbar_wait(&item_empty[ri.idx], ri.phase ^ 1u, p.err, kErrWaitProducer))) break;
+                    item_slot[ri.idx] = it < nitems ? it : -1;
+                    mbar_arrive(&item_full[ri.idx]);
+                    ri.next(kItemSlots);
+                }
+                if (it >= nitems) break;
+                int g = it;
+                const CUtensorMap* amap = &mA;
+                const CUtensorMap* wmap = &mW;
+                if constexpr (kPersist) {
+                    const int layer = it / ngroups;
+                    g = it - layer * ngroups;
+                    const int in = layer % 3;   // tower conv l reads buffer l mod 3
+                    amap = in == 0 ? &mA : (in == 1 ? &mAlo : &mW);
+                    wmap = &p.tower[layer].w;
+                    if (layer > 0) {   // the previous layer's groups whose rows this item's halos read
+                        const unsigned* prev = p.flags + size_t(layer - 1) * ngroups;
+                        for (int d = g > 0 ? g - 1 : 0; d <= g + 1 && d < ngroups && ok; ++d)
+                            ok = flag_wait(prev + d, kEpiWarps, p.err, kErrWaitLayer);
+                        if (!ok) break;
+                        fence_proxy_async_global();   // the loads below (async proxy) after the acquires
+                    }
+                }
                 for (int c = 0; c < p.nchunks && ok; ++c) {
                     if (!(ok = mbar_wait(&sm.a_empty[ra.idx], ra.phase ^ 1u, p.err, kErrWaitProducer))) break;
                     mbar_arrive_expect_tx(&sm.a_full[ra.idx], a_tx);
@@ -494,7 +551,7 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                     for (int u = 0; u < kTiles; ++u) {   // each tile's own halo (a tile past the frame reads zeros)
                         const int y0 = (g * kTiles + u) * 128 - (p.n + 2);
                         uint8_t* abuf = sm.a + ra.idx * a_stage + size_t(u) * C::kOps * p.a_bytes;
-                        tma_load_2d(&mA, abuf, &sm.a_full[ra.idx], c * C::kKc, y0);
+                        tma_load_2d(amap, abuf, &sm.a_full[ra.idx], c * C::kKc, y0);
                         if (kSplit) tma_load_2d(&mAlo, abuf + p.a_bytes, &sm.a_full[ra.idx], c * C::kKc, y0);
                     }
                     ra.next(p.sa);
@@ -503,7 +560,7 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                         if (!(ok = mbar_wait(&sm.b_empty[rb.idx], rb.phase ^ 1u, p.err, kErrWaitProducer))) break;
                         mbar_arrive_expect_tx(&sm.b_full[rb.idx], b_tx);
                         uint8_t* bbuf = sm.b + rb.idx * (C::kOps * C::kBBytes);
-                        tma_load_2d(&mW, bbuf, &sm.b_full[rb.idx], (c * p.taps + t) * C::kKc, 0);
+                        tma_load_2d(wmap, bbuf, &sm.b_full[rb.idx], (c * p.taps + t) * C::kKc, 0);
                         if (kSplit) tma_load_2d(&mWlo, bbuf + C::kBBytes, &sm.b_full[rb.idx], (c * p.taps + t) * C::kKc, 0);
                         rb.next(p.sb);
                         ++nb;
@@ -544,8 +601,19 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
             uint32_t toff[9];
             tap_offsets(p, toff);
             if constexpr (kSeg == 0) {
-                // One accumulator run per tile.
-                for (int g = blockIdx.x; g < ngroups && ok; g += gridDim.x, ++j) {
+                // One accumulator run per tile (per item: the persistent tower's
+                // layers all have this shape).
+                Ring ri;
+                for (int k = 0; ok; ++k, ++j) {
+                    int it = blockIdx.x + k * int(gridDim.x);
+                    if constexpr (kPersist) {
+                        if (!(ok = mbar_wait(&item_full[ri.idx], ri.phase, p.err, kErrWaitMma))) break;
+                        it = item_slot[ri.idx];
+                        mbar_arrive(&item_empty[ri.idx]);
+                        ri.next(kItemSlots);
+                        if (it < 0) break;
+                    }
+                    if (it >= nitems) break;
                     const uint32_t acc = j & 1;
                     if (!(ok = mbar_wait(&sm.acc_empty[acc], ((j >> 1) & 1) ^ 1, p.err, kErrWaitMma))) break;
                     tc_fence_after();
@@ -667,7 +735,47 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
         ew.sbar = sm.skip_full + 2 * e;
         uint32_t j = 0;   // accumulator runs consumed (one per tile, or one per segment)
         const int segs = kSeg == 0 ? 1 : (p.taps == 1 ? p.nchunks : p.nchunks * (9 / (kSeg > 0 ? kSeg : 1)));
-        for (int g = blockIdx.x; g < ngroups; g += gridDim.x) {
+        Ring ri;
+        for (int k = 0;; ++k) {
+            int it = blockIdx.x + k * int(gridDim.x);
+            if constexpr (kPersist) {
+                if (!mbar_wait(&item_full[ri.idx], ri.phase, p.err, kErrWaitEpilogue)) break;
+                it = item_slot[ri.idx];
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&item_empty[ri.idx]);
+                ri.next(kItemSlots);
+                if (it < 0) break;
+            }
+            if (it >= nitems) break;
+            int g = it;
+            const float* scale = sm.bn;
+            const float* shift = sm.bn + N;
+            bool has_skip = p.skip != nullptr;
+            const CUtensorMap* omap = &mOut;
+            const CUtensorMap* smap = &mSkip;
+            if constexpr (kPersist) {
+                const int layer = it / ngroups;
+                g = it - layer * ngroups;
+                // Tower conv l writes buffer (l+1) mod 3; a block's second conv
+                // (l odd) adds its first conv's input, buffer (l-1) mod 3.
+                const int out = (layer + 1) % 3, res = (layer + 2) % 3;
+                omap = out == 0 ? &mWlo : (out == 1 ? &mOut : &mSkip);
+                smap = res == 0 ? &mWlo : (res == 1 ? &mOut : &mSkip);
+                has_skip = (layer & 1) != 0;
+                scale = p.tower[layer].scale;
+                shift = p.tower[layer].shift;
+                if (layer > 0) {
+                    // This warp reads the residual and overwrites rows that
+                    // earlier items read: acquire the previous layer's group
+                    // (whose own dependencies cover both) here as well.
+                    bool ok = true;
+                    if (lane == 0) {
+                        ok = flag_wait(p.flags + size_t(layer - 1) * ngroups + g, kEpiWarps, p.err, kErrWaitLayer);
+                        fence_proxy_async_global();
+                    }
+                    if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+                }
+            }
             const int tile = g * kTiles + u;
             const int q = tile * 128 + row_in_tile;
             bool valid = q < p.rows;
@@ -710,14 +818,21 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                 tc_fence_after();
                 const uint32_t taddr = lanes + acc * (kTiles * C::kTileCols);
                 if constexpr (C::kEpiTma)
-                    store_epilogue_tma<N, kBf16>(p, sm.bn, &mOut, &mSkip, taddr, tile * 128 + quarter * 32, valid,
-                                                 c_begin, c_end, ew, lane);
+                    store_epilogue_tma<N, kBf16>(p, scale, shift, has_skip, omap, smap, taddr, tile * 128 + quarter * 32,
+                                                 valid, c_begin, c_end, ew, lane);
                 else if (tile < p.ntiles)
                     store_epilogue_split<N>(p, sm.bn, taddr, q, valid, c_begin, c_end);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
                 ++j;
+                if constexpr (kPersist) {
+                    if (lane == 0) {   // this warp's part of the item has landed in global memory
+                        bulk_wait_all();
+                        fence_proxy_async_global();
+                        flag_add_release(p.flags + it, 1u);
+                    }
+                }
             }
         }
         if ((C::kEpiTma || C::kStack) && lane == 0) bulk_wait_all();   // every output box written before the CTA exits
@@ -937,7 +1052,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + acc * N;
             if constexpr (C::kEpiTma)
-                store_epilogue_tma<N, kBf16>(p, sm.bn, &mOut, &mSkip, taddr, (2 * pr + int(rank)) * 128 + quarter * 32,
+                store_epilogue_tma<N, kBf16>(p, sm.bn, sm.bn + N, p.skip != nullptr, &mOut, &mSkip, taddr,
+                                             (2 * pr + int(rank)) * 128 + quarter * 32,
                                              valid, c_begin, c_end, ew, lane);
             else
                 store_epilogue_split<N>(p, sm.bn, taddr, q, valid, c_begin, c_end);
@@ -1061,6 +1177,37 @@ cudaError_t launch_single(const ConvMaps& m, ConvArgs a, int sms, cudaStream_t s
     return launch_single_seg<N, kBf16, kSplit, kTiles, 0>(m, a, sms, s);
 }
 
+// The persistent tower: two tiles per item where both halos and two weight
+// stages fit (128 channels or fewer), else one; a CTA per SM at most.
+template <int N, bool kBf16, int kTiles>
+cudaError_t launch_persist_tiles(const CUtensorMap (&in)[3], const CUtensorMap (&out)[3], ConvArgs a, int sms,
+                                 cudaStream_t s) {
+    using C = ConvCfg<N, kBf16, false, kTiles>;
+    conv_smem_bytes(N, kBf16 ? kBF16 : kTF32, a.halo_rows, &a.sa, &a.sb, false, kTiles);
+    const size_t smem = smem_total(a.sa, a.sb, C::kOps * kTiles, C::kOps, a.a_bytes, C::kBBytes, C::kEpiBytes);
+    static std::atomic<size_t> configured{0};
+    if (smem > configured.load()) {
+        const cudaError_t e = cudaFuncSetAttribute(conv3x3_tc<N, kBf16, false, kTiles, 0, true>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return e;
+        configured = smem;
+    }
+    const int groups = (a.ntiles + kTiles - 1) / kTiles;
+    const int grid = std::max(1, std::min(groups * a.layers, sms));
+    return launch_pdl(conv3x3_tc<N, kBf16, false, kTiles, 0, true>, dim3(grid), dim3(kThreadsOf<kTiles>), smem, s,
+                      in[0], in[1], in[2], out[0], out[1], out[2], a);
+}
+
+template <int N, bool kBf16>
+cudaError_t launch_persist(const CUtensorMap (&in)[3], const CUtensorMap (&out)[3], const ConvArgs& a, int sms,
+                           cudaStream_t s) {
+    if constexpr (N <= 128) {
+        if (conv_smem_bytes(N, kBf16 ? kBF16 : kTF32, a.halo_rows, nullptr, nullptr, false, 2) <= 227 * 1024)
+            return launch_persist_tiles<N, kBf16, 2>(in, out, a, sms, s);
+    }
+    return launch_persist_tiles<N, kBf16, 1>(in, out, a, sms, s);
+}
+
 template <int N, bool kBf16, bool kSplit>
 cudaError_t launch_one(const ConvMaps& m, ConvArgs a, int form, int sms, cudaStream_t s) {
     using C = ConvCfg<N, kBf16, kSplit>;
@@ -1140,6 +1287,32 @@ void set_conv_path(int path) { g_conv_path = path; }
 
 std::atomic<int> g_conv_segment{-1};
 void set_conv_segment(int steps) { g_conv_segment = steps; }
+
+std::atomic<int> g_tower_persistent{-1};
+void set_tower_persistent(int mode) { g_tower_persistent = mode; }
+
+bool tower_persistent(int n_out, int precision) {
+    const int mode = g_tower_persistent.load();
+    if (mode == 0 || precision == kTF32x3) return false;
+    if (mode == 1) return true;
+    return n_out <= 128;
+}
+
+cudaError_t launch_tower_persistent(const CUtensorMap (&in)[3], const CUtensorMap (&out)[3], const ConvArgs& a,
+                                    int n_out, int precision, int sms, cudaStream_t s) {
+    if (a.ntiles <= 0 || a.layers <= 0) return cudaSuccess;
+    if (precision == kTF32x3 || a.tower == nullptr || a.flags == nullptr) return cudaErrorNotSupported;
+    const bool bf16 = precision == kBF16;
+    switch (n_out) {
+        case 32: return bf16 ? launch_persist<32, true>(in, out, a, sms, s) : launch_persist<32, false>(in, out, a, sms, s);
+        case 64: return bf16 ? launch_persist<64, true>(in, out, a, sms, s) : launch_persist<64, false>(in, out, a, sms, s);
+        case 128:
+            return bf16 ? launch_persist<128, true>(in, out, a, sms, s) : launch_persist<128, false>(in, out, a, sms, s);
+        case 256:
+            return bf16 ? launch_persist<256, true>(in, out, a, sms, s) : launch_persist<256, false>(in, out, a, sms, s);
+        default: return cudaErrorNotSupported;
+    }
+}
 
 // Which form a layer runs: by default the CTA pair for 256 output
 // channels, where a weight tile is 32 KB per tap and halving it per SM

@@ -562,6 +562,15 @@ size_t feat_floats(const NetShape& s) {
     return (2 * A + 3) / 4 * 4 + (A + 3) / 4 * 4;
 }
 
+namespace {
+// The persistent tower's counters: one per tower conv and 128-row tile of a
+// full batch, and the next-item counter.
+size_t tower_flags_for(const NetShape& s, int max_batch) {
+    const size_t tiles = (size_t(max_batch) * Frame(s.board).S + 127) / 128;
+    return size_t(2 * s.blocks) * tiles + 1;
+}
+} // namespace
+
 size_t Workspace::bytes_for(const NetShape& s, int precision, int max_batch) {
     const Frame fr(s.board);
     const size_t rows = size_t(max_batch) * fr.S;
@@ -583,6 +592,7 @@ size_t Workspace::bytes_for(const NetShape& s, int precision, int max_batch) {
     c.take(B * size_t(s.value_hidden) * 4);
     c.take(B * stones_record_bytes(s.history, s.board));
     c.take(16);
+    c.take(tower_flags_for(s, max_batch) * 4);
     return c.used;
 }
 
@@ -611,6 +621,8 @@ void Workspace::place(const Weights& w, uint8_t* base) {
     hid = reinterpret_cast<float*>(at(c.take(B * size_t(s.value_hidden) * 4)));
     records = at(c.take(B * stones_record_bytes(s.history, s.board)));
     err = reinterpret_cast<int*>(at(c.take(16)));
+    tower_flag_count = tower_flags_for(s, max_batch_);
+    tower_flags = reinterpret_cast<unsigned*>(at(c.take(tower_flag_count * 4)));
     const uint32_t KC = uint32_t(chunk_channels(precision));
     map_stem = make_tensor_map(stem_in, precision, ks, rows, KC, uint32_t(fr.halo));
     map_stem_lo = precision == kTF32x3 ? make_tensor_map(stem_in_lo, precision, ks, rows, KC, uint32_t(fr.halo)) : map_stem;
@@ -673,6 +685,7 @@ std::string kernel_error_text(int code) {
         case kErrProbeTimeout: return "bounded wait ran out";
         case kErrWaitHeadLoad: return "the head kernel's copy thread waited too long for a free stage";
         case kErrWaitHeadData: return "the head kernel waited too long for its trunk rows";
+        case kErrWaitLayer: return "the persistent tower waited too long for the previous layer";
         default: return "kernel error " + std::to_string(code);
     }
 }
@@ -701,6 +714,15 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
     st.ld = w.kstem();
     st.out = ws.stem_in;
     st.out_lo = ws.stem_in_lo;
+    // Small boards run the fused tower; the others, where it applies, the
+    // persistent tower (whose counters the stem operand kernel zeroes).
+    const bool fused = ws.fused && g_tower_fused.load() != 0;
+    const int pass_tiles = (B * fr.S + 127) / 128;
+    const bool persistent = !fused && sh.blocks > 0 && ws.tower_flags != nullptr &&
+                            size_t(2 * sh.blocks) * size_t(pass_tiles) + 1 <= ws.tower_flag_count &&
+                            tower_persistent(w.n_out(), precision);
+    st.flags = persistent ? ws.tower_flags : nullptr;
+    st.nflags = persistent ? 2 * sh.blocks * pass_tiles + 1 : 0;
     mark_begin(kSlotStemPack);
     check(launch_stem_pack(st, precision, s), "stem operand");
     mark_end(kSlotStemPack);
@@ -733,7 +755,6 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
     };
     // The stem: conv -> BN -> ReLU as one tap over the packed operand (in
     // the fused tower's launch when that runs it).
-    const bool fused = ws.fused && g_tower_fused.load() != 0;
     if (fused && ws.fused_plan.stem_nch > 0) {
         mark_begin(kSlotStemGemm);
         mark_end(kSlotStemGemm);
@@ -773,6 +794,26 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
             mark_begin(kSlotTower + i);
             mark_end(kSlotTower + i);
         }
+    } else if (persistent) {
+        // Every tower conv in one launch: conv l reads trunk[l % 3] and
+        // writes trunk[(l + 1) % 3], so the trunk ends in trunk[2·blocks % 3]
+        // as the per-layer rotation leaves it.
+        a.taps = 9;
+        a.nchunks = tower_chunks;
+        a.out = a.out_lo = nullptr;
+        a.skip = a.skip_lo = nullptr;
+        a.scale = a.shift = nullptr;
+        a.tower = w.fused_layers();
+        a.layers = 2 * sh.blocks;
+        a.flags = ws.tower_flags;
+        mark_begin(kSlotTower);
+        check(launch_tower_persistent(ws.map, ws.emap, a, w.n_out(), precision, dev.sms, s), "persistent tower");
+        mark_end(kSlotTower);
+        for (int i = 1; i < 2 * sh.blocks; ++i) {   // the per-conv slots, empty
+            mark_begin(kSlotTower + i);
+            mark_end(kSlotTower + i);
+        }
+        x = (2 * sh.blocks) % 3;
     } else {
         for (int i = 0; i < sh.blocks; ++i) {
             const int mid = (x + 1) % 3, out = (x + 2) % 3;

@@ -140,6 +140,10 @@ public:
     float* hid = nullptr;         // [max_batch][value_hidden]: value FC1 output
     uint8_t* records = nullptr;   // [max_batch][stones_record_bytes]: encoder input (infer_stones)
     int* err = nullptr;           // kernel error word
+    // The persistent tower's counters: per tower conv and tile group (up to
+    // the tiles of max_batch), then the pass's next-item counter.
+    unsigned* tower_flags = nullptr;
+    size_t tower_flag_count = 0;
     CUtensorMap map[3]{}, map_lo[3]{};
     CUtensorMap emap[3]{};        // the frames in the conv epilogue's {32, 32} boxes (split mode: high planes)
     CUtensorMap emap_lo[3]{};     // split mode: the low planes in the same boxes

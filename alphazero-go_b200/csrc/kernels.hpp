@@ -45,6 +45,7 @@ enum KernelError : int {
     kErrProbeTimeout = 5,   // the bounded-wait probe's wait ran out (expected by its test)
     kErrWaitHeadLoad = 6,   // the head kernel's copy thread waited too long for a free stage
     kErrWaitHeadData = 7,   // the head kernel's readers waited too long for a board row
+    kErrWaitLayer = 8,      // the persistent tower waited too long for the previous layer's tile groups
 };
 
 
@@ -67,6 +68,8 @@ struct Frame {
     size_t row(int b, int y, int x) const { return size_t(b) * S + size_t(y + 1) * (n + 1) + x; }
 };
 
+struct FusedLayer;
+
 // One fused 3x3 convolution + folded batch norm (+ skip) + ReLU.
 struct ConvArgs {
     int n, S;          // board, frame rows per board
@@ -86,6 +89,13 @@ struct ConvArgs {
     const float* scale;   // [N] folded batch norm (0 for padded channels)
     const float* shift;   // [N]
     int* err;          // kernel error word (KernelError)
+    // The persistent tower (every tower conv in one launch): the layers'
+    // weight maps and batch norms, their number, and per (layer, tile group)
+    // the count of epilogue warps that have stored their part of it, zeroed
+    // by the pass's stem operand kernel.
+    const FusedLayer* tower;
+    int layers;
+    unsigned* flags;
 };
 
 struct ConvMaps {
@@ -113,6 +123,22 @@ void set_conv_path(int path);
 // accumulator run per tile.
 void set_conv_segment(int steps);
 
+// The persistent tower: every tower conv (a.layers of them, a.tower's
+// entries) in one launch of one CTA per SM (bf16 and tf32; the split mode
+// runs per layer). CTAs take (layer, tile group) items in order; an item's
+// halo loads wait for the three groups of the previous layer whose rows
+// they read. Block b's first conv reads buffer 2b mod 3 and writes the
+// next; its second reads that and adds the first's input. in[i]: the
+// frames in halo boxes; out[i]: in the epilogue's {32, 32} boxes.
+// Returns cudaErrorNotSupported where it does not apply (the caller then
+// launches per layer).
+cudaError_t launch_tower_persistent(const CUtensorMap (&in)[3], const CUtensorMap (&out)[3], const ConvArgs& a,
+                                    int n_out, int precision, int sms, cudaStream_t s);
+// Whether the persistent tower runs for n_out channels in `precision` (and
+// the test hook's choice: -1 the default, 0 per layer, 1 persistent).
+bool tower_persistent(int n_out, int precision);
+void set_tower_persistent(int mode);
+
 // The stem's packed operand: the [B][P][A] fp32 input unfolded into frame
 // rows of K = 9*P values (column t*P + p), ld elements apart. The stem conv
 // itself then runs as a one-tap GEMM on the tensor-core kernel.
@@ -120,6 +146,8 @@ struct StemArgs {
     const float* in;    // [B][P][A]
     int B, P, n, S, ld;
     void* out; void* out_lo;
+    unsigned* flags;    // the persistent tower's counters, zeroed here (null: none)
+    int nflags;
 };
 cudaError_t launch_stem_pack(const StemArgs& a, int precision, cudaStream_t s);
 

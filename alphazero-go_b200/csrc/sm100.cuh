@@ -159,6 +159,39 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 // (TMA, tensor core) accesses of them.
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// Orders this thread's global-memory accesses in the generic proxy with its
+// async-proxy (TMA) accesses of global memory, both ways.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// -------------------------------------------------- counters between CTAs
+
+// Adds v to *flag with release semantics at GPU scope: this thread's earlier
+// writes are visible to a thread that reads the sum with acquire.
+__device__ __forceinline__ void flag_add_release(unsigned* flag, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned flag_load_acquire(const unsigned* flag) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    return v;
+}
+
+// Waits until *flag >= target, for at most kWaitLimitNs. On timeout records
+// `code` in *err (first error wins) and returns false.
+__device__ __forceinline__ bool flag_wait(const unsigned* flag, unsigned target, int* err, int code) {
+    if (flag_load_acquire(flag) >= target) return true;
+    const uint64_t start = global_timer();
+    for (;;) {
+        __nanosleep(100);
+        if (flag_load_acquire(flag) >= target) return true;
+        if (global_timer() - start > kWaitLimitNs) {
+            atomicCAS(err, 0, code);
+            return false;
+        }
+    }
+}
+
 // ------------------------------------------------------------------ tcgen05
 
 // Allocates `ncols` TMEM columns (a power of two >= 32) for this CTA and

@@ -42,6 +42,9 @@ __global__ void __launch_bounds__(256) stem_pack_kernel(const StemArgs a) {
     int* table = reinterpret_cast<int*>(planes + size_t(a.P) * A);
     grid_dependency_wait();
     grid_launch_dependents();
+    if (a.flags)   // the persistent tower's counters start each pass at zero
+        for (int i = int(blockIdx.x * blockDim.x + threadIdx.x); i < a.nflags; i += int(gridDim.x * blockDim.x))
+            a.flags[i] = 0u;
     for (int i = threadIdx.x; i < W * pieces; i += blockDim.x) {
         const int e = i / pieces, j = i % pieces, k = j * W + e;
         int code = -1;

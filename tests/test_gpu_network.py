@@ -29,7 +29,9 @@ def conv_path(request, engine):
     each weight tile (N <= 128; wider layers fall back to one tile)."""
     engine.cuda_probe.set_conv_path(request.param)
     engine.cuda_probe.set_tower_fused(0)   # the per-layer kernels, also for small boards
+    engine.cuda_probe.set_tower_persistent(0)   # and for larger ones
     yield request.param
+    engine.cuda_probe.set_tower_persistent(-1)
     engine.cuda_probe.set_tower_fused(-1)
     engine.cuda_probe.set_conv_path(0)
 
