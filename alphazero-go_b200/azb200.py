@@ -119,6 +119,7 @@ def lib() -> C.CDLL:
             L.azb_probe_set_conv_segment.argtypes = [C.c_int]
             L.azb_probe_set_tower_fused.argtypes = [C.c_int]
             L.azb_probe_set_tower_persistent.argtypes = [C.c_int]
+            L.azb_probe_starve_tower.argtypes = [C.c_int]
             L.azb_probe_binary_version.argtypes = [C.c_int]
             L.azb_probe_device_architecture.argtypes = [C.c_int]
             L.azb_probe_fill.argtypes = [C.c_int, _F, s, C.c_float, s] + err
@@ -512,6 +513,11 @@ class cuda_probe:
     def set_tower_persistent(mode: int):
         """bf16/tf32 towers too large to fuse: -1 default (one persistent launch at <= 128 channels), 0 per layer, 1 always."""
         lib().azb_probe_set_tower_persistent(mode)
+
+    @staticmethod
+    def starve_tower(on: bool):
+        """Failure detection: the persistent tower's waits for a previous layer run out (1 s) and the pass fails."""
+        lib().azb_probe_starve_tower(1 if on else 0)
 
     @staticmethod
     def set_conv_segment(steps: int):

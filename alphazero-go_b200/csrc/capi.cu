@@ -233,6 +233,7 @@ void azb_probe_set_conv_path(int path) { set_conv_path(path); }
 void azb_probe_set_conv_segment(int steps) { set_conv_segment(steps); }
 void azb_probe_set_tower_fused(int mode) { set_tower_fused(mode); }
 void azb_probe_set_tower_persistent(int mode) { set_tower_persistent(mode); }
+void azb_probe_starve_tower(int on) { set_tower_starve(on); }
 
 int azb_probe_binary_version(int device) { return device_info(device).binary_version; }
 int azb_probe_device_architecture(int device) { return device_info(device).architecture; }

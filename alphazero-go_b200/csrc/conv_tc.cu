@@ -539,7 +539,7 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                     if (layer > 0) {   // the previous layer's groups whose rows this item's halos read
                         const unsigned* prev = p.flags + size_t(layer - 1) * ngroups;
                         for (int d = g > 0 ? g - 1 : 0; d <= g + 1 && d < ngroups && ok; ++d)
-                            ok = flag_wait(prev + d, kEpiWarps, p.err, kErrWaitLayer);
+                            ok = flag_wait(prev + d, kEpiWarps + p.flag_extra, p.err, kErrWaitLayer);
                         if (!ok) break;
                         fence_proxy_async_global();   // the loads below (async proxy) after the acquires
                     }
@@ -770,7 +770,8 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                     // (whose own dependencies cover both) here as well.
                     bool ok = true;
                     if (lane == 0) {
-                        ok = flag_wait(p.flags + size_t(layer - 1) * ngroups + g, kEpiWarps, p.err, kErrWaitLayer);
+                        ok = flag_wait(p.flags + size_t(layer - 1) * ngroups + g, kEpiWarps + p.flag_extra, p.err,
+                                       kErrWaitLayer);
                         fence_proxy_async_global();
                     }
                     if (!__shfl_sync(0xffffffffu, ok, 0)) break;
@@ -1290,6 +1291,10 @@ void set_conv_segment(int steps) { g_conv_segment = steps; }
 
 std::atomic<int> g_tower_persistent{-1};
 void set_tower_persistent(int mode) { g_tower_persistent = mode; }
+
+std::atomic<int> g_tower_starve{0};
+void set_tower_starve(int on) { g_tower_starve = on; }
+bool tower_starve() { return g_tower_starve.load() != 0; }
 
 bool tower_persistent(int n_out, int precision) {
     const int mode = g_tower_persistent.load();

@@ -806,6 +806,7 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
         a.tower = w.fused_layers();
         a.layers = 2 * sh.blocks;
         a.flags = ws.tower_flags;
+        a.flag_extra = tower_starve() ? 1u : 0u;
         mark_begin(kSlotTower);
         check(launch_tower_persistent(ws.map, ws.emap, a, w.n_out(), precision, dev.sms, s), "persistent tower");
         mark_end(kSlotTower);

@@ -96,6 +96,7 @@ struct ConvArgs {
     const FusedLayer* tower;
     int layers;
     unsigned* flags;
+    unsigned flag_extra;   // 0; the failure-detection test's 1 makes every wait for a previous layer run out
 };
 
 struct ConvMaps {
@@ -124,12 +125,13 @@ void set_conv_path(int path);
 void set_conv_segment(int steps);
 
 // The persistent tower: every tower conv (a.layers of them, a.tower's
-// entries) in one launch of one CTA per SM (bf16 and tf32; the split mode
-// runs per layer). CTAs take (layer, tile group) items in order; an item's
-// halo loads wait for the three groups of the previous layer whose rows
-// they read. Block b's first conv reads buffer 2b mod 3 and writes the
-// next; its second reads that and adds the first's input. in[i]: the
-// frames in halo boxes; out[i]: in the epilogue's {32, 32} boxes.
+// entries) in one launch of at most one CTA per SM (bf16 and tf32; the
+// split mode runs per layer). CTAs take (layer, tile group) items in
+// layer-major order from a counter; an item's halo loads wait for the three
+// groups of the previous layer whose rows they read. Tower conv l reads
+// frame buffer l mod 3 and writes (l+1) mod 3; a block's second conv adds
+// (l-1) mod 3, the block's input. in[i]: the frames in halo boxes; out[i]:
+// in the epilogue's {32, 32} boxes.
 // Returns cudaErrorNotSupported where it does not apply (the caller then
 // launches per layer).
 cudaError_t launch_tower_persistent(const CUtensorMap (&in)[3], const CUtensorMap (&out)[3], const ConvArgs& a,
@@ -138,6 +140,11 @@ cudaError_t launch_tower_persistent(const CUtensorMap (&in)[3], const CUtensorMa
 // the test hook's choice: -1 the default, 0 per layer, 1 persistent).
 bool tower_persistent(int n_out, int precision);
 void set_tower_persistent(int mode);
+// Test hook: nonzero makes the persistent tower wait for one counter step
+// more than its epilogue warps add, so its first wait for a previous layer
+// runs out (bounded) and the pass reports kErrWaitLayer.
+void set_tower_starve(int on);
+bool tower_starve();
 
 // The stem's packed operand: the [B][P][A] fp32 input unfolded into frame
 // rows of K = 9*P values (column t*P + p), ld elements apart. The stem conv

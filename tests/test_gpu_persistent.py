@@ -103,3 +103,29 @@ def test_persistent_towers_on_two_streams(engine, oracle):
             runner.close()
     finally:
         engine.cuda_probe.set_tower_persistent(-1)
+
+
+def test_persistent_tower_wait_runs_out_and_recovers(engine, oracle):
+    """Failure detection without a GPU fault: with the counters' target one
+    step beyond what the epilogue warps add, the first wait for a previous
+    layer ends after its bound, the pass reports it, and the next pass on the
+    same handle gives the per-layer path's bits."""
+    O = oracle
+    c = O.NetConfig(19, 1, 2, 64, 64, False)
+    params, buffers = O.make_network(c, 87, O.KIND_TEST)
+    x = O.random_planes(c, 88, 16)
+    layered = _run(engine, c, params, buffers, x, engine.BF16, False)
+    engine.cuda_probe.set_tower_persistent(1)
+    try:
+        with engine.CudaInference(engine.NetDesc.of(c), params, buffers, 16, 0, engine.BF16) as net:
+            engine.cuda_probe.starve_tower(True)
+            try:
+                with pytest.raises(RuntimeError, match="the persistent tower waited too long for the previous layer"):
+                    net.infer(x)
+            finally:
+                engine.cuda_probe.starve_tower(False)
+            again = net.infer(x)
+            for k in range(2):
+                assert np.array_equal(again[k], layered[k]), k
+    finally:
+        engine.cuda_probe.set_tower_persistent(-1)
