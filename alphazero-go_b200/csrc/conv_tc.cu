@@ -25,6 +25,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstdio>
+#include <type_traits>
 
 #include "kernels.hpp"
 #include "sm100.cuh"
@@ -68,6 +69,11 @@ struct ConvCfg {
         kEpiTma ? uint32_t(kEpiWarps) * (kBf16 ? 4096u : 8192u) : (kStack ? uint32_t(kEpiWarps) * 4096u : 0u);
     static_assert(N % 32 == 0 && N >= 32 && N <= 256, "N is a multiple of 32 in [32, 256]");
 };
+
+// The persistent tower's frame maps; nothing for the per-layer launches.
+struct NoFrames {};
+template <bool kPersist>
+using FramesOf = std::conditional_t<kPersist, TowerFrames, NoFrames>;
 
 constexpr int kThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 // The two-tile form adds warp 10, which issues the second tile's MMAs: one
@@ -363,18 +369,19 @@ __device__ __forceinline__ void store_epilogue_tma(const ConvArgs& p, const floa
 // rows are stored as zeros (they must stay zero); rows past the frame are
 // clipped by TMA.
 template <int N, int kMine>
-__device__ __forceinline__ void store_split_sums(const ConvArgs& p, const float* bn, float (&sum)[kMine * 32],
+__device__ __forceinline__ void store_split_sums(const ConvArgs& p, const float* scale, const float* shift,
+                                                 const void* res_hi, const void* res_lo, float (&sum)[kMine * 32],
                                                  const CUtensorMap* mhi, const CUtensorMap* mlo, uint8_t* box,
                                                  int row0, int q, bool valid, int c_begin, int lane) {
     using Box = EpiBox<false>;
     if (row0 >= p.rows) return;   // the warp's rows are all past the frame
-    const bool skip = valid && p.skip != nullptr;
+    const bool skip = valid && res_hi != nullptr;
 #pragma unroll
     for (int cc = 0; cc < kMine; ++cc) {
         const int c0 = (c_begin + cc) * 32;
         const size_t off = size_t(q) * p.ld + c0;
-        const float4* hi = reinterpret_cast<const float4*>(static_cast<const float*>(p.skip) + off);
-        const float4* lo = reinterpret_cast<const float4*>(static_cast<const float*>(p.skip_lo) + off);
+        const float4* hi = reinterpret_cast<const float4*>(static_cast<const float*>(res_hi) + off);
+        const float4* lo = reinterpret_cast<const float4*>(static_cast<const float*>(res_lo) + off);
         // The chunk's outputs replace its sums (no second 32-float array live
         // beside the sums and the residual).
         float* y = &sum[cc * 32];
@@ -390,7 +397,7 @@ __device__ __forceinline__ void store_split_sums(const ConvArgs& p, const float*
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const int i = 4 * u + e;
-                y[i] = valid ? split_out(y[i], bn[c0 + i], bn[N + c0 + i], skip, h[e], l[e]) : 0.0f;
+                y[i] = valid ? split_out(y[i], scale[c0 + i], shift[c0 + i], skip, h[e], l[e]) : 0.0f;
             }
         }
 #pragma unroll
@@ -441,9 +448,11 @@ template <int N, bool kBf16, bool kSplit, int kTiles, int kSeg, bool kPersist = 
 __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
     conv3x3_tc(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAlo,
                const __grid_constant__ CUtensorMap mW, const __grid_constant__ CUtensorMap mWlo,
-               const __grid_constant__ CUtensorMap mOut, const __grid_constant__ CUtensorMap mSkip, const ConvArgs p) {
+               const __grid_constant__ CUtensorMap mOut, const __grid_constant__ CUtensorMap mSkip, const ConvArgs p,
+               const __grid_constant__ FramesOf<kPersist> tf) {
     using C = ConvCfg<N, kBf16, kSplit, kTiles>;
-    static_assert(!kPersist || (!kSplit && kSeg == 0), "the persistent tower: bf16 and tf32");
+    static_assert(!kPersist || (!kSplit && kSeg == 0) || (C::kStack && kSeg != 0 && kTiles == 1),
+                  "the persistent tower: bf16 and tf32, or the split mode's segmented single tiles");
     extern __shared__ uint8_t smem_raw[];
     const Smem sm = carve(smem_raw, p.sa, p.sb, C::kOps * kTiles, C::kOps, p.a_bytes, C::kBBytes, C::kEpiBytes);
     const int ngroups = (p.ntiles + kTiles - 1) / kTiles;   // a CTA takes kTiles consecutive tiles at a time
@@ -529,13 +538,17 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                 if (it >= nitems) break;
                 int g = it;
                 const CUtensorMap* amap = &mA;
+                const CUtensorMap* alo = &mAlo;
                 const CUtensorMap* wmap = &mW;
+                const CUtensorMap* wlo = &mWlo;
                 if constexpr (kPersist) {
                     const int layer = it / ngroups;
                     g = it - layer * ngroups;
                     const int in = layer % 3;   // tower conv l reads buffer l mod 3
-                    amap = in == 0 ? &mA : (in == 1 ? &mAlo : &mW);
+                    amap = &tf.in[in];
+                    alo = &tf.in_lo[in];
                     wmap = &p.tower[layer].w;
+                    wlo = &p.tower[layer].w_lo;
                     if (layer > 0) {   // the previous layer's groups whose rows this item's halos read
                         const unsigned* prev = p.flags + size_t(layer - 1) * ngroups;
                         for (int d = g > 0 ? g - 1 : 0; d <= g + 1 && d < ngroups && ok; ++d)
@@ -552,7 +565,7 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                         const int y0 = (g * kTiles + u) * 128 - (p.n + 2);
                         uint8_t* abuf = sm.a + ra.idx * a_stage + size_t(u) * C::kOps * p.a_bytes;
                         tma_load_2d(amap, abuf, &sm.a_full[ra.idx], c * C::kKc, y0);
-                        if (kSplit) tma_load_2d(&mAlo, abuf + p.a_bytes, &sm.a_full[ra.idx], c * C::kKc, y0);
+                        if (kSplit) tma_load_2d(alo, abuf + p.a_bytes, &sm.a_full[ra.idx], c * C::kKc, y0);
                     }
                     ra.next(p.sa);
                     ++na;
@@ -561,7 +574,7 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                         mbar_arrive_expect_tx(&sm.b_full[rb.idx], b_tx);
                         uint8_t* bbuf = sm.b + rb.idx * (C::kOps * C::kBBytes);
                         tma_load_2d(wmap, bbuf, &sm.b_full[rb.idx], (c * p.taps + t) * C::kKc, 0);
-                        if (kSplit) tma_load_2d(&mWlo, bbuf + C::kBBytes, &sm.b_full[rb.idx], (c * p.taps + t) * C::kKc, 0);
+                        if (kSplit) tma_load_2d(wlo, bbuf + C::kBBytes, &sm.b_full[rb.idx], (c * p.taps + t) * C::kKc, 0);
                         rb.next(p.sb);
                         ++nb;
                     }
@@ -668,7 +681,17 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                 // would slow every MMA after it.
                 static_assert(C::kStack && 9 % kSeg == 0, "segments: stacked split mode, kSeg divides 9");
                 const bool one_tap = p.taps == 1;
-                for (int g = blockIdx.x; g < ngroups && ok; g += gridDim.x) {
+                Ring ri;
+                for (int k = 0; ok; ++k) {
+                    int it = blockIdx.x + k * int(gridDim.x);
+                    if constexpr (kPersist) {
+                        if (!(ok = mbar_wait(&item_full[ri.idx], ri.phase, p.err, kErrWaitMma))) break;
+                        it = item_slot[ri.idx];
+                        mbar_arrive(&item_empty[ri.idx]);
+                        ri.next(kItemSlots);
+                        if (it < 0) break;
+                    }
+                    if (it >= nitems) break;
                     uint32_t acc = 0, d = 0;
                     for (int c = 0; c < p.nchunks && ok; ++c) {
                         if (!(ok = mbar_wait(&sm.a_full[ra.idx], ra.phase, p.err, kErrWaitMma))) break;
@@ -750,18 +773,21 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
             int g = it;
             const float* scale = sm.bn;
             const float* shift = sm.bn + N;
-            bool has_skip = p.skip != nullptr;
-            const CUtensorMap* omap = &mOut;
-            const CUtensorMap* smap = &mSkip;
+            const void* res_hi = p.skip;   // the residual (null: none)
+            const void* res_lo = p.skip_lo;
+            const CUtensorMap* omap = &mOut;    // the output (split: its high plane)
+            const CUtensorMap* smap = &mSkip;   // the residual's boxes (stacked split: the output's low plane)
             if constexpr (kPersist) {
                 const int layer = it / ngroups;
                 g = it - layer * ngroups;
                 // Tower conv l writes buffer (l+1) mod 3; a block's second conv
                 // (l odd) adds its first conv's input, buffer (l-1) mod 3.
                 const int out = (layer + 1) % 3, res = (layer + 2) % 3;
-                omap = out == 0 ? &mWlo : (out == 1 ? &mOut : &mSkip);
-                smap = res == 0 ? &mWlo : (res == 1 ? &mOut : &mSkip);
-                has_skip = (layer & 1) != 0;
+                const bool has_res = (layer & 1) != 0;
+                res_hi = has_res ? tf.trunk[res] : nullptr;
+                res_lo = has_res ? tf.trunk_lo[res] : nullptr;
+                omap = &tf.out[out];
+                smap = kSplit ? &tf.out_lo[out] : &tf.out[res];
                 scale = p.tower[layer].scale;
                 shift = p.tower[layer].shift;
                 if (layer > 0) {
@@ -790,12 +816,12 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                 // is released as soon as it has been read.
                 constexpr int kMine = kTiles == 2 ? kChunks : (kChunks >= 2 ? kChunks / 2 : 1);
                 const bool mine = c_begin < c_end && tile < p.ntiles;
-                if (mine && valid && p.skip != nullptr) {   // the residual reaches L2 while the tile accumulates
+                if (mine && valid && res_hi != nullptr) {   // the residual reaches L2 while the tile accumulates
                     const size_t off = size_t(q) * p.ld + size_t(c_begin) * 32;
 #pragma unroll
                     for (int cc = 0; cc < kMine; ++cc) {
-                        prefetch_l2(static_cast<const float*>(p.skip) + off + cc * 32);
-                        prefetch_l2(static_cast<const float*>(p.skip_lo) + off + cc * 32);
+                        prefetch_l2(static_cast<const float*>(res_hi) + off + cc * 32);
+                        prefetch_l2(static_cast<const float*>(res_lo) + off + cc * 32);
                     }
                 }
                 float sum[kMine * 32];
@@ -811,16 +837,23 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                 }
                 if (!ok) break;
                 if (mine)
-                    store_split_sums<N, kMine>(p, sm.bn, sum, &mOut, &mSkip, ew.obuf, tile * 128 + quarter * 32, q, valid,
-                                               c_begin, lane);
+                    store_split_sums<N, kMine>(p, scale, shift, res_hi, res_lo, sum, omap, smap, ew.obuf,
+                                               tile * 128 + quarter * 32, q, valid, c_begin, lane);
+                if constexpr (kPersist) {
+                    if (lane == 0) {   // this warp's part of the item has landed in global memory
+                        bulk_wait_all();
+                        fence_proxy_async_global();
+                        flag_add_release(p.flags + it, 1u);
+                    }
+                }
             } else {
                 const uint32_t acc = j & 1;
                 if (!mbar_wait(&sm.acc_full[acc], (j >> 1) & 1, p.err, kErrWaitEpilogue)) break;
                 tc_fence_after();
                 const uint32_t taddr = lanes + acc * (kTiles * C::kTileCols);
                 if constexpr (C::kEpiTma)
-                    store_epilogue_tma<N, kBf16>(p, scale, shift, has_skip, omap, smap, taddr, tile * 128 + quarter * 32,
-                                                 valid, c_begin, c_end, ew, lane);
+                    store_epilogue_tma<N, kBf16>(p, scale, shift, res_hi != nullptr, omap, smap, taddr,
+                                                 tile * 128 + quarter * 32, valid, c_begin, c_end, ew, lane);
                 else if (tile < p.ntiles)
                     store_epilogue_split<N>(p, sm.bn, taddr, q, valid, c_begin, c_end);
                 tc_fence_before();
@@ -1164,8 +1197,7 @@ cudaError_t launch_single_seg(const ConvMaps& m, ConvArgs a, int sms, cudaStream
     const int groups = (a.ntiles + kTiles - 1) / kTiles;
     const int grid = std::max(1, std::min(groups, sms));
     return launch_pdl(conv3x3_tc<N, kBf16, kSplit, kTiles, kSeg>, dim3(grid), dim3(kThreadsOf<kTiles>), smem, s, m.a,
-                      m.a_lo,
-                      m.w, m.w_lo, m.out, C::kStack ? m.out_lo : m.skip, a);
+                      m.a_lo, m.w, m.w_lo, m.out, C::kStack ? m.out_lo : m.skip, a, NoFrames{});
 }
 
 // The stacked split mode runs in segments of kDefaultSegment<N> taps unless
@@ -1178,35 +1210,35 @@ cudaError_t launch_single(const ConvMaps& m, ConvArgs a, int sms, cudaStream_t s
     return launch_single_seg<N, kBf16, kSplit, kTiles, 0>(m, a, sms, s);
 }
 
-// The persistent tower: two tiles per item where both halos and two weight
-// stages fit (128 channels or fewer), else one; a CTA per SM at most.
-template <int N, bool kBf16, int kTiles>
-cudaError_t launch_persist_tiles(const CUtensorMap (&in)[3], const CUtensorMap (&out)[3], ConvArgs a, int sms,
-                                 cudaStream_t s) {
-    using C = ConvCfg<N, kBf16, false, kTiles>;
-    conv_smem_bytes(N, kBf16 ? kBF16 : kTF32, a.halo_rows, &a.sa, &a.sb, false, kTiles);
+// The persistent tower: bf16 and tf32 take two tiles per item where both
+// halos and two weight stages fit (128 channels or fewer), else one; the
+// split mode one tile in its default segments. A CTA per SM at most. The six
+// per-layer map parameters are unused (valid maps, for the prefetch).
+template <int N, bool kBf16, bool kSplit, int kTiles, int kSeg>
+cudaError_t launch_persist_tiles(const TowerFrames& f, ConvArgs a, int sms, cudaStream_t s) {
+    using C = ConvCfg<N, kBf16, kSplit, kTiles>;
+    conv_smem_bytes(N, kBf16 ? kBF16 : (kSplit ? kTF32x3 : kTF32), a.halo_rows, &a.sa, &a.sb, false, kTiles);
     const size_t smem = smem_total(a.sa, a.sb, C::kOps * kTiles, C::kOps, a.a_bytes, C::kBBytes, C::kEpiBytes);
     static std::atomic<size_t> configured{0};
     if (smem > configured.load()) {
-        const cudaError_t e = cudaFuncSetAttribute(conv3x3_tc<N, kBf16, false, kTiles, 0, true>,
+        const cudaError_t e = cudaFuncSetAttribute(conv3x3_tc<N, kBf16, kSplit, kTiles, kSeg, true>,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
         if (e != cudaSuccess) return e;
         configured = smem;
     }
     const int groups = (a.ntiles + kTiles - 1) / kTiles;
     const int grid = std::max(1, std::min(groups * a.layers, sms));
-    return launch_pdl(conv3x3_tc<N, kBf16, false, kTiles, 0, true>, dim3(grid), dim3(kThreadsOf<kTiles>), smem, s,
-                      in[0], in[1], in[2], out[0], out[1], out[2], a);
+    return launch_pdl(conv3x3_tc<N, kBf16, kSplit, kTiles, kSeg, true>, dim3(grid), dim3(kThreadsOf<kTiles>), smem, s,
+                      f.in[0], f.in_lo[0], f.in[0], f.in_lo[0], f.out[0], f.out_lo[0], a, f);
 }
 
 template <int N, bool kBf16>
-cudaError_t launch_persist(const CUtensorMap (&in)[3], const CUtensorMap (&out)[3], const ConvArgs& a, int sms,
-                           cudaStream_t s) {
+cudaError_t launch_persist(const TowerFrames& f, const ConvArgs& a, int sms, cudaStream_t s) {
     if constexpr (N <= 128) {
         if (conv_smem_bytes(N, kBf16 ? kBF16 : kTF32, a.halo_rows, nullptr, nullptr, false, 2) <= 227 * 1024)
-            return launch_persist_tiles<N, kBf16, 2>(in, out, a, sms, s);
+            return launch_persist_tiles<N, kBf16, false, 2, 0>(f, a, sms, s);
     }
-    return launch_persist_tiles<N, kBf16, 1>(in, out, a, sms, s);
+    return launch_persist_tiles<N, kBf16, false, 1, 0>(f, a, sms, s);
 }
 
 template <int N, bool kBf16, bool kSplit>
@@ -1298,23 +1330,32 @@ bool tower_starve() { return g_tower_starve.load() != 0; }
 
 bool tower_persistent(int n_out, int precision) {
     const int mode = g_tower_persistent.load();
-    if (mode == 0 || precision == kTF32x3) return false;
+    if (mode == 0) return false;
+    // The split mode: in its default segments, at the widths whose weight
+    // planes stack (the 256-channel split layers run per layer).
+    if (precision == kTF32x3 && (n_out > 128 || g_conv_segment.load() == 0)) return false;
     if (mode == 1) return true;
     return n_out <= 128;
 }
 
-cudaError_t launch_tower_persistent(const CUtensorMap (&in)[3], const CUtensorMap (&out)[3], const ConvArgs& a,
-                                    int n_out, int precision, int sms, cudaStream_t s) {
+cudaError_t launch_tower_persistent(const TowerFrames& f, const ConvArgs& a, int n_out, int precision, int sms,
+                                    cudaStream_t s) {
     if (a.ntiles <= 0 || a.layers <= 0) return cudaSuccess;
-    if (precision == kTF32x3 || a.tower == nullptr || a.flags == nullptr) return cudaErrorNotSupported;
+    if (a.tower == nullptr || a.flags == nullptr) return cudaErrorNotSupported;
+    if (precision == kTF32x3) {
+        switch (n_out) {
+            case 32: return launch_persist_tiles<32, false, true, 1, kDefaultSegment<32>>(f, a, sms, s);
+            case 64: return launch_persist_tiles<64, false, true, 1, kDefaultSegment<64>>(f, a, sms, s);
+            case 128: return launch_persist_tiles<128, false, true, 1, kDefaultSegment<128>>(f, a, sms, s);
+            default: return cudaErrorNotSupported;
+        }
+    }
     const bool bf16 = precision == kBF16;
     switch (n_out) {
-        case 32: return bf16 ? launch_persist<32, true>(in, out, a, sms, s) : launch_persist<32, false>(in, out, a, sms, s);
-        case 64: return bf16 ? launch_persist<64, true>(in, out, a, sms, s) : launch_persist<64, false>(in, out, a, sms, s);
-        case 128:
-            return bf16 ? launch_persist<128, true>(in, out, a, sms, s) : launch_persist<128, false>(in, out, a, sms, s);
-        case 256:
-            return bf16 ? launch_persist<256, true>(in, out, a, sms, s) : launch_persist<256, false>(in, out, a, sms, s);
+        case 32: return bf16 ? launch_persist<32, true>(f, a, sms, s) : launch_persist<32, false>(f, a, sms, s);
+        case 64: return bf16 ? launch_persist<64, true>(f, a, sms, s) : launch_persist<64, false>(f, a, sms, s);
+        case 128: return bf16 ? launch_persist<128, true>(f, a, sms, s) : launch_persist<128, false>(f, a, sms, s);
+        case 256: return bf16 ? launch_persist<256, true>(f, a, sms, s) : launch_persist<256, false>(f, a, sms, s);
         default: return cudaErrorNotSupported;
     }
 }

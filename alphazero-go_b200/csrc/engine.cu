@@ -808,7 +808,16 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
         a.flags = ws.tower_flags;
         a.flag_extra = tower_starve() ? 1u : 0u;
         mark_begin(kSlotTower);
-        check(launch_tower_persistent(ws.map, ws.emap, a, w.n_out(), precision, dev.sms, s), "persistent tower");
+        TowerFrames tf;
+        for (int i = 0; i < 3; ++i) {
+            tf.in[i] = ws.map[i];
+            tf.in_lo[i] = ws.map_lo[i];
+            tf.out[i] = ws.emap[i];
+            tf.out_lo[i] = ws.emap_lo[i];
+            tf.trunk[i] = ws.trunk[i];
+            tf.trunk_lo[i] = ws.trunk_lo[i];
+        }
+        check(launch_tower_persistent(tf, a, w.n_out(), precision, dev.sms, s), "persistent tower");
         mark_end(kSlotTower);
         for (int i = 1; i < 2 * sh.blocks; ++i) {   // the per-conv slots, empty
             mark_begin(kSlotTower + i);

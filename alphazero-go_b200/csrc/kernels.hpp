@@ -99,6 +99,14 @@ struct ConvArgs {
     unsigned flag_extra;   // 0; the failure-detection test's 1 makes every wait for a previous layer run out
 };
 
+// The three frame buffers as the persistent tower addresses them.
+struct TowerFrames {
+    CUtensorMap in[3], in_lo[3];     // halo boxes {chunk, halo_rows} (in_lo: the split mode's low planes)
+    CUtensorMap out[3], out_lo[3];   // the epilogue's {32, 32} boxes
+    const void* trunk[3];            // the frames (the split mode reads its residual directly)
+    const void* trunk_lo[3];
+};
+
 struct ConvMaps {
     CUtensorMap a, a_lo;             // input activations: box {chunk, halo_rows}
     CUtensorMap w, w_lo;             // weights [N][9*Cin]: box {chunk, N}
@@ -125,19 +133,19 @@ void set_conv_path(int path);
 void set_conv_segment(int steps);
 
 // The persistent tower: every tower conv (a.layers of them, a.tower's
-// entries) in one launch of at most one CTA per SM (bf16 and tf32; the
-// split mode runs per layer). CTAs take (layer, tile group) items in
-// layer-major order from a counter; an item's halo loads wait for the three
-// groups of the previous layer whose rows they read. Tower conv l reads
-// frame buffer l mod 3 and writes (l+1) mod 3; a block's second conv adds
-// (l-1) mod 3, the block's input. in[i]: the frames in halo boxes; out[i]:
-// in the epilogue's {32, 32} boxes.
+// entries) in one launch of at most one CTA per SM (bf16 and tf32 at any
+// width, the split mode at 128 channels or fewer). CTAs take (layer, tile
+// group) items in layer-major order from a counter; an item's halo loads
+// wait for the three groups of the previous layer whose rows they read.
+// Tower conv l reads frame buffer l mod 3 and writes (l+1) mod 3; a block's
+// second conv adds (l-1) mod 3, the block's input.
 // Returns cudaErrorNotSupported where it does not apply (the caller then
 // launches per layer).
-cudaError_t launch_tower_persistent(const CUtensorMap (&in)[3], const CUtensorMap (&out)[3], const ConvArgs& a,
-                                    int n_out, int precision, int sms, cudaStream_t s);
+cudaError_t launch_tower_persistent(const TowerFrames& f, const ConvArgs& a, int n_out, int precision, int sms,
+                                    cudaStream_t s);
 // Whether the persistent tower runs for n_out channels in `precision` (and
-// the test hook's choice: -1 the default, 0 per layer, 1 persistent).
+// the test hook's choice: -1 the default, 0 per layer, 1 persistent where
+// it applies). The split mode needs its default accumulation segments.
 bool tower_persistent(int n_out, int precision);
 void set_tower_persistent(int mode);
 // Test hook: nonzero makes the persistent tower wait for one counter step

@@ -177,15 +177,18 @@ __device__ __forceinline__ unsigned flag_load_acquire(const unsigned* flag) {
     return v;
 }
 
-// Waits until *flag >= target, for at most kWaitLimitNs. On timeout records
-// `code` in *err (first error wins) and returns false.
+// Waits until *flag >= target, for at most half of kWaitLimitNs: a wait for
+// another CTA's work starves this CTA's own pipeline waits (bounded by
+// kWaitLimitNs), so it must run out first for the error word to name the
+// cause. On timeout records `code` in *err (first error wins) and returns
+// false.
 __device__ __forceinline__ bool flag_wait(const unsigned* flag, unsigned target, int* err, int code) {
     if (flag_load_acquire(flag) >= target) return true;
     const uint64_t start = global_timer();
     for (;;) {
         __nanosleep(100);
         if (flag_load_acquire(flag) >= target) return true;
-        if (global_timer() - start > kWaitLimitNs) {
+        if (global_timer() - start > kWaitLimitNs / 2) {
             atomicCAS(err, 0, code);
             return false;
         }

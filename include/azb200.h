@@ -254,9 +254,10 @@ void azb_probe_set_tower_fused(int mode);
 void azb_probe_set_tower_persistent(int mode);
 /* Nonzero: the persistent tower waits for one counter step more than its
  * epilogue warps add, so its first wait for a previous layer runs out (after
- * its 1 s bound) and the pass fails with "cuda: the persistent tower waited
- * too long for the previous layer"; the next pass runs normally. For the
- * failure-detection test. */
+ * its bound of half a second, before the pipeline waits it starves) and the
+ * pass fails with "cuda: the persistent tower waited too long for the
+ * previous layer"; the next pass runs normally. For the failure-detection
+ * test. */
 void azb_probe_starve_tower(int on);
 /* cuda_probe::binaryVersion / deviceArchitecture / fill (include/azgo/cuda.hpp:93-103). */
 int azb_probe_binary_version(int device);

@@ -1,7 +1,8 @@
 """The persistent tower (alphazero-go_b200/csrc/conv_tc.cu, kPersist): every
-tower conv of a bf16 or tf32 network in one launch, CTAs taking (layer, tile
-group) items from a counter, each item's halo loads waiting (bounded) for
-the previous layer's groups whose rows they read.
+tower conv of a network in one launch (bf16 and tf32; tf32x3 at 128 channels
+or fewer, in its accumulation segments), CTAs taking (layer, tile group)
+items from a counter, each item's halo loads waiting (bounded) for the
+previous layer's groups whose rows they read.
 
 Each item runs the per-layer kernel's MMAs and epilogue on the same rows,
 so its outputs must equal the per-layer path's bit for bit (logits, values,
@@ -29,7 +30,7 @@ def _run(engine, c, params, buffers, x, precision, persistent):
         engine.cuda_probe.set_tower_persistent(-1)
 
 
-@pytest.mark.parametrize("precision", ["bf16", "tf32"])
+@pytest.mark.parametrize("precision", ["bf16", "tf32", "tf32x3"])
 @pytest.mark.parametrize("shape,B", [((19, 2, 64, 1, False), 64), ((19, 3, 128, 1, False), 7), ((13, 2, 32, 8, True), 5),
                                      ((11, 1, 64, 1, False), 1), ((19, 2, 128, 1, True), 200),
                                      ((19, 1, 256, 1, False), 33), ((15, 4, 64, 2, False), 300)])
