@@ -511,12 +511,12 @@ class cuda_probe:
 
     @staticmethod
     def set_tower_persistent(mode: int):
-        """bf16/tf32 towers too large to fuse: -1 default (one persistent launch at <= 128 channels), 0 per layer, 1 always."""
+        """Towers too large to fuse: -1 default (one persistent launch at <= 128 channels), 0 per layer, 1 at any width (bf16/tf32)."""
         lib().azb_probe_set_tower_persistent(mode)
 
     @staticmethod
     def starve_tower(on: bool):
-        """Failure detection: the persistent tower's waits for a previous layer run out (1 s) and the pass fails."""
+        """Failure detection: the persistent tower's waits for a previous layer run out (0.5 s) and the pass fails."""
         lib().azb_probe_starve_tower(1 if on else 0)
 
     @staticmethod

@@ -430,15 +430,15 @@ __device__ __forceinline__ void store_split_sums(const ConvArgs& p, const float*
 // per tile). mOut/mSkip: the epilogue's output and residual boxes; in the
 // stacked split mode the high and low output planes.
 //
-// kPersist: the persistent tower (bf16 and tf32). Items are (layer, tile
-// group) = (it / ngroups, it % ngroups); the producer takes the pass's next
-// item from a global counter and hands its index to the MMA and epilogue
-// warps through a shared-memory ring. Every item's dependencies have lower
-// indices and were therefore taken by CTAs already running, so the tower
-// progresses however many of its CTAs are resident (another stream's
-// kernels may hold SMs, a second tower among them). The six maps are then the
-// three frames in halo boxes (mA, mAlo, mW) and in the epilogue's boxes
-// (mWlo, mOut, mSkip); the weights and batch norms come from p.tower. Each
+// kPersist: the persistent tower (bf16 and tf32; the stacked split mode in
+// its segments). Items are (layer, tile group) = (it / ngroups, it %
+// ngroups); the producer takes the pass's next item from a global counter
+// and hands its index to the MMA and epilogue warps through a shared-memory
+// ring. Every item's dependencies have lower indices and were therefore
+// taken by CTAs already running, so the tower progresses however many of
+// its CTAs are resident (another stream's kernels may hold SMs, a second
+// tower among them). The frames come from tf (the six map parameters are
+// then unused), the weights and batch norms from p.tower. Each
 // epilogue warp adds 1 to its item's counter once its stores have landed;
 // an item's halo loads wait until the counters of the previous layer's
 // groups g-1, g, g+1 (the rows its halo reads) have reached kEpiWarps.

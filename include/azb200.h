@@ -245,12 +245,13 @@ void azb_probe_set_conv_segment(int steps);
  * same arithmetic as the per-layer kernels, bit for bit). -1 the default,
  * 0 the per-layer kernels always. For tests and measurements. */
 void azb_probe_set_tower_fused(int mode);
-/* Larger boards in bf16 and tf32 run every tower conv in one persistent
- * launch: CTAs take (layer, tile group) items in order, each waiting for the
+/* Towers that do not fuse run every tower conv in one persistent launch:
+ * CTAs take (layer, tile group) items in order, each waiting for the
  * previous layer's groups its halo reads (bounded waits; the same
  * arithmetic as the per-layer kernels, bit for bit). -1 the default (128
- * or fewer channels), 0 per layer always, 1 at any width. For tests and
- * measurements. */
+ * or fewer channels, every precision), 0 per layer always, 1 at any width
+ * (bf16 and tf32; TF32X3 only up to 128 channels, in its default
+ * accumulation segments). For tests and measurements. */
 void azb_probe_set_tower_persistent(int mode);
 /* Nonzero: the persistent tower waits for one counter step more than its
  * epilogue warps add, so its first wait for a previous layer runs out (after
