@@ -244,6 +244,19 @@ __device__ __forceinline__ void store_epilogue_split(const ConvArgs& p, const fl
 // stay zero), rows past the frame are clipped by TMA. The residual input
 // arrives the same way, one chunk ahead, in two boxes. Same arithmetic as
 // store_epilogue.
+// What an epilogue item reads and writes besides its accumulator: the
+// folded batch norm, the residual (null: none), the output's boxes (split:
+// its high plane) and the residual's boxes (stacked split: the output's low
+// plane).
+struct ItemIo {
+    const float* scale;
+    const float* shift;
+    const void* res_hi;
+    const void* res_lo;
+    const CUtensorMap* omap;
+    const CUtensorMap* smap;
+};
+
 struct EpiWarp {
     uint8_t* obuf;        // 2 output boxes
     uint8_t* sbuf;        // 2 residual boxes
@@ -758,6 +771,24 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
         ew.sbar = sm.skip_full + 2 * e;
         uint32_t j = 0;   // accumulator runs consumed (one per tile, or one per segment)
         const int segs = kSeg == 0 ? 1 : (p.taps == 1 ? p.nchunks : p.nchunks * (9 / (kSeg > 0 ? kSeg : 1)));
+        // An item's ItemIo, derived where it is used rather than held across
+        // the segments' accumulation (registers are at the 168 cap).
+        auto item_io = [&](int layer) {
+            ItemIo io{sm.bn, sm.bn + N, p.skip, p.skip_lo, &mOut, &mSkip};
+            if constexpr (kPersist) {
+                // Tower conv l writes buffer (l+1) mod 3; a block's second conv
+                // (l odd) adds its first conv's input, buffer (l-1) mod 3.
+                const int out = (layer + 1) % 3, res = (layer + 2) % 3;
+                const bool has_res = (layer & 1) != 0;
+                io.res_hi = has_res ? tf.trunk[res] : nullptr;
+                io.res_lo = has_res ? tf.trunk_lo[res] : nullptr;
+                io.omap = &tf.out[out];
+                io.smap = kSplit ? &tf.out_lo[out] : &tf.out[res];
+                io.scale = p.tower[layer].scale;
+                io.shift = p.tower[layer].shift;
+            }
+            return io;
+        };
         Ring ri;
         for (int k = 0;; ++k) {
             int it = blockIdx.x + k * int(gridDim.x);
@@ -770,26 +801,10 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                 if (it < 0) break;
             }
             if (it >= nitems) break;
-            int g = it;
-            const float* scale = sm.bn;
-            const float* shift = sm.bn + N;
-            const void* res_hi = p.skip;   // the residual (null: none)
-            const void* res_lo = p.skip_lo;
-            const CUtensorMap* omap = &mOut;    // the output (split: its high plane)
-            const CUtensorMap* smap = &mSkip;   // the residual's boxes (stacked split: the output's low plane)
+            int g = it, layer = 0;
             if constexpr (kPersist) {
-                const int layer = it / ngroups;
+                layer = it / ngroups;
                 g = it - layer * ngroups;
-                // Tower conv l writes buffer (l+1) mod 3; a block's second conv
-                // (l odd) adds its first conv's input, buffer (l-1) mod 3.
-                const int out = (layer + 1) % 3, res = (layer + 2) % 3;
-                const bool has_res = (layer & 1) != 0;
-                res_hi = has_res ? tf.trunk[res] : nullptr;
-                res_lo = has_res ? tf.trunk_lo[res] : nullptr;
-                omap = &tf.out[out];
-                smap = kSplit ? &tf.out_lo[out] : &tf.out[res];
-                scale = p.tower[layer].scale;
-                shift = p.tower[layer].shift;
                 if (layer > 0) {
                     // This warp reads the residual and overwrites rows that
                     // earlier items read: acquire the previous layer's group
@@ -816,12 +831,15 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                 // is released as soon as it has been read.
                 constexpr int kMine = kTiles == 2 ? kChunks : (kChunks >= 2 ? kChunks / 2 : 1);
                 const bool mine = c_begin < c_end && tile < p.ntiles;
-                if (mine && valid && res_hi != nullptr) {   // the residual reaches L2 while the tile accumulates
-                    const size_t off = size_t(q) * p.ld + size_t(c_begin) * 32;
+                if (mine && valid) {   // the residual reaches L2 while the tile accumulates
+                    const ItemIo io = item_io(layer);
+                    if (io.res_hi != nullptr) {
+                        const size_t off = size_t(q) * p.ld + size_t(c_begin) * 32;
 #pragma unroll
-                    for (int cc = 0; cc < kMine; ++cc) {
-                        prefetch_l2(static_cast<const float*>(res_hi) + off + cc * 32);
-                        prefetch_l2(static_cast<const float*>(res_lo) + off + cc * 32);
+                        for (int cc = 0; cc < kMine; ++cc) {
+                            prefetch_l2(static_cast<const float*>(io.res_hi) + off + cc * 32);
+                            prefetch_l2(static_cast<const float*>(io.res_lo) + off + cc * 32);
+                        }
                     }
                 }
                 float sum[kMine * 32];
@@ -836,9 +854,11 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                     if (lane == 0) mbar_arrive(&sm.acc_empty[acc]);
                 }
                 if (!ok) break;
-                if (mine)
-                    store_split_sums<N, kMine>(p, scale, shift, res_hi, res_lo, sum, omap, smap, ew.obuf,
-                                               tile * 128 + quarter * 32, q, valid, c_begin, lane);
+                if (mine) {
+                    const ItemIo io = item_io(layer);
+                    store_split_sums<N, kMine>(p, io.scale, io.shift, io.res_hi, io.res_lo, sum, io.omap, io.smap,
+                                               ew.obuf, tile * 128 + quarter * 32, q, valid, c_begin, lane);
+                }
                 if constexpr (kPersist) {
                     if (lane == 0) {   // this warp's part of the item has landed in global memory
                         bulk_wait_all();
@@ -851,8 +871,9 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                 if (!mbar_wait(&sm.acc_full[acc], (j >> 1) & 1, p.err, kErrWaitEpilogue)) break;
                 tc_fence_after();
                 const uint32_t taddr = lanes + acc * (kTiles * C::kTileCols);
+                const ItemIo io = item_io(layer);
                 if constexpr (C::kEpiTma)
-                    store_epilogue_tma<N, kBf16>(p, scale, shift, res_hi != nullptr, omap, smap, taddr,
+                    store_epilogue_tma<N, kBf16>(p, io.scale, io.shift, io.res_hi != nullptr, io.omap, io.smap, taddr,
                                                  tile * 128 + quarter * 32, valid, c_begin, c_end, ew, lane);
                 else if (tile < p.ntiles)
                     store_epilogue_split<N>(p, sm.bn, taddr, q, valid, c_begin, c_end);
