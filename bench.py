@@ -627,7 +627,10 @@ def run_sweep(args):
             with E.CudaInference(desc, params, buffers, B, 0, prec) as net:
                 net.stage(x)
                 steps = 50 if B * n * n * filters < 1 << 26 else 10
-                ms, conv_ms = net.time(B, 5, steps, conv=True)
+                # Passes as they run (events around the timed loop only), then
+                # the conv kernels alone (events around every launch).
+                ms, _ = net.time(B, 5, steps)
+                _, conv_ms = net.time(B, 2, steps, conv=True)
             runner = E.make_cuda_runner(desc, params, buffers, B, 2, 0, prec)
             for sl in range(2):
                 runner.input(sl)[:] = x
