@@ -549,7 +549,7 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                     ri.next(kItemSlots);
                 }
                 if (it >= nitems) break;
-                int g = it;
+                int g = it, taps = p.taps, nchunks = p.nchunks;
                 const CUtensorMap* amap = &mA;
                 const CUtensorMap* alo = &mAlo;
                 const CUtensorMap* wmap = &mW;
@@ -557,11 +557,20 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                 if constexpr (kPersist) {
                     const int layer = it / ngroups;
                     g = it - layer * ngroups;
-                    const int in = layer % 3;   // tower conv l reads buffer l mod 3
-                    amap = &tf.in[in];
-                    alo = &tf.in_lo[in];
-                    wmap = &p.tower[layer].w;
-                    wlo = &p.tower[layer].w_lo;
+                    const int conv = layer - p.stem_first;   // the tower conv; -1: the stem
+                    if (conv < 0) {   // the stem: one tap over its packed operand
+                        amap = &tf.stem;
+                        alo = &tf.stem_lo;
+                        taps = 1;
+                        nchunks = p.stem_nchunks;
+                    } else {
+                        const int in = conv % 3;   // tower conv l reads buffer l mod 3
+                        amap = &tf.in[in];
+                        alo = &tf.in_lo[in];
+                    }
+                    const FusedLayer& fl = p.tower[conv < 0 ? p.layers - 1 : conv];
+                    wmap = &fl.w;
+                    wlo = &fl.w_lo;
                     if (layer > 0) {   // the previous layer's groups whose rows this item's halos read
                         const unsigned* prev = p.flags + size_t(layer - 1) * ngroups;
                         for (int d = g > 0 ? g - 1 : 0; d <= g + 1 && d < ngroups && ok; ++d)
@@ -570,7 +579,7 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                         fence_proxy_async_global();   // the loads below (async proxy) after the acquires
                     }
                 }
-                for (int c = 0; c < p.nchunks && ok; ++c) {
+                for (int c = 0; c < nchunks && ok; ++c) {
                     if (!(ok = mbar_wait(&sm.a_empty[ra.idx], ra.phase ^ 1u, p.err, kErrWaitProducer))) break;
                     mbar_arrive_expect_tx(&sm.a_full[ra.idx], a_tx);
 #pragma unroll
@@ -582,12 +591,12 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                     }
                     ra.next(p.sa);
                     ++na;
-                    for (int t = 0; t < p.taps; ++t) {
+                    for (int t = 0; t < taps; ++t) {
                         if (!(ok = mbar_wait(&sm.b_empty[rb.idx], rb.phase ^ 1u, p.err, kErrWaitProducer))) break;
                         mbar_arrive_expect_tx(&sm.b_full[rb.idx], b_tx);
                         uint8_t* bbuf = sm.b + rb.idx * (C::kOps * C::kBBytes);
-                        tma_load_2d(wmap, bbuf, &sm.b_full[rb.idx], (c * p.taps + t) * C::kKc, 0);
-                        if (kSplit) tma_load_2d(wlo, bbuf + C::kBBytes, &sm.b_full[rb.idx], (c * p.taps + t) * C::kKc, 0);
+                        tma_load_2d(wmap, bbuf, &sm.b_full[rb.idx], (c * taps + t) * C::kKc, 0);
+                        if (kSplit) tma_load_2d(wlo, bbuf + C::kBBytes, &sm.b_full[rb.idx], (c * taps + t) * C::kKc, 0);
                         rb.next(p.sb);
                         ++nb;
                     }
@@ -640,19 +649,27 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                         if (it < 0) break;
                     }
                     if (it >= nitems) break;
+                    // The persistent tower's stem item: one tap, the centre view.
+                    int taps = p.taps, nchunks = p.nchunks;
+                    uint32_t off0 = toff[0];
+                    if (kPersist && it < p.stem_first * ngroups) {
+                        taps = 1;
+                        nchunks = p.stem_nchunks;
+                        off0 = toff[4];
+                    }
                     const uint32_t acc = j & 1;
                     if (!(ok = mbar_wait(&sm.acc_empty[acc], ((j >> 1) & 1) ^ 1, p.err, kErrWaitMma))) break;
                     tc_fence_after();
                     const uint32_t d = tmem_mine + acc * (kTiles * C::kTileCols);   // tile u's at + u * kTileCols
-                    for (int c = 0; c < p.nchunks && ok; ++c) {
+                    for (int c = 0; c < nchunks && ok; ++c) {
                         if (!(ok = mbar_wait(&sm.a_full[ra.idx], ra.phase, p.err, kErrWaitMma))) break;
                         const uint64_t ac = a_desc + ra.idx * a_stage;
 #pragma unroll
                         for (int t = 0; t < 9; ++t) {
-                            if (t >= p.taps) break;
+                            if (t >= taps) break;
                             if (!(ok = mbar_wait(&sm.b_full[rb.idx], rb.phase, p.err, kErrWaitMma))) break;
                             tc_fence_after();
-                            const uint64_t at = ac + toff[t], bt = b_desc + rb.idx * b_stage;
+                            const uint64_t at = ac + (t == 0 ? off0 : toff[t]), bt = b_desc + rb.idx * b_stage;
 #pragma unroll
                             for (int k = 0; k < C::kSteps; ++k) {
 #pragma unroll
@@ -693,7 +710,6 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                 // tap positions: a counter and branch per tap in this thread
                 // would slow every MMA after it.
                 static_assert(C::kStack && 9 % kSeg == 0, "segments: stacked split mode, kSeg divides 9");
-                const bool one_tap = p.taps == 1;
                 Ring ri;
                 for (int k = 0; ok; ++k) {
                     int it = blockIdx.x + k * int(gridDim.x);
@@ -705,13 +721,22 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                         if (it < 0) break;
                     }
                     if (it >= nitems) break;
+                    // The persistent tower's stem item: one tap, the centre view.
+                    int taps = p.taps, nchunks = p.nchunks;
+                    uint32_t off0 = toff[0];
+                    if (kPersist && it < p.stem_first * ngroups) {
+                        taps = 1;
+                        nchunks = p.stem_nchunks;
+                        off0 = toff[4];
+                    }
+                    const bool one_tap = taps == 1;
                     uint32_t acc = 0, d = 0;
-                    for (int c = 0; c < p.nchunks && ok; ++c) {
+                    for (int c = 0; c < nchunks && ok; ++c) {
                         if (!(ok = mbar_wait(&sm.a_full[ra.idx], ra.phase, p.err, kErrWaitMma))) break;
                         const uint64_t ac = a_desc + ra.idx * a_stage;
 #pragma unroll
                         for (int t = 0; t < 9; ++t) {
-                            if (t >= p.taps) break;
+                            if (t >= taps) break;
                             if (t % kSeg == 0) {   // open a segment on the next accumulator
                                 acc = j & 1;
                                 if (!(ok = mbar_wait(&sm.acc_empty[acc], ((j >> 1) & 1) ^ 1, p.err, kErrWaitMma))) break;
@@ -719,7 +744,7 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                             }
                             if (!(ok = mbar_wait(&sm.b_full[rb.idx], rb.phase, p.err, kErrWaitMma))) break;
                             tc_fence_after();
-                            const uint64_t at = ac + toff[t], bt = b_desc + rb.idx * b_stage;
+                            const uint64_t at = ac + (t == 0 ? off0 : toff[t]), bt = b_desc + rb.idx * b_stage;
 #pragma unroll
                             for (int k = 0; k < C::kSteps; ++k) {
 #pragma unroll
@@ -770,22 +795,31 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
         ew.sbuf = ew.obuf + C::kEpiBytes / kEpiWarps / 2;
         ew.sbar = sm.skip_full + 2 * e;
         uint32_t j = 0;   // accumulator runs consumed (one per tile, or one per segment)
-        const int segs = kSeg == 0 ? 1 : (p.taps == 1 ? p.nchunks : p.nchunks * (9 / (kSeg > 0 ? kSeg : 1)));
+        // Accumulator runs per tile: one, or the split mode's segments (a
+        // one-tap pass: one per chunk); the persistent tower's stem items
+        // are one-tap.
+        auto segs_of = [&](int taps, int nchunks) {
+            return kSeg == 0 ? 1 : (taps == 1 ? nchunks : nchunks * (9 / (kSeg > 0 ? kSeg : 1)));
+        };
+        const int layer_segs = segs_of(p.taps, p.nchunks);
         // An item's ItemIo, derived where it is used rather than held across
         // the segments' accumulation (registers are at the 168 cap).
         auto item_io = [&](int layer) {
             ItemIo io{sm.bn, sm.bn + N, p.skip, p.skip_lo, &mOut, &mSkip};
             if constexpr (kPersist) {
                 // Tower conv l writes buffer (l+1) mod 3; a block's second conv
-                // (l odd) adds its first conv's input, buffer (l-1) mod 3.
-                const int out = (layer + 1) % 3, res = (layer + 2) % 3;
-                const bool has_res = (layer & 1) != 0;
+                // (l odd) adds its first conv's input, buffer (l-1) mod 3. The
+                // stem (l = -1) writes buffer 0 and adds nothing.
+                const int conv = layer - p.stem_first;
+                const int out = (conv + 4) % 3, res = (conv + 2) % 3;
+                const bool has_res = conv >= 0 && (conv & 1) != 0;
                 io.res_hi = has_res ? tf.trunk[res] : nullptr;
                 io.res_lo = has_res ? tf.trunk_lo[res] : nullptr;
                 io.omap = &tf.out[out];
-                io.smap = kSplit ? &tf.out_lo[out] : &tf.out[res];
-                io.scale = p.tower[layer].scale;
-                io.shift = p.tower[layer].shift;
+                io.smap = kSplit ? &tf.out_lo[out] : &tf.out[has_res ? res : out];
+                const FusedLayer& fl = p.tower[conv < 0 ? p.layers - 1 : conv];
+                io.scale = fl.scale;
+                io.shift = fl.shift;
             }
             return io;
         };
@@ -844,6 +878,8 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                 }
                 float sum[kMine * 32];
                 bool ok = true;
+                const bool stem_item = kPersist && layer < p.stem_first;
+                const int segs = stem_item ? segs_of(1, p.stem_nchunks) : layer_segs;
                 for (int sg = 0; sg < segs; ++sg, ++j) {
                     const uint32_t acc = j & 1;
                     if (!(ok = mbar_wait(&sm.acc_full[acc], (j >> 1) & 1, p.err, kErrWaitEpilogue))) break;

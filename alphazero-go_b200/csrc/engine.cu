@@ -563,11 +563,11 @@ size_t feat_floats(const NetShape& s) {
 }
 
 namespace {
-// The persistent tower's counters: one per tower conv and 128-row tile of a
-// full batch, and the next-item counter.
+// The persistent tower's counters: one per layer (the stem and the tower
+// convs) and 128-row tile of a full batch, and the next-item counter.
 size_t tower_flags_for(const NetShape& s, int max_batch) {
     const size_t tiles = (size_t(max_batch) * Frame(s.board).S + 127) / 128;
-    return size_t(2 * s.blocks) * tiles + 1;
+    return size_t(2 * s.blocks + 1) * tiles + 1;
 }
 } // namespace
 
@@ -719,10 +719,10 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
     const bool fused = ws.fused && g_tower_fused.load() != 0;
     const int pass_tiles = (B * fr.S + 127) / 128;
     const bool persistent = !fused && sh.blocks > 0 && ws.tower_flags != nullptr &&
-                            size_t(2 * sh.blocks) * size_t(pass_tiles) + 1 <= ws.tower_flag_count &&
+                            size_t(2 * sh.blocks + 1) * size_t(pass_tiles) + 1 <= ws.tower_flag_count &&
                             tower_persistent(w.n_out(), precision);
     st.flags = persistent ? ws.tower_flags : nullptr;
-    st.nflags = persistent ? 2 * sh.blocks * pass_tiles + 1 : 0;
+    st.nflags = persistent ? (2 * sh.blocks + 1) * pass_tiles + 1 : 0;
     mark_begin(kSlotStemPack);
     check(launch_stem_pack(st, precision, s), "stem operand");
     mark_end(kSlotStemPack);
@@ -754,8 +754,8 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
         mark_end(timer_slot);
     };
     // The stem: conv -> BN -> ReLU as one tap over the packed operand (in
-    // the fused tower's launch when that runs it).
-    if (fused && ws.fused_plan.stem_nch > 0) {
+    // the fused or the persistent tower's launch when that runs it).
+    if ((fused && ws.fused_plan.stem_nch > 0) || persistent) {
         mark_begin(kSlotStemGemm);
         mark_end(kSlotStemGemm);
     } else {
@@ -795,20 +795,25 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
             mark_end(kSlotTower + i);
         }
     } else if (persistent) {
-        // Every tower conv in one launch: conv l reads trunk[l % 3] and
-        // writes trunk[(l + 1) % 3], so the trunk ends in trunk[2·blocks % 3]
-        // as the per-layer rotation leaves it.
+        // The stem and every tower conv in one launch: the stem writes
+        // trunk[0], conv l reads trunk[l % 3] and writes trunk[(l + 1) % 3],
+        // so the trunk ends in trunk[2·blocks % 3] as the per-layer rotation
+        // leaves it.
         a.taps = 9;
         a.nchunks = tower_chunks;
         a.out = a.out_lo = nullptr;
         a.skip = a.skip_lo = nullptr;
         a.scale = a.shift = nullptr;
         a.tower = w.fused_layers();
-        a.layers = 2 * sh.blocks;
+        a.layers = 2 * sh.blocks + 1;
         a.flags = ws.tower_flags;
         a.flag_extra = tower_starve() ? 1u : 0u;
+        a.stem_first = 1;
+        a.stem_nchunks = w.kstem() / chunk_channels(precision);
         mark_begin(kSlotTower);
         TowerFrames tf;
+        tf.stem = ws.map_stem;
+        tf.stem_lo = ws.map_stem_lo;
         for (int i = 0; i < 3; ++i) {
             tf.in[i] = ws.map[i];
             tf.in_lo[i] = ws.map_lo[i];

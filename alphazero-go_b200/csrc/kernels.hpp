@@ -97,10 +97,16 @@ struct ConvArgs {
     int layers;
     unsigned* flags;
     unsigned flag_extra;   // 0; the failure-detection test's 1 makes every wait for a previous layer run out
+    // 1: the persistent tower's layer 0 is the stem, one tap over the stem's
+    // packed operand of stem_nchunks chunks (its weights the table's last
+    // entry), writing buffer 0; tower conv l is then layer l + 1.
+    int stem_first;
+    int stem_nchunks;
 };
 
 // The three frame buffers as the persistent tower addresses them.
 struct TowerFrames {
+    CUtensorMap stem, stem_lo;       // the stem's packed operand in halo boxes
     CUtensorMap in[3], in_lo[3];     // halo boxes {chunk, halo_rows} (in_lo: the split mode's low planes)
     CUtensorMap out[3], out_lo[3];   // the epilogue's {32, 32} boxes
     const void* trunk[3];            // the frames (the split mode reads its residual directly)
