@@ -70,10 +70,10 @@ struct ConvCfg {
     static_assert(N % 32 == 0 && N >= 32 && N <= 256, "N is a multiple of 32 in [32, 256]");
 };
 
-// The persistent tower's frame maps; nothing for the per-layer launches.
-struct NoFrames {};
+// The persistent tower's parameters; nothing for the per-layer launches.
+struct NoTower {};
 template <bool kPersist>
-using FramesOf = std::conditional_t<kPersist, TowerFrames, NoFrames>;
+using TowerOf = std::conditional_t<kPersist, TowerArgs, NoTower>;
 
 constexpr int kThreads = 320;   // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 // The two-tile form adds warp 10, which issues the second tile's MMAs: one
@@ -280,14 +280,17 @@ struct EpiBox {
 // box per role (kBufs 1, as built) the next chunk's residual is requested as
 // soon as this chunk's has been read, and the output box is refilled once
 // the previous store has read it; with two, one chunk ahead and two behind.
-template <int N, bool kBf16>
+// kOwnShift: the shift is its own array (the persistent tower's layer
+// table); otherwise it follows the scale (shared memory, shift at N).
+template <int N, bool kBf16, bool kOwnShift = false>
 __device__ __forceinline__ void store_epilogue_tma(const ConvArgs& p, const float* scale, const float* shift,
-                                                   bool skip, const CUtensorMap* omap, const CUtensorMap* smap,
+                                                   const void* res, const CUtensorMap* omap, const CUtensorMap* smap,
                                                    uint32_t taddr, int row0, bool valid, int c_begin, int c_end,
                                                    EpiWarp& ew, int lane) {
     using Box = EpiBox<kBf16>;
     constexpr uint32_t kBox = Box::kBytes;
     if (row0 >= p.rows || c_begin >= c_end) return;   // nothing of this warp's to store
+    const bool skip = res != nullptr;   // the residual, read through smap
     if (skip && lane == 0) {
         mbar_arrive_expect_tx(&ew.sbar[0], kBox);
         tma_load_2d(smap, ew.sbuf, &ew.sbar[0], c_begin * 32, row0);
@@ -305,7 +308,8 @@ __device__ __forceinline__ void store_epilogue_tma(const ConvArgs& p, const floa
         float y[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-            y[i] = __fadd_rn(__fmul_rn(scale[c * 32 + i], __uint_as_float(v[i])), shift[c * 32 + i]);
+            y[i] = __fadd_rn(__fmul_rn(scale[c * 32 + i], __uint_as_float(v[i])),
+                             kOwnShift ? shift[c * 32 + i] : scale[N + c * 32 + i]);
         if (skip) {
             mbar_wait(&ew.sbar[cb], (ew.sphase >> cb) & 1u, p.err, kErrWaitEpilogue);
             ew.sphase ^= 1u << cb;
@@ -451,7 +455,7 @@ __device__ __forceinline__ void store_split_sums(const ConvArgs& p, const float*
 // taken by CTAs already running, so the tower progresses however many of
 // its CTAs are resident (another stream's kernels may hold SMs, a second
 // tower among them). The frames come from tf (the six map parameters are
-// then unused), the weights and batch norms from p.tower. Each
+// then unused), the weights and batch norms from tf.tower. Each
 // epilogue warp adds 1 to its item's counter once its stores have landed;
 // an item's halo loads wait until the counters of the previous layer's
 // groups g-1, g, g+1 (the rows its halo reads) have reached kEpiWarps.
@@ -462,17 +466,18 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
     conv3x3_tc(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAlo,
                const __grid_constant__ CUtensorMap mW, const __grid_constant__ CUtensorMap mWlo,
                const __grid_constant__ CUtensorMap mOut, const __grid_constant__ CUtensorMap mSkip, const ConvArgs p,
-               const __grid_constant__ FramesOf<kPersist> tf) {
+               const __grid_constant__ TowerOf<kPersist> tf) {
     using C = ConvCfg<N, kBf16, kSplit, kTiles>;
     static_assert(!kPersist || (!kSplit && kSeg == 0) || (C::kStack && kSeg != 0 && kTiles == 1),
                   "the persistent tower: bf16 and tf32, or the split mode's segmented single tiles");
     extern __shared__ uint8_t smem_raw[];
     const Smem sm = carve(smem_raw, p.sa, p.sb, C::kOps * kTiles, C::kOps, p.a_bytes, C::kBBytes, C::kEpiBytes);
     const int ngroups = (p.ntiles + kTiles - 1) / kTiles;   // a CTA takes kTiles consecutive tiles at a time
-    const int nitems = kPersist ? p.layers * ngroups : ngroups;
+    int nitems = ngroups;
+    if constexpr (kPersist) nitems = tf.layers * ngroups;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // The persistent tower's item ring lives where the batch norm would (its
-    // batch norms are read from p.tower): kItemSlots full and empty barriers,
+    // batch norms are read from tf.tower): kItemSlots full and empty barriers,
     // then the slots' item indices (-1: no more items).
     constexpr int kItemSlots = 4;
     uint64_t* item_full = reinterpret_cast<uint64_t*>(sm.bn);
@@ -542,7 +547,7 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
             for (int k = 0; ok; ++k) {
                 int it = blockIdx.x + k * int(gridDim.x);
                 if constexpr (kPersist) {   // take the pass's next item and hand it on
-                    it = int(atomicAdd(p.flags + size_t(p.layers) * ngroups, 1u));
+                    it = int(atomicAdd(tf.flags + size_t(tf.layers) * ngroups, 1u));
                     if (!(ok = mbar_wait(&item_empty[ri.idx], ri.phase ^ 1u, p.err, kErrWaitProducer))) break;
                     item_slot[ri.idx] = it < nitems ? it : -1;
                     mbar_arrive(&item_full[ri.idx]);
@@ -557,24 +562,24 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                 if constexpr (kPersist) {
                     const int layer = it / ngroups;
                     g = it - layer * ngroups;
-                    const int conv = layer - p.stem_first;   // the tower conv; -1: the stem
+                    const int conv = layer - tf.stem_first;   // the tower conv; -1: the stem
                     if (conv < 0) {   // the stem: one tap over its packed operand
                         amap = &tf.stem;
                         alo = &tf.stem_lo;
                         taps = 1;
-                        nchunks = p.stem_nchunks;
+                        nchunks = tf.stem_nchunks;
                     } else {
                         const int in = conv % 3;   // tower conv l reads buffer l mod 3
                         amap = &tf.in[in];
                         alo = &tf.in_lo[in];
                     }
-                    const FusedLayer& fl = p.tower[conv < 0 ? p.layers - 1 : conv];
+                    const FusedLayer& fl = tf.tower[conv < 0 ? tf.layers - 1 : conv];
                     wmap = &fl.w;
                     wlo = &fl.w_lo;
                     if (layer > 0) {   // the previous layer's groups whose rows this item's halos read
-                        const unsigned* prev = p.flags + size_t(layer - 1) * ngroups;
+                        const unsigned* prev = tf.flags + size_t(layer - 1) * ngroups;
                         for (int d = g > 0 ? g - 1 : 0; d <= g + 1 && d < ngroups && ok; ++d)
-                            ok = flag_wait(prev + d, kEpiWarps + p.flag_extra, p.err, kErrWaitLayer);
+                            ok = flag_wait(prev + d, kEpiWarps + tf.flag_extra, p.err, kErrWaitLayer);
                         if (!ok) break;
                         fence_proxy_async_global();   // the loads below (async proxy) after the acquires
                     }
@@ -652,10 +657,12 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                     // The persistent tower's stem item: one tap, the centre view.
                     int taps = p.taps, nchunks = p.nchunks;
                     uint32_t off0 = toff[0];
-                    if (kPersist && it < p.stem_first * ngroups) {
-                        taps = 1;
-                        nchunks = p.stem_nchunks;
-                        off0 = toff[4];
+                    if constexpr (kPersist) {
+                        if (it < tf.stem_first * ngroups) {
+                            taps = 1;
+                            nchunks = tf.stem_nchunks;
+                            off0 = toff[4];
+                        }
                     }
                     const uint32_t acc = j & 1;
                     if (!(ok = mbar_wait(&sm.acc_empty[acc], ((j >> 1) & 1) ^ 1, p.err, kErrWaitMma))) break;
@@ -724,10 +731,12 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                     // The persistent tower's stem item: one tap, the centre view.
                     int taps = p.taps, nchunks = p.nchunks;
                     uint32_t off0 = toff[0];
-                    if (kPersist && it < p.stem_first * ngroups) {
-                        taps = 1;
-                        nchunks = p.stem_nchunks;
-                        off0 = toff[4];
+                    if constexpr (kPersist) {
+                        if (it < tf.stem_first * ngroups) {
+                            taps = 1;
+                            nchunks = tf.stem_nchunks;
+                            off0 = toff[4];
+                        }
                     }
                     const bool one_tap = taps == 1;
                     uint32_t acc = 0, d = 0;
@@ -810,14 +819,14 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                 // Tower conv l writes buffer (l+1) mod 3; a block's second conv
                 // (l odd) adds its first conv's input, buffer (l-1) mod 3. The
                 // stem (l = -1) writes buffer 0 and adds nothing.
-                const int conv = layer - p.stem_first;
+                const int conv = layer - tf.stem_first;
                 const int out = (conv + 4) % 3, res = (conv + 2) % 3;
                 const bool has_res = conv >= 0 && (conv & 1) != 0;
                 io.res_hi = has_res ? tf.trunk[res] : nullptr;
                 io.res_lo = has_res ? tf.trunk_lo[res] : nullptr;
                 io.omap = &tf.out[out];
                 io.smap = kSplit ? &tf.out_lo[out] : &tf.out[has_res ? res : out];
-                const FusedLayer& fl = p.tower[conv < 0 ? p.layers - 1 : conv];
+                const FusedLayer& fl = tf.tower[conv < 0 ? tf.layers - 1 : conv];
                 io.scale = fl.scale;
                 io.shift = fl.shift;
             }
@@ -845,7 +854,7 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                     // (whose own dependencies cover both) here as well.
                     bool ok = true;
                     if (lane == 0) {
-                        ok = flag_wait(p.flags + size_t(layer - 1) * ngroups + g, kEpiWarps + p.flag_extra, p.err,
+                        ok = flag_wait(tf.flags + size_t(layer - 1) * ngroups + g, kEpiWarps + tf.flag_extra, p.err,
                                        kErrWaitLayer);
                         fence_proxy_async_global();
                     }
@@ -878,8 +887,10 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                 }
                 float sum[kMine * 32];
                 bool ok = true;
-                const bool stem_item = kPersist && layer < p.stem_first;
-                const int segs = stem_item ? segs_of(1, p.stem_nchunks) : layer_segs;
+                int segs = layer_segs;
+                if constexpr (kPersist) {
+                    if (layer < tf.stem_first) segs = segs_of(1, tf.stem_nchunks);
+                }
                 for (int sg = 0; sg < segs; ++sg, ++j) {
                     const uint32_t acc = j & 1;
                     if (!(ok = mbar_wait(&sm.acc_full[acc], (j >> 1) & 1, p.err, kErrWaitEpilogue))) break;
@@ -899,7 +910,7 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                     if (lane == 0) {   // this warp's part of the item has landed in global memory
                         bulk_wait_all();
                         fence_proxy_async_global();
-                        flag_add_release(p.flags + it, 1u);
+                        flag_add_release(tf.flags + it, 1u);
                     }
                 }
             } else {
@@ -909,7 +920,7 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                 const uint32_t taddr = lanes + acc * (kTiles * C::kTileCols);
                 const ItemIo io = item_io(layer);
                 if constexpr (C::kEpiTma)
-                    store_epilogue_tma<N, kBf16>(p, io.scale, io.shift, io.res_hi != nullptr, io.omap, io.smap, taddr,
+                    store_epilogue_tma<N, kBf16, kPersist>(p, io.scale, io.shift, io.res_hi, io.omap, io.smap, taddr,
                                                  tile * 128 + quarter * 32, valid, c_begin, c_end, ew, lane);
                 else if (tile < p.ntiles)
                     store_epilogue_split<N>(p, sm.bn, taddr, q, valid, c_begin, c_end);
@@ -921,7 +932,7 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                     if (lane == 0) {   // this warp's part of the item has landed in global memory
                         bulk_wait_all();
                         fence_proxy_async_global();
-                        flag_add_release(p.flags + it, 1u);
+                        flag_add_release(tf.flags + it, 1u);
                     }
                 }
             }
@@ -1143,7 +1154,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + acc * N;
             if constexpr (C::kEpiTma)
-                store_epilogue_tma<N, kBf16>(p, sm.bn, sm.bn + N, p.skip != nullptr, &mOut, &mSkip, taddr,
+                store_epilogue_tma<N, kBf16>(p, sm.bn, sm.bn + N, p.skip, &mOut, &mSkip, taddr,
                                              (2 * pr + int(rank)) * 128 + quarter * 32,
                                              valid, c_begin, c_end, ew, lane);
             else
@@ -1254,7 +1265,7 @@ cudaError_t launch_single_seg(const ConvMaps& m, ConvArgs a, int sms, cudaStream
     const int groups = (a.ntiles + kTiles - 1) / kTiles;
     const int grid = std::max(1, std::min(groups, sms));
     return launch_pdl(conv3x3_tc<N, kBf16, kSplit, kTiles, kSeg>, dim3(grid), dim3(kThreadsOf<kTiles>), smem, s, m.a,
-                      m.a_lo, m.w, m.w_lo, m.out, C::kStack ? m.out_lo : m.skip, a, NoFrames{});
+                      m.a_lo, m.w, m.w_lo, m.out, C::kStack ? m.out_lo : m.skip, a, NoTower{});
 }
 
 // The stacked split mode runs in segments of kDefaultSegment<N> taps unless
@@ -1272,7 +1283,7 @@ cudaError_t launch_single(const ConvMaps& m, ConvArgs a, int sms, cudaStream_t s
 // split mode one tile in its default segments. A CTA per SM at most. The six
 // per-layer map parameters are unused (valid maps, for the prefetch).
 template <int N, bool kBf16, bool kSplit, int kTiles, int kSeg>
-cudaError_t launch_persist_tiles(const TowerFrames& f, ConvArgs a, int sms, cudaStream_t s) {
+cudaError_t launch_persist_tiles(const TowerArgs& f, ConvArgs a, int sms, cudaStream_t s) {
     using C = ConvCfg<N, kBf16, kSplit, kTiles>;
     conv_smem_bytes(N, kBf16 ? kBF16 : (kSplit ? kTF32x3 : kTF32), a.halo_rows, &a.sa, &a.sb, false, kTiles);
     const size_t smem = smem_total(a.sa, a.sb, C::kOps * kTiles, C::kOps, a.a_bytes, C::kBBytes, C::kEpiBytes);
@@ -1284,13 +1295,13 @@ cudaError_t launch_persist_tiles(const TowerFrames& f, ConvArgs a, int sms, cuda
         configured = smem;
     }
     const int groups = (a.ntiles + kTiles - 1) / kTiles;
-    const int grid = std::max(1, std::min(groups * a.layers, sms));
+    const int grid = std::max(1, std::min(groups * f.layers, sms));
     return launch_pdl(conv3x3_tc<N, kBf16, kSplit, kTiles, kSeg, true>, dim3(grid), dim3(kThreadsOf<kTiles>), smem, s,
                       f.in[0], f.in_lo[0], f.in[0], f.in_lo[0], f.out[0], f.out_lo[0], a, f);
 }
 
 template <int N, bool kBf16>
-cudaError_t launch_persist(const TowerFrames& f, const ConvArgs& a, int sms, cudaStream_t s) {
+cudaError_t launch_persist(const TowerArgs& f, const ConvArgs& a, int sms, cudaStream_t s) {
     if constexpr (N <= 128) {
         if (conv_smem_bytes(N, kBf16 ? kBF16 : kTF32, a.halo_rows, nullptr, nullptr, false, 2) <= 227 * 1024)
             return launch_persist_tiles<N, kBf16, false, 2, 0>(f, a, sms, s);
@@ -1395,10 +1406,10 @@ bool tower_persistent(int n_out, int precision) {
     return n_out <= 128;
 }
 
-cudaError_t launch_tower_persistent(const TowerFrames& f, const ConvArgs& a, int n_out, int precision, int sms,
+cudaError_t launch_tower_persistent(const TowerArgs& f, const ConvArgs& a, int n_out, int precision, int sms,
                                     cudaStream_t s) {
-    if (a.ntiles <= 0 || a.layers <= 0) return cudaSuccess;
-    if (a.tower == nullptr || a.flags == nullptr) return cudaErrorNotSupported;
+    if (a.ntiles <= 0 || f.layers <= 0) return cudaSuccess;
+    if (f.tower == nullptr || f.flags == nullptr) return cudaErrorNotSupported;
     if (precision == kTF32x3) {
         switch (n_out) {
             case 32: return launch_persist_tiles<32, false, true, 1, kDefaultSegment<32>>(f, a, sms, s);

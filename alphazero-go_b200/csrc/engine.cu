@@ -804,14 +804,14 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
         a.out = a.out_lo = nullptr;
         a.skip = a.skip_lo = nullptr;
         a.scale = a.shift = nullptr;
-        a.tower = w.fused_layers();
-        a.layers = 2 * sh.blocks + 1;
-        a.flags = ws.tower_flags;
-        a.flag_extra = tower_starve() ? 1u : 0u;
-        a.stem_first = 1;
-        a.stem_nchunks = w.kstem() / chunk_channels(precision);
         mark_begin(kSlotTower);
-        TowerFrames tf;
+        TowerArgs tf;
+        tf.tower = w.fused_layers();
+        tf.layers = 2 * sh.blocks + 1;
+        tf.flags = ws.tower_flags;
+        tf.flag_extra = tower_starve() ? 1u : 0u;
+        tf.stem_first = 1;
+        tf.stem_nchunks = w.kstem() / chunk_channels(precision);
         tf.stem = ws.map_stem;
         tf.stem_lo = ws.map_stem_lo;
         for (int i = 0; i < 3; ++i) {

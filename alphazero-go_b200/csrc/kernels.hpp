@@ -89,28 +89,28 @@ struct ConvArgs {
     const float* scale;   // [N] folded batch norm (0 for padded channels)
     const float* shift;   // [N]
     int* err;          // kernel error word (KernelError)
-    // The persistent tower (every tower conv in one launch): the layers'
-    // weight maps and batch norms, their number, and per (layer, tile group)
-    // the count of epilogue warps that have stored their part of it, zeroed
-    // by the pass's stem operand kernel.
-    const FusedLayer* tower;
-    int layers;
-    unsigned* flags;
-    unsigned flag_extra;   // 0; the failure-detection test's 1 makes every wait for a previous layer run out
-    // 1: the persistent tower's layer 0 is the stem, one tap over the stem's
-    // packed operand of stem_nchunks chunks (its weights the table's last
-    // entry), writing buffer 0; tower conv l is then layer l + 1.
-    int stem_first;
-    int stem_nchunks;
 };
 
-// The three frame buffers as the persistent tower addresses them.
-struct TowerFrames {
+// The persistent tower's own parameters (a separate kernel parameter, so
+// the per-layer kernels' ConvArgs stay as they are): the stem's packed
+// operand and the three frame buffers as it addresses them, the layer
+// table, and per (layer, tile group) the count of epilogue warps that have
+// stored their part of it, zeroed by the pass's stem operand kernel.
+struct TowerArgs {
     CUtensorMap stem, stem_lo;       // the stem's packed operand in halo boxes
     CUtensorMap in[3], in_lo[3];     // halo boxes {chunk, halo_rows} (in_lo: the split mode's low planes)
     CUtensorMap out[3], out_lo[3];   // the epilogue's {32, 32} boxes
     const void* trunk[3];            // the frames (the split mode reads its residual directly)
     const void* trunk_lo[3];
+    const FusedLayer* tower;         // the layers' weight maps and batch norms (tower convs, then the stem)
+    int layers;
+    unsigned* flags;
+    unsigned flag_extra;   // 0; the failure-detection test's 1 makes every wait for a previous layer run out
+    // 1: layer 0 is the stem, one tap over its packed operand of
+    // stem_nchunks chunks (its weights the table's last entry), writing
+    // buffer 0; tower conv l is then layer l + 1.
+    int stem_first;
+    int stem_nchunks;
 };
 
 struct ConvMaps {
@@ -147,7 +147,7 @@ void set_conv_segment(int steps);
 // second conv adds (l-1) mod 3, the block's input.
 // Returns cudaErrorNotSupported where it does not apply (the caller then
 // launches per layer).
-cudaError_t launch_tower_persistent(const TowerFrames& f, const ConvArgs& a, int n_out, int precision, int sms,
+cudaError_t launch_tower_persistent(const TowerArgs& t, const ConvArgs& a, int n_out, int precision, int sms,
                                     cudaStream_t s);
 // Whether the persistent tower runs for n_out channels in `precision` (and
 // the test hook's choice: -1 the default, 0 per layer, 1 persistent where
