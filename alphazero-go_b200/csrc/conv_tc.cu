@@ -455,7 +455,9 @@ __device__ __forceinline__ void store_split_sums(const ConvArgs& p, const float*
 // taken by CTAs already running, so the tower progresses however many of
 // its CTAs are resident (another stream's kernels may hold SMs, a second
 // tower among them). The frames come from tf (the six map parameters are
-// then unused), the weights and batch norms from tf.tower. Each
+// then unused), the weights and batch norms from tf.tower. With
+// tf.stem_first, layer 0 is the stem: one tap (the centre view) over the
+// stem's packed operand, tf.stem_nchunks chunks. Each
 // epilogue warp adds 1 to its item's counter once its stores have landed;
 // an item's halo loads wait until the counters of the previous layer's
 // groups g-1, g, g+1 (the rows its halo reads) have reached kEpiWarps.
