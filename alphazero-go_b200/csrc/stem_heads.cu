@@ -58,13 +58,22 @@ __global__ void __launch_bounds__(256) stem_pack_kernel(const StemArgs a) {
         __syncthreads();
         for (int i = threadIdx.x; i < a.P * A; i += blockDim.x) planes[i] = __ldg(a.in + size_t(b) * a.P * A + i);
         __syncthreads();
-        for (int item = threadIdx.x; item < A * pieces; item += blockDim.x) {
-            const int pt = item / pieces, j = item - pt * pieces;
-            const int py = pt / a.n, px = pt - py * a.n;
+        // Thread t keeps piece j = t % pieces of every row it writes (its W
+        // column codes in registers) and steps through the points t / pieces,
+        // + per_step, ...: no division per piece. Consecutive threads write
+        // consecutive pieces of a row, then the next point's row.
+        const int per_step = int(blockDim.x) / pieces;
+        if (int(threadIdx.x) >= per_step * pieces) continue;
+        const int j = int(threadIdx.x) % pieces, first = int(threadIdx.x) / pieces;
+        int codes[W];
+#pragma unroll
+        for (int e = 0; e < W; ++e) codes[e] = table[e * pieces + j];
+        int py = first / a.n, px = first - py * a.n;
+        for (int pt = first; pt < A; pt += per_step) {
             float v[W];
 #pragma unroll
             for (int e = 0; e < W; ++e) {
-                const int code = table[e * pieces + j];
+                const int code = codes[e];
                 v[e] = 0.0f;
                 if (code >= 0) {
                     const int y = py + ((code >> 2) & 3) - 1, x = px + (code & 3) - 1;
@@ -88,6 +97,11 @@ __global__ void __launch_bounds__(256) stem_pack_kernel(const StemArgs a) {
                 *reinterpret_cast<float4*>(static_cast<float*>(a.out_lo) + off) = l;
             } else {
                 *reinterpret_cast<float4*>(static_cast<float*>(a.out) + off) = make_float4(v[0], v[1], v[2], v[3]);
+            }
+            px += per_step;
+            while (px >= a.n) {
+                px -= a.n;
+                ++py;
             }
         }
     }
