@@ -37,3 +37,18 @@ def test_reference_arm_line():
     e2e = line["e2e"]
     assert e2e["value"] == line["value"] and e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
     assert "workload" in line["config"]
+
+
+def test_engine_arm_fails_loudly_without_a_gpu():
+    """The engine arm has no CPU fallback: without a usable GPU it exits
+    non-zero with the reason and prints no measurement line."""
+    import azb200
+
+    ok, _ = azb200.cuda_available(0)
+    if ok:
+        return   # a GPU is present; the GPU tests cover the engine arm
+    r = subprocess.run([sys.executable, "bench.py", "--steps", "1", "--warmup", "3", "--no-cpu-baseline",
+                        "--no-selfplay"], cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert r.returncode != 0
+    assert "no usable GPU" in (r.stdout + r.stderr)
+    assert not [l for l in r.stdout.splitlines() if l.startswith("{") and '"value"' in l]
