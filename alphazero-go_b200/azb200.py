@@ -103,6 +103,9 @@ def lib() -> C.CDLL:
             L.azb_runner_input.argtypes = [C.c_void_p, C.c_int]
             L.azb_runner_input.restype = _F
             L.azb_runner_begin.argtypes = [C.c_void_p, C.c_int, C.c_int, DONE_FN, C.c_void_p]
+            L.azb_runner_begin_stones.argtypes = [C.c_void_p, C.c_int, C.c_int, DONE_FN, C.c_void_p]
+            L.azb_runner_records.argtypes = [C.c_void_p, C.c_int]
+            L.azb_runner_records.restype = C.POINTER(C.c_uint8)
             for fn in (L.azb_runner_logits, L.azb_runner_values, L.azb_runner_ownership):
                 fn.argtypes = [C.c_void_p, C.c_int]
                 fn.restype = _F
@@ -442,7 +445,17 @@ class BatchRunner:
     def ownership(self, slot: int, B: int) -> np.ndarray:
         return np.ctypeslib.as_array(lib().azb_runner_ownership(self.h, slot), shape=(B, self.desc.area))
 
-    def begin(self, slot: int, B: int, done) -> None:
+    def records(self, slot: int) -> np.ndarray:
+        """The slot's pinned position-record staging, [max_batch][stones_record_bytes]."""
+        d = self.desc
+        p = lib().azb_runner_records(self.h, slot)
+        return np.ctypeslib.as_array(p, shape=(self.max_batch(), stones_record_bytes(d.history, d.board)))
+
+    def begin_stones(self, slot: int, B: int, done) -> None:
+        """begin() from the first B records of records(slot), encoded on the device."""
+        self.begin(slot, B, done, _entry=lib().azb_runner_begin_stones)
+
+    def begin(self, slot: int, B: int, done, _entry=None) -> None:
         """done(slot, error) is called exactly once, from the runner's thread."""
         with self._cb_lock:
             key = self._next
@@ -457,7 +470,7 @@ class BatchRunner:
         cb = DONE_FN(trampoline)
         with self._cb_lock:
             self._callbacks[key] = (done, cb)
-        if lib().azb_runner_begin(self.h, slot, B, cb, None) != 0:
+        if (_entry or lib().azb_runner_begin)(self.h, slot, B, cb, None) != 0:
             with self._cb_lock:
                 self._callbacks.pop(key, None)
             raise IndexError(f"slot {slot} out of range")

@@ -1,7 +1,8 @@
 """Builds libazb200.so in place: every CUDA source of csrc/ compiled for
 sm_100a only (SASS, no PTX) with the CUDA runtime linked statically, so the
 library loads on a machine without a GPU (the driver API is reached at run
-time through cudaGetDriverEntryPoint).
+time through cudaGetDriverEntryPoint). Translation units compile in
+parallel into _build/ (git-ignored), then link.
 
     python alphazero-go_b200/build_ext.py [--force]
 """
@@ -56,17 +57,65 @@ def up_to_date() -> bool:
     return all(os.path.getmtime(p) <= t for p in deps)
 
 
+OBJ = os.path.join(HERE, "_build")
+COMPILE = [f for f in FLAGS if f != "-shared"]
+
+
+def _object(src: str, khash: str) -> tuple[list[str], str]:
+    """The compile command of one translation unit and its object path. The
+    object's key covers the unit, every header, the flags and the compiler;
+    only engine.cu, which prints the kernel hash, also depends on the others."""
+    h = hashlib.sha256()
+    for path in [src] + [p for p in sources() if p.endswith((".cuh", ".hpp"))] + [os.path.join(INCLUDE, "azb200.h")]:
+        with open(path, "rb") as f:
+            h.update(f.read())
+    h.update(" ".join(COMPILE).encode())
+    defs = []
+    if os.path.basename(src) == "engine.cu":
+        defs = [f"-DAZB_KERNEL_HASH=\"{khash}\""]
+        h.update(khash.encode())
+    obj = os.path.join(OBJ, f"{os.path.basename(src)}.{h.hexdigest()[:12]}.o")
+    cmd = [NVCC, *COMPILE, "-c", *defs, "-I", CSRC, "-I", INCLUDE, "-o", obj + ".tmp", src]
+    return cmd, obj
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
+    """Compiles the translation units in parallel into _build/, then links."""
     if not force and up_to_date():
         return OUT
-    cu = [p for p in sources() if p.endswith((".cu", ".cpp"))]
-    cmd = [NVCC, *FLAGS, f"-DAZB_KERNEL_HASH=\"{kernel_hash()}\"", "-I", CSRC, "-I", INCLUDE, "-o", OUT + ".tmp", *cu]
+    from concurrent.futures import ThreadPoolExecutor
+
+    khash = kernel_hash()
+    os.makedirs(OBJ, exist_ok=True)
+    units = [_object(p, khash) for p in sources() if p.endswith((".cu", ".cpp"))]
+
+    def compile_one(unit):
+        cmd, obj = unit
+        if os.path.exists(obj) and not force:
+            return None
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            return f"{os.path.basename(cmd[-1])}: nvcc failed ({r.returncode}):\n{r.stdout}\n{r.stderr}"
+        os.replace(obj + ".tmp", obj)
+        return None
+
+    with ThreadPoolExecutor(max_workers=min(len(units), os.cpu_count() or 4)) as pool:
+        failures = [f for f in pool.map(compile_one, units) if f]
+    if failures:
+        raise RuntimeError("\n".join(failures))
+    link = [NVCC, *FLAGS, "-o", OUT + ".tmp", *[obj for _, obj in units]]
     if verbose:
-        print(" ".join(cmd))
-    r = subprocess.run(cmd, capture_output=True, text=True)
+        print(" ".join(link), flush=True)
+    r = subprocess.run(link, capture_output=True, text=True)
     if r.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
+        raise RuntimeError(f"nvcc link failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
     os.replace(OUT + ".tmp", OUT)
+    keep = {os.path.basename(obj) for _, obj in units}
+    for f in os.listdir(OBJ):   # objects of earlier sources
+        if f.endswith(".o") and f not in keep:
+            os.remove(os.path.join(OBJ, f))
     return OUT
 
 

@@ -171,12 +171,27 @@ float* azb_runner_input(azb_runner* r, int slot) {
     return r->impl->input(slot);
 }
 
-int azb_runner_begin(azb_runner* r, int slot, int B, azb_done_fn done, void* ctx) {
+namespace {
+int begin_pass(azb_runner* r, int slot, int B, azb_done_fn done, void* ctx, Runner::Input from) {
     if (!r || slot < 0 || slot >= r->impl->slots()) return -1;
     r->impl->begin(slot, B, [done, ctx](int s, const std::string& error) {
         if (done) done(ctx, s, error.c_str());
-    });
+    }, from);
     return 0;
+}
+}  // namespace
+
+int azb_runner_begin(azb_runner* r, int slot, int B, azb_done_fn done, void* ctx) {
+    return begin_pass(r, slot, B, done, ctx, Runner::Input::kPlanes);
+}
+
+uint8_t* azb_runner_records(azb_runner* r, int slot) {
+    if (!r || slot < 0 || slot >= r->impl->slots()) return nullptr;
+    return r->impl->records(slot);
+}
+
+int azb_runner_begin_stones(azb_runner* r, int slot, int B, azb_done_fn done, void* ctx) {
+    return begin_pass(r, slot, B, done, ctx, Runner::Input::kRecords);
 }
 
 const float* azb_runner_logits(const azb_runner* r, int slot) {

@@ -116,51 +116,76 @@ const LayoutEntry& Layout::buffer(const std::string& name) const {
 
 namespace {
 
+// "12.9" from the runtime's 12090.
 std::string version_text(int v) { return std::to_string(v / 1000) + "." + std::to_string((v % 1000) / 10); }
 
-void set_up(int device, DeviceInfo& d) {
+int attribute(cudaDeviceAttr what, int device) {
+    int v = 0;
+    check(cudaDeviceGetAttribute(&v, what, device), "cudaDeviceGetAttribute");
+    return v;
+}
+
+// Device admission, once per device. The checks run in the order in which a
+// failure says the most: the runtime sees the device; the device is the
+// architecture this library's machine code (sm_100a only, no PTX) was built
+// for, which the runtime confirms by finding the code for one of its
+// kernels; the device grants the opt-in shared memory and the thread-block
+// clusters the tensor-core kernels are built around; and a first kernel
+// transforms a pattern copied in from the host, which is copied back and
+// checked, so copies in both directions and a launch all work.
+void admit(int device, DeviceInfo& d) {
     int count = 0;
-    const cudaError_t e = cudaGetDeviceCount(&count);
-    if (e != cudaSuccess) throw std::runtime_error(std::string("no CUDA device: ") + cudaGetErrorString(e));
+    if (const cudaError_t e = cudaGetDeviceCount(&count); e != cudaSuccess)
+        throw std::runtime_error(std::string("no CUDA device: ") + cudaGetErrorString(e));
     if (count < 1) throw std::runtime_error("no CUDA device");
     if (device < 0 || device >= count)
         throw std::runtime_error("no CUDA device " + std::to_string(device) + " (" + std::to_string(count) + " present)");
     check(cudaSetDevice(device), "cudaSetDevice");
-    cudaDeviceProp prop;
+    cudaDeviceProp prop{};
     check(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
     d.name = prop.name;
-    d.architecture = 10 * prop.major + prop.minor;
-    d.sms = prop.multiProcessorCount;
     d.total_memory = prop.totalGlobalMem;
+    d.architecture = 10 * attribute(cudaDevAttrComputeCapabilityMajor, device) +
+                     attribute(cudaDevAttrComputeCapabilityMinor, device);
+    d.sms = attribute(cudaDevAttrMultiProcessorCount, device);
     const std::string sm = "sm_" + std::to_string(d.architecture);
-    // SASS for sm_100a only: another architecture finds no machine code.
-    cudaFuncAttributes attr;
-    if (fill_attributes(&attr) != cudaSuccess) {
-        cudaGetLastError();
+
+    cudaFuncAttributes image{};
+    if (fill_attributes(&image) != cudaSuccess) {
+        cudaGetLastError();   // not sticky: the context stays usable
         throw std::runtime_error("no kernels for this GPU (" + sm + "; built for sm_100a)");
     }
-    d.binary_version = attr.binaryVersion;
+    d.binary_version = image.binaryVersion;
     if (d.binary_version != d.architecture || d.architecture != 100)
         throw std::runtime_error("kernels built for sm_" + std::to_string(d.binary_version) + "; this GPU is " + sm);
-    // A first kernel, through memory, a stream and back.
-    float* probe = nullptr;
-    check(cudaMalloc(&probe, 16 * sizeof(float)), "cudaMalloc");
-    cudaStream_t s;
-    check(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate");
-    float host[16] = {};
-    cudaError_t r = launch_fill(probe, 16, 1.5f, s);
-    if (r == cudaSuccess) r = cudaMemcpyAsync(host, probe, sizeof host, cudaMemcpyDeviceToHost, s);
-    if (r == cudaSuccess) r = cudaStreamSynchronize(s);
-    cudaStreamDestroy(s);
-    cudaFree(probe);
+    if (attribute(cudaDevAttrMaxSharedMemoryPerBlockOptin, device) < 227 * 1024)
+        throw std::runtime_error(sm + " grants less than 227 KB of shared memory per block");
+    if (!attribute(cudaDevAttrClusterLaunch, device))
+        throw std::runtime_error(sm + " does not launch thread-block clusters");
+
+    constexpr int kWords = 64;
+    uint32_t sent[kWords], back[kWords] = {};
+    for (int i = 0; i < kWords; ++i) sent[i] = 0x9E3779B9u * uint32_t(i + 1);
+    uint32_t* dev = nullptr;
+    cudaStream_t stream = nullptr;
+    cudaError_t r = cudaMalloc(&dev, sizeof sent);
+    if (r == cudaSuccess) r = cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking);
+    if (r == cudaSuccess) r = cudaMemcpyAsync(dev, sent, sizeof sent, cudaMemcpyHostToDevice, stream);
+    if (r == cudaSuccess) r = launch_admission_probe(dev, kWords, stream);
+    if (r == cudaSuccess) r = cudaMemcpyAsync(back, dev, sizeof back, cudaMemcpyDeviceToHost, stream);
+    if (r == cudaSuccess) r = cudaStreamSynchronize(stream);
+    if (stream) cudaStreamDestroy(stream);
+    if (dev) cudaFree(dev);
     check(r, "first kernel");
-    for (float v : host)
-        if (v != 1.5f) throw std::runtime_error("the first kernel wrote wrong values");
-    int drv = 0, rt = 0;
-    check(cudaDriverGetVersion(&drv), "cudaDriverGetVersion");
-    check(cudaRuntimeGetVersion(&rt), "cudaRuntimeGetVersion");
-    d.description = d.name + " " + sm + ", driver API " + version_text(drv) + ", runtime " + version_text(rt) +
-                    ", kernels " + AZB_KERNEL_HASH;
+    for (int i = 0; i < kWords; ++i)
+        if (back[i] != admission_probe_value(sent[i], i)) throw std::runtime_error("the first kernel wrote wrong values");
+
+    int driver_api = 0, runtime = 0;
+    check(cudaDriverGetVersion(&driver_api), "cudaDriverGetVersion");
+    check(cudaRuntimeGetVersion(&runtime), "cudaRuntimeGetVersion");
+    // The reference's cudaDescription() format (include/azgo/cuda.hpp:45-49).
+    d.description = d.name + " " + sm + ", driver API " + version_text(driver_api) + ", runtime " +
+                    version_text(runtime) + ", kernels " + AZB_KERNEL_HASH;
     d.usable = true;
 }
 
@@ -179,7 +204,7 @@ const DeviceInfo& device_info(int device) {
     if (!slot) {
         slot = std::make_unique<DeviceInfo>();
         try {
-            set_up(device, *slot);
+            admit(device, *slot);
         } catch (const std::exception& e) {
             slot->usable = false;
             slot->why = e.what();
@@ -1033,173 +1058,6 @@ void Inference::time(int B, int warmup, int steps, bool with_copies, double* ms,
 Hooks& hooks() {
     static Hooks h;
     return h;
-}
-
-// ------------------------------------------------------------------ runner
-
-namespace {
-
-constexpr size_t kMemoryMargin = size_t(512) << 20;
-
-// The completion thread polls a pass's event as the reference does (every
-// 50 to 200 us, src/cuda/cuda_runner.cu:47-48), but first yields for up to
-// kSpinUs: a small board's pass takes well under 100 us, and a sleep of
-// 50 us (more with the kernel's timer slack) would report it late and leave
-// the GPU idle. (A blocking-sync event woke the thread later still.)
-constexpr int kPollFirstUs = 50, kPollLastUs = 200, kSpinUs = 100;
-
-cudaError_t wait_for(cudaEvent_t event) {
-    const auto start = std::chrono::steady_clock::now();
-    int sleep_us = kPollFirstUs;
-    for (;;) {
-        const cudaError_t e = cudaEventQuery(event);
-        if (e != cudaErrorNotReady) return e;
-        if (std::chrono::steady_clock::now() - start < std::chrono::microseconds(kSpinUs)) {
-            std::this_thread::yield();
-            continue;
-        }
-        std::this_thread::sleep_for(std::chrono::microseconds(sleep_us));
-        sleep_us = std::min(kPollLastUs, 2 * sleep_us);
-    }
-}
-
-} // namespace
-
-Runner::Runner(const NetShape& s, const float* params, size_t n_params, const float* buffers, size_t n_buffers,
-               int max_batch, int slots, int device, int precision)
-    : shape_(s), device_(device), max_batch_(max_batch) {
-    if (max_batch < 1) throw std::invalid_argument("makeCudaRunner: maxBatch must be >= 1");
-    if (slots < 1 || slots > 2) throw std::invalid_argument("makeCudaRunner: slots must be in [1, 2]");
-    require_device(device);
-    check_fits(device, hub_bytes(s, precision, max_batch, slots), max_batch, 1);
-    w_ = std::make_unique<Weights>(s, precision, device, params, n_params, buffers, n_buffers);
-    for (int i = 0; i < slots; ++i) {
-        auto sl = std::make_unique<Slot>();
-        sl->ws = std::make_unique<Workspace>(*w_, max_batch);
-        check(cudaStreamCreateWithFlags(&sl->stream, cudaStreamNonBlocking), "cudaStreamCreate");
-        check(cudaEventCreateWithFlags(&sl->event, cudaEventDisableTiming), "cudaEventCreate");
-        const size_t B = size_t(max_batch);
-        check(cudaHostAlloc(reinterpret_cast<void**>(&sl->in_host), B * s.planes() * s.area() * 4, cudaHostAllocDefault), "cudaHostAlloc");
-        check(cudaHostAlloc(reinterpret_cast<void**>(&sl->logits_host), B * s.actions() * 4, cudaHostAllocDefault), "cudaHostAlloc");
-        check(cudaHostAlloc(reinterpret_cast<void**>(&sl->values_host), B * 4, cudaHostAllocDefault), "cudaHostAlloc");
-        if (s.ownership)
-            check(cudaHostAlloc(reinterpret_cast<void**>(&sl->own_host), B * s.area() * 4, cudaHostAllocDefault), "cudaHostAlloc");
-        check(cudaHostAlloc(reinterpret_cast<void**>(&sl->err_host), sizeof(int), cudaHostAllocDefault), "cudaHostAlloc");
-        *sl->err_host = 0;
-        slots_.push_back(std::move(sl));
-    }
-    completion_ = std::thread([this] { completion_loop(); });
-}
-
-Runner::~Runner() {
-    {
-        std::lock_guard<std::mutex> lock(mutex_);
-        stop_ = true;
-    }
-    wake_.notify_all();
-    if (completion_.joinable()) completion_.join();   // after every pass in flight has been reported
-    cudaSetDevice(device_);
-    for (auto& sl : slots_) {
-        if (sl->stream) cudaStreamSynchronize(sl->stream);
-        if (sl->event) cudaEventDestroy(sl->event);
-        if (sl->stream) cudaStreamDestroy(sl->stream);
-        for (void* p : {static_cast<void*>(sl->in_host), static_cast<void*>(sl->logits_host),
-                        static_cast<void*>(sl->values_host), static_cast<void*>(sl->own_host),
-                        static_cast<void*>(sl->err_host)})
-            if (p) cudaFreeHost(p);
-        sl->ws.reset();
-    }
-}
-
-void Runner::begin(int slot, int B, Done done) {
-    std::string error;
-    if (slot < 0 || slot >= slots()) {
-        error = "runner: slot out of range";
-        slot = 0;
-    } else {
-        Slot& s = *slots_[size_t(slot)];
-        try {
-            check(cudaSetDevice(device_), "cudaSetDevice");
-            const size_t in = size_t(B) * shape_.planes() * shape_.area();
-            if (B >= 1 && B <= max_batch_)
-                check(cudaMemcpyAsync(s.ws->stage, s.in_host, in * 4, cudaMemcpyHostToDevice, s.stream), "input");
-            encode_forward(*w_, *s.ws, B, s.stream, false);
-            const int delay = hooks().copy_out_delay_us.load();
-            if (delay > 0) check(launch_spin(1000ull * unsigned(delay), s.stream), "spin");
-            check(cudaMemcpyAsync(s.logits_host, s.ws->logits, size_t(B) * shape_.actions() * 4, cudaMemcpyDeviceToHost,
-                                  s.stream), "logits");
-            check(cudaMemcpyAsync(s.values_host, s.ws->values, size_t(B) * 4, cudaMemcpyDeviceToHost, s.stream), "values");
-            if (shape_.ownership)
-                check(cudaMemcpyAsync(s.own_host, s.ws->ownership, size_t(B) * shape_.area() * 4, cudaMemcpyDeviceToHost,
-                                      s.stream), "ownership");
-            check(cudaMemcpyAsync(s.err_host, s.ws->err, sizeof(int), cudaMemcpyDeviceToHost, s.stream), "error word");
-            // Recorded after the copies: done means the outputs are on the host.
-            check(cudaEventRecord(s.event, s.stream), "cudaEventRecord");
-        } catch (const std::exception& e) {
-            error = e.what();
-            // The event may not cover this pass; make it complete trivially.
-            cudaGetLastError();
-            cudaEventRecord(s.event, s.stream);
-        }
-    }
-    {
-        std::lock_guard<std::mutex> lock(mutex_);
-        queue_.push_back(Pass{slot, std::move(done), std::move(error)});
-    }
-    wake_.notify_all();
-}
-
-void Runner::completion_loop() {
-    cudaSetDevice(device_);
-    for (;;) {
-        Pass pass;
-        {
-            std::unique_lock<std::mutex> lock(mutex_);
-            wake_.wait(lock, [&] { return stop_ || !queue_.empty(); });
-            if (queue_.empty()) return;   // stop_, and nothing in flight
-            pass = std::move(queue_.front());
-            queue_.pop_front();
-        }
-        std::string error = pass.error;
-        Slot& s = *slots_[size_t(pass.slot)];
-        const cudaError_t e = wait_for(s.event);
-        if (error.empty() && e != cudaSuccess) error = std::string("cuda: ") + cudaGetErrorString(e);
-        if (error.empty() && *s.err_host != 0) error = "cuda: " + kernel_error_text(*s.err_host);
-        *s.err_host = 0;
-        // Failure injection: after n passes, the next one fails (once).
-        int left = hooks().fail_countdown.load();
-        while (left > 0 && !hooks().fail_countdown.compare_exchange_weak(left, left - 1)) {
-        }
-        if (left == 1 && error.empty()) error = "cuda: injected failure (a test hook)";
-        ++hooks().passes_completed;
-        if (pass.done) pass.done(pass.slot, error);
-    }
-}
-
-// -------------------------------------------------------------- memory
-
-double hub_bytes(const NetShape& s, int precision, int max_batch, int slots) {
-    return double(slots) * double(Workspace::bytes_for(s, precision, max_batch)) +
-           double(Weights::bytes_for(s, precision));
-}
-
-void check_fits(int device, double need, int max_batch, int hubs) {
-    require_device(device);
-    double have;
-    const size_t limit = hooks().memory_limit.load();
-    if (limit > 0) {
-        have = double(limit);
-    } else {
-        size_t free_b = 0, total = 0;
-        check(cudaMemGetInfo(&free_b, &total), "cudaMemGetInfo");
-        have = free_b > kMemoryMargin ? double(free_b - kMemoryMargin) : 0.0;
-    }
-    if (need <= have) return;
-    throw std::runtime_error("cuda: inference needs " + std::to_string(static_cast<long long>(need / 1e6)) +
-                             " MB of GPU memory at inference_batch " + std::to_string(max_batch) +
-                             (hubs > 1 ? " (" + std::to_string(hubs) + " hubs)" : std::string()) + ", more than the " +
-                             std::to_string(static_cast<long long>(have / 1e6)) +
-                             " MB the GPU has free; lower inference_batch");
 }
 
 } // namespace azb

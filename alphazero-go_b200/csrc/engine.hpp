@@ -4,6 +4,7 @@
 // (include/azb200.h) is a thin layer over these classes (capi.cu).
 #pragma once
 #include <atomic>
+#include <chrono>
 #include <condition_variable>
 #include <cstddef>
 #include <cstdint>
@@ -222,47 +223,66 @@ private:
     float* pin_out_ = nullptr;
 };
 
-// The BatchRunner (include/azgo/inference_hub.hpp:41-53; src/cuda/cuda_runner.cu:53-194).
+// The BatchRunner (include/azgo/inference_hub.hpp:41-53): slots of pinned
+// staging and a workspace each, one reporter thread for every done() call
+// (runner.cu).
 class Runner {
 public:
     using Done = std::function<void(int slot, const std::string& error)>;
+    // What begin() reads from the slot's staging: float planes (input()) or
+    // position records for the device encoder (records()).
+    enum class Input { kPlanes, kRecords };
     Runner(const NetShape& s, const float* params, size_t n_params, const float* buffers, size_t n_buffers,
            int max_batch, int slots, int device, int precision);
     ~Runner();
-    int slots() const { return static_cast<int>(slots_.size()); }
+    Runner(const Runner&) = delete;
+    Runner& operator=(const Runner&) = delete;
+    int slots() const;
     int max_batch() const { return max_batch_; }
-    float* input(int slot) { return slots_.at(static_cast<size_t>(slot))->in_host; }
-    const float* logits(int slot) const { return slots_.at(static_cast<size_t>(slot))->logits_host; }
-    const float* values(int slot) const { return slots_.at(static_cast<size_t>(slot))->values_host; }
-    const float* ownership(int slot) const { return slots_.at(static_cast<size_t>(slot))->own_host; }
-    void begin(int slot, int B, Done done);
+    float* input(int slot);       // [max_batch][planes][area]
+    uint8_t* records(int slot);   // [max_batch][stones_record_bytes(history, board)]
+    const float* logits(int slot) const;
+    const float* values(int slot) const;
+    const float* ownership(int slot) const;
+    // Returns at once; done(slot, error) follows exactly once, from the
+    // reporter thread, after the outputs reached the slot's staging.
+    void begin(int slot, int B, Done done, Input from = Input::kPlanes);
 
 private:
-    struct Slot {
-        std::unique_ptr<Workspace> ws;
-        cudaStream_t stream = nullptr;
-        cudaEvent_t event = nullptr;
-        float *in_host = nullptr, *logits_host = nullptr, *values_host = nullptr, *own_host = nullptr;
-        int* err_host = nullptr;
-    };
-    struct Pass {
+    struct Slot;
+    struct Refusal {
         int slot;
         Done done;
         std::string error;
     };
-    void completion_loop();
+    void enqueue(Slot& sl, int B, Input from);
+    void refuse(int slot, Done done, std::string error);
+    bool any_live() const;
+    std::chrono::steady_clock::time_point predicted_finish(const Slot& sl) const;
+    int await_first(cudaError_t* status);
+    void report(int slot, cudaError_t status);
+    void report_loop();
+    void release_slots();
+
     NetShape shape_;
     int device_, max_batch_;
     std::unique_ptr<Weights> w_;
     std::vector<std::unique_ptr<Slot>> slots_;
-    std::mutex mutex_;
+    std::mutex mu_;
     std::condition_variable wake_;
-    std::deque<Pass> queue_;
-    bool stop_ = false;
-    std::thread completion_;
+    std::deque<Refusal> refused_;
+    bool closing_ = false;
+    // The reporter's own state: its estimate of a pass's GPU time and when it last reported one.
+    double service_us_ = 0.0;
+    std::chrono::steady_clock::time_point last_finish_{};
+    std::thread reporter_;
 };
 
-// Memory checks (src/cuda/cuda_runner.cu:196-256).
+// Device memory of `slots` workspaces and one weight replica, and the
+// admission check before allocating it (checkCudaInferenceMemory,
+// include/azgo/cuda.hpp:63): throws the reference's "cuda: inference needs
+// N MB ... lower inference_batch" when `need` exceeds the free memory less a
+// 512 MB reserve (or the test hook's limit).
 double hub_bytes(const NetShape& s, int precision, int max_batch, int slots);
 void check_fits(int device, double need, int max_batch, int hubs);
 
@@ -273,6 +293,8 @@ struct Hooks {
     std::atomic<size_t> memory_limit{0};
     std::atomic<long long> passes_completed{0};
     std::atomic<int> copy_out_delay_us{0};
+    // Steps the failure countdown for one reported pass; true for the pass it marks.
+    bool pass_marked_to_fail();
 };
 Hooks& hooks();
 

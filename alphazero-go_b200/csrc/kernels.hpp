@@ -266,6 +266,11 @@ cudaError_t launch_fill(float* data, size_t n, float value, cudaStream_t s);
 cudaError_t launch_tanh(float* data, size_t n, cudaStream_t s);   // data = tanhf(data), as the heads compute it
 cudaError_t fill_attributes(cudaFuncAttributes* attr);
 cudaError_t launch_spin(unsigned long long ns, cudaStream_t s);
+// Device admission's first kernel: data[i] = admission_probe_value(data[i], i).
+__host__ __device__ inline uint32_t admission_probe_value(uint32_t x, int i) {
+    return (x ^ (x >> 13)) * 5u + uint32_t(i);
+}
+cudaError_t launch_admission_probe(uint32_t* data, int n, cudaStream_t s);
 // A kernel that waits on an mbarrier nothing arrives on, with a limit of
 // `limit_ns`; it leaves kErrProbeTimeout in *err and returns.
 cudaError_t launch_bounded_wait_probe(int* err, unsigned long long limit_ns, cudaStream_t s);

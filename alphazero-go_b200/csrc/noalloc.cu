@@ -4,12 +4,11 @@
 // a static device array instead of a workspace allocated with cudaMalloc.
 //
 // Who needs it: callers that may not allocate device memory at the moment
-// they evaluate. A host that captures its own work into a CUDA graph cannot
-// call cudaMalloc inside the capture; an application that hands the GPU's
-// memory to its own pool allocator, or runs under a fixed memory budget,
-// forbids allocations behind its back; and on a latency-critical path
-// cudaMalloc can synchronise the whole device. Such a caller creates its
-// azb_infer handle once at set-up (that uploads the weights) and then
+// they evaluate. An application that hands the GPU's memory to its own pool
+// allocator, or runs under a fixed device-memory budget, forbids
+// allocations behind its back; and on a latency-critical path cudaMalloc
+// can synchronise the whole device. Such a caller creates its azb_infer
+// handle once at set-up (that allocates, and uploads the weights) and then
 // evaluates through this entry point, which allocates nothing.
 //
 // The array holds kScratchBytes on every GPU that loads this library, for as

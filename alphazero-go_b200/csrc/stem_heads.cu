@@ -537,6 +537,19 @@ cudaError_t launch_spin(unsigned long long ns, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+namespace {
+__global__ void admission_probe_kernel(uint32_t* data, int n) {
+    const int i = int(blockIdx.x * blockDim.x + threadIdx.x);
+    if (i < n) data[i] = admission_probe_value(data[i], i);
+}
+}  // namespace
+
+cudaError_t launch_admission_probe(uint32_t* data, int n, cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    admission_probe_kernel<<<(n + 127) / 128, 128, 0, s>>>(data, n);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_bounded_wait_probe(int* err, unsigned long long limit_ns, cudaStream_t s) {
     bounded_wait_probe<<<1, 32, 0, s>>>(err, limit_ns);
     return cudaGetLastError();

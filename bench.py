@@ -140,9 +140,13 @@ class ClockSampler:
         self.t1 = datetime.datetime.now()
 
     def stop(self) -> dict | None:
+        """Stops sampling; the summary of [mark_start, mark_stop]."""
         if self.proc is None:
             return None
-        self.proc.terminate()
+        self._collect()
+        return self.window(self.t0, self.t1)
+
+    def _collect(self):
         try:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
@@ -153,7 +157,7 @@ class ClockSampler:
         rows = [r.split(",") for r in self.out.read().splitlines() if r.strip()]
         self.out.close()
         os.unlink(self.out.name)
-        samples = []
+        self.samples = samples = []
         for r in rows:
             r = [c.strip() for c in r]
             if len(r) < 11:
@@ -166,14 +170,18 @@ class ClockSampler:
                 samples.append((when, float(r[3]), float(r[4]), r[7:11]))
             except ValueError:
                 continue
+
+    def window(self, t0, t1) -> dict | None:
+        """Median SM clock, max clock and throttle reasons of the samples in [t0, t1]."""
+        samples = getattr(self, "samples", None)
         if not samples:
             return None
         inside = samples
-        if self.t0 and self.t1:
+        if t0 and t1:
             slack = datetime.timedelta(seconds=0.1)
-            inside = [x for x in samples if self.t0 - slack <= x[0] <= self.t1 + slack]
+            inside = [x for x in samples if t0 - slack <= x[0] <= t1 + slack]
             if not inside:
-                mid = self.t0 + (self.t1 - self.t0) / 2
+                mid = t0 + (t1 - t0) / 2
                 inside = [min(samples, key=lambda x: abs((x[0] - mid).total_seconds()))]
         reasons = set()
         for x in inside:
@@ -295,11 +303,12 @@ def selfplay_cpu_sample(plies: int = 6):
     core; oracle/_ref/libazselfplay_ref.so): one game per worker, each cut at
     `plies` plies (move cap), so the sample ends in seconds."""
     sys.path.insert(0, os.path.join(ROOT, "alphazero-go_b200"))
-    import azb200 as E
-    import selfplay as SP
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    import selfplay as SP   # ctypes over the library given below; it maps no engine library
 
-    sp_desc = E.NetDesc(SP_BOARD, 1, SP_BLOCKS, SP_FILTERS, SP_VH, 0)
-    p, b = E.synth_network(sp_desc, SEED, 0)
+    sp_desc = O.NetConfig(SP_BOARD, 1, SP_BLOCKS, SP_FILTERS, SP_VH, False)
+    p, b = O.make_network(sp_desc, SEED, O.KIND_BENCH)   # the reference's seeded Network, restated
     workers = len(os.sched_getaffinity(0))
     lib = os.path.join(ROOT, "oracle", "_ref", "libazselfplay_ref.so")
     r = SP.play(sp_desc, p, b, backend="blas", workers=workers, simulations=SP_SIMS, mcts_batch=SP_MCTS_BATCH,
@@ -392,6 +401,72 @@ def run_selfplay(d: "Dist", dev: int) -> dict | None:
                    "(alphazero-go_b200/host), one slice of 512 games per GPU, host wall clock, max over ranks"}
 
 
+def runner_passes(runner, B: int, n: int) -> None:
+    """n passes of B positions through the runner's C ABI, both slots kept in
+    flight (each slot begins again as soon as its done() arrives)."""
+    done_q, cv = [], threading.Condition()
+
+    def done(slot, err):
+        with cv:
+            done_q.append((slot, err))
+            cv.notify()
+
+    inflight = started = 0
+    for s in range(min(runner.slots(), n)):
+        runner.begin(s, B, done)
+        inflight += 1
+        started += 1
+    errors = []
+    while inflight:
+        with cv:
+            while not done_q:
+                cv.wait()
+            slot, err = done_q.pop(0)
+        inflight -= 1
+        if err:
+            errors.append(err)
+        if started < n and not errors:
+            runner.begin(slot, B, done)
+            inflight += 1
+            started += 1
+    if errors:
+        raise RuntimeError(errors[0])
+
+
+def fp32_class_records(d: "Dist", E, desc, params, buffers, x, dev: int, steps: int) -> dict:
+    """C4 in TF32X3 and TF32 on this rank's batch: device passes (CUDA
+    events, inputs resident), the runner's C ABI with 2 slots and host copies
+    (wall clock), and the tower conv's rate (events around each launch).
+    Positions/s are summed over ranks from the max-over-ranks times."""
+    out = {}
+    for pname, prec in (("tf32x3", E.TF32X3), ("tf32", E.TF32)):
+        with E.CudaInference(desc, params, buffers, BATCH, dev, prec) as net:
+            net.stage(x)
+            net.time(BATCH, 0, 2)
+            d.barrier()
+            ms, _ = net.time(BATCH, 0, steps)
+            _, conv_ms = net.time(BATCH, 0, 2, conv=True)
+        ms, conv_avg_ms = d.max(ms), d.max(conv_ms / (2 * 2 * BLOCKS))
+        runner = E.make_cuda_runner(desc, params, buffers, BATCH, 2, dev, prec)
+        for sl in range(2):
+            runner.input(sl)[:] = x
+        runner_passes(runner, BATCH, 2)
+        d.barrier()
+        t0 = time.perf_counter()
+        runner_passes(runner, BATCH, steps)
+        run_s = d.max(time.perf_counter() - t0)
+        runner.close()
+        out[pname] = {"positions_per_s": d.world * BATCH * steps / (ms / 1e3),
+                      "e2e_positions_per_s": d.world * BATCH * steps / run_s,
+                      "conv_tflops": conv_flops_per_position() * BATCH / (conv_avg_ms * 1e-3) / 1e12,
+                      "ms_per_pass": ms / steps, "steps": steps}
+    out["how"] = ("C4 at batch 1024 per GPU; positions_per_s: device passes by CUDA events (inputs resident); "
+                  "e2e_positions_per_s: BatchRunner C ABI, 2 slots, host copies, wall clock; conv_tflops: events "
+                  "around every tower conv (useful FLOPs: one product per MAC, whatever the mode's MMA count)")
+    out["parity"] = "tf32x3: maxErr <= 1e-4 vs the reference forward (tests/test_gpu_gates.py); tf32: reported"
+    return out
+
+
 def run_engine(args, d: Dist):
     import numpy as np
 
@@ -423,13 +498,22 @@ def run_engine(args, d: Dist):
     d.barrier()
     if sampler:
         sampler.mark_stop()
-    clocks = sampler.stop() if sampler else None
     ms = d.max(ms)
     value = d.world * BATCH * args.steps / (ms / 1e3)
 
-    # --- the conv kernel alone, per launch (CUDA events around each launch)
-    _, conv_ms = net.time(BATCH, 0, max(2, min(args.steps, 5)), conv=True)
-    conv_launches = 2 * BLOCKS * max(2, min(args.steps, 5))
+    # --- the conv kernel alone, per launch: CUDA events around each launch.
+    # The events stop programmatic dependent launch from overlapping a
+    # launch's start with its predecessor's tail, so this is a lower bound
+    # on the kernel's rate inside a pass (the whole-pass figure is higher).
+    roof_passes = max(2, min(args.steps, 5))
+    roof_t0 = datetime.datetime.now()
+    r0 = time.perf_counter()
+    _, conv_ms = net.time(BATCH, 0, roof_passes, conv=True)
+    roof_s = time.perf_counter() - r0
+    roof_t1 = datetime.datetime.now()
+    clocks = sampler.stop() if sampler else None
+    roof_clocks = sampler.window(roof_t0, roof_t1) if sampler else None
+    conv_launches = 2 * BLOCKS * roof_passes
     conv_avg_ms = d.max(conv_ms / conv_launches)
     conv_tflops = conv_flops_per_position() * BATCH / (conv_avg_ms * 1e-3) / 1e12
 
@@ -446,45 +530,19 @@ def run_engine(args, d: Dist):
     runner = E.make_cuda_runner(desc, params, buffers, BATCH, 2, dev, precision)
     for s in range(2):
         runner.input(s)[:] = x
-    done_q, lock = [], threading.Condition()
-
-    def done(slot, err):
-        with lock:
-            done_q.append((slot, err))
-            lock.notify()
-
-    def run_passes(n):
-        inflight = 0
-        started = 0
-        for s in range(min(2, n)):
-            runner.begin(s, BATCH, done)
-            inflight += 1
-            started += 1
-        errors = []
-        while inflight:
-            with lock:
-                while not done_q:
-                    lock.wait()
-                slot, err = done_q.pop(0)
-            inflight -= 1
-            if err:
-                errors.append(err)
-            if started < n and not errors:
-                runner.begin(slot, BATCH, done)
-                inflight += 1
-                started += 1
-        if errors:
-            raise RuntimeError(errors[0])
-
-    run_passes(args.warmup)
+    runner_passes(runner, BATCH, args.warmup)
     d.barrier()
     t0 = time.perf_counter()
-    run_passes(args.steps)
+    runner_passes(runner, BATCH, args.steps)
     e2e_s = time.perf_counter() - t0
     d.barrier()
     e2e_s = d.max(e2e_s)
     runner.close()
     e2e = d.world * BATCH * args.steps / e2e_s
+
+    # --- the same workload in the fp32-class modes (the reference's CUDA
+    # engine computes in fp32): TF32X3 meets the 1e-4 gate, TF32 is reported
+    fp32_class = fp32_class_records(d, E, desc, params, buffers, x, dev, min(args.steps, 10))
 
     # --- end to end from position records (the device encoder): one synchronous
     # CudaInference call per pass, records in and logits/values out every pass
@@ -551,12 +609,16 @@ def run_engine(args, d: Dist):
             "roofline": {"bound": "tensor", "achieved": conv_tflops, "peak": peak, "unit": "TFLOP/s",
                          "frac": conv_tflops / peak, "traffic": traffic, "peak_source": peak_note,
                          "kernel": "conv3x3_tc_pair<256,bf16>", "flop_per_launch": conv_flops_per_position() * BATCH,
-                         "avg_launch_ms": conv_avg_ms},
+                         "avg_launch_ms": conv_avg_ms, "launches": conv_launches, "timed_region_s": roof_s,
+                         "sm_mhz": roof_clocks["sm_mhz"] if roof_clocks else None,
+                         "how": "CUDA events around every conv launch of the passes (which stops each launch "
+                                "overlapping its predecessor's tail: a lower bound on the in-pass rate)"},
             "tensor_tflops_whole_pass": flops_per_position() * BATCH * d.world * args.steps / (ms / 1e3) / 1e12,
             "gpu_launches": args.steps * (2 * BLOCKS + 5),   # stem operand + stem GEMM + tower + 3 head launches
             "clocks": clocks,
             "cpu_baseline": cpu,
             "e2e_records": e2e_records,
+            "fp32_class": fp32_class,
         }
         if selfplay is not None:
             line["selfplay"] = selfplay
@@ -634,35 +696,9 @@ def run_sweep(args):
             runner = E.make_cuda_runner(desc, params, buffers, B, 2, 0, prec)
             for sl in range(2):
                 runner.input(sl)[:] = x
-            done_q, cv = [], threading.Condition()
-
-            def done(slot, err):
-                with cv:
-                    done_q.append((slot, err))
-                    cv.notify()
-
-            def passes(k):
-                inflight = started = 0
-                for sl in range(min(2, k)):
-                    runner.begin(sl, B, done)
-                    inflight += 1
-                    started += 1
-                while inflight:
-                    with cv:
-                        while not done_q:
-                            cv.wait()
-                        sl, err = done_q.pop(0)
-                    inflight -= 1
-                    if err:
-                        raise RuntimeError(err)
-                    if started < k:
-                        runner.begin(sl, B, done)
-                        inflight += 1
-                        started += 1
-
-            passes(3)
+            runner_passes(runner, B, 3)
             t0 = time.perf_counter()
-            passes(steps)
+            runner_passes(runner, B, steps)
             run_s = time.perf_counter() - t0
             runner.close()
             line["engine"][pname] = {"positions_per_s": B * steps / (ms / 1e3),

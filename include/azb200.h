@@ -118,10 +118,9 @@ int azb_infer_run(azb_infer* h, const float* input, int B, float* logits, float*
 size_t azb_infer_bytes(const azb_infer* h);
 
 /* azb_infer_run without allocating: no counterpart in the reference. For
- * callers that may not allocate device memory when they evaluate -- work
- * being captured into a CUDA graph (cudaMalloc is not allowed during a
- * capture), hosts whose own pool allocator owns the GPU's memory or that run
- * under a fixed budget, latency-critical paths where cudaMalloc may
+ * callers that may not allocate device memory when they evaluate -- hosts
+ * whose own pool allocator owns the GPU's memory or that run under a fixed
+ * device-memory budget, latency-critical paths where cudaMalloc may
  * synchronise the device. The handle is created once at set-up (that
  * allocates, and uploads the weights); this call then runs the same forward
  * pass with all its scratch (input staging, stem operand, activation frames,
@@ -196,6 +195,16 @@ float* azb_runner_input(azb_runner* r, int slot);
  * in, forward, copy out and returns at once. A batch out of range or an
  * enqueue error is reported through done (never by returning). */
 int azb_runner_begin(azb_runner* r, int slot, int B, azb_done_fn done, void* ctx);
+/* The same pass from position records instead of planes (the record
+ * format of azb_stones_record_bytes): azb_runner_records(slot) is pinned
+ * [max_batch][azb_stones_record_bytes(history, board)] staging, and
+ * azb_runner_begin_stones encodes its first B records on the device (the
+ * reference's encodePlanes, src/encode.cpp:15-43) before the forward pass,
+ * so ~H*n*n bytes per position cross to the GPU instead of (2H+2)*n*n
+ * floats. No reference counterpart: the reference's BatchRunner takes
+ * planes only, encoded on the host (src/mcts.cpp:117-132). */
+uint8_t* azb_runner_records(azb_runner* r, int slot);
+int azb_runner_begin_stones(azb_runner* r, int slot, int B, azb_done_fn done, void* ctx);
 const float* azb_runner_logits(const azb_runner* r, int slot);
 const float* azb_runner_values(const azb_runner* r, int slot);
 const float* azb_runner_ownership(const azb_runner* r, int slot);

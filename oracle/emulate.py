@@ -94,6 +94,53 @@ def forward(cfg: O.NetConfig, params, buffers, inp: np.ndarray, mode: str):
     return logits, v
 
 
+def calibrated_network(cfg: O.NetConfig, seed: int, calib_seed: int = 99, calib_positions: int = 16):
+    """A seeded network whose batch norms normalise what reaches them.
+
+    Network(cfg, seed) with BASELINE.json's batch-norm distributions
+    (make_network, KIND_BENCH), then, layer by layer in forward order, each
+    batch norm's running mean and variance replaced by the float64 mean and
+    variance (+1e-3) of its input over `calib_positions` positions
+    (positions(cfg, calib_seed, ...)), as a trained network's running
+    statistics describe its own activations. gamma and beta keep their
+    random values. With 20 residual blocks the uncalibrated network's logits
+    span +-1e4 and its values saturate at +-1; calibrated, logits stay within
+    a few units, values spread over (-1, 1) and the best moves are nearly
+    tied, so precision gates on it can fail. Returns (params, buffers)."""
+    params, buffers = O.make_network(cfg, seed, O.KIND_BENCH)
+    offs = {n: (s, o) for n, s, o in O.layout(cfg, 0)}
+    boffs = {n: (s, o) for n, s, o in O.layout(cfg, 1)}
+
+    def T(name):
+        s, o = offs[name] if name in offs else boffs[name]
+        return (params if name in offs else buffers)[o:o + s].astype(np.float64)
+
+    def fit(pre, z):
+        flat = z.reshape(-1, z.shape[-1])
+        for stat, v in (("runMean", flat.mean(0)), ("runVar", flat.var(0) + 1e-3)):
+            s, o = boffs[f"{pre}.{stat}"]
+            buffers[o:o + s] = v.astype(np.float32)
+        sc = T(pre + ".gamma") / np.sqrt(T(pre + ".runVar") + np.float64(np.float32(1e-5)))
+        return (z - T(pre + ".runMean")) * sc + T(pre + ".beta")
+
+    n, F = cfg.board, cfg.filters
+    x = positions_f64(cfg, calib_seed, calib_positions)
+    h = np.maximum(fit("stem.bn", conv3(x, T("stem.conv.w").reshape(F, -1), n)), 0)
+    for i in range(cfg.blocks):
+        m = np.maximum(fit(f"block{i}.bn1", conv3(h, T(f"block{i}.conv1.w").reshape(F, -1), n)), 0)
+        h = np.maximum(fit(f"block{i}.bn2", conv3(m, T(f"block{i}.conv2.w").reshape(F, -1), n)) + h, 0)
+    fit("policy.bn", h @ T("policy.conv.w").reshape(2, F).T)
+    fit("value.bn", h @ T("value.conv.w").reshape(1, F).T)
+    if cfg.ownership:
+        fit("ownership.bn", h @ T("ownership.conv.w").reshape(1, F).T)
+    return params, buffers
+
+
+def positions_f64(cfg: O.NetConfig, seed: int, B: int) -> np.ndarray:
+    """positions(cfg, seed, B) as float64 [B][A][planes] (channels last)."""
+    return O.positions(cfg, seed, B).transpose(0, 2, 1).astype(np.float64)
+
+
 def gates(logits, values, ref_logits, ref_values) -> dict:
     pr, pm = O.softmax(ref_logits), O.softmax(logits)
     return {

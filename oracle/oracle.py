@@ -176,6 +176,9 @@ def ref() -> C.CDLL:
         R.azref_layout_entry.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_char_p, C.c_size_t,
                                          C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]
         R.azref_export.argtypes = [C.c_void_p, _F, _F]
+        R.azref_import.argtypes = [C.c_void_p, _F, _F]
+        R.azref_infer_threads.argtypes = [C.c_void_p, C.c_char_p, _F, C.c_int, _F, _F, _F, C.c_int, C.c_char_p,
+                                          C.c_size_t]
         R.azref_infer.argtypes = [C.c_void_p, C.c_char_p, _F, C.c_int, _F, _F, _F, C.c_char_p, C.c_size_t]
         R.azref_inputs_positions.argtypes = [C.c_int, C.c_int, C.c_uint64, C.c_long, C.c_int, _F]
         R.azref_inputs_planes.argtypes = [C.c_uint64, C.c_size_t, _F]
@@ -225,7 +228,20 @@ class RefNetwork:
         R.azref_export(self.h, _fp(params), _fp(buffers))
         return params, buffers
 
-    def infer(self, x: np.ndarray, backend: str = "naive"):
+    @classmethod
+    def from_arenas(cls, cfg: NetConfig, params: np.ndarray, buffers: np.ndarray) -> "RefNetwork":
+        """The reference's Network of this shape holding the given arenas' tensors."""
+        net = cls(cfg, 0, None)
+        p = np.ascontiguousarray(params, np.float32)
+        b = np.ascontiguousarray(buffers, np.float32)
+        R = ref()
+        assert p.size == R.azref_floats(net.h, 0) and b.size == R.azref_floats(net.h, 1)
+        R.azref_import(net.h, _fp(p), _fp(b))
+        return net
+
+    def infer(self, x: np.ndarray, backend: str = "naive", threads: int = 1):
+        """Network::infer (src/network.cpp:171-183); with threads > 1 the
+        batch is split over that many workers (same outputs, position by position)."""
         cfg = self.cfg
         x = np.ascontiguousarray(x, np.float32)
         B = x.shape[0]
@@ -233,7 +249,11 @@ class RefNetwork:
         values = np.zeros(B, np.float32)
         own = np.zeros((B, cfg.area), np.float32) if cfg.ownership else None
         err = C.create_string_buffer(256)
-        rc = ref().azref_infer(self.h, backend.encode(), _fp(x), B, _fp(logits), _fp(values), _fp(own), err, 256)
+        if threads > 1:
+            rc = ref().azref_infer_threads(self.h, backend.encode(), _fp(x), B, _fp(logits), _fp(values), _fp(own),
+                                           threads, err, 256)
+        else:
+            rc = ref().azref_infer(self.h, backend.encode(), _fp(x), B, _fp(logits), _fp(values), _fp(own), err, 256)
         if rc != 0:
             raise RuntimeError(err.value.decode())
         return logits, values, own

@@ -185,6 +185,57 @@ int azref_infer(azref_net* h, const char* backend, const float* input, int B, fl
     }
 }
 
+// Network::infer over B positions split into `threads` contiguous slices,
+// each slice on its own thread with its own single-threaded backend and
+// Workspace, as the reference's workers share one read-only Network
+// (include/azgo/evaluator.hpp's LocalEvaluator). Each position's outputs
+// are those of infer alone: the reference's forward is batch independent.
+int azref_infer_threads(azref_net* h, const char* backend, const float* input, int B, float* logits, float* values,
+                        float* ownership, int threads, char* err, size_t cap) {
+    try {
+        const NetConfig& cfg = h->net.config();
+        const size_t P = static_cast<size_t>(cfg.planes()) * cfg.area();
+        threads = std::max(1, std::min(threads, B));
+        const int per = (B + threads - 1) / threads;
+        std::vector<std::thread> pool;
+        std::mutex m;
+        std::string first_error;
+        for (int t = 0; t < threads; ++t) {
+            const int lo = t * per, n = std::min(B, lo + per) - lo;
+            if (n <= 0) break;
+            pool.emplace_back([&, lo, n] {
+                try {
+                    std::unique_ptr<Backend> be = makeBackend(backend, 1);
+                    Workspace ws(cfg, n, *be);
+                    h->net.infer(ws, input + lo * P, n, logits + static_cast<size_t>(lo) * cfg.actions(), values + lo,
+                                 ownership ? ownership + static_cast<size_t>(lo) * cfg.area() : nullptr);
+                } catch (const std::exception& e) {
+                    std::lock_guard<std::mutex> lock(m);
+                    if (first_error.empty()) first_error = e.what();
+                }
+            });
+        }
+        for (auto& th : pool) th.join();
+        if (!first_error.empty()) throw std::runtime_error(first_error);
+        return 0;
+    } catch (const std::exception& e) {
+        fail(err, cap, e.what());
+        return -1;
+    }
+}
+
+// Replaces the network's tensors with the two ParamLayout arenas
+// (params() then buffers() at their offsets), e.g. to run the reference
+// forward on weights made or changed outside it.
+void azref_import(azref_net* h, const float* params, const float* buffers) {
+    const auto views = h->net.params();
+    for (size_t i = 0; i < views.size(); ++i)
+        std::memcpy(views[i].value, params + h->layout.params[i].offset, views[i].size * sizeof(float));
+    const auto bufs = h->net.buffers();
+    for (size_t i = 0; i < bufs.size(); ++i)
+        std::memcpy(bufs[i].value, buffers + h->layout.buffers[i].offset, bufs[i].size * sizeof(float));
+}
+
 // Positions with one history position, encoded by the reference's
 // encodePlanes (src/encode.cpp:14-43); the stones are drawn exactly as
 // azoracle.c's az_inputs_positions draws them.

@@ -1,7 +1,7 @@
 """azb_infer_run_noalloc through the C ABI: the forward pass for callers that
-may not allocate device memory when they evaluate (work captured into a CUDA
-graph, hosts whose pool allocator owns the GPU's memory, latency-critical
-paths). Its scratch lives in the library's static device array; its results
+may not allocate device memory when they evaluate (hosts whose pool
+allocator owns the GPU's memory or that run under a fixed device-memory
+budget, latency-critical paths). Its scratch lives in the library's static device array; its results
 must equal azb_infer_run's on the same handle and inputs (tolerance 0: the
 same kernels run on the same weights), on two calls in a row, including a
 call whose frame padding lies where the previous call wrote real points.
