@@ -389,7 +389,7 @@ template <int N, int kMine>
 __device__ __forceinline__ void store_split_sums(const ConvArgs& p, const float* scale, const float* shift,
                                                  const void* res_hi, const void* res_lo, float (&sum)[kMine * 32],
                                                  const CUtensorMap* mhi, const CUtensorMap* mlo, uint8_t* box,
-                                                 int row0, int q, bool valid, int c_begin, int lane) {
+                                                 int row0, int q, bool valid, int c_begin, int lane, int col0 = 0) {
     using Box = EpiBox<false>;
     if (row0 >= p.rows) return;   // the warp's rows are all past the frame
     const bool skip = valid && res_hi != nullptr;
@@ -436,7 +436,7 @@ __device__ __forceinline__ void store_split_sums(const ConvArgs& p, const float*
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-                tma_store_2d(plane == 0 ? mhi : mlo, box, c0, row0);
+                tma_store_2d(plane == 0 ? mhi : mlo, box, col0 + c0, row0);
                 bulk_commit();
             }
         }
@@ -446,6 +446,17 @@ __device__ __forceinline__ void store_split_sums(const ConvArgs& p, const float*
 // kSeg: the stacked split mode's accumulation segment in taps (0: one run
 // per tile). mOut/mSkip: the epilogue's output and residual boxes; in the
 // stacked split mode the high and low output planes.
+//
+// kWide: the stacked split mode for a layer of 2N output channels, as two
+// column halves of N: item it is tile group it / 2 and output channels
+// [(it % 2) N, (it % 2 + 1) N). Each item loads its half's weight rows (mW
+// and mWlo in boxes of N rows), reads its half of the batch norm (scale and
+// shift of all 2N channels in shared memory) and of the residual, and
+// stores its half of the output. The two halves of a tile are consecutive
+// items, so the second finds the halo in L2. This keeps 256-channel layers
+// in the segmented accumulation (each segment's large products on their own
+// accumulator, summed in round-to-nearest), which one 256-column
+// accumulator per tile cannot hold beside its running sums.
 //
 // kPersist: the persistent tower (bf16 and tf32; the stacked split mode in
 // its segments). Items are (layer, tile group) = (it / ngroups, it %
@@ -463,7 +474,7 @@ __device__ __forceinline__ void store_split_sums(const ConvArgs& p, const float*
 // groups g-1, g, g+1 (the rows its halo reads) have reached kEpiWarps.
 // Writes need no wait of their own: the buffer an item overwrites was last
 // read by items that those same dependencies already include.
-template <int N, bool kBf16, bool kSplit, int kTiles, int kSeg, bool kPersist = false>
+template <int N, bool kBf16, bool kSplit, int kTiles, int kSeg, bool kPersist = false, bool kWide = false>
 __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
     conv3x3_tc(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAlo,
                const __grid_constant__ CUtensorMap mW, const __grid_constant__ CUtensorMap mWlo,
@@ -472,11 +483,15 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
     using C = ConvCfg<N, kBf16, kSplit, kTiles>;
     static_assert(!kPersist || (!kSplit && kSeg == 0) || (C::kStack && kSeg != 0 && kTiles == 1),
                   "the persistent tower: bf16 and tf32, or the split mode's segmented single tiles");
+    static_assert(!kWide || (C::kStack && kSeg != 0 && kTiles == 1 && !kPersist && 2 * N <= 256),
+                  "column halves: the stacked split mode's segmented single tiles, per layer");
+    constexpr int kBnCh = kWide ? 2 * N : N;   // batch-norm channels in shared memory (shift at kBnCh)
     extern __shared__ uint8_t smem_raw[];
     const Smem sm = carve(smem_raw, p.sa, p.sb, C::kOps * kTiles, C::kOps, p.a_bytes, C::kBBytes, C::kEpiBytes);
     const int ngroups = (p.ntiles + kTiles - 1) / kTiles;   // a CTA takes kTiles consecutive tiles at a time
     int nitems = ngroups;
     if constexpr (kPersist) nitems = tf.layers * ngroups;
+    if constexpr (kWide) nitems = 2 * ngroups;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // The persistent tower's item ring lives where the batch norm would (its
     // batch norms are read from tf.tower): kItemSlots full and empty barriers,
@@ -523,9 +538,9 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
     }
     if (warp == 1) tmem_alloc(sm.tmem_slot, C::kTmemCols);
     if (!kPersist)
-        for (int i = threadIdx.x; i < N; i += kThreadsOf<kTiles>) {
+        for (int i = threadIdx.x; i < kBnCh; i += kThreadsOf<kTiles>) {
             sm.bn[i] = p.scale[i];
-            sm.bn[N + i] = p.shift[i];
+            sm.bn[kBnCh + i] = p.shift[i];
         }
     tc_fence_before();
     __syncthreads();
@@ -556,7 +571,11 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                     ri.next(kItemSlots);
                 }
                 if (it >= nitems) break;
-                int g = it, taps = p.taps, nchunks = p.nchunks;
+                int g = it, taps = p.taps, nchunks = p.nchunks, wrow = 0;
+                if constexpr (kWide) {   // a tile group's column half: its weight rows
+                    g = it >> 1;
+                    wrow = (it & 1) * N;
+                }
                 const CUtensorMap* amap = &mA;
                 const CUtensorMap* alo = &mAlo;
                 const CUtensorMap* wmap = &mW;
@@ -602,8 +621,9 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                         if (!(ok = mbar_wait(&sm.b_empty[rb.idx], rb.phase ^ 1u, p.err, kErrWaitProducer))) break;
                         mbar_arrive_expect_tx(&sm.b_full[rb.idx], b_tx);
                         uint8_t* bbuf = sm.b + rb.idx * (C::kOps * C::kBBytes);
-                        tma_load_2d(wmap, bbuf, &sm.b_full[rb.idx], (c * taps + t) * C::kKc, 0);
-                        if (kSplit) tma_load_2d(wlo, bbuf + C::kBBytes, &sm.b_full[rb.idx], (c * taps + t) * C::kKc, 0);
+                        tma_load_2d(wmap, bbuf, &sm.b_full[rb.idx], (c * taps + t) * C::kKc, wrow);
+                        if (kSplit)
+                            tma_load_2d(wlo, bbuf + C::kBBytes, &sm.b_full[rb.idx], (c * taps + t) * C::kKc, wrow);
                         rb.next(p.sb);
                         ++nb;
                     }
@@ -815,8 +835,16 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
         const int layer_segs = segs_of(p.taps, p.nchunks);
         // An item's ItemIo, derived where it is used rather than held across
         // the segments' accumulation (registers are at the 168 cap).
-        auto item_io = [&](int layer) {
+        auto item_io = [&](int layer, int col0) {
             ItemIo io{sm.bn, sm.bn + N, p.skip, p.skip_lo, &mOut, &mSkip};
+            if constexpr (kWide) {   // this item's column half (the residual's rows hold all 2N channels)
+                io.scale = sm.bn + col0;
+                io.shift = sm.bn + kBnCh + col0;
+                if (p.skip) {
+                    io.res_hi = static_cast<const float*>(p.skip) + col0;
+                    io.res_lo = static_cast<const float*>(p.skip_lo) + col0;
+                }
+            }
             if constexpr (kPersist) {
                 // Tower conv l writes buffer (l+1) mod 3; a block's second conv
                 // (l odd) adds its first conv's input, buffer (l-1) mod 3. The
@@ -846,7 +874,11 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                 if (it < 0) break;
             }
             if (it >= nitems) break;
-            int g = it, layer = 0;
+            int g = it, layer = 0, col0 = 0;
+            if constexpr (kWide) {   // a tile group's column half
+                g = it >> 1;
+                col0 = (it & 1) * N;
+            }
             if constexpr (kPersist) {
                 layer = it / ngroups;
                 g = it - layer * ngroups;
@@ -877,7 +909,7 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                 constexpr int kMine = kTiles == 2 ? kChunks : (kChunks >= 2 ? kChunks / 2 : 1);
                 const bool mine = c_begin < c_end && tile < p.ntiles;
                 if (mine && valid) {   // the residual reaches L2 while the tile accumulates
-                    const ItemIo io = item_io(layer);
+                    const ItemIo io = item_io(layer, col0);
                     if (io.res_hi != nullptr) {
                         const size_t off = size_t(q) * p.ld + size_t(c_begin) * 32;
 #pragma unroll
@@ -904,9 +936,9 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                 }
                 if (!ok) break;
                 if (mine) {
-                    const ItemIo io = item_io(layer);
+                    const ItemIo io = item_io(layer, col0);
                     store_split_sums<N, kMine>(p, io.scale, io.shift, io.res_hi, io.res_lo, sum, io.omap, io.smap,
-                                               ew.obuf, tile * 128 + quarter * 32, q, valid, c_begin, lane);
+                                               ew.obuf, tile * 128 + quarter * 32, q, valid, c_begin, lane, col0);
                 }
                 if constexpr (kPersist) {
                     if (lane == 0) {   // this warp's part of the item has landed in global memory
@@ -920,7 +952,7 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                 if (!mbar_wait(&sm.acc_full[acc], (j >> 1) & 1, p.err, kErrWaitEpilogue)) break;
                 tc_fence_after();
                 const uint32_t taddr = lanes + acc * (kTiles * C::kTileCols);
-                const ItemIo io = item_io(layer);
+                const ItemIo io = item_io(layer, 0);
                 if constexpr (C::kEpiTma)
                     store_epilogue_tma<N, kBf16, kPersist>(p, io.scale, io.shift, io.res_hi, io.omap, io.smap, taddr,
                                                  tile * 128 + quarter * 32, valid, c_begin, c_end, ew, lane);
@@ -1270,6 +1302,27 @@ cudaError_t launch_single_seg(const ConvMaps& m, ConvArgs a, int sms, cudaStream
                       m.a_lo, m.w, m.w_lo, m.out, C::kStack ? m.out_lo : m.skip, a, NoTower{});
 }
 
+// A 2N-channel layer in the split mode as two column halves of N (kWide),
+// one CTA per item (a tile group's half), in the stacked mode's default
+// segments. The weight maps are the pair form's (boxes of N = n_out / 2 rows).
+template <int N>
+cudaError_t launch_wide(const ConvMaps& m, ConvArgs a, int sms, cudaStream_t s) {
+    using C = ConvCfg<N, false, true, 1>;
+    constexpr int kSeg = kDefaultSegment<N>;
+    conv_smem_bytes(N, kTF32x3, a.halo_rows, &a.sa, &a.sb, false, 1);
+    const size_t smem = smem_total(a.sa, a.sb, C::kOps, C::kOps, a.a_bytes, C::kBBytes, C::kEpiBytes);
+    static std::atomic<size_t> configured{0};
+    if (smem > configured.load()) {
+        const cudaError_t e = cudaFuncSetAttribute(conv3x3_tc<N, false, true, 1, kSeg, false, true>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e != cudaSuccess) return e;
+        configured = smem;
+    }
+    const int grid = std::max(1, std::min(2 * a.ntiles, sms));
+    return launch_pdl(conv3x3_tc<N, false, true, 1, kSeg, false, true>, dim3(grid), dim3(kThreadsOf<1>), smem, s, m.a,
+                      m.a_lo, m.w_pair, m.w_lo_pair, m.out, m.out_lo, a, NoTower{});
+}
+
 // The stacked split mode runs in segments of kDefaultSegment<N> taps unless
 // the test hook asks for one run per tile (a.seg == 0).
 template <int N, bool kBf16, bool kSplit, int kTiles>
@@ -1457,6 +1510,13 @@ cudaError_t launch_conv(const ConvMaps& maps, const ConvArgs& args, int n_out, i
     ConvArgs a = args;
     const int segment = g_conv_segment.load();
     a.seg = segment < 0 ? 1 : segment;   // 0: one run per tile; otherwise segments of kDefaultSegment<N> taps
+    // The split mode at 256 channels: two segmented column halves of 128
+    // (one 256-column accumulator run per tile drifts: tcgen05 accumulates in
+    // fp32 rounding toward zero, 864 MMAs per tile, ~4e-4 on the 19x19 20x256
+    // network's logits), unless a test hook asks for the pair form or for
+    // one run per tile.
+    if (precision == kTF32x3 && n_out == 256 && a.seg != 0 && g_conv_path.load() != kFormPair)
+        return launch_wide<128>(maps, a, sms, s);
     switch (precision) {
         case kTF32: return dispatch_n<false, false>(n_out, maps, a, form, sms, s);
         case kTF32x3: return dispatch_n<false, true>(n_out, maps, a, form, sms, s);

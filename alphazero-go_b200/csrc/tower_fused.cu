@@ -24,6 +24,13 @@
 // Warps: 0 loads (the group's input, then every layer's weight tiles), 1
 // issues the MMAs and owns TMEM, 2-9 the epilogue (warp w reads TMEM lanes
 // 32(w % 4)...; the two warps of a lane quarter split the output columns).
+// The split mode at 64 channels (two input chunks, each with its own
+// stacked accumulator) adds warp 10 as a second MMA issuer: each thread
+// issues one chunk's MMAs, in the order one thread would, so every
+// accumulator sees the same MMAs in the same order (the same bits). One
+// thread cannot issue that mode's 144 MMAs per layer as fast as the tensor
+// core runs them; two can. The producer then interleaves the two chunks'
+// weight stages, so both issuers find their next stage loaded.
 #include <algorithm>
 #include <atomic>
 
@@ -35,8 +42,11 @@ namespace azb {
 
 namespace {
 
-constexpr int kFusedThreads = 320;
 constexpr int kFusedEpiWarps = 8;
+// Threads per CTA: the loader, the MMA issuer and eight epilogue warps; the
+// split mode adds the second issuer's warp (warp 10).
+template <bool kSplit>
+constexpr int kFusedThreads = kSplit ? 352 : 320;
 
 template <int N, bool kBf16, bool kSplit, int kTps = 1>
 struct FusedCfg {
@@ -106,7 +116,7 @@ template <bool kSplit>
 constexpr int kFusedCtas = kSplit ? 1 : 2;
 
 template <int N, bool kBf16, bool kSplit, int kTps>
-__global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
+__global__ void __launch_bounds__(kFusedThreads<kSplit>, kFusedCtas<kSplit>)
     tower_fused(const __grid_constant__ CUtensorMap mIn, const __grid_constant__ CUtensorMap mInLo,
                 const __grid_constant__ CUtensorMap mOut, const __grid_constant__ CUtensorMap mOutLo,
                 const __grid_constant__ CUtensorMap mStem, const __grid_constant__ CUtensorMap mStemLo,
@@ -118,6 +128,9 @@ __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
     const int ngroups = (p.boards + p.group - 1) / p.group;
     const int group_rows = p.group * p.S;
     const uint32_t tmem_cols = fused_tmem_cols(N, kSplit, p.nch);
+    // Two issuers where each input chunk has its own accumulator and there
+    // are two chunks; issuer i then owns chunk i's stages.
+    const int issuers = kSplit && p.nch == 2 ? 2 : 1;
 
     // Zero both activation buffers: the halos and the rows past the group
     // stay zero for the whole launch.
@@ -143,10 +156,10 @@ __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
             mbar_init(&sm.wempty[i], 1);
         }
         mbar_init(sm.in_full, 1);
-        mbar_init(sm.acc_full, 1);
+        mbar_init(sm.acc_full, uint32_t(issuers));
         mbar_init(sm.act_ready, kFusedEpiWarps);
         mbar_init(sm.out_done, p.heads ? kFusedEpiWarps : 1);   // heads: every epilogue warp reads x
-        mbar_init(sm.done, 1);
+        mbar_init(sm.done, uint32_t(issuers));
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
@@ -190,20 +203,24 @@ __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
                     const bool stem = st_ < first;
                     const FusedLayer& L = stem ? *p.stem : p.layer[st_ - first];
                     // The stem: one tile per chunk (its stage otherwise empty).
+                    // With two issuers the chunks' stages alternate (tap
+                    // groups outer); else chunk-major, one issuer's order.
                     const int taps = stem ? 1 : 9, per_stage = stem ? 1 : kTps;
-                    for (int c = 0; c < (stem ? p.stem_nch : p.nch) && ok; ++c)
-                        for (int t0 = 0; t0 < taps; t0 += per_stage) {
-                            if (!(ok = mbar_wait(&sm.wempty[rw.idx], rw.phase ^ 1u, p.err, kErrWaitProducer))) break;
-                            mbar_arrive_expect_tx(&sm.wfull[rw.idx], uint32_t(per_stage) * C::kTap);
-                            for (int j = 0; j < per_stage; ++j) {
-                                uint8_t* st = sm.ring + size_t(rw.idx) * C::kStage + size_t(j) * C::kTap;
-                                const int x = (c * taps + t0 + j) * C::kKc;
-                                tma_load_2d(&L.w, st, &sm.wfull[rw.idx], x, 0);
-                                if (kSplit) tma_load_2d(&L.w_lo, st + C::kWTile, &sm.wfull[rw.idx], x, 0);
-                            }
-                            rw.next(p.stages);
-                            ++nw;
+                    const int nch = stem ? p.stem_nch : p.nch, groups = taps / per_stage;
+                    for (int i = 0; i < nch * groups && ok; ++i) {
+                        const int c = issuers == 2 ? i % nch : i / groups;
+                        const int t0 = (issuers == 2 ? i / nch : i % groups) * per_stage;
+                        if (!(ok = mbar_wait(&sm.wempty[rw.idx], rw.phase ^ 1u, p.err, kErrWaitProducer))) break;
+                        mbar_arrive_expect_tx(&sm.wfull[rw.idx], uint32_t(per_stage) * C::kTap);
+                        for (int j = 0; j < per_stage; ++j) {
+                            uint8_t* st = sm.ring + size_t(rw.idx) * C::kStage + size_t(j) * C::kTap;
+                            const int x = (c * taps + t0 + j) * C::kKc;
+                            tma_load_2d(&L.w, st, &sm.wfull[rw.idx], x, 0);
+                            if (kSplit) tma_load_2d(&L.w_lo, st + C::kWTile, &sm.wfull[rw.idx], x, 0);
                         }
+                        rw.next(p.stages);
+                        ++nw;
+                    }
                 }
             }
             // Every copy issued has landed before the CTA may exit.
@@ -213,9 +230,12 @@ __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
             }
             if (k > 0) mbar_wait(sm.in_full, (k - 1) & 1, p.err, kErrWaitDrain);
         }
-    } else if (warp == 1) {
-        // --------------------------------------------------------- MMA issue
-        if (lane == 0) {
+    } else if (warp == 1 || (kSplit && warp == 2 + kFusedEpiWarps)) {
+        // -------------------------------------------------------- MMA issue
+        // Issuer `me` issues the MMAs of the stages it owns and walks past
+        // the others; with one issuer it owns them all.
+        const int me = warp == 1 ? 0 : 1;
+        if (lane == 0 && me < issuers) {
             Ring rw;
             bool ok = true;
             uint32_t k = 0, layers_done = 0;
@@ -238,21 +258,24 @@ __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
                     if (st_ < first) {
                         // The stem: a one-tap GEMM over the packed operand in mid.
                         for (int c = 0; c < p.stem_nch && ok; ++c) {
-                            if (!(ok = mbar_wait(&sm.wfull[rw.idx], rw.phase, p.err, kErrWaitMma))) break;
-                            tc_fence_after();
-                            const uint64_t at = sw128_desc(a1) + c * chunk16 + centre16, bt = ring_desc + rw.idx * kStage16;
+                            if (c % issuers == me) {
+                                if (!(ok = mbar_wait(&sm.wfull[rw.idx], rw.phase, p.err, kErrWaitMma))) break;
+                                tc_fence_after();
+                                const uint64_t at = sw128_desc(a1) + c * chunk16 + centre16,
+                                               bt = ring_desc + rw.idx * kStage16;
 #pragma unroll
-                            for (int kk = 0; kk < C::kSteps; ++kk) {
-                                if constexpr (kSplit) {
-                                    const uint32_t d = tmem + uint32_t(c) * 2u * N;
-                                    constexpr uint32_t kIdescStack = umma_idesc(2 * N, kBf16);
-                                    umma<kBf16>(d, at + 2 * kk, bt + 2 * kk, kIdescStack, kk != 0);
-                                    umma<kBf16>(d + N, at + plane16 + 2 * kk, bt + 2 * kk, umma_idesc(N, kBf16), 1);
-                                } else {
-                                    umma<kBf16>(tmem, at + 2 * kk, bt + 2 * kk, umma_idesc(N, kBf16), (c | kk) != 0);
+                                for (int kk = 0; kk < C::kSteps; ++kk) {
+                                    if constexpr (kSplit) {
+                                        const uint32_t d = tmem + uint32_t(c) * 2u * N;
+                                        constexpr uint32_t kIdescStack = umma_idesc(2 * N, kBf16);
+                                        umma<kBf16>(d, at + 2 * kk, bt + 2 * kk, kIdescStack, kk != 0);
+                                        umma<kBf16>(d + N, at + plane16 + 2 * kk, bt + 2 * kk, umma_idesc(N, kBf16), 1);
+                                    } else {
+                                        umma<kBf16>(tmem, at + 2 * kk, bt + 2 * kk, umma_idesc(N, kBf16), (c | kk) != 0);
+                                    }
                                 }
+                                umma_commit(&sm.wempty[rw.idx]);
                             }
-                            umma_commit(&sm.wempty[rw.idx]);
                             rw.next(p.stages);
                         }
                         if (!ok) break;
@@ -262,34 +285,69 @@ __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
                     }
                     const int l = st_ - first;
                     const uint64_t a_desc = sw128_desc((l & 1) ? a1 : a0);
-                    for (int c = 0; c < p.nch && ok; ++c) {
-                        const uint64_t ac = a_desc + c * chunk16;
-                        uint64_t bs = 0;   // the current stage's descriptor
+                    if (issuers == 2) {
+                        // Tap groups outer, the two chunks' stages alternating;
+                        // this issuer's chunk is `me`, its own accumulator.
+                        const uint64_t ac = a_desc + me * chunk16;
+                        const uint32_t d = tmem + uint32_t(me) * 2u * N;
 #pragma unroll
-                        for (int t = 0; t < 9; ++t) {
-                            if (t % kTps == 0) {
-                                if (!(ok = mbar_wait(&sm.wfull[rw.idx], rw.phase, p.err, kErrWaitMma))) break;
-                                tc_fence_after();
-                                bs = ring_desc + rw.idx * kStage16;
-                            }
-                            const uint64_t at = ac + centre16 + (t / 3 - 1) * int(row16) + (t % 3 - 1) * 8,
-                                           bt = bs + (t % kTps) * kTap16;
+                        for (int t0 = 0; t0 < 9; t0 += kTps) {
 #pragma unroll
-                            for (int kk = 0; kk < C::kSteps; ++kk) {
-                                if constexpr (kSplit) {
-                                    // Per input chunk its own stacked accumulator:
-                                    // [0, N) a_hi.b_hi, [N, 2N) a_hi.b_lo + a_lo.b_hi.
-                                    const uint32_t d = tmem + uint32_t(c) * 2u * N;
-                                    constexpr uint32_t kIdescStack = umma_idesc(2 * N, kBf16);
-                                    umma<kBf16>(d, at + 2 * kk, bt + 2 * kk, kIdescStack, (t | kk) != 0);
-                                    umma<kBf16>(d + N, at + plane16 + 2 * kk, bt + 2 * kk, umma_idesc(N, kBf16), 1);
-                                } else {
-                                    umma<kBf16>(tmem, at + 2 * kk, bt + 2 * kk, umma_idesc(N, kBf16), (c | t | kk) != 0);
+                            for (int c = 0; c < 2; ++c) {
+                                if (c == me) {
+                                    if (!(ok = mbar_wait(&sm.wfull[rw.idx], rw.phase, p.err, kErrWaitMma))) break;
+                                    tc_fence_after();
+                                    const uint64_t bs = ring_desc + rw.idx * kStage16;
+#pragma unroll
+                                    for (int j = 0; j < kTps; ++j) {
+                                        const int t = t0 + j;
+                                        const uint64_t at = ac + centre16 + (t / 3 - 1) * int(row16) + (t % 3 - 1) * 8,
+                                                       bt = bs + j * kTap16;
+#pragma unroll
+                                        for (int kk = 0; kk < C::kSteps; ++kk) {
+                                            constexpr uint32_t kIdescStack = umma_idesc(2 * N, kBf16);
+                                            umma<kBf16>(d, at + 2 * kk, bt + 2 * kk, kIdescStack, (t | kk) != 0);
+                                            umma<kBf16>(d + N, at + plane16 + 2 * kk, bt + 2 * kk,
+                                                        umma_idesc(N, kBf16), 1);
+                                        }
+                                    }
+                                    umma_commit(&sm.wempty[rw.idx]);
                                 }
-                            }
-                            if (t % kTps == kTps - 1) {
-                                umma_commit(&sm.wempty[rw.idx]);
                                 rw.next(p.stages);
+                            }
+                            if (!ok) break;
+                        }
+                    } else {
+                        for (int c = 0; c < p.nch && ok; ++c) {
+                            const uint64_t ac = a_desc + c * chunk16;
+                            uint64_t bs = 0;   // the current stage's descriptor
+#pragma unroll
+                            for (int t = 0; t < 9; ++t) {
+                                if (t % kTps == 0) {
+                                    if (!(ok = mbar_wait(&sm.wfull[rw.idx], rw.phase, p.err, kErrWaitMma))) break;
+                                    tc_fence_after();
+                                    bs = ring_desc + rw.idx * kStage16;
+                                }
+                                const uint64_t at = ac + centre16 + (t / 3 - 1) * int(row16) + (t % 3 - 1) * 8,
+                                               bt = bs + (t % kTps) * kTap16;
+#pragma unroll
+                                for (int kk = 0; kk < C::kSteps; ++kk) {
+                                    if constexpr (kSplit) {
+                                        // Per input chunk its own stacked accumulator:
+                                        // [0, N) a_hi.b_hi, [N, 2N) a_hi.b_lo + a_lo.b_hi.
+                                        const uint32_t d = tmem + uint32_t(c) * 2u * N;
+                                        constexpr uint32_t kIdescStack = umma_idesc(2 * N, kBf16);
+                                        umma<kBf16>(d, at + 2 * kk, bt + 2 * kk, kIdescStack, (t | kk) != 0);
+                                        umma<kBf16>(d + N, at + plane16 + 2 * kk, bt + 2 * kk, umma_idesc(N, kBf16), 1);
+                                    } else {
+                                        umma<kBf16>(tmem, at + 2 * kk, bt + 2 * kk, umma_idesc(N, kBf16),
+                                                    (c | t | kk) != 0);
+                                    }
+                                }
+                                if (t % kTps == kTps - 1) {
+                                    umma_commit(&sm.wempty[rw.idx]);
+                                    rw.next(p.stages);
+                                }
                             }
                         }
                     }
@@ -302,7 +360,7 @@ __global__ void __launch_bounds__(kFusedThreads, kFusedCtas<kSplit>)
             umma_commit(sm.done);
             mbar_wait(sm.done, 0, p.err, kErrWaitDrain);
         }
-    } else {
+    } else if (warp < 2 + kFusedEpiWarps) {
         // ---------------------------------------------------------- epilogue
         const int e = warp - 2, quarter = warp & 3, half = e >> 2;
         const bool active = N >= 64 || half == 0;
@@ -506,7 +564,7 @@ cudaError_t launch_fused_tps(const FusedMaps& m, const FusedArgs& a, size_t smem
     }
     const int groups = (a.boards + a.group - 1) / a.group;
     const int grid = std::max(1, std::min(groups, sms * ctas));
-    return launch_pdl(tower_fused<N, kBf16, kSplit, kTps>, dim3(grid), dim3(kFusedThreads), smem, s, m.in, m.in_lo,
+    return launch_pdl(tower_fused<N, kBf16, kSplit, kTps>, dim3(grid), dim3(kFusedThreads<kSplit>), smem, s, m.in, m.in_lo,
                       m.out, m.out_lo, m.stem, m.stem_lo, a);
 }
 
