@@ -109,6 +109,17 @@ def lib() -> C.CDLL:
             for fn in (L.azb_runner_logits, L.azb_runner_values, L.azb_runner_ownership):
                 fn.argtypes = [C.c_void_p, C.c_int]
                 fn.restype = _F
+            PI = C.POINTER(C.c_int)
+            L.azb_hub_create.argtypes = [D, _F, s, _F, s, PI, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                         C.POINTER(C.c_void_p)] + err
+            L.azb_hub_create_fake.argtypes = [C.c_int] * 9 + [C.POINTER(C.c_void_p)] + err
+            L.azb_hub_destroy.argtypes = [C.c_void_p]
+            L.azb_hub_lanes.argtypes = [C.c_void_p]
+            L.azb_hub_pass_cap.argtypes = [C.c_void_p]
+            L.azb_hub_evaluate.argtypes = [C.c_void_p, C.c_int, _F, C.c_int, _F, _F] + err
+            L.azb_hub_evaluate_records.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, _F, _F] + err
+            L.azb_hub_stats.argtypes = [C.c_void_p, C.c_int, C.POINTER(C.c_longlong), C.POINTER(C.c_longlong),
+                                        C.POINTER(C.c_longlong), C.POINTER(C.c_double)]
             L.azb_workspace_bytes.argtypes = [D, C.c_int, C.c_int]
             L.azb_workspace_bytes.restype = s
             L.azb_check_memory.argtypes = [D, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int] + err
@@ -347,7 +358,7 @@ class CudaInference:
             raise CudaError(e.value.decode())
         return ms.value, (cms.value if conv else None)
 
-    STAGES = ("stem_operand", "stem_gemm", "tower", "head_conv", "head_fc", "head_out")
+    STAGES = ("stem_operand", "stem_gemm", "tower", "head_conv", "head_tail", "unused")
 
     def time_stages(self, B: int, steps: int) -> dict:
         """Device ms per stage, summed over `steps` passes (events around every launch)."""
@@ -474,6 +485,85 @@ class BatchRunner:
             with self._cb_lock:
                 self._callbacks.pop(key, None)
             raise IndexError(f"slot {slot} out of range")
+
+
+# ------------------------------------------------------------------ hub
+
+HUB_PLANES, HUB_RECORDS = 0, 1
+
+
+class Hub:
+    """azb_hub: leaf batching for many worker threads over one runner per GPU
+    (the role of the reference's InferenceHub + WorkerEvaluators for "cuda",
+    include/azgo/inference_hub.hpp:83-150). evaluate() blocks until the
+    worker's positions are back; ctypes releases the GIL meanwhile."""
+
+    def __init__(self, desc: NetDesc, params=None, buffers=None, devices=(0,), max_batch: int = 256,
+                 slots: int = 2, precision: int = TF32, input_mode: int = HUB_PLANES, *, fake: dict | None = None):
+        self.desc = desc
+        h = C.c_void_p()
+        e = _err()
+        if fake is not None:   # the CPU stand-in for the GPU passes (host-logic tests)
+            rc = lib().azb_hub_create_fake(desc.board, desc.history, fake.get("lanes", 1), max_batch, slots,
+                                           fake.get("quantum", 1), input_mode, fake.get("delay_us", 0),
+                                           fake.get("fail_after", 0), C.byref(h), e, 1024)
+        else:
+            self._params = np.ascontiguousarray(params, np.float32)
+            self._buffers = np.ascontiguousarray(buffers, np.float32)
+            devs = (C.c_int * len(devices))(*devices)
+            rc = lib().azb_hub_create(C.byref(desc), _fp(self._params), self._params.size, _fp(self._buffers),
+                                      self._buffers.size, devs, len(devices), max_batch, slots, precision,
+                                      input_mode, C.byref(h), e, 1024)
+        if rc != 0:
+            raise CudaError(e.value.decode())
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().azb_hub_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def lanes(self) -> int:
+        return lib().azb_hub_lanes(self.h)
+
+    def pass_cap(self) -> int:
+        return lib().azb_hub_pass_cap(self.h)
+
+    def evaluate(self, lane: int, x: np.ndarray):
+        """(logits [B][A+1], values [B]) for planes [B][P][A]."""
+        x = np.ascontiguousarray(x, np.float32)
+        B = x.shape[0]
+        logits = np.empty((B, self.desc.actions), np.float32)
+        values = np.empty(B, np.float32)
+        e = _err()
+        if lib().azb_hub_evaluate(self.h, lane, _fp(x), B, _fp(logits), _fp(values), e, 1024) != 0:
+            raise CudaError(e.value.decode())
+        return logits, values
+
+    def evaluate_records(self, lane: int, records: np.ndarray):
+        records = np.ascontiguousarray(records, np.uint8)
+        B = records.shape[0]
+        logits = np.empty((B, self.desc.actions), np.float32)
+        values = np.empty(B, np.float32)
+        e = _err()
+        if lib().azb_hub_evaluate_records(self.h, lane, records.ctypes.data, B, _fp(logits), _fp(values), e,
+                                          1024) != 0:
+            raise CudaError(e.value.decode())
+        return logits, values
+
+    def stats(self, lane: int) -> dict:
+        p, n, f, t = C.c_longlong(), C.c_longlong(), C.c_longlong(), C.c_double()
+        lib().azb_hub_stats(self.h, lane, C.byref(p), C.byref(n), C.byref(f), C.byref(t))
+        return {"passes": p.value, "positions": n.value, "full_passes": f.value, "gpu_seconds": t.value}
 
 
 def make_cuda_runner(desc, params, buffers, max_batch: int, slots: int = 2, device: int = 0,

@@ -594,6 +594,8 @@ size_t tower_flags_for(const NetShape& s, int max_batch) {
     const size_t tiles = (size_t(max_batch) * Frame(s.board).S + 127) / 128;
     return size_t(2 * s.blocks + 1) * tiles + 1;
 }
+// The head tail kernel's counters: one per tile of 16 boards.
+size_t tail_counters_for(int max_batch) { return (size_t(max_batch) + 15) / 16; }
 } // namespace
 
 size_t Workspace::bytes_for(const NetShape& s, int precision, int max_batch) {
@@ -617,7 +619,7 @@ size_t Workspace::bytes_for(const NetShape& s, int precision, int max_batch) {
     c.take(B * size_t(s.value_hidden) * 4);
     c.take(B * stones_record_bytes(s.history, s.board));
     c.take(16);
-    c.take(tower_flags_for(s, max_batch) * 4);
+    c.take((tail_counters_for(max_batch) + tower_flags_for(s, max_batch)) * 4);
     return c.used;
 }
 
@@ -646,8 +648,10 @@ void Workspace::place(const Weights& w, uint8_t* base) {
     hid = reinterpret_cast<float*>(at(c.take(B * size_t(s.value_hidden) * 4)));
     records = at(c.take(B * stones_record_bytes(s.history, s.board)));
     err = reinterpret_cast<int*>(at(c.take(16)));
+    tail_count_n = tail_counters_for(max_batch_);
     tower_flag_count = tower_flags_for(s, max_batch_);
-    tower_flags = reinterpret_cast<unsigned*>(at(c.take(tower_flag_count * 4)));
+    tail_count = reinterpret_cast<unsigned*>(at(c.take((tail_count_n + tower_flag_count) * 4)));
+    tower_flags = tail_count + tail_count_n;
     const uint32_t KC = uint32_t(chunk_channels(precision));
     map_stem = make_tensor_map(stem_in, precision, ks, rows, KC, uint32_t(fr.halo));
     map_stem_lo = precision == kTF32x3 ? make_tensor_map(stem_in_lo, precision, ks, rows, KC, uint32_t(fr.halo)) : map_stem;
@@ -746,8 +750,10 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
     const bool persistent = !fused && sh.blocks > 0 && ws.tower_flags != nullptr &&
                             size_t(2 * sh.blocks + 1) * size_t(pass_tiles) + 1 <= ws.tower_flag_count &&
                             tower_persistent(w.n_out(), precision);
-    st.flags = persistent ? ws.tower_flags : nullptr;
-    st.nflags = persistent ? (2 * sh.blocks + 1) * pass_tiles + 1 : 0;
+    // The counters the pass uses start at zero: the head tail kernel's (16
+    // boards each), then, with the persistent tower, the tower's.
+    st.flags = ws.tail_count;
+    st.nflags = int(ws.tail_count_n) + (persistent ? (2 * sh.blocks + 1) * pass_tiles + 1 : 0);
     mark_begin(kSlotStemPack);
     check(launch_stem_pack(st, precision, s), "stem operand");
     mark_end(kSlotStemPack);
@@ -798,6 +804,7 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
     h.feat_val = int((2 * size_t(sh.area()) + 3) / 4 * 4);
     h.feat_ld = int(feat_floats(sh));
     h.hid = ws.hid;
+    h.tail_count = ws.tail_count;
     h.err = ws.err;
     const int tower_chunks = w.cpad() / chunk_channels(precision);
     int x = 0;
@@ -864,14 +871,15 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
     }
     h.trunk = ws.trunk[x];
     h.trunk_lo = ws.trunk_lo[x];
+    // The heads: the 1x1 convolutions streamed from the trunk, then the FCs
+    // and the value's finish in one launch; the fused tower runs all of it.
     mark_begin(kSlotHeadConv);
-    if (!fused) check(launch_head_conv(h, precision, dev.sms, s), "head convolutions");   // fused: done in the tower
+    if (!fused) check(launch_head_conv(h, precision, dev.sms, s), "head convolutions");
     mark_end(kSlotHeadConv);
     mark_begin(kSlotHeadFc);
-    check(launch_head_fc(h, s), "head FC");
+    if (!fused) check(launch_head_tail(h, s), "head tail");
     mark_end(kSlotHeadFc);
-    mark_begin(kSlotHeadOut);
-    check(launch_head_out(h, s), "head outputs");
+    mark_begin(kSlotHeadOut);   // (the finish runs in the tail launch)
     mark_end(kSlotHeadOut);
 }
 

@@ -145,6 +145,10 @@ public:
     // the tiles of max_batch), then the pass's next-item counter.
     unsigned* tower_flags = nullptr;
     size_t tower_flag_count = 0;
+    // The head tail kernel's counters (one per 16 boards), just before the
+    // tower's: the stem operand kernel zeroes both at a pass's start.
+    unsigned* tail_count = nullptr;
+    size_t tail_count_n = 0;
     CUtensorMap map[3]{}, map_lo[3]{};
     CUtensorMap emap[3]{};        // the frames in the conv epilogue's {32, 32} boxes (split mode: high planes)
     CUtensorMap emap_lo[3]{};     // split mode: the low planes in the same boxes
@@ -172,7 +176,7 @@ struct PassTimer {
 };
 enum TimerSlot : int { kSlotStemPack = 0, kSlotStemGemm, kSlotHeadConv, kSlotHeadFc, kSlotHeadOut, kSlotTower };
 // Stage totals Inference::time reports: these six, in this order.
-constexpr int kTimedStages = 6;   // stem operand, stem GEMM, tower, head conv, head FC, head finish
+constexpr int kTimedStages = 6;   // stem operand, stem GEMM, tower, head conv, head tail, (0: no finish launch)
 
 // Network::forward (src/network.cpp:228-309) on the GPU: stem, the tower's
 // fused convolutions, the fused heads; all on one stream.

@@ -154,4 +154,155 @@ struct HeadLane {
     }
 };
 
+// ------------------------------------------------------------ head FCs
+//
+// The policy FC (2A -> A+1, + bias) and the value FC1 (A -> V, + bias,
+// ReLU) as warp-level dot products, shared by the head tail kernel
+// (stem_heads.cu) and the fused small-board tower (tower_fused.cu). One warp
+// computes kOuts consecutive outputs [o0, o0 + kOuts) for G <= kBoards
+// boards: lane l sums the 16-byte input pieces j = l, l + 32, ... of every
+// (output, board) with fmaf over a piece's four values in order (weights
+// and inputs zero-padded to whole pieces); the 32 lane partials of every sum
+// are then added in one fixed tree, pairs over lane bit 4 first, then bits
+// 3, 2, 1, 0: by halving reduce-scatter steps while a lane holds more than
+// one sum (at the step over bit b a lane keeps the half of its sums that bit
+// selects and adds its partner's copy), by butterfly steps after. The tree
+// does not depend on the sum's (output, board) index nor on kOuts x
+// kBoards, so a board's outputs are the same bits in any tile, slot or kernel.
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+template <int kOuts, int kBoards>
+struct FcWarp {
+    static constexpr int kSums = kOuts * kBoards;
+    static_assert((kSums & (kSums - 1)) == 0 && kSums >= 2 && kSums <= 1024, "a power of two of sums");
+    static constexpr int kLogSums = kSums >= 512 ? 9 : kSums >= 256 ? 8 : kSums >= 128 ? 7 : kSums >= 64 ? 6
+                                  : kSums >= 32 ? 5 : kSums >= 16 ? 4 : kSums >= 8 ? 3 : kSums >= 4 ? 2 : 1;
+    static constexpr int kHeld = kSums >= 32 ? kSums / 32 : 1;   // sums a lane holds at the end
+
+    // acc[k], k = o * kBoards + g: the dot of output o0 + o's weight row
+    // with board g's inputs, x(g, j) the board's input piece j.
+    template <class X>
+    __device__ __forceinline__ static void dot(const float4* W, int n4, int ncols, int o0, int G, X x,
+                                               float (&acc)[kSums], int lane) {
+#pragma unroll
+        for (int k = 0; k < kSums; ++k) acc[k] = 0.0f;
+        for (int j = lane; j < n4; j += 32) {
+            float4 w[kOuts];
+#pragma unroll
+            for (int o = 0; o < kOuts; ++o)
+                w[o] = o0 + o < ncols ? __ldg(W + size_t(o0 + o) * n4 + j) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+            for (int g = 0; g < kBoards; ++g) {
+                if (g >= G) break;
+                const float4 v = x(g, j);
+#pragma unroll
+                for (int o = 0; o < kOuts; ++o) {
+                    float& c = acc[o * kBoards + g];
+                    c = fmaf(w[o].x, v.x, c);
+                    c = fmaf(w[o].y, v.y, c);
+                    c = fmaf(w[o].z, v.z, c);
+                    c = fmaf(w[o].w, v.w, c);
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < 5; ++t) {
+            const int off = 16 >> t;
+            if (t < kLogSums) {
+                const int half = kSums >> (t + 1);
+                const bool upper = (lane & off) != 0;
+#pragma unroll
+                for (int k = 0; k < half; ++k) {
+                    const float send = upper ? acc[k] : acc[k + half];
+                    const float keep = upper ? acc[k + half] : acc[k];
+                    acc[k] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+                }
+            } else {
+                acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], off);
+            }
+        }
+    }
+
+    // The index k of the lane's h-th finished sum, or -1 where another lane
+    // of a butterfly group reports it.
+    __device__ __forceinline__ static int held(int lane, int h) {
+        if constexpr (kSums >= 32) {
+            return lane * kHeld + h;
+        } else {
+            const int shift = 5 - kLogSums;
+            return (lane & ((1 << shift) - 1)) == 0 ? lane >> shift : -1;
+        }
+    }
+};
+
+// One tile's FC outputs: this warp's share of the policy outputs [0, A+1)
+// and the value FC1 outputs [0, V) (kOuts at a time, the quads numbered
+// policy first), for the G boards from b0 whose inputs x(g, j) are the
+// feature rows: the policy features for policy outputs (pieces of 2A
+// values), the value features for value outputs (A values). Writes logits
+// and the ReLU of the hidden layer (hid_at(g) gives a board's hidden row).
+template <int kOuts, int kBoards, class XPol, class XVal, class HidAt>
+__device__ __forceinline__ void head_fc_quads(const HeadArgs& a, int b0, int G, int quad0, int quad_step, XPol xpol,
+                                              XVal xval, HidAt hid_at, int lane) {
+    using Fc = FcWarp<kOuts, kBoards>;
+    const int L = a.A + 1, V = a.V;
+    const int pol_quads = (L + kOuts - 1) / kOuts, quads = pol_quads + (V + kOuts - 1) / kOuts;
+    const int n4p = (2 * a.A + 3) / 4, n4v = (a.A + 3) / 4;
+    for (int q = quad0; q < quads; q += quad_step) {
+        const bool policy = q < pol_quads;
+        const int o0 = (policy ? q : q - pol_quads) * kOuts;
+        float acc[Fc::kSums];
+        if (policy)
+            Fc::dot(reinterpret_cast<const float4*>(a.fc_w), n4p, L, o0, G, xpol, acc, lane);
+        else
+            Fc::dot(reinterpret_cast<const float4*>(a.v1_w), n4v, V, o0, G, xval, acc, lane);
+#pragma unroll
+        for (int h = 0; h < Fc::kHeld; ++h) {
+            const int k = Fc::held(lane, h);
+            if (k < 0) continue;
+            const int o = o0 + k / kBoards, g = k % kBoards;
+            if (g >= G || o >= (policy ? L : V)) continue;
+            if (policy) {
+                a.logits[size_t(b0 + g) * L + o] = __fadd_rn(acc[h], __ldg(a.fc_b + o));
+            } else {
+                const float y = __fadd_rn(acc[h], __ldg(a.v1_b + o));
+                hid_at(g)[o] = y > 0.0f ? y : 0.0f;
+            }
+        }
+    }
+}
+
+// One warp finishes board b: value = tanh(v2 . hid + b2) and, when asked
+// for, the softmax over the A+1 logits. hid and logits may have been written
+// by other CTAs: read through L2.
+__device__ __forceinline__ void head_finish_board(const HeadArgs& a, int b, const float* hid, int lane) {
+    const int L = a.A + 1, V = a.V;
+    float acc = 0.0f;
+    for (int i = lane; i < V; i += 32) acc = fmaf(__ldg(a.v2_w + i), __ldcg(hid + i), acc);
+    acc = warp_sum(acc);
+    if (lane == 0) a.values[b] = tanhf(__fadd_rn(acc, __ldg(a.v2_b)));
+    if (a.probs) {
+        const float* lg = a.logits + size_t(b) * L;
+        float m = -INFINITY;
+        for (int o = lane; o < L; o += 32) m = fmaxf(m, __ldcg(lg + o));
+        m = warp_max(m);
+        float s = 0.0f;
+        for (int o = lane; o < L; o += 32) s += expf(__ldcg(lg + o) - m);
+        s = warp_sum(s);
+        const float inv = 1.0f / s;
+        for (int o = lane; o < L; o += 32) a.probs[size_t(b) * L + o] = expf(__ldcg(lg + o) - m) * inv;
+    }
+}
+
 } // namespace azb

@@ -167,7 +167,7 @@ struct StemArgs {
     const float* in;    // [B][P][A]
     int B, P, n, S, ld;
     void* out; void* out_lo;
-    unsigned* flags;    // the persistent tower's counters, zeroed here (null: none)
+    unsigned* flags;    // the pass's counters (the head tail's, then the persistent tower's), zeroed here
     int nflags;
 };
 cudaError_t launch_stem_pack(const StemArgs& a, int precision, cudaStream_t s);
@@ -210,6 +210,7 @@ struct HeadArgs {
                         // then value features from feat_val, zeros to a multiple of 4
     int feat_ld, feat_val;
     float* hid;         // scratch [B][V]: value FC1 after ReLU
+    unsigned* tail_count;   // per 16-board tile: the head tail kernel's finished CTAs (zero at a pass's start)
     int* err;           // kernel error word (a bounded wait that ran out)
 };
 cudaError_t launch_head_conv(const HeadArgs& a, int precision, int sms, cudaStream_t s);   // 1x1 convs -> feat
@@ -258,8 +259,8 @@ size_t fused_tower_smem(int n_out, int precision, int nch, int act_bytes, int la
 cudaError_t launch_fused_tower(const FusedMaps& maps, const FusedArgs& a, int n_out, int precision, int sms,
                                cudaStream_t s);
 
-cudaError_t launch_head_fc(const HeadArgs& a, cudaStream_t s);                            // feat -> logits, hid
-cudaError_t launch_head_out(const HeadArgs& a, cudaStream_t s);                           // hid -> value; softmax
+// feat -> logits, hid -> values (and probs): the FCs and the value's finish in one launch.
+cudaError_t launch_head_tail(const HeadArgs& a, cudaStream_t s);
 
 // Test hooks and context checks.
 cudaError_t launch_fill(float* data, size_t n, float value, cudaStream_t s);

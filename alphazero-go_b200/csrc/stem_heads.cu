@@ -152,35 +152,23 @@ __global__ void __launch_bounds__(256) encode_planes_kernel(const EncodeArgs a) 
 
 // --------------------------------------------------------------- the heads
 //
-// Three launches, each at its own roofline:
+// Two launches (the small-board fused tower runs all of it in its own):
 //  1. head_conv_kernel streams the trunk once through shared memory
 //     (bulk copies; HBM-bound): the policy (2),
 //     value (1) and ownership (1) 1x1 convolutions of every board point,
 //     their batch norms and ReLU (ownership: tanh, straight to its output);
 //     features land in a small [B][3A] buffer, the policy part in the
 //     reference's flatten order c*A + p (src/network.cpp:278-285).
-//  2. head_fc_kernel: the policy FC (2A -> A+1, + bias) and value FC1
+//  2. head_tail_kernel: the policy FC (2A -> A+1, + bias) and value FC1
 //     (A -> V, + bias, ReLU) for tiles of 16 boards x 32 outputs, each FC
-//     weight read once per tile, the tile's inputs in shared memory.
-//  3. head_out_kernel: one warp per board, the value FC2 and tanh, and the
-//     softmax over the A+1 logits.
+//     weight read once per tile, the tile's inputs in shared memory; the
+//     last CTA of a board tile then runs the value FC2 and tanh, and the
+//     softmax over the A+1 logits, a warp per board.
 // Every output is a fixed-order sum over its own board's data: the results
 // do not depend on the batch or on where a board sits in it.
 
 constexpr int kHeadThreads = 256;
 constexpr int kFcBoards = 16;    // boards per FC tile: each weight is read once per 16 boards
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
 
 // The trunk streamed once through shared memory. A copy thread (warp 8)
 // stages `kbr` board rows at a time into a ring of `stages` buffers: the n
@@ -286,26 +274,27 @@ __global__ void __launch_bounds__(kHcThreads, 1)
     }
 }
 
-// A tile of kFcBoards (16) boards x 32 outputs of the policy FC (tiles
-// 0 .. ceil((A+1)/32) - 1 of gridDim.y) or of the value FC1 (the rest); the
-// tile's inputs, [16][n rounded up to 4], sit in shared memory. Each warp
-// takes kFcOuts (4) outputs for the 16 boards: lane l sums inputs
-// 4l .. 4l+3, 4l+128 .. in order (16-byte loads of the padded weight rows
-// and of the inputs, the inputs reused across the 4 outputs in registers),
-// then a reduce-scatter over the lanes (62 shuffles for 64 sums) leaves lane
-// l the totals k = 2l, 2l+1 (k = output*16 + board). Every total is the same
-// tree of additions over the same lanes, whatever its k: a board's outputs
-// do not depend on its slot in the tile.
+// The heads after their 1x1 convolutions, in one launch: a CTA takes a tile
+// of kFcBoards (16) boards x 32 outputs of the policy FC (output tiles 0 ..
+// ceil((A+1)/32) - 1 of gridDim.y) or of the value FC1 (the rest), with the
+// tile's inputs, [16][n rounded up to 4], in shared memory; each warp takes
+// kFcOuts (4) outputs for the 16 boards (head_fc_quads: every weight read
+// once per 16 boards). The last CTA of a board tile to finish (a counter per
+// board tile, zeroed by the pass's stem operand kernel) then runs the value
+// FC2 + tanh and, when asked for, the softmax over A+1 for the tile's boards,
+// a warp per board, reading the other CTAs' hidden layers and logits through
+// L2. One launch instead of an FC launch and a finishing launch.
 constexpr int kFcOuts = 4;
-__global__ void __launch_bounds__(kHeadThreads) head_fc_kernel(const HeadArgs a) {
+__global__ void __launch_bounds__(kHeadThreads) head_tail_kernel(const HeadArgs a) {
     extern __shared__ float4 xs[];
+    __shared__ unsigned last_cta;
     grid_dependency_wait();
     grid_launch_dependents();
     const int A = a.A, L = A + 1, V = a.V;
-    const int outs_per_cta = (kHeadThreads / 32) * kFcOuts;
+    constexpr int kWarps = kHeadThreads / 32, outs_per_cta = kWarps * kFcOuts;
     const int pol_tiles = (L + outs_per_cta - 1) / outs_per_cta;
     const bool policy = int(blockIdx.y) < pol_tiles;
-    const int n_in = policy ? 2 * A : A, n4 = (n_in + 3) / 4, ncols = policy ? L : V;
+    const int n_in = policy ? 2 * A : A, n4 = (n_in + 3) / 4;
     const int foff = policy ? 0 : a.feat_val;   // multiples of 4 floats, as is feat_ld
     const int b0 = blockIdx.x * kFcBoards, G = min(kFcBoards, a.B - b0);
     const float4* feat4 = reinterpret_cast<const float4*>(a.feat);
@@ -315,77 +304,26 @@ __global__ void __launch_bounds__(kHeadThreads) head_fc_kernel(const HeadArgs a)
     }
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int o0 = (policy ? int(blockIdx.y) : int(blockIdx.y) - pol_tiles) * outs_per_cta + warp * kFcOuts;
-    if (o0 >= ncols) return;
-    const float4* W = reinterpret_cast<const float4*>(policy ? a.fc_w : a.v1_w);
-    float acc[kFcOuts * kFcBoards];
-#pragma unroll
-    for (int k = 0; k < kFcOuts * kFcBoards; ++k) acc[k] = 0.0f;
-    for (int j = lane; j < n4; j += 32) {
-        float4 w[kFcOuts];
-#pragma unroll
-        for (int o = 0; o < kFcOuts; ++o)
-            w[o] = o0 + o < ncols ? __ldg(W + size_t(o0 + o) * n4 + j) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-        for (int g = 0; g < kFcBoards; ++g) {
-            const float4 x = xs[g * n4 + j];
-#pragma unroll
-            for (int o = 0; o < kFcOuts; ++o) {
-                float& c = acc[o * kFcBoards + g];
-                c = fmaf(w[o].x, x.x, c);
-                c = fmaf(w[o].y, x.y, c);
-                c = fmaf(w[o].z, x.z, c);
-                c = fmaf(w[o].w, x.w, c);
-            }
-        }
+    // This CTA's quads: the policy quads of its policy tile, or the value
+    // quads of its value tile (quads are numbered policy first).
+    const int pol_quads = (L + kFcOuts - 1) / kFcOuts;
+    const int tile_quad0 = policy ? int(blockIdx.y) * outs_per_cta / kFcOuts
+                                  : pol_quads + (int(blockIdx.y) - pol_tiles) * outs_per_cta / kFcOuts;
+    const int tile_quads = policy ? min(kWarps, pol_quads - tile_quad0)
+                                  : min(kWarps, pol_quads + (V + kFcOuts - 1) / kFcOuts - tile_quad0);
+    if (warp < tile_quads) {
+        auto x = [&](int g, int j) { return xs[g * n4 + j]; };
+        head_fc_quads<kFcOuts, kFcBoards>(a, b0, G, tile_quad0 + warp, 1 << 30, x, x,
+                                          [&](int g) { return a.hid + size_t(b0 + g) * V; }, lane);
     }
-    // Reduce-scatter: at the step over lane bit b (offset 2^b), a lane keeps
-    // the half of its sums that bit selects and adds its partner's copy.
-#pragma unroll
-    for (int half = kFcOuts * kFcBoards / 2, off = 16; off >= 1; half >>= 1, off >>= 1) {
-        const bool upper = (lane & off) != 0;
-#pragma unroll
-        for (int k = 0; k < half; ++k) {
-            const float send = upper ? acc[k] : acc[k + half];
-            const float keep = upper ? acc[k + half] : acc[k];
-            acc[k] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-        }
-    }
-    const float* bias = policy ? a.fc_b : a.v1_b;
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        const int k = 2 * lane + j, o = o0 + k / kFcBoards, g = k % kFcBoards;
-        if (o >= ncols || g >= G) continue;
-        const float y = __fadd_rn(acc[j], __ldg(bias + o));
-        if (policy) a.logits[size_t(b0 + g) * L + o] = y;
-        else a.hid[size_t(b0 + g) * V + o] = y > 0.0f ? y : 0.0f;
-    }
-}
-
-// One warp per board: value = tanh(v2 . hid + b2), and the softmax over the
-// A+1 logits when asked for.
-__global__ void __launch_bounds__(kHeadThreads) head_out_kernel(const HeadArgs a) {
-    grid_dependency_wait();
-    grid_launch_dependents();
-    const int lane = threadIdx.x & 31, L = a.A + 1, V = a.V;
-    const int b = blockIdx.x * (kHeadThreads / 32) + (threadIdx.x >> 5);
-    if (b >= a.B) return;
-    const float* hid = a.hid + size_t(b) * V;
-    float acc = 0.0f;
-    for (int i = lane; i < V; i += 32) acc = fmaf(__ldg(a.v2_w + i), hid[i], acc);
-    acc = warp_sum(acc);
-    if (lane == 0) a.values[b] = tanhf(__fadd_rn(acc, __ldg(a.v2_b)));
-    if (a.probs) {
-        const float* lg = a.logits + size_t(b) * L;
-        float m = -INFINITY;
-        for (int o = lane; o < L; o += 32) m = fmaxf(m, lg[o]);
-        m = warp_max(m);
-        float s = 0.0f;
-        for (int o = lane; o < L; o += 32) s += expf(lg[o] - m);
-        s = warp_sum(s);
-        const float inv = 1.0f / s;
-        for (int o = lane; o < L; o += 32) a.probs[size_t(b) * L + o] = expf(lg[o] - m) * inv;
-    }
+    // The board tile's last CTA finishes it.
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last_cta = atomicAdd(a.tail_count + blockIdx.x, 1u) + 1u == gridDim.y;
+    __syncthreads();
+    if (!last_cta) return;
+    __threadfence();
+    for (int g = warp; g < G; g += kWarps) head_finish_board(a, b0 + g, a.hid + size_t(b0 + g) * V, lane);
 }
 
 // ------------------------------------------------------------ small kernels
@@ -499,22 +437,17 @@ cudaError_t launch_head_conv(const HeadArgs& a, int precision, int sms, cudaStre
     }
 }
 
-cudaError_t launch_head_fc(const HeadArgs& a, cudaStream_t s) {
+cudaError_t launch_head_tail(const HeadArgs& a, cudaStream_t s) {
     if (a.B <= 0) return cudaSuccess;
+    if (a.tail_count == nullptr) return cudaErrorInvalidValue;
     const int L = a.A + 1, outs = (kHeadThreads / 32) * kFcOuts;
     const dim3 grid((a.B + kFcBoards - 1) / kFcBoards, (L + outs - 1) / outs + (a.V + outs - 1) / outs);
     const size_t smem = size_t((2 * a.A + 3) / 4) * 4 * kFcBoards * sizeof(float);
     if (smem > 48 * 1024) {
-        const cudaError_t e = cudaFuncSetAttribute(head_fc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        const cudaError_t e = cudaFuncSetAttribute(head_tail_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
         if (e != cudaSuccess) return e;
     }
-    return launch_pdl(head_fc_kernel, grid, dim3(kHeadThreads), smem, s, a);
-}
-
-cudaError_t launch_head_out(const HeadArgs& a, cudaStream_t s) {
-    if (a.B <= 0) return cudaSuccess;
-    return launch_pdl(head_out_kernel, dim3((a.B + kHeadThreads / 32 - 1) / (kHeadThreads / 32)), dim3(kHeadThreads), 0,
-                      s, a);
+    return launch_pdl(head_tail_kernel, grid, dim3(kHeadThreads), smem, s, a);
 }
 
 cudaError_t launch_fill(float* data, size_t n, float value, cudaStream_t s) {

@@ -43,6 +43,12 @@ namespace azb {
 namespace {
 
 constexpr int kFusedEpiWarps = 8;
+constexpr int kFusedFcBoards = 4;   // boards per group at most (5x5: three frames per 128-row tile)
+
+// A barrier of the eight epilogue warps (warps 2-9) alone.
+__device__ __forceinline__ void epilogue_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * kFusedEpiWarps) : "memory");
+}
 // Threads per CTA: the loader, the MMA issuer and eight epilogue warps; the
 // split mode adds the second issuer's warp (warp 10).
 template <bool kSplit>
@@ -528,6 +534,22 @@ __global__ void __launch_bounds__(kFusedThreads<kSplit>, kFusedCtas<kSplit>)
                     hl.step(p.head, base, pts, piece, where, lane);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(sm.out_done);   // x may be overwritten by the next group's input
+                // The rest of the heads for the group's boards, from the
+                // features the epilogue warps just wrote (global memory: the
+                // named barrier makes them visible across the warps): the
+                // policy FC and value FC1 (the head tail kernel's lane split
+                // and tree, the same bits), then a warp per board finishes
+                // the value (FC2, tanh) and, when asked for, the softmax.
+                epilogue_sync();
+                const float4* feat4 = reinterpret_cast<const float4*>(p.head.feat);
+                const size_t ld4 = size_t(p.head.feat_ld) / 4, val4 = size_t(p.head.feat_val) / 4;
+                auto xpol = [=](int gb, int j) { return feat4[size_t(first_board + gb) * ld4 + j]; };
+                auto xval = [=](int gb, int j) { return feat4[size_t(first_board + gb) * ld4 + val4 + j]; };
+                auto hid_at = [&](int gb) { return p.head.hid + size_t(first_board + gb) * p.head.V; };
+                head_fc_quads<4, kFusedFcBoards>(p.head, first_board, boards, e, kFusedEpiWarps, xpol, xval, hid_at,
+                                                 lane);
+                epilogue_sync();
+                for (int gb = e; gb < boards; gb += kFusedEpiWarps) head_finish_board(p.head, first_board + gb, hid_at(gb), lane);
             } else if (e == 0 && lane == 0) {
                 // The tower's output (x) leaves once every epilogue warp has
                 // written the last layer.

@@ -34,4 +34,30 @@ azb_net_desc describe(const azgo::NetConfig& c);
 std::unique_ptr<azgo::BatchRunner> makeCudaRunnerOn(const azgo::Network& net, int maxBatch, int slots, int device,
                                                     int precision = -1);
 
+// One evaluator per worker over an azb_hub with a lane per device: the
+// counterpart of the reference's WorkerEvaluators(net, "cuda", ...)
+// (include/azgo/inference_hub.hpp:151-176) for one or more GPUs in one
+// process. Worker w evaluates on lane w % devices.size(), so a slice's
+// games are split across the GPUs. records: the hub carries stone records
+// (the planes are encoded on the GPU).
+class HubEvaluators {
+public:
+    HubEvaluators(const azgo::Network& net, const std::vector<int>& devices, int workers, int maxRequest,
+                  int inferenceBatch, int slots, int precision, bool records);
+    ~HubEvaluators();
+    HubEvaluators(const HubEvaluators&) = delete;
+    HubEvaluators& operator=(const HubEvaluators&) = delete;
+    azgo::Evaluator& forWorker(int worker);
+    int workers() const { return static_cast<int>(evaluators_.size()); }
+    long long evaluations() const;     // positions evaluated, all lanes
+    long long passes() const;          // passes run, all lanes
+    long long fullPasses() const;      // passes of exactly passCap() positions
+    int passCap() const;
+    int lanes() const;
+
+private:
+    azb_hub* hub_ = nullptr;
+    std::vector<std::unique_ptr<azgo::Evaluator>> evaluators_;
+};
+
 } // namespace azb_host

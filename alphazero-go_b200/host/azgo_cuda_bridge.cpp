@@ -148,6 +148,78 @@ std::unique_ptr<azgo::BatchRunner> makeCudaRunnerOn(const azgo::Network& net, in
     return std::make_unique<Runner>(net, maxBatch, slots, device, precision < 0 ? defaultPrecision() : precision);
 }
 
+namespace {
+
+// The reference's Evaluator (include/azgo/evaluator.hpp) over a hub lane.
+class HubEvaluator : public azgo::Evaluator {
+public:
+    HubEvaluator(azb_hub* hub, int lane, const azgo::NetConfig& cfg, int maxRequest)
+        : hub_(hub), lane_(lane), n_(cfg.boardSize), history_(cfg.history), max_request_(maxRequest) {}
+    int boardSize() const override { return n_; }
+    int history() const override { return history_; }
+    int maxBatch() const override { return max_request_; }
+    void evaluate(const float* input, int B, float* logits, float* values) override {
+        char err[1024] = {};
+        if (azb_hub_evaluate(hub_, lane_, input, B, logits, values, err, sizeof err) != 0) {
+            const std::string msg(err);
+            if (msg.rfind("GPU inference failed", 0) == 0) throw std::runtime_error(msg);
+            throw std::invalid_argument(msg);
+        }
+    }
+
+private:
+    azb_hub* hub_;
+    int lane_, n_, history_, max_request_;
+};
+
+} // namespace
+
+HubEvaluators::HubEvaluators(const azgo::Network& net, const std::vector<int>& devices, int workers, int maxRequest,
+                             int inferenceBatch, int slots, int precision, bool records) {
+    if (workers < 1) throw std::invalid_argument("HubEvaluators: workers must be >= 1");
+    if (devices.empty()) throw std::invalid_argument("HubEvaluators: no devices");
+    const azb_net_desc d = describe(net.config());
+    const Arenas a = arenas(net);
+    char err[1024] = {};
+    if (azb_hub_create(&d, a.params.data(), a.params.size(), a.buffers.data(), a.buffers.size(), devices.data(),
+                       static_cast<int>(devices.size()), inferenceBatch, slots,
+                       precision < 0 ? defaultPrecision() : precision, records ? AZB_HUB_RECORDS : AZB_HUB_PLANES,
+                       &hub_, err, sizeof err) != 0)
+        throw std::runtime_error(err);
+    if (maxRequest < 1 || maxRequest > azb_hub_pass_cap(hub_)) {
+        azb_hub_destroy(hub_);
+        throw std::invalid_argument("HubEvaluators: maxRequest must be in [1, " + std::to_string(inferenceBatch) + "]");
+    }
+    for (int w = 0; w < workers; ++w)
+        evaluators_.push_back(std::make_unique<HubEvaluator>(hub_, w % static_cast<int>(devices.size()),
+                                                             net.config(), maxRequest));
+}
+
+HubEvaluators::~HubEvaluators() {
+    evaluators_.clear();
+    azb_hub_destroy(hub_);   // waits for passes in flight
+}
+
+azgo::Evaluator& HubEvaluators::forWorker(int worker) { return *evaluators_.at(static_cast<size_t>(worker)); }
+
+namespace {
+long long lane_sum(azb_hub* hub, int which) {
+    long long total = 0;
+    for (int l = 0; l < azb_hub_lanes(hub); ++l) {
+        long long passes = 0, positions = 0, full = 0;
+        azb_hub_stats(hub, l, &passes, &positions, &full, nullptr);
+        total += which == 0 ? positions : which == 1 ? passes : full;
+    }
+    return total;
+}
+} // namespace
+
+long long HubEvaluators::evaluations() const { return lane_sum(hub_, 0); }
+long long HubEvaluators::passes() const { return lane_sum(hub_, 1); }
+long long HubEvaluators::fullPasses() const { return lane_sum(hub_, 2); }
+int HubEvaluators::passCap() const { return azb_hub_pass_cap(hub_); }
+int HubEvaluators::lanes() const { return azb_hub_lanes(hub_); }
+
 } // namespace azb_host
 
 namespace azgo {

@@ -145,6 +145,72 @@ NetConfig make_config(int board, int history, int blocks, int filters, int value
 // calls it, and selfplay_slice.cpp (which defines it) is not linked here.
 void azgo::setThreadQos(CpuQos) {}
 
+namespace {
+
+struct SliceOutcome {
+    double seconds = 0;
+    long long positions = 0;
+    uint64_t hash = 0;
+};
+
+// Games [first, first + count) of `generation` on `nw` worker threads, each
+// with evaluators.forWorker(w): playSelfPlayGame with the game's own seed,
+// the records hashed in index order.
+template <class Evaluators>
+SliceOutcome play_slice(Evaluators& evaluators, int nw, const SelfPlayConfig& sp, uint64_t seed, int generation,
+                       int first, int count, std::chrono::steady_clock::time_point start) {
+    std::vector<GameRecord> records(static_cast<size_t>(std::max(0, count)));
+    std::atomic<int> next{0};
+    std::atomic<bool> stop{false};
+    std::atomic<long long> pos{0};
+    std::mutex error_mutex;
+    std::exception_ptr first_error;
+    auto work = [&](int w) {
+        try {
+            CountingEvaluator ev(evaluators.forWorker(w));
+            while (!stop) {
+                const int k = next++;
+                if (k >= count) break;
+                const int i = first + k;
+                Rng rng(deriveSeed(seed, static_cast<uint64_t>(generation), kPhaseSelfPlay, static_cast<uint64_t>(i)));
+                GameRecord record = playSelfPlayGame(ev, sp, rng);
+                pos += record.positions();
+                records[static_cast<size_t>(k)] = std::move(record);
+            }
+        } catch (...) {
+            std::lock_guard<std::mutex> lock(error_mutex);
+            if (!first_error) first_error = std::current_exception();
+            stop = true;
+        }
+    };
+    std::vector<std::thread> threads;
+    for (int w = 0; w < nw; ++w) threads.emplace_back(work, w);
+    for (std::thread& t : threads) t.join();
+    if (first_error) std::rethrow_exception(first_error);
+    SliceOutcome r;
+    r.seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - start).count();
+    r.positions = pos;
+    Fnv f;
+    for (const GameRecord& g : records) hash_record(f, g);
+    r.hash = f.h;
+    return r;
+}
+
+SelfPlayConfig selfplay_config(int simulations, int mcts_batch, float c_puct, int temperature_moves, float komi,
+                               int max_moves) {
+    SelfPlayConfig sp;
+    sp.mcts.simulations = simulations;
+    sp.mcts.batchSize = mcts_batch;
+    sp.mcts.cPuct = c_puct;
+    sp.temperatureMoves = temperature_moves;
+    sp.komi = komi;
+    sp.maxMoves = max_moves;
+    sp.resignation = false;
+    return sp;
+}
+
+} // namespace
+
 extern "C" {
 
 // Plays games [first, first + count) of `generation` and reports the slice's
@@ -164,59 +230,57 @@ int azsp_play(int board, int history, int blocks, int filters, int value_hidden,
 #endif
         Network net(make_config(board, history, blocks, filters, value_hidden), 0);
         load_arenas(net, params, n_params, buffers, n_buffers);
-
-        SelfPlayConfig sp;
-        sp.mcts.simulations = simulations;
-        sp.mcts.batchSize = mcts_batch;
-        sp.mcts.cPuct = c_puct;
-        sp.temperatureMoves = temperature_moves;
-        sp.komi = komi;
-        sp.maxMoves = max_moves;
-        sp.resignation = false;
-
+        const SelfPlayConfig sp = selfplay_config(simulations, mcts_batch, c_puct, temperature_moves, komi, max_moves);
         const auto start = std::chrono::steady_clock::now();
         const int nw = std::max(1, std::min(workers, count));
-        std::vector<GameRecord> records(static_cast<size_t>(std::max(0, count)));
         WorkerEvaluators evaluators(net, backend, nw, mcts_batch, inference_batch);
-        std::atomic<int> next{0};
-        std::atomic<bool> stop{false};
-        std::atomic<long long> pos{0};
-        std::mutex error_mutex;
-        std::exception_ptr first_error;
-        auto work = [&](int w) {
-            try {
-                CountingEvaluator ev(evaluators.forWorker(w));
-                while (!stop) {
-                    const int k = next++;
-                    if (k >= count) break;
-                    const int i = first + k;
-                    Rng rng(deriveSeed(seed, static_cast<uint64_t>(generation), kPhaseSelfPlay, static_cast<uint64_t>(i)));
-                    GameRecord record = playSelfPlayGame(ev, sp, rng);
-                    pos += record.positions();
-                    records[static_cast<size_t>(k)] = std::move(record);
-                }
-            } catch (...) {
-                std::lock_guard<std::mutex> lock(error_mutex);
-                if (!first_error) first_error = std::current_exception();
-                stop = true;
-            }
-        };
-        std::vector<std::thread> threads;
-        for (int w = 0; w < nw; ++w) threads.emplace_back(work, w);
-        for (std::thread& t : threads) t.join();
-        if (first_error) std::rethrow_exception(first_error);
-        if (seconds) *seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - start).count();
-        if (positions) *positions = pos;
+        const SliceOutcome r = play_slice(evaluators, nw, sp, seed, generation, first, count, start);
+        if (seconds) *seconds = r.seconds;
+        if (positions) *positions = r.positions;
         if (evaluations) *evaluations = evaluators.evaluations();
-        Fnv f;
-        for (const GameRecord& g : records) hash_record(f, g);
-        if (record_hash) *record_hash = f.h;
+        if (record_hash) *record_hash = r.hash;
         return 0;
     } catch (const std::exception& e) {
         put(err, cap, e.what());
         return -1;
     }
 }
+
+#ifdef AZSP_WITH_ENGINE
+// The same slice on the engine's own hub (azb_hub) with a lane per device
+// in `devices` (worker w on lane w % n_devices) instead of the reference's
+// InferenceHub: records != 0 carries stone records to the GPU. Also reports
+// the hub's passes, those of exactly its pass cap, and the cap.
+int azsp_play_hub(int board, int history, int blocks, int filters, int value_hidden, const float* params,
+                  size_t n_params, const float* buffers, size_t n_buffers, const int* devices, int n_devices,
+                  int records, int workers, int inference_batch, int precision, int simulations, int mcts_batch,
+                  float c_puct, int temperature_moves, float komi, int max_moves, uint64_t seed, int generation,
+                  int first, int count, double* seconds, long long* positions, long long* evaluations,
+                  uint64_t* record_hash, long long* passes, long long* full_passes, int* pass_cap, char* err,
+                  size_t cap) {
+    try {
+        Network net(make_config(board, history, blocks, filters, value_hidden), 0);
+        load_arenas(net, params, n_params, buffers, n_buffers);
+        const SelfPlayConfig sp = selfplay_config(simulations, mcts_batch, c_puct, temperature_moves, komi, max_moves);
+        const auto start = std::chrono::steady_clock::now();
+        const int nw = std::max(1, std::min(workers, count));
+        azb_host::HubEvaluators evaluators(net, std::vector<int>(devices, devices + n_devices), nw, mcts_batch,
+                                           inference_batch, 2, precision, records != 0);
+        const SliceOutcome r = play_slice(evaluators, nw, sp, seed, generation, first, count, start);
+        if (seconds) *seconds = r.seconds;
+        if (positions) *positions = r.positions;
+        if (evaluations) *evaluations = evaluators.evaluations();
+        if (record_hash) *record_hash = r.hash;
+        if (passes) *passes = evaluators.passes();
+        if (full_passes) *full_passes = evaluators.fullPasses();
+        if (pass_cap) *pass_cap = evaluators.passCap();
+        return 0;
+    } catch (const std::exception& e) {
+        put(err, cap, e.what());
+        return -1;
+    }
+}
+#endif
 
 // An arena wave: matches m = 0 .. n_matches-1 between network a_net[m] and
 // network b_net[m] (or, when b_net[m] < 0, a uniform bot searching

@@ -39,6 +39,12 @@ def _lib(path: str) -> C.CDLL:
                                  [C.c_char_p] + [C.c_int] * 4 + [C.POINTER(C.c_double), C.POINTER(C.c_longlong),
                                                                  PU, PU, C.c_char_p, C.c_size_t])
         L.azsp_arena.restype = C.c_int
+        if hasattr(L, "azsp_play_hub"):
+            PL, PD = C.POINTER(C.c_longlong), C.POINTER(C.c_double)
+            L.azsp_play_hub.argtypes = ([C.c_int] * 5 + [F, C.c_size_t, F, C.c_size_t, PI] + [C.c_int] * 6 +
+                                        [C.c_float, C.c_int, C.c_float, C.c_int, C.c_uint64, C.c_int, C.c_int,
+                                         C.c_int, PD, PL, PL, PU, PL, PL, PI, C.c_char_p, C.c_size_t])
+            L.azsp_play_hub.restype = C.c_int
         _libs[path] = L
     return _libs[path]
 
@@ -70,6 +76,36 @@ def play(desc, params: np.ndarray, buffers: np.ndarray, *, backend: str = "cuda"
     return {"seconds": s, "positions": pos.value, "evaluations": evals.value, "record_hash": h.value,
             "playouts_per_s": pos.value * simulations / s if s > 0 else 0.0,
             "evaluations_per_s": evals.value / s if s > 0 else 0.0}
+
+
+def play_hub(desc, params: np.ndarray, buffers: np.ndarray, *, devices=(0,), records: bool = False,
+             workers: int = 512, inference_batch: int = 256, precision: int = 2, simulations: int = 200,
+             mcts_batch: int = 8, c_puct: float = 1.5, temperature_moves: int = 7, komi: float = 7.5,
+             max_moves: int = 0, seed: int = 1, generation: int = 0, first: int = 0, count: int = 512,
+             lib_path: str | None = None) -> dict:
+    """play() on the engine's own hub (azb_hub): a lane per device in
+    `devices`, worker w on lane w % len(devices); records=True carries stone
+    records to the GPU. Adds the hub's passes, its full passes and its cap."""
+    L = _lib(lib_path or LIB_PATH)
+    p = np.ascontiguousarray(params, np.float32)
+    b = np.ascontiguousarray(buffers, np.float32)
+    F = C.POINTER(C.c_float)
+    devs = (C.c_int * len(devices))(*devices)
+    secs, pos, evals, h = C.c_double(), C.c_longlong(), C.c_longlong(), C.c_uint64()
+    passes, full, cap = C.c_longlong(), C.c_longlong(), C.c_int()
+    err = C.create_string_buffer(1024)
+    rc = L.azsp_play_hub(desc.board, desc.history, desc.blocks, desc.filters, desc.value_hidden,
+                         p.ctypes.data_as(F), p.size, b.ctypes.data_as(F), b.size, devs, len(devices), int(records),
+                         workers, inference_batch, precision, simulations, mcts_batch, c_puct, temperature_moves,
+                         komi, max_moves, seed, generation, first, count, C.byref(secs), C.byref(pos),
+                         C.byref(evals), C.byref(h), C.byref(passes), C.byref(full), C.byref(cap), err, 1024)
+    if rc != 0:
+        raise RuntimeError(err.value.decode())
+    s = secs.value
+    return {"seconds": s, "positions": pos.value, "evaluations": evals.value, "record_hash": h.value,
+            "playouts_per_s": pos.value * simulations / s if s > 0 else 0.0,
+            "evaluations_per_s": evals.value / s if s > 0 else 0.0,
+            "passes": passes.value, "full_passes": full.value, "pass_cap": cap.value}
 
 
 def arena(desc, nets: list, matches: list, *, first: int = 0, count: int | None = None, simulations: int = 100,

@@ -164,7 +164,9 @@ int azb_infer_run_stones(azb_infer* h, const uint8_t* records, int B, float* log
                          char* err, size_t err_cap);
 /* Per-stage device time of `steps` passes (CUDA events around every launch,
  * summed over the passes): stage_ms[0..5] = stem operand, stem GEMM, tower
- * convs, head 1x1 convs, head FCs, head finish (value tanh, softmax).
+ * convs, head 1x1 convs, head tail (FCs, value tanh, softmax: one launch),
+ * and 0 (the finish has no launch of its own). Small boards run the stem GEMM
+ * and every head stage inside the tower launch.
  * Measurement only; no reference counterpart. */
 int azb_infer_time_stages(azb_infer* h, int B, int steps, double* stage_ms, char* err, size_t err_cap);
 /* Read back the device outputs of the last enqueued pass. */
@@ -208,6 +210,50 @@ int azb_runner_begin_stones(azb_runner* r, int slot, int B, azb_done_fn done, vo
 const float* azb_runner_logits(const azb_runner* r, int slot);
 const float* azb_runner_values(const azb_runner* r, int slot);
 const float* azb_runner_ownership(const azb_runner* r, int slot);
+
+/* ------------------------------------------------------------------ hub */
+
+/* Leaf batching for many search threads over one runner per GPU, in one
+ * process: the role of the reference's InferenceHub + WorkerEvaluators for
+ * the "cuda" backend (include/azgo/inference_hub.hpp:83-150,
+ * src/inference_hub.cpp:95-295), with one lane (runner) per device, so one
+ * process drives several GPUs (the reference pins device 0,
+ * src/cuda/cuda_context.cu:51). Each worker thread is bound to a lane and
+ * calls azb_hub_evaluate, which blocks until its positions are evaluated.
+ * Workers copy their rows into the filling pass's pinned staging themselves
+ * (no dispatcher thread copies); a pass launches when full or when its GPU
+ * is idle; its size is capped at the largest whole number of the engine's
+ * tiles within max_batch (azb_hub_pass_cap). A failed pass fails every later
+ * request ("GPU inference failed: ..."); destroying the hub fails requests
+ * not yet launched and waits for those in flight. Outputs are those of the
+ * runner: a position's results do not depend on its pass.
+ * input_mode AZB_HUB_RECORDS: passes carry position records and the GPU
+ * encodes them (azb_runner_begin_stones); planes given to azb_hub_evaluate
+ * are turned into records on the calling thread (0/1 stone planes only). */
+typedef struct azb_hub azb_hub;
+enum { AZB_HUB_PLANES = 0, AZB_HUB_RECORDS = 1 };
+int azb_hub_create(const azb_net_desc* desc, const float* params, size_t n_params, const float* buffers,
+                   size_t n_buffers, const int* devices, int n_devices, int max_batch, int slots, int precision,
+                   int input_mode, azb_hub** out, char* err, size_t err_cap);
+/* The same hub logic over a CPU stand-in for the GPU passes (no GPU): after
+ * delay_us, each position's value is the FNV-1a hash of its planes' bytes,
+ * top 24 bits / 2^24, and logit a is value + a; after fail_after passes
+ * (when > 0) one pass fails. quantum: the boards of a whole tile. For tests. */
+int azb_hub_create_fake(int board, int history, int lanes, int max_batch, int slots, int quantum, int input_mode,
+                        int delay_us, int fail_after, azb_hub** out, char* err, size_t err_cap);
+void azb_hub_destroy(azb_hub* h);
+int azb_hub_lanes(const azb_hub* h);
+int azb_hub_pass_cap(const azb_hub* h);
+/* B positions ([B][planes][area] floats, or records) on lane `lane`; logits
+ * [B][area+1], values [B]. Thread-safe. 0, or -1 with err. */
+int azb_hub_evaluate(azb_hub* h, int lane, const float* input, int B, float* logits, float* values, char* err,
+                     size_t err_cap);
+int azb_hub_evaluate_records(azb_hub* h, int lane, const uint8_t* records, int B, float* logits, float* values,
+                             char* err, size_t err_cap);
+/* A lane's completed passes, their positions, the passes that were full
+ * (exactly azb_hub_pass_cap positions) and their summed begin-to-done seconds. */
+int azb_hub_stats(const azb_hub* h, int lane, long long* passes, long long* positions, long long* full_passes,
+                  double* gpu_seconds);
 
 /* ------------------------------------------------------- memory checks */
 

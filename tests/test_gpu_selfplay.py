@@ -8,6 +8,7 @@ index order.
 """
 import os
 
+import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
@@ -73,3 +74,41 @@ def test_arena_wave_independent_of_workers_and_batching(engine, sp):
     a = sp.arena(d, nets, WAVE, first=0, count=5, **kw)
     b = sp.arena(d, nets, WAVE, first=5, count=9, **kw)
     assert a["games"] + b["games"] == reference
+
+
+@pytest.mark.parametrize("precision", ["tf32x3", "bf16"])
+def test_engine_hub_plays_the_reference_hubs_games(engine, sp, precision):
+    """The engine's own hub (azb_hub: workers copy their own rows, passes
+    capped at whole tiles, a lane per GPU) plays byte for byte the games the
+    reference's InferenceHub plays over the same engine, with planes or with
+    stone records carried to the GPU, for any worker count and batch cap;
+    on every GPU present as lanes, the same again."""
+    d = engine.NetDesc(9, 1, 2, 32, 32, 0)
+    p, b = engine.synth_network(d, 805, 1)
+    kw = dict(precision=engine.PRECISIONS[precision], simulations=32, mcts_batch=8, temperature_moves=6, seed=806,
+              generation=2, first=4, count=8)
+    want = sp.play(d, p, b, backend="cuda", workers=4, inference_batch=64, **kw)["record_hash"]
+    devices = list(range(min(engine.device_count(), 2)))
+    for records in (False, True):
+        for workers, batch in ((1, 8), (8, 64), (8, 100)):
+            for devs in ({0}, set(devices)):
+                r = sp.play_hub(d, p, b, devices=sorted(devs), records=records, workers=workers,
+                                inference_batch=batch, **kw)
+                assert r["record_hash"] == want, (records, workers, batch, devs)
+                assert r["evaluations"] > 0 and r["passes"] > 0
+                # 9x9 frames run in the small-board tower's groups of one board: any cap is whole tiles
+                assert r["pass_cap"] == batch
+
+
+def test_engine_hub_pass_cap_whole_tiles(engine):
+    """19x19 frames are 400 rows: a pass is whole 128-row tiles when its
+    boards are a multiple of 8, so a cap of 100 becomes 96."""
+    d = engine.NetDesc(19, 1, 1, 32, 32, 0)
+    p, b = engine.synth_network(d, 807, 1)
+    with engine.Hub(d, p, b, devices=[0], max_batch=100, precision=engine.BF16) as hub:
+        assert hub.pass_cap() == 96
+        x = engine.synth_positions(d, 807, 8)
+        with engine.CudaInference(d, p, b, 8, 0, engine.BF16) as net:
+            want = net.infer(x)
+        got = hub.evaluate(0, x)
+        assert np.array_equal(got[0], want[0]) and np.array_equal(got[1], want[1])
