@@ -1,14 +1,19 @@
 // azb_hub: leaf batching for many search threads over one runner per GPU,
 // in one process. It serves the role of the reference's InferenceHub and
 // WorkerEvaluators for the "cuda" backend (include/azgo/inference_hub.hpp:
-// 83-150, src/inference_hub.cpp:95-295) with three differences in design:
+// 83-150, src/inference_hub.cpp:95-295), designed differently:
 //
-//  * No dispatcher thread copies rows. A worker reserves rows in its lane's
-//    filling pass under the lane's lock, then copies its positions straight
-//    into that pass's page-locked staging (and later its results out of it)
-//    without the lock, so the copies of many workers run in parallel instead
-//    of one after another on one thread (self-play on a GPU is bound by the
-//    host's cores).
+//  * No dispatcher thread. A request is given rows in its lane's filling
+//    pass under the lane's lock, by whichever thread has room to give: the
+//    arriving thread itself, or the thread that frees or launches a pass
+//    (the runner's completion thread, or a worker). Small requests are
+//    copied into the pass's page-locked staging by that thread, outside the
+//    lock, so a waiting worker blocks once, for its results; large ones
+//    (over 64 KB of input, e.g. 19x19 boards with history 8) are woken to
+//    copy their own rows, in parallel. The completion thread scatters each
+//    pass's results straight into the waiting requests' arrays and frees
+//    the pass at once, so the next pass can fill while the requests of the
+//    last one are still waking up.
 //  * A pass's size is capped at the largest whole number of the engine's
 //    tiles that fits the batch limit (a 128-row tile of frame rows holds 8
 //    19x19 boards, 32 9x9 boards in the per-layer kernels; the small-board
@@ -16,20 +21,21 @@
 //  * One lane (runner, device) per GPU in the process: a caller binds each
 //    of its workers to a lane, e.g. games partitioned across GPUs.
 //
-// The flush policy is the reference's: a pass launches as soon as it is full,
-// or as soon as its GPU has nothing in flight and every row reserved in it
-// has been copied in; with two passes per lane one computes while the next
-// fills. A failed pass fails its requests and every later one (the failure
-// is sticky, as in the reference's hub); destroying a hub fails requests
-// not yet launched ("inference hub shut down") and waits for the passes in
-// flight and for every thread still inside evaluate.
+// The flush policy is the reference's: a pass launches as soon as it is full
+// or as soon as its GPU has nothing in flight (once every row given in it has
+// been copied in); with two passes per lane one computes while the next
+// fills. Waiting requests are given rows oldest first. A failed pass fails
+// its requests and every later one (the failure is sticky, as in the
+// reference's hub); destroying a hub refuses requests that have no rows yet
+// ("inference hub shut down"), lets the filling and in-flight passes finish
+// and waits for every thread still inside evaluate.
 //
 // Input: float planes as the reference's Evaluator takes them ([B][2H+2][n*n],
 // encodePlanes' layout) or position records (azb_stones_record_bytes). A
-// records-mode hub converts planes to records in the calling thread (exact:
-// the planes of a position are 0/1 stone and side-to-move indicators) and
-// the GPU encodes them back, so ~H*n*n bytes per position cross to the
-// device instead of (2H+2)*n*n floats.
+// records-mode hub converts planes to records as it copies them (exact: the
+// planes of a position are 0/1 stone and side-to-move indicators) and the
+// GPU encodes them back, so ~H*n*n bytes per position cross to the device
+// instead of (2H+2)*n*n floats.
 #include <algorithm>
 #include <chrono>
 #include <condition_variable>
@@ -239,13 +245,23 @@ public:
     ~Lane() {
         std::unique_lock<std::mutex> lock(mu_);
         closing_ = true;
-        // Requests not launched yet fail; passes in flight finish.
-        for (size_t i = 0; i < passes_.size(); ++i)
-            if (passes_[i].state == kFilling) give_back(int(i), "inference hub shut down");
-        room_.notify_all();
+        admit_waiting(lock);   // refuses the requests still waiting for rows (gives none)
+        // A filling pass goes once its rows are in (its requests finish, as
+        // a reference hub's packed batch does); an empty one is dropped.
+        if (filling_ >= 0) {
+            Pass& f = passes_[size_t(filling_)];
+            const int s = filling_;
+            filling_ = -1;
+            if (f.reserved == 0) {
+                f = Pass{};
+            } else {
+                f.full = true;
+                if (f.written == f.reserved) launch(s, lock);
+            }
+        }
         drained_.wait(lock, [&] { return inside_ == 0 && in_flight_ == 0; });
         lock.unlock();
-        engine_.reset();   // joins nothing in flight: every pass has returned
+        engine_.reset();   // every pass has returned
     }
 
     int cap() const { return cap_; }
@@ -280,6 +296,37 @@ public:
     }
 
 private:
+    enum State { kFree, kFilling, kFlight };
+    static constexpr const char* kShutDown = "inference hub shut down";
+
+    // One evaluate call, on its caller's stack while it waits.
+    struct Request {
+        int B = 0;
+        const float* planes = nullptr;     // its input: planes, or
+        const uint8_t* records = nullptr;  // records
+        float* logits = nullptr;
+        float* values = nullptr;
+        int slot = -1, off = 0;   // its rows, once given
+        bool self_copy = false;   // given rows, it copies its input itself (a large request)
+        bool done = false;        // its results are in its arrays (or error is set)
+        bool discard = false;     // its rows hold stand-ins: no results to copy
+        std::string bad;          // why its input was refused (records mode)
+        std::string error;        // why it got no rows, or why its pass failed
+        std::condition_variable wake;
+    };
+    // Requests of up to this many input bytes are copied in by the thread
+    // that gives them rows (the one that frees or launches a pass), so a
+    // waiting worker wakes once, for its results; larger ones are woken to
+    // copy their own rows, in parallel with each other.
+    static constexpr size_t kAdmitterCopyBytes = size_t(64) << 10;
+    struct Pass {
+        State state = kFree;
+        int reserved = 0, written = 0;   // rows given to requests / copied in by them
+        bool full = false;               // launch once every reserved row is written
+        std::vector<Request*> members;
+        Clock::time_point started{};
+    };
+
     // The last thread out of evaluate lets a waiting destructor go on.
     void leave() {
         std::lock_guard<std::mutex> lock(mu_);
@@ -287,111 +334,149 @@ private:
     }
 
     void run_request(const float* planes, const uint8_t* records, int B, float* logits, float* values) {
+        std::unique_lock<std::mutex> lock(mu_);
+        Request r;
+        r.B = B;
+        r.planes = planes;
+        r.records = records;
+        r.logits = logits;
+        r.values = values;
+        waiting_.push_back(&r);
+        deliver(admit_waiting(lock), lock);
+        r.wake.wait(lock, [&] { return r.done || r.self_copy; });
+        if (!r.done) {   // a large request: its rows are copied here
+            lock.unlock();
+            copy_rows(r);
+            lock.lock();
+            wrote(r, lock);
+            r.wake.wait(lock, [&] { return r.done; });
+        }
+        lock.unlock();
+        if (r.slot < 0) {   // refused before it got rows
+            if (r.error == kShutDown) throw std::logic_error("azb_hub: evaluate after shutdown");
+            throw std::runtime_error("GPU inference failed: " + r.error);
+        }
+        if (!r.error.empty()) throw std::runtime_error("GPU inference failed: " + r.error);
+        if (!r.bad.empty()) throw std::invalid_argument(r.bad);
+    }
+
+    // A request's input into its rows of its pass's staging (no lock: the
+    // rows are its own until the pass launches, which waits for them).
+    void copy_rows(Request& r) {
         const int A = n_ * n_, P = 2 * H_ + 2;
         const size_t rec = stones_record_bytes(H_, n_);
-        std::unique_lock<std::mutex> lock(mu_);
-        const int slot = reserve(B, lock);
-        Pass& p = passes_[size_t(slot)];
-        const int off = p.reserved;
-        p.reserved += B;
-        ++p.readers;
-        lock.unlock();
-
-        // This request's rows, copied in without the lock.
-        std::string bad;
         if (records_) {
-            uint8_t* dst = engine_->records(slot) + size_t(off) * rec;
-            for (int b = 0; b < B; ++b) {
+            uint8_t* dst = engine_->records(r.slot) + size_t(r.off) * rec;
+            for (int b = 0; b < r.B; ++b) {
                 uint8_t* row = dst + size_t(b) * rec;
-                if (records) {
-                    std::memcpy(row, records + size_t(b) * rec, rec);
-                } else if (!planes_to_record(planes + size_t(b) * P * A, n_, H_, row)) {
-                    if (bad.empty())
-                        bad = "azb_hub: position " + std::to_string(b) + "'s planes are not stone planes (records mode)";
+                if (r.records) {
+                    std::memcpy(row, r.records + size_t(b) * rec, rec);
+                } else if (!planes_to_record(r.planes + size_t(b) * P * A, n_, H_, row)) {
+                    if (r.bad.empty())
+                        r.bad = "azb_hub: position " + std::to_string(b) + "'s planes are not stone planes (records mode)";
                     std::memset(row, 0, rec);
                     row[size_t(H_) * A] = 1;   // a valid record in its place (its results are not used)
                 }
             }
         } else {
-            std::memcpy(engine_->planes(slot) + size_t(off) * P * A, planes, size_t(B) * P * A * sizeof(float));
+            std::memcpy(engine_->planes(r.slot) + size_t(r.off) * P * A, r.planes, size_t(r.B) * P * A * sizeof(float));
         }
-
-        lock.lock();
-        p.written += B;
-        if (p.written == p.reserved && (p.full || in_flight_ == 0)) launch(slot, lock);
-        p.back.wait(lock, [&] { return p.state == kReturned; });
-        const std::string error = p.error;
-        lock.unlock();
-        // Its results, copied out without the lock (the pass is not reused
-        // before its last request has taken them).
-        if (error.empty() && bad.empty()) {
-            std::memcpy(logits, engine_->logits(slot) + size_t(off) * (A + 1), size_t(B) * (A + 1) * sizeof(float));
-            std::memcpy(values, engine_->values(slot) + size_t(off), size_t(B) * sizeof(float));
-        }
-        lock.lock();
-        if (--p.readers == 0) {
-            p = Pass{};
-            room_.notify_all();
-        }
-        lock.unlock();
-        if (!error.empty()) throw std::runtime_error("GPU inference failed: " + error);
-        if (!bad.empty()) throw std::invalid_argument(bad);
     }
 
-    enum State { kFree, kFilling, kFlight, kReturned };
-    struct Pass {
-        State state = kFree;
-        int reserved = 0, written = 0;   // rows reserved by requests / copied in by them
-        int readers = 0;                 // requests still to take their rows out
-        bool full = false;               // launch once every reserved row is written
-        std::string error;
-        Clock::time_point started{};
-        std::condition_variable back;    // its requests wait here for the pass to return
-        Pass& operator=(Pass&& o) {
-            state = o.state;
-            reserved = o.reserved;
-            written = o.written;
-            readers = o.readers;
-            full = o.full;
-            error = std::move(o.error);
-            started = o.started;
-            return *this;
+    // A request's rows are in: count them, and launch its pass when it is
+    // complete and full or its GPU idle. Under the lock.
+    void wrote(Request& r, std::unique_lock<std::mutex>& lock) {
+        r.discard = !r.bad.empty();
+        Pass& p = passes_[size_t(r.slot)];
+        p.written += r.B;
+        if (p.written == p.reserved && (p.full || in_flight_ == 0)) {
+            launch(r.slot, lock);
+            deliver(admit_waiting(lock), lock);   // requests waiting for rows take the next pass
         }
-    };
+    }
 
-    // A pass with room for B more rows: the filling pass, or a free one made
-    // the filling pass (a filling pass without room is closed and launched
-    // once its rows are in). Waits for a pass to come free. Under the lock.
-    int reserve(int B, std::unique_lock<std::mutex>& lock) {
-        for (;;) {
-            if (!failed_.empty()) throw std::runtime_error("GPU inference failed: " + failed_);
-            if (closing_) throw std::logic_error("azb_hub: evaluate after shutdown");
-            if (filling_ >= 0) {
-                Pass& f = passes_[size_t(filling_)];
-                if (f.reserved + B <= cap_) return filling_;
-                f.full = true;   // no room: it goes as soon as its rows are in
+    // Copies in the small requests this thread gave rows to, then counts
+    // them (which may launch passes and give more requests rows). Under the
+    // lock; dropped for the copies.
+    void deliver(std::vector<Request*> mine, std::unique_lock<std::mutex>& lock) {
+        while (!mine.empty()) {
+            lock.unlock();
+            for (Request* q : mine) copy_rows(*q);
+            lock.lock();
+            std::vector<Request*> next;
+            for (Request* q : mine) {
+                q->discard = !q->bad.empty();
+                Pass& p = passes_[size_t(q->slot)];
+                p.written += q->B;
+                if (p.written == p.reserved && (p.full || in_flight_ == 0)) {
+                    launch(q->slot, lock);
+                    std::vector<Request*> more = admit_waiting(lock);
+                    next.insert(next.end(), more.begin(), more.end());
+                }
+            }
+            mine = std::move(next);
+        }
+    }
+
+    // Requests waiting for rows, oldest first: each is given rows in the
+    // filling pass (a free pass becomes the filling pass when there is none)
+    // and woken alone, so a freed pass wakes only the requests it takes. A
+    // filling pass that cannot take the next request is closed: it goes as
+    // soon as its rows are in. After a failure or at shutdown the waiting
+    // requests are refused. Under the lock (dropped while a pass launches).
+    std::vector<Request*> admit_waiting(std::unique_lock<std::mutex>& lock) {
+        std::vector<Request*> mine;
+        const size_t row_bytes = records_ ? stones_record_bytes(H_, n_) : size_t(2 * H_ + 2) * n_ * n_ * sizeof(float);
+        while (!waiting_.empty()) {
+            if (!failed_.empty() || closing_) {
+                for (Request* q : waiting_) {
+                    q->error = failed_.empty() ? kShutDown : failed_;
+                    q->done = true;
+                    q->wake.notify_one();
+                }
+                waiting_.clear();
+                break;
+            }
+            if (filling_ < 0) {
+                for (size_t i = 0; i < passes_.size() && filling_ < 0; ++i)
+                    if (passes_[i].state == kFree) {
+                        passes_[i].state = kFilling;
+                        filling_ = int(i);
+                    }
+                if (filling_ < 0) break;   // every pass is busy: the next one to return admits
+            }
+            Pass& f = passes_[size_t(filling_)];
+            Request* q = waiting_.front();
+            if (f.reserved + q->B > cap_) {
+                f.full = true;
                 const int s = filling_;
                 filling_ = -1;
                 if (f.written == f.reserved) launch(s, lock);
                 continue;
             }
-            for (size_t i = 0; i < passes_.size(); ++i)
-                if (passes_[i].state == kFree) {
-                    passes_[i].state = kFilling;
-                    filling_ = int(i);
-                    return filling_;
-                }
-            room_.wait(lock);
+            waiting_.pop_front();
+            q->slot = filling_;
+            q->off = f.reserved;
+            f.reserved += q->B;
+            f.members.push_back(q);
+            if (size_t(q->B) * row_bytes <= kAdmitterCopyBytes) {
+                mine.push_back(q);
+            } else {
+                q->self_copy = true;
+                q->wake.notify_one();
+            }
         }
+        return mine;
     }
 
     // Starts pass `slot` (every reserved row written). Under the lock; drops
-    // it while the engine enqueues. After a failure nothing new runs.
+    // it while the engine enqueues. After a failure nothing new runs: the
+    // pass's requests fail at once.
     void launch(int slot, std::unique_lock<std::mutex>& lock) {
         Pass& p = passes_[size_t(slot)];
         if (filling_ == slot) filling_ = -1;
-        if (!failed_.empty() || closing_) {
-            give_back(slot, failed_.empty() ? "inference hub shut down" : failed_);
+        if (!failed_.empty()) {
+            finish(slot, failed_);
             return;
         }
         p.state = kFlight;
@@ -403,18 +488,23 @@ private:
         lock.lock();
     }
 
-    // Hands a pass back to its requests with `error`. Under the lock.
-    void give_back(int slot, const std::string& error) {
+    // Wakes every request of a pass with `error` (results already copied
+    // when it is empty) and frees the pass. Under the lock.
+    void finish(int slot, const std::string& error) {
         Pass& p = passes_[size_t(slot)];
-        if (filling_ == slot) filling_ = -1;
-        p.state = kReturned;
-        p.error = error;
-        if (!error.empty() && failed_.empty() && error != "inference hub shut down") failed_ = error;
-        p.back.notify_all();
-        if (p.readers == 0) p = Pass{};
+        if (!error.empty() && failed_.empty()) failed_ = error;
+        for (Request* q : p.members) {
+            q->error = error;
+            q->done = true;
+            q->wake.notify_one();
+        }
+        p = Pass{};
     }
 
-    // The engine's done(slot, error), on its completion thread.
+    // The engine's done(slot, error), on its completion thread: scatters the
+    // results into the waiting requests' arrays (outputs are A+2 floats a
+    // position, smaller than its input), frees the pass, launches the
+    // filling pass if the GPU went idle, and admits waiting requests.
     void on_done(int slot, const std::string& error) {
         std::unique_lock<std::mutex> lock(mu_);
         Pass& p = passes_[size_t(slot)];
@@ -424,13 +514,26 @@ private:
             stats_positions_ += p.reserved;
             if (p.reserved == cap_) ++stats_full_;
             stats_seconds_ += std::chrono::duration<double>(Clock::now() - p.started).count();
+            // The pass stays in flight for everyone else while it is copied out.
+            const std::vector<Request*> members = p.members;
+            lock.unlock();
+            const size_t L = size_t(n_) * n_ + 1;
+            const float* lg = engine_->logits(slot);
+            const float* v = engine_->values(slot);
+            for (Request* q : members) {
+                if (q->discard) continue;
+                std::memcpy(q->logits, lg + size_t(q->off) * L, size_t(q->B) * L * sizeof(float));
+                std::memcpy(q->values, v + size_t(q->off), size_t(q->B) * sizeof(float));
+            }
+            lock.lock();
         }
-        give_back(slot, error);
+        finish(slot, error);
         // The GPU is idle: the filling pass goes if its rows are all in.
         if (in_flight_ == 0 && filling_ >= 0) {
             Pass& f = passes_[size_t(filling_)];
             if (f.reserved > 0 && f.written == f.reserved) launch(filling_, lock);
         }
+        deliver(admit_waiting(lock), lock);
         if (in_flight_ == 0) drained_.notify_all();
     }
 
@@ -439,7 +542,8 @@ private:
     const bool records_;
     const int n_, H_;
     mutable std::mutex mu_;
-    std::condition_variable room_, drained_;
+    std::condition_variable drained_;
+    std::deque<Request*> waiting_;
     std::vector<Pass> passes_;
     int filling_ = -1, in_flight_ = 0, inside_ = 0;
     bool closing_ = false;

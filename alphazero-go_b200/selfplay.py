@@ -41,7 +41,7 @@ def _lib(path: str) -> C.CDLL:
         L.azsp_arena.restype = C.c_int
         if hasattr(L, "azsp_play_hub"):
             PL, PD = C.POINTER(C.c_longlong), C.POINTER(C.c_double)
-            L.azsp_play_hub.argtypes = ([C.c_int] * 5 + [F, C.c_size_t, F, C.c_size_t, PI] + [C.c_int] * 6 +
+            L.azsp_play_hub.argtypes = ([C.c_int] * 5 + [F, C.c_size_t, F, C.c_size_t, PI] + [C.c_int] * 7 +
                                         [C.c_float, C.c_int, C.c_float, C.c_int, C.c_uint64, C.c_int, C.c_int,
                                          C.c_int, PD, PL, PL, PU, PL, PL, PI, C.c_char_p, C.c_size_t])
             L.azsp_play_hub.restype = C.c_int

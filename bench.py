@@ -381,24 +381,43 @@ def run_selfplay(d: "Dist", dev: int) -> dict | None:
 
     sp_desc = E.NetDesc(SP_BOARD, 1, SP_BLOCKS, SP_FILTERS, SP_VH, 0)
     p, b = E.synth_network(sp_desc, SEED, 0)
-    try:
-        r = SP.play(sp_desc, p, b, backend="cuda", workers=SP_GAMES, inference_batch=SP_BATCH, device=dev,
-                    precision=E.TF32X3, simulations=SP_SIMS, mcts_batch=SP_MCTS_BATCH, c_puct=SP_CPUCT,
-                    temperature_moves=SP_TEMP, komi=SP_KOMI, max_moves=0, seed=SEED, generation=0,
-                    first=d.rank * SP_GAMES, count=SP_GAMES)
-        ok = 1.0
-    except Exception as e:   # not built here, or failed: every rank still takes the same collectives
-        r, ok = {"seconds": 0.0, "positions": 0, "evaluations": 0}, 0.0
-        err = str(e)
-    secs = d.max(r["seconds"])
-    pos, evals, oks = d.sum(float(r["positions"])), d.sum(float(r["evaluations"])), d.sum(ok)
-    if oks < d.world:
-        return {"workload": SP_WORKLOAD, "unavailable": err if ok == 0.0 else "self-play failed on another rank"}
-    return {"workload": SP_WORKLOAD, "playouts_per_s": pos * SP_SIMS / secs, "positions_evaluated_per_s": evals / secs,
-            "games": SP_GAMES * d.world, "positions": int(pos), "evaluations": int(evals), "seconds": secs,
+    kw = dict(precision=E.TF32X3, simulations=SP_SIMS, mcts_batch=SP_MCTS_BATCH, c_puct=SP_CPUCT,
+              temperature_moves=SP_TEMP, komi=SP_KOMI, max_moves=0, seed=SEED, generation=0,
+              first=d.rank * SP_GAMES, count=SP_GAMES)
+    out = {}
+    # The engine's own hub (azb_hub), then the reference's InferenceHub over
+    # the same engine: the same games (equal record hashes), two batchers.
+    for name, play in (("engine_hub", lambda: SP.play_hub(sp_desc, p, b, devices=[dev], workers=SP_GAMES,
+                                                          inference_batch=SP_BATCH, **kw)),
+                       ("reference_hub", lambda: SP.play(sp_desc, p, b, backend="cuda", workers=SP_GAMES,
+                                                         inference_batch=SP_BATCH, device=dev, **kw))):
+        try:
+            r, ok, err = play(), 1.0, ""
+        except Exception as e:   # not built here, or failed: every rank still takes the same collectives
+            r, ok, err = {"seconds": 0.0, "positions": 0, "evaluations": 0}, 0.0, str(e)
+        secs = d.max(r["seconds"])
+        pos, evals, oks = d.sum(float(r["positions"])), d.sum(float(r["evaluations"])), d.sum(ok)
+        if oks < d.world:
+            out[name] = {"unavailable": err if ok == 0.0 else "self-play failed on another rank"}
+            continue
+        out[name] = {"playouts_per_s": pos * SP_SIMS / secs, "positions_evaluated_per_s": evals / secs,
+                     "positions": int(pos), "evaluations": int(evals), "seconds": secs,
+                     "record_hash": r.get("record_hash")}
+        if name == "engine_hub":
+            out[name].update({"passes": r["passes"], "full_passes": r["full_passes"], "pass_cap": r["pass_cap"]})
+    main = out.get("engine_hub", {})
+    if "unavailable" in main or not main:
+        main = out.get("reference_hub", {})
+    if "playouts_per_s" not in main:
+        return {"workload": SP_WORKLOAD, "unavailable": main.get("unavailable", "self-play failed")}
+    return {"workload": SP_WORKLOAD, "playouts_per_s": main["playouts_per_s"],
+            "positions_evaluated_per_s": main["positions_evaluated_per_s"], "games": SP_GAMES * d.world,
+            "positions": main["positions"], "evaluations": main["evaluations"], "seconds": main["seconds"],
             "precision": "tf32x3 (the mode that meets the parity gate on this network)",
-            "how": "the reference's playSelfPlayGame and InferenceHub over this engine's bridge "
-                   "(alphazero-go_b200/host), one slice of 512 games per GPU, host wall clock, max over ranks"}
+            "engine_hub": out.get("engine_hub"), "reference_hub": out.get("reference_hub"),
+            "how": "the reference's playSelfPlayGame over this engine: playouts_per_s through the engine's own hub "
+                   "(azb_hub); reference_hub: through the reference's InferenceHub and the bridge; one slice of "
+                   "512 games per GPU, host wall clock, max over ranks"}
 
 
 def runner_passes(runner, B: int, n: int) -> None:

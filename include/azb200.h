@@ -220,13 +220,15 @@ const float* azb_runner_ownership(const azb_runner* r, int slot);
  * process drives several GPUs (the reference pins device 0,
  * src/cuda/cuda_context.cu:51). Each worker thread is bound to a lane and
  * calls azb_hub_evaluate, which blocks until its positions are evaluated.
- * Workers copy their rows into the filling pass's pinned staging themselves
- * (no dispatcher thread copies); a pass launches when full or when its GPU
- * is idle; its size is capped at the largest whole number of the engine's
- * tiles within max_batch (azb_hub_pass_cap). A failed pass fails every later
- * request ("GPU inference failed: ..."); destroying the hub fails requests
- * not yet launched and waits for those in flight. Outputs are those of the
- * runner: a position's results do not depend on its pass.
+ * There is no dispatcher thread: the thread that gives a request rows in the
+ * filling pass copies it into the pass's pinned staging (large requests copy
+ * themselves, in parallel), and the runner's completion thread copies the
+ * results back; a pass launches when full or when its GPU is idle; its size
+ * is capped at the largest whole number of the engine's tiles within
+ * max_batch (azb_hub_pass_cap). A failed pass fails every later request
+ * ("GPU inference failed: ..."); destroying the hub refuses requests that
+ * have no rows yet and waits for the passes that have. Outputs are those of
+ * the runner: a position's results do not depend on its pass.
  * input_mode AZB_HUB_RECORDS: passes carry position records and the GPU
  * encodes them (azb_runner_begin_stones); planes given to azb_hub_evaluate
  * are turned into records on the calling thread (0/1 stone planes only). */
