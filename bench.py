@@ -669,6 +669,7 @@ def run_profile_case(args):
 
     name, _, pname = args.profile_case.partition(":")
     n, blocks, filters, vh, B = SWEEP[name]
+    B = args.batch or B
     prec = {"tf32x3": E.TF32X3, "tf32": E.TF32, "bf16": E.BF16}[pname or "bf16"]
     desc = E.NetDesc(n, 1, blocks, filters, vh, 0)
     params, buffers = E.synth_network(desc, SEED, 0)
@@ -763,6 +764,7 @@ def main():
     ap.add_argument("--no-selfplay", action="store_true", help="skip the C5 self-play figures")
     ap.add_argument("--only-device", action="store_true", help="device-resident passes only (for profilers)")
     ap.add_argument("--profile-case", default=None, help="CONFIG:PRECISION, e.g. C2:tf32x3: device passes only, for ncu")
+    ap.add_argument("--batch", type=int, default=0, help="--profile-case: positions per pass (default: the config's)")
     ap.add_argument("--sweep", action="store_true",
                     help="one JSON line per configuration C1..C4: every precision, runner, and the reference's engines")
     args = ap.parse_args()
