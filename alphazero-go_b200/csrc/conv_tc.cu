@@ -1289,13 +1289,7 @@ cudaError_t launch_single_seg(const ConvMaps& m, ConvArgs a, int sms, cudaStream
     using C = ConvCfg<N, kBf16, kSplit, kTiles>;
     conv_smem_bytes(N, kBf16 ? kBF16 : (kSplit ? kTF32x3 : kTF32), a.halo_rows, &a.sa, &a.sb, false, kTiles);
     const size_t smem = smem_total(a.sa, a.sb, C::kOps * kTiles, C::kOps, a.a_bytes, C::kBBytes, C::kEpiBytes);
-    static std::atomic<size_t> configured{0};   // the largest size this instantiation was opened for
-    if (smem > configured.load()) {
-        const cudaError_t e = cudaFuncSetAttribute(conv3x3_tc<N, kBf16, kSplit, kTiles, kSeg>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-        if (e != cudaSuccess) return e;
-        configured = smem;
-    }
+    if (const cudaError_t e = open_smem<conv3x3_tc<N, kBf16, kSplit, kTiles, kSeg>>(smem); e != cudaSuccess) return e;
     const int groups = (a.ntiles + kTiles - 1) / kTiles;
     const int grid = std::max(1, std::min(groups, sms));
     return launch_pdl(conv3x3_tc<N, kBf16, kSplit, kTiles, kSeg>, dim3(grid), dim3(kThreadsOf<kTiles>), smem, s, m.a,
@@ -1311,13 +1305,8 @@ cudaError_t launch_wide(const ConvMaps& m, ConvArgs a, int sms, cudaStream_t s) 
     constexpr int kSeg = kDefaultSegment<N>;
     conv_smem_bytes(N, kTF32x3, a.halo_rows, &a.sa, &a.sb, false, 1);
     const size_t smem = smem_total(a.sa, a.sb, C::kOps, C::kOps, a.a_bytes, C::kBBytes, C::kEpiBytes);
-    static std::atomic<size_t> configured{0};
-    if (smem > configured.load()) {
-        const cudaError_t e = cudaFuncSetAttribute(conv3x3_tc<N, false, true, 1, kSeg, false, true>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-        if (e != cudaSuccess) return e;
-        configured = smem;
-    }
+    if (const cudaError_t e = open_smem<conv3x3_tc<N, false, true, 1, kSeg, false, true>>(smem); e != cudaSuccess)
+        return e;
     const int grid = std::max(1, std::min(2 * a.ntiles, sms));
     return launch_pdl(conv3x3_tc<N, false, true, 1, kSeg, false, true>, dim3(grid), dim3(kThreadsOf<1>), smem, s, m.a,
                       m.a_lo, m.w_pair, m.w_lo_pair, m.out, m.out_lo, a, NoTower{});
@@ -1342,13 +1331,8 @@ cudaError_t launch_persist_tiles(const TowerArgs& f, ConvArgs a, int sms, cudaSt
     using C = ConvCfg<N, kBf16, kSplit, kTiles>;
     conv_smem_bytes(N, kBf16 ? kBF16 : (kSplit ? kTF32x3 : kTF32), a.halo_rows, &a.sa, &a.sb, false, kTiles);
     const size_t smem = smem_total(a.sa, a.sb, C::kOps * kTiles, C::kOps, a.a_bytes, C::kBBytes, C::kEpiBytes);
-    static std::atomic<size_t> configured{0};
-    if (smem > configured.load()) {
-        const cudaError_t e = cudaFuncSetAttribute(conv3x3_tc<N, kBf16, kSplit, kTiles, kSeg, true>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-        if (e != cudaSuccess) return e;
-        configured = smem;
-    }
+    if (const cudaError_t e = open_smem<conv3x3_tc<N, kBf16, kSplit, kTiles, kSeg, true>>(smem); e != cudaSuccess)
+        return e;
     const int groups = (a.ntiles + kTiles - 1) / kTiles;
     const int grid = std::max(1, std::min(groups * f.layers, sms));
     return launch_pdl(conv3x3_tc<N, kBf16, kSplit, kTiles, kSeg, true>, dim3(grid), dim3(kThreadsOf<kTiles>), smem, s,
@@ -1370,13 +1354,7 @@ cudaError_t launch_one(const ConvMaps& m, ConvArgs a, int form, int sms, cudaStr
     if (form == kFormPair) {
         conv_smem_bytes(N, kBf16 ? kBF16 : (kSplit ? kTF32x3 : kTF32), a.halo_rows, &a.sa, &a.sb, true, 1);
         const size_t smem = smem_total(a.sa, a.sb, C::kOps, C::kOps, a.a_bytes, C::kBBytes / 2, C::kEpiBytes);
-        static std::atomic<size_t> configured{0};
-        if (smem > configured.load()) {
-            const cudaError_t e = cudaFuncSetAttribute(conv3x3_tc_pair<N, kBf16, kSplit>,
-                                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-            if (e != cudaSuccess) return e;
-            configured = smem;
-        }
+        if (const cudaError_t e = open_smem<conv3x3_tc_pair<N, kBf16, kSplit>>(smem); e != cudaSuccess) return e;
         const int pairs = (a.ntiles + 1) / 2;
         const int grid = 2 * std::max(1, std::min(pairs, sms / 2));
         return launch_pdl(conv3x3_tc_pair<N, kBf16, kSplit>, dim3(grid), dim3(kThreads), smem, s, m.a, m.a_lo, m.w_pair,

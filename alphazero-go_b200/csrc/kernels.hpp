@@ -10,6 +10,7 @@
 // padding rows are zeroed once when a buffer is allocated and no kernel ever
 // writes them, so a 3x3 convolution reads its 'same' padding as plain rows.
 #pragma once
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
 #include <cuda.h>
@@ -33,6 +34,25 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// Lets `Kernel` use `bytes` of dynamic shared memory on the current device.
+// The attribute belongs to the device, so each device is opened once (and
+// again for a larger size): one process may launch on several GPUs.
+constexpr int kMaxDevices = 64;
+template <auto Kernel>
+cudaError_t open_smem(size_t bytes) {
+    static std::atomic<size_t> opened[kMaxDevices];
+    int dev = 0;
+    if (const cudaError_t e = cudaGetDevice(&dev); e != cudaSuccess) return e;
+    if (dev >= 0 && dev < kMaxDevices && bytes <= opened[dev].load()) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+    if (e == cudaSuccess && dev >= 0 && dev < kMaxDevices) {
+        size_t seen = opened[dev].load();
+        while (seen < bytes && !opened[dev].compare_exchange_weak(seen, bytes)) {
+        }
+    }
+    return e;
 }
 
 // Error codes a kernel leaves in its error word (0: none).

@@ -395,13 +395,7 @@ cudaError_t launch_head_conv_as(const HeadArgs& a, int sms, cudaStream_t s) {
     const size_t stage = size_t(kbr) * br_bytes;
     const int stages = int(std::max<size_t>(2, std::min<size_t>(8, kBudget / stage)));
     const size_t smem = 128 + size_t(stages) * stage + size_t(stages) * 16;
-    static std::atomic<size_t> opened{0};
-    if (smem > opened.load()) {
-        const cudaError_t e = cudaFuncSetAttribute(head_conv_kernel<kMode, kLpr, kNch>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-        if (e != cudaSuccess) return e;
-        opened = smem;
-    }
+    if (const cudaError_t e = open_smem<head_conv_kernel<kMode, kLpr, kNch>>(smem); e != cudaSuccess) return e;
     const int nblk = (a.B * a.n + kbr - 1) / kbr;
     const unsigned grid = static_cast<unsigned>(std::max(1, std::min(nblk, sms)));
     return launch_pdl(head_conv_kernel<kMode, kLpr, kNch>, dim3(grid), dim3(kHcThreads), smem, s, a, stages, kbr,

@@ -577,13 +577,7 @@ __global__ void __launch_bounds__(kFusedThreads<kSplit>, kFusedCtas<kSplit>)
 
 template <int N, bool kBf16, bool kSplit, int kTps>
 cudaError_t launch_fused_tps(const FusedMaps& m, const FusedArgs& a, size_t smem, int ctas, int sms, cudaStream_t s) {
-    static std::atomic<size_t> configured{0};
-    if (smem > configured.load()) {
-        const cudaError_t e = cudaFuncSetAttribute(tower_fused<N, kBf16, kSplit, kTps>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-        if (e != cudaSuccess) return e;
-        configured = smem;
-    }
+    if (const cudaError_t e = open_smem<tower_fused<N, kBf16, kSplit, kTps>>(smem); e != cudaSuccess) return e;
     const int groups = (a.boards + a.group - 1) / a.group;
     const int grid = std::max(1, std::min(groups, sms * ctas));
     return launch_pdl(tower_fused<N, kBf16, kSplit, kTps>, dim3(grid), dim3(kFusedThreads<kSplit>), smem, s, m.in, m.in_lo,

@@ -298,6 +298,27 @@ def cpu_reference_sample(steps: int, warmup: int, per_step_calls: int = 1, secon
     return total_pos / total_t, workers, sample
 
 
+def cpu_batch_sample(batch: int = 16):
+    """The reference's CPU engine at a large batch: one Network::infer call of
+    `batch` C4 positions on one worker (its blas backend is single-threaded by
+    design, src/backend_blas.cpp:56-70), after one untimed call of 1. A bounded
+    stand-in for BASELINE.json's batch of 1024, which one worker would take
+    minutes to evaluate; positions/s does not depend on the batch there."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    cfg = O.NetConfig(BOARD, HISTORY, BLOCKS, FILTERS, VALUE_HIDDEN, False)
+    net = O.RefNetwork(cfg, SEED, O.KIND_BENCH)
+    x = O.ref_positions(cfg, SEED, batch)
+    backend = "blas" if "OpenBLAS" in O.blas_description() else "naive"
+    net.infer(x[:1], backend)
+    t0 = time.perf_counter()
+    net.infer(x, backend)
+    secs = time.perf_counter() - t0
+    return {"value": batch / secs, "unit": UNIT, "cores": 1, "kind": "reference", "batch": batch,
+            "sample": f"one Network::infer of {batch} positions on one worker ({backend}), {secs:.1f} s"}
+
+
 def selfplay_cpu_sample(plies: int = 6):
     """The reference's self-play on its own CPU engine (blas, one worker per
     core; oracle/_ref/libazselfplay_ref.so): one game per worker, each cut at
@@ -360,6 +381,10 @@ def run_reference(args):
         "cpu_baseline": {"value": rate, "unit": UNIT, "cores": workers, "kind": "reference", "sample": sample},
         "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    try:
+        line["cpu_batch"] = cpu_batch_sample()
+    except Exception as e:
+        line["cpu_batch"] = {"unavailable": f"reference CPU engine failed: {e}"}
     try:
         line["ref_cuda"] = refcuda_sample()
     except Exception as e:
