@@ -569,12 +569,23 @@ bool fused_tower_plan(const NetShape& s, int precision, FusedArgs* plan) {
     a.layers = 2 * s.blocks;
     a.nch = cpad_for(s.filters, precision) / chunk_channels(precision);
     a.top = round_up(s.board + 2, 8);
-    a.act_bytes = round_up((a.top + 128 + s.board + 2) * 128, 1024);
+    // A sub-buffer holds the rows a group's real points read: the zero halo
+    // above, the group's frames and the zero halo below. The rows of a
+    // 128-row tile past the group are outputs nobody reads; their taps read
+    // on into the next sub-buffer, or past the last into the weight ring.
+    const int group_rows = a.group * fr.S;
+    a.act_bytes = round_up((a.top + group_rows + s.board + 2) * 128, 1024);
     // The stem joins the launch when its packed operand has as many chunks
     // as a stored row (it is staged in the mid buffer).
     const int stem_nch = stem_k_for(s, precision) / chunk_channels(precision);
     a.stem_nch = stem_nch == a.nch ? stem_nch : 0;
-    if (fused_tower_smem(n_out, precision, a.nch, a.act_bytes, a.layers, &a.stages) == 0) return false;
+    const size_t smem = fused_tower_smem(n_out, precision, a.nch, a.act_bytes, a.layers, &a.stages);
+    if (smem == 0) return false;
+    // Those reads stay inside the CTA's shared memory: the furthest, a tap
+    // of the tile's last row in the last sub-buffer, ends before the ring
+    // does (the ring's smallest: two stages of one tap).
+    const size_t over = size_t(a.top + 128 + s.board + 2) * 128 - size_t(a.act_bytes);
+    if (over > size_t(2) * n_out * 128) return false;
     *plan = a;
     return true;
 }

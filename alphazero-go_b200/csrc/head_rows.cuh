@@ -191,28 +191,41 @@ struct FcWarp {
     static constexpr int kHeld = kSums >= 32 ? kSums / 32 : 1;   // sums a lane holds at the end
 
     // acc[k], k = o * kBoards + g: the dot of output o0 + o's weight row
-    // with board g's inputs, x(g, j) the board's input piece j.
-    template <class X>
+    // with board g's inputs, x(g, j) the board's input piece j. kTwo: a lane
+    // loads its pieces j and j + 32 together (one round trip for both where
+    // the inputs are short), adding them in the same order.
+    template <bool kTwo = false, class X>
     __device__ __forceinline__ static void dot(const float4* W, int n4, int ncols, int o0, int G, X x,
                                                float (&acc)[kSums], int lane) {
 #pragma unroll
         for (int k = 0; k < kSums; ++k) acc[k] = 0.0f;
-        for (int j = lane; j < n4; j += 32) {
-            float4 w[kOuts];
+        constexpr int kPieces = kTwo ? 2 : 1;
+        for (int j = lane; j < n4; j += 32 * kPieces) {
+            const bool two = kTwo && j + 32 < n4;
+            float4 w[kPieces][kOuts];
 #pragma unroll
-            for (int o = 0; o < kOuts; ++o)
-                w[o] = o0 + o < ncols ? __ldg(W + size_t(o0 + o) * n4 + j) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            for (int u = 0; u < kPieces; ++u)
+#pragma unroll
+                for (int o = 0; o < kOuts; ++o)
+                    w[u][o] = o0 + o < ncols && (u == 0 || two) ? __ldg(W + size_t(o0 + o) * n4 + j + 32 * u)
+                                                                : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
             for (int g = 0; g < kBoards; ++g) {
                 if (g >= G) break;
-                const float4 v = x(g, j);
+                float4 v[kPieces];
 #pragma unroll
-                for (int o = 0; o < kOuts; ++o) {
-                    float& c = acc[o * kBoards + g];
-                    c = fmaf(w[o].x, v.x, c);
-                    c = fmaf(w[o].y, v.y, c);
-                    c = fmaf(w[o].z, v.z, c);
-                    c = fmaf(w[o].w, v.w, c);
+                for (int u = 0; u < kPieces; ++u) v[u] = u == 0 || two ? x(g, j + 32 * u) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+                for (int u = 0; u < kPieces; ++u) {
+                    if (u > 0 && !two) break;
+#pragma unroll
+                    for (int o = 0; o < kOuts; ++o) {
+                        float& c = acc[o * kBoards + g];
+                        c = fmaf(w[u][o].x, v[u].x, c);
+                        c = fmaf(w[u][o].y, v[u].y, c);
+                        c = fmaf(w[u][o].z, v[u].z, c);
+                        c = fmaf(w[u][o].w, v[u].w, c);
+                    }
                 }
             }
         }
@@ -246,41 +259,54 @@ struct FcWarp {
     }
 };
 
-// One tile's FC outputs: this warp's share of the policy outputs [0, A+1)
-// and the value FC1 outputs [0, V) (kOuts at a time, the quads numbered
-// policy first), for the G boards from b0 whose inputs x(g, j) are the
-// feature rows: the policy features for policy outputs (pieces of 2A
-// values), the value features for value outputs (A values). Writes logits
-// and the ReLU of the hidden layer (hid_at(g) gives a board's hidden row).
+// Quads of the FC outputs (kOuts at a time): the policy outputs [0, A+1)
+// first, then the value FC1 outputs [0, V).
+template <int kOuts>
+__device__ __forceinline__ int head_fc_quad_count(const HeadArgs& a) {
+    return (a.A + 1 + kOuts - 1) / kOuts + (a.V + kOuts - 1) / kOuts;
+}
+
+// One quad q of the FC outputs for the G boards from b0, whose inputs
+// x(g, j) are the feature rows: the policy features for policy outputs
+// (pieces of 2A values), the value features for value outputs (A values).
+// Writes logits and the ReLU of the hidden layer (hid_at(g) gives a board's
+// hidden row).
+template <int kOuts, int kBoards, bool kTwo = false, class XPol, class XVal, class HidAt>
+__device__ __forceinline__ void head_fc_quad(const HeadArgs& a, int b0, int G, int q, XPol xpol, XVal xval,
+                                             HidAt hid_at, int lane) {
+    using Fc = FcWarp<kOuts, kBoards>;
+    const int L = a.A + 1, V = a.V;
+    const int pol_quads = (L + kOuts - 1) / kOuts;
+    const int n4p = (2 * a.A + 3) / 4, n4v = (a.A + 3) / 4;
+    const bool policy = q < pol_quads;
+    const int o0 = (policy ? q : q - pol_quads) * kOuts;
+    float acc[Fc::kSums];
+    if (policy)
+        Fc::template dot<kTwo>(reinterpret_cast<const float4*>(a.fc_w), n4p, L, o0, G, xpol, acc, lane);
+    else
+        Fc::template dot<kTwo>(reinterpret_cast<const float4*>(a.v1_w), n4v, V, o0, G, xval, acc, lane);
+#pragma unroll
+    for (int h = 0; h < Fc::kHeld; ++h) {
+        const int k = Fc::held(lane, h);
+        if (k < 0) continue;
+        const int o = o0 + k / kBoards, g = k % kBoards;
+        if (g >= G || o >= (policy ? L : V)) continue;
+        if (policy) {
+            a.logits[size_t(b0 + g) * L + o] = __fadd_rn(acc[h], __ldg(a.fc_b + o));
+        } else {
+            const float y = __fadd_rn(acc[h], __ldg(a.v1_b + o));
+            hid_at(g)[o] = y > 0.0f ? y : 0.0f;
+        }
+    }
+}
+
+// One tile's FC outputs: this warp's share of the quads (quad0, quad0 +
+// quad_step, ...).
 template <int kOuts, int kBoards, class XPol, class XVal, class HidAt>
 __device__ __forceinline__ void head_fc_quads(const HeadArgs& a, int b0, int G, int quad0, int quad_step, XPol xpol,
                                               XVal xval, HidAt hid_at, int lane) {
-    using Fc = FcWarp<kOuts, kBoards>;
-    const int L = a.A + 1, V = a.V;
-    const int pol_quads = (L + kOuts - 1) / kOuts, quads = pol_quads + (V + kOuts - 1) / kOuts;
-    const int n4p = (2 * a.A + 3) / 4, n4v = (a.A + 3) / 4;
-    for (int q = quad0; q < quads; q += quad_step) {
-        const bool policy = q < pol_quads;
-        const int o0 = (policy ? q : q - pol_quads) * kOuts;
-        float acc[Fc::kSums];
-        if (policy)
-            Fc::dot(reinterpret_cast<const float4*>(a.fc_w), n4p, L, o0, G, xpol, acc, lane);
-        else
-            Fc::dot(reinterpret_cast<const float4*>(a.v1_w), n4v, V, o0, G, xval, acc, lane);
-#pragma unroll
-        for (int h = 0; h < Fc::kHeld; ++h) {
-            const int k = Fc::held(lane, h);
-            if (k < 0) continue;
-            const int o = o0 + k / kBoards, g = k % kBoards;
-            if (g >= G || o >= (policy ? L : V)) continue;
-            if (policy) {
-                a.logits[size_t(b0 + g) * L + o] = __fadd_rn(acc[h], __ldg(a.fc_b + o));
-            } else {
-                const float y = __fadd_rn(acc[h], __ldg(a.v1_b + o));
-                hid_at(g)[o] = y > 0.0f ? y : 0.0f;
-            }
-        }
-    }
+    const int quads = head_fc_quad_count<kOuts>(a);
+    for (int q = quad0; q < quads; q += quad_step) head_fc_quad<kOuts, kBoards>(a, b0, G, q, xpol, xval, hid_at, lane);
 }
 
 // One warp finishes board b: value = tanh(v2 . hid + b2) and, when asked

@@ -254,7 +254,7 @@ struct FusedArgs {
     int layers;          // 2 * blocks
     int nch;             // 128-byte channel chunks per stored row (cpad / chunk)
     int top;             // the group's first row in an activation buffer: >= n + 2, a multiple of 8
-    int act_bytes;       // one (plane, chunk) buffer: 1024-aligned, top + 128 + n + 2 rows of 128 bytes
+    int act_bytes;       // one (plane, chunk) buffer: 1024-aligned, top + group * S + n + 2 rows of 128 bytes
     int stages;          // weight ring depth (set by the launcher)
     int stem_nch;        // > 0: the stem runs here too, over its packed operand of stem_nch (== nch) chunks
     const FusedLayer* layer;   // [layers]

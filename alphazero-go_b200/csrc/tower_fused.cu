@@ -14,12 +14,22 @@
 // [a_hi.b_hi | a_hi.b_lo + a_lo.b_hi] accumulator per input chunk (its
 // segments), the same epilogue roundings; the outputs are the same bits.
 //
-// Shared memory: two activation buffers (x: a block's input and output, the
-// output written in place over the residual it reads; mid: the block's
-// middle activation), each [plane][chunk] sub-buffers of frame rows x 128
-// bytes in the 128-byte swizzle, the group's rows from row `top` (a multiple
-// of 8, at least n + 2: the zero halo above), zero elsewhere; a
-// ring of weight tiles (one (chunk, tap) tile per stage, both planes).
+// Shared memory: activation buffers of [plane][chunk] sub-buffers of frame
+// rows x 128 bytes in the 128-byte swizzle, the group's rows from row `top`
+// (a multiple of 8, at least n + 2: the zero halo above), then n + 2 zero
+// rows; then a ring of weight tiles (one (chunk, tap) tile per stage, both
+// planes), as deep as the room left. A 128-row tile's rows past the group
+// are outputs nothing reads: their taps read on into the next sub-buffer (or
+// the ring), which costs no room.
+//
+// The split mode keeps one activation buffer: every step writes its output
+// over its input in place (its MMAs have all read it), and a block's input,
+// which its second conv adds back, waits in TMEM beside the accumulators,
+// put there by the epilogue warps while the block's first conv is on the
+// tensor core (and read back with the accumulators). The other modes, two
+// CTAs to an SM with half the registers, keep two (x: a block's input and
+// output, the output written in place over the residual it reads; mid: the
+// block's middle activation).
 //
 // Warps: 0 loads (the group's input, then every layer's weight tiles), 1
 // issues the MMAs and owns TMEM, 2-9 the epilogue (warp w reads TMEM lanes
@@ -45,10 +55,6 @@ namespace {
 constexpr int kFusedEpiWarps = 8;
 constexpr int kFusedFcBoards = 4;   // boards per group at most (5x5: three frames per 128-row tile)
 
-// A barrier of the eight epilogue warps (warps 2-9) alone.
-__device__ __forceinline__ void epilogue_sync() {
-    asm volatile("bar.sync 1, %0;" ::"n"(32 * kFusedEpiWarps) : "memory");
-}
 // Threads per CTA: the loader, the MMA issuer and eight epilogue warps; the
 // split mode adds the second issuer's warp (warp 10).
 template <bool kSplit>
@@ -74,28 +80,36 @@ struct FusedCfg {
 };
 
 // The TMEM columns a configuration needs: the split mode one stacked
-// accumulator (2N columns) per input chunk, else one of N.
+// accumulator (2N columns) per input chunk, then N columns of the block
+// input (fp32, the residual); else one accumulator of N.
+__host__ __device__ constexpr uint32_t fused_acc_cols(int n_out, bool split, int nch) {
+    return uint32_t(split ? 2 * n_out * nch : n_out);
+}
 __host__ __device__ constexpr uint32_t fused_tmem_cols(int n_out, bool split, int nch) {
-    const int cols = split ? 2 * n_out * nch : n_out;
+    const int cols = int(fused_acc_cols(n_out, split, nch)) + (split ? n_out : 0);
     return cols <= 32 ? 32u : cols <= 64 ? 64u : cols <= 128 ? 128u : cols <= 256 ? 256u : 512u;
 }
 
+// Activation buffers: one in the split mode, else two.
+__host__ __device__ constexpr int fused_act_bufs(bool split) { return split ? 1 : 2; }
+
 struct FusedSmem {
-    uint8_t* act[2];   // x, mid
+    uint8_t* act[2];   // x, mid (the split mode: both the one buffer)
     uint8_t* ring;
     float* bn;         // every layer's folded batch norm: layer l's scale at l * 2N, shift at l * 2N + N
     uint64_t *wfull, *wempty, *in_full, *acc_full, *act_ready, *out_done, *done;
+    uint64_t* epi;     // the epilogue warps' own barrier (one arrival per warp)
     uint32_t* tmem_slot;
 };
 
 __device__ __forceinline__ FusedSmem fused_carve(uint8_t* raw, const FusedArgs& p, int ops, uint32_t stage_bytes,
-                                             int n_out) {
+                                             int n_out, int bufs) {
     FusedSmem s;
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
     const size_t buf = size_t(ops) * p.nch * p.act_bytes;
     s.act[0] = base;
-    s.act[1] = base + buf;
-    s.ring = base + 2 * buf;
+    s.act[1] = base + (bufs - 1) * buf;
+    s.ring = base + bufs * buf;
     s.bn = reinterpret_cast<float*>(s.ring + size_t(p.stages) * stage_bytes);
     uint64_t* bars = reinterpret_cast<uint64_t*>(s.bn + size_t(p.layers + 1) * 2 * n_out);
     s.wfull = bars;
@@ -105,7 +119,8 @@ __device__ __forceinline__ FusedSmem fused_carve(uint8_t* raw, const FusedArgs& 
     s.act_ready = s.acc_full + 1;
     s.out_done = s.act_ready + 1;
     s.done = s.out_done + 1;
-    s.tmem_slot = reinterpret_cast<uint32_t*>(s.done + 1);
+    s.epi = s.done + 1;
+    s.tmem_slot = reinterpret_cast<uint32_t*>(s.epi + 1);
     return s;
 }
 
@@ -129,7 +144,8 @@ __global__ void __launch_bounds__(kFusedThreads<kSplit>, kFusedCtas<kSplit>)
                 const __grid_constant__ FusedArgs p) {
     using C = FusedCfg<N, kBf16, kSplit, kTps>;
     extern __shared__ uint8_t smem_raw[];
-    const FusedSmem sm = fused_carve(smem_raw, p, C::kOps, C::kStage, N);
+    constexpr int kBufs = fused_act_bufs(kSplit);
+    const FusedSmem sm = fused_carve(smem_raw, p, C::kOps, C::kStage, N, kBufs);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ngroups = (p.boards + p.group - 1) / p.group;
     const int group_rows = p.group * p.S;
@@ -138,10 +154,10 @@ __global__ void __launch_bounds__(kFusedThreads<kSplit>, kFusedCtas<kSplit>)
     // are two chunks; issuer i then owns chunk i's stages.
     const int issuers = kSplit && p.nch == 2 ? 2 : 1;
 
-    // Zero both activation buffers: the halos and the rows past the group
+    // Zero the activation buffers: the halos and the rows past the group
     // stay zero for the whole launch.
     {
-        const size_t words = 2 * size_t(C::kOps) * p.nch * p.act_bytes / 16;
+        const size_t words = size_t(kBufs) * C::kOps * p.nch * p.act_bytes / 16;
         uint4* w = reinterpret_cast<uint4*>(sm.act[0]);
         for (size_t i = threadIdx.x; i < words; i += blockDim.x) w[i] = make_uint4(0, 0, 0, 0);
         fence_proxy_async_smem();
@@ -166,6 +182,7 @@ __global__ void __launch_bounds__(kFusedThreads<kSplit>, kFusedCtas<kSplit>)
         mbar_init(sm.act_ready, kFusedEpiWarps);
         mbar_init(sm.out_done, p.heads ? kFusedEpiWarps : 1);   // heads: every epilogue warp reads x
         mbar_init(sm.done, uint32_t(issuers));
+        mbar_init(sm.epi, kFusedEpiWarps);
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
@@ -374,8 +391,50 @@ __global__ void __launch_bounds__(kFusedThreads<kSplit>, kFusedCtas<kSplit>)
         const int row = quarter * 32 + lane;    // row of the tile (and TMEM lane)
         const int brow = p.top + row;           // its row in the activation buffers
         const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16);
-        uint32_t k = 0, layers_done = 0;
+        // This warp's residual columns: the block input at its rows and
+        // output columns, fp32 (the split mode's hi + lo, as added).
+        const uint32_t tres = taddr + fused_acc_cols(N, kSplit, p.nch) + uint32_t(col0);
+        uint32_t k = 0, layers_done = 0, epi_uses = 0;
         bool ok = true;
+        // The epilogue warps' barrier (bounded, where a named barrier would
+        // wait forever for a warp that gave up): global writes before it are
+        // visible to every epilogue warp after it.
+        auto epi_sync = [&]() -> bool {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(sm.epi);
+            const bool fine = mbar_wait(sm.epi, epi_uses & 1, p.err, kErrWaitEpilogue);
+            ++epi_uses;
+            __syncwarp();
+            return fine;
+        };
+        // The heads' FCs of a group (policy FC and value FC1, the head tail
+        // kernel's lane split and tree: the same bits) run while the next
+        // group's layers are on the tensor core, a slice of this warp's quads
+        // (e, e + 8, ...) per step; a warp per board then finishes the value
+        // (FC2, tanh) and, when asked for, the softmax. The last group's run
+        // after its own heads.
+        int pend = -1, pend_boards = 0;   // the group whose FCs are pending: its first board
+        const float4* feat4 = reinterpret_cast<const float4*>(p.head.feat);
+        const size_t ld4 = size_t(p.head.feat_ld) / 4, val4 = size_t(p.head.feat_val) / 4;
+        auto xpol = [&](int gb, int j) { return feat4[size_t(pend + gb) * ld4 + j]; };
+        auto xval = [&](int gb, int j) { return feat4[size_t(pend + gb) * ld4 + val4 + j]; };
+        auto hid_at = [&](int gb) { return p.head.hid + size_t(pend + gb) * p.head.V; };
+        const int fc_quads = p.heads ? head_fc_quad_count<4>(p.head) : 0;
+        const int warp_quads = (fc_quads + kFusedEpiWarps - 1) / kFusedEpiWarps;
+        const int slice = (warp_quads + steps - 2) / (steps - 1);   // quads per step, the last step left for the finish
+        auto fc_slice = [&](int i0, int i1) {
+            for (int i = i0; i < i1; ++i) {
+                const int q = e + i * kFusedEpiWarps;
+                if (q >= fc_quads) break;
+                head_fc_quad<4, kFusedFcBoards, true>(p.head, pend, pend_boards, q, xpol, xval, hid_at, lane);
+            }
+        };
+        auto fc_finish = [&]() -> bool {
+            if (!epi_sync()) return false;   // every warp's FC outputs are in
+            for (int gb = e; gb < pend_boards; gb += kFusedEpiWarps) head_finish_board(p.head, pend + gb, hid_at(gb), lane);
+            pend = -1;
+            return true;
+        };
         for (int g = blockIdx.x; g < ngroups && ok; g += gridDim.x, ++k) {
             const int boards = min(p.group, p.boards - g * p.group);
             bool valid = row < boards * p.S;
@@ -384,17 +443,47 @@ __global__ void __launch_bounds__(kFusedThreads<kSplit>, kFusedCtas<kSplit>)
                 valid = r >= p.n + 1 && (r % (p.n + 1)) != p.n;
             }
             for (int st_ = 0; st_ < steps && ok; ++st_) {
-                if (!(ok = mbar_wait(sm.acc_full, layers_done & 1, p.err, kErrWaitEpilogue))) break;
-                tc_fence_after();
                 const bool stem = st_ < first;
                 const int l = stem ? p.layers : st_ - first;   // the batch norm's entry
+                const bool skip = !stem && (l & 1) != 0;   // the block's second conv adds the block input
+                if (kSplit && !stem && !skip && active) {
+                    // A block's first conv: while its MMAs read the block input,
+                    // this warp copies its part (every lane its row, 32
+                    // columns) into TMEM, where the second conv's epilogue
+                    // reads it back: the buffer then takes each output in place.
+                    // The group's first step reads the loaded input.
+                    if (st_ == 0 && !(ok = mbar_wait(sm.in_full, k & 1, p.err, kErrWaitEpilogue))) break;
+                    uint32_t r[32];
+                    const uint8_t* hi = sm.act[0] + size_t(col0 / 32) * p.act_bytes;
+                    const uint8_t* lo = sm.act[0] + (size_t(p.nch) + col0 / 32) * p.act_bytes;
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        const float4 h = *reinterpret_cast<const float4*>(hi + swz(brow, u));
+                        const float4 l4 = *reinterpret_cast<const float4*>(lo + swz(brow, u));
+                        r[4 * u] = __float_as_uint(__fadd_rn(h.x, l4.x));
+                        r[4 * u + 1] = __float_as_uint(__fadd_rn(h.y, l4.y));
+                        r[4 * u + 2] = __float_as_uint(__fadd_rn(h.z, l4.z));
+                        r[4 * u + 3] = __float_as_uint(__fadd_rn(h.w, l4.w));
+                    }
+                    tmem_st32(tres, r);
+                    tmem_wait_st();
+                }
+                if (pend >= 0) {
+                    if (st_ < steps - 1)
+                        fc_slice(st_ * slice, (st_ + 1) * slice);
+                    else if (!(ok = fc_finish()))
+                        break;
+                }
+                if (!(ok = mbar_wait(sm.acc_full, layers_done & 1, p.err, kErrWaitEpilogue))) break;
+                tc_fence_after();
                 uint8_t* out = stem || (l & 1) ? sm.act[0] : sm.act[1];
-                const bool skip = !stem && (l & 1) != 0;   // the block's second conv adds its input (x, written in place)
                 if (active) {
 #pragma unroll
                     for (int cb = 0; cb < C::kWarpCols / 32; ++cb) {
                         const int c0 = col0 + cb * 32;   // 32 output channels
                         float acc[32];
+                        uint32_t rv[32];   // the split mode: the block input, at the block's second conv
+                        if (kSplit && skip) tmem_ld32(tres, rv);   // (complete at the accumulators' wait)
                         if constexpr (kSplit) {
 #pragma unroll 1
                             for (int c = 0; c < p.nch; ++c) {
@@ -467,17 +556,19 @@ __global__ void __launch_bounds__(kFusedThreads<kSplit>, kFusedCtas<kSplit>)
                                                   __fadd_rn(__fmul_rn(a.z, acc[4 * u + 2]), b.z),
                                                   __fadd_rn(__fmul_rn(a.w, acc[4 * u + 3]), b.w)};
                                     if (skip) {
-                                        const float4 h = *reinterpret_cast<const float4*>(hi + swz(brow, u));
-                                        float4 r = h;
+                                        float r[4];
                                         if constexpr (kSplit) {
-                                            const float4 l4 = *reinterpret_cast<const float4*>(lo + swz(brow, u));
-                                            r = make_float4(__fadd_rn(h.x, l4.x), __fadd_rn(h.y, l4.y), __fadd_rn(h.z, l4.z),
-                                                            __fadd_rn(h.w, l4.w));
+#pragma unroll
+                                            for (int q = 0; q < 4; ++q) r[q] = __uint_as_float(rv[4 * u + q]);
+                                        } else {
+                                            const float4 h = *reinterpret_cast<const float4*>(hi + swz(brow, u));
+                                            r[0] = h.x;
+                                            r[1] = h.y;
+                                            r[2] = h.z;
+                                            r[3] = h.w;
                                         }
-                                        y[0] = __fadd_rn(y[0], r.x);
-                                        y[1] = __fadd_rn(y[1], r.y);
-                                        y[2] = __fadd_rn(y[2], r.z);
-                                        y[3] = __fadd_rn(y[3], r.w);
+#pragma unroll
+                                        for (int q = 0; q < 4; ++q) y[q] = __fadd_rn(y[q], r[q]);
                                     }
 #pragma unroll
                                     for (int q = 0; q < 4; ++q) y[q] = y[q] > 0.0f ? y[q] : 0.0f;
@@ -534,22 +625,11 @@ __global__ void __launch_bounds__(kFusedThreads<kSplit>, kFusedCtas<kSplit>)
                     hl.step(p.head, base, pts, piece, where, lane);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(sm.out_done);   // x may be overwritten by the next group's input
-                // The rest of the heads for the group's boards, from the
-                // features the epilogue warps just wrote (global memory: the
-                // named barrier makes them visible across the warps): the
-                // policy FC and value FC1 (the head tail kernel's lane split
-                // and tree, the same bits), then a warp per board finishes
-                // the value (FC2, tanh) and, when asked for, the softmax.
-                epilogue_sync();
-                const float4* feat4 = reinterpret_cast<const float4*>(p.head.feat);
-                const size_t ld4 = size_t(p.head.feat_ld) / 4, val4 = size_t(p.head.feat_val) / 4;
-                auto xpol = [=](int gb, int j) { return feat4[size_t(first_board + gb) * ld4 + j]; };
-                auto xval = [=](int gb, int j) { return feat4[size_t(first_board + gb) * ld4 + val4 + j]; };
-                auto hid_at = [&](int gb) { return p.head.hid + size_t(first_board + gb) * p.head.V; };
-                head_fc_quads<4, kFusedFcBoards>(p.head, first_board, boards, e, kFusedEpiWarps, xpol, xval, hid_at,
-                                                 lane);
-                epilogue_sync();
-                for (int gb = e; gb < boards; gb += kFusedEpiWarps) head_finish_board(p.head, first_board + gb, hid_at(gb), lane);
+                // The features every epilogue warp wrote are visible to all;
+                // the group's FCs wait for the next group's steps.
+                if (!(ok = epi_sync())) break;
+                pend = first_board;
+                pend_boards = boards;
             } else if (e == 0 && lane == 0) {
                 // The tower's output (x) leaves once every epilogue warp has
                 // written the last layer.
@@ -563,6 +643,10 @@ __global__ void __launch_bounds__(kFusedThreads<kSplit>, kFusedCtas<kSplit>)
                 bulk_wait_read<0>();   // x may be overwritten by the next group's input
                 mbar_arrive(sm.out_done);
             }
+        }
+        if (ok && pend >= 0) {   // the last group's FCs
+            fc_slice(0, warp_quads);
+            fc_finish();
         }
         if (e == 0 && lane == 0) bulk_wait_all();   // every store complete before the CTA exits
     }
@@ -604,13 +688,13 @@ cudaError_t launch_fused_one(const FusedMaps& m, FusedArgs a, int sms, cudaStrea
 size_t fused_tower_smem(int n_out, int precision, int nch, int act_bytes, int layers, int* stages, int ctas,
                         int taps_per_stage) {
     const int ops = precision == kTF32x3 ? 2 : 1;
-    const size_t acts = 2 * size_t(ops) * nch * act_bytes;
+    const size_t acts = size_t(fused_act_bufs(precision == kTF32x3)) * ops * nch * act_bytes;
     const size_t stage = size_t(taps_per_stage) * ops * n_out * 128;
     const size_t bn = size_t(layers + 1) * 2 * n_out * 4;   // the tower's convs and the stem
     // An SM's 228 KB, less 1 KB reserved per CTA, shared by `ctas` CTAs.
     const size_t kMax = ctas > 1 ? (228 * 1024) / size_t(ctas) - 1024 : 227 * 1024;
     for (int st = 8; st >= 2; --st) {
-        const size_t total = 1024 + acts + st * stage + bn + (2 * st + 5) * 8 + 16;
+        const size_t total = 1024 + acts + st * stage + bn + (2 * st + 6) * 8 + 16;
         if (total <= kMax) {
             if (stages) *stages = st;
             return total;
