@@ -172,21 +172,37 @@ __device__ __forceinline__ void store_split_planes(float* hi_dst, float* lo_dst,
 // keep the sum within a few fp32 roundings). An epilogue thread adds one
 // segment's two halves ([0, N) the large products, [N, 2N) the small ones)
 // of its row's kMine 32-column chunks from c_begin into its running sums.
+// With more than one chunk the halves go 16 columns at a time: the running
+// sums of all the chunks stay live, so two 32-column loads beside them
+// would not fit in the registers.
 template <int N, int kMine>
 __device__ __forceinline__ void add_segment(uint32_t taddr, int c_begin, float (&sum)[kMine * 32], bool first) {
+    constexpr int kCols = kMine > 1 ? 16 : 32;
 #pragma unroll
     for (int cc = 0; cc < kMine; ++cc) {
-        uint32_t v[32], w[32];
-        tmem_ld32(taddr + uint32_t(c_begin + cc) * 32u, v);
-        tmem_ld32(taddr + uint32_t(N + (c_begin + cc) * 32), w);
-        tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {   // paired: half the instructions on this SM's issue slots
-            const float2 part = fadd2_rn(make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])),
-                                         make_float2(__uint_as_float(w[i]), __uint_as_float(w[i + 1])));
-            const float2 s2 = first ? part : fadd2_rn(make_float2(sum[cc * 32 + i], sum[cc * 32 + i + 1]), part);
-            sum[cc * 32 + i] = s2.x;
-            sum[cc * 32 + i + 1] = s2.y;
+        for (int h = 0; h < 32; h += kCols) {
+            uint32_t v[kCols], w[kCols];
+            const uint32_t col = uint32_t(c_begin + cc) * 32u + uint32_t(h);
+            if constexpr (kCols == 32) {
+                tmem_ld32(taddr + col, v);
+                tmem_ld32(taddr + uint32_t(N) + col, w);
+            } else {
+                tmem_ld16(taddr + col, v);
+                tmem_ld16(taddr + uint32_t(N) + col, w);
+            }
+            tmem_wait_ld();
+            tmem_hold(v);
+            tmem_hold(w);
+#pragma unroll
+            for (int i = 0; i < kCols; i += 2) {   // paired: half the instructions on this SM's issue slots
+                const int k = cc * 32 + h + i;
+                const float2 part = fadd2_rn(make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])),
+                                             make_float2(__uint_as_float(w[i]), __uint_as_float(w[i + 1])));
+                const float2 s2 = first ? part : fadd2_rn(make_float2(sum[k], sum[k + 1]), part);
+                sum[k] = s2.x;
+                sum[k + 1] = s2.y;
+            }
         }
     }
 }

@@ -257,6 +257,25 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// After tmem_wait_ld: ties registers a tcgen05.ld wrote to the wait, so no
+// use of them is scheduled before it (to the compiler they are written at
+// the load).
+template <int K>
+__device__ __forceinline__ void tmem_hold(uint32_t (&v)[K]) {
+#pragma unroll
+    for (int i = 0; i < K; ++i) asm volatile("" : "+r"(v[i]));
+}
+
+// 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+}
+
 // The store counterpart: 32 consecutive 32-bit columns of this thread's lane.
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
     asm volatile(
@@ -421,6 +440,22 @@ __device__ __forceinline__ float2 fadd2_rn(float2 a, float2 b) {
         "mov.b64 ra, {%2, %3};\n\t"
         "mov.b64 rb, {%4, %5};\n\t"
         "add.rn.f32x2 rd, ra, rb;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
+// The same for subtraction (sub.rn.f32x2). (No packed multiply here: on
+// this toolchain a mul.rn.f32x2 feeding an add.rn.f32x2 is contracted into
+// one fused multiply-add, one rounding where two were asked for; scalar
+// __fmul_rn / __fadd_rn are not.)
+__device__ __forceinline__ float2 fsub2_rn(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rb, {%4, %5};\n\t"
+        "sub.rn.f32x2 rd, ra, rb;\n\t"
         "mov.b64 {%0, %1}, rd;\n\t}"
         : "=f"(d.x), "=f"(d.y)
         : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));

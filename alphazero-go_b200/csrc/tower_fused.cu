@@ -77,6 +77,7 @@ struct FusedCfg {
     // lane quarter, the other idle).
     static constexpr int kWarpCols = N >= 64 ? N / 2 : N;
     static_assert(N == 32 || N == 64, "the fused tower runs 32 or 64 output channels");
+    static_assert(kWarpCols == 32, "an epilogue warp takes 32 output columns");
 };
 
 // The TMEM columns a configuration needs: the split mode one stacked
@@ -477,30 +478,96 @@ __global__ void __launch_bounds__(kFusedThreads<kSplit>, kFusedCtas<kSplit>)
                 if (!(ok = mbar_wait(sm.acc_full, layers_done & 1, p.err, kErrWaitEpilogue))) break;
                 tc_fence_after();
                 uint8_t* out = stem || (l & 1) ? sm.act[0] : sm.act[1];
-                if (active) {
+                if (active && kSplit) {
+                    // The split mode, its 32 columns in two halves of 16: the
+                    // second half's TMEM loads fly while the first half's
+                    // pieces are computed. Per column the accumulator is
+                    // (hh + mixed) of chunk 0, then + (hh + mixed) of chunk 1.
+                    const float4* sc4 = reinterpret_cast<const float4*>(sm.bn + size_t(l) * 2 * N + col0);
+                    const float4* sh4 = reinterpret_cast<const float4*>(sm.bn + size_t(l) * 2 * N + N + col0);
+                    uint8_t* hi = out + size_t(col0 / 32) * p.act_bytes;
+                    uint8_t* lo = out + (size_t(p.nch) + col0 / 32) * p.act_bytes;
+                    const bool two = p.nch == 2;
+                    uint32_t rv[32];   // the block input, at the block's second conv
+                    uint32_t v0[16], w0[16], v1[16], w1[16];
+                    float acc[16];
+                    auto load = [&](int h) {
+                        const uint32_t at = taddr + uint32_t(col0 + 16 * h);
+                        tmem_ld16(at, v0);
+                        tmem_ld16(at + N, w0);
+                        if (two) {
+                            tmem_ld16(at + 2 * N, v1);
+                            tmem_ld16(at + 3 * N, w1);
+                        }
+                    };
+                    auto combine = [&]() {
+#pragma unroll
+                        for (int i = 0; i < 16; i += 2) {
+                            float2 s2 = fadd2_rn(make_float2(__uint_as_float(v0[i]), __uint_as_float(v0[i + 1])),
+                                                 make_float2(__uint_as_float(w0[i]), __uint_as_float(w0[i + 1])));
+                            if (two)
+                                s2 = fadd2_rn(s2, fadd2_rn(make_float2(__uint_as_float(v1[i]), __uint_as_float(v1[i + 1])),
+                                                           make_float2(__uint_as_float(w1[i]), __uint_as_float(w1[i + 1]))));
+                            acc[i] = s2.x;
+                            acc[i + 1] = s2.y;
+                        }
+                    };
+                    // Pieces 4h..4h+3: the batch norm, the residual, ReLU, the
+                    // tf32 split, the stores (the reference's separate
+                    // roundings, src/cuda/kernels.cu:172-176).
+                    auto pieces = [&](int h) {
+                        if (!valid) return;
+#pragma unroll
+                        for (int uu = 0; uu < 4; ++uu) {
+                            const int u = 4 * h + uu;
+                            const float4 a = sc4[u], b = sh4[u];
+                            // (The batch norm stays scalar: a packed multiply
+                            // feeding a packed add is fused into one rounding.)
+                            float2 y01 = make_float2(__fadd_rn(__fmul_rn(a.x, acc[4 * uu]), b.x),
+                                                     __fadd_rn(__fmul_rn(a.y, acc[4 * uu + 1]), b.y));
+                            float2 y23 = make_float2(__fadd_rn(__fmul_rn(a.z, acc[4 * uu + 2]), b.z),
+                                                     __fadd_rn(__fmul_rn(a.w, acc[4 * uu + 3]), b.w));
+                            if (skip) {
+                                y01 = fadd2_rn(y01, make_float2(__uint_as_float(rv[4 * u]), __uint_as_float(rv[4 * u + 1])));
+                                y23 = fadd2_rn(y23, make_float2(__uint_as_float(rv[4 * u + 2]), __uint_as_float(rv[4 * u + 3])));
+                            }
+                            y01.x = y01.x > 0.0f ? y01.x : 0.0f;
+                            y01.y = y01.y > 0.0f ? y01.y : 0.0f;
+                            y23.x = y23.x > 0.0f ? y23.x : 0.0f;
+                            y23.y = y23.y > 0.0f ? y23.y : 0.0f;
+                            const float4 hv = make_float4(to_tf32(y01.x), to_tf32(y01.y), to_tf32(y23.x), to_tf32(y23.y));
+                            const float2 l01 = fsub2_rn(y01, make_float2(hv.x, hv.y));
+                            const float2 l23 = fsub2_rn(y23, make_float2(hv.z, hv.w));
+                            *reinterpret_cast<float4*>(hi + swz(brow, u)) = hv;
+                            *reinterpret_cast<float4*>(lo + swz(brow, u)) = make_float4(l01.x, l01.y, l23.x, l23.y);
+                        }
+                    };
+                    auto hold = [&]() {
+                        tmem_hold(v0);
+                        tmem_hold(w0);
+                        if (two) {
+                            tmem_hold(v1);
+                            tmem_hold(w1);
+                        }
+                    };
+                    if (skip) tmem_ld32(tres, rv);
+                    load(0);
+                    tmem_wait_ld();
+                    hold();
+                    if (skip) tmem_hold(rv);
+                    combine();
+                    load(1);   // in flight during the first half's pieces
+                    pieces(0);
+                    tmem_wait_ld();
+                    hold();
+                    combine();
+                    pieces(1);
+                } else if (active) {
 #pragma unroll
                     for (int cb = 0; cb < C::kWarpCols / 32; ++cb) {
                         const int c0 = col0 + cb * 32;   // 32 output channels
                         float acc[32];
-                        uint32_t rv[32];   // the split mode: the block input, at the block's second conv
-                        if (kSplit && skip) tmem_ld32(tres, rv);   // (complete at the accumulators' wait)
-                        if constexpr (kSplit) {
-#pragma unroll 1
-                            for (int c = 0; c < p.nch; ++c) {
-                                uint32_t v[32], w[32];
-                                tmem_ld32(taddr + uint32_t(c) * 2u * N + uint32_t(c0), v);
-                                tmem_ld32(taddr + uint32_t(c) * 2u * N + uint32_t(N + c0), w);
-                                tmem_wait_ld();
-#pragma unroll
-                                for (int i = 0; i < 32; i += 2) {
-                                    const float2 part = fadd2_rn(make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])),
-                                                                 make_float2(__uint_as_float(w[i]), __uint_as_float(w[i + 1])));
-                                    const float2 s2 = c == 0 ? part : fadd2_rn(make_float2(acc[i], acc[i + 1]), part);
-                                    acc[i] = s2.x;
-                                    acc[i + 1] = s2.y;
-                                }
-                            }
-                        } else {
+                        {
                             uint32_t v[32];
                             tmem_ld32(taddr + uint32_t(c0), v);
                             tmem_wait_ld();
@@ -545,9 +612,8 @@ __global__ void __launch_bounds__(kFusedThreads<kSplit>, kFusedCtas<kSplit>)
                                     *reinterpret_cast<uint4*>(at) = o;
                                 }
                             } else {
-                                // fp32: channel block c0 is chunk c0 / 32 (split: both planes).
+                                // fp32 (tf32 mode): channel block c0 is chunk c0 / 32.
                                 uint8_t* hi = out + size_t(c0 / 32) * p.act_bytes;
-                                uint8_t* lo = out + (size_t(p.nch) + c0 / 32) * p.act_bytes;
 #pragma unroll
                                 for (int u = 0; u < 8; ++u) {
                                     const float4 a = sc4[u], b = sh4[u];
@@ -556,33 +622,15 @@ __global__ void __launch_bounds__(kFusedThreads<kSplit>, kFusedCtas<kSplit>)
                                                   __fadd_rn(__fmul_rn(a.z, acc[4 * u + 2]), b.z),
                                                   __fadd_rn(__fmul_rn(a.w, acc[4 * u + 3]), b.w)};
                                     if (skip) {
-                                        float r[4];
-                                        if constexpr (kSplit) {
-#pragma unroll
-                                            for (int q = 0; q < 4; ++q) r[q] = __uint_as_float(rv[4 * u + q]);
-                                        } else {
-                                            const float4 h = *reinterpret_cast<const float4*>(hi + swz(brow, u));
-                                            r[0] = h.x;
-                                            r[1] = h.y;
-                                            r[2] = h.z;
-                                            r[3] = h.w;
-                                        }
-#pragma unroll
-                                        for (int q = 0; q < 4; ++q) y[q] = __fadd_rn(y[q], r[q]);
+                                        const float4 h = *reinterpret_cast<const float4*>(hi + swz(brow, u));
+                                        y[0] = __fadd_rn(y[0], h.x);
+                                        y[1] = __fadd_rn(y[1], h.y);
+                                        y[2] = __fadd_rn(y[2], h.z);
+                                        y[3] = __fadd_rn(y[3], h.w);
                                     }
 #pragma unroll
                                     for (int q = 0; q < 4; ++q) y[q] = y[q] > 0.0f ? y[q] : 0.0f;
-                                    if constexpr (kSplit) {
-                                        float4 h, l4;
-                                        h.x = to_tf32(y[0]); l4.x = __fsub_rn(y[0], h.x);
-                                        h.y = to_tf32(y[1]); l4.y = __fsub_rn(y[1], h.y);
-                                        h.z = to_tf32(y[2]); l4.z = __fsub_rn(y[2], h.z);
-                                        h.w = to_tf32(y[3]); l4.w = __fsub_rn(y[3], h.w);
-                                        *reinterpret_cast<float4*>(hi + swz(brow, u)) = h;
-                                        *reinterpret_cast<float4*>(lo + swz(brow, u)) = l4;
-                                    } else {
-                                        *reinterpret_cast<float4*>(hi + swz(brow, u)) = make_float4(y[0], y[1], y[2], y[3]);
-                                    }
+                                    *reinterpret_cast<float4*>(hi + swz(brow, u)) = make_float4(y[0], y[1], y[2], y[3]);
                                 }
                             }
                         }
