@@ -924,17 +924,6 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                 // is released as soon as it has been read.
                 constexpr int kMine = kTiles == 2 ? kChunks : (kChunks >= 2 ? kChunks / 2 : 1);
                 const bool mine = c_begin < c_end && tile < p.ntiles;
-                if (mine && valid) {   // the residual reaches L2 while the tile accumulates
-                    const ItemIo io = item_io(layer, col0);
-                    if (io.res_hi != nullptr) {
-                        const size_t off = size_t(q) * p.ld + size_t(c_begin) * 32;
-#pragma unroll
-                        for (int cc = 0; cc < kMine; ++cc) {
-                            prefetch_l2(static_cast<const float*>(io.res_hi) + off + cc * 32);
-                            prefetch_l2(static_cast<const float*>(io.res_lo) + off + cc * 32);
-                        }
-                    }
-                }
                 float sum[kMine * 32];
                 bool ok = true;
                 int segs = layer_segs;
@@ -943,6 +932,20 @@ __global__ void __launch_bounds__(kThreadsOf<kTiles>, 1)
                 }
                 for (int sg = 0; sg < segs; ++sg, ++j) {
                     const uint32_t acc = j & 1;
+                    if (sg == segs - 1 && mine && valid) {
+                        // The residual reaches L2 while the last segment
+                        // accumulates (earlier, a pass whose frames overflow
+                        // L2 evicts it again before the store reads it).
+                        const ItemIo io = item_io(layer, col0);
+                        if (io.res_hi != nullptr) {
+                            const size_t off = size_t(q) * p.ld + size_t(c_begin) * 32;
+#pragma unroll
+                            for (int cc = 0; cc < kMine; ++cc) {
+                                prefetch_l2(static_cast<const float*>(io.res_hi) + off + cc * 32);
+                                prefetch_l2(static_cast<const float*>(io.res_lo) + off + cc * 32);
+                            }
+                        }
+                    }
                     if (!(ok = mbar_wait(&sm.acc_full[acc], (j >> 1) & 1, p.err, kErrWaitEpilogue))) break;
                     tc_fence_after();
                     if (mine) add_segment<N, kMine>(lanes + acc * (kTiles * C::kTileCols), c_begin, sum, sg == 0);

@@ -8,6 +8,7 @@
 #include <cuda_bf16.h>
 
 #include "kernels.hpp"
+#include "sm100.cuh"
 
 namespace azb {
 
@@ -62,7 +63,10 @@ struct HeadLane {
     static constexpr int kScatter = kLog < 4 ? kLog : 4;       // steps that halve the 16 sums
     static constexpr int kBfly = kLog - kScatter;              // butterfly steps after them
     static constexpr int kOwn = (kHcSlots * 4) >> kScatter;    // finished sums per lane
-    float w[4][kC];
+    // The 1x1 weights of this lane's channels, heads paired for the packed
+    // fma (each half an IEEE fmaf: the same bits as one head at a time):
+    // (policy 0, policy 1), (value, ownership).
+    float2 w01[kC], w23[kC];
     float bn_scale[kOwn], bn_shift[kOwn];
 
     __device__ __forceinline__ void load(const HeadArgs& a, int lane) {
@@ -73,10 +77,8 @@ struct HeadLane {
             for (int e = 0; e < W; ++e) {
                 const int ch = (l + j * kLpr) * W + e, i = j * W + e;
                 const bool real = ch < a.F;
-                w[0][i] = real ? __ldg(a.pol_w + ch) : 0.0f;
-                w[1][i] = real ? __ldg(a.pol_w + a.F + ch) : 0.0f;
-                w[2][i] = real ? __ldg(a.val_w + ch) : 0.0f;
-                w[3][i] = real && a.ownership ? __ldg(a.own_w + ch) : 0.0f;
+                w01[i] = make_float2(real ? __ldg(a.pol_w + ch) : 0.0f, real ? __ldg(a.pol_w + a.F + ch) : 0.0f);
+                w23[i] = make_float2(real ? __ldg(a.val_w + ch) : 0.0f, real && a.ownership ? __ldg(a.own_w + ch) : 0.0f);
             }
         // The batch norm of the sums this lane finishes (head k % 4 of its
         // sums k = (l >> kBfly) * kOwn + j), the same for every step.
@@ -99,7 +101,7 @@ struct HeadLane {
 #pragma unroll
         for (int s = 0; s < kHcSlots; ++s) {
             const int row = base + s * kGroups + grp;
-            float z[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            float2 z01 = make_float2(0.0f, 0.0f), z23 = z01;
             if (row < rows) {
 #pragma unroll
                 for (int j = 0; j < kNch; ++j) {
@@ -107,13 +109,17 @@ struct HeadLane {
                     float f[W];
                     pc.values(f);
 #pragma unroll
-                    for (int e = 0; e < W; ++e)
-#pragma unroll
-                        for (int h = 0; h < 4; ++h) z[h] = fmaf(w[h][j * W + e], f[e], z[h]);
+                    for (int e = 0; e < W; ++e) {
+                        const float2 ff = make_float2(f[e], f[e]);
+                        z01 = ffma2_rn(w01[j * W + e], ff, z01);
+                        z23 = ffma2_rn(w23[j * W + e], ff, z23);
+                    }
                 }
             }
-#pragma unroll
-            for (int h = 0; h < 4; ++h) acc[s * 4 + h] = z[h];
+            acc[s * 4] = z01.x;
+            acc[s * 4 + 1] = z01.y;
+            acc[s * 4 + 2] = z23.x;
+            acc[s * 4 + 3] = z23.y;
         }
         // Reduce-scatter over the high lane bits of the group while there
         // is more than one sum to split, then a butterfly over the rest.
@@ -186,6 +192,7 @@ template <int kOuts, int kBoards>
 struct FcWarp {
     static constexpr int kSums = kOuts * kBoards;
     static_assert((kSums & (kSums - 1)) == 0 && kSums >= 2 && kSums <= 1024, "a power of two of sums");
+    static_assert(kOuts % 2 == 0, "outputs go in pairs");
     static constexpr int kLogSums = kSums >= 512 ? 9 : kSums >= 256 ? 8 : kSums >= 128 ? 7 : kSums >= 64 ? 6
                                   : kSums >= 32 ? 5 : kSums >= 16 ? 4 : kSums >= 8 ? 3 : kSums >= 4 ? 2 : 1;
     static constexpr int kHeld = kSums >= 32 ? kSums / 32 : 1;   // sums a lane holds at the end
@@ -218,13 +225,17 @@ struct FcWarp {
 #pragma unroll
                 for (int u = 0; u < kPieces; ++u) {
                     if (u > 0 && !two) break;
+                    // Outputs in pairs through the packed fma (each half an
+                    // IEEE fmaf, in the same order: the same bits).
 #pragma unroll
-                    for (int o = 0; o < kOuts; ++o) {
-                        float& c = acc[o * kBoards + g];
-                        c = fmaf(w[u][o].x, v[u].x, c);
-                        c = fmaf(w[u][o].y, v[u].y, c);
-                        c = fmaf(w[u][o].z, v[u].z, c);
-                        c = fmaf(w[u][o].w, v[u].w, c);
+                    for (int o = 0; o < kOuts; o += 2) {
+                        float2 c = make_float2(acc[o * kBoards + g], acc[(o + 1) * kBoards + g]);
+                        c = ffma2_rn(make_float2(w[u][o].x, w[u][o + 1].x), make_float2(v[u].x, v[u].x), c);
+                        c = ffma2_rn(make_float2(w[u][o].y, w[u][o + 1].y), make_float2(v[u].y, v[u].y), c);
+                        c = ffma2_rn(make_float2(w[u][o].z, w[u][o + 1].z), make_float2(v[u].z, v[u].z), c);
+                        c = ffma2_rn(make_float2(w[u][o].w, w[u][o + 1].w), make_float2(v[u].w, v[u].w), c);
+                        acc[o * kBoards + g] = c.x;
+                        acc[(o + 1) * kBoards + g] = c.y;
                     }
                 }
             }

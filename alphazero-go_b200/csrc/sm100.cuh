@@ -462,6 +462,21 @@ __device__ __forceinline__ float2 fsub2_rn(float2 a, float2 b) {
     return d;
 }
 
+// Two IEEE fused multiply-adds in one instruction (fma.rn.f32x2): element
+// for element __fmaf_rn(a, b, c).
+__device__ __forceinline__ float2 ffma2_rn(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rb, {%4, %5};\n\t"
+        "mov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
 // Round-to-nearest (ties away) to tf32, as cvt.rna.tf32.f32 does; the low
 // 13 bits of the result are zero, so a tf32 MMA reads it exactly.
 __device__ __forceinline__ float to_tf32(float x) {
