@@ -609,7 +609,9 @@ class cuda_probe:
 
     @staticmethod
     def set_tower_fused(mode: int):
-        """-1 default (one launch for the tower of boards up to 10x10 with <= 64 channels), 0 per-layer kernels."""
+        """-1 default (one launch for the tower of boards up to 10x10 with <= 64 channels; tf32x3 at 64
+        channels runs two groups of boards per CTA where that saves a round of CTAs), 0 per-layer kernels,
+        1 fused with one group per CTA, 2 fused with two groups per CTA wherever the shape allows."""
         lib().azb_probe_set_tower_fused(mode)
 
     @staticmethod

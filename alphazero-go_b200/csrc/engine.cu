@@ -553,7 +553,7 @@ Weights::~Weights() {
 // -------------------------------------------------------------- workspace
 
 namespace {
-std::atomic<int> g_tower_fused{-1};   // -1 default (on where it applies), 0 off
+std::atomic<int> g_tower_fused{-1};   // -1 default (on where it applies), 0 off, 1 without board pairs, 2 pairs always
 }
 
 void set_tower_fused(int mode) { g_tower_fused = mode; }
@@ -827,6 +827,7 @@ void encode_forward(const Weights& w, Workspace& ws, int B, cudaStream_t s, bool
         fa.layer = w.fused_layers();
         fa.stem = w.fused_layers() + 2 * sh.blocks;
         fa.heads = 1;   // the heads' 1x1 convolutions from the resident trunk; no trunk is stored
+        fa.pairs = g_tower_fused.load() == 1 ? 0 : g_tower_fused.load() == 2 ? 2 : 1;   // 1, 2: for tests
         fa.head = h;
         fa.err = ws.err;
         const FusedMaps fm{ws.fmap, ws.fmap_lo, ws.fmap, ws.fmap_lo, ws.smap, ws.smap_lo};

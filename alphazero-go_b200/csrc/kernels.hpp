@@ -260,6 +260,7 @@ struct FusedArgs {
     const FusedLayer* layer;   // [layers]
     const FusedLayer* stem;    // the stem conv (one tap), when stem_nch > 0
     int heads;           // 1: the heads' 1x1 convolutions run here too (into head.feat), and no trunk is stored
+    int pairs;           // the split mode at two input chunks, two groups per CTA at once: 0 never, 1 where it pays, 2 always
     HeadArgs head;
     int* err;
 };

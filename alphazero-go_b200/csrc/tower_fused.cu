@@ -707,6 +707,557 @@ __global__ void __launch_bounds__(kFusedThreads<kSplit>, kFusedCtas<kSplit>)
     }
 }
 
+// ------------------------------------------------------------- board pairs
+//
+// The split mode at 64 channels with two groups of boards in flight per CTA.
+// One group alone runs each layer as its MMAs, then its epilogue (TMEM
+// reads, batch norm, the stores): the tensor core idles through the one and
+// the epilogue warps through the other. Two groups, each with its own
+// activation buffer, its own issuing thread and four epilogue warps, keep the
+// tensor core busy with one group's MMAs while the other's epilogue runs,
+// and every weight stage feeds both (it is released after both issuers'
+// commits). TMEM holds per group one stacked accumulator of 128 columns
+// (group g at 128 g), its block input (at 256 + 64 g) and its chunk-0 sums
+// (at 384 + 64 g): the two input chunks are two segments in time on the same
+// accumulator (the epilogue reads chunk 0's, parks its sums, before chunk
+// 1's MMAs start on it), the same MMAs and the same sums, in the same order,
+// as the one-group kernel's two stacks, so the outputs are the same bits.
+// At every step the epilogue reads both groups' chunk-0 segments before
+// either's chunk-1 segment: the issuers share the weight stages (a ring
+// shorter than a chunk's taps), so one group's second segment must never
+// wait for the other group's output.
+//
+// Warps: 0 loads (both groups' inputs, then the weight stages both
+// consume), 1 and 10 issue group 0's and group 1's MMAs, 2-9 run both
+// groups' epilogues, group 0's then group 1's at every step, and the heads.
+constexpr int kPairThreads = 352;
+constexpr uint32_t kPairTmemCols = 512;
+
+template <int kTps>
+struct PairCfg {
+    static constexpr int N = 64, kKc = 32, kSteps = 4;
+    static constexpr uint32_t kWTile = 64u * 128u;           // one plane of a (chunk, tap) weight tile
+    static constexpr uint32_t kTap = 2u * kWTile;            // both planes
+    static constexpr uint32_t kStage = uint32_t(kTps) * kTap;
+};
+
+struct PairSmem {
+    uint8_t* act[2];   // each group's activations: [plane][chunk] sub-buffers
+    uint8_t* ring;
+    float* bn;
+    uint64_t *wfull, *wempty;
+    // Two each, one per group.
+    uint64_t *in_full, *seg_full, *seg_empty, *act_ready, *out_done, *epi;
+    uint64_t* done;
+    uint32_t* tmem_slot;
+};
+
+__device__ __forceinline__ PairSmem pair_carve(uint8_t* raw, const FusedArgs& p, uint32_t stage_bytes) {
+    PairSmem s;
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+    const size_t buf = 2 * size_t(p.nch) * p.act_bytes;
+    s.act[0] = base;
+    s.act[1] = base + buf;
+    s.ring = base + 2 * buf;
+    s.bn = reinterpret_cast<float*>(s.ring + size_t(p.stages) * stage_bytes);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(s.bn + size_t(p.layers + 1) * 2 * 64);
+    s.wfull = bars;
+    s.wempty = bars + p.stages;
+    uint64_t* g = s.wempty + p.stages;
+    s.in_full = g;
+    s.seg_full = g + 2;
+    s.seg_empty = g + 4;
+    s.act_ready = g + 6;
+    s.out_done = g + 8;
+    s.epi = g + 10;
+    s.done = g + 12;
+    s.tmem_slot = reinterpret_cast<uint32_t*>(s.done + 1);
+    return s;
+}
+
+template <int kTps>
+__global__ void __launch_bounds__(kPairThreads, 1)
+    tower_fused_pair(const __grid_constant__ CUtensorMap mIn, const __grid_constant__ CUtensorMap mInLo,
+                     const __grid_constant__ CUtensorMap mStem, const __grid_constant__ CUtensorMap mStemLo,
+                     const __grid_constant__ FusedArgs p) {
+    using C = PairCfg<kTps>;
+    constexpr int N = C::N;
+    extern __shared__ uint8_t smem_raw[];
+    const PairSmem sm = pair_carve(smem_raw, p, C::kStage);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ngroups = (p.boards + p.group - 1) / p.group, npairs = (ngroups + 1) / 2;
+    const int group_rows = p.group * p.S;
+    {
+        const size_t words = 2 * 2 * size_t(p.nch) * p.act_bytes / 16;
+        uint4* w = reinterpret_cast<uint4*>(sm.act[0]);
+        for (size_t i = threadIdx.x; i < words; i += blockDim.x) w[i] = make_uint4(0, 0, 0, 0);
+        fence_proxy_async_smem();
+        const int nbn = (p.layers + (p.stem_nch > 0 ? 1 : 0)) * 2 * N;
+        for (int i = threadIdx.x; i < nbn; i += blockDim.x) {
+            const int l = i / (2 * N), j = i % (2 * N);
+            const FusedLayer& L = l < p.layers ? p.layer[l] : *p.stem;
+            sm.bn[i] = j < N ? L.scale[j] : L.shift[j - N];
+        }
+    }
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < p.stages; ++i) {
+            mbar_init(&sm.wfull[i], 1);
+            mbar_init(&sm.wempty[i], 2);   // both issuers
+        }
+        for (int g = 0; g < 2; ++g) {
+            mbar_init(&sm.in_full[g], 1);
+            mbar_init(&sm.seg_full[g], 1);
+            mbar_init(&sm.seg_empty[g], kFusedEpiWarps);
+            mbar_init(&sm.act_ready[g], kFusedEpiWarps);
+            mbar_init(&sm.out_done[g], kFusedEpiWarps);
+            mbar_init(&sm.epi[g], kFusedEpiWarps);
+        }
+        mbar_init(sm.done, 2);
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_map(&mIn);
+        tma_prefetch_map(&mInLo);
+    }
+    if (warp == 1) tmem_alloc(sm.tmem_slot, kPairTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *sm.tmem_slot;
+    grid_dependency_wait();
+    grid_launch_dependents();
+
+    const int first = p.stem_nch > 0 ? 1 : 0, steps = p.layers + first;
+    const int in_chunks = first ? p.stem_nch : p.nch;
+    const uint32_t in_tx = uint32_t(group_rows) * 128u * 2u * uint32_t(in_chunks);
+    if (warp == 0) {
+        // ---------------------------------------------------------- producer
+        if (lane == 0) {
+            Ring rw;
+            uint32_t nw = 0, kin[2] = {0, 0};
+            bool ok = true;
+            for (int P = blockIdx.x; P < npairs && ok; P += gridDim.x) {
+                for (int g = 0; g < 2 && ok; ++g) {
+                    const int grp = 2 * P + g;
+                    if (grp >= ngroups) continue;
+                    // The group's previous pair has been read out of its buffer.
+                    if (kin[g] > 0 && !(ok = mbar_wait(&sm.out_done[g], (kin[g] - 1) & 1, p.err, kErrWaitProducer))) break;
+                    mbar_arrive_expect_tx(&sm.in_full[g], in_tx);
+                    for (int pl = 0; pl < 2; ++pl)
+                        for (int c = 0; c < in_chunks; ++c)
+                            tma_load_2d(first ? (pl ? &mStemLo : &mStem) : (pl ? &mInLo : &mIn),
+                                        sm.act[g] + (size_t(pl) * p.nch + c) * p.act_bytes + size_t(p.top) * 128,
+                                        &sm.in_full[g], c * C::kKc, grp * group_rows);
+                    ++kin[g];
+                }
+                for (int st_ = 0; st_ < steps && ok; ++st_) {
+                    const bool stem = st_ < first;
+                    const FusedLayer& L = stem ? *p.stem : p.layer[st_ - first];
+                    // Chunk-major, one issuer's order: a chunk's taps in
+                    // stages of kTps (the stem: one tap, one stage per chunk).
+                    const int taps = stem ? 1 : 9, per_stage = stem ? 1 : kTps;
+                    const int nch = stem ? p.stem_nch : p.nch;
+                    for (int c = 0; c < nch && ok; ++c)
+                        for (int t0 = 0; t0 < taps && ok; t0 += per_stage) {
+                            if (!(ok = mbar_wait(&sm.wempty[rw.idx], rw.phase ^ 1u, p.err, kErrWaitProducer))) break;
+                            mbar_arrive_expect_tx(&sm.wfull[rw.idx], uint32_t(per_stage) * C::kTap);
+                            for (int j = 0; j < per_stage; ++j) {
+                                uint8_t* st = sm.ring + size_t(rw.idx) * C::kStage + size_t(j) * C::kTap;
+                                const int x = (c * taps + t0 + j) * C::kKc;
+                                tma_load_2d(&L.w, st, &sm.wfull[rw.idx], x, 0);
+                                tma_load_2d(&L.w_lo, st + C::kWTile, &sm.wfull[rw.idx], x, 0);
+                            }
+                            rw.next(p.stages);
+                            ++nw;
+                        }
+                }
+            }
+            // Every copy issued has landed before the CTA may exit.
+            for (uint32_t s = 0; s < uint32_t(p.stages) && s < nw; ++s) {
+                const uint32_t uses = (nw - s + p.stages - 1) / p.stages;
+                mbar_wait(&sm.wfull[s], (uses - 1) & 1, p.err, kErrWaitDrain);
+            }
+            for (int g = 0; g < 2; ++g)
+                if (kin[g] > 0) mbar_wait(&sm.in_full[g], (kin[g] - 1) & 1, p.err, kErrWaitDrain);
+        }
+    } else if (warp == 1 || warp == 2 + kFusedEpiWarps) {
+        // -------------------------------------------------------- MMA issue
+        // Issuer g: its group's MMAs, a segment per input chunk on the
+        // group's accumulator. Where its group is absent (an odd number of
+        // groups) it walks the ring all the same, releasing each stage.
+        const int g = warp == 1 ? 0 : 1;
+        if (lane == 0) {
+            Ring rw;
+            bool ok = true;
+            uint32_t segs = 0, steps_done = 0, kin = 0;
+            const uint64_t a_desc = sw128_desc(smem_u32(sm.act[g]));
+            const uint64_t ring_desc = sw128_desc(smem_u32(sm.ring));
+            const uint32_t d = tmem + uint32_t(g) * 128u;
+            constexpr uint32_t kStage16 = C::kStage >> 4, kTap16 = C::kTap >> 4;
+            constexpr uint32_t kIdescStack = umma_idesc(2 * N, false), kIdesc = umma_idesc(N, false);
+            const uint32_t plane16 = (uint32_t(p.nch) * uint32_t(p.act_bytes)) >> 4, chunk16 = uint32_t(p.act_bytes) >> 4;
+            const uint32_t centre16 = uint32_t(p.top) * 8u, row16 = uint32_t(p.n + 1) * 8u;
+            for (int P = blockIdx.x; P < npairs && ok; P += gridDim.x) {
+                const bool mine = 2 * P + g < ngroups;
+                for (int st_ = 0; st_ < steps && ok; ++st_) {
+                    const bool stem = st_ < first;
+                    const int taps = stem ? 1 : 9, per_stage = stem ? 1 : kTps;
+                    const int nch = stem ? p.stem_nch : p.nch;
+                    if (mine) {
+                        // The group's input is loaded, or its previous step
+                        // written (and read out of TMEM).
+                        ok = st_ == 0 ? mbar_wait(&sm.in_full[g], kin & 1, p.err, kErrWaitMma)
+                                      : mbar_wait(&sm.act_ready[g], (steps_done - 1) & 1, p.err, kErrWaitMma);
+                        if (!ok) break;
+                    }
+                    for (int c = 0; c < nch && ok; ++c) {
+                        // The accumulator's previous segment has been read.
+                        if (mine && !(ok = mbar_wait(&sm.seg_empty[g], (segs & 1) ^ 1, p.err, kErrWaitMma))) break;
+                        tc_fence_after();
+                        const uint64_t ac = a_desc + uint32_t(c) * chunk16 + centre16;
+                        for (int t0 = 0; t0 < taps && ok; t0 += per_stage) {
+                            if (!(ok = mbar_wait(&sm.wfull[rw.idx], rw.phase, p.err, kErrWaitMma))) break;
+                            if (mine) {
+                                tc_fence_after();
+                                const uint64_t bs = ring_desc + rw.idx * kStage16;
+                                if (stem) {
+#pragma unroll
+                                    for (int kk = 0; kk < C::kSteps; ++kk) {
+                                        umma<false>(d, ac + 2 * kk, bs + 2 * kk, kIdescStack, kk != 0);
+                                        umma<false>(d + N, ac + plane16 + 2 * kk, bs + 2 * kk, kIdesc, 1);
+                                    }
+                                } else {
+#pragma unroll
+                                    for (int j = 0; j < kTps; ++j) {
+                                        const int t = t0 + j;
+                                        const uint64_t at = ac + (t / 3 - 1) * int(row16) + (t % 3 - 1) * 8,
+                                                       bt = bs + j * kTap16;
+#pragma unroll
+                                        for (int kk = 0; kk < C::kSteps; ++kk) {
+                                            umma<false>(d, at + 2 * kk, bt + 2 * kk, kIdescStack, (t | kk) != 0);
+                                            umma<false>(d + N, at + plane16 + 2 * kk, bt + 2 * kk, kIdesc, 1);
+                                        }
+                                    }
+                                }
+                                umma_commit(&sm.wempty[rw.idx]);
+                            } else {
+                                mbar_arrive(&sm.wempty[rw.idx]);
+                            }
+                            rw.next(p.stages);
+                        }
+                        if (!ok) break;
+                        if (mine) {
+                            umma_commit(&sm.seg_full[g]);
+                            ++segs;
+                        }
+                    }
+                    if (mine) ++steps_done;
+                }
+                if (mine) ++kin;
+            }
+            // Every MMA issued is complete before TMEM is freed (also after an error).
+            umma_commit(sm.done);
+            mbar_wait(sm.done, 0, p.err, kErrWaitDrain);
+        }
+    } else if (warp < 2 + kFusedEpiWarps) {
+        // ---------------------------------------------------------- epilogue
+        // Eight warps for both groups, each step group 0's epilogue then
+        // group 1's (so one group's runs while the other's MMAs do): warp w
+        // reads TMEM lanes 32 (w % 4) ..., the two warps of a lane quarter
+        // split the output columns, as in the one-group kernel.
+        const int e = warp - 2, quarter = warp & 3, half = e >> 2;
+        const int col0 = half * 32;
+        const int row = quarter * 32 + lane;    // row of the tile (and TMEM lane)
+        const int brow = p.top + row;           // its row in a group's buffer
+        const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16);
+        uint32_t segs[2] = {0, 0}, steps_done[2] = {0, 0}, kin = 0, epi_uses = 0;
+        bool ok = true;
+        auto epi_sync = [&]() -> bool {   // the eight epilogue warps (bounded)
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.epi[0]);
+            const bool fine = mbar_wait(&sm.epi[0], epi_uses & 1, p.err, kErrWaitEpilogue);
+            ++epi_uses;
+            __syncwarp();
+            return fine;
+        };
+        // A pair's FCs run during the next pair's steps, as in the one-group
+        // kernel (boards [pend, pend + pend_boards), both groups', in runs of
+        // at most kFusedFcBoards).
+        int pend = -1, pend_boards = 0, fb = 0;
+        const float4* feat4 = reinterpret_cast<const float4*>(p.head.feat);
+        const size_t ld4 = size_t(p.head.feat_ld) / 4, val4 = size_t(p.head.feat_val) / 4;
+        auto xpol = [&](int gb, int j) { return feat4[size_t(fb + gb) * ld4 + j]; };
+        auto xval = [&](int gb, int j) { return feat4[size_t(fb + gb) * ld4 + val4 + j]; };
+        auto hid_at = [&](int gb) { return p.head.hid + size_t(fb + gb) * p.head.V; };
+        const int fc_quads = head_fc_quad_count<4>(p.head);
+        const int warp_quads = (fc_quads + kFusedEpiWarps - 1) / kFusedEpiWarps;
+        const int slice = (warp_quads + steps - 2) / (steps - 1);
+        auto fc_slice = [&](int i0, int i1) {
+            for (int i = i0; i < i1; ++i) {
+                const int q = e + i * kFusedEpiWarps;
+                if (q >= fc_quads) break;
+                for (int b0 = 0; b0 < pend_boards; b0 += kFusedFcBoards) {
+                    fb = pend + b0;
+                    head_fc_quad<4, kFusedFcBoards, true>(p.head, fb, min(kFusedFcBoards, pend_boards - b0), q, xpol,
+                                                          xval, hid_at, lane);
+                }
+            }
+        };
+        auto fc_finish = [&]() -> bool {
+            if (!epi_sync()) return false;
+            fb = pend;
+            for (int gb = e; gb < pend_boards; gb += kFusedEpiWarps) head_finish_board(p.head, pend + gb, hid_at(gb), lane);
+            pend = -1;
+            return true;
+        };
+        for (int P = blockIdx.x; P < npairs && ok; P += gridDim.x) {
+            const int ng = 2 * P + 1 < ngroups ? 2 : 1;   // groups in this pair
+            bool valid[2];
+            int boards[2];
+            for (int g = 0; g < 2; ++g) {
+                boards[g] = g < ng ? min(p.group, p.boards - (2 * P + g) * p.group) : 0;
+                valid[g] = row < boards[g] * p.S;
+                if (valid[g]) {
+                    const int r = row % p.S;
+                    valid[g] = r >= p.n + 1 && (r % (p.n + 1)) != p.n;
+                }
+            }
+            for (int st_ = 0; st_ < steps && ok; ++st_) {
+                const bool stem = st_ < first;
+                const int l = stem ? p.layers : st_ - first;   // the batch norm's entry
+                const bool skip = !stem && (l & 1) != 0;   // (every step has two segments: nch == stem_nch == 2)
+                if (pend >= 0) {
+                    if (st_ < steps - 1)
+                        fc_slice(st_ * slice, (st_ + 1) * slice);
+                    else if (!(ok = fc_finish()))
+                        break;
+                }
+                // Chunk 0's segment of each group first, its sums (hh + mixed)
+                // parked in TMEM (at 384 + 64 g): the two issuers share the
+                // weight stages, so neither group's second segment may wait
+                // for the other group's output.
+                for (int g = 0; g < ng && ok; ++g) {
+                    const uint8_t* hi = sm.act[g] + size_t(col0 / 32) * p.act_bytes;
+                    const uint8_t* lo = sm.act[g] + (size_t(p.nch) + col0 / 32) * p.act_bytes;
+                    const uint32_t stack = taddr + uint32_t(g) * 128u + uint32_t(col0);
+                    if (!stem && !skip) {
+                        // A block's first conv: its input (hi + lo, fp32) into
+                        // TMEM (at 256 + 64 g) for the second conv's epilogue.
+                        if (st_ == 0 && !(ok = mbar_wait(&sm.in_full[g], kin & 1, p.err, kErrWaitEpilogue))) break;
+                        uint32_t r[32];
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) {
+                            const float4 a4 = *reinterpret_cast<const float4*>(hi + swz(brow, u));
+                            const float4 l4 = *reinterpret_cast<const float4*>(lo + swz(brow, u));
+                            r[4 * u] = __float_as_uint(__fadd_rn(a4.x, l4.x));
+                            r[4 * u + 1] = __float_as_uint(__fadd_rn(a4.y, l4.y));
+                            r[4 * u + 2] = __float_as_uint(__fadd_rn(a4.z, l4.z));
+                            r[4 * u + 3] = __float_as_uint(__fadd_rn(a4.w, l4.w));
+                        }
+                        tmem_st32(taddr + 256u + uint32_t(g) * 64u + uint32_t(col0), r);
+                    }
+                    if (!(ok = mbar_wait(&sm.seg_full[g], segs[g] & 1, p.err, kErrWaitEpilogue))) break;
+                    tc_fence_after();
+                    uint32_t part[32];
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        uint32_t v0[16], w0[16];
+                        tmem_ld16(stack + 16u * h, v0);
+                        tmem_ld16(stack + N + 16u * h, w0);
+                        tmem_wait_ld();
+                        tmem_hold(v0);
+                        tmem_hold(w0);
+#pragma unroll
+                        for (int i = 0; i < 16; i += 2) {
+                            const float2 pa = fadd2_rn(make_float2(__uint_as_float(v0[i]), __uint_as_float(v0[i + 1])),
+                                                       make_float2(__uint_as_float(w0[i]), __uint_as_float(w0[i + 1])));
+                            part[16 * h + i] = __float_as_uint(pa.x);
+                            part[16 * h + i + 1] = __float_as_uint(pa.y);
+                        }
+                    }
+                    tmem_st32(taddr + 384u + uint32_t(g) * 64u + uint32_t(col0), part);
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sm.seg_empty[g]);
+                    ++segs[g];
+                }
+                // Then per group chunk 1's segment added to the parked sums,
+                // and the output.
+                for (int g = 0; g < ng && ok; ++g) {
+                    uint8_t* const buf = sm.act[g];
+                    const uint32_t stack = taddr + uint32_t(g) * 128u + uint32_t(col0);
+                    uint8_t* hi = buf + size_t(col0 / 32) * p.act_bytes;
+                    uint8_t* lo = buf + (size_t(p.nch) + col0 / 32) * p.act_bytes;
+                    if (!(ok = mbar_wait(&sm.seg_full[g], segs[g] & 1, p.err, kErrWaitEpilogue))) break;
+                    tc_fence_after();
+                    float acc[32];
+                    {
+                        uint32_t pv[32];
+                        tmem_ld32(taddr + 384u + uint32_t(g) * 64u + uint32_t(col0), pv);
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            uint32_t v0[16], w0[16];
+                            tmem_ld16(stack + 16u * h, v0);
+                            tmem_ld16(stack + N + 16u * h, w0);
+                            tmem_wait_ld();
+                            tmem_hold(v0);
+                            tmem_hold(w0);
+                            if (h == 0) tmem_hold(pv);
+#pragma unroll
+                            for (int i = 0; i < 16; i += 2) {
+                                const int k = 16 * h + i;
+                                const float2 pa = fadd2_rn(make_float2(__uint_as_float(v0[i]), __uint_as_float(v0[i + 1])),
+                                                           make_float2(__uint_as_float(w0[i]), __uint_as_float(w0[i + 1])));
+                                const float2 sa = fadd2_rn(make_float2(__uint_as_float(pv[k]), __uint_as_float(pv[k + 1])), pa);
+                                acc[k] = sa.x;
+                                acc[k + 1] = sa.y;
+                            }
+                        }
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sm.seg_empty[g]);
+                    ++segs[g];
+                    uint32_t rv[32];
+                    if (skip) {
+                        tmem_ld32(taddr + 256u + uint32_t(g) * 64u + uint32_t(col0), rv);
+                        tmem_wait_ld();
+                        tmem_hold(rv);
+                    }
+                    if (valid[g]) {
+                        // The batch norm, the residual, ReLU, the tf32 split, the
+                        // stores in place (the reference's separate roundings,
+                        // src/cuda/kernels.cu:172-176).
+                        const float4* sc4 = reinterpret_cast<const float4*>(sm.bn + size_t(l) * 2 * N + col0);
+                        const float4* sh4 = reinterpret_cast<const float4*>(sm.bn + size_t(l) * 2 * N + N + col0);
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) {
+                            const float4 a = sc4[u], b = sh4[u];
+                            float2 y01 = make_float2(__fadd_rn(__fmul_rn(a.x, acc[4 * u]), b.x),
+                                                     __fadd_rn(__fmul_rn(a.y, acc[4 * u + 1]), b.y));
+                            float2 y23 = make_float2(__fadd_rn(__fmul_rn(a.z, acc[4 * u + 2]), b.z),
+                                                     __fadd_rn(__fmul_rn(a.w, acc[4 * u + 3]), b.w));
+                            if (skip) {
+                                y01 = fadd2_rn(y01, make_float2(__uint_as_float(rv[4 * u]), __uint_as_float(rv[4 * u + 1])));
+                                y23 = fadd2_rn(y23, make_float2(__uint_as_float(rv[4 * u + 2]), __uint_as_float(rv[4 * u + 3])));
+                            }
+                            y01.x = y01.x > 0.0f ? y01.x : 0.0f;
+                            y01.y = y01.y > 0.0f ? y01.y : 0.0f;
+                            y23.x = y23.x > 0.0f ? y23.x : 0.0f;
+                            y23.y = y23.y > 0.0f ? y23.y : 0.0f;
+                            const float4 hv = make_float4(to_tf32(y01.x), to_tf32(y01.y), to_tf32(y23.x), to_tf32(y23.y));
+                            const float2 l01 = fsub2_rn(y01, make_float2(hv.x, hv.y));
+                            const float2 l23 = fsub2_rn(y23, make_float2(hv.z, hv.w));
+                            *reinterpret_cast<float4*>(hi + swz(brow, u)) = hv;
+                            *reinterpret_cast<float4*>(lo + swz(brow, u)) = make_float4(l01.x, l01.y, l23.x, l23.y);
+                        }
+                    }
+                    fence_proxy_async_smem();   // the writes, visible to the group's next MMAs
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sm.act_ready[g]);
+                    ++steps_done[g];
+                }
+            }
+            if (!ok) break;
+            // The pair's heads: each group's 1x1 convolutions once every
+            // epilogue warp has written its last layer (the one-group kernel's
+            // lane split and tree: the same bits); the FCs wait for the next
+            // pair's steps.
+            using H = HeadLane<kTF32x3, 16, 1>;
+            H hl;
+            hl.load(p.head, lane);
+            for (int g = 0; g < ng && ok; ++g) {
+                if (!(ok = mbar_wait(&sm.act_ready[g], (steps_done[g] - 1) & 1, p.err, kErrWaitEpilogue))) break;
+                const int A = p.n * p.n, pts = boards[g] * A, n = p.n, S = p.S, top = p.top;
+                const int first_board = (2 * P + g) * p.group;
+                const size_t act_bytes = size_t(p.act_bytes), lo_off = size_t(p.nch) * act_bytes;
+                const uint8_t* xbuf = sm.act[g];
+                auto piece = [=](int pt, int j) {
+                    const int b = pt / A, q = pt - b * A, y = q / n, xx = q - y * n;
+                    const int pr = top + b * S + (y + 1) * (n + 1) + xx, c = j >> 3, u = j & 7;
+                    TrunkPiece<kTF32x3> pc;
+                    pc.hi = *reinterpret_cast<const uint4*>(xbuf + size_t(c) * act_bytes + swz(pr, u));
+                    pc.lo = *reinterpret_cast<const uint4*>(xbuf + lo_off + size_t(c) * act_bytes + swz(pr, u));
+                    return pc;
+                };
+                auto where = [=](int pt, int* b, int* q) {
+                    *b = first_board + pt / A;
+                    *q = pt % A;
+                };
+                for (int base = e * H::kStepRows; base < pts; base += kFusedEpiWarps * H::kStepRows)
+                    hl.step(p.head, base, pts, piece, where, lane);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.out_done[g]);   // the buffer may take the group's next input
+            }
+            if (!ok || !(ok = epi_sync())) break;   // the features, visible to every epilogue warp
+            pend = 2 * P * p.group;
+            pend_boards = boards[0] + boards[1];
+            ++kin;
+        }
+        if (ok && pend >= 0) {   // the last pair's FCs
+            fc_slice(0, warp_quads);
+            fc_finish();
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kPairTmemCols);
+    }
+}
+
+template <int kTps>
+cudaError_t launch_pair_tps(const FusedMaps& m, const FusedArgs& a, size_t smem, int sms, cudaStream_t s) {
+    if (const cudaError_t e = open_smem<tower_fused_pair<kTps>>(smem); e != cudaSuccess) return e;
+    const int groups = (a.boards + a.group - 1) / a.group, pairs = (groups + 1) / 2;
+    const int grid = std::max(1, std::min(pairs, sms));
+    return launch_pdl(tower_fused_pair<kTps>, dim3(grid), dim3(kPairThreads), smem, s, m.in, m.in_lo, m.stem,
+                      m.stem_lo, a);
+}
+
+// Shared memory of a pair launch (0 when it does not fit): both groups'
+// buffers, then as many weight stages as the room left allows (two at least).
+size_t fused_pair_smem(int nch, int act_bytes, int layers, int* stages, int taps_per_stage) {
+    const size_t acts = 2 * 2 * size_t(nch) * act_bytes;
+    const size_t stage = size_t(taps_per_stage) * 2 * 64 * 128;
+    const size_t bn = size_t(layers + 1) * 2 * 64 * 4;
+    for (int st = 8; st >= 2; --st) {
+        const size_t total = 1024 + acts + st * stage + bn + (2 * st + 13) * 8 + 16;
+        if (total <= 227 * 1024) {
+            if (stages) *stages = st;
+            return total;
+        }
+    }
+    return 0;
+}
+
+// The pair kernel where it applies (the split mode at two input chunks,
+// heads in the launch) and pays: a pair costs ~1.7 one group's time on an SM
+// (measured: both groups' MMAs share the SM's shared-memory operand reads,
+// which bound a layer's MMA phase; what overlaps is the epilogue), so pairs
+// run only where they save rounds of CTAs: 9x9 at 256 boards (two rounds of
+// one group, one of pairs) 183 -> 166 us; at 148 boards 103 against 171 us,
+// at 1024 594 against 615 us. Three taps per stage where two such stages
+// fit, else one.
+cudaError_t launch_fused_pairs(const FusedMaps& m, FusedArgs a, int sms, cudaStream_t s, bool* launched) {
+    *launched = false;
+    if (!a.pairs || !a.heads || a.nch != 2) return cudaSuccess;
+    const int groups = (a.boards + a.group - 1) / a.group;
+    const int rounds = (groups + sms - 1) / sms, pair_rounds = ((groups + 1) / 2 + sms - 1) / sms;
+    if (a.pairs == 1 && 10 * rounds <= 18 * pair_rounds) return cudaSuccess;
+    for (int tps : {3, 1}) {
+        const size_t smem = fused_pair_smem(a.nch, a.act_bytes, a.layers, &a.stages, tps);
+        if (smem == 0) continue;
+        *launched = true;
+        return tps == 3 ? launch_pair_tps<3>(m, a, smem, sms, s) : launch_pair_tps<1>(m, a, smem, sms, s);
+    }
+    return cudaSuccess;
+}
+
 template <int N, bool kBf16, bool kSplit, int kTps>
 cudaError_t launch_fused_tps(const FusedMaps& m, const FusedArgs& a, size_t smem, int ctas, int sms, cudaStream_t s) {
     if (const cudaError_t e = open_smem<tower_fused<N, kBf16, kSplit, kTps>>(smem); e != cudaSuccess) return e;
@@ -720,6 +1271,11 @@ cudaError_t launch_fused_tps(const FusedMaps& m, const FusedArgs& a, size_t smem
 // it, then three taps per ring stage, each with at least two stages.
 template <int N, bool kBf16, bool kSplit>
 cudaError_t launch_fused_one(const FusedMaps& m, FusedArgs a, int sms, cudaStream_t s) {
+    if constexpr (kSplit && N == 64) {
+        bool launched = false;
+        const cudaError_t e = launch_fused_pairs(m, a, sms, s, &launched);
+        if (launched || e != cudaSuccess) return e;
+    }
     const int precision = kBf16 ? kBF16 : (kSplit ? kTF32x3 : kTF32);
     for (int ctas = kFusedCtas<kSplit>; ctas >= 1; --ctas)
         for (int tps : {3, 1}) {

@@ -299,8 +299,11 @@ void azb_probe_set_conv_segment(int steps);
 /* Boards whose frame rows fit one 128-row tile (n <= 10) with 32 or 64
  * output channels run the residual tower as one launch, each CTA keeping a
  * group of boards' activations in shared memory through every block (the
- * same arithmetic as the per-layer kernels, bit for bit). -1 the default,
- * 0 the per-layer kernels always. For tests and measurements. */
+ * same arithmetic as the per-layer kernels, bit for bit). -1 the default
+ * (the split mode at 64 channels with two groups of boards per CTA where that
+ * saves a round of CTAs), 0 the per-layer kernels always, 1 the fused launch
+ * with one group per CTA, 2 with two wherever the shape allows. For tests and
+ * measurements. */
 void azb_probe_set_tower_fused(int mode);
 /* Towers that do not fuse run every tower conv in one persistent launch:
  * CTAs take (layer, tile group) items in order, each waiting for the

@@ -61,3 +61,28 @@ def test_fused_tower_batch_independent(engine, oracle):
             alone = net.infer(pool[s:s + 1])
             for k in range(3):
                 assert np.array_equal(whole[k][s], alone[k][0]), (s, k)
+
+
+@pytest.mark.parametrize("shape,B", [((9, 6, 64, 1, False), 1), ((9, 6, 64, 1, False), 2), ((9, 6, 64, 1, False), 3),
+                                     ((9, 2, 64, 1, False), 301), ((7, 3, 64, 2, True), 5), ((5, 2, 64, 1, False), 20),
+                                     ((10, 2, 64, 8, True), 9)])
+def test_fused_pairs_equal_one_group(engine, oracle, shape, B):
+    """The split mode at 64 channels runs two groups of boards per CTA: the
+    same bits as one group per CTA, for odd and even group counts, several
+    pairs per CTA, the stem in the launch or not (history 8)."""
+    O = oracle
+    n, blocks, filters, history, own = shape
+    c = O.NetConfig(n, history, blocks, filters, 64, own)
+    params, buffers = O.make_network(c, 75, O.KIND_TEST)
+    x = O.random_planes(c, 76, B)
+    outs = []
+    for mode in (1, 2):
+        engine.cuda_probe.set_tower_fused(mode)
+        try:
+            with engine.CudaInference(engine.NetDesc.of(c), params, buffers, B, 0, engine.TF32X3) as net:
+                outs.append(net.infer(x, probs=True))
+        finally:
+            engine.cuda_probe.set_tower_fused(-1)
+    for k in range(len(outs[0])):
+        if outs[0][k] is not None:
+            assert np.array_equal(outs[0][k], outs[1][k]), (shape, B, k)
