@@ -192,7 +192,6 @@ template <int kOuts, int kBoards>
 struct FcWarp {
     static constexpr int kSums = kOuts * kBoards;
     static_assert((kSums & (kSums - 1)) == 0 && kSums >= 2 && kSums <= 1024, "a power of two of sums");
-    static_assert(kOuts % 2 == 0, "outputs go in pairs");
     static constexpr int kLogSums = kSums >= 512 ? 9 : kSums >= 256 ? 8 : kSums >= 128 ? 7 : kSums >= 64 ? 6
                                   : kSums >= 32 ? 5 : kSums >= 16 ? 4 : kSums >= 8 ? 3 : kSums >= 4 ? 2 : 1;
     static constexpr int kHeld = kSums >= 32 ? kSums / 32 : 1;   // sums a lane holds at the end
@@ -225,17 +224,13 @@ struct FcWarp {
 #pragma unroll
                 for (int u = 0; u < kPieces; ++u) {
                     if (u > 0 && !two) break;
-                    // Outputs in pairs through the packed fma (each half an
-                    // IEEE fmaf, in the same order: the same bits).
 #pragma unroll
-                    for (int o = 0; o < kOuts; o += 2) {
-                        float2 c = make_float2(acc[o * kBoards + g], acc[(o + 1) * kBoards + g]);
-                        c = ffma2_rn(make_float2(w[u][o].x, w[u][o + 1].x), make_float2(v[u].x, v[u].x), c);
-                        c = ffma2_rn(make_float2(w[u][o].y, w[u][o + 1].y), make_float2(v[u].y, v[u].y), c);
-                        c = ffma2_rn(make_float2(w[u][o].z, w[u][o + 1].z), make_float2(v[u].z, v[u].z), c);
-                        c = ffma2_rn(make_float2(w[u][o].w, w[u][o + 1].w), make_float2(v[u].w, v[u].w), c);
-                        acc[o * kBoards + g] = c.x;
-                        acc[(o + 1) * kBoards + g] = c.y;
+                    for (int o = 0; o < kOuts; ++o) {
+                        float& c = acc[o * kBoards + g];
+                        c = fmaf(w[u][o].x, v[u].x, c);
+                        c = fmaf(w[u][o].y, v[u].y, c);
+                        c = fmaf(w[u][o].z, v[u].z, c);
+                        c = fmaf(w[u][o].w, v[u].w, c);
                     }
                 }
             }

@@ -692,8 +692,10 @@ __global__ void __launch_bounds__(kFusedThreads<kSplit>, kFusedCtas<kSplit>)
                 mbar_arrive(sm.out_done);
             }
         }
-        if (ok && pend >= 0) {   // the last group's FCs
-            fc_slice(0, warp_quads);
+        if (ok && pend >= 0) {   // the last group's FCs: on the critical path, eight outputs per warp step
+            const int octs = head_fc_quad_count<8>(p.head);
+            for (int q = e; q < octs; q += kFusedEpiWarps)
+                head_fc_quad<8, kFusedFcBoards>(p.head, pend, pend_boards, q, xpol, xval, hid_at, lane);
             fc_finish();
         }
         if (e == 0 && lane == 0) bulk_wait_all();   // every store complete before the CTA exits
@@ -1196,8 +1198,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             pend_boards = boards[0] + boards[1];
             ++kin;
         }
-        if (ok && pend >= 0) {   // the last pair's FCs
-            fc_slice(0, warp_quads);
+        if (ok && pend >= 0) {   // the last pair's FCs: on the critical path, eight outputs per warp step
+            const int octs = head_fc_quad_count<8>(p.head);
+            for (int q = e; q < octs; q += kFusedEpiWarps)
+                for (int b0 = 0; b0 < pend_boards; b0 += kFusedFcBoards) {
+                    fb = pend + b0;
+                    head_fc_quad<8, kFusedFcBoards>(p.head, fb, min(kFusedFcBoards, pend_boards - b0), q, xpol, xval,
+                                                    hid_at, lane);
+                }
             fc_finish();
         }
     }
