@@ -416,27 +416,21 @@ __device__ __forceinline__ void store_split_sums(const ConvArgs& p, const float*
         const float4* hi = reinterpret_cast<const float4*>(static_cast<const float*>(res_hi) + off);
         const float4* lo = reinterpret_cast<const float4*>(static_cast<const float*>(res_lo) + off);
         // The chunk's outputs replace its sums (no second 32-float array live
-        // beside the sums and the residual). The residual's pieces are
-        // requested four at a time (each plane) before any of them is used:
-        // two round trips to L2 per chunk, not eight, within the registers.
+        // beside the sums and the residual).
         float* y = &sum[cc * 32];
 #pragma unroll
-        for (int u0 = 0; u0 < 8; u0 += 4) {
-            float4 h4[4], l4[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                h4[u] = skip ? hi[u0 + u] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                l4[u] = skip ? lo[u0 + u] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int u = 0; u < 8; ++u) {
+            float4 h4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), l4 = h4;
+            if (skip) {
+                h4 = hi[u];
+                l4 = lo[u];
             }
+            const float* h = &h4.x;
+            const float* l = &l4.x;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const float* h = &h4[u].x;
-                const float* l = &l4[u].x;
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int i = 4 * (u0 + u) + e;
-                    y[i] = valid ? split_out(y[i], scale[c0 + i], shift[c0 + i], skip, h[e], l[e]) : 0.0f;
-                }
+            for (int e = 0; e < 4; ++e) {
+                const int i = 4 * u + e;
+                y[i] = valid ? split_out(y[i], scale[c0 + i], shift[c0 + i], skip, h[e], l[e]) : 0.0f;
             }
         }
 #pragma unroll
