@@ -743,10 +743,11 @@ struct PairCfg {
     static constexpr uint32_t kStage = uint32_t(kTps) * kTap;
 };
 
+// (The batch norm is read through the read-only cache, not staged: its
+// 6.6 KB would take the room of the second three-tap weight stage.)
 struct PairSmem {
     uint8_t* act[2];   // each group's activations: [plane][chunk] sub-buffers
     uint8_t* ring;
-    float* bn;
     uint64_t *wfull, *wempty;
     // Two each, one per group.
     uint64_t *in_full, *seg_full, *seg_empty, *act_ready, *out_done, *epi;
@@ -761,8 +762,7 @@ __device__ __forceinline__ PairSmem pair_carve(uint8_t* raw, const FusedArgs& p,
     s.act[0] = base;
     s.act[1] = base + buf;
     s.ring = base + 2 * buf;
-    s.bn = reinterpret_cast<float*>(s.ring + size_t(p.stages) * stage_bytes);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(s.bn + size_t(p.layers + 1) * 2 * 64);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(s.ring + size_t(p.stages) * stage_bytes);
     s.wfull = bars;
     s.wempty = bars + p.stages;
     uint64_t* g = s.wempty + p.stages;
@@ -794,12 +794,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         uint4* w = reinterpret_cast<uint4*>(sm.act[0]);
         for (size_t i = threadIdx.x; i < words; i += blockDim.x) w[i] = make_uint4(0, 0, 0, 0);
         fence_proxy_async_smem();
-        const int nbn = (p.layers + (p.stem_nch > 0 ? 1 : 0)) * 2 * N;
-        for (int i = threadIdx.x; i < nbn; i += blockDim.x) {
-            const int l = i / (2 * N), j = i % (2 * N);
-            const FusedLayer& L = l < p.layers ? p.layer[l] : *p.stem;
-            sm.bn[i] = j < N ? L.scale[j] : L.shift[j - N];
-        }
     }
     if (threadIdx.x == 0) {
         for (int i = 0; i < p.stages; ++i) {
@@ -1131,11 +1125,13 @@ __global__ void __launch_bounds__(kPairThreads, 1)
                         // The batch norm, the residual, ReLU, the tf32 split, the
                         // stores in place (the reference's separate roundings,
                         // src/cuda/kernels.cu:172-176).
-                        const float4* sc4 = reinterpret_cast<const float4*>(sm.bn + size_t(l) * 2 * N + col0);
-                        const float4* sh4 = reinterpret_cast<const float4*>(sm.bn + size_t(l) * 2 * N + N + col0);
+                        // (the weight arena's pieces are 256-byte aligned: 16-byte loads)
+                        const FusedLayer& L = stem ? *p.stem : p.layer[l];
+                        const float4* sc4 = reinterpret_cast<const float4*>(L.scale + col0);
+                        const float4* sh4 = reinterpret_cast<const float4*>(L.shift + col0);
 #pragma unroll
                         for (int u = 0; u < 8; ++u) {
-                            const float4 a = sc4[u], b = sh4[u];
+                            const float4 a = __ldg(sc4 + u), b = __ldg(sh4 + u);
                             float2 y01 = make_float2(__fadd_rn(__fmul_rn(a.x, acc[4 * u]), b.x),
                                                      __fadd_rn(__fmul_rn(a.y, acc[4 * u + 1]), b.y));
                             float2 y23 = make_float2(__fadd_rn(__fmul_rn(a.z, acc[4 * u + 2]), b.z),
@@ -1229,12 +1225,11 @@ cudaError_t launch_pair_tps(const FusedMaps& m, const FusedArgs& a, size_t smem,
 
 // Shared memory of a pair launch (0 when it does not fit): both groups'
 // buffers, then as many weight stages as the room left allows (two at least).
-size_t fused_pair_smem(int nch, int act_bytes, int layers, int* stages, int taps_per_stage) {
+size_t fused_pair_smem(int nch, int act_bytes, int /*layers*/, int* stages, int taps_per_stage) {
     const size_t acts = 2 * 2 * size_t(nch) * act_bytes;
     const size_t stage = size_t(taps_per_stage) * 2 * 64 * 128;
-    const size_t bn = size_t(layers + 1) * 2 * 64 * 4;
     for (int st = 8; st >= 2; --st) {
-        const size_t total = 1024 + acts + st * stage + bn + (2 * st + 13) * 8 + 16;
+        const size_t total = 1024 + acts + st * stage + (2 * st + 13) * 8 + 16;
         if (total <= 227 * 1024) {
             if (stages) *stages = st;
             return total;
