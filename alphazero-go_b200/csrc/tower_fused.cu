@@ -749,7 +749,8 @@ struct PairSmem {
     uint8_t* act[2];   // each group's activations: [plane][chunk] sub-buffers
     uint8_t* ring;
     uint64_t *wfull, *wempty;
-    // Two each, one per group.
+    // Two each, one per group (epi: only [0] is used, the eight epilogue
+    // warps' barrier for both groups).
     uint64_t *in_full, *seg_full, *seg_empty, *act_ready, *out_done, *epi;
     uint64_t* done;
     uint32_t* tmem_slot;
