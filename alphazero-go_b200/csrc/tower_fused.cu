@@ -1244,9 +1244,10 @@ size_t fused_pair_smem(int nch, int act_bytes, int /*layers*/, int* stages, int 
 // (measured: both groups' MMAs share the SM's shared-memory operand reads,
 // which bound a layer's MMA phase; what overlaps is the epilogue), so pairs
 // run only where they save rounds of CTAs: 9x9 at 256 boards (two rounds of
-// one group, one of pairs) 183 -> 166 us; at 148 boards 103 against 171 us,
-// at 1024 594 against 615 us. Three taps per stage where two such stages
-// fit, else one.
+// one group, one of pairs) 184 -> 160 us; at 148 boards 103 against 163 us,
+// at 300 and 444 267 against 306 us, at 600 434 against 452 us, at 1024 601
+// against 596 us (within the noise; one group). Three taps per stage where
+// two such stages fit, else one.
 cudaError_t launch_fused_pairs(const FusedMaps& m, FusedArgs a, int sms, cudaStream_t s, bool* launched) {
     *launched = false;
     if (!a.pairs || !a.heads || a.nch != 2) return cudaSuccess;
